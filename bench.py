@@ -1,0 +1,366 @@
+#!/usr/bin/env python3
+"""Decode benchmark for the B200 path: batch-1 tok/s on the Llama-3.1-8B-shape
+Q4_K_M model, with the Q4_K GEMV's HBM roofline fraction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decoded token: embed -> 32 layers (RMSNorm+QKV+RoPE GEMV,
+Q8_0 append + split-K attention, O GEMV + residual, RMSNorm+gate/up GEMV +
+SwiGLU, down GEMV + residual) -> lm_head GEMV -> first-index argmax, with the
+token fed back on the device.  Weights (4.9 GB) are synthetic, seeded, and
+generated in HBM; the KV cache is prefilled with a 512-token random prompt.
+Weights exceed L2 (126 MB), so no flush is needed between steps.
+
+At --gpus N > 1 each rank decodes its own sequence on its own GPU (replicas,
+weak scaling; the value is the sum over ranks, timed as the max over ranks).
+``--impl reference`` times the reference's own C implementation of the path
+(oracle/_ref, compiled from the reference sources; else the oracle port) on
+host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s bs1, 8B-shape Q4_K_M; Q4_K/Q6_K GEMV HBM GB/s vs peak"
+PROMPT = 512
+GATEUP_PART = 3
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--shape", default="llama8b")
+    ap.add_argument("--prompt", type=int, default=PROMPT)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_setup(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(name: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons while the timed region runs."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int):
+        self.dev, self.proc, self.lines = dev, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU side
+def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
+    """Reference (or oracle) CPU path on a bounded sample of the 8B-shape token:
+    each step runs 2 of the 32 layers (forward_layer_view at the current
+    position, KV prefilled to `prompt`) plus 1/16 of the output-head rows;
+    one token costs 16 such steps.  Returns (tok/s, kind, sample text)."""
+    import numpy as np
+    from oracle.oracle_py import Oracle, Reference
+    from shukuchi_b200 import synth
+
+    s = synth.SHAPES[shape_name]
+    rng = np.random.default_rng(0)
+    layers = [synth.make_layer(rng, s) for _ in range(2)]
+    head_rows = s.n_vocab // 16
+    head = synth.quant_matrix(rng, s.t_out, head_rows, s.n_embd)
+    sub = synth.Model(s, layers, np.zeros(1, np.uint8), np.zeros(1, np.float32), head)
+    import dataclasses
+    sub.shape = dataclasses.replace(s, n_layers=2)
+    hidden = rng.normal(0, 1, s.n_embd).astype(np.float32)
+    kvd = s.n_kv_heads * s.head_dim
+    max_seq = prompt + steps + warmup + 2
+    if Reference.available():
+        R = Reference()
+        kind = "reference"
+        h, step_fn = R.forward_layer_fn(sub, max_seq)
+        kvh = R.L.ref_engine_kv(h)
+        for p in range(prompt):
+            kk = rng.normal(0, 1, kvd).astype(np.float32)
+            for layer in range(2):
+                R.L.ref_kv_append(kvh, layer, p, kk.ctypes.data, kk.ctypes.data)
+
+        def layer_fwd(layer, pos):
+            step_fn(layer, pos, hidden)
+
+        def head_fn():
+            R.matvec(s.t_out, head, hidden, head_rows, s.n_embd)
+    else:
+        O = Oracle(threads=1)
+        kind = "port"
+        ms = O.model_struct(sub)
+        kv = O.kv_create(2, s.n_kv_heads, s.head_dim, max_seq)
+        for p in range(prompt):
+            kk = rng.normal(0, 1, kvd).astype(np.float32)
+            for layer in range(2):
+                O.L.orc_kv_append(kv, layer, p, kk.ctypes.data, kk.ctypes.data)
+        import ctypes
+
+        def layer_fwd(layer, pos):
+            assert O.L.orc_forward_layer(ctypes.byref(ms), kv, layer, pos, hidden.ctypes.data) == 0
+
+        def head_fn():
+            O.matvec(s.t_out, head, hidden, head_rows, s.n_embd)
+
+    pos = prompt
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        layer_fwd(0, pos)
+        layer_fwd(1, pos)
+        head_fn()
+        dt = time.perf_counter() - t0
+        np.clip(hidden, -1e4, 1e4, out=hidden)
+        pos += 1
+        if i >= warmup:
+            times.append(dt)
+    per_token = 16.0 * sum(times) / len(times)
+    sample = (f"{steps} steps of 2/32 layers of {s.name} at positions {prompt}+ plus 1/16 of the "
+              f"output-head rows; token time = 16 x step time")
+    return 1.0 / per_token, kind, sample
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    v, kind, sample = cpu_sample(args.steps, args.warmup, args.shape, args.prompt)
+    line = {
+        "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.shape} Q4_K_M decode bs1 after a {args.prompt}-token prompt",
+                   "model": args.shape, "global_batch": 1, "seq_len": args.prompt, "parallelism": "none"},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU side
+def run_ours(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+    from shukuchi_b200 import cuda as sc
+    from shukuchi_b200 import synth
+    from shukuchi_b200.synth_device import make_device_model
+
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    shape = synth.SHAPES[args.shape]
+    ctx = sc.Context(local)
+    wts = make_device_model(shape, seed=1234 + rank, device=f"cuda:{local}")
+    total = args.prompt + 2 * (args.warmup + args.steps) + 8
+    kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, total)
+    m = sc.DeviceModel(ctx, kv, wts.desc)
+    for i, lv in enumerate(wts.layers):
+        m.set_layer(i, lv)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{local}")
+
+    # prompt, token by token (the reference has no batched prefill)
+    import numpy as np
+    rng = np.random.default_rng(rank)
+    prompt = rng.integers(0, shape.n_vocab, args.prompt).astype(np.uint32)
+    nxt = 0
+    for i, t in enumerate(prompt):
+        nxt = m.token_step(int(t), i, want_next=(i == len(prompt) - 1))
+    pos = args.prompt
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up
+    m.decode_steps(nxt, pos, args.warmup)
+    pos += args.warmup
+    nxt = m.last_token()
+    barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        m.decode_steps(nxt, pos, args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ctx.check()
+    ms = ev0.elapsed_time(ev1)
+    pos += args.steps
+    nxt = m.last_token()
+    t_max = torch.tensor([ms], device="cuda")
+    if ws > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    ms_per_step = ms_max / args.steps
+    value = ws * args.steps / (ms_max / 1000.0)
+
+    # end to end through the public call: host token in (pinned H2D), host
+    # token out (D2H), one call per token
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        nxt = m.token_step(int(nxt), pos, want_next=True)
+        pos += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    if ws > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e = ws * args.steps / (float(e_ms.item()) / 1000.0)
+
+    # dominant kernel: gate/up Q4_K GEMV (dual matrix, SwiGLU epilogue), timed
+    # per launch with events on the launching stream, rotating layers so no
+    # launch finds its weights in L2
+    durs = []
+    wbytes = 0
+    for i in range(max(args.steps, 32)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        wbytes = m.launch_part(i % shape.n_layers, GATEUP_PART)
+        b.record(stream)
+        durs.append((a, b))
+    torch.cuda.synchronize()
+    ctx.check()
+    avg = sum(a.elapsed_time(b) for a, b in durs[4:]) / len(durs[4:]) / 1000.0
+    alg = wbytes + 4 * (shape.n_embd + shape.n_ff)
+    peak, peak_kind = peaks()
+    achieved = alg / avg / 1e9
+    # whole-step bytes at the mean context of the timed region
+    mean_ctx = args.prompt + args.warmup + args.steps / 2
+    step_bytes = synth.token_bytes(shape) + synth.kv_bytes_per_pos(shape) * mean_ctx
+    step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        v, kind, sample = cpu_sample(12, 1, args.shape, args.prompt)
+        cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample}
+
+    launches_per_step = 1 + 5 * shape.n_layers + 2
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{shape.name} Q4_K_M decode bs1 after a {args.prompt}-token prompt, "
+                               f"Q8_0 KV, weights resident in HBM",
+                   "model": shape.name, "global_batch": ws, "seq_len": args.prompt,
+                   "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                   "l2": "no flush: 4.9 GB of weights per step exceed the 126 MB L2"},
+        "clocks": clk.summary(),
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K> gate/up (dual) + SwiGLU",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "bytes_per_launch": alg,
+                     "traffic": ncu_traffic("gemv_gateup_llama8b.md")},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
+                          "frac": step_gbs / peak},
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+    kv.close()
+    ctx.close()
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+    else:
+        run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,210 @@
+/*
+ * shk_cuda.h -- C ABI of the B200 (sm_100a) decode path for the Shukuchi engine.
+ *
+ * This library replaces the reference's Apple Metal backend
+ * (engine/include/metal_ops.h:5-26) and adds device-side versions of the ops
+ * (engine/include/ops.h:9-38), the Q8_0 KV cache (engine/include/kv_cache.h:5-37)
+ * and the per-layer forward (engine/src/engine.c:76-229), so the C engine keeps
+ * its model/layer API and CLI while all math runs as hand-written CUDA kernels.
+ *
+ * Conventions
+ *  - Plain C types only.  Pointers named *_dev are device pointers; *_host are
+ *    host pointers.  `stream` is a cudaStream_t passed as void* (NULL = the
+ *    context's compute stream).
+ *  - Every call returns an int status: 0 ok, negative SHK_E* on error.  There is
+ *    NO CPU fallback: an error is returned to the caller.
+ *  - Device-side waits are bounded; a wait that runs out records SHK_ETIMEOUT
+ *    in the context's error word (shk_cuda_check).
+ *  - One compute thread per context; shk_cuda_layer_stage may be called from a
+ *    separate loader thread (it uses the context's own copy stream).
+ *  - Weight tensors are in GGUF block layout: Q4_K (ggml type 12, 144-byte
+ *    super-blocks) and Q6_K (type 14, 210-byte super-blocks), rows of k/256
+ *    blocks.  Device weight pointers must be 16-byte aligned.
+ */
+#ifndef SHK_CUDA_H
+#define SHK_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum shk_status {
+    SHK_OK = 0,
+    SHK_EINVAL = -1,       /* bad argument / shape */
+    SHK_ENOMEM = -2,       /* device or pinned allocation failed */
+    SHK_ECUDA = -3,        /* CUDA runtime error */
+    SHK_EUNSUPPORTED = -4, /* dtype or shape not handled (e.g. Q5_K) */
+    SHK_ETIMEOUT = -5,     /* a bounded device wait ran out */
+    SHK_ENODEV = -6,       /* no usable CUDA device */
+    SHK_ENCCL = -7,        /* collective failure */
+    SHK_EDEVICE = -8       /* kernel reported an error (bad position/token) */
+};
+
+typedef struct shk_ctx shk_ctx;     /* device, streams, error word, counters */
+typedef struct shk_kv shk_kv;       /* Q8_0 KV cache in HBM */
+typedef struct shk_model shk_model; /* dims, scratch, captured decode step */
+
+struct shk_cuda_config {
+    int device;     /* CUDA ordinal; -1 = current device */
+    uint32_t flags; /* reserved, 0 */
+};
+
+/* ---- context: replaces metal_ops_init/metal_ops_shutdown/metal_available/
+ *      metal_ops_report (engine/include/metal_ops.h:5-6, 24-25) ---- */
+shk_ctx *shk_cuda_init(const struct shk_cuda_config *cfg);
+void shk_cuda_shutdown(shk_ctx *ctx);
+int shk_cuda_available(void);
+void shk_cuda_report(shk_ctx *ctx);
+/* Synchronises the compute stream and returns SHK_ETIMEOUT / SHK_EDEVICE if a
+ * kernel recorded a device-side error since the last call (which clears it). */
+int shk_cuda_check(shk_ctx *ctx);
+const char *shk_cuda_strerror(int status);
+void *shk_cuda_stream(shk_ctx *ctx);       /* compute stream (cudaStream_t) */
+int shk_cuda_num_sms(shk_ctx *ctx);
+
+/* ---- memory helpers for the engine and loader ---- */
+int shk_cuda_dev_alloc(shk_ctx *ctx, size_t bytes, void **out_dev);
+int shk_cuda_dev_free(shk_ctx *ctx, void *p_dev);
+int shk_cuda_host_alloc(shk_ctx *ctx, size_t bytes, void **out_host); /* pinned */
+int shk_cuda_host_free(shk_ctx *ctx, void *p_host);
+int shk_cuda_memcpy_h2d(shk_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes, void *stream);
+int shk_cuda_memcpy_d2h(shk_ctx *ctx, void *dst_host, const void *src_dev, size_t bytes, void *stream);
+int shk_cuda_sync(shk_ctx *ctx, void *stream);
+
+/* ---- dequantise-matvec: replaces metal_matmul_q4k_vec / metal_matmul_q6k_vec
+ *      (engine/include/metal_ops.h:7-23) as called from op_matmul_q4_k /
+ *      op_matmul_q6_k (engine/src/ops.c:266-314, 361-404).
+ *      y[r] = sum_k dequant(W[r,k]) * x[k], W m x k, k % 256 == 0.  Async. ---- */
+int shk_cuda_matmul_q4k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev, float *y_dev,
+                            uint32_t m, uint32_t k, void *stream);
+int shk_cuda_matmul_q6k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev, float *y_dev,
+                            uint32_t m, uint32_t k, void *stream);
+/* Same contract as metal_matmul_q{4,6}k_vec: HOST weights/x/y, synchronous
+ * (copies in, computes, copies out).  For callers that keep the reference's
+ * host-resident layer buffers unchanged. */
+int shk_cuda_matmul_q4k_vec_host(shk_ctx *ctx, const void *w_host, const float *x_host,
+                                 float *y_host, uint32_t m, uint32_t k);
+int shk_cuda_matmul_q6k_vec_host(shk_ctx *ctx, const void *w_host, const float *x_host,
+                                 float *y_host, uint32_t m, uint32_t k);
+
+/* ---- op-level glue on device (engine/include/ops.h:9-38) ---- */
+/* op_rmsnorm, n = 1 (engine/src/ops.c:195-214) */
+int shk_cuda_rmsnorm(shk_ctx *ctx, const float *x_dev, const float *w_dev, float *y_dev,
+                     uint32_t d, void *stream);
+/* op_rope (engine/src/ops.c:216-238); in place */
+int shk_cuda_rope(shk_ctx *ctx, float *qk_dev, uint32_t n_heads, uint32_t head_dim, uint32_t pos,
+                  float rope_theta, void *stream);
+/* SwiGLU of op_mlp_swiglu (engine/src/ops.c:491-496) */
+int shk_cuda_swiglu(shk_ctx *ctx, const float *gate_dev, const float *up_dev, float *h_dev,
+                    uint32_t n, void *stream);
+/* op_embed for one token, Q4_K (12) or F16 (1) table (engine/src/ops.c:533-577) */
+int shk_cuda_embed(shk_ctx *ctx, const void *table_dev, uint32_t dtype, uint32_t n_vocab,
+                   uint32_t token, float *out_dev, uint32_t n_embd, void *stream);
+/* first-index argmax (engine/src/engine.c:424-431); result to host */
+int shk_cuda_argmax(shk_ctx *ctx, const float *x_dev, uint32_t n, uint32_t *out_host);
+
+/* ---- Q8_0 KV cache in HBM (engine/include/kv_cache.h:11-37).  Quantisation
+ *      is bit-identical to q8_quantize_vec (engine/src/kv_cache.c:28-55). ---- */
+struct shk_kv_config {
+    uint32_t n_layers;
+    uint32_t n_kv_heads;
+    uint32_t head_dim; /* 64 or 128 */
+    uint32_t block_size; /* kept for API parity; storage is per position */
+    uint32_t max_seq_len; /* not capped at 2048 */
+};
+shk_kv *shk_cuda_kv_create(shk_ctx *ctx, const struct shk_kv_config *cfg);
+void shk_cuda_kv_destroy(shk_kv *kv);
+/* kv_cache_append (engine/src/kv_cache.c:130-155); k/v: n_kv*head_dim fp32 */
+int shk_cuda_kv_append(shk_kv *kv, uint32_t layer, uint32_t pos, const float *k_dev,
+                       const float *v_dev, void *stream);
+/* kv_cache_read_range (engine/src/kv_cache.c:175-199): fp32 [pos][n_kv*hd] */
+int shk_cuda_kv_read_range(shk_kv *kv, uint32_t layer, uint32_t start, uint32_t end,
+                           float *k_dev, float *v_dev, void *stream);
+/* raw 36-byte {float scale; int8 q[32]} blocks, reference order
+ * [pos][n_kv*hd/32] -- for byte-exact comparisons */
+int shk_cuda_kv_read_blocks(shk_kv *kv, uint32_t layer, uint32_t start, uint32_t end,
+                            void *k_dev, void *v_dev, void *stream);
+/* kv_cache_read_range + op_attention over positions [0, seq_len) fused on the
+ * Q8_0 cache (engine/src/engine.c:137-158, engine/src/ops.c:406-461).  If
+ * k_new_dev/v_new_dev are non-NULL they are first appended at seq_len-1. */
+int shk_cuda_kv_attend(shk_kv *kv, uint32_t layer, const float *q_dev, const float *k_new_dev,
+                       const float *v_new_dev, float *out_dev, uint32_t n_heads, uint32_t seq_len,
+                       float scale, void *stream);
+/* kv_cache_clear / kv_cache_get_seq_len (engine/src/kv_cache.c:230-248) */
+void shk_cuda_kv_clear(shk_kv *kv);
+uint32_t shk_cuda_kv_seq_len(shk_kv *kv, uint32_t layer);
+
+/* ---- model: per-layer forward, embed, lm_head+argmax, captured decode step ---- */
+struct shk_model_desc {            /* struct model_info (model_loader.h:66-74) + resident */
+    uint32_t n_layers, n_embd, n_heads, n_kv_heads, head_dim, n_ff, n_vocab;
+    float rope_theta;              /* 0 -> 10000, as engine/src/engine.c:86 */
+    const void *tok_embd_dev;      /* token_embd, resident */
+    uint32_t tok_embd_dtype;
+    const void *output_dev;        /* output (lm_head), resident */
+    uint32_t output_dtype;
+};
+struct shk_layer_desc {            /* struct layer_view (model_loader.h:28-56), DEVICE pointers */
+    const float *attn_norm, *ffn_norm;
+    const void *attn_q, *attn_k, *attn_v, *attn_o, *ffn_gate, *ffn_up, *ffn_down;
+    uint32_t attn_q_dtype, attn_k_dtype, attn_v_dtype, attn_o_dtype;
+    uint32_t ffn_gate_dtype, ffn_up_dtype, ffn_down_dtype;
+    uint32_t row_stride_v, row_stride_down; /* 0 = dense rows; else padded row bytes */
+};
+shk_model *shk_cuda_model_create(shk_ctx *ctx, const struct shk_model_desc *desc, shk_kv *kv);
+void shk_cuda_model_destroy(shk_model *m);
+/* Registers device weights of a layer for the captured whole-token step. */
+int shk_cuda_model_set_layer(shk_model *m, uint32_t layer, const struct shk_layer_desc *lv);
+/* forward_layer_view (engine/src/engine.c:76-229) on device-resident weights:
+ * hidden_dev (n_embd fp32) is updated in place; K/V appended at pos. */
+int shk_cuda_forward_layer(shk_model *m, const struct shk_layer_desc *lv, uint32_t layer,
+                           uint32_t pos, float *hidden_dev, void *stream);
+/* op_embed(token) into the model's hidden state */
+int shk_cuda_model_embed(shk_model *m, uint32_t token, void *stream);
+/* lm_head on the raw residual (no final norm, engine/src/engine.c:403-422) and
+ * first-index argmax.  logits_host may be NULL. */
+int shk_cuda_model_lm_head(shk_model *m, uint32_t *token_host, float *logits_host, void *stream);
+float *shk_cuda_model_hidden(shk_model *m); /* device pointer to hidden[n_embd] */
+/* One whole token through embed -> all layers (-> lm_head -> argmax when
+ * want_next) as one captured CUDA graph.  token and pos come from the host;
+ * the next token (and logits if logits_host != NULL) are copied back.  All
+ * layers must be registered with shk_cuda_model_set_layer. */
+int shk_cuda_token_step(shk_model *m, uint32_t token, uint32_t pos, int want_next,
+                        uint32_t *next_host, float *logits_host);
+/* Device-only decode steps: token and position stay on the device (argmax
+ * feeds the next embed, position auto-increments).  Used for throughput. */
+int shk_cuda_decode_steps(shk_model *m, uint32_t first_token, uint32_t first_pos, uint32_t n_steps,
+                          void *stream);
+int shk_cuda_model_token(shk_model *m, uint32_t *token_host); /* last argmax */
+/* Profiling hook: enqueue one part of a registered layer's step at the device
+ * position of the last step (part 0 RMSNorm+QKV+RoPE GEMV, 1 append+attention,
+ * 2 O-proj+residual, 3 RMSNorm+gate/up+SwiGLU, 4 down+residual; 5 = lm_head
+ * GEMV, layer ignored).  Returns the algorithmic bytes of that launch's
+ * weights in *bytes_out (nullable). */
+int shk_cuda_model_launch_part(shk_model *m, uint32_t layer, uint32_t part, void *stream,
+                               uint64_t *bytes_out);
+
+/* ---- layer streaming: pinned staging -> HBM on the context's copy stream
+ *      (replaces the host-only prefetch ring, engine/src/prefetch.c:39-280) ---- */
+/* Queue an async H2D copy of a staged layer blob into dst_dev and record the
+ * completion event of `slot`.  Callable from the loader thread. */
+int shk_cuda_layer_stage(shk_ctx *ctx, uint32_t slot, void *dst_dev, const void *pinned_src,
+                         size_t bytes);
+/* Strided variant: rows of src_row_bytes copied to rows of dst_row_bytes
+ * (pads Q6_K rows to 16-byte multiples). */
+int shk_cuda_layer_stage_rows(shk_ctx *ctx, uint32_t slot, void *dst_dev, size_t dst_row_bytes,
+                              const void *pinned_src, size_t src_row_bytes, size_t rows);
+/* Marks the end of a slot's staging sequence (records its event). */
+int shk_cuda_layer_commit(shk_ctx *ctx, uint32_t slot);
+/* 1 if the slot's copies completed, 0 if still in flight (wait = 0), or block
+ * until complete (wait != 0). */
+int shk_cuda_layer_ready(shk_ctx *ctx, uint32_t slot, int wait);
+/* Make `stream` wait (on the device) for the slot's copies. */
+int shk_cuda_layer_wait(shk_ctx *ctx, uint32_t slot, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,57 @@
+// attn.cuh -- Q8_0 KV cache layout, quantise-on-append and split-K decode attention.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace shk {
+
+// HBM layout of the Q8_0 KV cache.  One region per (layer, kv head) holding, for
+// positions 0..max_seq-1: K quants [max_seq][hd] int8, K scales [max_seq][hd/32]
+// fp32, then the same for V.  A (scale, 32 quants) pair is exactly one of the
+// reference's 36-byte blocks (engine/src/kv_cache.c:7-10); blocks never straddle
+// heads because hd is a multiple of 32.
+struct KvLayout {
+  int8_t* base;        // device allocation
+  uint32_t n_layers, n_kv, hd, max_seq;
+  size_t head_bytes;   // bytes of one (layer, kv head) region
+  size_t kq_off, ks_off, vq_off, vs_off;  // offsets inside a region
+  __host__ __device__ int8_t* region(uint32_t layer, uint32_t kvh) const {
+    return base + ((size_t)layer * n_kv + kvh) * head_bytes;
+  }
+};
+
+KvLayout kv_layout_make(uint32_t n_layers, uint32_t n_kv, uint32_t hd, uint32_t max_seq);
+
+struct AttnArgs {
+  KvLayout kv;
+  uint32_t layer;
+  uint32_t n_heads;
+  float scale;              // 1/sqrt(hd)
+  const float* q;           // n_heads * hd  (after RoPE)
+  const float* k_new;       // n_kv * hd     (after RoPE), appended at *pos; null: no append
+  const float* v_new;       // n_kv * hd
+  const uint32_t* pos;      // device: position of the new token; attention covers [0, pos]
+  float* out;               // n_heads * hd
+  float* part;              // split partials: n_kv * max_splits * G * (hd + 2)
+  int* counters;            // n_kv ints, zero between launches (self-resetting)
+  uint32_t max_splits;
+  uint32_t min_per_split;
+  int* err;
+};
+
+cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream);
+size_t attn_part_floats(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_splits);
+
+// Quantise and store one token's K and V (engine/src/kv_cache.c:130-155).
+cudaError_t kv_append_launch(const KvLayout& kv, uint32_t layer, const uint32_t* pos,
+                             const float* k, const float* v, int* err, cudaStream_t stream);
+// Dequantise positions [start, end) to fp32, reference order [pos][n_kv*hd]
+// (engine/src/kv_cache.c:175-199).
+cudaError_t kv_read_range_launch(const KvLayout& kv, uint32_t layer, uint32_t start, uint32_t end,
+                                 float* k_out, float* v_out, cudaStream_t stream);
+// Export raw 36-byte blocks in the reference order [pos][n_kv*hd/32][36].
+cudaError_t kv_read_blocks_launch(const KvLayout& kv, uint32_t layer, uint32_t start, uint32_t end,
+                                  uint8_t* k_out, uint8_t* v_out, cudaStream_t stream);
+
+}  // namespace shk

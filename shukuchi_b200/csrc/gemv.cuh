@@ -1,0 +1,83 @@
+// gemv.cuh -- batch-1 Q4_K / Q6_K dequantise-matvec for sm_100a (host-side plan API).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace shk {
+
+// Epilogue applied to each output row.
+enum GemvEpi : uint8_t {
+  EPI_STORE = 0,   // y[r] = acc
+  EPI_ADD = 1,     // y[r] += acc            (residual add, engine/src/engine.c:164-166)
+  EPI_ROPE = 2,    // RoPE on the (2i, 2i+1) pair, then store (engine/src/ops.c:216-238)
+  EPI_SWIGLU = 3,  // dual rows: y[r] = silu(gate) * up    (engine/src/ops.c:491-496)
+};
+
+constexpr int GEMV_MAX_SEGS = 4;
+constexpr int GEMV_WARPS = 8;  // consumer warps; one more warp issues the bulk copies
+constexpr int GEMV_THREADS = 32 * (GEMV_WARPS + 1);
+constexpr int GEMV_STAGES = 4;
+
+struct GemvSeg {
+  const uint8_t* w;     // matrix: m rows, row r at w + r * row_stride
+  const uint8_t* w2;    // second matrix of a dual (gate/up) segment, same shape
+  float* y;             // output, m floats
+  uint32_t m;           // rows
+  uint32_t nb;          // 256-element super-blocks per row
+  uint32_t row_stride;  // bytes between rows; multiple of 16
+  uint32_t chunk_rows;  // rows per pipeline stage (multiple of rg)
+  uint32_t unit_cost;   // bytes per rg-row unit (both matrices for dual)
+  uint32_t rope_hd;     // head_dim for EPI_ROPE
+  uint8_t qt;           // 12 = Q4_K, 14 = Q6_K
+  uint8_t epi;          // GemvEpi
+  uint8_t rg;           // rows per warp task
+  uint8_t dual;         // 1 for gate/up pairs
+};
+
+struct GemvArgs {
+  GemvSeg seg[GEMV_MAX_SEGS];
+  uint32_t nseg;
+  uint32_t k;               // input dimension shared by all segments
+  const float* x;           // k floats
+  const float* norm_w;      // optional: x <- rmsnorm(x) * norm_w  (eps 1e-5)
+  const uint32_t* pos;      // device position for EPI_ROPE
+  float rope_theta;
+  uint32_t stage_bytes;     // bytes per pipeline stage
+  uint64_t total_cost;      // sum over segments of units * unit_cost
+  int* err;                 // device error word
+};
+
+struct GemvPlan {
+  GemvArgs args;
+  int grid = 0;
+  size_t smem = 0;
+  int has4 = 0, has6 = 0;
+};
+
+// Describes one matrix for planning.
+struct GemvMat {
+  const void* w;
+  const void* w2;  // non-null => dual segment (gate/up)
+  float* y;
+  uint32_t m;
+  uint32_t qt;
+  uint32_t row_stride;  // 0 => dense rows
+  uint8_t epi;
+  uint32_t rope_hd;
+};
+
+// Returns 0 on success, negative on unsupported shapes (caller may fall back).
+int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const float* x,
+              const float* norm_w, const uint32_t* pos, float rope_theta, int* err,
+              int num_sms);
+// Sets the kernels' dynamic shared-memory limit; call once per device.
+cudaError_t gemv_init();
+cudaError_t gemv_launch(const GemvPlan& p, cudaStream_t stream);
+
+// Simple fallback for layouts the staged kernel does not take (rows not a
+// multiple of 16 bytes).  Same math, plain loads.
+cudaError_t gemv_generic_launch(uint32_t qt, const void* w, const float* x, float* y, uint32_t m,
+                                uint32_t k, cudaStream_t stream);
+
+}  // namespace shk

@@ -1,0 +1,219 @@
+// glue.cu -- embedding lookup, first-index argmax and stand-alone glue ops.
+//
+// The decode step fuses RMSNorm, RoPE, SwiGLU and the residual adds into the
+// GEMV prologue/epilogues (gemv.cu); the stand-alone kernels here back the
+// op-level C entry points (ops.h equivalents) and the token-feedback path.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "glue.cuh"
+
+namespace shk {
+namespace {
+
+// op_embed, Q4_K and F16 branches (engine/src/ops.c:533-577).  The token id
+// is read from device memory so a captured graph can feed back the argmax.
+__global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t dtype,
+                             const uint32_t* __restrict__ tok_p, uint32_t n_vocab, float* out,
+                             uint32_t n_embd, int* err) {
+  const uint32_t tok = *tok_p;
+  if (tok >= n_vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) set_error(err, DERR_BAD_TOKEN);
+    return;
+  }
+  if (dtype == 1) {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(table) + (size_t)tok * n_embd;
+    for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < n_embd; j += gridDim.x * blockDim.x)
+      out[j] = ref_half(row[j]);
+    return;
+  }
+  // Q4_K: one thread per element, same per-element formula as the reference:
+  // y = (d * sc) * q - dmin * m.
+  const uint32_t nb = n_embd / QK;
+  const uint8_t* row = table + (size_t)tok * nb * Q4K_BYTES;
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n_embd; e += gridDim.x * blockDim.x) {
+    const uint8_t* blk = row + (size_t)(e / QK) * Q4K_BYTES;
+    const uint32_t l = e % QK, grp = l / 64, w = l % 64, sub = 2 * grp + (w >= 32);
+    const float d = ref_half(blk[0] | (blk[1] << 8)), dmin = ref_half(blk[2] | (blk[3] << 8));
+    const uint8_t* sc = blk + 4;
+    uint32_t s, m;
+    if (sub < 4) {
+      s = sc[sub] & 63;
+      m = sc[sub + 4] & 63;
+    } else {
+      s = (sc[sub + 4] & 0xF) | ((sc[sub - 4] >> 6) << 4);
+      m = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4);
+    }
+    const uint8_t qb = blk[16 + 32 * grp + (w & 31)];
+    const uint32_t q = (w >= 32) ? (qb >> 4) : (qb & 0xF);
+    const float d1 = d * (float)s, m1 = dmin * (float)m;
+    out[e] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+  }
+}
+
+// First index of the maximum (engine/src/engine.c:424-431: strict > keeps the
+// earliest index).  Block partials then the last block merges.  Optionally
+// advances the device position counter (token feedback in a captured step).
+constexpr int AM_THREADS = 512;
+__global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restrict__ x, uint32_t n,
+                                                            float* part_v, uint32_t* part_i,
+                                                            int* counter, uint32_t* tok_out,
+                                                            uint32_t* pos_inc) {
+  __shared__ float sv[AM_THREADS / 32];
+  __shared__ uint32_t si[AM_THREADS / 32];
+  __shared__ int last;
+  const uint32_t per = (n + gridDim.x - 1) / gridDim.x;
+  const uint32_t lo = blockIdx.x * per, hi = min(n, lo + per);
+  float bv = -INFINITY;
+  uint32_t bi = 0xFFFFFFFFu;
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += AM_THREADS) {
+    const float v = x[i];
+    if (bi == 0xFFFFFFFFu || v > bv) {  // i increases: strict > keeps the first
+      bv = v;
+      bi = i;
+    }
+  }
+  auto better = [](float v1, uint32_t i1, float v2, uint32_t i2) {
+    if (i2 == 0xFFFFFFFFu) return false;
+    if (i1 == 0xFFFFFFFFu) return true;
+    return v2 > v1 || (v2 == v1 && i2 < i1);
+  };
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(bv, bi, ov, oi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = sv[0];
+    uint32_t ix = si[0];
+    for (int w = 1; w < AM_THREADS / 32; ++w)
+      if (better(v, ix, sv[w], si[w])) {
+        v = sv[w];
+        ix = si[w];
+      }
+    part_v[blockIdx.x] = v;
+    part_i[blockIdx.x] = ix;
+    __threadfence();
+    last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  float v = __ldcg(&part_v[0]);
+  uint32_t ix = __ldcg(&part_i[0]);
+  for (uint32_t b = 1; b < gridDim.x; ++b) {
+    const float ov = __ldcg(&part_v[b]);
+    const uint32_t oi = __ldcg(&part_i[b]);
+    if (better(v, ix, ov, oi)) {
+      v = ov;
+      ix = oi;
+    }
+  }
+  // NaN logits never compare greater; an all-NaN vector yields index 0 as in
+  // the reference loop.
+  *tok_out = (ix == 0xFFFFFFFFu) ? 0u : ix;
+  if (pos_inc) *pos_inc += 1;
+  *counter = 0;
+}
+
+// op_rmsnorm, n = 1 (engine/src/ops.c:195-214)
+__global__ void rmsnorm_kernel(const float* x, const float* w, float* y, uint32_t d) {
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (uint32_t w2 = 0; w2 < blockDim.x / 32; ++w2) tot += red[w2];
+  const float inv = 1.0f / sqrtf(tot / (float)d + 1e-5f);
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) y[i] = (x[i] * inv) * w[i];
+}
+
+// op_rope (engine/src/ops.c:216-238)
+__global__ void rope_kernel(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos_p,
+                            float theta) {
+  const uint32_t pairs = n_heads * (hd / 2);
+  const uint32_t pos = *pos_p;
+  for (uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x) {
+    const uint32_t h = p / (hd / 2), i = 2 * (p % (hd / 2));
+    const float freq = powf(1.0f / theta, (float)i / (float)hd);
+    const float ang = (float)pos * freq;
+    const float c = cosf(ang), s = sinf(ang);
+    float* v = qk + (size_t)h * hd + i;
+    const float a = v[0], b = v[1];
+    v[0] = a * c - b * s;
+    v[1] = a * s + b * c;
+  }
+}
+
+// SwiGLU (engine/src/ops.c:491-496)
+__global__ void swiglu_kernel(const float* g, const float* u, float* h, uint32_t n) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float gt = g[i];
+    const float sig = 1.0f / (1.0f + expf(-gt));
+    h[i] = (gt * sig) * u[i];
+  }
+}
+
+__global__ void add_kernel(float* y, const float* x, uint32_t n) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    y[i] = y[i] + x[i];
+}
+
+}  // namespace
+
+cudaError_t embed_launch(const void* table, uint32_t dtype, const uint32_t* tok, uint32_t n_vocab,
+                         float* out, uint32_t n_embd, int* err, cudaStream_t st) {
+  embed_kernel<<<(n_embd + 255) / 256, 256, 0, st>>>(static_cast<const uint8_t*>(table), dtype, tok,
+                                                     n_vocab, out, n_embd, err);
+  return cudaGetLastError();
+}
+
+int argmax_blocks(uint32_t n) {
+  const uint32_t b = (n + 4095) / 4096;
+  return (int)(b < 1 ? 1 : (b > 148 ? 148 : b));
+}
+
+cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* part_i, int* counter,
+                          uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st) {
+  argmax_kernel<<<argmax_blocks(n), AM_THREADS, 0, st>>>(x, n, part_v, part_i, counter, tok_out,
+                                                         pos_inc);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_launch(const float* x, const float* w, float* y, uint32_t d, cudaStream_t st) {
+  rmsnorm_kernel<<<1, 1024, 0, st>>>(x, w, y, d);
+  return cudaGetLastError();
+}
+
+cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos, float theta,
+                        cudaStream_t st) {
+  const uint32_t pairs = n_heads * (hd / 2);
+  rope_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(qk, n_heads, hd, pos, theta);
+  return cudaGetLastError();
+}
+
+cudaError_t swiglu_launch(const float* g, const float* u, float* h, uint32_t n, cudaStream_t st) {
+  swiglu_kernel<<<(n + 255) / 256, 256, 0, st>>>(g, u, h, n);
+  return cudaGetLastError();
+}
+
+cudaError_t add_launch(float* y, const float* x, uint32_t n, cudaStream_t st) {
+  add_kernel<<<(n + 255) / 256, 256, 0, st>>>(y, x, n);
+  return cudaGetLastError();
+}
+
+}  // namespace shk

@@ -1,0 +1,854 @@
+// shk_cuda.cu -- C ABI (include/shk_cuda.h) over the sm_100a decode kernels.
+#include "../../include/shk_cuda.h"
+
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <new>
+#include <unordered_map>
+#include <vector>
+
+#include "attn.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "glue.cuh"
+
+using namespace shk;
+
+#define CK(expr)                                              \
+  do {                                                        \
+    cudaError_t e_ = (expr);                                  \
+    if (e_ != cudaSuccess) {                                  \
+      fprintf(stderr, "shk_cuda: %s: %s\n", #expr, cudaGetErrorString(e_)); \
+      return SHK_ECUDA;                                       \
+    }                                                         \
+  } while (0)
+
+struct shk_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t compute = nullptr;
+  cudaStream_t copy = nullptr;
+  int* d_err = nullptr;
+  int* h_err = nullptr;  // pinned
+  // op-level scratch
+  uint32_t* d_u32 = nullptr;   // [0] pos for op rope, [1] token for op embed, [2] argmax result
+  uint32_t* h_u32 = nullptr;   // pinned mirror
+  float* am_v = nullptr;
+  uint32_t* am_i = nullptr;
+  int* am_cnt = nullptr;
+  // synchronous host-pointer matvec scratch
+  void* hv_w = nullptr;
+  size_t hv_w_cap = 0;
+  float* hv_x = nullptr;
+  size_t hv_x_cap = 0;
+  float* hv_y = nullptr;
+  size_t hv_y_cap = 0;
+  // staging
+  std::mutex stage_mu;
+  std::unordered_map<uint32_t, cudaEvent_t> slot_ev;
+  // counters (shk_cuda_report)
+  uint64_t n_matvec = 0, n_matvec_host = 0, n_fwd = 0, n_steps = 0, n_staged = 0, bytes_staged = 0;
+};
+
+struct shk_kv {
+  shk_ctx* ctx = nullptr;
+  KvLayout L{};
+  std::vector<uint32_t> seq;
+  float* part = nullptr;
+  int* counters = nullptr;
+  uint32_t max_splits = 1;
+  uint32_t* d_iota = nullptr;  // d_iota[p] == p, used as a device position pointer
+};
+
+namespace {
+
+struct LayerPlans {
+  GemvPlan qkv, o, gateup, down;
+  bool ok = false;
+};
+
+}  // namespace
+
+struct shk_model {
+  shk_ctx* ctx = nullptr;
+  shk_model_desc d{};
+  shk_kv* kv = nullptr;
+  float *hidden = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+        *act = nullptr, *logits = nullptr;
+  uint32_t* d_tok = nullptr;  // [0] token, [1] position
+  uint32_t* h_tok = nullptr;  // pinned: [0] token in, [1] pos in, [2] token out
+  float* am_v = nullptr;
+  uint32_t* am_i = nullptr;
+  int* am_cnt = nullptr;
+  std::vector<shk_layer_desc> layers;
+  std::vector<uint8_t> have;
+  std::vector<LayerPlans> plans;
+  GemvPlan head;
+  bool head_ok = false;
+  cudaGraphExec_t g_layers = nullptr, g_head = nullptr, g_loop = nullptr;
+};
+
+namespace {
+
+int ctx_err_check(shk_ctx* c) {
+  CK(cudaStreamSynchronize(c->compute));
+  CK(cudaMemcpy(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  const int e = *c->h_err;
+  if (e) {
+    CK(cudaMemset(c->d_err, 0, sizeof(int)));
+    return (e == DERR_TIMEOUT_FULL || e == DERR_TIMEOUT_EMPTY) ? SHK_ETIMEOUT : SHK_EDEVICE;
+  }
+  return SHK_OK;
+}
+
+cudaStream_t pick(shk_ctx* c, void* s) { return s ? static_cast<cudaStream_t>(s) : c->compute; }
+
+int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y, uint32_t m,
+               uint32_t k, cudaStream_t st) {
+  if (!w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
+  if (m == 0) return SHK_OK;
+  GemvMat mt{w, nullptr, y, m, qt, 0, EPI_STORE, 0};
+  GemvPlan p;
+  const int rc = gemv_plan(p, &mt, 1, k, x, nullptr, nullptr, 0.f, c->d_err, c->num_sms);
+  if (rc == -2) return SHK_EUNSUPPORTED;
+  if (rc == 0) {
+    CK(gemv_launch(p, st));
+  } else {
+    // rows not 16-byte multiples, unaligned base, or too large for the staged
+    // kernel: plain-load kernel with the same math
+    CK(gemv_generic_launch(qt, w, x, y, m, k, st));
+  }
+  c->n_matvec++;
+  return SHK_OK;
+}
+
+template <typename T>
+int grow(T** p, size_t* cap, size_t need) {
+  if (*cap >= need) return SHK_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  if (cudaMalloc(reinterpret_cast<void**>(p), need) != cudaSuccess) return SHK_ENOMEM;
+  *cap = need;
+  return SHK_OK;
+}
+
+int matvec_host(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y, uint32_t m,
+                uint32_t k) {
+  if (!w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
+  const size_t wb = (size_t)m * (k / QK) * (qt == T_Q4K ? Q4K_BYTES : Q6K_BYTES);
+  int rc;
+  if ((rc = grow(&c->hv_w, &c->hv_w_cap, wb)) || (rc = grow(&c->hv_x, &c->hv_x_cap, (size_t)k * 4)) ||
+      (rc = grow(&c->hv_y, &c->hv_y_cap, (size_t)m * 4)))
+    return rc;
+  CK(cudaMemcpyAsync(c->hv_w, w, wb, cudaMemcpyHostToDevice, c->compute));
+  CK(cudaMemcpyAsync(c->hv_x, x, (size_t)k * 4, cudaMemcpyHostToDevice, c->compute));
+  rc = matvec_dev(c, qt, c->hv_w, c->hv_x, c->hv_y, m, k, c->compute);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(y, c->hv_y, (size_t)m * 4, cudaMemcpyDeviceToHost, c->compute));
+  CK(cudaStreamSynchronize(c->compute));
+  c->n_matvec_host++;
+  return ctx_err_check(c);
+}
+
+}  // namespace
+
+extern "C" {
+
+int shk_cuda_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n > 0;
+}
+
+const char* shk_cuda_strerror(int s) {
+  switch (s) {
+    case SHK_OK: return "ok";
+    case SHK_EINVAL: return "invalid argument";
+    case SHK_ENOMEM: return "out of memory";
+    case SHK_ECUDA: return "CUDA runtime error";
+    case SHK_EUNSUPPORTED: return "unsupported dtype or shape";
+    case SHK_ETIMEOUT: return "bounded device wait ran out";
+    case SHK_ENODEV: return "no CUDA device";
+    case SHK_ENCCL: return "collective failure";
+    case SHK_EDEVICE: return "kernel reported an error";
+    default: return "unknown";
+  }
+}
+
+shk_ctx* shk_cuda_init(const shk_cuda_config* cfg) {
+  if (!shk_cuda_available()) return nullptr;
+  shk_ctx* c = new (std::nothrow) shk_ctx();
+  if (!c) return nullptr;
+  int dev = cfg ? cfg->device : -1;
+  if (dev < 0) {
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  }
+  c->device = dev;
+  bool ok = cudaSetDevice(dev) == cudaSuccess;
+  ok = ok && cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess;
+  ok = ok && cudaStreamCreateWithFlags(&c->compute, cudaStreamNonBlocking) == cudaSuccess;
+  ok = ok && cudaStreamCreateWithFlags(&c->copy, cudaStreamNonBlocking) == cudaSuccess;
+  ok = ok && cudaMalloc(&c->d_err, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMemset(c->d_err, 0, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&c->h_err, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMalloc(&c->d_u32, 16 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&c->h_u32, 16 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMalloc(&c->am_v, 256 * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMalloc(&c->am_i, 256 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMalloc(&c->am_cnt, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMemset(c->am_cnt, 0, sizeof(int)) == cudaSuccess;
+  ok = ok && gemv_init() == cudaSuccess;
+  if (!ok) {
+    shk_cuda_shutdown(c);
+    return nullptr;
+  }
+  return c;
+}
+
+void shk_cuda_shutdown(shk_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->compute) cudaStreamSynchronize(c->compute);
+  if (c->copy) cudaStreamSynchronize(c->copy);
+  for (auto& kv : c->slot_ev) cudaEventDestroy(kv.second);
+  cudaFree(c->d_err);
+  cudaFreeHost(c->h_err);
+  cudaFree(c->d_u32);
+  cudaFreeHost(c->h_u32);
+  cudaFree(c->am_v);
+  cudaFree(c->am_i);
+  cudaFree(c->am_cnt);
+  cudaFree(c->hv_w);
+  cudaFree(c->hv_x);
+  cudaFree(c->hv_y);
+  if (c->compute) cudaStreamDestroy(c->compute);
+  if (c->copy) cudaStreamDestroy(c->copy);
+  delete c;
+}
+
+void shk_cuda_report(shk_ctx* c) {
+  if (!c) return;
+  fprintf(stderr,
+          "shk_cuda: device=%d sms=%d matvec_calls=%llu matvec_host_calls=%llu layer_forwards=%llu "
+          "token_steps=%llu staged_copies=%llu staged_bytes=%llu\n",
+          c->device, c->num_sms, (unsigned long long)c->n_matvec,
+          (unsigned long long)c->n_matvec_host, (unsigned long long)c->n_fwd,
+          (unsigned long long)c->n_steps, (unsigned long long)c->n_staged,
+          (unsigned long long)c->bytes_staged);
+}
+
+int shk_cuda_check(shk_ctx* c) {
+  if (!c) return SHK_EINVAL;
+  return ctx_err_check(c);
+}
+
+void* shk_cuda_stream(shk_ctx* c) { return c ? c->compute : nullptr; }
+int shk_cuda_num_sms(shk_ctx* c) { return c ? c->num_sms : 0; }
+
+int shk_cuda_dev_alloc(shk_ctx* c, size_t bytes, void** out) {
+  if (!c || !out) return SHK_EINVAL;
+  *out = nullptr;
+  return cudaMalloc(out, bytes ? bytes : 1) == cudaSuccess ? SHK_OK : SHK_ENOMEM;
+}
+int shk_cuda_dev_free(shk_ctx* c, void* p) {
+  (void)c;
+  return cudaFree(p) == cudaSuccess ? SHK_OK : SHK_ECUDA;
+}
+int shk_cuda_host_alloc(shk_ctx* c, size_t bytes, void** out) {
+  if (!c || !out) return SHK_EINVAL;
+  *out = nullptr;
+  return cudaMallocHost(out, bytes ? bytes : 1) == cudaSuccess ? SHK_OK : SHK_ENOMEM;
+}
+int shk_cuda_host_free(shk_ctx* c, void* p) {
+  (void)c;
+  return cudaFreeHost(p) == cudaSuccess ? SHK_OK : SHK_ECUDA;
+}
+int shk_cuda_memcpy_h2d(shk_ctx* c, void* dst, const void* src, size_t bytes, void* s) {
+  if (!c) return SHK_EINVAL;
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, pick(c, s)));
+  return SHK_OK;
+}
+int shk_cuda_memcpy_d2h(shk_ctx* c, void* dst, const void* src, size_t bytes, void* s) {
+  if (!c) return SHK_EINVAL;
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, pick(c, s)));
+  return SHK_OK;
+}
+int shk_cuda_sync(shk_ctx* c, void* s) {
+  if (!c) return SHK_EINVAL;
+  CK(cudaStreamSynchronize(pick(c, s)));
+  return SHK_OK;
+}
+
+int shk_cuda_matmul_q4k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
+                            uint32_t k, void* s) {
+  if (!c) return SHK_EINVAL;
+  return matvec_dev(c, T_Q4K, w, x, y, m, k, pick(c, s));
+}
+int shk_cuda_matmul_q6k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
+                            uint32_t k, void* s) {
+  if (!c) return SHK_EINVAL;
+  return matvec_dev(c, T_Q6K, w, x, y, m, k, pick(c, s));
+}
+int shk_cuda_matmul_q4k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
+                                 uint32_t k) {
+  if (!c) return SHK_EINVAL;
+  return matvec_host(c, T_Q4K, w, x, y, m, k);
+}
+int shk_cuda_matmul_q6k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
+                                 uint32_t k) {
+  if (!c) return SHK_EINVAL;
+  return matvec_host(c, T_Q6K, w, x, y, m, k);
+}
+
+int shk_cuda_rmsnorm(shk_ctx* c, const float* x, const float* w, float* y, uint32_t d, void* s) {
+  if (!c || !x || !w || !y || !d) return SHK_EINVAL;
+  CK(rmsnorm_launch(x, w, y, d, pick(c, s)));
+  return SHK_OK;
+}
+
+int shk_cuda_rope(shk_ctx* c, float* qk, uint32_t n_heads, uint32_t hd, uint32_t pos, float theta,
+                  void* s) {
+  if (!c || !qk || hd == 0 || (hd & 1)) return SHK_EINVAL;
+  cudaStream_t st = pick(c, s);
+  // position goes through a stream-ordered copy so the call stays async
+  CK(cudaStreamSynchronize(st));
+  c->h_u32[0] = pos;
+  CK(cudaMemcpyAsync(c->d_u32, c->h_u32, 4, cudaMemcpyHostToDevice, st));
+  CK(rope_launch(qk, n_heads, hd, c->d_u32, theta, st));
+  return SHK_OK;
+}
+
+int shk_cuda_swiglu(shk_ctx* c, const float* g, const float* u, float* h, uint32_t n, void* s) {
+  if (!c || !g || !u || !h) return SHK_EINVAL;
+  CK(swiglu_launch(g, u, h, n, pick(c, s)));
+  return SHK_OK;
+}
+
+int shk_cuda_embed(shk_ctx* c, const void* table, uint32_t dtype, uint32_t n_vocab, uint32_t token,
+                   float* out, uint32_t n_embd, void* s) {
+  if (!c || !table || !out || !n_embd) return SHK_EINVAL;
+  if (dtype != 1 && dtype != T_Q4K) return SHK_EUNSUPPORTED;
+  if (dtype == T_Q4K && n_embd % QK) return SHK_EINVAL;
+  if (token >= n_vocab) return SHK_EINVAL;
+  cudaStream_t st = pick(c, s);
+  CK(cudaStreamSynchronize(st));
+  c->h_u32[1] = token;
+  CK(cudaMemcpyAsync(c->d_u32 + 1, c->h_u32 + 1, 4, cudaMemcpyHostToDevice, st));
+  CK(embed_launch(table, dtype, c->d_u32 + 1, n_vocab, out, n_embd, c->d_err, st));
+  return SHK_OK;
+}
+
+int shk_cuda_argmax(shk_ctx* c, const float* x, uint32_t n, uint32_t* out) {
+  if (!c || !x || !out || !n) return SHK_EINVAL;
+  CK(argmax_launch(x, n, c->am_v, c->am_i, c->am_cnt, c->d_u32 + 2, nullptr, c->compute));
+  CK(cudaMemcpyAsync(c->h_u32 + 2, c->d_u32 + 2, 4, cudaMemcpyDeviceToHost, c->compute));
+  CK(cudaStreamSynchronize(c->compute));
+  *out = c->h_u32[2];
+  return SHK_OK;
+}
+
+// ------------------------------- KV cache -------------------------------------
+
+shk_kv* shk_cuda_kv_create(shk_ctx* c, const shk_kv_config* cfg) {
+  if (!c || !cfg || !cfg->n_layers || !cfg->n_kv_heads || !cfg->max_seq_len) return nullptr;
+  if (cfg->head_dim != 64 && cfg->head_dim != 128) return nullptr;
+  shk_kv* kv = new (std::nothrow) shk_kv();
+  if (!kv) return nullptr;
+  kv->ctx = c;
+  kv->L = kv_layout_make(cfg->n_layers, cfg->n_kv_heads, cfg->head_dim, cfg->max_seq_len);
+  kv->seq.assign(cfg->n_layers, 0);
+  // split-K fan-out: about two CTAs per SM across the KV heads
+  kv->max_splits = std::max<uint32_t>(1, std::min<uint32_t>(64, (2 * c->num_sms + cfg->n_kv_heads - 1) / cfg->n_kv_heads));
+  const size_t bytes = kv->L.head_bytes * cfg->n_layers * cfg->n_kv_heads;
+  // partials sized for up to 8 query heads per KV head
+  const size_t part = attn_part_floats(8 * cfg->n_kv_heads, cfg->n_kv_heads, cfg->head_dim, kv->max_splits);
+  bool ok = cudaMalloc(&kv->L.base, bytes) == cudaSuccess;
+  ok = ok && cudaMemset(kv->L.base, 0, bytes) == cudaSuccess;
+  ok = ok && cudaMalloc(&kv->part, part * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMalloc(&kv->counters, cfg->n_kv_heads * sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMemset(kv->counters, 0, cfg->n_kv_heads * sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMalloc(&kv->d_iota, (size_t)cfg->max_seq_len * sizeof(uint32_t)) == cudaSuccess;
+  if (ok) {
+    std::vector<uint32_t> io(cfg->max_seq_len);
+    for (uint32_t i = 0; i < cfg->max_seq_len; ++i) io[i] = i;
+    ok = cudaMemcpy(kv->d_iota, io.data(), io.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  }
+  if (!ok) {
+    shk_cuda_kv_destroy(kv);
+    return nullptr;
+  }
+  return kv;
+}
+
+void shk_cuda_kv_destroy(shk_kv* kv) {
+  if (!kv) return;
+  if (kv->ctx) cudaStreamSynchronize(kv->ctx->compute);
+  cudaFree(kv->L.base);
+  cudaFree(kv->part);
+  cudaFree(kv->counters);
+  cudaFree(kv->d_iota);
+  delete kv;
+}
+
+int shk_cuda_kv_append(shk_kv* kv, uint32_t layer, uint32_t pos, const float* k, const float* v,
+                       void* s) {
+  if (!kv || !k || !v || layer >= kv->L.n_layers || pos >= kv->L.max_seq) return SHK_EINVAL;
+  CK(kv_append_launch(kv->L, layer, kv->d_iota + pos, k, v, kv->ctx->d_err, pick(kv->ctx, s)));
+  kv->seq[layer] = std::max(kv->seq[layer], pos + 1);
+  return SHK_OK;
+}
+
+int shk_cuda_kv_read_range(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t end, float* k,
+                           float* v, void* s) {
+  if (!kv || !k || !v || end < start || layer >= kv->L.n_layers || end > kv->L.max_seq)
+    return SHK_EINVAL;
+  CK(kv_read_range_launch(kv->L, layer, start, end, k, v, pick(kv->ctx, s)));
+  return SHK_OK;
+}
+
+int shk_cuda_kv_read_blocks(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t end, void* k,
+                            void* v, void* s) {
+  if (!kv || !k || !v || end < start || layer >= kv->L.n_layers || end > kv->L.max_seq)
+    return SHK_EINVAL;
+  CK(kv_read_blocks_launch(kv->L, layer, start, end, static_cast<uint8_t*>(k),
+                           static_cast<uint8_t*>(v), pick(kv->ctx, s)));
+  return SHK_OK;
+}
+
+int shk_cuda_kv_attend(shk_kv* kv, uint32_t layer, const float* q, const float* k_new,
+                       const float* v_new, float* out, uint32_t n_heads, uint32_t seq_len,
+                       float scale, void* s) {
+  if (!kv || !q || !out || layer >= kv->L.n_layers || seq_len == 0 || seq_len > kv->L.max_seq)
+    return SHK_EINVAL;
+  if (n_heads % kv->L.n_kv || n_heads / kv->L.n_kv > 8) return SHK_EUNSUPPORTED;
+  if ((k_new == nullptr) != (v_new == nullptr)) return SHK_EINVAL;
+  AttnArgs a{};
+  a.kv = kv->L;
+  a.layer = layer;
+  a.n_heads = n_heads;
+  a.scale = scale;
+  a.q = q;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.pos = kv->d_iota + (seq_len - 1);
+  a.out = out;
+  a.part = kv->part;
+  a.counters = kv->counters;
+  a.max_splits = kv->max_splits;
+  a.min_per_split = 64;
+  a.err = kv->ctx->d_err;
+  CK(attn_decode_launch(a, pick(kv->ctx, s)));
+  if (k_new) kv->seq[layer] = std::max(kv->seq[layer], seq_len);
+  return SHK_OK;
+}
+
+void shk_cuda_kv_clear(shk_kv* kv) {
+  if (kv) std::fill(kv->seq.begin(), kv->seq.end(), 0u);
+}
+
+uint32_t shk_cuda_kv_seq_len(shk_kv* kv, uint32_t layer) {
+  return (kv && layer < kv->L.n_layers) ? kv->seq[layer] : 0;
+}
+
+// --------------------------------- model --------------------------------------
+
+namespace {
+
+void model_free_graphs(shk_model* m) {
+  if (m->g_layers) cudaGraphExecDestroy(m->g_layers);
+  if (m->g_head) cudaGraphExecDestroy(m->g_head);
+  if (m->g_loop) cudaGraphExecDestroy(m->g_loop);
+  m->g_layers = m->g_head = m->g_loop = nullptr;
+}
+
+int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
+  const shk_model_desc& d = m->d;
+  shk_ctx* c = m->ctx;
+  const uint32_t hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+  const uint32_t* pos = m->d_tok + 1;
+  GemvMat qkv[3] = {
+      {lv.attn_q, nullptr, m->q, qd, lv.attn_q_dtype, 0, EPI_ROPE, hd},
+      {lv.attn_k, nullptr, m->k, kvd, lv.attn_k_dtype, 0, EPI_ROPE, hd},
+      {lv.attn_v, nullptr, m->v, kvd, lv.attn_v_dtype, lv.row_stride_v, EPI_STORE, 0},
+  };
+  const float theta = d.rope_theta > 0.f ? d.rope_theta : 10000.0f;
+  int rc = gemv_plan(P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos, theta, c->d_err, c->num_sms);
+  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  GemvMat o{lv.attn_o, nullptr, m->hidden, d.n_embd, lv.attn_o_dtype, 0, EPI_ADD, 0};
+  rc = gemv_plan(P.o, &o, 1, qd, m->att, nullptr, nullptr, 0.f, c->d_err, c->num_sms);
+  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  if (lv.ffn_gate_dtype != lv.ffn_up_dtype) return SHK_EUNSUPPORTED;
+  GemvMat gu{lv.ffn_gate, lv.ffn_up, m->act, d.n_ff, lv.ffn_gate_dtype, 0, EPI_SWIGLU, 0};
+  rc = gemv_plan(P.gateup, &gu, 1, d.n_embd, m->hidden, lv.ffn_norm, nullptr, 0.f, c->d_err, c->num_sms);
+  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, EPI_ADD, 0};
+  rc = gemv_plan(P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr, 0.f, c->d_err, c->num_sms);
+  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  P.ok = true;
+  return SHK_OK;
+}
+
+// Enqueues one layer: fused RMSNorm+QKV(+RoPE), append+attention, O(+residual),
+// RMSNorm+gate/up(+SwiGLU), down(+residual).  `pos` is a device pointer.
+int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint32_t* pos,
+                  cudaStream_t st) {
+  GemvPlan qkv = P.qkv;
+  qkv.args.pos = pos;
+  CK(gemv_launch(qkv, st));
+  AttnArgs a{};
+  a.kv = m->kv->L;
+  a.layer = layer;
+  a.n_heads = m->d.n_heads;
+  a.scale = 1.0f / sqrtf((float)m->d.head_dim);
+  a.q = m->q;
+  a.k_new = m->k;
+  a.v_new = m->v;
+  a.pos = pos;
+  a.out = m->att;
+  a.part = m->kv->part;
+  a.counters = m->kv->counters;
+  a.max_splits = m->kv->max_splits;
+  a.min_per_split = 64;
+  a.err = m->ctx->d_err;
+  CK(attn_decode_launch(a, st));
+  CK(gemv_launch(P.o, st));
+  CK(gemv_launch(P.gateup, st));
+  CK(gemv_launch(P.down, st));
+  return SHK_OK;
+}
+
+int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos) {
+  CK(gemv_launch(m->head, st));
+  CK(argmax_launch(m->logits, m->d.n_vocab, m->am_v, m->am_i, m->am_cnt, m->d_tok,
+                   advance_pos ? m->d_tok + 1 : nullptr, st));
+  return SHK_OK;
+}
+
+int enqueue_layers(shk_model* m, cudaStream_t st) {
+  CK(embed_launch(m->d.tok_embd_dev, m->d.tok_embd_dtype, m->d_tok, m->d.n_vocab, m->hidden,
+                  m->d.n_embd, m->ctx->d_err, st));
+  for (uint32_t l = 0; l < m->d.n_layers; ++l) {
+    const int rc = enqueue_layer(m, m->plans[l], l, m->d_tok + 1, st);
+    if (rc) return rc;
+  }
+  return SHK_OK;
+}
+
+int capture(shk_model* m, int which, cudaGraphExec_t* out) {
+  cudaStream_t st = m->ctx->compute;
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  // 0: embed + all layers;  1: lm_head + argmax;  2: both, argmax advancing *pos
+  int rc = which == 1 ? SHK_OK : enqueue_layers(m, st);
+  if (!rc && which != 0) rc = enqueue_head(m, st, which == 2);
+  const cudaError_t ee = cudaStreamEndCapture(st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ee != cudaSuccess) return SHK_ECUDA;
+  const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  return ie == cudaSuccess ? SHK_OK : SHK_ECUDA;
+}
+
+bool model_ready(shk_model* m) {
+  for (uint32_t l = 0; l < m->d.n_layers; ++l)
+    if (!m->have[l] || !m->plans[l].ok) return false;
+  return m->head_ok;
+}
+
+}  // namespace
+
+shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv) {
+  if (!c || !d || !kv) return nullptr;
+  if (!d->n_layers || !d->n_embd || !d->n_heads || !d->n_kv_heads || !d->n_ff || !d->n_vocab)
+    return nullptr;
+  if (d->head_dim * d->n_heads != d->n_embd || kv->L.hd != d->head_dim ||
+      kv->L.n_kv != d->n_kv_heads || kv->L.n_layers != d->n_layers)
+    return nullptr;
+  shk_model* m = new (std::nothrow) shk_model();
+  if (!m) return nullptr;
+  m->ctx = c;
+  m->d = *d;
+  m->kv = kv;
+  const uint32_t qd = d->n_heads * d->head_dim, kvd = d->n_kv_heads * d->head_dim;
+  bool ok = true;
+  auto A = [&](float** p, size_t n) { ok = ok && cudaMalloc(p, n * sizeof(float)) == cudaSuccess; };
+  A(&m->hidden, d->n_embd);
+  A(&m->q, qd);
+  A(&m->k, kvd);
+  A(&m->v, kvd);
+  A(&m->att, qd);
+  A(&m->act, d->n_ff);
+  A(&m->logits, d->n_vocab);
+  A(&m->am_v, 256);
+  ok = ok && cudaMalloc(&m->am_i, 256 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMalloc(&m->am_cnt, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMemset(m->am_cnt, 0, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMalloc(&m->d_tok, 4 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMemset(m->d_tok, 0, 4 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&m->h_tok, 4 * sizeof(uint32_t)) == cudaSuccess;
+  if (ok) ok = cudaMemset(m->hidden, 0, d->n_embd * sizeof(float)) == cudaSuccess;
+  if (!ok) {
+    shk_cuda_model_destroy(m);
+    return nullptr;
+  }
+  m->layers.resize(d->n_layers);
+  m->have.assign(d->n_layers, 0);
+  m->plans.resize(d->n_layers);
+  GemvMat hm{d->output_dev, nullptr, m->logits, d->n_vocab, d->output_dtype, 0, EPI_STORE, 0};
+  m->head_ok = gemv_plan(m->head, &hm, 1, d->n_embd, m->hidden, nullptr, nullptr, 0.f, c->d_err,
+                         c->num_sms) == 0;
+  return m;
+}
+
+void shk_cuda_model_destroy(shk_model* m) {
+  if (!m) return;
+  if (m->ctx) cudaStreamSynchronize(m->ctx->compute);
+  model_free_graphs(m);
+  cudaFree(m->hidden);
+  cudaFree(m->q);
+  cudaFree(m->k);
+  cudaFree(m->v);
+  cudaFree(m->att);
+  cudaFree(m->act);
+  cudaFree(m->logits);
+  cudaFree(m->am_v);
+  cudaFree(m->am_i);
+  cudaFree(m->am_cnt);
+  cudaFree(m->d_tok);
+  cudaFreeHost(m->h_tok);
+  delete m;
+}
+
+float* shk_cuda_model_hidden(shk_model* m) { return m ? m->hidden : nullptr; }
+
+int shk_cuda_model_set_layer(shk_model* m, uint32_t layer, const shk_layer_desc* lv) {
+  if (!m || !lv || layer >= m->d.n_layers) return SHK_EINVAL;
+  LayerPlans P;
+  const int rc = build_layer_plans(m, *lv, P);
+  if (rc) return rc;
+  m->layers[layer] = *lv;
+  m->plans[layer] = P;
+  m->have[layer] = 1;
+  model_free_graphs(m);
+  return SHK_OK;
+}
+
+int shk_cuda_forward_layer(shk_model* m, const shk_layer_desc* lv, uint32_t layer, uint32_t pos,
+                           float* hidden, void* s) {
+  if (!m || !lv || !hidden || layer >= m->d.n_layers || pos >= m->kv->L.max_seq) return SHK_EINVAL;
+  cudaStream_t st = pick(m->ctx, s);
+  LayerPlans P;
+  int rc = build_layer_plans(m, *lv, P);
+  if (rc) return rc;
+  if (hidden != m->hidden) CK(cudaMemcpyAsync(m->hidden, hidden, m->d.n_embd * 4, cudaMemcpyDeviceToDevice, st));
+  rc = enqueue_layer(m, P, layer, m->kv->d_iota + pos, st);
+  if (rc) return rc;
+  if (hidden != m->hidden) CK(cudaMemcpyAsync(hidden, m->hidden, m->d.n_embd * 4, cudaMemcpyDeviceToDevice, st));
+  m->kv->seq[layer] = std::max(m->kv->seq[layer], pos + 1);
+  m->ctx->n_fwd++;
+  return SHK_OK;
+}
+
+int shk_cuda_model_embed(shk_model* m, uint32_t token, void* s) {
+  if (!m) return SHK_EINVAL;
+  if (token >= m->d.n_vocab) return SHK_EINVAL;
+  cudaStream_t st = pick(m->ctx, s);
+  CK(cudaStreamSynchronize(st));
+  m->h_tok[0] = token;
+  CK(cudaMemcpyAsync(m->d_tok, m->h_tok, 4, cudaMemcpyHostToDevice, st));
+  CK(embed_launch(m->d.tok_embd_dev, m->d.tok_embd_dtype, m->d_tok, m->d.n_vocab, m->hidden,
+                  m->d.n_embd, m->ctx->d_err, st));
+  return SHK_OK;
+}
+
+int shk_cuda_model_lm_head(shk_model* m, uint32_t* token, float* logits, void* s) {
+  if (!m || !m->head_ok) return SHK_EINVAL;
+  cudaStream_t st = pick(m->ctx, s);
+  int rc = enqueue_head(m, st, false);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, st));
+  if (logits) CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->d.n_vocab * 4, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (token) *token = m->h_tok[2];
+  return ctx_err_check(m->ctx);
+}
+
+int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_next, uint32_t* next,
+                        float* logits) {
+  if (!m || token >= m->d.n_vocab || pos >= m->kv->L.max_seq) return SHK_EINVAL;
+  if (!model_ready(m)) return SHK_EINVAL;
+  cudaStream_t st = m->ctx->compute;
+  int rc;
+  if (!m->g_layers && (rc = capture(m, 0, &m->g_layers))) return rc;
+  if (!m->g_head && (rc = capture(m, 1, &m->g_head))) return rc;
+  CK(cudaStreamSynchronize(st));  // h_tok is reused below
+  m->h_tok[0] = token;
+  m->h_tok[1] = pos;
+  CK(cudaMemcpyAsync(m->d_tok, m->h_tok, 8, cudaMemcpyHostToDevice, st));
+  CK(cudaGraphLaunch(m->g_layers, st));
+  if (want_next) {
+    CK(cudaGraphLaunch(m->g_head, st));
+    CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, st));
+    if (logits) CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->d.n_vocab * 4, cudaMemcpyDeviceToHost, st));
+  }
+  CK(cudaStreamSynchronize(st));
+  for (uint32_t l = 0; l < m->d.n_layers; ++l) m->kv->seq[l] = std::max(m->kv->seq[l], pos + 1);
+  m->ctx->n_steps++;
+  rc = ctx_err_check(m->ctx);
+  if (rc) return rc;
+  if (want_next && next) *next = m->h_tok[2];
+  return SHK_OK;
+}
+
+int shk_cuda_decode_steps(shk_model* m, uint32_t first_token, uint32_t first_pos, uint32_t n,
+                          void* s) {
+  if (!m || first_token >= m->d.n_vocab || (uint64_t)first_pos + n > m->kv->L.max_seq) return SHK_EINVAL;
+  if (!model_ready(m)) return SHK_EINVAL;
+  cudaStream_t st = pick(m->ctx, s);
+  int rc;
+  if (!m->g_layers && (rc = capture(m, 0, &m->g_layers))) return rc;
+  if (!m->g_head && (rc = capture(m, 1, &m->g_head))) return rc;
+  CK(cudaStreamSynchronize(st));
+  m->h_tok[0] = first_token;
+  m->h_tok[1] = first_pos;
+  CK(cudaMemcpyAsync(m->d_tok, m->h_tok, 8, cudaMemcpyHostToDevice, st));
+  // Each step: embed(*tok) + layers at *pos, then lm_head + argmax writes the
+  // next token and advances *pos.  No host round trip between steps.
+  if (!m->g_loop && (rc = capture(m, 2, &m->g_loop))) return rc;
+  for (uint32_t i = 0; i < n; ++i) CK(cudaGraphLaunch(m->g_loop, st));
+  for (uint32_t l = 0; l < m->d.n_layers; ++l)
+    m->kv->seq[l] = std::max(m->kv->seq[l], first_pos + n);
+  m->ctx->n_steps += n;
+  return SHK_OK;
+}
+
+int shk_cuda_model_token(shk_model* m, uint32_t* token) {
+  if (!m || !token) return SHK_EINVAL;
+  CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, m->ctx->compute));
+  CK(cudaStreamSynchronize(m->ctx->compute));
+  *token = m->h_tok[2];
+  return ctx_err_check(m->ctx);
+}
+
+int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void* s,
+                               uint64_t* bytes_out) {
+  if (!m || part > 5 || (part < 5 && (layer >= m->d.n_layers || !m->have[layer] || !m->plans[layer].ok)))
+    return SHK_EINVAL;
+  cudaStream_t st = pick(m->ctx, s);
+  auto wbytes = [](const GemvPlan& p) {
+    uint64_t b = 0;
+    for (uint32_t i = 0; i < p.args.nseg; ++i) {
+      const GemvSeg& g = p.args.seg[i];
+      const uint64_t bb = g.qt == T_Q4K ? Q4K_BYTES : Q6K_BYTES;
+      b += (uint64_t)g.m * g.nb * bb * (g.dual ? 2 : 1);
+    }
+    return b;
+  };
+  uint64_t bytes = 0;
+  if (part == 5) {
+    if (!m->head_ok) return SHK_EINVAL;
+    CK(gemv_launch(m->head, st));
+    bytes = wbytes(m->head);
+  } else if (part == 1) {
+    AttnArgs a{};
+    a.kv = m->kv->L;
+    a.layer = layer;
+    a.n_heads = m->d.n_heads;
+    a.scale = 1.0f / sqrtf((float)m->d.head_dim);
+    a.q = m->q;
+    a.k_new = nullptr;  // read-only: attend over [0, *pos] without appending
+    a.v_new = nullptr;
+    a.pos = m->d_tok + 1;
+    a.out = m->att;
+    a.part = m->kv->part;
+    a.counters = m->kv->counters;
+    a.max_splits = m->kv->max_splits;
+    a.min_per_split = 64;
+    a.err = m->ctx->d_err;
+    CK(attn_decode_launch(a, st));
+  } else {
+    const LayerPlans& P = m->plans[layer];
+    const GemvPlan* p = part == 0 ? &P.qkv : part == 2 ? &P.o : part == 3 ? &P.gateup : &P.down;
+    CK(gemv_launch(*p, st));
+    bytes = wbytes(*p);
+  }
+  if (bytes_out) *bytes_out = bytes;
+  return SHK_OK;
+}
+
+// ------------------------------- staging ---------------------------------------
+
+static cudaEvent_t slot_event(shk_ctx* c, uint32_t slot) {
+  std::lock_guard<std::mutex> g(c->stage_mu);
+  auto it = c->slot_ev.find(slot);
+  if (it != c->slot_ev.end()) return it->second;
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  c->slot_ev[slot] = e;
+  return e;
+}
+
+int shk_cuda_layer_stage(shk_ctx* c, uint32_t slot, void* dst, const void* src, size_t bytes) {
+  if (!c || !dst || !src) return SHK_EINVAL;
+  (void)slot;
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->copy));
+  {
+    std::lock_guard<std::mutex> g(c->stage_mu);
+    c->n_staged++;
+    c->bytes_staged += bytes;
+  }
+  return SHK_OK;
+}
+
+int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_row,
+                              const void* src, size_t src_row, size_t rows) {
+  if (!c || !dst || !src || dst_row < src_row) return SHK_EINVAL;
+  (void)slot;
+  CK(cudaMemcpy2DAsync(dst, dst_row, src, src_row, src_row, rows, cudaMemcpyHostToDevice, c->copy));
+  {
+    std::lock_guard<std::mutex> g(c->stage_mu);
+    c->n_staged++;
+    c->bytes_staged += src_row * rows;
+  }
+  return SHK_OK;
+}
+
+int shk_cuda_layer_commit(shk_ctx* c, uint32_t slot) {
+  if (!c) return SHK_EINVAL;
+  cudaEvent_t e = slot_event(c, slot);
+  if (!e) return SHK_ECUDA;
+  CK(cudaEventRecord(e, c->copy));
+  return SHK_OK;
+}
+
+int shk_cuda_layer_ready(shk_ctx* c, uint32_t slot, int wait) {
+  if (!c) return SHK_EINVAL;
+  cudaEvent_t e = slot_event(c, slot);
+  if (!e) return SHK_ECUDA;
+  if (wait) {
+    CK(cudaEventSynchronize(e));
+    return 1;
+  }
+  const cudaError_t q = cudaEventQuery(e);
+  if (q == cudaSuccess) return 1;
+  if (q == cudaErrorNotReady) return 0;
+  return SHK_ECUDA;
+}
+
+int shk_cuda_layer_wait(shk_ctx* c, uint32_t slot, void* s) {
+  if (!c) return SHK_EINVAL;
+  cudaEvent_t e = slot_event(c, slot);
+  if (!e) return SHK_ECUDA;
+  CK(cudaStreamWaitEvent(pick(c, s), e, 0));
+  return SHK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,182 @@
+"""Seeded synthetic K-quant tensors and llama-shaped models.
+
+The value distributions follow the benchmark description of the decode path:
+
+* Q4_K super-blocks (144 B): fp16 ``d`` and ``dmin`` ~ |N(0, 0.002)|, 12 uniform
+  scale bytes, 128 uniform quant bytes.
+* Q6_K super-blocks (210 B): 128 B ``ql`` + 64 B ``qh`` uniform, 16 int8 scales
+  uniform in [-32, 31], fp16 ``d`` ~ |N(0, 0.0005)|.
+* Norm weights: fp32 1 + N(0, 0.02).
+
+Subnormal fp16 scales are kept on purpose: the reference decodes them at half
+their IEEE value (engine/src/ops.c:65-78) and the GPU path must match that.
+"""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+
+import numpy as np
+
+QK = 256
+Q4K_BYTES = 144
+Q6K_BYTES = 210
+T_F32, T_F16, T_Q4K, T_Q6K = 0, 1, 12, 14
+BLOCK_BYTES = {T_Q4K: Q4K_BYTES, T_Q6K: Q6K_BYTES}
+
+
+def q4k_blocks(rng: np.random.Generator, n_blocks: int, d_sigma: float = 0.002) -> np.ndarray:
+    """n_blocks Q4_K super-blocks as a (n_blocks, 144) uint8 array."""
+    b = rng.integers(0, 256, size=(n_blocks, Q4K_BYTES), dtype=np.uint8)
+    d = np.abs(rng.normal(0.0, d_sigma, size=(n_blocks, 2))).astype(np.float16)
+    b[:, 0:4] = d.view(np.uint8).reshape(n_blocks, 4)
+    return b
+
+
+def q6k_blocks(rng: np.random.Generator, n_blocks: int, d_sigma: float = 0.0005) -> np.ndarray:
+    """n_blocks Q6_K super-blocks as a (n_blocks, 210) uint8 array."""
+    b = rng.integers(0, 256, size=(n_blocks, Q6K_BYTES), dtype=np.uint8)
+    sc = rng.integers(-32, 32, size=(n_blocks, 16), dtype=np.int8)
+    b[:, 192:208] = sc.view(np.uint8)
+    d = np.abs(rng.normal(0.0, d_sigma, size=(n_blocks, 1))).astype(np.float16)
+    b[:, 208:210] = d.view(np.uint8).reshape(n_blocks, 2)
+    return b
+
+
+def quant_matrix(rng: np.random.Generator, qtype: int, rows: int, cols: int) -> np.ndarray:
+    """A rows x cols matrix in GGUF row-major block layout (flat uint8)."""
+    assert cols % QK == 0
+    nb = rows * (cols // QK)
+    blocks = q4k_blocks(rng, nb) if qtype == T_Q4K else q6k_blocks(rng, nb)
+    return blocks.reshape(-1)
+
+
+def norm_weight(rng: np.random.Generator, n: int) -> np.ndarray:
+    return (1.0 + rng.normal(0.0, 0.02, size=n)).astype(np.float32)
+
+
+@dataclasses.dataclass
+class ModelShape:
+    name: str
+    n_layers: int
+    n_embd: int
+    n_heads: int
+    n_kv_heads: int
+    n_ff: int
+    n_vocab: int
+    # quant types per tensor (Q4_K_M mix: attn_v, ffn_down, output in Q6_K)
+    t_q: int = T_Q4K
+    t_k: int = T_Q4K
+    t_v: int = T_Q6K
+    t_o: int = T_Q4K
+    t_gate: int = T_Q4K
+    t_up: int = T_Q4K
+    t_down: int = T_Q6K
+    t_embd: int = T_Q4K
+    t_out: int = T_Q6K
+
+    @property
+    def head_dim(self) -> int:
+        return self.n_embd // self.n_heads
+
+
+SHAPES = {
+    # TinyLlama-1.1B shape
+    "tinyllama": ModelShape("tinyllama-1.1b-shape", 22, 2048, 32, 4, 5632, 32000),
+    # Llama-3.1-8B shape
+    "llama8b": ModelShape("llama-3.1-8b-shape", 32, 4096, 32, 8, 14336, 128256),
+    # Llama-3.3-70B shape
+    "llama70b": ModelShape("llama-3.3-70b-shape", 80, 8192, 64, 8, 28672, 128256),
+    # small shapes for fast tests
+    "tiny": ModelShape("tiny", 2, 256, 4, 2, 512, 1000),
+    "small": ModelShape("small", 3, 512, 8, 2, 1536, 2048),
+}
+
+
+@dataclasses.dataclass
+class LayerWeights:
+    attn_norm: np.ndarray
+    wq: np.ndarray
+    wk: np.ndarray
+    wv: np.ndarray
+    wo: np.ndarray
+    ffn_norm: np.ndarray
+    wg: np.ndarray
+    wu: np.ndarray
+    wd: np.ndarray
+
+
+@dataclasses.dataclass
+class Model:
+    shape: ModelShape
+    layers: list
+    tok_embd: np.ndarray
+    output_norm: np.ndarray
+    output: np.ndarray
+
+    def digest(self) -> str:
+        h = hashlib.sha256()
+        for L in self.layers:
+            for a in dataclasses.astuple(L):
+                h.update(np.ascontiguousarray(a).tobytes())
+        for a in (self.tok_embd, self.output_norm, self.output):
+            h.update(np.ascontiguousarray(a).tobytes())
+        return h.hexdigest()
+
+
+def make_layer(rng: np.random.Generator, s: ModelShape) -> LayerWeights:
+    D, hd = s.n_embd, s.head_dim
+    return LayerWeights(
+        attn_norm=norm_weight(rng, D),
+        wq=quant_matrix(rng, s.t_q, s.n_heads * hd, D),
+        wk=quant_matrix(rng, s.t_k, s.n_kv_heads * hd, D),
+        wv=quant_matrix(rng, s.t_v, s.n_kv_heads * hd, D),
+        wo=quant_matrix(rng, s.t_o, D, s.n_heads * hd),
+        ffn_norm=norm_weight(rng, D),
+        wg=quant_matrix(rng, s.t_gate, s.n_ff, D),
+        wu=quant_matrix(rng, s.t_up, s.n_ff, D),
+        wd=quant_matrix(rng, s.t_down, D, s.n_ff),
+    )
+
+
+def make_model(shape: ModelShape | str, seed: int = 0, n_layers: int | None = None) -> Model:
+    s = SHAPES[shape] if isinstance(shape, str) else shape
+    if n_layers is not None:
+        s = dataclasses.replace(s, n_layers=n_layers)
+    rng = np.random.default_rng(seed)
+    layers = [make_layer(rng, s) for _ in range(s.n_layers)]
+    tok = quant_matrix(rng, s.t_embd, s.n_vocab, s.n_embd)
+    onorm = norm_weight(rng, s.n_embd)
+    out = quant_matrix(rng, s.t_out, s.n_vocab, s.n_embd)
+    return Model(s, layers, tok, onorm, out)
+
+
+def layer_bytes(s: ModelShape) -> int:
+    """Bytes of one layer's nine tensors packed at 32-byte alignment
+    (engine/src/model_loader.c:181-201)."""
+    D, hd = s.n_embd, s.head_dim
+
+    def qb(t, r, c):
+        return r * (c // QK) * BLOCK_BYTES[t]
+
+    sizes = [4 * D, qb(s.t_q, s.n_heads * hd, D), qb(s.t_k, s.n_kv_heads * hd, D),
+             qb(s.t_v, s.n_kv_heads * hd, D), qb(s.t_o, D, s.n_heads * hd), 4 * D,
+             qb(s.t_gate, s.n_ff, D), qb(s.t_up, s.n_ff, D), qb(s.t_down, D, s.n_ff)]
+    off = 0
+    for sz in sizes:
+        off = (off + 31) & ~31
+        off += sz
+    return off
+
+
+def token_bytes(s: ModelShape) -> int:
+    """Algorithmic weight bytes streamed per decoded token: every layer, the
+    output head, and one embedding row."""
+    head = s.n_vocab * (s.n_embd // QK) * BLOCK_BYTES[s.t_out]
+    embd_row = (s.n_embd // QK) * BLOCK_BYTES[s.t_embd]
+    return s.n_layers * layer_bytes(s) + head + embd_row
+
+
+def kv_bytes_per_pos(s: ModelShape) -> int:
+    """Q8_0 K+V bytes read per cached position per token (36-byte blocks)."""
+    return s.n_layers * 2 * (s.n_kv_heads * s.head_dim // 32) * 36

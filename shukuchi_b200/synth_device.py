@@ -1,0 +1,86 @@
+"""Seeded synthetic K-quant weights generated directly in HBM with torch's
+device RNG (same value distributions as ``synth.py``, different stream).
+
+Used where a full-size model would take too long to build on the host
+(e.g. the 4.9 GB Llama-3.1-8B-shape model for the decode benchmark).  Q6_K
+rows that are not 16-byte multiples are padded.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from . import cuda as sc
+from .synth import BLOCK_BYTES, QK, ModelShape, T_Q4K, T_Q6K
+
+
+def _fill_blocks(buf: torch.Tensor, qtype: int, rows: int, cols: int, stride: int, gen) -> None:
+    """buf: uint8 view of rows * stride bytes."""
+    nb = cols // QK
+    bb = BLOCK_BYTES[qtype]
+    v = buf.view(rows, stride)[:, : nb * bb]
+    v.copy_(torch.randint(0, 256, v.shape, dtype=torch.uint8, device=buf.device, generator=gen))
+    blocks = v.view(rows, nb, bb)
+    if qtype == T_Q4K:
+        d = (torch.randn((rows, nb, 2), device=buf.device, generator=gen) * 0.002).abs().half()
+        blocks[:, :, 0:4] = d.view(torch.uint8).view(rows, nb, 4)
+    else:
+        sc8 = torch.randint(-32, 32, (rows, nb, 16), dtype=torch.int8, device=buf.device, generator=gen)
+        blocks[:, :, 192:208] = sc8.view(torch.uint8)
+        d = (torch.randn((rows, nb, 1), device=buf.device, generator=gen) * 0.0005).abs().half()
+        blocks[:, :, 208:210] = d.view(torch.uint8).view(rows, nb, 2)
+
+
+def _matrix(qtype, rows, cols, device, gen, keep):
+    rb = (cols // QK) * BLOCK_BYTES[qtype]
+    stride = (rb + 15) // 16 * 16
+    t = torch.zeros(rows * stride, dtype=torch.uint8, device=device)
+    _fill_blocks(t, qtype, rows, cols, stride, gen)
+    keep.append(t)
+    return t.data_ptr(), (0 if stride == rb else stride)
+
+
+@dataclasses.dataclass
+class DeviceWeights:
+    shape: ModelShape
+    keep: list
+    layers: list
+    desc: sc.ModelDesc
+
+    def layer_bytes(self) -> int:
+        return sum(t.numel() for t in self.keep) // max(1, self.shape.n_layers)
+
+
+def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
+                      distinct_layers: int | None = None) -> DeviceWeights:
+    """All weights in HBM.  distinct_layers < n_layers reuses layer buffers
+    cyclically (only for smoke-sized runs; the benchmark uses distinct layers)."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    keep: list = []
+    s = shape
+    hd = s.head_dim
+    nd = distinct_layers or s.n_layers
+    made = []
+    for _ in range(nd):
+        an = (1 + 0.02 * torch.randn(s.n_embd, device=device, generator=gen)).float()
+        fn = (1 + 0.02 * torch.randn(s.n_embd, device=device, generator=gen)).float()
+        keep += [an, fn]
+        q, _ = _matrix(s.t_q, s.n_heads * hd, s.n_embd, device, gen, keep)
+        k, _ = _matrix(s.t_k, s.n_kv_heads * hd, s.n_embd, device, gen, keep)
+        v, sv = _matrix(s.t_v, s.n_kv_heads * hd, s.n_embd, device, gen, keep)
+        o, _ = _matrix(s.t_o, s.n_embd, s.n_heads * hd, device, gen, keep)
+        g, _ = _matrix(s.t_gate, s.n_ff, s.n_embd, device, gen, keep)
+        u, _ = _matrix(s.t_up, s.n_ff, s.n_embd, device, gen, keep)
+        dn, sd = _matrix(s.t_down, s.n_embd, s.n_ff, device, gen, keep)
+        made.append(sc.LayerDesc(an.data_ptr(), fn.data_ptr(), q, k, v, o, g, u, dn,
+                                 s.t_q, s.t_k, s.t_v, s.t_o, s.t_gate, s.t_up, s.t_down, sv, sd))
+    layers = [made[i % nd] for i in range(s.n_layers)]
+    te, _ = _matrix(s.t_embd, s.n_vocab, s.n_embd, device, gen, keep)
+    out, so = _matrix(s.t_out, s.n_vocab, s.n_embd, device, gen, keep)
+    assert so == 0, "output head rows must be 16-byte multiples"
+    desc = sc.ModelDesc(s.n_layers, s.n_embd, s.n_heads, s.n_kv_heads, hd, s.n_ff, s.n_vocab, 0.0,
+                        te, s.t_embd, out, s.t_out)
+    torch.cuda.synchronize(device)
+    return DeviceWeights(s, keep, layers, desc)

@@ -1,0 +1,89 @@
+"""Q4_K / Q6_K dequantise-matvec on the GPU vs the oracle (op_matmul_q4_k /
+op_matmul_q6_k restated).  Tolerance: per row |dy| <= 4*sqrt(k)*2^-24 * sum|w*x|
+(two fp32 summation orders)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import gemv_tolerance, golden, to_dev
+from shukuchi_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def run_gemv(ctx, qt, w, x, m, k):
+    wd, xd = to_dev(w), to_dev(x)
+    yd = torch.full((m,), float("nan"), device="cuda")
+    ctx.matmul(qt, wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), m, k,
+               stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    return yd.cpu().numpy()
+
+
+def check(oracle, ctx, qt, m, k, seed, subnormal=False, xscale=1.0):
+    rng = np.random.default_rng(seed)
+    blocks = (synth.q4k_blocks if qt == 12 else synth.q6k_blocks)(rng, m * (k // 256))
+    if subnormal:
+        from golden.make_golden import subnormal_scales
+        subnormal_scales(blocks, qt, rng, frac=0.7)
+    w = blocks.reshape(-1)
+    x = (rng.normal(0, 1, k) * xscale).astype(np.float32)
+    y = run_gemv(ctx, qt, w, x, m, k)
+    yr = oracle.matvec(qt, w, x, m, k)
+    tol = gemv_tolerance(oracle, qt, w, x, m, k)
+    err = np.abs(y.astype(np.float64) - yr)
+    assert np.all(err <= tol), (np.max(err / tol), int(np.argmax(err / tol)))
+
+
+@pytest.mark.parametrize("m,k", [(1, 256), (7, 512), (64, 2048), (333, 1024), (1024, 4096),
+                                 (4096, 4096), (1000, 14336), (3, 8192)])
+def test_q4k(oracle, ctx, m, k):
+    check(oracle, ctx, 12, m, k, seed=m + k)
+
+
+@pytest.mark.parametrize("m,k", [(1, 256), (9, 512), (256, 2048), (1024, 4096), (777, 4096),
+                                 (4096, 14336), (100, 5632), (64, 1792), (5, 3584)])
+def test_q6k(oracle, ctx, m, k):
+    # 5632 / 1792 / 3584 give rows that are not 16-byte multiples: plain-load kernel
+    check(oracle, ctx, 14, m, k, seed=m * 3 + k)
+
+
+@pytest.mark.parametrize("qt", [12, 14])
+def test_subnormal_scales(oracle, ctx, qt):
+    # the reference decodes subnormal fp16 scales at half value; GPU must too
+    check(oracle, ctx, qt, 64, 1024, seed=99, subnormal=True)
+
+
+@pytest.mark.parametrize("qt", [12, 14])
+def test_large_and_tiny_inputs(oracle, ctx, qt):
+    check(oracle, ctx, qt, 128, 2048, seed=5, xscale=1e6)
+    check(oracle, ctx, qt, 128, 2048, seed=6, xscale=1e-6)
+
+
+def test_golden_vectors(oracle, ctx):
+    for name, qt in (("gemv_q4k", 12), ("gemv_q6k", 14)):
+        g = golden(name)
+        m, k = int(g["m"]), int(g["k"])
+        y = run_gemv(ctx, qt, g["w"], g["x"], m, k)
+        tol = gemv_tolerance(oracle, qt, g["w"], g["x"], m, k)
+        assert np.all(np.abs(y.astype(np.float64) - g["y"]) <= tol), name
+
+
+def test_host_pointer_variant(oracle, ctx):
+    rng = np.random.default_rng(3)
+    for qt in (12, 14):
+        m, k = 300, 4096
+        w = synth.quant_matrix(rng, qt, m, k)
+        x = rng.normal(0, 1, k).astype(np.float32)
+        y = np.zeros(m, np.float32)
+        ctx.matmul_host(qt, w, x, y, m, k)
+        tol = gemv_tolerance(oracle, qt, w, x, m, k)
+        assert np.all(np.abs(y.astype(np.float64) - oracle.matvec(qt, w, x, m, k)) <= tol)
+
+
+def test_rejects_bad_shapes(ctx):
+    from shukuchi_b200.cuda import ShkError
+    d = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ShkError):
+        ctx.matmul(12, d.data_ptr(), d.data_ptr(), d.data_ptr(), 1, 100)  # k % 256

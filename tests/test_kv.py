@@ -1,0 +1,111 @@
+"""Q8_0 KV cache on the GPU: appended blocks must be BIT-identical to the
+reference quantiser (q8_quantize_vec) for identical fp32 input; attention over
+the cache vs the oracle (kv_cache_read_range + op_attention), relative
+tolerance 2e-5 of max|out| per head."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import to_dev
+from shukuchi_b200 import cuda as sc
+
+pytestmark = pytest.mark.gpu
+
+
+def kv_inputs(rng, T, KV, hd):
+    k = rng.normal(0, 1, (T, KV * hd)).astype(np.float32)
+    v = rng.normal(0, 1, (T, KV * hd)).astype(np.float32)
+    # exercise: an all-zero block (scale 1), exact .5 ties, a saturating value
+    k[0, :32] = 0.0
+    v[min(1, T - 1), 32:64] = (np.arange(32) - 16) * 0.5 + 0.25
+    k[T - 1, 5] = 1e30
+    return k, v
+
+
+@pytest.mark.parametrize("KV,hd", [(2, 64), (8, 128), (4, 64)])
+def test_append_bit_exact(oracle, ctx, KV, hd):
+    rng = np.random.default_rng(KV * hd)
+    T = 40
+    k, v = kv_inputs(rng, T, KV, hd)
+    kv = sc.KvCache(ctx, 2, KV, hd, 64)
+    try:
+        kd, vd = to_dev(k), to_dev(v)
+        for t in range(T):
+            kv.append(1, t, kd[t].data_ptr(), vd[t].data_ptr())
+        nb = KV * hd // 32 * 36
+        kb = torch.zeros(T * nb, dtype=torch.uint8, device="cuda")
+        vb = torch.zeros_like(kb)
+        kv.read_blocks(1, 0, T, kb.data_ptr(), vb.data_ptr())
+        torch.cuda.synchronize()
+        ctx.check()
+        ref_k = np.concatenate([oracle.q8_quantize(k[t]) for t in range(T)])
+        ref_v = np.concatenate([oracle.q8_quantize(v[t]) for t in range(T)])
+        assert np.array_equal(kb.cpu().numpy(), ref_k)
+        assert np.array_equal(vb.cpu().numpy(), ref_v)
+        assert kv.seq_len(1) == T and kv.seq_len(0) == 0
+        # read_range dequantises exactly like q8_dequantize_vec
+        ko = torch.zeros(T * KV * hd, device="cuda")
+        vo = torch.zeros_like(ko)
+        kv.read_range(1, 0, T, ko.data_ptr(), vo.data_ptr())
+        torch.cuda.synchronize()
+        okv = oracle.kv_create(2, KV, hd, 64)
+        try:
+            for t in range(T):
+                oracle.L.orc_kv_append(okv, 1, t, k[t].ctypes.data, v[t].ctypes.data)
+            rk = np.zeros(T * KV * hd, np.float32)
+            rv = np.zeros_like(rk)
+            oracle.L.orc_kv_read_range(okv, 1, 0, T, rk.ctypes.data, rv.ctypes.data)
+        finally:
+            oracle.kv_destroy(okv)
+        assert np.array_equal(ko.cpu().numpy(), rk) and np.array_equal(vo.cpu().numpy(), rv)
+        kv.clear()
+        assert kv.seq_len(1) == 0
+    finally:
+        kv.close()
+
+
+@pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64)])
+@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049])
+def test_attend(oracle, ctx, H, KV, hd, seq):
+    rng = np.random.default_rng(H * 131 + seq)
+    k, v = kv_inputs(rng, seq, KV, hd)
+    k[seq - 1, 5] = 3.0
+    q = rng.normal(0, 1, H * hd).astype(np.float32)
+    kv = sc.KvCache(ctx, 1, KV, hd, seq + 8)
+    try:
+        kd, vd, qd = to_dev(k), to_dev(v), to_dev(q)
+        for t in range(seq - 1):
+            kv.append(0, t, kd[t].data_ptr(), vd[t].data_ptr())
+        out = torch.zeros(H * hd, device="cuda")
+        scale = np.float32(1.0 / np.sqrt(hd))
+        # the last position is appended by the fused attention kernel itself
+        kv.attend(0, qd.data_ptr(), out.data_ptr(), H, seq, float(scale),
+                  k_new=kd[seq - 1].data_ptr(), v_new=vd[seq - 1].data_ptr())
+        torch.cuda.synchronize()
+        ctx.check()
+        got = out.cpu().numpy()
+    finally:
+        kv.close()
+    okv = oracle.kv_create(1, KV, hd, seq + 8)
+    try:
+        for t in range(seq):
+            oracle.L.orc_kv_append(okv, 0, t, k[t].ctypes.data, v[t].ctypes.data)
+        K = np.zeros(seq * KV * hd, np.float32)
+        V = np.zeros_like(K)
+        oracle.L.orc_kv_read_range(okv, 0, 0, seq, K.ctypes.data, V.ctypes.data)
+    finally:
+        oracle.kv_destroy(okv)
+    ref = oracle.attention(q, K, V, H, KV, hd, seq, scale)
+    err = np.abs(got - ref).reshape(H, hd).max(axis=1)
+    lim = 2e-5 * np.maximum(np.abs(ref).reshape(H, hd).max(axis=1), 1.0)
+    assert np.all(err <= lim), (err / lim).max()
+
+
+def test_attend_rejects_out_of_range(ctx):
+    kv = sc.KvCache(ctx, 1, 2, 64, 16)
+    try:
+        q = torch.zeros(4 * 64, device="cuda")
+        with pytest.raises(sc.ShkError):
+            kv.attend(0, q.data_ptr(), q.data_ptr(), 4, 17, 0.125)
+    finally:
+        kv.close()

@@ -1,0 +1,112 @@
+"""Whole-layer and whole-model decode on the GPU vs the oracle (forward_layer_view
+and engine_generate restated).  Acceptance, as stated for this path:
+greedy token ids identical, and per decode step
+max|logit_gpu - logit_ref| <= 1e-2 * std(logit_ref)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from shukuchi_b200 import cuda as sc
+from shukuchi_b200 import synth
+from shukuchi_b200.device_model import GpuDecoder, upload
+
+pytestmark = pytest.mark.gpu
+
+
+def assert_logits(got, ref):
+    for t in range(ref.shape[0]):
+        tol = 1e-2 * float(np.std(ref[t]))
+        err = float(np.max(np.abs(got[t] - ref[t])))
+        assert err <= tol, (t, err, tol)
+
+
+def test_layer_forward_matches_oracle(oracle, ctx):
+    model = synth.make_model("small", seed=3)
+    s = model.shape
+    up = upload(model)
+    kv = sc.KvCache(ctx, s.n_layers, s.n_kv_heads, s.head_dim, 64)
+    dm = sc.DeviceModel(ctx, kv, up.desc)
+    okv = oracle.kv_create(s.n_layers, s.n_kv_heads, s.head_dim, 64)
+    try:
+        rng = np.random.default_rng(0)
+        for pos in range(6):
+            hid = rng.normal(0, 1, s.n_embd).astype(np.float32)
+            hd = torch.from_numpy(hid.copy()).cuda()
+            ref = hid.copy()
+            for layer in range(s.n_layers):
+                dm.forward_layer(up.layers[layer], layer, pos, hd.data_ptr())
+                assert oracle.L.orc_forward_layer(
+                    __import__("ctypes").byref(oracle.model_struct(model)), okv, layer, pos,
+                    ref.ctypes.data) == 0
+                torch.cuda.synchronize()
+                ctx.check()
+                got = hd.cpu().numpy()
+                err = np.max(np.abs(got - ref))
+                assert err <= 1e-4 * max(1.0, float(np.max(np.abs(ref)))), (pos, layer, err)
+                hd.copy_(torch.from_numpy(ref))  # re-sync so errors do not compound
+            # KV blocks written by the fused path are bit-identical when fed the
+            # same fp32 K/V: checked in test_kv; here the caches must agree closely
+        assert kv.seq_len(0) == 6
+    finally:
+        oracle.kv_destroy(okv)
+        dm.close()
+        kv.close()
+
+
+def test_tiny_model_golden(ctx):
+    g = golden("tiny_model")
+    model = synth.make_model("tiny", seed=int(g["seed"]))
+    dec = GpuDecoder(ctx, model, max_seq=64)
+    try:
+        n = len(g["tokens"])
+        logits = np.zeros((n, model.shape.n_vocab), np.float32)
+        toks = dec.generate(g["prompt"], n, logits_out=logits)
+    finally:
+        dec.close()
+    assert np.array_equal(toks, g["tokens"])
+    assert_logits(logits, g["logits"])
+
+
+@pytest.mark.parametrize("shape,n_prompt,n_decode", [("small", 5, 12)])
+def test_generate_matches_oracle(oracle, ctx, shape, n_prompt, n_decode):
+    model = synth.make_model(shape, seed=21)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, model.shape.n_vocab, n_prompt).astype(np.uint32)
+    t_ref, l_ref = oracle.generate(model, prompt, n_decode)
+    dec = GpuDecoder(ctx, model, max_seq=64)
+    try:
+        logits = np.zeros_like(l_ref)
+        toks = dec.generate(prompt, n_decode, logits_out=logits)
+        # device-resident loop (token feedback on the GPU) gives the same ids
+        dec.kv.clear()
+        for i, t in enumerate(prompt[:-1]):
+            dec.m.token_step(int(t), i, want_next=False)
+        dec.m.decode_steps(int(prompt[-1]), n_prompt - 1, 1)
+        first = dec.m.last_token()
+        dec.m.decode_steps(first, n_prompt, n_decode - 1)
+        last = dec.m.last_token()
+    finally:
+        dec.close()
+    assert np.array_equal(toks, t_ref)
+    assert_logits(logits, l_ref)
+    assert first == t_ref[0] and last == t_ref[-1]
+
+
+@pytest.mark.slow
+def test_tinyllama_shape_8_plus_16(oracle, ctx):
+    """TinyLlama-1.1B shape (22 layers, d 2048, 32/4 heads, ffn 5632, vocab
+    32000, Q4_K_M mix with Q6_K ffn_down rows of 22 blocks): 8 random prompt
+    ids, 16 greedy tokens."""
+    model = synth.make_model("tinyllama", seed=0)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, 32000, 8).astype(np.uint32)
+    t_ref, l_ref = oracle.generate(model, prompt, 16)
+    dec = GpuDecoder(ctx, model, max_seq=2048)
+    try:
+        logits = np.zeros_like(l_ref)
+        toks = dec.generate(prompt, 16, logits_out=logits)
+    finally:
+        dec.close()
+    assert np.array_equal(toks, t_ref)
+    assert_logits(logits, l_ref)

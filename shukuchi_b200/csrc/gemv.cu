@@ -2,25 +2,30 @@
 //
 // Reference semantics: op_matmul_q4_k / op_matmul_q6_k (engine/src/ops.c:266-314,
 // 361-404): y[r] = sum_k dequant(W[r, k]) * x[k] over 256-element super-blocks
-// laid out row-major as in GGUF.  Summation order differs (parallel partial sums);
-// results agree with the reference to fp32 rounding.
+// laid out row-major as in GGUF.  Summation order differs from the reference's
+// sequential fp32 sum; results agree to fp32 rounding.
 //
 // Kernel shape (one CTA per SM, persistent over a byte-balanced row range):
-//  * warp 8 is the producer: one lane streams whole-row chunks of the weight
-//    matrix into a 4-stage shared-memory ring with cp.async.bulk (TMA, 1-D,
-//    no tensor map, no multicast), completion tracked by mbarrier tx-counts;
-//  * warps 0-7 are consumers: while the first chunks are in flight they build
-//    the input vector in shared memory (optionally RMS-normalised), then decode
-//    blocks from the ring.
+//  * warp 8 is the producer: one lane bulk-copies x, then streams whole-row
+//    chunks of the weight matrix into a shared-memory ring with cp.async.bulk
+//    (TMA, 1-D, no tensor map, no multicast), completion tracked by mbarrier
+//    tx-counts; a per-stage generation tag orders consumers that skip ahead;
+//  * warps 0-7 are consumers: they turn x into the fixed-point form below while
+//    the first chunks are in flight, then decode blocks from the ring.  The last
+//    warp to finish a chunk's tasks releases its stage.
 //
-// Dequant arithmetic ("denormal nibble" trick): a quant field is isolated in
-// place with one AND, leaving the integer q at bit p of an otherwise-zero word,
-// i.e. the fp32 denormal q * 2^(p-149).  The input element was stored
-// pre-multiplied by 2^(69-p), so one FFMA gives q * x * 2^-80 exactly rounded,
-// with no int->float conversion per weight.  Two weights go per __ffma2_rn.
-// Per sub-block the partial sum is rescaled by d*sc*2^80 and the min / -32
-// offsets are applied through precomputed sums of x.  Constraint: |x| < 2^58.
+// Arithmetic: the weights' integer quants are multiplied with integer limbs of
+// x by dp4a, exactly, in int32.  Each 256-element block of x is written as
+// X_b * x_int with X_b a power of two and |x_int| <= 2^22 (24-bit fixed point,
+// relative step 2^-22 of the block maximum, i.e. fp32-level precision for the
+// dot product), and x_int = l0 + 256*l1 + 65536*l2 with int8 limbs.  Per
+// sub-block the three limb sums are scaled by the 6-bit (Q4_K) or int8 (Q6_K)
+// sub-block scale with IMAD, then per block converted to float and multiplied by
+// d * X_b.  The Q4_K min term uses fp32 sums of x; the Q6_K -32 offset is folded
+// into the dp4a accumulators' initial value.  Integer packing keeps the
+// per-weight work on the dp4a/IMAD path instead of the half-rate logic pipe.
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdint.h>
 
 #include <algorithm>
@@ -31,67 +36,71 @@
 namespace shk {
 namespace {
 
-constexpr int XEXP = 69;
-constexpr float BACK = 0x1p80f;  // 2^80
-
-// Bit position at which the Q4_K weight for element e lands after masking
-// (see q4k_block): low-nibble half {0,8,16,12}, high-nibble half {4,12,8,16}.
-__device__ __forceinline__ int q4_pos(uint32_t e) {
-  const uint32_t tab = ((e & 63u) < 32u) ? 0x0C100800u : 0x10080C04u;
-  return (int)((tab >> (8u * (e & 3u))) & 0xFFu);
-}
-// Q6_K: byte k of the combined word at 8k, byte 3 at 16 (after >> 8).
-__device__ __forceinline__ int q6_pos(uint32_t e) {
-  const uint32_t k = e & 3u;
-  return k == 3u ? 16 : (int)(8u * k);
-}
-
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// x limbs live in shared memory as int4 vectors {l0 word, l1 word, l2 word, 0}
+// (4 elements each) under an XOR swizzle: vector v is stored at v ^ xsw(v).
+// Lanes of a warp read x at the same offset inside different blocks; without
+// the swizzle every lane would hit the same four banks.  xsw is constant over
+// each aligned run of 8 vectors, so a lane computes it once per run.
+__device__ __forceinline__ uint32_t xsw(uint32_t v) { return ((v >> 3) ^ (v >> 6) ^ (v >> 8)) & 7u; }
+
+__device__ __forceinline__ int dp4a(uint32_t a, int b, int c) { return __dp4a((int)a, b, c); }
+
+__device__ __forceinline__ float limbs_to_float(int a0, int a1, int a2) {
+  return fmaf(65536.0f, (float)a2, fmaf(256.0f, (float)a1, (float)a0));
+}
+
 // ------------------------------- Q4_K ---------------------------------------
-// One lane handles 64-element group j (32 quant bytes) of a block: the low
-// nibbles are sub-block 2j, the high nibbles sub-block 2j+1.
-template <bool DUAL>
-__device__ __forceinline__ void q4k_block(const uint8_t* __restrict__ blk_a,
-                                          const uint8_t* __restrict__ blk_b, int j,
-                                          const float* __restrict__ xb, float2 xsum,
-                                          float& acc_a, float& acc_b) {
-  const uint4 ha = *reinterpret_cast<const uint4*>(blk_a);
-  const uint4 qa0 = *reinterpret_cast<const uint4*>(blk_a + 16 + 32 * j);
-  const uint4 qa1 = *reinterpret_cast<const uint4*>(blk_a + 32 + 32 * j);
-  uint4 hb = ha, qb0 = qa0, qb1 = qa1;
-  if (DUAL) {
-    hb = *reinterpret_cast<const uint4*>(blk_b);
-    qb0 = *reinterpret_cast<const uint4*>(blk_b + 16 + 32 * j);
-    qb1 = *reinterpret_cast<const uint4*>(blk_b + 32 + 32 * j);
+// Lane (s, j) handles 64-element group j (32 quant bytes) of block b for RL rows
+// (and both matrices of a dual segment): the low nibbles are sub-block 2j, the
+// high nibbles sub-block 2j+1.  x limbs are loaded once and used NR times.
+template <int RL, bool DUAL>
+__device__ __forceinline__ void q4k_block_rows(const uint8_t* __restrict__ blk, uint32_t row_stride,
+                                               uint32_t dual_off, int j,
+                                               const int4* __restrict__ xq, uint32_t v0, float xb,
+                                               float2 xsum, float (&acc)[RL][2]) {
+  constexpr int NR = RL * (DUAL ? 2 : 1);
+  uint4 hdr[NR];
+  uint32_t w[NR][8];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const uint8_t* p = blk + (size_t)(r % RL) * row_stride + (r >= RL ? dual_off : 0);
+    hdr[r] = *reinterpret_cast<const uint4*>(p);
+    const uint4 q0 = *reinterpret_cast<const uint4*>(p + 16 + 32 * j);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(p + 32 + 32 * j);
+    w[r][0] = q0.x; w[r][1] = q0.y; w[r][2] = q0.z; w[r][3] = q0.w;
+    w[r][4] = q1.x; w[r][5] = q1.y; w[r][6] = q1.z; w[r][7] = q1.w;
   }
-  const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
-  const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
-  float2 alo = make_float2(0.f, 0.f), ahi = alo, blo = alo, bhi = alo;
+  int S[NR][2][3];
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) S[r][h][0] = S[r][h][1] = S[r][h][2] = 0;
+  const uint32_t slo = xsw(v0), shi = xsw(v0 + 8);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float4 xl = *reinterpret_cast<const float4*>(xb + 4 * i);
-    const float4 xh = *reinterpret_cast<const float4*>(xb + 32 + 4 * i);
-    {
-      const uint32_t w = wa[i], w12 = w >> 12;
-      alo = ffma2(make_float2(u2f_bits(w & 0xFu), u2f_bits(w & 0xF00u)), make_float2(xl.x, xl.y), alo);
-      alo = ffma2(make_float2(u2f_bits(w & 0xF0000u), u2f_bits(w12 & 0xF000u)), make_float2(xl.z, xl.w), alo);
-      ahi = ffma2(make_float2(u2f_bits(w & 0xF0u), u2f_bits(w & 0xF000u)), make_float2(xh.x, xh.y), ahi);
-      ahi = ffma2(make_float2(u2f_bits(w12 & 0xF00u), u2f_bits(w12 & 0xF0000u)), make_float2(xh.z, xh.w), ahi);
-    }
-    if (DUAL) {
-      const uint32_t w = wb[i], w12 = w >> 12;
-      blo = ffma2(make_float2(u2f_bits(w & 0xFu), u2f_bits(w & 0xF00u)), make_float2(xl.x, xl.y), blo);
-      blo = ffma2(make_float2(u2f_bits(w & 0xF0000u), u2f_bits(w12 & 0xF000u)), make_float2(xl.z, xl.w), blo);
-      bhi = ffma2(make_float2(u2f_bits(w & 0xF0u), u2f_bits(w & 0xF000u)), make_float2(xh.x, xh.y), bhi);
-      bhi = ffma2(make_float2(u2f_bits(w12 & 0xF00u), u2f_bits(w12 & 0xF0000u)), make_float2(xh.z, xh.w), bhi);
+    const int4 xl = xq[v0 + (i ^ slo)];
+    const int4 xh = xq[v0 + 8 + (i ^ shi)];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const uint32_t lo = w[r][i] & 0x0F0F0F0Fu, hi = (w[r][i] >> 4) & 0x0F0F0F0Fu;
+      S[r][0][0] = dp4a(lo, xl.x, S[r][0][0]);
+      S[r][0][1] = dp4a(lo, xl.y, S[r][0][1]);
+      S[r][0][2] = dp4a(lo, xl.z, S[r][0][2]);
+      S[r][1][0] = dp4a(hi, xh.x, S[r][1][0]);
+      S[r][1][1] = dp4a(hi, xh.y, S[r][1][1]);
+      S[r][1][2] = dp4a(hi, xh.z, S[r][1][2]);
     }
   }
-  // Scales/mins of sub-blocks 2j and 2j+1 (engine/src/ops.c:107-115 get_scale_min_k4).
+  // Scales/mins of sub-blocks 2j, 2j+1 (engine/src/ops.c:107-115 get_scale_min_k4),
+  // decoded four at a time from the packed 12-byte field.
   const int sh = (j & 1) * 16;
-  auto apply = [&](const uint4& h, float2 lo, float2 hi, float& acc) {
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const uint4 h = hdr[r];
     uint32_t scw, mw;
     if (j < 2) {
       scw = h.y & 0x3F3F3F3Fu;
@@ -100,43 +109,42 @@ __device__ __forceinline__ void q4k_block(const uint8_t* __restrict__ blk_a,
       scw = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
       mw = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
     }
-    const float d = ref_half(h.x & 0xFFFFu) * BACK;
-    const float dmin = ref_half(h.x >> 16);
-    const float sc0 = (float)((scw >> sh) & 0xFFu), sc1 = (float)((scw >> (sh + 8)) & 0xFFu);
-    const float m0 = (float)((mw >> sh) & 0xFFu), m1 = (float)((mw >> (sh + 8)) & 0xFFu);
-    acc = fmaf(d * sc0, lo.x + lo.y, acc);
-    acc = fmaf(d * sc1, hi.x + hi.y, acc);
-    acc = fmaf(-(dmin * m0), xsum.x, acc);
-    acc = fmaf(-(dmin * m1), xsum.y, acc);
-  };
-  apply(ha, alo, ahi, acc_a);
-  if (DUAL) apply(hb, blo, bhi, acc_b);
+    const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
+    const int m0 = (mw >> sh) & 0xFF, m1 = (mw >> (sh + 8)) & 0xFF;
+    const int a0 = sc0 * S[r][0][0] + sc1 * S[r][1][0];
+    const int a1 = sc0 * S[r][0][1] + sc1 * S[r][1][1];
+    const int a2 = sc0 * S[r][0][2] + sc1 * S[r][1][2];
+    const float d = ref_half(h.x & 0xFFFFu), dmin = ref_half(h.x >> 16);
+    const float mins = fmaf((float)m0, xsum.x, (float)m1 * xsum.y);
+    acc[r % RL][r / RL] += fmaf(d * xb, limbs_to_float(a0, a1, a2), -(dmin * mins));
+  }
 }
 
-template <int RG, bool DUAL>
+template <int RL, bool DUAL>
 __device__ __forceinline__ void q4k_task(const uint8_t* __restrict__ rows, uint32_t row_stride,
                                          uint32_t nb, int rows_valid, uint32_t dual_off,
-                                         const float* __restrict__ x4,
-                                         const float* __restrict__ xs32, int lane, float& acc_a,
-                                         float& acc_b) {
-  constexpr int SPR = 8 / RG;  // block slots per row
+                                         const int4* __restrict__ xq, const float* __restrict__ xbs,
+                                         const float* __restrict__ xs32, int lane, int lg_rg,
+                                         float (&acc)[RL][2]) {
+  const int SPR = 8 >> lg_rg;  // block slots per row group
   const int slot = lane >> 2, j = lane & 3;
-  const int r = slot / SPR, s = slot % SPR;
-  acc_a = 0.f;
-  acc_b = 0.f;
-  if (r < rows_valid) {
-    const uint8_t* row = rows + (size_t)r * row_stride;
+  const int g = slot >> (3 - lg_rg), s = slot & (SPR - 1);
+#pragma unroll
+  for (int r = 0; r < RL; ++r) acc[r][0] = acc[r][1] = 0.f;
+  if (g * RL < rows_valid) {
+    const uint8_t* row = rows + (size_t)(g * RL) * row_stride;
     for (uint32_t b = s; b < nb; b += SPR) {
       const float2 xsum = *reinterpret_cast<const float2*>(xs32 + b * 8 + 2 * j);
-      q4k_block<DUAL>(row + b * Q4K_BYTES, row + dual_off + b * Q4K_BYTES, j,
-                      x4 + b * QK + 64 * j, xsum, acc_a, acc_b);
+      q4k_block_rows<RL, DUAL>(row + (size_t)b * Q4K_BYTES, row_stride, dual_off, j, xq,
+                               b * 64 + 16 * j, xbs[b], xsum, acc);
     }
   }
+  for (int o = 16 >> lg_rg; o > 0; o >>= 1)
 #pragma unroll
-  for (int o = 16 / RG; o > 0; o >>= 1) {
-    acc_a += __shfl_xor_sync(0xffffffffu, acc_a, o);
-    if (DUAL) acc_b += __shfl_xor_sync(0xffffffffu, acc_b, o);
-  }
+    for (int r = 0; r < RL; ++r) {
+      acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], o);
+      if (DUAL) acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], o);
+    }
 }
 
 // ------------------------------- Q6_K ---------------------------------------
@@ -212,96 +220,133 @@ __device__ __forceinline__ void load8(const uint8_t* p, uint32_t o[2]) {
   }
 }
 
-// One lane handles half n (128 elements) of a Q6_K block
-// (engine/src/ops.c:167-193 dequantize_row_q6_k).
-template <int MU>
-__device__ __forceinline__ void q6k_block(const uint8_t* __restrict__ blk, int n,
-                                          const float* __restrict__ xh,
-                                          const float* __restrict__ xm, float& acc) {
-  uint32_t A[8], B[8], H[8], S[2];
-  load32<MU>(blk + 64 * n, A);
-  load32<MU>(blk + 64 * n + 32, B);
-  load32<MU>(blk + 128 + 32 * n, H);
-  load8<MU>(blk + 192 + 8 * n, S);
-  const uint32_t dbits = *reinterpret_cast<const uint16_t*>(blk + 208);
+// One lane handles half n (128 elements) of a Q6_K block for RL rows
+// (engine/src/ops.c:167-193 dequantize_row_q6_k).  For each 32-bit word i of
+// ql/qh, four words of exact 6-bit quants are formed (element groups +0, +32,
+// +64, +96) and fed to dp4a.  Each 16-element scale group's three limb sums
+// start at -32 * (sum of x limbs), which applies the -32 offset.
+template <int MU, int RL>
+__device__ __forceinline__ void q6k_block_rows(const uint8_t* __restrict__ blk, uint32_t row_stride,
+                                               int n, const int4* __restrict__ xq, uint32_t b,
+                                               const int4* __restrict__ xi, float xb,
+                                               float (&acc)[RL]) {
+  uint32_t A[RL][8], B[RL][8], H[RL][8], SC[RL][2], db[RL];
+#pragma unroll
+  for (int r = 0; r < RL; ++r) {
+    const uint8_t* p = blk + (size_t)r * row_stride;
+    load32<MU>(p + 64 * n, A[r]);
+    load32<MU>(p + 64 * n + 32, B[r]);
+    load32<MU>(p + 128 + 32 * n, H[r]);
+    load8<MU>(p + 192 + 8 * n, SC[r]);
+    db[r] = *reinterpret_cast<const uint16_t*>(p + 208);
+  }
   const uint32_t M = 0x0F0F0F0Fu;
-  float2 a[8];
+  const uint32_t vb = b * 64 + 32 * n;  // first int4 of this half; group g at vb + 8g
+  uint32_t sw[4];
 #pragma unroll
-  for (int t = 0; t < 8; ++t) a[t] = make_float2(0.f, 0.f);
+  for (int g = 0; g < 4; ++g) sw[g] = xsw(vb + 8 * g);
+  int T[RL][3];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int is = i >> 2;
-    const uint32_t h = H[i];
-    // combined 6-bit quants, bits 6-7 of each byte are don't-care
-    const uint32_t Q[4] = {lop_sel(A[i], h << 4, M), lop_sel(B[i], h << 2, M),
-                           lop_sel(A[i] >> 4, h, M), lop_sel(B[i] >> 4, h >> 2, M)};
+  for (int r = 0; r < RL; ++r) T[r][0] = T[r][1] = T[r][2] = 0;
+#pragma unroll
+  for (int is = 0; is < 2; ++is) {
+    int S[RL][4][3];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const float4 xv = *reinterpret_cast<const float4*>(xh + 32 * g + 4 * i);
-      const uint32_t q = Q[g], q8 = q >> 8;
-      float2& ac = a[2 * g + is];
-      ac = ffma2(make_float2(u2f_bits(q & 0x3Fu), u2f_bits(q & 0x3F00u)), make_float2(xv.x, xv.y), ac);
-      ac = ffma2(make_float2(u2f_bits(q & 0x3F0000u), u2f_bits(q8 & 0x3F0000u)), make_float2(xv.z, xv.w), ac);
-    }
-  }
-  const float d = ref_half(dbits);
-  const float4 m0 = *reinterpret_cast<const float4*>(xm);
-  const float4 m1 = *reinterpret_cast<const float4*>(xm + 4);
-  const float mm[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      const int4 init = xi[2 * g + is];  // -32 * limb sums of this 16-group
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-#pragma unroll
-    for (int is = 0; is < 2; ++is) {
-      const int si = is + 2 * g;  // scale index within this half
-      const int sc = (int)(int8_t)((S[si >> 2] >> (8 * (si & 3))) & 0xFFu);
-      const float t = fmaf(a[2 * g + is].x + a[2 * g + is].y, BACK, mm[si]);
-      acc = fmaf(d * (float)sc, t, acc);
+      for (int r = 0; r < RL; ++r) {
+        S[r][g][0] = init.x;
+        S[r][g][1] = init.y;
+        S[r][g][2] = init.z;
+      }
     }
+#pragma unroll
+    for (int i = 4 * is; i < 4 * is + 4; ++i) {
+      int4 xv[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) xv[g] = xq[vb + 8 * g + (i ^ sw[g])];
+#pragma unroll
+      for (int r = 0; r < RL; ++r) {
+        const uint32_t h = H[r][i];
+        const uint32_t hm = h & 0x33333333u, hn = h & 0xCCCCCCCCu;
+        const uint32_t Q[4] = {lop_sel(A[r][i], hm << 4, M), lop_sel(B[r][i], hn << 2, M),
+                               lop_sel(A[r][i] >> 4, hm, M), lop_sel(B[r][i] >> 4, hn >> 2, M)};
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          S[r][g][0] = dp4a(Q[g], xv[g].x, S[r][g][0]);
+          S[r][g][1] = dp4a(Q[g], xv[g].y, S[r][g][1]);
+          S[r][g][2] = dp4a(Q[g], xv[g].z, S[r][g][2]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RL; ++r)
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int si = is + 2 * g;  // scale index within this half
+        const int sc = (int)(int8_t)((SC[r][si >> 2] >> (8 * (si & 3))) & 0xFFu);
+        T[r][0] += sc * S[r][g][0];
+        T[r][1] += sc * S[r][g][1];
+        T[r][2] += sc * S[r][g][2];
+      }
   }
+#pragma unroll
+  for (int r = 0; r < RL; ++r)
+    acc[r] = fmaf(ref_half(db[r]) * xb, limbs_to_float(T[r][0], T[r][1], T[r][2]), acc[r]);
 }
 
-template <int C>
-__device__ __forceinline__ void q6k_class(const uint8_t* __restrict__ row, uint32_t nb, int s,
-                                          int spr, int n, const float* __restrict__ x6,
-                                          const float* __restrict__ xm16, float& acc) {
+template <int C, int RL>
+__device__ __forceinline__ void q6k_class(const uint8_t* __restrict__ row, uint32_t row_stride,
+                                          uint32_t nb, int s, int spr, int n,
+                                          const int4* __restrict__ xq, const int4* __restrict__ xi16,
+                                          const float* __restrict__ xbs, float (&acc)[RL]) {
   if (nb <= (uint32_t)C) return;
   const uint32_t nbc = (nb - C + 3) / 4;
   for (uint32_t t = s; t < nbc; t += spr) {
     const uint32_t b = C + 4 * t;
-    q6k_block<(2 * C) & 7>(row + (size_t)b * Q6K_BYTES, n, x6 + b * QK + 128 * n,
-                           xm16 + b * 16 + 8 * n, acc);
+    q6k_block_rows<(2 * C) & 7, RL>(row + (size_t)b * Q6K_BYTES, row_stride, n, xq, b,
+                                    xi16 + b * 16 + 8 * n, xbs[b], acc);
   }
 }
 
-template <int RG, bool DUAL>
+template <int RL>
+__device__ __forceinline__ void q6k_rows(const uint8_t* __restrict__ row, uint32_t row_stride,
+                                         uint32_t nb, int s, int spr, int n, const int4* xq,
+                                         const int4* xi16, const float* xbs, float (&acc)[RL]) {
+  q6k_class<0, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
+  q6k_class<1, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
+  q6k_class<2, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
+  q6k_class<3, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
+}
+
+template <int RL, bool DUAL>
 __device__ __forceinline__ void q6k_task(const uint8_t* __restrict__ rows, uint32_t row_stride,
                                          uint32_t nb, int rows_valid, uint32_t dual_off,
-                                         const float* __restrict__ x6,
-                                         const float* __restrict__ xm16, int lane, float& acc_a,
-                                         float& acc_b) {
-  constexpr int SPR = 16 / RG;
+                                         const int4* __restrict__ xq, const float* __restrict__ xbs,
+                                         const int4* __restrict__ xi16, int lane, int lg_rg,
+                                         float (&acc)[RL][2]) {
+  const int SPR = 16 >> lg_rg;
   const int slot = lane >> 1, n = lane & 1;
-  const int r = slot / SPR, s = slot % SPR;
-  acc_a = 0.f;
-  acc_b = 0.f;
-  if (r < rows_valid) {
-    const uint8_t* row = rows + (size_t)r * row_stride;
-    q6k_class<0>(row, nb, s, SPR, n, x6, xm16, acc_a);
-    q6k_class<1>(row, nb, s, SPR, n, x6, xm16, acc_a);
-    q6k_class<2>(row, nb, s, SPR, n, x6, xm16, acc_a);
-    q6k_class<3>(row, nb, s, SPR, n, x6, xm16, acc_a);
-    if (DUAL) {
-      const uint8_t* row2 = row + dual_off;
-      q6k_class<0>(row2, nb, s, SPR, n, x6, xm16, acc_b);
-      q6k_class<1>(row2, nb, s, SPR, n, x6, xm16, acc_b);
-      q6k_class<2>(row2, nb, s, SPR, n, x6, xm16, acc_b);
-      q6k_class<3>(row2, nb, s, SPR, n, x6, xm16, acc_b);
-    }
-  }
+  const int g = slot >> (4 - lg_rg), s = slot & (SPR - 1);
+  float a0[RL], a1[RL];
 #pragma unroll
-  for (int o = 16 / RG; o > 0; o >>= 1) {
-    acc_a += __shfl_xor_sync(0xffffffffu, acc_a, o);
-    if (DUAL) acc_b += __shfl_xor_sync(0xffffffffu, acc_b, o);
+  for (int r = 0; r < RL; ++r) a0[r] = a1[r] = 0.f;
+  if (g * RL < rows_valid) {
+    const uint8_t* row = rows + (size_t)(g * RL) * row_stride;
+    q6k_rows<RL>(row, row_stride, nb, s, SPR, n, xq, xi16, xbs, a0);
+    if (DUAL) q6k_rows<RL>(row + dual_off, row_stride, nb, s, SPR, n, xq, xi16, xbs, a1);
+  }
+  for (int o = 16 >> lg_rg; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < RL; ++r) {
+      a0[r] += __shfl_xor_sync(0xffffffffu, a0[r], o);
+      if (DUAL) a1[r] += __shfl_xor_sync(0xffffffffu, a1[r], o);
+    }
+#pragma unroll
+  for (int r = 0; r < RL; ++r) {
+    acc[r][0] = a0[r];
+    acc[r][1] = a1[r];
   }
 }
 
@@ -309,10 +354,12 @@ __device__ __forceinline__ void q6k_task(const uint8_t* __restrict__ rows, uint3
 struct Range {
   uint32_t ub, ue;
 };
+// Task units (rg*rl rows) of segment s whose starting cost lies in [lo, hi).
 __device__ __forceinline__ Range seg_units(const GemvArgs& a, int s, uint64_t seg_off, uint64_t lo,
                                            uint64_t hi) {
   const GemvSeg& g = a.seg[s];
-  const uint64_t units = (g.m + g.rg - 1) / g.rg;
+  const uint32_t ur = (uint32_t)g.rg * g.rl;
+  const uint64_t units = (g.m + ur - 1) / ur;
   auto first_at_or_after = [&](uint64_t c) -> uint64_t {
     if (c <= seg_off) return 0;
     const uint64_t u = (c - seg_off + g.unit_cost - 1) / g.unit_cost;
@@ -321,86 +368,155 @@ __device__ __forceinline__ Range seg_units(const GemvArgs& a, int s, uint64_t se
   return Range{(uint32_t)first_at_or_after(lo), (uint32_t)first_at_or_after(hi)};
 }
 
-template <int RG>
-__device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, const uint8_t* rows,
-                                         int rows_valid, uint32_t dual_off, const float* x4,
-                                         const float* x6, const float* xs32, const float* xm16,
-                                         int lane, float& acc_a, float& acc_b) {
-  if (g.qt == T_Q4K) {
-    if (RG <= 8) {
-      constexpr int R = RG <= 8 ? RG : 8;
-      if (g.dual)
-        q4k_task<R, true>(rows, g.row_stride, g.nb, rows_valid, dual_off, x4, xs32, lane, acc_a, acc_b);
-      else
-        q4k_task<R, false>(rows, g.row_stride, g.nb, rows_valid, dual_off, x4, xs32, lane, acc_a, acc_b);
-    }
-  } else {
-    if (g.dual)
-      q6k_task<RG, true>(rows, g.row_stride, g.nb, rows_valid, dual_off, x6, xm16, lane, acc_a, acc_b);
-    else
-      q6k_task<RG, false>(rows, g.row_stride, g.nb, rows_valid, dual_off, x6, xm16, lane, acc_a, acc_b);
-  }
-}
-
-template <int RG>
-__device__ __forceinline__ void task_and_store(const GemvArgs& a, const GemvSeg& g,
-                                               const uint8_t* rows, uint32_t row0, int rows_valid,
-                                               uint32_t dual_off, const float* x4, const float* x6,
-                                               const float* xs32, const float* xm16, int lane) {
-  float acc_a, acc_b;
-  run_task<RG>(a, g, rows, rows_valid, dual_off, x4, x6, xs32, xm16, lane, acc_a, acc_b);
-  constexpr int LPR = 32 / RG;  // lanes per row
-  const int r = lane / LPR;
+template <int RL>
+__device__ __forceinline__ void store_rows(const GemvArgs& a, const GemvSeg& g, uint32_t row0,
+                                           int nvalid, const float (&acc)[RL][2]) {
   if (g.epi == EPI_ROPE) {
-    const float partner = __shfl_down_sync(0xffffffffu, acc_a, LPR);
-    if ((lane % LPR) == 0 && (r & 1) == 0 && r + 1 < rows_valid) {
+    // (2i, 2i+1) pairs are adjacent rows of this lane (RL even, row0 even)
+    const float p = (float)(*a.pos);
+#pragma unroll
+    for (int r = 0; r + 1 < RL; r += 2) {
+      if (r + 1 >= nvalid) break;
       const uint32_t row = row0 + r;
       const uint32_t i = row % g.rope_hd;
-      const float inv_theta = 1.0f / a.rope_theta;
-      const float freq = powf(inv_theta, (float)i / (float)g.rope_hd);
-      const float ang = (float)(*a.pos) * freq;
-      const float c = cosf(ang), s = sinf(ang);
-      g.y[row] = acc_a * c - partner * s;
-      g.y[row + 1] = acc_a * s + partner * c;
+      // angle = pos * freq in fp32 as engine/src/ops.c:227-228; freq comes from
+      // a table built with the host libm powf, so the angle matches bit for bit
+      const float ang = p * a.rope_freq[i >> 1];
+      const float c = cosf(ang), sn = sinf(ang);
+      const float x0 = acc[r][0], x1 = acc[r + 1][0];
+      g.y[row] = x0 * c - x1 * sn;
+      g.y[row + 1] = x0 * sn + x1 * c;
     }
     return;
   }
-  if ((lane % LPR) == 0 && r < rows_valid) {
+#pragma unroll
+  for (int r = 0; r < RL; ++r) {
+    if (r >= nvalid) break;
     const uint32_t row = row0 + r;
     if (g.epi == EPI_STORE) {
-      g.y[row] = acc_a;
+      g.y[row] = acc[r][0];
     } else if (g.epi == EPI_ADD) {
-      g.y[row] = g.y[row] + acc_a;
-    } else {  // EPI_SWIGLU
-      const float gt = acc_a;
+      g.y[row] = g.y[row] + acc[r][0];
+    } else {  // EPI_SWIGLU: silu(gate) * up
+      const float gt = acc[r][0];
       const float sig = 1.0f / (1.0f + expf(-gt));
-      g.y[row] = (gt * sig) * acc_b;
+      g.y[row] = (gt * sig) * acc[r][1];
     }
   }
+}
+
+struct XView {
+  const int4* xq;     // swizzled limb vectors, K/4
+  const float* xbs;   // per-256-block scale X_b, K/256
+  const float* xs32;  // Q4_K: fp32 sums of x per 32-element sub-block, K/32
+  const int4* xi16;   // Q6_K: -32 * limb sums per 16-element group, K/16
+};
+
+template <int QT, int RL, bool DUAL>
+__device__ __forceinline__ void task_and_store(const GemvArgs& a, const GemvSeg& g,
+                                               const uint8_t* rows, uint32_t row0, int rows_valid,
+                                               uint32_t dual_off, const XView& x, int lane) {
+  const int lg_rg = __ffs(g.rg) - 1;
+  float acc[RL][2];
+  if (QT == T_Q4K)
+    q4k_task<RL, DUAL>(rows, g.row_stride, g.nb, rows_valid, dual_off, x.xq, x.xbs, x.xs32, lane,
+                       lg_rg, acc);
+  else
+    q6k_task<RL, DUAL>(rows, g.row_stride, g.nb, rows_valid, dual_off, x.xq, x.xbs, x.xi16, lane,
+                       lg_rg, acc);
+  const int lpg = 32 >> lg_rg;  // lanes per row group
+  const int grp = lane >> (5 - lg_rg);
+  if ((lane & (lpg - 1)) == 0 && grp * RL < rows_valid)
+    store_rows<RL>(a, g, row0 + grp * RL, rows_valid - grp * RL, acc);
+}
+
+// (qt, dual, rl) -> instantiation; the planner only picks these.
+__device__ __forceinline__ void dispatch_task(const GemvArgs& a, const GemvSeg& g,
+                                              const uint8_t* rows, uint32_t row0, int rv,
+                                              uint32_t dual_off, const XView& x, int lane) {
+#define SHK_TASK(QT, RL, DU)                                            \
+  task_and_store<QT, RL, DU>(a, g, rows, row0, rv, dual_off, x, lane); \
+  return
+  const int key = (g.qt == T_Q4K ? 0 : 100) + (g.dual ? 10 : 0) + g.rl;
+  switch (key) {
+    case 4: SHK_TASK(T_Q4K, 4, false);
+    case 2: SHK_TASK(T_Q4K, 2, false);
+    case 1: SHK_TASK(T_Q4K, 1, false);
+    case 12: SHK_TASK(T_Q4K, 2, true);
+    case 11: SHK_TASK(T_Q4K, 1, true);
+    case 102: SHK_TASK(T_Q6K, 2, false);
+    case 101: SHK_TASK(T_Q6K, 1, false);
+    case 111: SHK_TASK(T_Q6K, 1, true);
+    default: return;
+  }
+#undef SHK_TASK
+}
+
+// Shared-memory map: [full | empty | xbar barriers][done][gen][red]
+// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)][xi16 (K*1, Q6_K)]
+// [stage ring].  The producer first bulk-copies x into the limb-vector slot;
+// consumers turn it into limbs in place.
+constexpr int SMEM_HDR = 8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES + 4 * 32;
+
+// Bounded spin until the producer has claimed stage `st` for chunk `it`.  A
+// consumer may run several ring cycles ahead of a stage (it skips chunks with
+// no task for it), so the mbarrier parity alone could name a stale phase; the
+// tag makes the following parity wait refer to chunk `it` exactly.
+__device__ __forceinline__ bool wait_gen(const volatile uint32_t* gen, uint32_t st, uint32_t it,
+                                         int* err) {
+  if (gen[st] == it) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (gen[st] != it) {
+    if (globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
+      set_error(err, DERR_TIMEOUT_FULL);
+      return false;
+    }
+  }
+  return true;
+}
+
+// X_b array padded to a 16-byte multiple so xs32 (float2 loads) and xi16
+// (int4 loads) stay aligned for every K.
+__host__ __device__ __forceinline__ uint32_t xbs_floats(uint32_t K) { return ((K / 256) + 3) & ~3u; }
+
+__host__ __device__ __forceinline__ size_t x_region_bytes(uint32_t K, bool has4, bool has6) {
+  size_t b = (size_t)K * 4 + (size_t)xbs_floats(K) * 4;
+  if (has4) b += (size_t)(K / 32) * 4;
+  if (has6) b += (size_t)K;  // int4 per 16 elements
+  return b;
 }
 
 template <bool HAS4, bool HAS6>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + GEMV_STAGES;
-  float* red = reinterpret_cast<float*>(smem + 64);
-  float* xbase = red + 32;
-  const uint32_t K = a.k;
-  float* x4 = xbase;
-  float* x6 = x4 + (HAS4 ? K : 0);
-  float* xs32 = x6 + (HAS6 ? K : 0);
-  float* xm16 = xs32 + (HAS4 ? K / 32 : 0);
-  size_t stage_off = (size_t)(reinterpret_cast<uint8_t*>(xm16 + (HAS6 ? K / 16 : 0)) - smem);
+  uint64_t* empty = full + GEMV_MAX_STAGES;
+  uint64_t* xbar = empty + GEMV_MAX_STAGES;
+  int* done = reinterpret_cast<int*>(xbar + 1);
+  volatile uint32_t* gen = reinterpret_cast<volatile uint32_t*>(done + GEMV_MAX_STAGES);
+  float* red = reinterpret_cast<float*>(smem + 8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES);
+  uint8_t* xreg = smem + ((SMEM_HDR + 127) & ~127);
+  const uint32_t K = a.k, NS = a.n_stages;
+  float* xraw = reinterpret_cast<float*>(xreg);  // raw x, then limb vectors in place
+  int4* xq = reinterpret_cast<int4*>(xreg);
+  float* xbs = reinterpret_cast<float*>(xreg + (size_t)K * 4);
+  float* xs32 = xbs + xbs_floats(K);
+  int4* xi16 = reinterpret_cast<int4*>(xreg + (size_t)K * 4 + (size_t)xbs_floats(K) * 4 +
+                                       (HAS4 ? (size_t)(K / 32) * 4 : 0));
+  size_t stage_off = (size_t)(xreg - smem) + x_region_bytes(K, HAS4, HAS6);
   stage_off = (stage_off + 127) & ~(size_t)127;
   uint8_t* stages = smem + stage_off;
+  const bool x_tma = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GEMV_STAGES; ++s) {
+    for (uint32_t s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], GEMV_WARPS);
+      mbar_init(&empty[s], 1);
+      done[s] = 0;
+      gen[s] = 0xFFFFFFFFu;
     }
+    mbar_init(xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -411,36 +527,41 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   if (warp == GEMV_WARPS) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
+      if (x_tma) {
+        mbar_arrive_expect_tx(xbar, K * 4);
+        bulk_g2s(xraw, a.x, K * 4, xbar);
+      }
       uint32_t it = 0;
       bool ok = true;
       uint64_t seg_off = 0;
       for (uint32_t s = 0; s < a.nseg && ok; ++s) {
         const GemvSeg& g = a.seg[s];
         const Range rr = seg_units(a, s, seg_off, lo, hi);
-        const uint32_t cu = g.chunk_rows / g.rg;
+        const uint32_t ur = (uint32_t)g.rg * g.rl, cu = g.chunk_rows / ur;
         for (uint32_t u = rr.ub; u < rr.ue && ok; u += cu) {
-          const uint32_t r0 = u * g.rg;
-          const uint32_t r1 = min(min(u + cu, rr.ue) * g.rg, g.m);
+          const uint32_t r0 = u * ur;
+          const uint32_t r1 = min(min(u + cu, rr.ue) * ur, g.m);
           const uint32_t bytes = (r1 - r0) * g.row_stride;
-          const int st = it % GEMV_STAGES;
-          if (it >= GEMV_STAGES &&
-              !mbar_wait_bounded(&empty[st], ((it / GEMV_STAGES) - 1) & 1, a.err, DERR_TIMEOUT_EMPTY)) {
+          const uint32_t st = it % NS;
+          if (it >= NS && !mbar_wait_bounded(&empty[st], ((it / NS) - 1) & 1, a.err, DERR_TIMEOUT_EMPTY)) {
             ok = false;
             break;
           }
           uint8_t* dst = stages + (size_t)st * a.stage_bytes;
+          gen[st] = it;
           mbar_arrive_expect_tx(&full[st], g.dual ? 2 * bytes : bytes);
           bulk_g2s(dst, g.w + (size_t)r0 * g.row_stride, bytes, &full[st]);
           if (g.dual) bulk_g2s(dst + bytes, g.w2 + (size_t)r0 * g.row_stride, bytes, &full[st]);
           ++it;
         }
-        seg_off += (uint64_t)((g.m + g.rg - 1) / g.rg) * g.unit_cost;
+        seg_off += (uint64_t)((g.m + ur - 1) / ur) * g.unit_cost;
       }
       // Do not leave the CTA with copies in flight: wait (bounded) for the
-      // last issued stages to land.
-      const uint32_t n_tail = it < (uint32_t)GEMV_STAGES ? it : (uint32_t)GEMV_STAGES;
+      // last issued stages and the input vector to land.
+      const uint32_t n_tail = it < NS ? it : NS;
       for (uint32_t t = it - n_tail; t < it; ++t)
-        mbar_wait_bounded(&full[t % GEMV_STAGES], (t / GEMV_STAGES) & 1, a.err, DERR_TIMEOUT_FULL);
+        mbar_wait_bounded(&full[t % NS], (t / NS) & 1, a.err, DERR_TIMEOUT_FULL);
+      if (x_tma) mbar_wait_bounded(xbar, 0, a.err, DERR_TIMEOUT_FULL);
     }
     return;
   }
@@ -448,15 +569,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   // ------------------------------ consumers -------------------------------
   const int ctid = threadIdx.x;  // 0 .. 32*GEMV_WARPS-1
   constexpr int CT = 32 * GEMV_WARPS;
+  if (x_tma) {
+    if (!mbar_wait_bounded(xbar, 0, a.err, DERR_TIMEOUT_FULL)) return;
+  } else {
+    for (uint32_t i = ctid; i < K; i += CT) xraw[i] = a.x[i];
+    named_sync(1, CT);
+  }
   float inv_rms = 1.0f;
   if (a.norm_w) {
     // RMSNorm prologue (engine/src/ops.c:195-214), fixed-order reduction so
     // every CTA derives the identical scale.
     float ss = 0.f;
-    for (uint32_t i = ctid; i < K; i += CT) {
-      const float v = a.x[i];
-      ss = fmaf(v, v, ss);
-    }
+    for (uint32_t i = ctid; i < K; i += CT) ss = fmaf(xraw[i], xraw[i], ss);
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     named_sync(1, CT);
@@ -465,61 +589,119 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
     for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
     inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
   }
-  // Build scaled input copies and per-group sums; warp w takes 32-element
-  // groups w, w+8, ...
-  for (uint32_t g32 = warp; g32 < K / 32; g32 += GEMV_WARPS) {
-    const uint32_t i = g32 * 32 + lane;
-    float v = a.x[i];
-    if (a.norm_w) v = (v * inv_rms) * a.norm_w[i];
-    if (HAS4) {
-      x4[i] = ldexpf(v, XEXP - q4_pos(i));
-      const float s = warp_sum(v);
-      if (lane == 0) xs32[g32] = s;
-    }
-    if (HAS6) {
-      x6[i] = ldexpf(v, XEXP - q6_pos(i));
-      float s = v;
+  // Fixed-point conversion.  A thread owns one 32-element group (8 vectors);
+  // the 8 threads of a 256-block (consecutive lanes) share its maximum.  The
+  // swizzle only permutes vectors inside a group, so the rewrite is in place.
+  // Whole warps iterate together so the 8-lane shuffles always see full lanes.
+  for (uint32_t base = warp * 32; base < K / 32; base += CT) {
+    const uint32_t g32 = base + lane;
+    const bool valid = g32 < K / 32;
+    float v[32];
+    const float4* src = reinterpret_cast<const float4*>(xraw) + 8 * (valid ? g32 : 0);
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if ((lane & 15) == 0) xm16[2 * g32 + (lane >> 4)] = -32.0f * s;
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = src[q];
+      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+    }
+    if (a.norm_w && valid) {
+      const float* wn = a.norm_w + 32 * g32;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = (v[e] * inv_rms) * __ldg(wn + e);
+    }
+    float amax = 0.f;
+    bool finite = true;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      amax = fmaxf(amax, fabsf(v[e]));
+      finite = finite && isfinite(v[e]);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
+    }
+    // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
+    // whose maximum is below 2^-104 are scaled as if it were 2^-104.
+    const int f = amax > 0.f ? max(ilogbf(amax), -104) : 0;
+    const float xb = finite ? ldexpf(1.0f, f - 21) : __int_as_float(0x7fc00000);
+    const float inv_xb = ldexpf(1.0f, 21 - f);
+    if (!valid) continue;
+    if ((g32 & 7) == 0) xbs[g32 >> 3] = xb;
+    float s16a = 0.f, s16b = 0.f;
+    int l16[2][3] = {{0, 0, 0}, {0, 0, 0}};
+    uint32_t wl[8][3];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int t = finite ? __float2int_rn(v[e] * inv_xb) : 0;
+      const int l0 = (int)(int8_t)(t & 0xFF);
+      const int t1 = (t - l0) >> 8;
+      const int l1 = (int)(int8_t)(t1 & 0xFF);
+      const int l2 = (t1 - l1) >> 8;
+      const int q = e >> 2, c = e & 3;
+      if (c == 0) wl[q][0] = wl[q][1] = wl[q][2] = 0u;
+      wl[q][0] |= (uint32_t)(l0 & 0xFF) << (8 * c);
+      wl[q][1] |= (uint32_t)(l1 & 0xFF) << (8 * c);
+      wl[q][2] |= (uint32_t)(l2 & 0xFF) << (8 * c);
+      if (e < 16) s16a += v[e]; else s16b += v[e];
+      l16[e >> 4][0] += l0;
+      l16[e >> 4][1] += l1;
+      l16[e >> 4][2] += l2;
+    }
+    if (HAS4) xs32[g32] = s16a + s16b;
+    if (HAS6) {
+      xi16[2 * g32] = make_int4(-32 * l16[0][0], -32 * l16[0][1], -32 * l16[0][2], 0);
+      xi16[2 * g32 + 1] = make_int4(-32 * l16[1][0], -32 * l16[1][1], -32 * l16[1][2], 0);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t vi = 8 * g32 + q;
+      xq[vi ^ xsw(vi)] = make_int4((int)wl[q][0], (int)wl[q][1], (int)wl[q][2], 0);
     }
   }
   named_sync(1, CT);
+  const XView xv{xq, xbs, xs32, xi16};
 
+  // Chunks are walked in the producer's order; a warp waits only for chunks
+  // that hold one of its tasks, and the last warp to finish a chunk's tasks
+  // releases the stage.
   uint32_t it = 0, gtask = 0;
   uint64_t seg_off = 0;
   for (uint32_t s = 0; s < a.nseg; ++s) {
     const GemvSeg& g = a.seg[s];
     const Range rr = seg_units(a, s, seg_off, lo, hi);
-    const uint32_t cu = g.chunk_rows / g.rg;
+    const uint32_t ur = (uint32_t)g.rg * g.rl, cu = g.chunk_rows / ur;
     for (uint32_t u = rr.ub; u < rr.ue; u += cu) {
-      const uint32_t r0 = u * g.rg;
-      const uint32_t r1 = min(min(u + cu, rr.ue) * g.rg, g.m);
+      const uint32_t r0 = u * ur;
+      const uint32_t r1 = min(min(u + cu, rr.ue) * ur, g.m);
       const uint32_t nrows = r1 - r0;
-      const int st = it % GEMV_STAGES;
-      if (!mbar_wait_bounded(&full[st], (it / GEMV_STAGES) & 1, a.err, DERR_TIMEOUT_FULL)) return;
-      const uint8_t* buf = stages + (size_t)st * a.stage_bytes;
-      const uint32_t ntasks = (nrows + g.rg - 1) / g.rg;
-      const uint32_t dual_off = nrows * g.row_stride;
+      const uint32_t st = it % NS;
+      const uint32_t ntasks = (nrows + ur - 1) / ur;
       uint32_t t = (uint32_t)((warp - (int)(gtask % GEMV_WARPS) + GEMV_WARPS) % GEMV_WARPS);
-      for (; t < ntasks; t += GEMV_WARPS) {
-        const int rv = (int)min((uint32_t)g.rg, nrows - t * g.rg);
-        const uint8_t* rows = buf + (size_t)t * g.rg * g.row_stride;
-        const uint32_t row0 = r0 + t * g.rg;
-        switch (g.rg) {
-          case 1: task_and_store<1>(a, g, rows, row0, rv, dual_off, x4, x6, xs32, xm16, lane); break;
-          case 2: task_and_store<2>(a, g, rows, row0, rv, dual_off, x4, x6, xs32, xm16, lane); break;
-          case 4: task_and_store<4>(a, g, rows, row0, rv, dual_off, x4, x6, xs32, xm16, lane); break;
-          case 8: task_and_store<8>(a, g, rows, row0, rv, dual_off, x4, x6, xs32, xm16, lane); break;
-          default: task_and_store<16>(a, g, rows, row0, rv, dual_off, x4, x6, xs32, xm16, lane); break;
+      if (t < ntasks) {
+        if (!wait_gen(gen, st, it, a.err)) return;
+        if (!mbar_wait_bounded(&full[st], (it / NS) & 1, a.err, DERR_TIMEOUT_FULL)) return;
+        const uint8_t* buf = stages + (size_t)st * a.stage_bytes;
+        const uint32_t dual_off = nrows * g.row_stride;
+        uint32_t mine = 0;
+        for (; t < ntasks; t += GEMV_WARPS, ++mine) {
+          const int rv = (int)min(ur, nrows - t * ur);
+          const uint8_t* rows = buf + (size_t)t * ur * g.row_stride;
+          dispatch_task(a, g, rows, r0 + t * ur, rv, dual_off, xv, lane);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_block();
+          const int prev = atomicAdd(&done[st], (int)mine);
+          if (prev + (int)mine == (int)ntasks) {
+            done[st] = 0;
+            mbar_arrive(&empty[st]);
+          }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
       gtask += ntasks;
       ++it;
     }
-    seg_off += (uint64_t)((g.m + g.rg - 1) / g.rg) * g.unit_cost;
+    seg_off += (uint64_t)((g.m + ur - 1) / ur) * g.unit_cost;
   }
 }
 
@@ -580,7 +762,8 @@ __global__ void gemv_generic_kernel(uint32_t qt, const uint8_t* __restrict__ w,
 }  // namespace
 
 int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const float* x,
-              const float* norm_w, const uint32_t* pos, float rope_theta, int* err, int num_sms) {
+              const float* norm_w, const uint32_t* pos, const float* rope_freq, int* err,
+              int num_sms) {
   if (nmats < 1 || nmats > GEMV_MAX_SEGS || k == 0 || k % QK) return -1;
   GemvArgs& a = p.args;
   a = GemvArgs{};
@@ -589,7 +772,7 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
   a.x = x;
   a.norm_w = norm_w;
   a.pos = pos;
-  a.rope_theta = rope_theta;
+  a.rope_freq = rope_freq;
   a.err = err;
   p.has4 = p.has6 = 0;
   const uint32_t nb = k / QK;
@@ -615,34 +798,45 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     g.dual = mt.w2 ? 1 : 0;
     if (g.dual != (mt.epi == EPI_SWIGLU)) return -1;
     g.rope_hd = mt.rope_hd;
-    if (mt.epi == EPI_ROPE && (mt.rope_hd == 0 || (mt.rope_hd & 1) || !pos)) return -1;
-    uint32_t rg = 1;
+    if (mt.epi == EPI_ROPE && (mt.rope_hd == 0 || (mt.rope_hd & 1) || !pos || !rope_freq)) return -1;
+    // rg: row groups per warp task so that every lane has a block to work on;
+    // rl: rows per lane (x reuse), smaller for dual segments and huge rows.
+    uint32_t rg = 1, rl;
+    const uint32_t mats_per_row = g.dual ? 2 : 1;
     if (mt.qt == T_Q4K) {
       p.has4 = 1;
       while (rg * 2 <= 8 && rg * 2 * nb <= 8) rg *= 2;
+      rl = g.dual ? 2 : 4;
     } else {
       p.has6 = 1;
       const uint32_t nbc = (nb + 3) / 4;
       while (rg * 2 <= 16 && rg * 2 * nbc <= 16) rg *= 2;
+      rl = g.dual ? 1 : 2;
     }
-    if (mt.epi == EPI_ROPE && rg < 2) rg = 2;
+    while (rl > 1 && (uint64_t)rg * rl * g.row_stride * mats_per_row > 40960) rl /= 2;
+    if (mt.epi == EPI_ROPE && rl < 2) {
+      if (mt.qt != T_Q4K) return -2;  // RoPE rows come from Q4_K q/k projections
+      rl = 2;
+    }
     g.rg = (uint8_t)rg;
-    g.unit_cost = rg * g.row_stride * (g.dual ? 2 : 1);
+    g.rl = (uint8_t)rl;
+    g.unit_cost = rg * rl * g.row_stride * mats_per_row;
     const uint32_t cu = std::max<uint32_t>(1, target / g.unit_cost);
-    g.chunk_rows = cu * rg;
+    g.chunk_rows = cu * rg * rl;
     stage = std::max<uint32_t>(stage, cu * g.unit_cost);
-    const uint64_t units = (mt.m + rg - 1) / rg;
+    const uint64_t units = (mt.m + rg * rl - 1) / (rg * rl);
     total += units * g.unit_cost;
     units_total += units;
   }
   a.stage_bytes = (stage + 127) & ~127u;
   a.total_cost = total;
-  size_t xbytes = 64 + 32 * 4;
-  if (p.has4) xbytes += (size_t)k * 4 + (k / 32) * 4;
-  if (p.has6) xbytes += (size_t)k * 4 + (k / 16) * 4;
+  size_t xbytes = (SMEM_HDR + 127) & ~(size_t)127;
+  xbytes += x_region_bytes(k, p.has4, p.has6);
   xbytes = (xbytes + 127) & ~(size_t)127;
-  p.smem = xbytes + (size_t)GEMV_STAGES * a.stage_bytes;
-  if (p.smem > 227 * 1024) return -4;
+  const size_t budget = 227 * 1024;
+  if (xbytes + 2 * (size_t)a.stage_bytes > budget) return -4;
+  a.n_stages = (uint32_t)std::min<size_t>(GEMV_MAX_STAGES, (budget - xbytes) / a.stage_bytes);
+  p.smem = xbytes + (size_t)a.n_stages * a.stage_bytes;
   p.grid = (int)std::min<uint64_t>((uint64_t)num_sms, units_total);
   if (p.grid < 1) p.grid = 1;
   return 0;

@@ -17,7 +17,7 @@ enum GemvEpi : uint8_t {
 constexpr int GEMV_MAX_SEGS = 4;
 constexpr int GEMV_WARPS = 8;  // consumer warps; one more warp issues the bulk copies
 constexpr int GEMV_THREADS = 32 * (GEMV_WARPS + 1);
-constexpr int GEMV_STAGES = 4;
+constexpr int GEMV_MAX_STAGES = 16;
 
 struct GemvSeg {
   const uint8_t* w;     // matrix: m rows, row r at w + r * row_stride
@@ -26,12 +26,13 @@ struct GemvSeg {
   uint32_t m;           // rows
   uint32_t nb;          // 256-element super-blocks per row
   uint32_t row_stride;  // bytes between rows; multiple of 16
-  uint32_t chunk_rows;  // rows per pipeline stage (multiple of rg)
-  uint32_t unit_cost;   // bytes per rg-row unit (both matrices for dual)
+  uint32_t chunk_rows;  // rows per pipeline stage (multiple of rg * rl)
+  uint32_t unit_cost;   // bytes per task unit of rg * rl rows (both matrices for dual)
   uint32_t rope_hd;     // head_dim for EPI_ROPE
   uint8_t qt;           // 12 = Q4_K, 14 = Q6_K
   uint8_t epi;          // GemvEpi
-  uint8_t rg;           // rows per warp task
+  uint8_t rg;           // row groups per warp task (lanes split across groups)
+  uint8_t rl;           // rows per lane (each loaded x value feeds rl rows)
   uint8_t dual;         // 1 for gate/up pairs
 };
 
@@ -42,8 +43,9 @@ struct GemvArgs {
   const float* x;           // k floats
   const float* norm_w;      // optional: x <- rmsnorm(x) * norm_w  (eps 1e-5)
   const uint32_t* pos;      // device position for EPI_ROPE
-  float rope_theta;
+  const float* rope_freq;   // EPI_ROPE: freq[i/2] = powf(1/theta, i/head_dim), host libm
   uint32_t stage_bytes;     // bytes per pipeline stage
+  uint32_t n_stages;        // ring depth (<= GEMV_MAX_STAGES)
   uint64_t total_cost;      // sum over segments of units * unit_cost
   int* err;                 // device error word
 };
@@ -69,7 +71,7 @@ struct GemvMat {
 
 // Returns 0 on success, negative on unsupported shapes (caller may fall back).
 int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const float* x,
-              const float* norm_w, const uint32_t* pos, float rope_theta, int* err,
+              const float* norm_w, const uint32_t* pos, const float* rope_freq, int* err,
               int num_sms);
 // Sets the kernels' dynamic shared-memory limit; call once per device.
 cudaError_t gemv_init();

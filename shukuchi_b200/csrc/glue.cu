@@ -143,14 +143,15 @@ __global__ void rmsnorm_kernel(const float* x, const float* w, float* y, uint32_
 }
 
 // op_rope (engine/src/ops.c:216-238)
+// freq[i/2] = powf(1/theta, i/hd) is computed on the host with the C library,
+// so pos * freq matches the reference's fp32 angle exactly.
 __global__ void rope_kernel(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos_p,
-                            float theta) {
+                            const float* freq) {
   const uint32_t pairs = n_heads * (hd / 2);
   const uint32_t pos = *pos_p;
   for (uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x) {
     const uint32_t h = p / (hd / 2), i = 2 * (p % (hd / 2));
-    const float freq = powf(1.0f / theta, (float)i / (float)hd);
-    const float ang = (float)pos * freq;
+    const float ang = (float)pos * freq[i >> 1];
     const float c = cosf(ang), s = sinf(ang);
     float* v = qk + (size_t)h * hd + i;
     const float a = v[0], b = v[1];
@@ -199,11 +200,16 @@ cudaError_t rmsnorm_launch(const float* x, const float* w, float* y, uint32_t d,
   return cudaGetLastError();
 }
 
-cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos, float theta,
-                        cudaStream_t st) {
+cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos,
+                        const float* freq, cudaStream_t st) {
   const uint32_t pairs = n_heads * (hd / 2);
-  rope_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(qk, n_heads, hd, pos, theta);
+  rope_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(qk, n_heads, hd, pos, freq);
   return cudaGetLastError();
+}
+
+void rope_freq_table(float theta, uint32_t hd, float* out) {
+  const float inv_theta = 1.0f / theta;
+  for (uint32_t i = 0; i + 1 < hd; i += 2) out[i / 2] = powf(inv_theta, (float)i / (float)hd);
 }
 
 cudaError_t swiglu_launch(const float* g, const float* u, float* h, uint32_t n, cudaStream_t st) {

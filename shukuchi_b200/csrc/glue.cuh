@@ -12,8 +12,11 @@ int argmax_blocks(uint32_t n);
 cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* part_i, int* counter,
                           uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st);
 cudaError_t rmsnorm_launch(const float* x, const float* w, float* y, uint32_t d, cudaStream_t st);
-cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos, float theta,
-                        cudaStream_t st);
+cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos,
+                        const float* freq, cudaStream_t st);
+// freq[i/2] = powf(1/theta, i/head_dim) for even i (engine/src/ops.c:223-227),
+// evaluated with the host C library.
+void rope_freq_table(float theta, uint32_t head_dim, float* out);
 cudaError_t swiglu_launch(const float* g, const float* u, float* h, uint32_t n, cudaStream_t st);
 cudaError_t add_launch(float* y, const float* x, uint32_t n, cudaStream_t st);
 

@@ -40,6 +40,8 @@ struct shk_ctx {
   float* am_v = nullptr;
   uint32_t* am_i = nullptr;
   int* am_cnt = nullptr;
+  float* d_freq = nullptr;  // RoPE frequency table for shk_cuda_rope (<= 512 entries)
+  float* h_freq = nullptr;  // pinned
   // synchronous host-pointer matvec scratch
   void* hv_w = nullptr;
   size_t hv_w_cap = 0;
@@ -87,8 +89,10 @@ struct shk_model {
   std::vector<shk_layer_desc> layers;
   std::vector<uint8_t> have;
   std::vector<LayerPlans> plans;
+  float* d_freq = nullptr;  // RoPE table: powf(1/theta, i/head_dim), host libm
   GemvPlan head;
-  bool head_ok = false;
+  bool head_ok = false;      // staged plan available for the output head
+  bool head_generic = false; // rows not 16-byte multiples: plain-load GEMV
   cudaGraphExec_t g_layers = nullptr, g_head = nullptr, g_loop = nullptr;
 };
 
@@ -113,7 +117,7 @@ int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y,
   if (m == 0) return SHK_OK;
   GemvMat mt{w, nullptr, y, m, qt, 0, EPI_STORE, 0};
   GemvPlan p;
-  const int rc = gemv_plan(p, &mt, 1, k, x, nullptr, nullptr, 0.f, c->d_err, c->num_sms);
+  const int rc = gemv_plan(p, &mt, 1, k, x, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc == -2) return SHK_EUNSUPPORTED;
   if (rc == 0) {
     CK(gemv_launch(p, st));
@@ -202,6 +206,8 @@ shk_ctx* shk_cuda_init(const shk_cuda_config* cfg) {
   ok = ok && cudaMalloc(&c->am_i, 256 * sizeof(uint32_t)) == cudaSuccess;
   ok = ok && cudaMalloc(&c->am_cnt, sizeof(int)) == cudaSuccess;
   ok = ok && cudaMemset(c->am_cnt, 0, sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMalloc(&c->d_freq, 512 * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&c->h_freq, 512 * sizeof(float)) == cudaSuccess;
   ok = ok && gemv_init() == cudaSuccess;
   if (!ok) {
     shk_cuda_shutdown(c);
@@ -223,6 +229,8 @@ void shk_cuda_shutdown(shk_ctx* c) {
   cudaFree(c->am_v);
   cudaFree(c->am_i);
   cudaFree(c->am_cnt);
+  cudaFree(c->d_freq);
+  cudaFreeHost(c->h_freq);
   cudaFree(c->hv_w);
   cudaFree(c->hv_x);
   cudaFree(c->hv_y);
@@ -313,13 +321,15 @@ int shk_cuda_rmsnorm(shk_ctx* c, const float* x, const float* w, float* y, uint3
 
 int shk_cuda_rope(shk_ctx* c, float* qk, uint32_t n_heads, uint32_t hd, uint32_t pos, float theta,
                   void* s) {
-  if (!c || !qk || hd == 0 || (hd & 1)) return SHK_EINVAL;
+  if (!c || !qk || hd == 0 || (hd & 1) || hd > 1024 || !(theta > 0.f)) return SHK_EINVAL;
   cudaStream_t st = pick(c, s);
-  // position goes through a stream-ordered copy so the call stays async
+  // position and frequency table go through stream-ordered copies
   CK(cudaStreamSynchronize(st));
   c->h_u32[0] = pos;
+  rope_freq_table(theta, hd, c->h_freq);
   CK(cudaMemcpyAsync(c->d_u32, c->h_u32, 4, cudaMemcpyHostToDevice, st));
-  CK(rope_launch(qk, n_heads, hd, c->d_u32, theta, st));
+  CK(cudaMemcpyAsync(c->d_freq, c->h_freq, (hd / 2) * sizeof(float), cudaMemcpyHostToDevice, st));
+  CK(rope_launch(qk, n_heads, hd, c->d_u32, c->d_freq, st));
   return SHK_OK;
 }
 
@@ -476,18 +486,17 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
       {lv.attn_k, nullptr, m->k, kvd, lv.attn_k_dtype, 0, EPI_ROPE, hd},
       {lv.attn_v, nullptr, m->v, kvd, lv.attn_v_dtype, lv.row_stride_v, EPI_STORE, 0},
   };
-  const float theta = d.rope_theta > 0.f ? d.rope_theta : 10000.0f;
-  int rc = gemv_plan(P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos, theta, c->d_err, c->num_sms);
+  int rc = gemv_plan(P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos, m->d_freq, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
   GemvMat o{lv.attn_o, nullptr, m->hidden, d.n_embd, lv.attn_o_dtype, 0, EPI_ADD, 0};
-  rc = gemv_plan(P.o, &o, 1, qd, m->att, nullptr, nullptr, 0.f, c->d_err, c->num_sms);
+  rc = gemv_plan(P.o, &o, 1, qd, m->att, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
   if (lv.ffn_gate_dtype != lv.ffn_up_dtype) return SHK_EUNSUPPORTED;
   GemvMat gu{lv.ffn_gate, lv.ffn_up, m->act, d.n_ff, lv.ffn_gate_dtype, 0, EPI_SWIGLU, 0};
-  rc = gemv_plan(P.gateup, &gu, 1, d.n_embd, m->hidden, lv.ffn_norm, nullptr, 0.f, c->d_err, c->num_sms);
+  rc = gemv_plan(P.gateup, &gu, 1, d.n_embd, m->hidden, lv.ffn_norm, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
   GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, EPI_ADD, 0};
-  rc = gemv_plan(P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr, 0.f, c->d_err, c->num_sms);
+  rc = gemv_plan(P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
   P.ok = true;
   return SHK_OK;
@@ -523,7 +532,11 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
 }
 
 int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos) {
-  CK(gemv_launch(m->head, st));
+  if (m->head_generic)
+    CK(gemv_generic_launch(m->d.output_dtype, m->d.output_dev, m->hidden, m->logits, m->d.n_vocab,
+                           m->d.n_embd, st));
+  else
+    CK(gemv_launch(m->head, st));
   CK(argmax_launch(m->logits, m->d.n_vocab, m->am_v, m->am_i, m->am_cnt, m->d_tok,
                    advance_pos ? m->d_tok + 1 : nullptr, st));
   return SHK_OK;
@@ -603,8 +616,22 @@ shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv
   m->have.assign(d->n_layers, 0);
   m->plans.resize(d->n_layers);
   GemvMat hm{d->output_dev, nullptr, m->logits, d->n_vocab, d->output_dtype, 0, EPI_STORE, 0};
-  m->head_ok = gemv_plan(m->head, &hm, 1, d->n_embd, m->hidden, nullptr, nullptr, 0.f, c->d_err,
-                         c->num_sms) == 0;
+  const int hp = gemv_plan(m->head, &hm, 1, d->n_embd, m->hidden, nullptr, nullptr, nullptr,
+                           c->d_err, c->num_sms);
+  if (hp == -2 || d->n_embd % QK) {  // unsupported dtype
+    shk_cuda_model_destroy(m);
+    return nullptr;
+  }
+  m->head_ok = true;
+  m->head_generic = hp != 0;
+  // RoPE frequencies with the host C library (engine/src/ops.c:223-227)
+  std::vector<float> fr(d->head_dim / 2);
+  rope_freq_table(d->rope_theta > 0.f ? d->rope_theta : 10000.0f, d->head_dim, fr.data());
+  if (cudaMalloc(&m->d_freq, fr.size() * sizeof(float)) != cudaSuccess ||
+      cudaMemcpy(m->d_freq, fr.data(), fr.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+    shk_cuda_model_destroy(m);
+    return nullptr;
+  }
   return m;
 }
 
@@ -624,6 +651,7 @@ void shk_cuda_model_destroy(shk_model* m) {
   cudaFree(m->am_cnt);
   cudaFree(m->d_tok);
   cudaFreeHost(m->h_tok);
+  cudaFree(m->d_freq);
   delete m;
 }
 
@@ -754,7 +782,7 @@ int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void
   };
   uint64_t bytes = 0;
   if (part == 5) {
-    if (!m->head_ok) return SHK_EINVAL;
+    if (!m->head_ok || m->head_generic) return SHK_EINVAL;
     CK(gemv_launch(m->head, st));
     bytes = wbytes(m->head);
   } else if (part == 1) {

@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 def test_embed_bit_exact(oracle, ctx):
     g = golden("embed")
     out = torch.zeros(512, device="cuda")
-    ctx.embed(to_dev(g["table"]).data_ptr(), 12, 10, int(g["token"]), out.data_ptr(), 512)
+    table_d = to_dev(g["table"])  # keep the device copy alive until the kernel ran
+    ctx.embed(table_d.data_ptr(), 12, 10, int(g["token"]), out.data_ptr(), 512)
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), g["out"])
     rng = np.random.default_rng(1)
@@ -54,9 +55,11 @@ def test_rmsnorm(oracle, ctx):
         x = rng.normal(0, 5, d).astype(np.float32)
         w = (1 + rng.normal(0, 0.02, d)).astype(np.float32)
         y = torch.zeros(d, device="cuda")
-        ctx.rmsnorm(to_dev(x).data_ptr(), to_dev(w).data_ptr(), y.data_ptr(), d)
+        xd, wd = to_dev(x), to_dev(w)
+        ctx.rmsnorm(xd.data_ptr(), wd.data_ptr(), y.data_ptr(), d)
         torch.cuda.synchronize()
-        np.testing.assert_allclose(y.cpu().numpy(), oracle.rmsnorm(x, w), rtol=2e-6, atol=1e-7)
+        # sum of squares in a different order: 1/sqrt(mean) agrees to ~sqrt(d)*eps
+        np.testing.assert_allclose(y.cpu().numpy(), oracle.rmsnorm(x, w), rtol=3e-5, atol=1e-7)
 
 
 @pytest.mark.parametrize("pos", [0, 1, 37, 2047, 32767])
@@ -75,6 +78,7 @@ def test_swiglu(oracle, ctx):
     g = rng.normal(0, 4, 5000).astype(np.float32)
     u = rng.normal(0, 4, 5000).astype(np.float32)
     h = torch.zeros(5000, device="cuda")
-    ctx.swiglu(to_dev(g).data_ptr(), to_dev(u).data_ptr(), h.data_ptr(), 5000)
+    gd, ud = to_dev(g), to_dev(u)
+    ctx.swiglu(gd.data_ptr(), ud.data_ptr(), h.data_ptr(), 5000)
     torch.cuda.synchronize()
     np.testing.assert_allclose(h.cpu().numpy(), oracle.swiglu(g, u), rtol=2e-6, atol=1e-6)

@@ -18,7 +18,9 @@
 // x by dp4a, exactly, in int32.  Each 256-element block of x is written as
 // X_b * x_int with X_b a power of two and |x_int| <= 2^22 (24-bit fixed point,
 // relative step 2^-22 of the block maximum, i.e. fp32-level precision for the
-// dot product), and x_int = l0 + 256*l1 + 65536*l2 with int8 limbs.  Per
+// dot product), and x_int = l0 + 256*l1 + 65536*l2 where l0, l1 are its two low
+// bytes (unsigned) and l2 its third byte read as signed: two's complement makes
+// the bytes of x_int exactly its limbs.  Per
 // sub-block the three limb sums are scaled by the 6-bit (Q4_K) or int8 (Q6_K)
 // sub-block scale with IMAD, then per block converted to float and multiplied by
 // d * X_b.  The Q4_K min term uses fp32 sums of x; the Q6_K -32 offset is folded
@@ -41,83 +43,104 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
 }
 
 // x limbs live in shared memory as int4 vectors {l0 word, l1 word, l2 word, 0}
-// (4 elements each) under an XOR swizzle: vector v is stored at v ^ xsw(v).
-// Lanes of a warp read x at the same offset inside different blocks; without
-// the swizzle every lane would hit the same four banks.  xsw is constant over
-// each aligned run of 8 vectors, so a lane computes it once per run.
-__device__ __forceinline__ uint32_t xsw(uint32_t v) { return ((v >> 3) ^ (v >> 6) ^ (v >> 8)) & 7u; }
+// (4 elements each).  Vector v is stored at v + v/64: one pad vector after
+// every 256-element block.  A block's 64 vectors are then contiguous (lanes use
+// constant offsets), and lanes reading the same offset in consecutive blocks
+// land in distinct bank groups.
+__device__ __forceinline__ uint32_t xpad(uint32_t v) { return v + (v >> 6); }
 
-__device__ __forceinline__ int dp4a(uint32_t a, int b, int c) { return __dp4a((int)a, b, c); }
+// Limbs 0 and 1 of x are unsigned bytes, limb 2 is a signed byte (see the
+// prologue); quants are unsigned and below 64, so limb 2 may use the signed form.
+__device__ __forceinline__ int dp4a_u(uint32_t a, int b, int c) {
+  return (int)__dp4a(a, (uint32_t)b, (uint32_t)c);
+}
+__device__ __forceinline__ int dp4a_s(uint32_t a, int b, int c) { return __dp4a((int)a, b, c); }
 
 __device__ __forceinline__ float limbs_to_float(int a0, int a1, int a2) {
   return fmaf(65536.0f, (float)a2, fmaf(256.0f, (float)a1, (float)a0));
 }
 
 // ------------------------------- Q4_K ---------------------------------------
-// Lane (s, j) handles 64-element group j (32 quant bytes) of block b for RL rows
-// (and both matrices of a dual segment): the low nibbles are sub-block 2j, the
-// high nibbles sub-block 2j+1.  x limbs are loaded once and used NR times.
+// A lane owns whole blocks b (all 256 elements) for RL rows (and both matrices
+// of a dual segment), so each row's scale/min decode and block epilogue is paid
+// once per 256 weights.  The four 64-element groups j are walked in a rolled
+// loop (compact code); within a group the low nibbles are sub-block 2j and the
+// high nibbles sub-block 2j+1 (engine/src/ops.c:117-142).
 template <int RL, bool DUAL>
-__device__ __forceinline__ void q4k_block_rows(const uint8_t* __restrict__ blk, uint32_t row_stride,
-                                               uint32_t dual_off, int j,
-                                               const int4* __restrict__ xq, uint32_t v0, float xb,
-                                               float2 xsum, float (&acc)[RL][2]) {
+__device__ __forceinline__ void q4k_block_rows(const uint8_t* const (&rp)[RL * (DUAL ? 2 : 1)],
+                                               uint32_t boff, const int4* __restrict__ xblk,
+                                               float xb, const float* __restrict__ xs,
+                                               float (&acc)[RL][2]) {
   constexpr int NR = RL * (DUAL ? 2 : 1);
-  uint4 hdr[NR];
-  uint32_t w[NR][8];
+  uint32_t scl[NR], sch[NR], ml[NR], mh[NR];
+  float dx[NR], dm[NR];
 #pragma unroll
   for (int r = 0; r < NR; ++r) {
-    const uint8_t* p = blk + (size_t)(r % RL) * row_stride + (r >= RL ? dual_off : 0);
-    hdr[r] = *reinterpret_cast<const uint4*>(p);
-    const uint4 q0 = *reinterpret_cast<const uint4*>(p + 16 + 32 * j);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(p + 32 + 32 * j);
-    w[r][0] = q0.x; w[r][1] = q0.y; w[r][2] = q0.z; w[r][3] = q0.w;
-    w[r][4] = q1.x; w[r][5] = q1.y; w[r][6] = q1.z; w[r][7] = q1.w;
+    const uint4 h = *reinterpret_cast<const uint4*>(rp[r] + boff);
+    // 6-bit scales/mins of sub-blocks 0-3 and 4-7, packed four per word
+    // (engine/src/ops.c:107-115 get_scale_min_k4)
+    scl[r] = h.y & 0x3F3F3F3Fu;
+    ml[r] = h.z & 0x3F3F3F3Fu;
+    sch[r] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    mh[r] = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    dx[r] = ref_half(h.x & 0xFFFFu) * xb;
+    dm[r] = ref_half(h.x >> 16);
   }
-  int S[NR][2][3];
+  int A[NR][3];
+  float M[NR];
 #pragma unroll
-  for (int r = 0; r < NR; ++r)
+  for (int r = 0; r < NR; ++r) {
+    A[r][0] = A[r][1] = A[r][2] = 0;
+    M[r] = 0.f;
+  }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) S[r][h][0] = S[r][h][1] = S[r][h][2] = 0;
-  const uint32_t slo = xsw(v0), shi = xsw(v0 + 8);
+  for (int j = 0; j < 4; ++j) {
+    int S[NR][2][3];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int4 xl = xq[v0 + (i ^ slo)];
-    const int4 xh = xq[v0 + 8 + (i ^ shi)];
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) S[r][hh][0] = S[r][hh][1] = S[r][hh][2] = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // qs words 4*half .. 4*half+3
+      uint4 w[NR];
+#pragma unroll
+      for (int r = 0; r < NR; ++r)
+        w[r] = *reinterpret_cast<const uint4*>(rp[r] + boff + 16 + 32 * j + 16 * half);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int4 xl = xblk[16 * j + 4 * half + i];
+        const int4 xh = xblk[16 * j + 8 + 4 * half + i];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          const uint32_t q = i == 0 ? w[r].x : i == 1 ? w[r].y : i == 2 ? w[r].z : w[r].w;
+          const uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;
+          S[r][0][0] = dp4a_u(lo, xl.x, S[r][0][0]);
+          S[r][0][1] = dp4a_u(lo, xl.y, S[r][0][1]);
+          S[r][0][2] = dp4a_s(lo, xl.z, S[r][0][2]);
+          S[r][1][0] = dp4a_u(hi, xh.x, S[r][1][0]);
+          S[r][1][1] = dp4a_u(hi, xh.y, S[r][1][1]);
+          S[r][1][2] = dp4a_s(hi, xh.z, S[r][1][2]);
+        }
+      }
+    }
+    const float2 xsum = *reinterpret_cast<const float2*>(xs + 2 * j);
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
-      const uint32_t lo = w[r][i] & 0x0F0F0F0Fu, hi = (w[r][i] >> 4) & 0x0F0F0F0Fu;
-      S[r][0][0] = dp4a(lo, xl.x, S[r][0][0]);
-      S[r][0][1] = dp4a(lo, xl.y, S[r][0][1]);
-      S[r][0][2] = dp4a(lo, xl.z, S[r][0][2]);
-      S[r][1][0] = dp4a(hi, xh.x, S[r][1][0]);
-      S[r][1][1] = dp4a(hi, xh.y, S[r][1][1]);
-      S[r][1][2] = dp4a(hi, xh.z, S[r][1][2]);
+      const uint32_t scw = j < 2 ? scl[r] : sch[r], mw = j < 2 ? ml[r] : mh[r];
+      // bytes 2(j&1), 2(j&1)+1 of the packed words: sub-blocks 2j, 2j+1
+      const int sc0 = (int)__byte_perm(scw, 0u, 0x4440 + 2 * (j & 1));
+      const int sc1 = (int)__byte_perm(scw, 0u, 0x4441 + 2 * (j & 1));
+      const int m0 = (int)__byte_perm(mw, 0u, 0x4440 + 2 * (j & 1));
+      const int m1 = (int)__byte_perm(mw, 0u, 0x4441 + 2 * (j & 1));
+      A[r][0] += sc0 * S[r][0][0] + sc1 * S[r][1][0];
+      A[r][1] += sc0 * S[r][0][1] + sc1 * S[r][1][1];
+      A[r][2] += sc0 * S[r][0][2] + sc1 * S[r][1][2];
+      M[r] = fmaf((float)m0, xsum.x, fmaf((float)m1, xsum.y, M[r]));
     }
   }
-  // Scales/mins of sub-blocks 2j, 2j+1 (engine/src/ops.c:107-115 get_scale_min_k4),
-  // decoded four at a time from the packed 12-byte field.
-  const int sh = (j & 1) * 16;
 #pragma unroll
-  for (int r = 0; r < NR; ++r) {
-    const uint4 h = hdr[r];
-    uint32_t scw, mw;
-    if (j < 2) {
-      scw = h.y & 0x3F3F3F3Fu;
-      mw = h.z & 0x3F3F3F3Fu;
-    } else {
-      scw = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-      mw = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-    }
-    const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
-    const int m0 = (mw >> sh) & 0xFF, m1 = (mw >> (sh + 8)) & 0xFF;
-    const int a0 = sc0 * S[r][0][0] + sc1 * S[r][1][0];
-    const int a1 = sc0 * S[r][0][1] + sc1 * S[r][1][1];
-    const int a2 = sc0 * S[r][0][2] + sc1 * S[r][1][2];
-    const float d = ref_half(h.x & 0xFFFFu), dmin = ref_half(h.x >> 16);
-    const float mins = fmaf((float)m0, xsum.x, (float)m1 * xsum.y);
-    acc[r % RL][r / RL] += fmaf(d * xb, limbs_to_float(a0, a1, a2), -(dmin * mins));
-  }
+  for (int r = 0; r < NR; ++r)
+    acc[r % RL][r / RL] += fmaf(dx[r], limbs_to_float(A[r][0], A[r][1], A[r][2]), -(dm[r] * M[r]));
 }
 
 template <int RL, bool DUAL>
@@ -126,18 +149,20 @@ __device__ __forceinline__ void q4k_task(const uint8_t* __restrict__ rows, uint3
                                          const int4* __restrict__ xq, const float* __restrict__ xbs,
                                          const float* __restrict__ xs32, int lane, int lg_rg,
                                          float (&acc)[RL][2]) {
-  const int SPR = 8 >> lg_rg;  // block slots per row group
-  const int slot = lane >> 2, j = lane & 3;
-  const int g = slot >> (3 - lg_rg), s = slot & (SPR - 1);
+  constexpr int NR = RL * (DUAL ? 2 : 1);
+  const int SPR = 32 >> lg_rg;  // block slots (lanes) per row group
+  const int g = lane >> (5 - lg_rg), s = lane & (SPR - 1);
 #pragma unroll
   for (int r = 0; r < RL; ++r) acc[r][0] = acc[r][1] = 0.f;
   if (g * RL < rows_valid) {
-    const uint8_t* row = rows + (size_t)(g * RL) * row_stride;
-    for (uint32_t b = s; b < nb; b += SPR) {
-      const float2 xsum = *reinterpret_cast<const float2*>(xs32 + b * 8 + 2 * j);
-      q4k_block_rows<RL, DUAL>(row + (size_t)b * Q4K_BYTES, row_stride, dual_off, j, xq,
-                               b * 64 + 16 * j, xbs[b], xsum, acc);
-    }
+    // Rows past rows_valid read stale (in-bounds) stage bytes; their results
+    // are never stored.
+    const uint8_t* rp[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+      rp[r] = rows + (size_t)(g * RL + (r % RL)) * row_stride + (r >= RL ? dual_off : 0);
+    for (uint32_t b = s; b < nb; b += SPR)
+      q4k_block_rows<RL, DUAL>(rp, b * Q4K_BYTES, xq + 65 * b, xbs[b], xs32 + 8 * b, acc);
   }
   for (int o = 16 >> lg_rg; o > 0; o >>= 1)
 #pragma unroll
@@ -148,75 +173,25 @@ __device__ __forceinline__ void q4k_task(const uint8_t* __restrict__ rows, uint3
 }
 
 // ------------------------------- Q6_K ---------------------------------------
-// Blocks are 210 bytes, so a block's offset inside a 16-byte-aligned row is
-// 2*b mod 16.  Lanes of a warp always work on blocks b == C (mod 4), which
-// share the alignment MU = 2*C mod 8 of every field; MU is a template constant.
-template <int MU>
-__device__ __forceinline__ void load32(const uint8_t* p, uint32_t o[8]) {
-  if (MU == 0) {
+// Blocks are 210 bytes: inside a 16-byte-aligned row, block b starts at an
+// address == 2*b (mod 4).  Lanes of a warp always work on blocks of the same
+// parity P, so every field is either word aligned (P = 0) or two bytes past a
+// word (P = 1); P is a template constant and fields are read as 32-bit words.
+template <int P, int NW>
+__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&o)[NW]) {
+  if (P == 0) {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint2 v = *reinterpret_cast<const uint2*>(p + 8 * i);
-      o[2 * i] = v.x;
-      o[2 * i + 1] = v.y;
-    }
-  } else if (MU == 4) {
-    o[0] = *reinterpret_cast<const uint32_t*>(p);
+    for (int i = 0; i < NW; ++i) o[i] = q[i];
+  } else {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - 2);
+    uint32_t prev = q[0];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const uint2 v = *reinterpret_cast<const uint2*>(p + 4 + 8 * i);
-      o[1 + 2 * i] = v.x;
-      o[2 + 2 * i] = v.y;
+    for (int i = 0; i < NW; ++i) {
+      const uint32_t nx = q[i + 1];
+      o[i] = __byte_perm(prev, nx, 0x5432);
+      prev = nx;
     }
-    o[7] = *reinterpret_cast<const uint32_t*>(p + 28);
-  } else if (MU == 2) {
-    const uint32_t a = *reinterpret_cast<const uint16_t*>(p);
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 2);
-    const uint2 d0 = *reinterpret_cast<const uint2*>(p + 6);
-    const uint2 d1 = *reinterpret_cast<const uint2*>(p + 14);
-    const uint2 d2 = *reinterpret_cast<const uint2*>(p + 22);
-    const uint32_t z = *reinterpret_cast<const uint16_t*>(p + 30);
-    o[0] = __byte_perm(a, w, 0x5410);
-    o[1] = __byte_perm(w, d0.x, 0x5432);
-    o[2] = __byte_perm(d0.x, d0.y, 0x5432);
-    o[3] = __byte_perm(d0.y, d1.x, 0x5432);
-    o[4] = __byte_perm(d1.x, d1.y, 0x5432);
-    o[5] = __byte_perm(d1.y, d2.x, 0x5432);
-    o[6] = __byte_perm(d2.x, d2.y, 0x5432);
-    o[7] = __byte_perm(d2.y, z, 0x5432);
-  } else {  // MU == 6
-    const uint32_t a = *reinterpret_cast<const uint16_t*>(p);
-    const uint2 d0 = *reinterpret_cast<const uint2*>(p + 2);
-    const uint2 d1 = *reinterpret_cast<const uint2*>(p + 10);
-    const uint2 d2 = *reinterpret_cast<const uint2*>(p + 18);
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 26);
-    const uint32_t z = *reinterpret_cast<const uint16_t*>(p + 30);
-    o[0] = __byte_perm(a, d0.x, 0x5410);
-    o[1] = __byte_perm(d0.x, d0.y, 0x5432);
-    o[2] = __byte_perm(d0.y, d1.x, 0x5432);
-    o[3] = __byte_perm(d1.x, d1.y, 0x5432);
-    o[4] = __byte_perm(d1.y, d2.x, 0x5432);
-    o[5] = __byte_perm(d2.x, d2.y, 0x5432);
-    o[6] = __byte_perm(d2.y, w, 0x5432);
-    o[7] = __byte_perm(w, z, 0x5432);
-  }
-}
-
-template <int MU>
-__device__ __forceinline__ void load8(const uint8_t* p, uint32_t o[2]) {
-  if (MU == 0) {
-    const uint2 v = *reinterpret_cast<const uint2*>(p);
-    o[0] = v.x;
-    o[1] = v.y;
-  } else if (MU == 4) {
-    o[0] = *reinterpret_cast<const uint32_t*>(p);
-    o[1] = *reinterpret_cast<const uint32_t*>(p + 4);
-  } else {  // 2 or 6: p+2 is 4-byte aligned
-    const uint32_t a = *reinterpret_cast<const uint16_t*>(p);
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 2);
-    const uint32_t z = *reinterpret_cast<const uint16_t*>(p + 6);
-    o[0] = __byte_perm(a, w, 0x5410);
-    o[1] = __byte_perm(w, z, 0x5432);
   }
 }
 
@@ -225,26 +200,24 @@ __device__ __forceinline__ void load8(const uint8_t* p, uint32_t o[2]) {
 // ql/qh, four words of exact 6-bit quants are formed (element groups +0, +32,
 // +64, +96) and fed to dp4a.  Each 16-element scale group's three limb sums
 // start at -32 * (sum of x limbs), which applies the -32 offset.
-template <int MU, int RL>
+template <int P, int RL>
 __device__ __forceinline__ void q6k_block_rows(const uint8_t* __restrict__ blk, uint32_t row_stride,
                                                int n, const int4* __restrict__ xq, uint32_t b,
                                                const int4* __restrict__ xi, float xb,
                                                float (&acc)[RL]) {
-  uint32_t A[RL][8], B[RL][8], H[RL][8], SC[RL][2], db[RL];
+  const uint32_t M = 0x0F0F0F0Fu;
+  const int4* xh = xq + 65 * b + 32 * n;  // this half's 32 vectors; group g at +8g
+  uint32_t A[RL][8], B[RL][8], H[RL][8], SC[RL][2];
+  float dd[RL];
 #pragma unroll
   for (int r = 0; r < RL; ++r) {
     const uint8_t* p = blk + (size_t)r * row_stride;
-    load32<MU>(p + 64 * n, A[r]);
-    load32<MU>(p + 64 * n + 32, B[r]);
-    load32<MU>(p + 128 + 32 * n, H[r]);
-    load8<MU>(p + 192 + 8 * n, SC[r]);
-    db[r] = *reinterpret_cast<const uint16_t*>(p + 208);
+    load_words<P, 8>(p + 64 * n, A[r]);
+    load_words<P, 8>(p + 64 * n + 32, B[r]);
+    load_words<P, 8>(p + 128 + 32 * n, H[r]);
+    load_words<P, 2>(p + 192 + 8 * n, SC[r]);
+    dd[r] = ref_half(*reinterpret_cast<const uint16_t*>(p + 208)) * xb;
   }
-  const uint32_t M = 0x0F0F0F0Fu;
-  const uint32_t vb = b * 64 + 32 * n;  // first int4 of this half; group g at vb + 8g
-  uint32_t sw[4];
-#pragma unroll
-  for (int g = 0; g < 4; ++g) sw[g] = xsw(vb + 8 * g);
   int T[RL][3];
 #pragma unroll
   for (int r = 0; r < RL; ++r) T[r][0] = T[r][1] = T[r][2] = 0;
@@ -265,7 +238,7 @@ __device__ __forceinline__ void q6k_block_rows(const uint8_t* __restrict__ blk, 
     for (int i = 4 * is; i < 4 * is + 4; ++i) {
       int4 xv[4];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) xv[g] = xq[vb + 8 * g + (i ^ sw[g])];
+      for (int g = 0; g < 4; ++g) xv[g] = xh[8 * g + i];
 #pragma unroll
       for (int r = 0; r < RL; ++r) {
         const uint32_t h = H[r][i];
@@ -274,9 +247,9 @@ __device__ __forceinline__ void q6k_block_rows(const uint8_t* __restrict__ blk, 
                                lop_sel(A[r][i] >> 4, hm, M), lop_sel(B[r][i] >> 4, hn >> 2, M)};
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          S[r][g][0] = dp4a(Q[g], xv[g].x, S[r][g][0]);
-          S[r][g][1] = dp4a(Q[g], xv[g].y, S[r][g][1]);
-          S[r][g][2] = dp4a(Q[g], xv[g].z, S[r][g][2]);
+          S[r][g][0] = dp4a_u(Q[g], xv[g].x, S[r][g][0]);
+          S[r][g][1] = dp4a_u(Q[g], xv[g].y, S[r][g][1]);
+          S[r][g][2] = dp4a_s(Q[g], xv[g].z, S[r][g][2]);
         }
       }
     }
@@ -285,28 +258,27 @@ __device__ __forceinline__ void q6k_block_rows(const uint8_t* __restrict__ blk, 
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int si = is + 2 * g;  // scale index within this half
-        const int sc = (int)(int8_t)((SC[r][si >> 2] >> (8 * (si & 3))) & 0xFFu);
+        const int sc = (int)(int8_t)__byte_perm(SC[r][si >> 2], 0u, 0x4440 + (si & 3));
         T[r][0] += sc * S[r][g][0];
         T[r][1] += sc * S[r][g][1];
         T[r][2] += sc * S[r][g][2];
       }
   }
 #pragma unroll
-  for (int r = 0; r < RL; ++r)
-    acc[r] = fmaf(ref_half(db[r]) * xb, limbs_to_float(T[r][0], T[r][1], T[r][2]), acc[r]);
+  for (int r = 0; r < RL; ++r) acc[r] = fmaf(dd[r], limbs_to_float(T[r][0], T[r][1], T[r][2]), acc[r]);
 }
 
-template <int C, int RL>
+template <int P, int RL>
 __device__ __forceinline__ void q6k_class(const uint8_t* __restrict__ row, uint32_t row_stride,
                                           uint32_t nb, int s, int spr, int n,
                                           const int4* __restrict__ xq, const int4* __restrict__ xi16,
                                           const float* __restrict__ xbs, float (&acc)[RL]) {
-  if (nb <= (uint32_t)C) return;
-  const uint32_t nbc = (nb - C + 3) / 4;
+  if (nb <= (uint32_t)P) return;
+  const uint32_t nbc = (nb - P + 1) / 2;
   for (uint32_t t = s; t < nbc; t += spr) {
-    const uint32_t b = C + 4 * t;
-    q6k_block_rows<(2 * C) & 7, RL>(row + (size_t)b * Q6K_BYTES, row_stride, n, xq, b,
-                                    xi16 + b * 16 + 8 * n, xbs[b], acc);
+    const uint32_t b = P + 2 * t;
+    q6k_block_rows<P, RL>(row + (size_t)b * Q6K_BYTES, row_stride, n, xq, b, xi16 + b * 16 + 8 * n,
+                          xbs[b], acc);
   }
 }
 
@@ -316,8 +288,6 @@ __device__ __forceinline__ void q6k_rows(const uint8_t* __restrict__ row, uint32
                                          const int4* xi16, const float* xbs, float (&acc)[RL]) {
   q6k_class<0, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
   q6k_class<1, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
-  q6k_class<2, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
-  q6k_class<3, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
 }
 
 template <int RL, bool DUAL>
@@ -479,8 +449,12 @@ __device__ __forceinline__ bool wait_gen(const volatile uint32_t* gen, uint32_t 
 // (int4 loads) stay aligned for every K.
 __host__ __device__ __forceinline__ uint32_t xbs_floats(uint32_t K) { return ((K / 256) + 3) & ~3u; }
 
+__host__ __device__ __forceinline__ size_t xq_bytes(uint32_t K) {
+  return (size_t)(K / 4 + K / 256) * 16;  // one pad vector per 64
+}
+
 __host__ __device__ __forceinline__ size_t x_region_bytes(uint32_t K, bool has4, bool has6) {
-  size_t b = (size_t)K * 4 + (size_t)xbs_floats(K) * 4;
+  size_t b = xq_bytes(K) + (size_t)xbs_floats(K) * 4;
   if (has4) b += (size_t)(K / 32) * 4;
   if (has6) b += (size_t)K;  // int4 per 16 elements
   return b;
@@ -497,16 +471,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   float* red = reinterpret_cast<float*>(smem + 8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES);
   uint8_t* xreg = smem + ((SMEM_HDR + 127) & ~127);
   const uint32_t K = a.k, NS = a.n_stages;
-  float* xraw = reinterpret_cast<float*>(xreg);  // raw x, then limb vectors in place
-  int4* xq = reinterpret_cast<int4*>(xreg);
-  float* xbs = reinterpret_cast<float*>(xreg + (size_t)K * 4);
+  int4* xq = reinterpret_cast<int4*>(xreg);  // padded limb vectors, xpad(K/4) of them
+  float* xbs = reinterpret_cast<float*>(xreg + xq_bytes(K));
   float* xs32 = xbs + xbs_floats(K);
-  int4* xi16 = reinterpret_cast<int4*>(xreg + (size_t)K * 4 + (size_t)xbs_floats(K) * 4 +
+  int4* xi16 = reinterpret_cast<int4*>(xreg + xq_bytes(K) + (size_t)xbs_floats(K) * 4 +
                                        (HAS4 ? (size_t)(K / 32) * 4 : 0));
   size_t stage_off = (size_t)(xreg - smem) + x_region_bytes(K, HAS4, HAS6);
   stage_off = (stage_off + 127) & ~(size_t)127;
   uint8_t* stages = smem + stage_off;
-  const bool x_tma = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -527,23 +499,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   if (warp == GEMV_WARPS) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
-      if (x_tma) {
-        mbar_arrive_expect_tx(xbar, K * 4);
-        bulk_g2s(xraw, a.x, K * 4, xbar);
-      }
-      uint32_t it = 0;
+      uint32_t it = 0, st = 0, ph = 0;  // chunk index, its stage, stage use parity
       bool ok = true;
       uint64_t seg_off = 0;
       for (uint32_t s = 0; s < a.nseg && ok; ++s) {
         const GemvSeg& g = a.seg[s];
         const Range rr = seg_units(a, s, seg_off, lo, hi);
-        const uint32_t ur = (uint32_t)g.rg * g.rl, cu = g.chunk_rows / ur;
+        const uint32_t lg_ur = __ffs((uint32_t)g.rg * g.rl) - 1, cu = g.chunk_rows >> lg_ur;
         for (uint32_t u = rr.ub; u < rr.ue && ok; u += cu) {
-          const uint32_t r0 = u * ur;
-          const uint32_t r1 = min(min(u + cu, rr.ue) * ur, g.m);
+          const uint32_t r0 = u << lg_ur;
+          const uint32_t r1 = min(min(u + cu, rr.ue) << lg_ur, g.m);
           const uint32_t bytes = (r1 - r0) * g.row_stride;
-          const uint32_t st = it % NS;
-          if (it >= NS && !mbar_wait_bounded(&empty[st], ((it / NS) - 1) & 1, a.err, DERR_TIMEOUT_EMPTY)) {
+          if (it >= NS && !mbar_wait_bounded(&empty[st], ph ^ 1u, a.err, DERR_TIMEOUT_EMPTY)) {
             ok = false;
             break;
           }
@@ -553,109 +520,132 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
           bulk_g2s(dst, g.w + (size_t)r0 * g.row_stride, bytes, &full[st]);
           if (g.dual) bulk_g2s(dst + bytes, g.w2 + (size_t)r0 * g.row_stride, bytes, &full[st]);
           ++it;
+          if (++st == NS) {
+            st = 0;
+            ph ^= 1u;
+          }
         }
-        seg_off += (uint64_t)((g.m + ur - 1) / ur) * g.unit_cost;
+        seg_off += (uint64_t)((g.m + (1u << lg_ur) - 1) >> lg_ur) * g.unit_cost;
       }
       // Do not leave the CTA with copies in flight: wait (bounded) for the
-      // last issued stages and the input vector to land.
+      // last issued stages to land.
       const uint32_t n_tail = it < NS ? it : NS;
       for (uint32_t t = it - n_tail; t < it; ++t)
         mbar_wait_bounded(&full[t % NS], (t / NS) & 1, a.err, DERR_TIMEOUT_FULL);
-      if (x_tma) mbar_wait_bounded(xbar, 0, a.err, DERR_TIMEOUT_FULL);
     }
     return;
   }
 
   // ------------------------------ consumers -------------------------------
-  const int ctid = threadIdx.x;  // 0 .. 32*GEMV_WARPS-1
   constexpr int CT = 32 * GEMV_WARPS;
-  if (x_tma) {
-    if (!mbar_wait_bounded(xbar, 0, a.err, DERR_TIMEOUT_FULL)) return;
-  } else {
-    for (uint32_t i = ctid; i < K; i += CT) xraw[i] = a.x[i];
-    named_sync(1, CT);
-  }
-  float inv_rms = 1.0f;
-  if (a.norm_w) {
-    // RMSNorm prologue (engine/src/ops.c:195-214), fixed-order reduction so
-    // every CTA derives the identical scale.
-    float ss = 0.f;
-    for (uint32_t i = ctid; i < K; i += CT) ss = fmaf(xraw[i], xraw[i], ss);
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    named_sync(1, CT);
-    float tot = 0.f;
+  constexpr int BPW = 4;  // 256-blocks per warp per pass (32 floats per lane)
+  const uint32_t NB = K / 256;
+  const bool xal = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  const bool wal = a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
+  // Fixed-point conversion.  Warp w owns 256-blocks w, w+8, ...; lane l holds
+  // elements 8l..8l+7 of a block (limb vectors 2l, 2l+1), so the block maximum
+  // is a warp reduction.  A pass loads up to BPW blocks per warp before using
+  // any of them.
+  for (uint32_t pass = 0; pass * GEMV_WARPS * BPW < NB; ++pass) {
+    float v[BPW][8];
 #pragma unroll
-    for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
-    inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
-  }
-  // Fixed-point conversion.  A thread owns one 32-element group (8 vectors);
-  // the 8 threads of a 256-block (consecutive lanes) share its maximum.  The
-  // swizzle only permutes vectors inside a group, so the rewrite is in place.
-  // Whole warps iterate together so the 8-lane shuffles always see full lanes.
-  for (uint32_t base = warp * 32; base < K / 32; base += CT) {
-    const uint32_t g32 = base + lane;
-    const bool valid = g32 < K / 32;
-    float v[32];
-    const float4* src = reinterpret_cast<const float4*>(xraw) + 8 * (valid ? g32 : 0);
+    for (int u = 0; u < BPW; ++u) {
+      const uint32_t kb = warp + GEMV_WARPS * (BPW * pass + u);
+      const float* src = a.x + 256 * (size_t)(kb < NB ? kb : 0) + 8 * lane;
+      if (xal) {
+        const float4 t0 = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 t1 = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        v[u][0] = t0.x; v[u][1] = t0.y; v[u][2] = t0.z; v[u][3] = t0.w;
+        v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
+      } else {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 t = src[q];
-      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+        for (int e = 0; e < 8; ++e) v[u][e] = __ldg(src + e);
+      }
     }
-    if (a.norm_w && valid) {
-      const float* wn = a.norm_w + 32 * g32;
+    if (a.norm_w) {
+      // RMSNorm prologue (engine/src/ops.c:195-214); the planner guarantees a
+      // single pass, and the fixed-order reduction gives every CTA the same scale.
+      float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] = (v[e] * inv_rms) * __ldg(wn + e);
-    }
-    float amax = 0.f;
-    bool finite = true;
+      for (int u = 0; u < BPW; ++u)
+        if (warp + GEMV_WARPS * u < NB)
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      amax = fmaxf(amax, fabsf(v[e]));
-      finite = finite && isfinite(v[e]);
-    }
+          for (int e = 0; e < 8; ++e) ss = fmaf(v[u][e], v[u][e], ss);
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      named_sync(1, CT);
+      float tot = 0.f;
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
-    }
-    // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
-    // whose maximum is below 2^-104 are scaled as if it were 2^-104.
-    const int f = amax > 0.f ? max(ilogbf(amax), -104) : 0;
-    const float xb = finite ? ldexpf(1.0f, f - 21) : __int_as_float(0x7fc00000);
-    const float inv_xb = ldexpf(1.0f, 21 - f);
-    if (!valid) continue;
-    if ((g32 & 7) == 0) xbs[g32 >> 3] = xb;
-    float s16a = 0.f, s16b = 0.f;
-    int l16[2][3] = {{0, 0, 0}, {0, 0, 0}};
-    uint32_t wl[8][3];
+      for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
+      const float inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const int t = finite ? __float2int_rn(v[e] * inv_xb) : 0;
-      const int l0 = (int)(int8_t)(t & 0xFF);
-      const int t1 = (t - l0) >> 8;
-      const int l1 = (int)(int8_t)(t1 & 0xFF);
-      const int l2 = (t1 - l1) >> 8;
-      const int q = e >> 2, c = e & 3;
-      if (c == 0) wl[q][0] = wl[q][1] = wl[q][2] = 0u;
-      wl[q][0] |= (uint32_t)(l0 & 0xFF) << (8 * c);
-      wl[q][1] |= (uint32_t)(l1 & 0xFF) << (8 * c);
-      wl[q][2] |= (uint32_t)(l2 & 0xFF) << (8 * c);
-      if (e < 16) s16a += v[e]; else s16b += v[e];
-      l16[e >> 4][0] += l0;
-      l16[e >> 4][1] += l1;
-      l16[e >> 4][2] += l2;
-    }
-    if (HAS4) xs32[g32] = s16a + s16b;
-    if (HAS6) {
-      xi16[2 * g32] = make_int4(-32 * l16[0][0], -32 * l16[0][1], -32 * l16[0][2], 0);
-      xi16[2 * g32 + 1] = make_int4(-32 * l16[1][0], -32 * l16[1][1], -32 * l16[1][2], 0);
+      for (int u = 0; u < BPW; ++u) {
+        const uint32_t kb = warp + GEMV_WARPS * u;
+        const float* wn = a.norm_w + 256 * (size_t)(kb < NB ? kb : 0) + 8 * lane;
+        float w[8];
+        if (wal) {
+          const float4 t0 = __ldg(reinterpret_cast<const float4*>(wn));
+          const float4 t1 = __ldg(reinterpret_cast<const float4*>(wn) + 1);
+          w[0] = t0.x; w[1] = t0.y; w[2] = t0.z; w[3] = t0.w;
+          w[4] = t1.x; w[5] = t1.y; w[6] = t1.z; w[7] = t1.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) w[e] = __ldg(wn + e);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
+      }
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const uint32_t vi = 8 * g32 + q;
-      xq[vi ^ xsw(vi)] = make_int4((int)wl[q][0], (int)wl[q][1], (int)wl[q][2], 0);
+    for (int u = 0; u < BPW; ++u) {
+      const uint32_t kb = warp + GEMV_WARPS * (BPW * pass + u);
+      if (kb >= NB) break;  // uniform across the warp
+      float amax = 0.f;
+      bool finite = true;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        amax = fmaxf(amax, fabsf(v[u][e]));
+        finite = finite && isfinite(v[u][e]);
+      }
+      amax = warp_max(amax);
+      finite = __all_sync(0xffffffffu, finite);
+      // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
+      // whose maximum is below 2^-104 are scaled as if it were 2^-104.
+      const int f = amax > 0.f ? max(ilogbf(amax), -104) : 0;
+      const float xb = finite ? ldexpf(1.0f, f - 21) : __int_as_float(0x7fc00000);
+      const float inv_xb = ldexpf(1.0f, 21 - f);
+      if (lane == 0) xbs[kb] = xb;
+      int t[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) t[e] = finite ? __float2int_rn(v[u][e] * inv_xb) : 0;
+      uint32_t lw[2][3];  // [vector][limb]: limb k of 4 elements = byte k of each
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const uint32_t sel = (uint32_t)k | ((uint32_t)(k + 4) << 4);
+          const uint32_t lo = __byte_perm((uint32_t)t[4 * h], (uint32_t)t[4 * h + 1], sel);
+          const uint32_t hi = __byte_perm((uint32_t)t[4 * h + 2], (uint32_t)t[4 * h + 3], sel);
+          lw[h][k] = __byte_perm(lo, hi, 0x5410);
+        }
+      const uint32_t v0 = 64 * kb + 2 * lane;
+      xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], 0);
+      xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], 0);
+      if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
+        float s = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = s;
+      }
+      if (HAS6) {  // -32 * limb sums per 16-element group (2 lanes)
+        int l0 = (int)__dp4a(lw[0][0], 0x01010101u, __dp4a(lw[1][0], 0x01010101u, 0u));
+        int l1 = (int)__dp4a(lw[0][1], 0x01010101u, __dp4a(lw[1][1], 0x01010101u, 0u));
+        int l2 = __dp4a((int)lw[0][2], 0x01010101, __dp4a((int)lw[1][2], 0x01010101, 0));
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
+        if ((lane & 1) == 0) xi16[16 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
+      }
     }
   }
   named_sync(1, CT);
@@ -664,29 +654,29 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   // Chunks are walked in the producer's order; a warp waits only for chunks
   // that hold one of its tasks, and the last warp to finish a chunk's tasks
   // releases the stage.
-  uint32_t it = 0, gtask = 0;
+  uint32_t it = 0, st = 0, ph = 0, gtask = 0;
   uint64_t seg_off = 0;
   for (uint32_t s = 0; s < a.nseg; ++s) {
     const GemvSeg& g = a.seg[s];
     const Range rr = seg_units(a, s, seg_off, lo, hi);
-    const uint32_t ur = (uint32_t)g.rg * g.rl, cu = g.chunk_rows / ur;
+    const uint32_t lg_ur = __ffs((uint32_t)g.rg * g.rl) - 1, ur = 1u << lg_ur;
+    const uint32_t cu = g.chunk_rows >> lg_ur;
     for (uint32_t u = rr.ub; u < rr.ue; u += cu) {
-      const uint32_t r0 = u * ur;
-      const uint32_t r1 = min(min(u + cu, rr.ue) * ur, g.m);
+      const uint32_t r0 = u << lg_ur;
+      const uint32_t r1 = min(min(u + cu, rr.ue) << lg_ur, g.m);
       const uint32_t nrows = r1 - r0;
-      const uint32_t st = it % NS;
-      const uint32_t ntasks = (nrows + ur - 1) / ur;
-      uint32_t t = (uint32_t)((warp - (int)(gtask % GEMV_WARPS) + GEMV_WARPS) % GEMV_WARPS);
+      const uint32_t ntasks = (nrows + ur - 1) >> lg_ur;
+      uint32_t t = (uint32_t)(warp - (int)(gtask % GEMV_WARPS) + GEMV_WARPS) % GEMV_WARPS;
       if (t < ntasks) {
         if (!wait_gen(gen, st, it, a.err)) return;
-        if (!mbar_wait_bounded(&full[st], (it / NS) & 1, a.err, DERR_TIMEOUT_FULL)) return;
+        if (!mbar_wait_bounded(&full[st], ph, a.err, DERR_TIMEOUT_FULL)) return;
         const uint8_t* buf = stages + (size_t)st * a.stage_bytes;
         const uint32_t dual_off = nrows * g.row_stride;
         uint32_t mine = 0;
         for (; t < ntasks; t += GEMV_WARPS, ++mine) {
-          const int rv = (int)min(ur, nrows - t * ur);
-          const uint8_t* rows = buf + (size_t)t * ur * g.row_stride;
-          dispatch_task(a, g, rows, r0 + t * ur, rv, dual_off, xv, lane);
+          const int rv = (int)min(ur, nrows - (t << lg_ur));
+          const uint8_t* rows = buf + (size_t)(t << lg_ur) * g.row_stride;
+          dispatch_task(a, g, rows, r0 + (t << lg_ur), rv, dual_off, xv, lane);
         }
         __syncwarp();
         if (lane == 0) {
@@ -700,8 +690,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
       }
       gtask += ntasks;
       ++it;
+      if (++st == NS) {
+        st = 0;
+        ph ^= 1u;
+      }
     }
-    seg_off += (uint64_t)((g.m + ur - 1) / ur) * g.unit_cost;
+    seg_off += (uint64_t)((g.m + ur - 1) >> lg_ur) * g.unit_cost;
   }
 }
 
@@ -765,6 +759,7 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
               const float* norm_w, const uint32_t* pos, const float* rope_freq, int* err,
               int num_sms) {
   if (nmats < 1 || nmats > GEMV_MAX_SEGS || k == 0 || k % QK) return -1;
+  if (norm_w && k > 256u * 4u * GEMV_WARPS) return -1;  // RMSNorm prologue is single-pass
   GemvArgs& a = p.args;
   a = GemvArgs{};
   a.nseg = nmats;
@@ -804,15 +799,19 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     uint32_t rg = 1, rl;
     const uint32_t mats_per_row = g.dual ? 2 : 1;
     if (mt.qt == T_Q4K) {
-      p.has4 = 1;
-      while (rg * 2 <= 8 && rg * 2 * nb <= 8) rg *= 2;
+      p.has4 = 1;  // a lane per block: 32 block slots per warp
+      while (rg * 2 <= 32 && rg * 2 * nb <= 32) rg *= 2;
       rl = g.dual ? 2 : 4;
     } else {
-      p.has6 = 1;
-      const uint32_t nbc = (nb + 3) / 4;
+      p.has6 = 1;  // a lane per half block, blocks walked by parity: 16 slots
+      const uint32_t nbc = (nb + 1) / 2;
       while (rg * 2 <= 16 && rg * 2 * nbc <= 16) rg *= 2;
       rl = g.dual ? 1 : 2;
     }
+    // Short matrices: fewer rows per lane so each CTA has about two tasks per
+    // consumer warp and no single warp carries a long tail.
+    const uint32_t rows_per_cta = (mt.m + num_sms - 1) / num_sms;
+    while (rl > 1 && rows_per_cta < GEMV_WARPS * rg * rl) rl /= 2;
     while (rl > 1 && (uint64_t)rg * rl * g.row_stride * mats_per_row > 40960) rl /= 2;
     if (mt.epi == EPI_ROPE && rl < 2) {
       if (mt.qt != T_Q4K) return -2;  // RoPE rows come from Q4_K q/k projections

@@ -204,6 +204,27 @@ int shk_cuda_layer_ready(shk_ctx *ctx, uint32_t slot, int wait);
 /* Make `stream` wait (on the device) for the slot's copies. */
 int shk_cuda_layer_wait(shk_ctx *ctx, uint32_t slot, void *stream);
 
+/* ---- argmax without any device allocation.  No counterpart in the reference:
+ *      it exists for callers that cannot call cudaMalloc (a sampler inside a
+ *      host runtime that has already reserved the device's memory in its own
+ *      pool, or code that holds only device pointers and a stream, no shk_ctx).
+ *
+ * Writes the first index of the maximum of x_dev[0..n) to *out_dev (device
+ * memory), on `stream` (a cudaStream_t; NULL = the legacy default stream), on
+ * the CURRENT device.  Same result as shk_cuda_argmax.  Asynchronous: read
+ * *out_dev after the stream has been synchronised.
+ *  - Scratch is a fixed 2304-byte array in the library's device image (block
+ *    partials + merge ticket); every GPU that loads the library holds it until
+ *    the process exits.  No cudaMalloc / cudaFree is called.
+ *  - The first call on each device looks up the array's device address (set-up
+ *    under a lock); make that first call before any stream capture.
+ *  - All calls on a device share the array: calls whose kernels overlap on the
+ *    GPU (e.g. on two streams at once) race and give wrong results.
+ *  - n must be 1..SHK_ARGMAX_NOALLOC_MAX_N; larger or zero n returns
+ *    SHK_EINVAL without launching anything. ---- */
+#define SHK_ARGMAX_NOALLOC_MAX_N 0xFFFFFFFEu
+int shk_cuda_argmax_noalloc(const float *x_dev, uint32_t n, uint32_t *out_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

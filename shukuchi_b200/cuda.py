@@ -80,6 +80,7 @@ _SIGS = {
     "shk_cuda_swiglu": (I, [P, P, P, P, U32, P]),
     "shk_cuda_embed": (I, [P, P, U32, U32, U32, P, U32, P]),
     "shk_cuda_argmax": (I, [P, P, U32, C.POINTER(U32)]),
+    "shk_cuda_argmax_noalloc": (I, [P, U32, P, P]),
     "shk_cuda_kv_create": (P, [P, C.POINTER(KvConfig)]),
     "shk_cuda_kv_destroy": (None, [P]),
     "shk_cuda_kv_append": (I, [P, U32, U32, P, P, P]),

@@ -34,6 +34,8 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s bs1, 8B-shape Q4_K_M; Q4_K/Q6_K GEMV HBM GB/s vs peak"
 PROMPT = 512
 GATEUP_PART = 3
+PART_NAMES = ("rmsnorm_qkv_rope", "append_attention", "o_proj_residual", "rmsnorm_gateup_swiglu",
+              "down_residual", "lm_head")
 
 
 def parse():
@@ -266,7 +268,9 @@ def run_ours(args, ws, rank, local):
     with ClockSampler(local) as clk:
         barrier()
         ev0.record(stream)
+        torch.cuda.nvtx.range_push("decode")  # lets ncu --nvtx-include "decode/" pick the timed launches
         m.decode_steps(nxt, pos, args.steps)
+        torch.cuda.nvtx.range_pop()
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -310,6 +314,24 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     ctx.check()
     avg = sum(a.elapsed_time(b) for a, b in durs[4:]) / len(durs[4:]) / 1000.0
+    # per-part device time of one token (each part launched alone, all layers;
+    # these serialise launches that the captured step overlaps, so they sum
+    # to a little more than ms_per_step)
+    parts = {}
+    for part, name in enumerate(PART_NAMES):
+        evs = []
+        n = 1 if part == 5 else shape.n_layers
+        for rep in range(2):
+            for layer in range(n):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                m.launch_part(layer, part)
+                b.record(stream)
+                if rep == 1:
+                    evs.append((a, b))
+        torch.cuda.synchronize()
+        parts[name] = round(sum(a.elapsed_time(b) for a, b in evs) * 1000.0, 1)
+    ctx.check()
     alg = wbytes + 4 * (shape.n_embd + shape.n_ff)
     peak, peak_kind = peaks()
     achieved = alg / avg / 1e9
@@ -340,6 +362,7 @@ def run_ours(args, ws, rank, local):
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "bytes_per_launch": alg,
                      "traffic": ncu_traffic("gemv_gateup_llama8b.md")},
+        "token_parts_us": parts,
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
                           "frac": step_gbs / peak},
         "cpu_baseline": cpu,

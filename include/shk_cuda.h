@@ -49,8 +49,13 @@ typedef struct shk_model shk_model; /* dims, scratch, captured decode step */
 
 struct shk_cuda_config {
     int device;     /* CUDA ordinal; -1 = current device */
-    uint32_t flags; /* reserved, 0 */
+    uint32_t flags; /* SHK_CUDA_FLAG_*; 0 = defaults */
 };
+/* Run whole-token decode (shk_cuda_token_step / shk_cuda_decode_steps) in the
+ * persistent decode kernel (one cooperative launch per call, grid-wide
+ * barriers between phases) instead of captured graphs of per-projection
+ * kernels.  Both give the same results within fp32 rounding. */
+#define SHK_CUDA_FLAG_PERSISTENT 2u
 
 /* ---- context: replaces metal_ops_init/metal_ops_shutdown/metal_available/
  *      metal_ops_report (engine/include/metal_ops.h:5-6, 24-25) ---- */
@@ -120,6 +125,11 @@ void shk_cuda_kv_destroy(shk_kv *kv);
 /* kv_cache_append (engine/src/kv_cache.c:130-155); k/v: n_kv*head_dim fp32 */
 int shk_cuda_kv_append(shk_kv *kv, uint32_t layer, uint32_t pos, const float *k_dev,
                        const float *v_dev, void *stream);
+/* kv_cache_append for positions start..start+n-1 in one launch, as the
+ * reference's prefill loop appends them one by one (engine/src/engine.c:352-380
+ * via forward_layer_view :133); k/v: n rows of n_kv*head_dim fp32 */
+int shk_cuda_kv_append_range(shk_kv *kv, uint32_t layer, uint32_t start, uint32_t n,
+                             const float *k_dev, const float *v_dev, void *stream);
 /* kv_cache_read_range (engine/src/kv_cache.c:175-199): fp32 [pos][n_kv*hd] */
 int shk_cuda_kv_read_range(shk_kv *kv, uint32_t layer, uint32_t start, uint32_t end,
                            float *k_dev, float *v_dev, void *stream);
@@ -178,6 +188,17 @@ int shk_cuda_token_step(shk_model *m, uint32_t token, uint32_t pos, int want_nex
 int shk_cuda_decode_steps(shk_model *m, uint32_t first_token, uint32_t first_pos, uint32_t n_steps,
                           void *stream);
 int shk_cuda_model_token(shk_model *m, uint32_t *token_host); /* last argmax */
+/* Timeline of the persistent decode kernel, for profiling (no counterpart in
+ * the reference, whose CPU loop has no phases).  shk_cuda_model_trace_enable
+ * (m, n) makes the following token_step / decode_steps launches record, on
+ * CTA 0, %globaltimer (ns) at the start and at the arrival at / departure from
+ * the grid barrier after each of the first n phases (n = 0 turns it off).
+ * shk_cuda_model_trace_read copies up to cap values of the last launch
+ * ([start, arrive_0, leave_0, arrive_1, ...]) and returns how many it wrote, or
+ * a negative status.  Phases per token: embed, 5 per layer (QKV, attention, O,
+ * gate/up, down), lm_head, argmax. */
+int shk_cuda_model_trace_enable(shk_model *m, uint32_t n_phases);
+int shk_cuda_model_trace_read(shk_model *m, uint64_t *out_host, uint32_t cap);
 /* Profiling hook: enqueue one part of a registered layer's step at the device
  * position of the last step (part 0 RMSNorm+QKV+RoPE GEMV, 1 append+attention,
  * 2 O-proj+residual, 3 RMSNorm+gate/up+SwiGLU, 4 down+residual; 5 = lm_head

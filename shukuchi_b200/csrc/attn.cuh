@@ -51,6 +51,8 @@ cudaError_t kv_append_launch(const KvLayout& kv, uint32_t layer, const uint32_t*
 cudaError_t kv_read_range_launch(const KvLayout& kv, uint32_t layer, uint32_t start, uint32_t end,
                                  float* k_out, float* v_out, cudaStream_t stream);
 // Export raw 36-byte blocks in the reference order [pos][n_kv*hd/32][36].
+cudaError_t kv_append_range_launch(const KvLayout& kv, uint32_t layer, uint32_t start, uint32_t n,
+                                   const float* k, const float* v, cudaStream_t stream);
 cudaError_t kv_read_blocks_launch(const KvLayout& kv, uint32_t layer, uint32_t start, uint32_t end,
                                   uint8_t* k_out, uint8_t* v_out, cudaStream_t stream);
 

@@ -1,0 +1,335 @@
+// attn_dev.cuh -- device side of the Q8_0 KV cache: bit-exact
+// quantise-on-append and one (KV head, position split) item of split-K decode
+// attention.  Used by the stand-alone attention kernel (attn.cu) and the
+// persistent decode kernel (decode.cu).
+//
+// Reference semantics:
+//  * q8_quantize_vec (engine/src/kv_cache.c:28-55): per 32 floats
+//    scale = maxabs / 127 (0 -> 1), q = clamp(lrintf(v / scale), -127, 127).
+//    The same IEEE division and round-half-even conversion are used, so
+//    blocks are bit-identical for identical fp32 input.
+//  * op_attention (engine/src/ops.c:406-461) over kv_cache_read_range output:
+//    query head h reads KV head h % n_kv_heads, score = dot(q, k) * scale,
+//    max-subtracted softmax, out = sum p * v.  Here the softmax is computed
+//    online per position range (split) and merged with a log-sum-exp combine by
+//    the last item of each KV head; results agree to fp32 rounding.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "attn.cuh"
+#include "common.cuh"
+
+namespace shk {
+namespace adev {
+
+// One warp quantises one 32-element block (lane = element).
+__device__ __forceinline__ void q8_block_store(float v, int8_t* q_dst, float* s_dst, int lane) {
+  const float amax = warp_max(fabsf(v));
+  float scale = amax / 127.0f;
+  if (scale == 0.0f) scale = 1.0f;
+  int q = __float2int_rn(v / scale);
+  q = q > 127 ? 127 : (q < -127 ? -127 : q);
+  q_dst[lane] = (int8_t)q;
+  if (lane == 0) *s_dst = scale;
+}
+
+// Appends k_new/v_new of KV head `kvh` at position pos; called by nw warps.
+__device__ __forceinline__ void append_head(const KvLayout& kv, uint32_t layer, uint32_t kvh,
+                                            uint32_t pos, const float* k_new, const float* v_new,
+                                            int warp, int lane, int nw) {
+  const uint32_t nblk = kv.hd / 32;
+  int8_t* reg = kv.region(layer, kvh);
+  for (uint32_t b = warp; b < 2 * nblk; b += nw) {
+    const bool isv = b >= nblk;
+    const uint32_t j = isv ? b - nblk : b;
+    const float v = __ldcg((isv ? v_new : k_new) + kvh * kv.hd + 32 * j + lane);
+    int8_t* qd = reg + (isv ? kv.vq_off : kv.kq_off) + (size_t)pos * kv.hd + 32 * j;
+    float* sd = reinterpret_cast<float*>(reg + (isv ? kv.vs_off : kv.ks_off)) + (size_t)pos * nblk + j;
+    q8_block_store(v, qd, sd, lane);
+  }
+}
+
+constexpr int ATT_MAX_SPLITS = 128;  // splits per KV head (the host caps max_splits at this)
+
+// int8 lanes of a 32-bit word -> fp32
+__device__ __forceinline__ void s8x4_to_f32(uint32_t w, float* f) {
+  f[0] = (float)(int8_t)(w & 0xFFu);
+  f[1] = (float)(int8_t)((w >> 8) & 0xFFu);
+  f[2] = (float)(int8_t)((w >> 16) & 0xFFu);
+  f[3] = (float)(int8_t)(w >> 24);
+}
+
+// The loads of one warp iteration: PPI positions starting at T.
+template <int HD>
+struct AttnTile {
+  static constexpr int LPP = HD / 32, PPI = 32 / LPP, EPL = HD / 32;
+  uint4 k0, k1;         // this lane's 32-byte Q8_0 K block
+  float ks;             // its scale
+  uint32_t vw[PPI];     // V: this lane's EPL columns of each position
+  float vs[PPI];        // their block scales
+  __device__ __forceinline__ void load(const int8_t* Kq, const float* Ks, const int8_t* Vq,
+                                       const float* Vs, uint32_t T, uint32_t p1, int lane) {
+    const uint32_t nt = min((uint32_t)PPI, p1 - T);
+    const uint32_t tl = lane / LPP, b = lane % LPP;
+    const uint32_t t = T + (tl < nt ? tl : 0);  // clamp to a valid position
+    const uint4* kp = reinterpret_cast<const uint4*>(Kq + (size_t)t * HD + 32 * b);
+    k0 = __ldcg(kp);
+    k1 = __ldcg(kp + 1);
+    ks = __ldcg(Ks + (size_t)t * (HD / 32) + b);
+#pragma unroll
+    for (int j = 0; j < PPI; ++j) {
+      const uint32_t tj = T + ((uint32_t)j < nt ? j : 0);
+      const int8_t* vp = Vq + (size_t)tj * HD + lane * EPL;
+      if (EPL == 4)
+        vw[j] = __ldcg(reinterpret_cast<const unsigned int*>(vp));
+      else
+        vw[j] = __ldcg(reinterpret_cast<const unsigned short*>(vp));
+      vs[j] = __ldcg(Vs + (size_t)tj * (HD / 32) + (lane * EPL) / 32);
+    }
+  }
+};
+
+// Shared memory of one attention item (floats): q rows padded to 36 so the
+// LPP lanes of a position read distinct banks; per-warp partials; split weights.
+template <int HD, int G, int NW>
+struct AttnSmem {
+  static constexpr int LPP = HD / 32;
+  static constexpr int QROW = 36;
+  static constexpr int Q = 0;
+  static constexpr int WM = Q + G * LPP * QROW;
+  static constexpr int WL = WM + NW * G;
+  static constexpr int WACC = WL + NW * G;
+  static constexpr int SW = WACC + NW * G * HD;
+  static constexpr int SL = SW + ATT_MAX_SPLITS * G;
+  static constexpr int FLAG = SL + G;
+  static constexpr int FLOATS = FLAG + 4;
+  static constexpr size_t BYTES = (size_t)FLOATS * 4;
+};
+
+__device__ __forceinline__ void att_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// q, the new K/V rows, the position and the cache may have been written
+// earlier in the same launch by other CTAs (persistent decode kernel): they are
+// read with ld.global.cg (L2).
+// One (KV head kvh, split) item by NW warps (thread ids 0..32*NW-1, synchronised
+// with named barrier 1).  The positions [0, *pos] are cut into at most `nsplit`
+// splits of at least min_per_split positions (multiples of PPI); items with
+// split >= the active count return at once.  Each warp iteration covers PPI =
+// 32/(HD/32) positions (8 at head_dim 128, 16 at 64), with the next
+// iteration's loads in flight while the current one computes:
+//  QK   HD/32 lanes per position, lane = one 32-element Q8_0 block: 32 FMAs
+//       per query head against q in shared memory, block scale, then a
+//       shuffle sum over the position's lanes;
+//  softmax  online per warp (running max / sum per query head);
+//  PV   lane = HD/32 output columns; per position one coalesced row read of V,
+//       p broadcast by shuffle with the V block scale folded in.
+// Warps merge in shared memory; splits merge through `part` (log-sum-exp),
+// the last item of the KV head (atomic ticket) writing the output.
+template <int HD, int G, int NW>
+__device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint32_t split,
+                                          uint32_t nsplit, float* sm) {
+  using Tile = AttnTile<HD>;
+  using SM = AttnSmem<HD, G, NW>;
+  constexpr int LPP = Tile::LPP, PPI = Tile::PPI, EPL = Tile::EPL;
+  constexpr int NT = 32 * NW;
+  const uint32_t KV = a.kv.n_kv;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t pos = __ldcg(a.pos);
+  if (pos >= a.kv.max_seq) {
+    if (tid == 0) set_error(a.err, DERR_BAD_POS);
+    return;
+  }
+  const uint32_t seq = pos + 1;
+  uint32_t n0 = (seq + a.min_per_split - 1) / a.min_per_split;
+  n0 = n0 < 1 ? 1 : (n0 > nsplit ? nsplit : n0);
+  const uint32_t per = (((seq + n0 - 1) / n0) + PPI - 1) / PPI * PPI;
+  const uint32_t active = (seq + per - 1) / per;  // every active split is non-empty
+  if (split >= active) return;
+  const uint32_t p0 = split * per, p1 = min(seq, p0 + per);
+
+  float (*qs)[LPP][SM::QROW] = reinterpret_cast<float (*)[LPP][SM::QROW]>(sm + SM::Q);
+  float (*wm)[G] = reinterpret_cast<float (*)[G]>(sm + SM::WM);
+  float (*wl)[G] = reinterpret_cast<float (*)[G]>(sm + SM::WL);
+  float (*wacc)[G][HD] = reinterpret_cast<float (*)[G][HD]>(sm + SM::WACC);
+  float (*sw)[G] = reinterpret_cast<float (*)[G]>(sm + SM::SW);
+  float* sL = sm + SM::SL;
+  int* is_last = reinterpret_cast<int*>(sm + SM::FLAG);
+
+  for (int i = tid; i < G * HD; i += NT) {
+    const int g = i / HD, d = i % HD;
+    qs[g][d / 32][d % 32] = __ldcg(a.q + (kvh + KV * g) * HD + d);  // query head kvh + KV*g (h % KV == kvh)
+  }
+  if (a.k_new && pos >= p0 && pos < p1)
+    append_head(a.kv, a.layer, kvh, pos, a.k_new, a.v_new, warp, lane, NW);
+  att_sync(NT);
+
+  const int8_t* reg = a.kv.region(a.layer, kvh);
+  const int8_t* Kq = reg + a.kv.kq_off;
+  const float* Ks = reinterpret_cast<const float*>(reg + a.kv.ks_off);
+  const int8_t* Vq = reg + a.kv.vq_off;
+  const float* Vs = reinterpret_cast<const float*>(reg + a.kv.vs_off);
+  const int b = lane % LPP;
+  const uint32_t tl = lane / LPP;
+
+  float m[G], l[G], acc[G][EPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[g][e] = 0.f;
+  }
+
+  constexpr uint32_t STEP = PPI * NW;
+  uint32_t T = p0 + PPI * warp;
+  Tile cur;
+  if (T < p1) cur.load(Kq, Ks, Vq, Vs, T, p1, lane);
+  for (; T < p1; T += STEP) {
+    Tile nxt;
+    if (T + STEP < p1) nxt.load(Kq, Ks, Vq, Vs, T + STEP, p1, lane);
+    const bool ok = T + tl < p1;
+    // ---- scores ----
+    float kf[32];
+    s8x4_to_f32(cur.k0.x, kf);
+    s8x4_to_f32(cur.k0.y, kf + 4);
+    s8x4_to_f32(cur.k0.z, kf + 8);
+    s8x4_to_f32(cur.k0.w, kf + 12);
+    s8x4_to_f32(cur.k1.x, kf + 16);
+    s8x4_to_f32(cur.k1.y, kf + 20);
+    s8x4_to_f32(cur.k1.z, kf + 24);
+    s8x4_to_f32(cur.k1.w, kf + 28);
+    float p[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4* qv = reinterpret_cast<const float4*>(&qs[g][b][0]);
+      float sb = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 q4 = qv[u];
+        sb = fmaf(q4.x, kf[4 * u], sb);
+        sb = fmaf(q4.y, kf[4 * u + 1], sb);
+        sb = fmaf(q4.z, kf[4 * u + 2], sb);
+        sb = fmaf(q4.w, kf[4 * u + 3], sb);
+      }
+      float sc = sb * cur.ks;
+#pragma unroll
+      for (int o = 1; o < LPP; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+      p[g] = sc;
+    }
+    // ---- online softmax (per warp) ----
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float sg = ok ? p[g] * a.scale : -INFINITY;
+      const float mn = fmaxf(m[g], warp_max(sg));  // position T is valid: finite
+      const float pg = ok ? expf(sg - mn) : 0.f;
+      p[g] = pg;
+      const float corr = (m[g] == -INFINITY) ? 0.f : expf(m[g] - mn);
+      l[g] = fmaf(l[g], corr, warp_sum(b == 0 ? pg : 0.f));
+      m[g] = mn;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[g][e] *= corr;
+    }
+    // ---- P.V ----
+#pragma unroll
+    for (int j = 0; j < PPI; ++j) {
+      float vf[4];
+      s8x4_to_f32(cur.vw[j], vf);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pj = __shfl_sync(0xffffffffu, p[g], j * LPP) * cur.vs[j];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(pj, vf[e], acc[g][e]);
+      }
+    }
+    cur = nxt;
+  }
+  // ---- merge the warps ----
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+  }
+  att_sync(NT);
+  const size_t rec = HD + 2;
+  float* part = a.part + ((size_t)kvh * a.max_splits * G) * rec;
+  for (int i = tid; i < G * HD; i += NT) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
+      L = fmaf(f, wl[w][g], L);
+      O = fmaf(f, wacc[w][g][d], O);
+    }
+    if (active == 1) {
+      a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O * (1.0f / L);
+    } else {
+      float* r = part + ((size_t)split * G + g) * rec;
+      r[2 + d] = O;
+      if (d == 0) {
+        r[0] = M;
+        r[1] = L;
+      }
+    }
+  }
+  if (active == 1) {
+    att_sync(NT);  // shared memory is reused by the caller's next item
+    return;
+  }
+  // ---- merge the splits: the last item of this KV head ----
+  __threadfence();
+  att_sync(NT);
+  if (tid == 0) {
+    const int prev = atomicAdd(&a.counters[kvh], 1);
+    *is_last = (prev == (int)active - 1);
+  }
+  att_sync(NT);
+  if (*is_last) {
+    __threadfence();
+    // split weights exp(m_s - M) per query head, then the weighted sums; every
+    // load of a pass is independent, so they are all in flight together
+    for (uint32_t i = tid; i < active * G; i += NT) sw[i / G][i % G] = __ldcg(&part[(size_t)i * rec]);
+    att_sync(NT);
+    for (int g = warp; g < G; g += NW) {
+      float M = -INFINITY;
+      for (uint32_t sp = lane; sp < active; sp += 32) M = fmaxf(M, sw[sp][g]);
+      M = warp_max(M);
+      float L = 0.f;
+      for (uint32_t sp = lane; sp < active; sp += 32) {
+        const float ms = sw[sp][g];
+        const float w = (ms == -INFINITY) ? 0.f : expf(ms - M);
+        sw[sp][g] = w;
+        L = fmaf(w, __ldcg(&part[((size_t)sp * G + g) * rec + 1]), L);
+      }
+      L = warp_sum(L);
+      if (lane == 0) sL[g] = L;
+    }
+    att_sync(NT);
+    for (int i = tid; i < G * HD; i += NT) {
+      const int g = i / HD, d = i % HD;
+      float O = 0.f;
+#pragma unroll 8
+      for (uint32_t sp = 0; sp < active; ++sp)
+        O = fmaf(sw[sp][g], __ldcg(&part[((size_t)sp * G + g) * rec + 2 + d]), O);
+      const float L = sL[g];
+      a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O * (1.0f / L);
+    }
+    if (tid == 0) a.counters[kvh] = 0;
+  }
+  att_sync(NT);  // shared memory is reused by the caller's next item
+}
+
+}  // namespace adev
+}  // namespace shk

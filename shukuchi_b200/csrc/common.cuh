@@ -19,6 +19,7 @@ constexpr int DERR_TIMEOUT_FULL = 1;   // consumer gave up waiting for a TMA sta
 constexpr int DERR_TIMEOUT_EMPTY = 2;  // producer gave up waiting for a free stage
 constexpr int DERR_BAD_POS = 3;        // position beyond the cache capacity
 constexpr int DERR_BAD_TOKEN = 4;      // token id beyond the vocabulary
+constexpr int DERR_TIMEOUT_GRID = 5;   // a CTA gave up waiting at a grid-wide barrier
 
 // Wall-clock budget for any device-side wait (nanoseconds).  Waits in these
 // kernels normally finish in microseconds; the budget only turns a broken

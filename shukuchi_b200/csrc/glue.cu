@@ -9,12 +9,14 @@
 
 #include "common.cuh"
 #include "glue.cuh"
+#include "glue_dev.cuh"
 
 namespace shk {
 namespace {
+using namespace gldev;
 
-// op_embed, Q4_K and F16 branches (engine/src/ops.c:533-577).  The token id
-// is read from device memory so a captured graph can feed back the argmax.
+// op_embed (engine/src/ops.c:533-577).  The token id is read from device
+// memory so a captured graph can feed back the argmax.
 __global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t dtype,
                              const uint32_t* __restrict__ tok_p, uint32_t n_vocab, float* out,
                              uint32_t n_embd, int* err) {
@@ -23,39 +25,13 @@ __global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t dtype,
     if (threadIdx.x == 0 && blockIdx.x == 0) set_error(err, DERR_BAD_TOKEN);
     return;
   }
-  if (dtype == 1) {
-    const uint16_t* row = reinterpret_cast<const uint16_t*>(table) + (size_t)tok * n_embd;
-    for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < n_embd; j += gridDim.x * blockDim.x)
-      out[j] = ref_half(row[j]);
-    return;
-  }
-  // Q4_K: one thread per element, same per-element formula as the reference:
-  // y = (d * sc) * q - dmin * m.
-  const uint32_t nb = n_embd / QK;
-  const uint8_t* row = table + (size_t)tok * nb * Q4K_BYTES;
-  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n_embd; e += gridDim.x * blockDim.x) {
-    const uint8_t* blk = row + (size_t)(e / QK) * Q4K_BYTES;
-    const uint32_t l = e % QK, grp = l / 64, w = l % 64, sub = 2 * grp + (w >= 32);
-    const float d = ref_half(blk[0] | (blk[1] << 8)), dmin = ref_half(blk[2] | (blk[3] << 8));
-    const uint8_t* sc = blk + 4;
-    uint32_t s, m;
-    if (sub < 4) {
-      s = sc[sub] & 63;
-      m = sc[sub + 4] & 63;
-    } else {
-      s = (sc[sub + 4] & 0xF) | ((sc[sub - 4] >> 6) << 4);
-      m = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4);
-    }
-    const uint8_t qb = blk[16 + 32 * grp + (w & 31)];
-    const uint32_t q = (w >= 32) ? (qb >> 4) : (qb & 0xF);
-    const float d1 = d * (float)s, m1 = dmin * (float)m;
-    out[e] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
-  }
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n_embd; e += gridDim.x * blockDim.x)
+    out[e] = embed_elem(table, dtype, tok, n_embd, e);
 }
 
-// First index of the maximum (engine/src/engine.c:424-431: strict > keeps the
-// earliest index).  Block partials then the last block merges.  Optionally
-// advances the device position counter (token feedback in a captured step).
+// First index of the maximum (engine/src/engine.c:424-431).  Block partials
+// then the last block merges.  Optionally advances the device position counter
+// (token feedback in a captured step).
 constexpr int AM_THREADS = 512;
 __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restrict__ x, uint32_t n,
                                                             float* part_v, uint32_t* part_i,
@@ -66,64 +42,19 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restr
   __shared__ int last;
   const uint32_t per = (n + gridDim.x - 1) / gridDim.x;
   const uint32_t lo = blockIdx.x * per, hi = min(n, lo + per);
-  float bv = -INFINITY;
-  uint32_t bi = 0xFFFFFFFFu;
-  for (uint32_t i = lo + threadIdx.x; i < hi; i += AM_THREADS) {
-    const float v = x[i];
-    if (bi == 0xFFFFFFFFu || v > bv) {  // i increases: strict > keeps the first
-      bv = v;
-      bi = i;
-    }
-  }
-  auto better = [](float v1, uint32_t i1, float v2, uint32_t i2) {
-    if (i2 == 0xFFFFFFFFu) return false;
-    if (i1 == 0xFFFFFFFFu) return true;
-    return v2 > v1 || (v2 == v1 && i2 < i1);
-  };
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (better(bv, bi, ov, oi)) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    sv[warp] = bv;
-    si[warp] = bi;
-  }
-  __syncthreads();
+  float bv;
+  uint32_t bi;
+  am_block<AM_THREADS>(x, lo, hi, sv, si, [] { __syncthreads(); }, bv, bi);
   if (threadIdx.x == 0) {
-    float v = sv[0];
-    uint32_t ix = si[0];
-    for (int w = 1; w < AM_THREADS / 32; ++w)
-      if (better(v, ix, sv[w], si[w])) {
-        v = sv[w];
-        ix = si[w];
-      }
-    part_v[blockIdx.x] = v;
-    part_i[blockIdx.x] = ix;
+    part_v[blockIdx.x] = bv;
+    part_i[blockIdx.x] = bi;
     __threadfence();
     last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
   }
   __syncthreads();
   if (!last || threadIdx.x != 0) return;
   __threadfence();
-  float v = __ldcg(&part_v[0]);
-  uint32_t ix = __ldcg(&part_i[0]);
-  for (uint32_t b = 1; b < gridDim.x; ++b) {
-    const float ov = __ldcg(&part_v[b]);
-    const uint32_t oi = __ldcg(&part_i[b]);
-    if (better(v, ix, ov, oi)) {
-      v = ov;
-      ix = oi;
-    }
-  }
-  // NaN logits never compare greater; an all-NaN vector yields index 0 as in
-  // the reference loop.
-  *tok_out = (ix == 0xFFFFFFFFu) ? 0u : ix;
+  *tok_out = am_merge(part_v, part_i, gridDim.x);
   if (pos_inc) *pos_inc += 1;
   *counter = 0;
 }

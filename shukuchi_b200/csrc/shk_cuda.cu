@@ -13,6 +13,7 @@
 
 #include "attn.cuh"
 #include "common.cuh"
+#include "decode.cuh"
 #include "gemv.cuh"
 #include "glue.cuh"
 
@@ -29,6 +30,7 @@ using namespace shk;
 
 struct shk_ctx {
   int device = 0;
+  uint32_t flags = 0;  // SHK_CUDA_FLAG_*
   int num_sms = 148;
   cudaStream_t compute = nullptr;
   cudaStream_t copy = nullptr;
@@ -94,6 +96,21 @@ struct shk_model {
   bool head_ok = false;      // staged plan available for the output head
   bool head_generic = false; // rows not 16-byte multiples: plain-load GEMV
   cudaGraphExec_t g_layers = nullptr, g_head = nullptr, g_loop = nullptr;
+  // persistent decode kernel: program tables in device memory, built on first use
+  struct Persist {
+    int state = 0;  // 0 not built, 1 ready, -1 not usable (graphs are used)
+    DecodeProgram P{};
+    size_t smem = 0;
+    int grid = 0;
+    uint32_t n_phases_full = 0;
+    GemvArgs* d_gemv = nullptr;
+    AttnArgs* d_attn = nullptr;
+    DecodePhase* d_phases = nullptr;
+    GridBar* d_bar = nullptr;
+  } pk;
+  uint64_t* d_trace = nullptr;  // persistent-kernel timeline (shk_cuda_model_trace_enable)
+  uint32_t trace_phases = 0;
+  uint32_t trace_last = 0;      // phases recorded by the last launch
 };
 
 namespace {
@@ -104,7 +121,8 @@ int ctx_err_check(shk_ctx* c) {
   const int e = *c->h_err;
   if (e) {
     CK(cudaMemset(c->d_err, 0, sizeof(int)));
-    return (e == DERR_TIMEOUT_FULL || e == DERR_TIMEOUT_EMPTY) ? SHK_ETIMEOUT : SHK_EDEVICE;
+    return (e == DERR_TIMEOUT_FULL || e == DERR_TIMEOUT_EMPTY || e == DERR_TIMEOUT_GRID) ? SHK_ETIMEOUT
+                                                                                        : SHK_EDEVICE;
   }
   return SHK_OK;
 }
@@ -193,6 +211,7 @@ shk_ctx* shk_cuda_init(const shk_cuda_config* cfg) {
     if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
   }
   c->device = dev;
+  c->flags = cfg ? cfg->flags : 0u;
   bool ok = cudaSetDevice(dev) == cudaSuccess;
   ok = ok && cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess;
   ok = ok && cudaStreamCreateWithFlags(&c->compute, cudaStreamNonBlocking) == cudaSuccess;
@@ -373,7 +392,7 @@ shk_kv* shk_cuda_kv_create(shk_ctx* c, const shk_kv_config* cfg) {
   kv->L = kv_layout_make(cfg->n_layers, cfg->n_kv_heads, cfg->head_dim, cfg->max_seq_len);
   kv->seq.assign(cfg->n_layers, 0);
   // split-K fan-out: about two CTAs per SM across the KV heads
-  kv->max_splits = std::max<uint32_t>(1, std::min<uint32_t>(64, (2 * c->num_sms + cfg->n_kv_heads - 1) / cfg->n_kv_heads));
+  kv->max_splits = std::max<uint32_t>(1, std::min<uint32_t>(128, (4 * c->num_sms + cfg->n_kv_heads - 1) / cfg->n_kv_heads));
   const size_t bytes = kv->L.head_bytes * cfg->n_layers * cfg->n_kv_heads;
   // partials sized for up to 8 query heads per KV head
   const size_t part = attn_part_floats(8 * cfg->n_kv_heads, cfg->n_kv_heads, cfg->head_dim, kv->max_splits);
@@ -410,6 +429,17 @@ int shk_cuda_kv_append(shk_kv* kv, uint32_t layer, uint32_t pos, const float* k,
   if (!kv || !k || !v || layer >= kv->L.n_layers || pos >= kv->L.max_seq) return SHK_EINVAL;
   CK(kv_append_launch(kv->L, layer, kv->d_iota + pos, k, v, kv->ctx->d_err, pick(kv->ctx, s)));
   kv->seq[layer] = std::max(kv->seq[layer], pos + 1);
+  return SHK_OK;
+}
+
+int shk_cuda_kv_append_range(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t n,
+                             const float* k, const float* v, void* s) {
+  if (!kv || !k || !v || layer >= kv->L.n_layers || start > kv->L.max_seq ||
+      n > kv->L.max_seq - start)
+    return SHK_EINVAL;
+  if (n == 0) return SHK_OK;
+  CK(kv_append_range_launch(kv->L, layer, start, n, k, v, pick(kv->ctx, s)));
+  kv->seq[layer] = std::max(kv->seq[layer], start + n);
   return SHK_OK;
 }
 
@@ -450,7 +480,7 @@ int shk_cuda_kv_attend(shk_kv* kv, uint32_t layer, const float* q, const float* 
   a.part = kv->part;
   a.counters = kv->counters;
   a.max_splits = kv->max_splits;
-  a.min_per_split = 64;
+  a.min_per_split = 32;
   a.err = kv->ctx->d_err;
   CK(attn_decode_launch(a, pick(kv->ctx, s)));
   if (k_new) kv->seq[layer] = std::max(kv->seq[layer], seq_len);
@@ -474,6 +504,12 @@ void model_free_graphs(shk_model* m) {
   if (m->g_head) cudaGraphExecDestroy(m->g_head);
   if (m->g_loop) cudaGraphExecDestroy(m->g_loop);
   m->g_layers = m->g_head = m->g_loop = nullptr;
+  auto& k = m->pk;
+  cudaFree(k.d_gemv);
+  cudaFree(k.d_attn);
+  cudaFree(k.d_phases);
+  cudaFree(k.d_bar);
+  k = shk_model::Persist{};
 }
 
 int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
@@ -502,13 +538,7 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
   return SHK_OK;
 }
 
-// Enqueues one layer: fused RMSNorm+QKV(+RoPE), append+attention, O(+residual),
-// RMSNorm+gate/up(+SwiGLU), down(+residual).  `pos` is a device pointer.
-int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint32_t* pos,
-                  cudaStream_t st) {
-  GemvPlan qkv = P.qkv;
-  qkv.args.pos = pos;
-  CK(gemv_launch(qkv, st));
+AttnArgs layer_attn_args(shk_model* m, uint32_t layer, const uint32_t* pos) {
   AttnArgs a{};
   a.kv = m->kv->L;
   a.layer = layer;
@@ -522,8 +552,19 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
   a.part = m->kv->part;
   a.counters = m->kv->counters;
   a.max_splits = m->kv->max_splits;
-  a.min_per_split = 64;
+  a.min_per_split = 32;
   a.err = m->ctx->d_err;
+  return a;
+}
+
+// Enqueues one layer: fused RMSNorm+QKV(+RoPE), append+attention, O(+residual),
+// RMSNorm+gate/up(+SwiGLU), down(+residual).  `pos` is a device pointer.
+int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint32_t* pos,
+                  cudaStream_t st) {
+  GemvPlan qkv = P.qkv;
+  qkv.args.pos = pos;
+  CK(gemv_launch(qkv, st));
+  const AttnArgs a = layer_attn_args(m, layer, pos);
   CK(attn_decode_launch(a, st));
   CK(gemv_launch(P.o, st));
   CK(gemv_launch(P.gateup, st));
@@ -568,6 +609,120 @@ int capture(shk_model* m, int which, cudaGraphExec_t* out) {
   const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   return ie == cudaSuccess ? SHK_OK : SHK_ECUDA;
+}
+
+// Builds the persistent decode kernel's program: GEMV plans with stages of at
+// most 16 KB (one ring serves every projection), per-layer attention args and
+// the phase list embed, [QKV, attention, O, gate/up, down] x L, lm_head,
+// argmax.  Leaves state -1 (graph path) when the shapes do not fit it.
+int build_persist(shk_model* m) {
+  auto& k = m->pk;
+  shk_ctx* c = m->ctx;
+  const shk_model_desc& d = m->d;
+  k.state = -1;
+  if (!(c->flags & SHK_CUDA_FLAG_PERSISTENT) || m->head_generic) return SHK_OK;
+  const uint32_t G = d.n_heads / d.n_kv_heads;
+  if (d.n_heads % d.n_kv_heads) return SHK_OK;
+  const uint32_t L = d.n_layers, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+  const uint32_t* pos = m->d_tok + 1;
+  const uint32_t stage_cap = 16384;
+  std::vector<GemvArgs> ga;
+  uint32_t stage = 0, kmax = 0;
+  auto add = [&](const GemvMat* mats, int n, uint32_t kk, const float* x, const float* nw) -> bool {
+    GemvPlan p;
+    if (gemv_plan(p, mats, n, kk, x, nw, pos, m->d_freq, c->d_err, c->num_sms, stage_cap)) return false;
+    ga.push_back(p.args);
+    stage = std::max(stage, p.args.stage_bytes);
+    kmax = std::max(kmax, kk);
+    return true;
+  };
+  for (uint32_t l = 0; l < L; ++l) {
+    const shk_layer_desc& lv = m->layers[l];
+    GemvMat qkv[3] = {
+        {lv.attn_q, nullptr, m->q, qd, lv.attn_q_dtype, 0, EPI_ROPE, hd},
+        {lv.attn_k, nullptr, m->k, kvd, lv.attn_k_dtype, 0, EPI_ROPE, hd},
+        {lv.attn_v, nullptr, m->v, kvd, lv.attn_v_dtype, lv.row_stride_v, EPI_STORE, 0},
+    };
+    GemvMat o{lv.attn_o, nullptr, m->hidden, d.n_embd, lv.attn_o_dtype, 0, EPI_ADD, 0};
+    GemvMat gu{lv.ffn_gate, lv.ffn_up, m->act, d.n_ff, lv.ffn_gate_dtype, 0, EPI_SWIGLU, 0};
+    GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, EPI_ADD, 0};
+    if (!add(qkv, 3, d.n_embd, m->hidden, lv.attn_norm) || !add(&o, 1, qd, m->att, nullptr) ||
+        !add(&gu, 1, d.n_embd, m->hidden, lv.ffn_norm) || !add(&dn, 1, d.n_ff, m->act, nullptr))
+      return SHK_OK;
+  }
+  GemvMat hm{d.output_dev, nullptr, m->logits, d.n_vocab, d.output_dtype, 0, EPI_STORE, 0};
+  if (!add(&hm, 1, d.n_embd, m->hidden, nullptr)) return SHK_OK;
+  std::vector<AttnArgs> aa(L);
+  for (uint32_t l = 0; l < L; ++l) aa[l] = layer_attn_args(m, l, pos);
+  std::vector<DecodePhase> ph;
+  ph.push_back({PH_EMBED, 0});
+  for (uint32_t l = 0; l < L; ++l) {
+    ph.push_back({PH_GEMV, 4 * l});
+    ph.push_back({PH_ATTN, l});
+    ph.push_back({PH_GEMV, 4 * l + 1});
+    ph.push_back({PH_GEMV, 4 * l + 2});
+    ph.push_back({PH_GEMV, 4 * l + 3});
+  }
+  ph.push_back({PH_GEMV, 4 * L});
+  ph.push_back({PH_ARGMAX, 0});
+  DecodeProgram& P = k.P;
+  P = DecodeProgram{};
+  P.stage_bytes = (stage + 127) & ~127u;
+  P.ns = 1;  // sized below
+  const size_t fixed = decode_smem(P, hd, G, kmax);  // header + x region + one stage
+  const size_t budget = 227 * 1024;
+  if (fixed > budget || budget - fixed < (size_t)P.stage_bytes) return SHK_OK;
+  P.ns = (uint32_t)std::min<size_t>(GEMV_MAX_STAGES, 1 + (budget - fixed) / P.stage_bytes);
+  if (P.ns < 2) return SHK_OK;
+  k.smem = decode_smem(P, hd, G, kmax);
+  k.grid = c->num_sms;
+  if (!decode_supported(hd, G, k.smem, k.grid)) return SHK_OK;
+  bool ok = cudaMalloc(&k.d_gemv, ga.size() * sizeof(GemvArgs)) == cudaSuccess;
+  ok = ok && cudaMalloc(&k.d_attn, aa.size() * sizeof(AttnArgs)) == cudaSuccess;
+  ok = ok && cudaMalloc(&k.d_phases, ph.size() * sizeof(DecodePhase)) == cudaSuccess;
+  ok = ok && cudaMalloc(&k.d_bar, sizeof(GridBar)) == cudaSuccess;
+  ok = ok && cudaMemcpy(k.d_gemv, ga.data(), ga.size() * sizeof(GemvArgs), cudaMemcpyHostToDevice) == cudaSuccess;
+  ok = ok && cudaMemcpy(k.d_attn, aa.data(), aa.size() * sizeof(AttnArgs), cudaMemcpyHostToDevice) == cudaSuccess;
+  ok = ok && cudaMemcpy(k.d_phases, ph.data(), ph.size() * sizeof(DecodePhase), cudaMemcpyHostToDevice) == cudaSuccess;
+  if (!ok) {
+    model_free_graphs(m);
+    m->pk.state = -1;
+    return SHK_ENOMEM;
+  }
+  P.gemv = k.d_gemv;
+  P.attn = k.d_attn;
+  P.phases = k.d_phases;
+  k.n_phases_full = (uint32_t)ph.size();
+  P.tok_embd = static_cast<const uint8_t*>(d.tok_embd_dev);
+  P.embd_dtype = d.tok_embd_dtype;
+  P.n_vocab = d.n_vocab;
+  P.n_embd = d.n_embd;
+  P.hidden = m->hidden;
+  P.logits = m->logits;
+  P.am_v = m->am_v;
+  P.am_i = m->am_i;
+  P.am_cnt = m->am_cnt;
+  P.tok = m->d_tok;
+  P.n_kv = d.n_kv_heads;
+  P.attn_nsplit = std::max<uint32_t>(1, std::min<uint32_t>(m->kv->max_splits, (uint32_t)k.grid / d.n_kv_heads));
+  P.bar = k.d_bar;
+  P.err = c->d_err;
+  k.state = 1;
+  return SHK_OK;
+}
+
+// One cooperative launch: n_steps tokens (with_head: lm_head + argmax per step).
+int launch_persist(shk_model* m, uint32_t n_steps, bool with_head, bool advance_pos, cudaStream_t st) {
+  auto& k = m->pk;
+  DecodeProgram P = k.P;
+  P.n_steps = n_steps;
+  P.n_phases = with_head ? k.n_phases_full : k.n_phases_full - 2;
+  P.advance_pos = advance_pos ? 1u : 0u;
+  P.trace = m->d_trace;
+  P.trace_cap_phases = m->trace_phases;
+  m->trace_last = m->d_trace ? std::min<uint32_t>(m->trace_phases, n_steps * P.n_phases) : 0;
+  CK(decode_launch(P, m->d.head_dim, m->d.n_heads / m->d.n_kv_heads, k.smem, k.grid, st));
+  return SHK_OK;
 }
 
 bool model_ready(shk_model* m) {
@@ -652,6 +807,7 @@ void shk_cuda_model_destroy(shk_model* m) {
   cudaFree(m->d_tok);
   cudaFreeHost(m->h_tok);
   cudaFree(m->d_freq);
+  cudaFree(m->d_trace);
   delete m;
 }
 
@@ -715,15 +871,23 @@ int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_nex
   if (!model_ready(m)) return SHK_EINVAL;
   cudaStream_t st = m->ctx->compute;
   int rc;
-  if (!m->g_layers && (rc = capture(m, 0, &m->g_layers))) return rc;
-  if (!m->g_head && (rc = capture(m, 1, &m->g_head))) return rc;
+  if (m->pk.state == 0 && (rc = build_persist(m))) return rc;
+  const bool persist = m->pk.state == 1;
+  if (!persist) {
+    if (!m->g_layers && (rc = capture(m, 0, &m->g_layers))) return rc;
+    if (!m->g_head && (rc = capture(m, 1, &m->g_head))) return rc;
+  }
   CK(cudaStreamSynchronize(st));  // h_tok is reused below
   m->h_tok[0] = token;
   m->h_tok[1] = pos;
   CK(cudaMemcpyAsync(m->d_tok, m->h_tok, 8, cudaMemcpyHostToDevice, st));
-  CK(cudaGraphLaunch(m->g_layers, st));
+  if (persist) {
+    if ((rc = launch_persist(m, 1, want_next != 0, false, st))) return rc;
+  } else {
+    CK(cudaGraphLaunch(m->g_layers, st));
+    if (want_next) CK(cudaGraphLaunch(m->g_head, st));
+  }
   if (want_next) {
-    CK(cudaGraphLaunch(m->g_head, st));
     CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, st));
     if (logits) CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->d.n_vocab * 4, cudaMemcpyDeviceToHost, st));
   }
@@ -742,20 +906,49 @@ int shk_cuda_decode_steps(shk_model* m, uint32_t first_token, uint32_t first_pos
   if (!model_ready(m)) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
   int rc;
-  if (!m->g_layers && (rc = capture(m, 0, &m->g_layers))) return rc;
-  if (!m->g_head && (rc = capture(m, 1, &m->g_head))) return rc;
+  if (m->pk.state == 0 && (rc = build_persist(m))) return rc;
+  const bool persist = m->pk.state == 1;
   CK(cudaStreamSynchronize(st));
   m->h_tok[0] = first_token;
   m->h_tok[1] = first_pos;
   CK(cudaMemcpyAsync(m->d_tok, m->h_tok, 8, cudaMemcpyHostToDevice, st));
   // Each step: embed(*tok) + layers at *pos, then lm_head + argmax writes the
   // next token and advances *pos.  No host round trip between steps.
-  if (!m->g_loop && (rc = capture(m, 2, &m->g_loop))) return rc;
-  for (uint32_t i = 0; i < n; ++i) CK(cudaGraphLaunch(m->g_loop, st));
+  if (persist) {
+    if (n && (rc = launch_persist(m, n, true, true, st))) return rc;
+  } else {
+    if (!m->g_loop && (rc = capture(m, 2, &m->g_loop))) return rc;
+    for (uint32_t i = 0; i < n; ++i) CK(cudaGraphLaunch(m->g_loop, st));
+  }
   for (uint32_t l = 0; l < m->d.n_layers; ++l)
     m->kv->seq[l] = std::max(m->kv->seq[l], first_pos + n);
   m->ctx->n_steps += n;
   return SHK_OK;
+}
+
+int shk_cuda_model_trace_enable(shk_model* m, uint32_t n_phases) {
+  if (!m) return SHK_EINVAL;
+  CK(cudaStreamSynchronize(m->ctx->compute));
+  cudaFree(m->d_trace);
+  m->d_trace = nullptr;
+  m->trace_phases = 0;
+  m->trace_last = 0;
+  if (n_phases == 0) return SHK_OK;
+  if (cudaMalloc(&m->d_trace, (1 + 2 * (size_t)n_phases) * sizeof(uint64_t)) != cudaSuccess) {
+    m->d_trace = nullptr;
+    return SHK_ENOMEM;
+  }
+  m->trace_phases = n_phases;
+  return SHK_OK;
+}
+
+int shk_cuda_model_trace_read(shk_model* m, uint64_t* out, uint32_t cap) {
+  if (!m || !out) return SHK_EINVAL;
+  if (!m->d_trace || m->trace_last == 0) return 0;
+  const uint32_t n = std::min<uint32_t>(cap, 1 + 2 * m->trace_last);
+  CK(cudaStreamSynchronize(m->ctx->compute));
+  CK(cudaMemcpy(out, m->d_trace, (size_t)n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+  return (int)n;
 }
 
 int shk_cuda_model_token(shk_model* m, uint32_t* token) {
@@ -799,7 +992,7 @@ int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void
     a.part = m->kv->part;
     a.counters = m->kv->counters;
     a.max_splits = m->kv->max_splits;
-    a.min_per_split = 64;
+    a.min_per_split = 32;
     a.err = m->ctx->d_err;
     CK(attn_decode_launch(a, st));
   } else {

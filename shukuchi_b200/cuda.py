@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libshk_cuda.so")
 HEADER = os.path.join(os.path.dirname(_HERE), "include", "shk_cuda.h")
 
 SHK_OK = 0
+FLAG_PERSISTENT = 2  # SHK_CUDA_FLAG_PERSISTENT: whole-token steps in the persistent decode kernel
 STATUS = {0: "SHK_OK", -1: "SHK_EINVAL", -2: "SHK_ENOMEM", -3: "SHK_ECUDA", -4: "SHK_EUNSUPPORTED",
           -5: "SHK_ETIMEOUT", -6: "SHK_ENODEV", -7: "SHK_ENCCL", -8: "SHK_EDEVICE"}
 
@@ -84,6 +85,7 @@ _SIGS = {
     "shk_cuda_kv_create": (P, [P, C.POINTER(KvConfig)]),
     "shk_cuda_kv_destroy": (None, [P]),
     "shk_cuda_kv_append": (I, [P, U32, U32, P, P, P]),
+    "shk_cuda_kv_append_range": (I, [P, U32, U32, U32, P, P, P]),
     "shk_cuda_kv_read_range": (I, [P, U32, U32, U32, P, P, P]),
     "shk_cuda_kv_read_blocks": (I, [P, U32, U32, U32, P, P, P]),
     "shk_cuda_kv_attend": (I, [P, U32, P, P, P, P, U32, U32, F, P]),
@@ -99,6 +101,8 @@ _SIGS = {
     "shk_cuda_token_step": (I, [P, U32, U32, I, C.POINTER(U32), P]),
     "shk_cuda_decode_steps": (I, [P, U32, U32, U32, P]),
     "shk_cuda_model_token": (I, [P, C.POINTER(U32)]),
+    "shk_cuda_model_trace_enable": (I, [P, U32]),
+    "shk_cuda_model_trace_read": (I, [P, C.POINTER(U64), U32]),
     "shk_cuda_model_launch_part": (I, [P, U32, U32, P, C.POINTER(U64)]),
     "shk_cuda_layer_stage": (I, [P, U32, P, P, SZ]),
     "shk_cuda_layer_stage_rows": (I, [P, U32, P, SZ, P, SZ, SZ]),
@@ -144,8 +148,8 @@ def _call(name: str, *args) -> int:
 class Context:
     """A device context (shk_ctx): compute + copy streams, error word."""
 
-    def __init__(self, device: int = 0):
-        cfg = CudaConfig(device, 0)
+    def __init__(self, device: int = 0, flags: int = 0):
+        cfg = CudaConfig(device, flags)
         self.h = lib().shk_cuda_init(C.byref(cfg))
         if not self.h:
             raise ShkError("shk_cuda_init", -6)
@@ -241,6 +245,9 @@ class KvCache:
     def append(self, layer, pos, k, v, stream=None):
         _call("shk_cuda_kv_append", self.h, layer, pos, k, v, stream)
 
+    def append_range(self, layer, start, n, k, v, stream=None):
+        _call("shk_cuda_kv_append_range", self.h, layer, start, n, k, v, stream)
+
     def read_range(self, layer, start, end, k, v, stream=None):
         _call("shk_cuda_kv_read_range", self.h, layer, start, end, k, v, stream)
 
@@ -301,6 +308,15 @@ class DeviceModel:
         b = C.c_uint64(0)
         _call("shk_cuda_model_launch_part", self.h, layer, part, stream, C.byref(b))
         return b.value
+
+    def trace_enable(self, n_phases: int):
+        _call("shk_cuda_model_trace_enable", self.h, n_phases)
+
+    def trace_read(self, cap: int):
+        buf = (U64 * cap)()
+        n = lib().shk_cuda_model_trace_read(self.h, buf, cap)
+        check("shk_cuda_model_trace_read", min(n, 0))
+        return list(buf[:n])
 
     def last_token(self) -> int:
         t = C.c_uint32(0)

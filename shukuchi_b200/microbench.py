@@ -1,0 +1,306 @@
+"""Kernel microbenchmarks on one GPU.
+
+  python -m shukuchi_b200.microbench gemv [--shapes QT,M,K ...] [--reps R]
+      Batch-1 dequant-matvec sweep (Q4_K = 12, Q6_K = 14), fp32 x ~ N(0,1),
+      seeded random blocks.  Each launch reads a different copy of the weights
+      (copies totalling >= 4x the L2 size, at least 2), launches captured in a
+      CUDA graph, CUDA-event timing on the launching stream.
+      Bytes per launch = weights + 4*K (x) + 4*M (y).
+
+  python -m shukuchi_b200.microbench kv [--ctx C ...] [--batch B ...]
+      Q8_0 KV cache: 64 query / 8 KV heads, head_dim 128, K/V ~ N(0,1).
+      One step = for each of B independent sequences, append one new K/V row
+      (quantise-on-append) and attend over all c+1 positions.  A pool of
+      sequences larger than 4x L2 is rotated so no step finds its cache in L2.
+      Bytes per sequence = (c+1)*2304 (Q8_0 K+V read) + 2304 (append write)
+      + 8 KB (new K/V fp32) + 32 KB (q) + 32 KB (out).
+
+  python -m shukuchi_b200.microbench parts [--shape llama8b] [--layers 8] [--prompt 512]
+      One decode token split into its kernels: a model of the given shape
+      with `--layers` distinct layers (more than 4x L2 of weights) is run
+      through a prompt, then each part (RMSNorm+QKV+RoPE GEMV, append +
+      attention, O + residual, RMSNorm + gate/up + SwiGLU, down + residual,
+      lm_head) is captured for all layers in a CUDA graph and timed per launch.
+
+  python -m shukuchi_b200.microbench timeline [--shape llama8b] [--layers 32] [--prompt 512]
+      The persistent decode kernel's own timeline: one decode_steps launch of
+      --steps tokens with CTA 0 recording %globaltimer around every grid
+      barrier; reports per phase kind the mean wall time (barrier to barrier)
+      and the part of it CTA 0 spent waiting at the barrier.
+
+One JSON line per case; `frac` is achieved GB/s over the measured HBM copy
+bandwidth (MEASURED_PEAKS.json when present).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from . import cuda as sc
+from .synth import BLOCK_BYTES, QK
+from .synth_device import _fill_blocks
+
+GEMV_SHAPES = [(12, 4096, 4096), (12, 14336, 4096), (12, 4096, 14336), (14, 4096, 14336),
+               (14, 128256, 4096)]
+_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def hbm_peak() -> tuple[float, str]:
+    p = os.path.join(_ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def l2_bytes() -> int:
+    return torch.cuda.get_device_properties(0).L2_cache_size
+
+
+def _time_graph(g: torch.cuda.CUDAGraph, stream, reps: int) -> float:
+    """ms per replay."""
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def gemv(args, ctx) -> None:
+    peak, kind = hbm_peak()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    shapes = [tuple(int(v) for v in s.split(",")) for s in args.shapes] if args.shapes else GEMV_SHAPES
+    for qt, m, k in shapes:
+        row = (k // QK) * BLOCK_BYTES[qt]
+        stride = (row + 15) // 16 * 16
+        wb = m * stride
+        ncopy = max(2, min(64, math.ceil(4 * l2_bytes() / wb)))
+        ws = []
+        for _ in range(ncopy):
+            t = torch.empty(wb, dtype=torch.uint8, device="cuda")
+            _fill_blocks(t, qt, m, k, stride, gen)
+            ws.append(t)
+        if stride != row:
+            raise SystemExit(f"rows of {qt},{m},{k} are not 16-byte multiples; use the C ABI row_stride")
+        x = torch.randn(k, device="cuda", generator=gen)
+        y = torch.empty(m, device="cuda")
+        s = torch.cuda.Stream()
+        nl = max(ncopy, args.launches)
+        with torch.cuda.stream(s):
+            for i in range(3):  # warm-up (also loads the kernels)
+                ctx.matmul(qt, ws[i % ncopy].data_ptr(), x.data_ptr(), y.data_ptr(), m, k, stream=s.cuda_stream)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(nl):
+                    ctx.matmul(qt, ws[i % ncopy].data_ptr(), x.data_ptr(), y.data_ptr(), m, k,
+                               stream=s.cuda_stream)
+        ms = _time_graph(g, s, args.reps)
+        ctx.check()
+        us = ms * 1000.0 / nl
+        alg = m * row + 4 * k + 4 * m
+        gbs = alg / (us * 1e-6) / 1e9
+        print(json.dumps({"bench": "gemv", "qtype": "Q4_K" if qt == 12 else "Q6_K", "m": m, "k": k,
+                          "us": round(us, 3), "bytes": alg, "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4), "peak_gbs": peak, "peak_kind": kind,
+                          "copies": ncopy}), flush=True)
+        del g, ws
+        torch.cuda.empty_cache()
+
+
+def kv(args, ctx) -> None:
+    peak, kind = hbm_peak()
+    H, KV, HD = 64, 8, 128
+    row = KV * HD
+    per_pos = 2 * KV * (HD + 4 * HD // 32)  # K + V Q8_0 bytes per position: 2304
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    for c in args.ctx:
+        for B in args.batch:
+            seq_bytes = (c + 8) * per_pos
+            pool = max(B, min(4096, math.ceil(4 * l2_bytes() / seq_bytes)))
+            pool = math.ceil(pool / B) * B
+            cache = sc.KvCache(ctx, pool, KV, HD, c + 8)
+            chunk = 8192
+            kbuf = torch.empty(chunk * row, device="cuda")
+            vbuf = torch.empty(chunk * row, device="cuda")
+            for sidx in range(pool):
+                for p0 in range(0, c, chunk):
+                    n = min(chunk, c - p0)
+                    kbuf.normal_(generator=gen)
+                    vbuf.normal_(generator=gen)
+                    cache.append_range(sidx, p0, n, kbuf.data_ptr(), vbuf.data_ptr())
+            q = torch.randn(B, H * HD, device="cuda", generator=gen)
+            kn = torch.randn(B, row, device="cuda", generator=gen)
+            vn = torch.randn(B, row, device="cuda", generator=gen)
+            out = torch.empty(B, H * HD, device="cuda")
+            torch.cuda.synchronize()
+            s = torch.cuda.Stream()
+            steps = pool // B
+            scale = 1.0 / math.sqrt(HD)
+            with torch.cuda.stream(s):
+                for b in range(B):  # warm-up
+                    cache.attend(b, q[b].data_ptr(), out[b].data_ptr(), H, c + 1, scale,
+                                 kn[b].data_ptr(), vn[b].data_ptr(), stream=s.cuda_stream)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for st in range(steps):
+                        for b in range(B):
+                            cache.attend(st * B + b, q[b].data_ptr(), out[b].data_ptr(), H, c + 1, scale,
+                                         kn[b].data_ptr(), vn[b].data_ptr(), stream=s.cuda_stream)
+            ms = _time_graph(g, s, args.reps)
+            ctx.check()
+            us = ms * 1000.0 / steps
+            alg = B * ((c + 1) * per_pos + per_pos + 2 * 4 * row + 2 * 4 * H * HD)
+            gbs = alg / (us * 1e-6) / 1e9
+            print(json.dumps({"bench": "kv", "ctx": c, "batch": B, "us_per_step": round(us, 3),
+                              "bytes": alg, "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                              "peak_gbs": peak, "peak_kind": kind, "pool": pool,
+                              "launches_per_step": B}), flush=True)
+            del g
+            cache.close()
+            torch.cuda.empty_cache()
+
+
+PART_NAMES = ("rmsnorm_qkv_rope", "append_attention", "o_proj_residual", "rmsnorm_gateup_swiglu",
+              "down_residual", "lm_head")
+
+
+def parts(args, ctx) -> None:
+    import dataclasses
+
+    import numpy as np
+
+    from . import synth
+    from .synth_device import make_device_model
+
+    peak, kind = hbm_peak()
+    shape = dataclasses.replace(synth.SHAPES[args.shape], n_layers=args.layers)
+    wts = make_device_model(shape, seed=7)
+    kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, args.prompt + 16)
+    m = sc.DeviceModel(ctx, kv, wts.desc)
+    try:
+        for i, lv in enumerate(wts.layers):
+            m.set_layer(i, lv)
+        rng = np.random.default_rng(0)
+        for i, t in enumerate(rng.integers(0, shape.n_vocab, args.prompt)):
+            m.token_step(int(t), i, want_next=(i == args.prompt - 1))
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        for part, name in enumerate(PART_NAMES):
+            n = 1 if part == 5 else shape.n_layers
+            reps = 8 if part == 5 else 1
+            with torch.cuda.stream(s):
+                wb = [m.launch_part(layer, part, stream=s.cuda_stream) for layer in range(n)]
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(reps):
+                        for layer in range(n):
+                            m.launch_part(layer, part, stream=s.cuda_stream)
+            ms = _time_graph(g, s, args.reps)
+            ctx.check()
+            us = ms * 1000.0 / (n * reps)
+            gbs = wb[0] / (us * 1e-6) / 1e9
+            print(json.dumps({"bench": "parts", "shape": shape.name, "part": name, "us": round(us, 2),
+                              "weight_bytes": wb[0], "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                              "peak_gbs": peak, "peak_kind": kind, "ctx": args.prompt}), flush=True)
+            del g
+    finally:
+        m.close()
+        kv.close()
+
+
+def timeline(args, ctx) -> None:
+    import dataclasses
+
+    import numpy as np
+
+    from . import synth
+    from .synth_device import make_device_model
+
+    shape = dataclasses.replace(synth.SHAPES[args.shape], n_layers=args.layers)
+    wts = make_device_model(shape, seed=7)
+    ctx = sc.Context(0, flags=sc.FLAG_PERSISTENT)
+    kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, args.prompt + args.steps + 8)
+    m = sc.DeviceModel(ctx, kv, wts.desc)
+    try:
+        for i, lv in enumerate(wts.layers):
+            m.set_layer(i, lv)
+        rng = np.random.default_rng(0)
+        nxt = 0
+        for i, t in enumerate(rng.integers(0, shape.n_vocab, args.prompt)):
+            nxt = m.token_step(int(t), i, want_next=(i == args.prompt - 1))
+        per_tok = 1 + 5 * shape.n_layers + 2
+        m.trace_enable(per_tok * args.steps)
+        m.decode_steps(nxt, args.prompt, args.steps)
+        torch.cuda.synchronize()
+        ctx.check()
+        tr = m.trace_read(1 + 2 * per_tok * args.steps)
+        m.trace_enable(0)
+        kinds = ["embed"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * shape.n_layers + ["lm_head", "argmax"]
+        wall, wait = {}, {}
+        prev = tr[0]
+        for i in range((len(tr) - 1) // 2):
+            arrive, leave = tr[1 + 2 * i], tr[2 + 2 * i]
+            k = kinds[i % per_tok]
+            wall.setdefault(k, []).append(leave - prev)
+            wait.setdefault(k, []).append(leave - arrive)
+            prev = leave
+        total_us = (tr[-1] - tr[0]) / 1000.0
+        out = {"bench": "timeline", "shape": shape.name, "ctx": args.prompt, "steps": args.steps,
+               "us_per_token": round(total_us / args.steps, 1), "phases": {}}
+        for k in wall:
+            out["phases"][k] = {"wall_us": round(float(np.mean(wall[k])) / 1000.0, 2),
+                                "cta0_wait_us": round(float(np.mean(wait[k])) / 1000.0, 2),
+                                "count_per_token": len(wall[k]) // args.steps}
+        print(json.dumps(out), flush=True)
+    finally:
+        m.close()
+        kv.close()
+        ctx.close()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemv")
+    g.add_argument("--shapes", nargs="*")
+    g.add_argument("--launches", type=int, default=20)
+    g.add_argument("--reps", type=int, default=5)
+    k = sub.add_parser("kv")
+    k.add_argument("--ctx", type=int, nargs="*", default=[1024, 4096, 16384, 32768])
+    k.add_argument("--batch", type=int, nargs="*", default=[1, 8, 32])
+    k.add_argument("--reps", type=int, default=5)
+    pp = sub.add_parser("parts")
+    pp.add_argument("--shape", default="llama8b")
+    pp.add_argument("--layers", type=int, default=8)
+    pp.add_argument("--prompt", type=int, default=512)
+    pp.add_argument("--reps", type=int, default=5)
+    tl = sub.add_parser("timeline")
+    tl.add_argument("--shape", default="llama8b")
+    tl.add_argument("--layers", type=int, default=32)
+    tl.add_argument("--prompt", type=int, default=512)
+    tl.add_argument("--steps", type=int, default=4)
+    args = ap.parse_args()
+    torch.cuda.set_device(0)
+    ctx = sc.Context(0)
+    try:
+        {"gemv": gemv, "kv": kv, "parts": parts, "timeline": timeline}[args.cmd](args, ctx)
+    finally:
+        ctx.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -22,6 +22,33 @@ def kv_inputs(rng, T, KV, hd):
     return k, v
 
 
+@pytest.mark.parametrize("KV,hd,start,T", [(8, 128, 0, 300), (4, 64, 17, 70000)])
+def test_append_range_bit_exact(oracle, ctx, KV, hd, start, T):
+    # bulk append (prefill-style) == per-position q8_quantize_vec; 70000
+    # positions take two launches (grid.y <= 65535)
+    rng = np.random.default_rng(T)
+    k, v = kv_inputs(rng, T, KV, hd)
+    kv = sc.KvCache(ctx, 1, KV, hd, start + T)
+    try:
+        kd, vd = to_dev(k), to_dev(v)
+        kv.append_range(0, start, T, kd.data_ptr(), vd.data_ptr())
+        nb = KV * hd // 32 * 36
+        kb = torch.zeros(T * nb, dtype=torch.uint8, device="cuda")
+        vb = torch.zeros_like(kb)
+        kv.read_blocks(0, start, start + T, kb.data_ptr(), vb.data_ptr())
+        torch.cuda.synchronize()
+        ctx.check()
+        ref_k = oracle.q8_quantize(k.reshape(-1))
+        ref_v = oracle.q8_quantize(v.reshape(-1))
+        assert np.array_equal(kb.cpu().numpy(), ref_k)
+        assert np.array_equal(vb.cpu().numpy(), ref_v)
+        assert kv.seq_len(0) == start + T
+        with pytest.raises(sc.ShkError):
+            kv.append_range(0, start + 1, T, kd.data_ptr(), vd.data_ptr())  # past max_seq
+    finally:
+        kv.close()
+
+
 @pytest.mark.parametrize("KV,hd", [(2, 64), (8, 128), (4, 64)])
 def test_append_bit_exact(oracle, ctx, KV, hd):
     rng = np.random.default_rng(KV * hd)

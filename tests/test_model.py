@@ -68,8 +68,20 @@ def test_tiny_model_golden(ctx):
     assert_logits(logits, g["logits"])
 
 
-@pytest.mark.parametrize("shape,n_prompt,n_decode", [("small", 5, 12)])
-def test_generate_matches_oracle(oracle, ctx, shape, n_prompt, n_decode):
+@pytest.fixture(scope="module")
+def ctx_persist():
+    """A context whose whole-token steps run in the persistent decode kernel
+    (graphs of per-projection kernels are the default)."""
+    c = sc.Context(0, flags=sc.FLAG_PERSISTENT)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("path", ["graphs", "persistent"])
+@pytest.mark.parametrize("shape,n_prompt,n_decode", [("small", 5, 12), ("tiny", 3, 9)])
+def test_generate_matches_oracle(oracle, ctx, ctx_persist, shape, n_prompt, n_decode, path):
+    if path == "persistent":
+        ctx = ctx_persist
     model = synth.make_model(shape, seed=21)
     rng = np.random.default_rng(9)
     prompt = rng.integers(0, model.shape.n_vocab, n_prompt).astype(np.uint32)

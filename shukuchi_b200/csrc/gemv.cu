@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
       done[s] = 0;
       gen[s] = 0xFFFFFFFFu;
     }
-    mbar_init(xbar, 1);
+    mbar_init(xbar, GEMV_WARPS);
     fence_mbar_init();
   }
   __syncthreads();
@@ -57,12 +57,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   RingPos pos;
   if (warp == GEMV_WARPS) {
     if (lane == 0) {
-      gemv_produce(a, R, pos, lo, hi);
+      gemv_produce(a, R, pos, lo, hi, xbar);
       ring_drain(R, pos, a.err);
     }
     return;
   }
-  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane);
+  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar);
   uint32_t gtask = 0;
   gemv_consume(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
 }
@@ -127,7 +127,6 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
               const float* norm_w, const uint32_t* pos, const float* rope_freq, int* err,
               int num_sms, uint32_t max_stage_bytes) {
   if (nmats < 1 || nmats > GEMV_MAX_SEGS || k == 0 || k % QK) return -1;
-  if (norm_w && k > 256u * 4u * GEMV_WARPS) return -1;  // RMSNorm prologue is single-pass
   GemvArgs& a = p.args;
   a = GemvArgs{};
   a.nseg = nmats;
@@ -163,28 +162,20 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     g.rope_hd = mt.rope_hd;
     if (mt.epi == EPI_ROPE && (mt.rope_hd == 0 || (mt.rope_hd & 1) || !pos || !rope_freq)) return -1;
     // rg: row groups per warp task so that every lane has a block to work on;
-    // rl: rows per lane (x reuse), smaller for dual segments and huge rows.
-    uint32_t rg = 1, rl;
+    // rl: output rows per lane group (2 rows, or 1 row / one gate-up pair).
+    uint32_t rg = 1;
     const uint32_t mats_per_row = g.dual ? 2 : 1;
     if (mt.qt == T_Q4K) {
       p.has4 = 1;  // a lane per block: 32 block slots per warp
       while (rg * 2 <= 32 && rg * 2 * nb <= 32) rg *= 2;
-      rl = g.dual ? 2 : 4;
     } else {
       p.has6 = 1;  // a lane per half block, blocks walked by parity: 16 slots
       const uint32_t nbc = (nb + 1) / 2;
       while (rg * 2 <= 16 && rg * 2 * nbc <= 16) rg *= 2;
-      rl = g.dual ? 1 : 2;
     }
-    // Short matrices: fewer rows per lane so each CTA has about two tasks per
-    // consumer warp and no single warp carries a long tail.
-    const uint32_t rows_per_cta = (mt.m + num_sms - 1) / num_sms;
-    while (rl > 1 && rows_per_cta < GEMV_WARPS * rg * rl) rl /= 2;
-    while (rl > 1 && (uint64_t)rg * rl * g.row_stride * mats_per_row > 40960) rl /= 2;
-    if (mt.epi == EPI_ROPE && rl < 2) {
-      if (mt.qt != T_Q4K) return -2;  // RoPE rows come from Q4_K q/k projections
-      rl = 2;
-    }
+    uint32_t rl = g.dual ? 1 : 2;
+    if (rl == 2 && (uint64_t)rg * 2 * g.row_stride > 40960) rl = 1;  // huge rows
+    if (mt.epi == EPI_ROPE && rl != 2) return -2;
     g.rg = (uint8_t)rg;
     g.rl = (uint8_t)rl;
     g.unit_cost = rg * rl * g.row_stride * mats_per_row;

@@ -58,29 +58,40 @@ __device__ __forceinline__ uint32_t xpad(uint32_t v) { return v + (v >> 6); }
 __device__ __forceinline__ int dp4a_u(uint32_t a, int b, int c) {
   return (int)__dp4a(a, (uint32_t)b, (uint32_t)c);
 }
-__device__ __forceinline__ int dp4a_s(uint32_t a, int b, int c) { return __dp4a((int)a, b, c); }
+// a: four unsigned bytes, b: four signed bytes
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
 __device__ __forceinline__ float limbs_to_float(int a0, int a1, int a2) {
   return fmaf(65536.0f, (float)a2, fmaf(256.0f, (float)a1, (float)a0));
 }
 
+// Code size matters here: the hot loops below are written so that one
+// compact body per quant type serves every segment kind (single, dual,
+// RoPE) -- a kernel whose instruction footprint overflows the SM's
+// instruction caches stalls on fetch rather than on memory.
+
 // ------------------------------- Q4_K ---------------------------------------
-// A lane owns whole blocks b (all 256 elements) for RL rows (and both matrices
-// of a dual segment), so each row's scale/min decode and block epilogue is paid
-// once per 256 weights.  The four 64-element groups j are walked in a rolled
-// loop (compact code); within a group the low nibbles are sub-block 2j and the
-// high nibbles sub-block 2j+1 (engine/src/ops.c:117-142).
-template <int RL, bool DUAL>
-__device__ __forceinline__ void q4k_block_rows(const uint8_t* const (&rp)[RL * (DUAL ? 2 : 1)],
-                                               uint32_t boff, const int4* __restrict__ xblk,
-                                               float xb, const float* __restrict__ xs,
-                                               float (&acc)[RL][2]) {
-  constexpr int NR = RL * (DUAL ? 2 : 1);
-  uint32_t scl[NR], sch[NR], ml[NR], mh[NR];
-  float dx[NR], dm[NR];
+// Two rows (r0, r1: consecutive rows, or the gate and up rows of a dual
+// segment) of one 256-element block against x block xblk.  The four
+// 64-element groups j (low nibbles = sub-block 2j, high nibbles = 2j+1,
+// engine/src/ops.c:117-142) run in a rolled loop.  High nibbles are used in
+// place (q << 4, masked, no shift): their dp4a sums are 16x, so the low
+// sub-block's scale is taken 16x as well and the block result is divided by 16
+// (exact).  Per group: |16 sc_lo S_lo + sc_hi S_hi| <= 2 * 63 * 32 * 240 * 255,
+// four groups stay below 2^31.
+__device__ __forceinline__ void q4k_block2(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
+                                           const int4* __restrict__ xblk, float xb,
+                                           const float* __restrict__ xs, float& acc0, float& acc1) {
+  const uint8_t* rp[2] = {r0, r1};
+  uint32_t scl[2], sch[2], ml[2], mh[2];
+  float dx[2], dm[2];
 #pragma unroll
-  for (int r = 0; r < NR; ++r) {
-    const uint4 h = *reinterpret_cast<const uint4*>(rp[r] + boff);
+  for (int r = 0; r < 2; ++r) {
+    const uint4 h = *reinterpret_cast<const uint4*>(rp[r]);
     // 6-bit scales/mins of sub-blocks 0-3 and 4-7, packed four per word
     // (engine/src/ops.c:107-115 get_scale_min_k4)
     scl[r] = h.y & 0x3F3F3F3Fu;
@@ -90,97 +101,55 @@ __device__ __forceinline__ void q4k_block_rows(const uint8_t* const (&rp)[RL * (
     dx[r] = ref_half(h.x & 0xFFFFu) * xb;
     dm[r] = ref_half(h.x >> 16);
   }
-  int A[NR][3];
-  float M[NR];
-#pragma unroll
-  for (int r = 0; r < NR; ++r) {
-    A[r][0] = A[r][1] = A[r][2] = 0;
-    M[r] = 0.f;
-  }
-#pragma unroll
+  int A[2][3] = {{0, 0, 0}, {0, 0, 0}};
+  float M[2] = {0.f, 0.f};
+#pragma unroll 1
   for (int j = 0; j < 4; ++j) {
-    int S[NR][2][3];
+    int S[2][2][3] = {{{0, 0, 0}, {0, 0, 0}}, {{0, 0, 0}, {0, 0, 0}}};
 #pragma unroll
-    for (int r = 0; r < NR; ++r)
+    for (int half = 0; half < 2; ++half) {
+      uint4 w[2];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) S[r][hh][0] = S[r][hh][1] = S[r][hh][2] = 0;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {  // qs words 4*half .. 4*half+3
-      uint4 w[NR];
-#pragma unroll
-      for (int r = 0; r < NR; ++r)
-        w[r] = *reinterpret_cast<const uint4*>(rp[r] + boff + 16 + 32 * j + 16 * half);
+      for (int r = 0; r < 2; ++r) w[r] = *reinterpret_cast<const uint4*>(rp[r] + 16 + 32 * j + 16 * half);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int4 xl = xblk[16 * j + 4 * half + i];
         const int4 xh = xblk[16 * j + 8 + 4 * half + i];
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
+        for (int r = 0; r < 2; ++r) {
           const uint32_t q = i == 0 ? w[r].x : i == 1 ? w[r].y : i == 2 ? w[r].z : w[r].w;
-          const uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;
+          const uint32_t lo = q & 0x0F0F0F0Fu, hi = q & 0xF0F0F0F0u;
           S[r][0][0] = dp4a_u(lo, xl.x, S[r][0][0]);
           S[r][0][1] = dp4a_u(lo, xl.y, S[r][0][1]);
-          S[r][0][2] = dp4a_s(lo, xl.z, S[r][0][2]);
+          S[r][0][2] = dp4a_us(lo, xl.z, S[r][0][2]);
           S[r][1][0] = dp4a_u(hi, xh.x, S[r][1][0]);
           S[r][1][1] = dp4a_u(hi, xh.y, S[r][1][1]);
-          S[r][1][2] = dp4a_s(hi, xh.z, S[r][1][2]);
+          S[r][1][2] = dp4a_us(hi, xh.z, S[r][1][2]);
         }
       }
     }
     const float2 xsum = *reinterpret_cast<const float2*>(xs + 2 * j);
+    const uint32_t sel = 0x4440u + 2u * (uint32_t)(j & 1);
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
+    for (int r = 0; r < 2; ++r) {
       const uint32_t scw = j < 2 ? scl[r] : sch[r], mw = j < 2 ? ml[r] : mh[r];
-      // bytes 2(j&1), 2(j&1)+1 of the packed words: sub-blocks 2j, 2j+1
-      const int sc0 = (int)__byte_perm(scw, 0u, 0x4440 + 2 * (j & 1));
-      const int sc1 = (int)__byte_perm(scw, 0u, 0x4441 + 2 * (j & 1));
-      const int m0 = (int)__byte_perm(mw, 0u, 0x4440 + 2 * (j & 1));
-      const int m1 = (int)__byte_perm(mw, 0u, 0x4441 + 2 * (j & 1));
-      A[r][0] += sc0 * S[r][0][0] + sc1 * S[r][1][0];
-      A[r][1] += sc0 * S[r][0][1] + sc1 * S[r][1][1];
-      A[r][2] += sc0 * S[r][0][2] + sc1 * S[r][1][2];
+      const int sc0 = (int)__byte_perm(scw, 0u, sel) << 4;  // x16: see above
+      const int sc1 = (int)__byte_perm(scw, 0u, sel + 1);
+      const int m0 = (int)__byte_perm(mw, 0u, sel);
+      const int m1 = (int)__byte_perm(mw, 0u, sel + 1);
+#pragma unroll
+      for (int l = 0; l < 3; ++l) A[r][l] += sc0 * S[r][0][l] + sc1 * S[r][1][l];
       M[r] = fmaf((float)m0, xsum.x, fmaf((float)m1, xsum.y, M[r]));
     }
   }
-#pragma unroll
-  for (int r = 0; r < NR; ++r)
-    acc[r % RL][r / RL] += fmaf(dx[r], limbs_to_float(A[r][0], A[r][1], A[r][2]), -(dm[r] * M[r]));
-}
-
-template <int RL, bool DUAL>
-__device__ __forceinline__ void q4k_task(const uint8_t* __restrict__ rows, uint32_t row_stride,
-                                         uint32_t nb, int rows_valid, uint32_t dual_off,
-                                         const int4* __restrict__ xq, const float* __restrict__ xbs,
-                                         const float* __restrict__ xs32, int lane, int lg_rg,
-                                         float (&acc)[RL][2]) {
-  constexpr int NR = RL * (DUAL ? 2 : 1);
-  const int SPR = 32 >> lg_rg;  // block slots (lanes) per row group
-  const int g = lane >> (5 - lg_rg), s = lane & (SPR - 1);
-#pragma unroll
-  for (int r = 0; r < RL; ++r) acc[r][0] = acc[r][1] = 0.f;
-  if (g * RL < rows_valid) {
-    // Rows past rows_valid read stale (in-bounds) stage bytes; their results
-    // are never stored.
-    const uint8_t* rp[NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r)
-      rp[r] = rows + (size_t)(g * RL + (r % RL)) * row_stride + (r >= RL ? dual_off : 0);
-    for (uint32_t b = s; b < nb; b += SPR)
-      q4k_block_rows<RL, DUAL>(rp, b * Q4K_BYTES, xq + 65 * b, xbs[b], xs32 + 8 * b, acc);
-  }
-  for (int o = 16 >> lg_rg; o > 0; o >>= 1)
-#pragma unroll
-    for (int r = 0; r < RL; ++r) {
-      acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], o);
-      if (DUAL) acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], o);
-    }
+  acc0 += fmaf(dx[0], limbs_to_float(A[0][0], A[0][1], A[0][2]) * 0.0625f, -(dm[0] * M[0]));
+  acc1 += fmaf(dx[1], limbs_to_float(A[1][0], A[1][1], A[1][2]) * 0.0625f, -(dm[1] * M[1]));
 }
 
 // ------------------------------- Q6_K ---------------------------------------
-// Blocks are 210 bytes: inside a 16-byte-aligned row, block b starts at an
-// address == 2*b (mod 4).  Lanes of a warp always work on blocks of the same
-// parity P, so every field is either word aligned (P = 0) or two bytes past a
-// word (P = 1); P is a template constant and fields are read as 32-bit words.
+// Words of a Q6_K block at byte offset off from p.  Blocks are 210 bytes and
+// rows 16-byte aligned, so a block starts 2 bytes past a word boundary when
+// its index is odd (P = 1): read the enclosing words and shift.
 template <int P, int NW>
 __device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&o)[NW]) {
   if (P == 0) {
@@ -199,129 +168,79 @@ __device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&o)[NW]) 
   }
 }
 
-// One lane handles half n (128 elements) of a Q6_K block for RL rows
-// (engine/src/ops.c:167-193 dequantize_row_q6_k).  For each 32-bit word i of
-// ql/qh, four words of exact 6-bit quants are formed (element groups +0, +32,
-// +64, +96) and fed to dp4a.  Each 16-element scale group's three limb sums
-// start at -32 * (sum of x limbs), which applies the -32 offset.
-template <int P, int RL>
-__device__ __forceinline__ void q6k_block_rows(const uint8_t* __restrict__ blk, uint32_t row_stride,
-                                               int n, const int4* __restrict__ xq, uint32_t b,
-                                               const int4* __restrict__ xi, float xb,
-                                               float (&acc)[RL]) {
-  const uint32_t M = 0x0F0F0F0Fu;
-  const int4* xh = xq + 65 * b + 32 * n;  // this half's 32 vectors; group g at +8g
-  uint32_t A[RL][8], B[RL][8], H[RL][8], SC[RL][2];
-  float dd[RL];
+// Half n (128 elements) of one Q6_K block for two rows (engine/src/ops.c:167-193
+// dequantize_row_q6_k).  For each 32-bit word i of ql/qh, four words of exact
+// 6-bit quants are formed (element groups +0, +32, +64, +96) and fed to dp4a;
+// each 16-element scale group's three limb sums start at -32 * (sum of x
+// limbs), which applies the -32 offset.  The two 16-element halves `is` of the
+// 32-element groups run in a rolled loop, each loading only its own words.
+template <int P>
+__device__ __forceinline__ void q6k_half2(const uint8_t* __restrict__ b0, const uint8_t* __restrict__ b1,
+                                          int n, const int4* __restrict__ xh,
+                                          const int4* __restrict__ xi, float xb, float& acc0,
+                                          float& acc1) {
+  const uint32_t MK = 0x0F0F0F0Fu;
+  const uint8_t* bp[2] = {b0, b1};
+  uint32_t SC[2][2];
+  float dd[2];
 #pragma unroll
-  for (int r = 0; r < RL; ++r) {
-    const uint8_t* p = blk + (size_t)r * row_stride;
-    load_words<P, 8>(p + 64 * n, A[r]);
-    load_words<P, 8>(p + 64 * n + 32, B[r]);
-    load_words<P, 8>(p + 128 + 32 * n, H[r]);
-    load_words<P, 2>(p + 192 + 8 * n, SC[r]);
-    dd[r] = ref_half(*reinterpret_cast<const uint16_t*>(p + 208)) * xb;
+  for (int r = 0; r < 2; ++r) {
+    load_words<P, 2>(bp[r] + 192 + 8 * n, SC[r]);
+    dd[r] = ref_half(*reinterpret_cast<const uint16_t*>(bp[r] + 208)) * xb;
   }
-  int T[RL][3];
-#pragma unroll
-  for (int r = 0; r < RL; ++r) T[r][0] = T[r][1] = T[r][2] = 0;
-#pragma unroll
+  int T[2][3] = {{0, 0, 0}, {0, 0, 0}};
+#pragma unroll 1
   for (int is = 0; is < 2; ++is) {
-    int S[RL][4][3];
+    uint32_t A[2][4], B[2][4], H[2][4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      load_words<P, 4>(bp[r] + 64 * n + 16 * is, A[r]);
+      load_words<P, 4>(bp[r] + 64 * n + 32 + 16 * is, B[r]);
+      load_words<P, 4>(bp[r] + 128 + 32 * n + 16 * is, H[r]);
+    }
+    int S[2][4][3];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int4 init = xi[2 * g + is];  // -32 * limb sums of this 16-group
 #pragma unroll
-      for (int r = 0; r < RL; ++r) {
+      for (int r = 0; r < 2; ++r) {
         S[r][g][0] = init.x;
         S[r][g][1] = init.y;
         S[r][g][2] = init.z;
       }
     }
 #pragma unroll
-    for (int i = 4 * is; i < 4 * is + 4; ++i) {
+    for (int i = 0; i < 4; ++i) {
       int4 xv[4];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) xv[g] = xh[8 * g + i];
+      for (int g = 0; g < 4; ++g) xv[g] = xh[8 * g + 4 * is + i];
 #pragma unroll
-      for (int r = 0; r < RL; ++r) {
+      for (int r = 0; r < 2; ++r) {
         const uint32_t h = H[r][i];
         const uint32_t hm = h & 0x33333333u, hn = h & 0xCCCCCCCCu;
-        const uint32_t Q[4] = {lop_sel(A[r][i], hm << 4, M), lop_sel(B[r][i], hn << 2, M),
-                               lop_sel(A[r][i] >> 4, hm, M), lop_sel(B[r][i] >> 4, hn >> 2, M)};
+        const uint32_t Q[4] = {lop_sel(A[r][i], hm << 4, MK), lop_sel(B[r][i], hn << 2, MK),
+                               lop_sel(A[r][i] >> 4, hm, MK), lop_sel(B[r][i] >> 4, hn >> 2, MK)};
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           S[r][g][0] = dp4a_u(Q[g], xv[g].x, S[r][g][0]);
           S[r][g][1] = dp4a_u(Q[g], xv[g].y, S[r][g][1]);
-          S[r][g][2] = dp4a_s(Q[g], xv[g].z, S[r][g][2]);
+          S[r][g][2] = dp4a_us(Q[g], xv[g].z, S[r][g][2]);
         }
       }
     }
 #pragma unroll
-    for (int r = 0; r < RL; ++r)
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const int si = is + 2 * g;  // scale index within this half
-        const int sc = (int)(int8_t)__byte_perm(SC[r][si >> 2], 0u, 0x4440 + (si & 3));
+        const uint32_t si = (uint32_t)is + 2u * g;  // scale index within this half
+        const int sc = (int)(int8_t)__byte_perm(SC[r][g >> 1], 0u, 0x4440u + (si & 3u));
         T[r][0] += sc * S[r][g][0];
         T[r][1] += sc * S[r][g][1];
         T[r][2] += sc * S[r][g][2];
       }
   }
-#pragma unroll
-  for (int r = 0; r < RL; ++r) acc[r] = fmaf(dd[r], limbs_to_float(T[r][0], T[r][1], T[r][2]), acc[r]);
-}
-
-template <int P, int RL>
-__device__ __forceinline__ void q6k_class(const uint8_t* __restrict__ row, uint32_t row_stride,
-                                          uint32_t nb, int s, int spr, int n,
-                                          const int4* __restrict__ xq, const int4* __restrict__ xi16,
-                                          const float* __restrict__ xbs, float (&acc)[RL]) {
-  if (nb <= (uint32_t)P) return;
-  const uint32_t nbc = (nb - P + 1) / 2;
-  for (uint32_t t = s; t < nbc; t += spr) {
-    const uint32_t b = P + 2 * t;
-    q6k_block_rows<P, RL>(row + (size_t)b * Q6K_BYTES, row_stride, n, xq, b, xi16 + b * 16 + 8 * n,
-                          xbs[b], acc);
-  }
-}
-
-template <int RL>
-__device__ __forceinline__ void q6k_rows(const uint8_t* __restrict__ row, uint32_t row_stride,
-                                         uint32_t nb, int s, int spr, int n, const int4* xq,
-                                         const int4* xi16, const float* xbs, float (&acc)[RL]) {
-  q6k_class<0, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
-  q6k_class<1, RL>(row, row_stride, nb, s, spr, n, xq, xi16, xbs, acc);
-}
-
-template <int RL, bool DUAL>
-__device__ __forceinline__ void q6k_task(const uint8_t* __restrict__ rows, uint32_t row_stride,
-                                         uint32_t nb, int rows_valid, uint32_t dual_off,
-                                         const int4* __restrict__ xq, const float* __restrict__ xbs,
-                                         const int4* __restrict__ xi16, int lane, int lg_rg,
-                                         float (&acc)[RL][2]) {
-  const int SPR = 16 >> lg_rg;
-  const int slot = lane >> 1, n = lane & 1;
-  const int g = slot >> (4 - lg_rg), s = slot & (SPR - 1);
-  float a0[RL], a1[RL];
-#pragma unroll
-  for (int r = 0; r < RL; ++r) a0[r] = a1[r] = 0.f;
-  if (g * RL < rows_valid) {
-    const uint8_t* row = rows + (size_t)(g * RL) * row_stride;
-    q6k_rows<RL>(row, row_stride, nb, s, SPR, n, xq, xi16, xbs, a0);
-    if (DUAL) q6k_rows<RL>(row + dual_off, row_stride, nb, s, SPR, n, xq, xi16, xbs, a1);
-  }
-  for (int o = 16 >> lg_rg; o > 0; o >>= 1)
-#pragma unroll
-    for (int r = 0; r < RL; ++r) {
-      a0[r] += __shfl_xor_sync(0xffffffffu, a0[r], o);
-      if (DUAL) a1[r] += __shfl_xor_sync(0xffffffffu, a1[r], o);
-    }
-#pragma unroll
-  for (int r = 0; r < RL; ++r) {
-    acc[r][0] = a0[r];
-    acc[r][1] = a1[r];
-  }
+  acc0 = fmaf(dd[0], limbs_to_float(T[0][0], T[0][1], T[0][2]), acc0);
+  acc1 = fmaf(dd[1], limbs_to_float(T[1][0], T[1][1], T[1][2]), acc1);
 }
 
 // ------------------------------ chunk walk ----------------------------------
@@ -342,88 +261,84 @@ __device__ __forceinline__ Range seg_units(const GemvArgs& a, int s, uint64_t se
   return Range{(uint32_t)first_at_or_after(lo), (uint32_t)first_at_or_after(hi)};
 }
 
-template <int RL>
-__device__ __forceinline__ void store_rows(const GemvArgs& a, const GemvSeg& g, uint32_t row0,
-                                           int nvalid, const float (&acc)[RL][2]) {
-  if (g.epi == EPI_ROPE) {
-    // (2i, 2i+1) pairs are adjacent rows of this lane (RL even, row0 even)
-    const float p = (float)__ldcg(a.pos);
-#pragma unroll
-    for (int r = 0; r + 1 < RL; r += 2) {
-      if (r + 1 >= nvalid) break;
-      const uint32_t row = row0 + r;
-      const uint32_t i = row % g.rope_hd;
-      // angle = pos * freq in fp32 as engine/src/ops.c:227-228; freq comes from
-      // a table built with the host libm powf, so the angle matches bit for bit
-      const float ang = p * a.rope_freq[i >> 1];
-      const float c = cosf(ang), sn = sinf(ang);
-      const float x0 = acc[r][0], x1 = acc[r + 1][0];
-      g.y[row] = x0 * c - x1 * sn;
-      g.y[row + 1] = x0 * sn + x1 * c;
-    }
+// Epilogue of one lane group: rl = 2 gives rows row, row+1 (o0, o1); rl = 1
+// one row (o0), or for a dual segment the gate (o0) and up (o1) of one row.
+__device__ __forceinline__ void store2(const GemvArgs& a, const GemvSeg& g, uint32_t row, int nvalid,
+                                       float o0, float o1) {
+  if (g.dual) {  // EPI_SWIGLU: silu(gate) * up (engine/src/ops.c:491-496)
+    const float sig = 1.0f / (1.0f + expf(-o0));
+    g.y[row] = (o0 * sig) * o1;
     return;
   }
-#pragma unroll
-  for (int r = 0; r < RL; ++r) {
-    if (r >= nvalid) break;
-    const uint32_t row = row0 + r;
-    if (g.epi == EPI_STORE) {
-      g.y[row] = acc[r][0];
-    } else if (g.epi == EPI_ADD) {
-      g.y[row] = __ldcg(&g.y[row]) + acc[r][0];
-    } else {  // EPI_SWIGLU: silu(gate) * up
-      const float gt = acc[r][0];
-      const float sig = 1.0f / (1.0f + expf(-gt));
-      g.y[row] = (gt * sig) * acc[r][1];
-    }
+  const bool two = g.rl == 2 && nvalid > 1;
+  if (g.epi == EPI_ROPE) {
+    // (2i, 2i+1) pairs are the two rows of this lane (rl = 2, row even)
+    if (!two) return;
+    const float p = (float)__ldcg(a.pos);
+    const uint32_t i = row % g.rope_hd;
+    // angle = pos * freq in fp32 as engine/src/ops.c:227-228; freq comes from
+    // a table built with the host libm powf, so the angle matches bit for bit
+    const float ang = p * a.rope_freq[i >> 1];
+    const float c = cosf(ang), sn = sinf(ang);
+    g.y[row] = o0 * c - o1 * sn;
+    g.y[row + 1] = o0 * sn + o1 * c;
+  } else if (g.epi == EPI_ADD) {
+    g.y[row] = __ldcg(&g.y[row]) + o0;
+    if (two) g.y[row + 1] = __ldcg(&g.y[row + 1]) + o1;
+  } else {
+    g.y[row] = o0;
+    if (two) g.y[row + 1] = o1;
   }
 }
 
 struct XView {
-  const int4* xq;     // swizzled limb vectors, K/4
+  const int4* xq;     // padded limb vectors, K/4 (+ one pad vector per 256-block)
   const float* xbs;   // per-256-block scale X_b, K/256
   const float* xs32;  // Q4_K: fp32 sums of x per 32-element sub-block, K/32
   const int4* xi16;   // Q6_K: -32 * limb sums per 16-element group, K/16
 };
 
-template <int QT, int RL, bool DUAL>
-__device__ __forceinline__ void task_and_store(const GemvArgs& a, const GemvSeg& g,
-                                               const uint8_t* rows, uint32_t row0, int rows_valid,
-                                               uint32_t dual_off, const XView& x, int lane) {
+// One task of a chunk: rg lane groups, each owning rl output rows (two row
+// pointers r0, r1 per lane: consecutive rows, gate/up rows, or r1 = r0 when a
+// single row is wanted).  Rows past rows_valid read stale (in-bounds) stage
+// bytes; their results are never stored.
+//  Q4_K: 32/rg lanes per group, a lane takes blocks s, s + 32/rg, ...
+//  Q6_K: 16/rg block slots per group, two lanes (halves n) per slot; blocks of
+//        even then odd index (their word alignments differ).
+__device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, const uint8_t* rows,
+                                         uint32_t row0, int rows_valid, uint32_t dual_off,
+                                         const XView& x, int lane) {
   const int lg_rg = __ffs(g.rg) - 1;
-  float acc[RL][2];
-  if (QT == T_Q4K)
-    q4k_task<RL, DUAL>(rows, g.row_stride, g.nb, rows_valid, dual_off, x.xq, x.xbs, x.xs32, lane,
-                       lg_rg, acc);
-  else
-    q6k_task<RL, DUAL>(rows, g.row_stride, g.nb, rows_valid, dual_off, x.xq, x.xbs, x.xi16, lane,
-                       lg_rg, acc);
-  const int lpg = 32 >> lg_rg;  // lanes per row group
-  const int grp = lane >> (5 - lg_rg);
-  if ((lane & (lpg - 1)) == 0 && grp * RL < rows_valid)
-    store_rows<RL>(a, g, row0 + grp * RL, rows_valid - grp * RL, acc);
-}
-
-// (qt, dual, rl) -> instantiation; the planner only picks these.
-__device__ __forceinline__ void dispatch_task(const GemvArgs& a, const GemvSeg& g,
-                                              const uint8_t* rows, uint32_t row0, int rv,
-                                              uint32_t dual_off, const XView& x, int lane) {
-#define SHK_TASK(QT, RL, DU)                                            \
-  task_and_store<QT, RL, DU>(a, g, rows, row0, rv, dual_off, x, lane); \
-  return
-  const int key = (g.qt == T_Q4K ? 0 : 100) + (g.dual ? 10 : 0) + g.rl;
-  switch (key) {
-    case 4: SHK_TASK(T_Q4K, 4, false);
-    case 2: SHK_TASK(T_Q4K, 2, false);
-    case 1: SHK_TASK(T_Q4K, 1, false);
-    case 12: SHK_TASK(T_Q4K, 2, true);
-    case 11: SHK_TASK(T_Q4K, 1, true);
-    case 102: SHK_TASK(T_Q6K, 2, false);
-    case 101: SHK_TASK(T_Q6K, 1, false);
-    case 111: SHK_TASK(T_Q6K, 1, true);
-    default: return;
+  const int rl = g.rl;
+  const bool q4 = g.qt == T_Q4K;
+  const int spr = q4 ? (32 >> lg_rg) : (16 >> lg_rg);
+  const int slot = q4 ? lane : (lane >> 1), n = q4 ? 0 : (lane & 1);
+  const int grp = slot >> (q4 ? 5 - lg_rg : 4 - lg_rg);
+  const int s = slot & (spr - 1);
+  float o0 = 0.f, o1 = 0.f;
+  if (grp * rl < rows_valid) {
+    const uint8_t* r0 = rows + (size_t)(grp * rl) * g.row_stride;
+    const uint8_t* r1 = g.dual ? r0 + dual_off : ((rl == 2 && grp * 2 + 1 < rows_valid) ? r0 + g.row_stride : r0);
+    if (q4) {
+      for (uint32_t b = s; b < g.nb; b += spr)
+        q4k_block2(r0 + (size_t)b * Q4K_BYTES, r1 + (size_t)b * Q4K_BYTES, x.xq + 65 * b, x.xbs[b],
+                   x.xs32 + 8 * b, o0, o1);
+    } else {
+      for (uint32_t b = 2 * s; b < g.nb; b += 2 * spr)
+        q6k_half2<0>(r0 + (size_t)b * Q6K_BYTES, r1 + (size_t)b * Q6K_BYTES, n, x.xq + 65 * b + 32 * n,
+                     x.xi16 + 16 * b + 8 * n, x.xbs[b], o0, o1);
+      for (uint32_t b = 2 * s + 1; b < g.nb; b += 2 * spr)
+        q6k_half2<1>(r0 + (size_t)b * Q6K_BYTES, r1 + (size_t)b * Q6K_BYTES, n, x.xq + 65 * b + 32 * n,
+                     x.xi16 + 16 * b + 8 * n, x.xbs[b], o0, o1);
+    }
   }
-#undef SHK_TASK
+  for (int o = 16 >> lg_rg; o > 0; o >>= 1) {
+    o0 += __shfl_xor_sync(0xffffffffu, o0, o);
+    o1 += __shfl_xor_sync(0xffffffffu, o1, o);
+  }
+  const int lpg = 32 >> lg_rg;  // lanes per group
+  if ((lane & (lpg - 1)) == 0 && grp * rl < rows_valid)
+    store2(a, g, row0 + grp * rl, rows_valid - grp * rl, o0, o1);
 }
 
 // Shared-memory map: [full | empty | xbar barriers][done][gen][red]
@@ -490,10 +405,18 @@ struct RingPos {
   }
 };
 
+#ifndef GEMV_PRE_STAGES
+#define GEMV_PRE_STAGES 1
+#endif
 // Producer (one lane): streams this CTA's chunks of plan `a` (cost range
-// [lo, hi)) into the ring.  False if a bounded wait ran out.
+// [lo, hi)) into the ring.  If xready is given, only GEMV_PRE_STAGES chunks
+// are issued before the consumers signal that their loads of x have landed:
+// a full ring of bulk copies queued ahead of those loads (about 30 MB over
+// all SMs) would delay them by several microseconds.  False if a bounded wait
+// ran out.
 __device__ __forceinline__ bool gemv_produce(const GemvArgs& a, const Ring& R, RingPos& p,
-                                             uint64_t lo, uint64_t hi) {
+                                             uint64_t lo, uint64_t hi, uint64_t* xready = nullptr) {
+  uint32_t issued = 0;
   uint64_t seg_off = 0;
   for (uint32_t s = 0; s < a.nseg; ++s) {
     const GemvSeg& g = a.seg[s];
@@ -503,6 +426,10 @@ __device__ __forceinline__ bool gemv_produce(const GemvArgs& a, const Ring& R, R
       const uint32_t r0 = u << lg_ur;
       const uint32_t r1 = min(min(u + cu, rr.ue) << lg_ur, g.m);
       const uint32_t bytes = (r1 - r0) * g.row_stride;
+      if (xready && issued == GEMV_PRE_STAGES &&
+          !mbar_wait_bounded(xready, 0, a.err, DERR_TIMEOUT_FULL))
+        return false;
+      ++issued;
       if (p.it >= R.ns && !mbar_wait_bounded(&R.empty[p.st], p.ph ^ 1u, a.err, DERR_TIMEOUT_EMPTY))
         return false;
       uint8_t* dst = R.stages + (size_t)p.st * R.stage_bytes;
@@ -539,123 +466,139 @@ struct XBuf {
 
 // Consumers (warps 0..GEMV_WARPS-1): x (optionally RMSNorm'ed) -> fixed-point
 // limb vectors in shared memory.  Ends with a consumer-only barrier.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Consumers (warps 0..GEMV_WARPS-1): x (optionally RMSNorm'ed) -> fixed-point
+// limb vectors in shared memory.  Warp w owns 256-blocks w, w+8, ...; lane l
+// holds elements 8l..8l+7 of a block (limb vectors 2l, 2l+1), so a block's
+// maximum is a warp reduction.  Raw x is first copied (cp.async, all copies in
+// flight at once) into the very slots the lane later overwrites with limbs;
+// xready (nullable) is arrived on by each warp once its copies have landed.
+// Rolled loops: this runs once per launch, compact code matters more.
+// Ends with a consumer-only barrier.
 template <bool HAS4, bool HAS6>
 __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
-                                              int warp, int lane) {
+                                              int warp, int lane, uint64_t* xready = nullptr) {
   constexpr int CT = 32 * GEMV_WARPS;
-  constexpr int BPW = 4;  // 256-blocks per warp per pass (32 floats per lane)
   const uint32_t K = a.k;
   const uint32_t NB = K / 256;
   int4* xq = xb_.xq;
   float* xbs = xb_.xbs;
   float* xs32 = xb_.xs32;
   int4* xi16 = xb_.xi16;
+  float4* xr = reinterpret_cast<float4*>(xq);  // raw x staged in the limb slots
   const bool xal = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  const bool wal = a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
-  // Fixed-point conversion.  Warp w owns 256-blocks w, w+8, ...; lane l holds
-  // elements 8l..8l+7 of a block (limb vectors 2l, 2l+1), so the block maximum
-  // is a warp reduction.  A pass loads up to BPW blocks per warp before using
-  // any of them.
-  for (uint32_t pass = 0; pass * GEMV_WARPS * BPW < NB; ++pass) {
-    float v[BPW][8];
-#pragma unroll
-    for (int u = 0; u < BPW; ++u) {
-      const uint32_t kb = warp + GEMV_WARPS * (BPW * pass + u);
-      const float* src = a.x + 256 * (size_t)(kb < NB ? kb : 0) + 8 * lane;
-      if (xal) {
-        const float4 t0 = __ldcg(reinterpret_cast<const float4*>(src));
-        const float4 t1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
-        v[u][0] = t0.x; v[u][1] = t0.y; v[u][2] = t0.z; v[u][3] = t0.w;
-        v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[u][e] = __ldcg(src + e);
-      }
+#pragma unroll 1
+  for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
+    const uint32_t v0 = 64 * kb + 2 * lane;
+    const float* src = a.x + 256 * (size_t)kb + 8 * lane;
+    if (xal) {
+      cp_async16(&xr[xpad(v0)], src);
+      cp_async16(&xr[xpad(v0 + 1)], src + 4);
+    } else {
+      xr[xpad(v0)] = make_float4(__ldcg(src), __ldcg(src + 1), __ldcg(src + 2), __ldcg(src + 3));
+      xr[xpad(v0 + 1)] = make_float4(__ldcg(src + 4), __ldcg(src + 5), __ldcg(src + 6), __ldcg(src + 7));
     }
-    if (a.norm_w) {
-      // RMSNorm prologue (engine/src/ops.c:195-214); the planner guarantees a
-      // single pass, and the fixed-order reduction gives every CTA the same scale.
-      float ss = 0.f;
-#pragma unroll
-      for (int u = 0; u < BPW; ++u)
-        if (warp + GEMV_WARPS * u < NB)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ss = fmaf(v[u][e], v[u][e], ss);
-      ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      named_sync(1, CT);
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
-      const float inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
-#pragma unroll
-      for (int u = 0; u < BPW; ++u) {
-        const uint32_t kb = warp + GEMV_WARPS * u;
-        const float* wn = a.norm_w + 256 * (size_t)(kb < NB ? kb : 0) + 8 * lane;
-        float w[8];
-        if (wal) {
-          const float4 t0 = __ldg(reinterpret_cast<const float4*>(wn));
-          const float4 t1 = __ldg(reinterpret_cast<const float4*>(wn) + 1);
-          w[0] = t0.x; w[1] = t0.y; w[2] = t0.z; w[3] = t0.w;
-          w[4] = t1.x; w[5] = t1.y; w[6] = t1.z; w[7] = t1.w;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) w[e] = __ldg(wn + e);
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < BPW; ++u) {
-      const uint32_t kb = warp + GEMV_WARPS * (BPW * pass + u);
-      if (kb >= NB) break;  // uniform across the warp
-      float amax = 0.f;
-      bool finite = true;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        amax = fmaxf(amax, fabsf(v[u][e]));
-        finite = finite && isfinite(v[u][e]);
-      }
-      amax = warp_max(amax);
-      finite = __all_sync(0xffffffffu, finite);
-      // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
-      // whose maximum is below 2^-104 are scaled as if it were 2^-104.
-      const int f = amax > 0.f ? max(ilogbf(amax), -104) : 0;
-      const float xb = finite ? ldexpf(1.0f, f - 21) : __int_as_float(0x7fc00000);
-      const float inv_xb = ldexpf(1.0f, 21 - f);
-      if (lane == 0) xbs[kb] = xb;
-      int t[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) t[e] = finite ? __float2int_rn(v[u][e] * inv_xb) : 0;
-      uint32_t lw[2][3];  // [vector][limb]: limb k of 4 elements = byte k of each
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-          const uint32_t sel = (uint32_t)k | ((uint32_t)(k + 4) << 4);
-          const uint32_t lo = __byte_perm((uint32_t)t[4 * h], (uint32_t)t[4 * h + 1], sel);
-          const uint32_t hi = __byte_perm((uint32_t)t[4 * h + 2], (uint32_t)t[4 * h + 3], sel);
-          lw[h][k] = __byte_perm(lo, hi, 0x5410);
-        }
+  }
+  cp_async_wait_all();
+  __syncwarp();
+  if (xready && lane == 0) mbar_arrive(xready);
+
+  const float* nw = a.norm_w;
+  float inv_rms = 1.0f;
+  if (nw) {
+    // RMSNorm prologue (engine/src/ops.c:195-214); the fixed-order reduction
+    // gives every CTA the same scale.
+    float ss = 0.f;
+#pragma unroll 1
+    for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
       const uint32_t v0 = 64 * kb + 2 * lane;
-      xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], 0);
-      xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], 0);
-      if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
-        float s = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = s;
+      const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
+      ss = fmaf(t0.x, t0.x, ss); ss = fmaf(t0.y, t0.y, ss); ss = fmaf(t0.z, t0.z, ss); ss = fmaf(t0.w, t0.w, ss);
+      ss = fmaf(t1.x, t1.x, ss); ss = fmaf(t1.y, t1.y, ss); ss = fmaf(t1.z, t1.z, ss); ss = fmaf(t1.w, t1.w, ss);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    named_sync(1, CT);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
+    inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
+  }
+  // norm weights of the first block (then one block ahead)
+  float4 w0 = make_float4(1.f, 1.f, 1.f, 1.f), w1 = w0;
+  if (nw && warp < (int)NB) {
+    w0 = __ldg(reinterpret_cast<const float4*>(nw + 256 * (size_t)warp + 8 * lane));
+    w1 = __ldg(reinterpret_cast<const float4*>(nw + 256 * (size_t)warp + 8 * lane) + 1);
+  }
+#pragma unroll 1
+  for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
+    float4 n0 = w0, n1 = w1;
+    if (nw && kb + GEMV_WARPS < NB) {
+      const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)(kb + GEMV_WARPS) + 8 * lane);
+      n0 = __ldg(wn);
+      n1 = __ldg(wn + 1);
+    }
+    const uint32_t v0 = 64 * kb + 2 * lane;
+    const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
+    float v[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+    if (nw) {
+      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = (v[e] * inv_rms) * w[e];
+    }
+    w0 = n0;
+    w1 = n1;
+    float amax = 0.f;
+    bool finite = true;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      amax = fmaxf(amax, fabsf(v[e]));
+      finite = finite && isfinite(v[e]);
+    }
+    amax = warp_max(amax);
+    finite = __all_sync(0xffffffffu, finite);
+    // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
+    // whose maximum is below 2^-104 are scaled as if it were 2^-104.
+    const int f = amax > 0.f ? max(ilogbf(amax), -104) : 0;
+    const float xbv = finite ? ldexpf(1.0f, f - 21) : __int_as_float(0x7fc00000);
+    const float inv_xb = ldexpf(1.0f, 21 - f);
+    if (lane == 0) xbs[kb] = xbv;
+    int t[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = finite ? __float2int_rn(v[e] * inv_xb) : 0;
+    uint32_t lw[2][3];  // [vector][limb]: limb k of 4 elements = byte k of each
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const uint32_t sel = (uint32_t)k | ((uint32_t)(k + 4) << 4);
+        const uint32_t lo = __byte_perm((uint32_t)t[4 * h], (uint32_t)t[4 * h + 1], sel);
+        const uint32_t hi = __byte_perm((uint32_t)t[4 * h + 2], (uint32_t)t[4 * h + 3], sel);
+        lw[h][k] = __byte_perm(lo, hi, 0x5410);
       }
-      if (HAS6) {  // -32 * limb sums per 16-element group (2 lanes)
-        int l0 = (int)__dp4a(lw[0][0], 0x01010101u, __dp4a(lw[1][0], 0x01010101u, 0u));
-        int l1 = (int)__dp4a(lw[0][1], 0x01010101u, __dp4a(lw[1][1], 0x01010101u, 0u));
-        int l2 = __dp4a((int)lw[0][2], 0x01010101, __dp4a((int)lw[1][2], 0x01010101, 0));
-        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-        l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
-        if ((lane & 1) == 0) xi16[16 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
-      }
+    xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], 0);
+    xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], 0);
+    if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
+      float sm = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+      sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+      sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+      if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = sm;
+    }
+    if (HAS6) {  // -32 * limb sums per 16-element group (2 lanes)
+      int l0 = (int)__dp4a(lw[0][0], 0x01010101u, __dp4a(lw[1][0], 0x01010101u, 0u));
+      int l1 = (int)__dp4a(lw[0][1], 0x01010101u, __dp4a(lw[1][1], 0x01010101u, 0u));
+      int l2 = __dp4a((int)lw[0][2], 0x01010101, __dp4a((int)lw[1][2], 0x01010101, 0));
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
+      if ((lane & 1) == 0) xi16[16 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
     }
   }
   named_sync(1, CT);
@@ -688,7 +631,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const Ring& R, R
         for (; t < ntasks; t += GEMV_WARPS, ++mine) {
           const int rv = (int)min(ur, nrows - (t << lg_ur));
           const uint8_t* rows = buf + (size_t)(t << lg_ur) * g.row_stride;
-          dispatch_task(a, g, rows, r0 + (t << lg_ur), rv, dual_off, xv, lane);
+          run_task(a, g, rows, r0 + (t << lg_ur), rv, dual_off, xv, lane);
         }
         __syncwarp();
         if (lane == 0) {

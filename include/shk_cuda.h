@@ -56,6 +56,9 @@ struct shk_cuda_config {
  * barriers between phases) instead of captured graphs of per-projection
  * kernels.  Both give the same results within fp32 rounding. */
 #define SHK_CUDA_FLAG_PERSISTENT 2u
+/* Capture the decode-step graphs without programmatic dependent launch
+ * (each kernel then starts only after its predecessor has finished). */
+#define SHK_CUDA_FLAG_NO_PDL 4u
 
 /* ---- context: replaces metal_ops_init/metal_ops_shutdown/metal_available/
  *      metal_ops_report (engine/include/metal_ops.h:5-6, 24-25) ---- */

@@ -60,6 +60,8 @@ constexpr int ATT_THREADS = 32 * ATT_WARPS;
 template <int HD, int G>
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
   __shared__ __align__(16) float sm[AttnSmem<HD, G, ATT_WARPS>::FLOATS];
+  pdl_trigger();
+  pdl_wait();
   attn_item<HD, G, ATT_WARPS>(a, blockIdx.x, blockIdx.y, gridDim.y, sm);
 }
 
@@ -107,10 +109,10 @@ template <int HD>
 cudaError_t attn_launch_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
   dim3 grid(a.kv.n_kv, a.max_splits);
   switch (G) {
-    case 1: attn_decode_kernel<HD, 1><<<grid, ATT_THREADS, 0, st>>>(a); break;
-    case 2: attn_decode_kernel<HD, 2><<<grid, ATT_THREADS, 0, st>>>(a); break;
-    case 4: attn_decode_kernel<HD, 4><<<grid, ATT_THREADS, 0, st>>>(a); break;
-    case 8: attn_decode_kernel<HD, 8><<<grid, ATT_THREADS, 0, st>>>(a); break;
+    case 1: return launch_k(attn_decode_kernel<HD, 1>, grid, dim3(ATT_THREADS), 0, st, a);
+    case 2: return launch_k(attn_decode_kernel<HD, 2>, grid, dim3(ATT_THREADS), 0, st, a);
+    case 4: return launch_k(attn_decode_kernel<HD, 4>, grid, dim3(ATT_THREADS), 0, st, a);
+    case 8: return launch_k(attn_decode_kernel<HD, 8>, grid, dim3(ATT_THREADS), 0, st, a);
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

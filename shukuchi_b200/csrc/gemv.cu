@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_trigger();  // the next kernel may be scheduled; it waits for this one before its reads
 
   const uint64_t lo = a.total_cost * blockIdx.x / gridDim.x;
   const uint64_t hi = a.total_cost * (blockIdx.x + 1) / gridDim.x;
@@ -62,6 +63,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
     }
     return;
   }
+  pdl_wait();  // x and the residual come from the previous kernel (weights do not)
   gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar);
   uint32_t gtask = 0;
   gemv_consume(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
@@ -215,12 +217,10 @@ cudaError_t gemv_init() {
 cudaError_t gemv_launch(const GemvPlan& p, cudaStream_t stream) {
   if (p.args.total_cost == 0) return cudaSuccess;
   if (p.has4 && p.has6)
-    gemv_kernel<true, true><<<p.grid, GEMV_THREADS, p.smem, stream>>>(p.args);
-  else if (p.has4)
-    gemv_kernel<true, false><<<p.grid, GEMV_THREADS, p.smem, stream>>>(p.args);
-  else
-    gemv_kernel<false, true><<<p.grid, GEMV_THREADS, p.smem, stream>>>(p.args);
-  return cudaGetLastError();
+    return launch_k(gemv_kernel<true, true>, dim3(p.grid), dim3(GEMV_THREADS), p.smem, stream, p.args);
+  if (p.has4)
+    return launch_k(gemv_kernel<true, false>, dim3(p.grid), dim3(GEMV_THREADS), p.smem, stream, p.args);
+  return launch_k(gemv_kernel<false, true>, dim3(p.grid), dim3(GEMV_THREADS), p.smem, stream, p.args);
 }
 
 cudaError_t gemv_generic_launch(uint32_t qt, const void* w, const float* x, float* y, uint32_t m,

@@ -20,6 +20,8 @@ using namespace gldev;
 __global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t dtype,
                              const uint32_t* __restrict__ tok_p, uint32_t n_vocab, float* out,
                              uint32_t n_embd, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t tok = *tok_p;
   if (tok >= n_vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) set_error(err, DERR_BAD_TOKEN);
@@ -40,6 +42,8 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restr
   __shared__ float sv[AM_THREADS / 32];
   __shared__ uint32_t si[AM_THREADS / 32];
   __shared__ int last;
+  pdl_trigger();
+  pdl_wait();
   const uint32_t per = (n + gridDim.x - 1) / gridDim.x;
   const uint32_t lo = blockIdx.x * per, hi = min(n, lo + per);
   float bv;
@@ -109,9 +113,8 @@ __global__ void add_kernel(float* y, const float* x, uint32_t n) {
 
 cudaError_t embed_launch(const void* table, uint32_t dtype, const uint32_t* tok, uint32_t n_vocab,
                          float* out, uint32_t n_embd, int* err, cudaStream_t st) {
-  embed_kernel<<<(n_embd + 255) / 256, 256, 0, st>>>(static_cast<const uint8_t*>(table), dtype, tok,
-                                                     n_vocab, out, n_embd, err);
-  return cudaGetLastError();
+  return launch_k(embed_kernel, dim3((n_embd + 255) / 256), dim3(256), 0, st,
+                  static_cast<const uint8_t*>(table), dtype, tok, n_vocab, out, n_embd, err);
 }
 
 int argmax_blocks(uint32_t n) {
@@ -121,9 +124,13 @@ int argmax_blocks(uint32_t n) {
 
 cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* part_i, int* counter,
                           uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st) {
-  argmax_kernel<<<argmax_blocks(n), AM_THREADS, 0, st>>>(x, n, part_v, part_i, counter, tok_out,
-                                                         pos_inc);
-  return cudaGetLastError();
+  return launch_k(argmax_kernel, dim3(argmax_blocks(n)), dim3(AM_THREADS), 0, st, x, n, part_v, part_i,
+                  counter, tok_out, pos_inc);
+}
+
+bool& pdl_enabled() {
+  static thread_local bool on = false;
+  return on;
 }
 
 cudaError_t rmsnorm_launch(const float* x, const float* w, float* y, uint32_t d, cudaStream_t st) {

@@ -572,20 +572,24 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
   return SHK_OK;
 }
 
-int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos) {
+// pdl_after_first: launches after the first one carry the programmatic
+// dependent launch attribute (used while capturing the decode-step graphs).
+int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos, bool pdl_after_first = false) {
   if (m->head_generic)
     CK(gemv_generic_launch(m->d.output_dtype, m->d.output_dev, m->hidden, m->logits, m->d.n_vocab,
                            m->d.n_embd, st));
   else
     CK(gemv_launch(m->head, st));
+  if (pdl_after_first) pdl_enabled() = true;
   CK(argmax_launch(m->logits, m->d.n_vocab, m->am_v, m->am_i, m->am_cnt, m->d_tok,
                    advance_pos ? m->d_tok + 1 : nullptr, st));
   return SHK_OK;
 }
 
-int enqueue_layers(shk_model* m, cudaStream_t st) {
+int enqueue_layers(shk_model* m, cudaStream_t st, bool pdl_after_first = false) {
   CK(embed_launch(m->d.tok_embd_dev, m->d.tok_embd_dtype, m->d_tok, m->d.n_vocab, m->hidden,
                   m->d.n_embd, m->ctx->d_err, st));
+  if (pdl_after_first) pdl_enabled() = true;
   for (uint32_t l = 0; l < m->d.n_layers; ++l) {
     const int rc = enqueue_layer(m, m->plans[l], l, m->d_tok + 1, st);
     if (rc) return rc;
@@ -597,9 +601,14 @@ int capture(shk_model* m, int which, cudaGraphExec_t* out) {
   cudaStream_t st = m->ctx->compute;
   cudaGraph_t g = nullptr;
   CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-  // 0: embed + all layers;  1: lm_head + argmax;  2: both, argmax advancing *pos
-  int rc = which == 1 ? SHK_OK : enqueue_layers(m, st);
-  if (!rc && which != 0) rc = enqueue_head(m, st, which == 2);
+  // 0: embed + all layers;  1: lm_head + argmax;  2: both, argmax advancing *pos.
+  // Every kernel after the first is a programmatic dependent launch: it is
+  // scheduled while its predecessor drains and waits for it before its reads.
+  const bool pdl = !(m->ctx->flags & SHK_CUDA_FLAG_NO_PDL);
+  pdl_enabled() = false;
+  int rc = which == 1 ? SHK_OK : enqueue_layers(m, st, pdl);
+  if (!rc && which != 0) rc = enqueue_head(m, st, which == 2, pdl);
+  pdl_enabled() = false;
   const cudaError_t ee = cudaStreamEndCapture(st, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);

@@ -16,6 +16,7 @@ HEADER = os.path.join(os.path.dirname(_HERE), "include", "shk_cuda.h")
 
 SHK_OK = 0
 FLAG_PERSISTENT = 2  # SHK_CUDA_FLAG_PERSISTENT: whole-token steps in the persistent decode kernel
+FLAG_NO_PDL = 4  # SHK_CUDA_FLAG_NO_PDL: decode-step graphs without programmatic dependent launch
 STATUS = {0: "SHK_OK", -1: "SHK_EINVAL", -2: "SHK_ENOMEM", -3: "SHK_ECUDA", -4: "SHK_EUNSUPPORTED",
           -5: "SHK_ETIMEOUT", -6: "SHK_ENODEV", -7: "SHK_ENCCL", -8: "SHK_EDEVICE"}
 

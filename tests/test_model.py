@@ -77,11 +77,21 @@ def ctx_persist():
     c.close()
 
 
-@pytest.mark.parametrize("path", ["graphs", "persistent"])
+@pytest.fixture(scope="module")
+def ctx_nopdl():
+    """A context whose decode-step graphs use plain stream order."""
+    c = sc.Context(0, flags=sc.FLAG_NO_PDL)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("path", ["graphs", "graphs_no_pdl", "persistent"])
 @pytest.mark.parametrize("shape,n_prompt,n_decode", [("small", 5, 12), ("tiny", 3, 9)])
-def test_generate_matches_oracle(oracle, ctx, ctx_persist, shape, n_prompt, n_decode, path):
+def test_generate_matches_oracle(oracle, ctx, ctx_persist, ctx_nopdl, shape, n_prompt, n_decode, path):
     if path == "persistent":
         ctx = ctx_persist
+    elif path == "graphs_no_pdl":
+        ctx = ctx_nopdl
     model = synth.make_model(shape, seed=21)
     rng = np.random.default_rng(9)
     prompt = rng.integers(0, model.shape.n_vocab, n_prompt).astype(np.uint32)

@@ -40,18 +40,24 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   const Ring R{full, empty, done, gen, smem + stage_off, NS, a.stage_bytes};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-      done[s] = 0;
-      gen[s] = 0xFFFFFFFFu;
+  const uint32_t tid = threadIdx.x;
+  if (tid <= NS) {  // one thread per barrier pair, in parallel
+    if (tid < NS) {
+      mbar_init(&full[tid], 1);
+      mbar_init(&empty[tid], 1);
+      done[tid] = 0;
+      gen[tid] = 0xFFFFFFFFu;
+    } else {
+      mbar_init(xbar, GEMV_WARPS);
     }
-    mbar_init(xbar, GEMV_WARPS);
     fence_mbar_init();
   }
-  __syncthreads();
   pdl_trigger();  // the next kernel may be scheduled; it waits for this one before its reads
+  if (warp < GEMV_WARPS) {
+    pdl_wait();  // x and the residual come from the previous kernel (weights do not)
+    gemv_x_issue(a, xb, warp, lane);
+  }
+  __syncthreads();
 
   const uint64_t lo = a.total_cost * blockIdx.x / gridDim.x;
   const uint64_t hi = a.total_cost * (blockIdx.x + 1) / gridDim.x;
@@ -63,8 +69,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
     }
     return;
   }
-  pdl_wait();  // x and the residual come from the previous kernel (weights do not)
-  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar);
+  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true);
   uint32_t gtask = 0;
   gemv_consume(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
 }

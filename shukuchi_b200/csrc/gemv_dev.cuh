@@ -466,6 +466,12 @@ struct XBuf {
 
 // Consumers (warps 0..GEMV_WARPS-1): x (optionally RMSNorm'ed) -> fixed-point
 // limb vectors in shared memory.  Ends with a consumer-only barrier.
+// Profiling hook: a build may define GEMV_STAMP(i) to record a timestamp at
+// point i of the prologue; empty by default.
+#ifndef GEMV_STAMP
+#define GEMV_STAMP(i)
+#endif
+
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
                : "memory");
@@ -482,17 +488,10 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // xready (nullable) is arrived on by each warp once its copies have landed.
 // Rolled loops: this runs once per launch, compact code matters more.
 // Ends with a consumer-only barrier.
-template <bool HAS4, bool HAS6>
-__device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
-                                              int warp, int lane, uint64_t* xready = nullptr) {
-  constexpr int CT = 32 * GEMV_WARPS;
-  const uint32_t K = a.k;
-  const uint32_t NB = K / 256;
-  int4* xq = xb_.xq;
-  float* xbs = xb_.xbs;
-  float* xs32 = xb_.xs32;
-  int4* xi16 = xb_.xi16;
-  float4* xr = reinterpret_cast<float4*>(xq);  // raw x staged in the limb slots
+// Step 1 of the prologue: start the copies of raw x into this lane's slots.
+__device__ __forceinline__ void gemv_x_issue(const GemvArgs& a, const XBuf& xb_, int warp, int lane) {
+  const uint32_t NB = a.k / 256;
+  float4* xr = reinterpret_cast<float4*>(xb_.xq);  // raw x staged in the limb slots
   const bool xal = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
 #pragma unroll 1
   for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
@@ -506,8 +505,27 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
       xr[xpad(v0 + 1)] = make_float4(__ldcg(src + 4), __ldcg(src + 5), __ldcg(src + 6), __ldcg(src + 7));
     }
   }
+  GEMV_STAMP(0);
+}
+
+// The rest: wait for the copies, RMSNorm scale, conversion.  x_issued: step 1
+// already ran (else it runs here).
+template <bool HAS4, bool HAS6>
+__device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
+                                              int warp, int lane, uint64_t* xready = nullptr,
+                                              bool x_issued = false) {
+  constexpr int CT = 32 * GEMV_WARPS;
+  const uint32_t K = a.k;
+  const uint32_t NB = K / 256;
+  int4* xq = xb_.xq;
+  float* xbs = xb_.xbs;
+  float* xs32 = xb_.xs32;
+  int4* xi16 = xb_.xi16;
+  float4* xr = reinterpret_cast<float4*>(xq);
+  if (!x_issued) gemv_x_issue(a, xb_, warp, lane);
   cp_async_wait_all();
   __syncwarp();
+  GEMV_STAMP(1);
   if (xready && lane == 0) mbar_arrive(xready);
 
   const float* nw = a.norm_w;
@@ -531,76 +549,93 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
     for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
     inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
   }
-  // norm weights of the first block (then one block ahead)
-  float4 w0 = make_float4(1.f, 1.f, 1.f, 1.f), w1 = w0;
-  if (nw && warp < (int)NB) {
-    w0 = __ldg(reinterpret_cast<const float4*>(nw + 256 * (size_t)warp + 8 * lane));
-    w1 = __ldg(reinterpret_cast<const float4*>(nw + 256 * (size_t)warp + 8 * lane) + 1);
-  }
+  GEMV_STAMP(2);
+  // Conversion, PU blocks per iteration: independent dependency chains in
+  // flight (a single block's chain -- reductions, shuffles, packing -- is long).
+  constexpr int PU = 4;
 #pragma unroll 1
-  for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
-    float4 n0 = w0, n1 = w1;
-    if (nw && kb + GEMV_WARPS < NB) {
-      const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)(kb + GEMV_WARPS) + 8 * lane);
-      n0 = __ldg(wn);
-      n1 = __ldg(wn + 1);
-    }
-    const uint32_t v0 = 64 * kb + 2 * lane;
-    const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
-    float v[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
-    if (nw) {
-      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  for (uint32_t kb0 = warp; kb0 < NB; kb0 += PU * GEMV_WARPS) {
+    float v[PU][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = (v[e] * inv_rms) * w[e];
-    }
-    w0 = n0;
-    w1 = n1;
-    float amax = 0.f;
-    bool finite = true;
+    for (int u = 0; u < PU; ++u) {
+      const uint32_t kb = kb0 + u * GEMV_WARPS;
+      const uint32_t kc = kb < NB ? kb : kb0;
+      const uint32_t v0 = 64 * kc + 2 * lane;
+      const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
+      v[u][0] = t0.x; v[u][1] = t0.y; v[u][2] = t0.z; v[u][3] = t0.w;
+      v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
+      if (nw) {
+        const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)kc + 8 * lane);
+        const float4 w0 = __ldg(wn), w1 = __ldg(wn + 1);
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      amax = fmaxf(amax, fabsf(v[e]));
-      finite = finite && isfinite(v[e]);
-    }
-    amax = warp_max(amax);
-    finite = __all_sync(0xffffffffu, finite);
-    // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
-    // whose maximum is below 2^-104 are scaled as if it were 2^-104.
-    const int f = amax > 0.f ? max(ilogbf(amax), -104) : 0;
-    const float xbv = finite ? ldexpf(1.0f, f - 21) : __int_as_float(0x7fc00000);
-    const float inv_xb = ldexpf(1.0f, 21 - f);
-    if (lane == 0) xbs[kb] = xbv;
-    int t[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) t[e] = finite ? __float2int_rn(v[e] * inv_xb) : 0;
-    uint32_t lw[2][3];  // [vector][limb]: limb k of 4 elements = byte k of each
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const uint32_t sel = (uint32_t)k | ((uint32_t)(k + 4) << 4);
-        const uint32_t lo = __byte_perm((uint32_t)t[4 * h], (uint32_t)t[4 * h + 1], sel);
-        const uint32_t hi = __byte_perm((uint32_t)t[4 * h + 2], (uint32_t)t[4 * h + 3], sel);
-        lw[h][k] = __byte_perm(lo, hi, 0x5410);
+        for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
       }
-    xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], 0);
-    xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], 0);
-    if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
-      float sm = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-      sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-      sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-      if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = sm;
     }
-    if (HAS6) {  // -32 * limb sums per 16-element group (2 lanes)
-      int l0 = (int)__dp4a(lw[0][0], 0x01010101u, __dp4a(lw[1][0], 0x01010101u, 0u));
-      int l1 = (int)__dp4a(lw[0][1], 0x01010101u, __dp4a(lw[1][1], 0x01010101u, 0u));
-      int l2 = __dp4a((int)lw[0][2], 0x01010101, __dp4a((int)lw[1][2], 0x01010101, 0));
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-      l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
-      if ((lane & 1) == 0) xi16[16 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
+    float amax[PU];
+    bool finite[PU];
+#pragma unroll
+    for (int u = 0; u < PU; ++u) {
+      amax[u] = 0.f;
+      finite[u] = true;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        amax[u] = fmaxf(amax[u], fabsf(v[u][e]));
+        finite[u] = finite[u] && isfinite(v[u][e]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < PU; ++u) amax[u] = fmaxf(amax[u], __shfl_xor_sync(0xffffffffu, amax[u], o));
+#pragma unroll
+    for (int u = 0; u < PU; ++u) {
+      const uint32_t kb = kb0 + u * GEMV_WARPS;
+      if (kb >= NB) break;  // uniform across the warp
+      const bool fin = __all_sync(0xffffffffu, finite[u]);
+      // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
+      // whose maximum is below 2^-104 (subnormal maxima included) are scaled as
+      // if it were 2^-104.  f from the exponent bits; the powers of two are
+      // built from bits (f - 21 and 21 - f stay within the normal range).
+      const int e8 = (int)((__float_as_uint(amax[u]) >> 23) & 0xFFu);
+      const int f = amax[u] > 0.f ? max(e8 - 127, -104) : 0;
+      const float xbv = fin ? __uint_as_float((uint32_t)(f - 21 + 127) << 23) : __int_as_float(0x7fc00000);
+      const float inv_xb = __uint_as_float((uint32_t)(21 - f + 127) << 23);
+      if (lane == 0) xbs[kb] = xbv;
+      int t[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) t[e] = fin ? __float2int_rn(v[u][e] * inv_xb) : 0;
+      uint32_t lw[2][3];  // [vector][limb]: limb k of 4 elements = byte k of each
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const uint32_t sel = (uint32_t)k | ((uint32_t)(k + 4) << 4);
+          const uint32_t lo = __byte_perm((uint32_t)t[4 * h], (uint32_t)t[4 * h + 1], sel);
+          const uint32_t hi = __byte_perm((uint32_t)t[4 * h + 2], (uint32_t)t[4 * h + 3], sel);
+          lw[h][k] = __byte_perm(lo, hi, 0x5410);
+        }
+      const uint32_t v0 = 64 * kb + 2 * lane;
+      xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], 0);
+      xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], 0);
+      if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
+        float sm = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = sm;
+      }
+      if (HAS6) {  // -32 * limb sums per 16-element group (2 lanes)
+        int l0 = (int)__dp4a(lw[0][0], 0x01010101u, __dp4a(lw[1][0], 0x01010101u, 0u));
+        int l1 = (int)__dp4a(lw[0][1], 0x01010101u, __dp4a(lw[1][1], 0x01010101u, 0u));
+        int l2 = __dp4a((int)lw[0][2], 0x01010101, __dp4a((int)lw[1][2], 0x01010101, 0));
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
+        if ((lane & 1) == 0) xi16[16 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
+      }
     }
   }
+  GEMV_STAMP(3);
   named_sync(1, CT);
 }
 

@@ -78,13 +78,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait on a phase parity.  Returns false (and records `code`) if the
 // phase did not complete within WAIT_BUDGET_NS.
+// The clock is read once per 32 polls and each unsuccessful poll backs off
+// briefly, so waiting warps leave the issue slots to the working ones.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
                                                   int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
+    __nanosleep(32);
+    if ((n & 31) == 0 && globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
       set_error(err, code);
       return false;
     }

@@ -157,15 +157,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) decode_kernel(const __grid_co
         xb.xbs = reinterpret_cast<float*>(xreg + xq_bytes(K));
         xb.xs32 = xb.xbs + xbs_floats(K);
         xb.xi16 = reinterpret_cast<int4*>(xreg + xq_bytes(K) + (size_t)xbs_floats(K) * 4 + (size_t)(K / 32) * 4);
-        if (h4 && h6)
-          gemv_prologue<true, true>(a, xb, red, warp, lane);
-        else if (h4)
-          gemv_prologue<true, false>(a, xb, red, warp, lane);
-        else
-          gemv_prologue<false, true>(a, xb, red, warp, lane);
         const uint64_t lo = a.total_cost * blockIdx.x / gridDim.x;
         const uint64_t hi = a.total_cost * (blockIdx.x + 1) / gridDim.x;
-        ok = gemv_consume(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+        if (h4 && h6) {
+          gemv_prologue<true, true>(a, xb, red, warp, lane);
+          ok = gemv_consume<true, true>(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+        } else if (h4) {
+          gemv_prologue<true, false>(a, xb, red, warp, lane);
+          ok = gemv_consume<true, false>(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+        } else {
+          gemv_prologue<false, true>(a, xb, red, warp, lane);
+          ok = gemv_consume<false, true>(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+        }
       } else if (d.kind == PH_ATTN) {
         const AttnArgs& aa = P.attn[d.idx];
         const uint32_t n_items = P.n_kv * P.attn_nsplit;

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   }
   gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true);
   uint32_t gtask = 0;
-  gemv_consume(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
+  gemv_consume<HAS4, HAS6>(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
 }
 
 // --------------------------- generic fallback ---------------------------------
@@ -180,8 +180,10 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
       const uint32_t nbc = (nb + 1) / 2;
       while (rg * 2 <= 16 && rg * 2 * nbc <= 16) rg *= 2;
     }
+    // Rows beyond 40 KB per task pair: one row per lane group (Q6_K has a
+    // single-row body; for Q4_K the second row pointer repeats the first).
     uint32_t rl = g.dual ? 1 : 2;
-    if (rl == 2 && (uint64_t)rg * 2 * g.row_stride > 40960) rl = 1;  // huge rows
+    if (rl == 2 && (uint64_t)rg * 2 * g.row_stride > 40960) rl = 1;
     if (mt.epi == EPI_ROPE && rl != 2) return -2;
     g.rg = (uint8_t)rg;
     g.rl = (uint8_t)rl;

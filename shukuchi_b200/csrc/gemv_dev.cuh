@@ -47,11 +47,12 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
 }
 
 // x limbs live in shared memory as int4 vectors {l0 word, l1 word, l2 word, 0}
-// (4 elements each).  Vector v is stored at v + v/64: one pad vector after
-// every 256-element block.  A block's 64 vectors are then contiguous (lanes use
-// constant offsets), and lanes reading the same offset in consecutive blocks
-// land in distinct bank groups.
-__device__ __forceinline__ uint32_t xpad(uint32_t v) { return v + (v >> 6); }
+// (4 elements each).  A 256-element block b takes 65 slots from 65b: its first
+// 32 vectors, one pad slot, then the last 32 (vector w of the block at
+// 65b + w + (w >= 32)).  Lanes reading the same offset of consecutive blocks
+// (Q4_K: a lane per block) and lanes reading half n of every second block
+// (Q6_K: 65*2s + 33n) then fall in distinct 16-byte bank groups.
+__device__ __forceinline__ uint32_t xpad(uint32_t v) { return v + (v >> 6) + ((v >> 5) & 1u); }
 
 // Limbs 0 and 1 of x are unsigned bytes, limb 2 is a signed byte (see the
 // prologue); quants are unsigned and below 64, so limb 2 may use the signed form.
@@ -113,8 +114,9 @@ __device__ __forceinline__ void q4k_block2(const uint8_t* __restrict__ r0, const
       for (int r = 0; r < 2; ++r) w[r] = *reinterpret_cast<const uint4*>(rp[r] + 16 + 32 * j + 16 * half);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int4 xl = xblk[16 * j + 4 * half + i];
-        const int4 xh = xblk[16 * j + 8 + 4 * half + i];
+        const int4* xj = xblk + 16 * j + (j >> 1);  // groups 2, 3 follow the pad slot
+        const int4 xl = xj[4 * half + i];
+        const int4 xh = xj[8 + 4 * half + i];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const uint32_t q = i == 0 ? w[r].x : i == 1 ? w[r].y : i == 2 ? w[r].z : w[r].w;
@@ -174,36 +176,40 @@ __device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&o)[NW]) 
 // each 16-element scale group's three limb sums start at -32 * (sum of x
 // limbs), which applies the -32 offset.  The two 16-element halves `is` of the
 // 32-element groups run in a rolled loop, each loading only its own words.
-template <int P>
-__device__ __forceinline__ void q6k_half2(const uint8_t* __restrict__ b0, const uint8_t* __restrict__ b1,
-                                          int n, const int4* __restrict__ xh,
-                                          const int4* __restrict__ xi, float xb, float& acc0,
-                                          float& acc1) {
+// NR = 2 rows (b0, b1) or NR = 1 (b0 only; rows of very long K, so that a
+// task and a pipeline stage stay small).
+template <int P, int NR>
+__device__ __forceinline__ void q6k_half(const uint8_t* __restrict__ b0, const uint8_t* __restrict__ b1,
+                                         int n, const int4* __restrict__ xh,
+                                         const int4* __restrict__ xi, float xb, float& acc0,
+                                         float& acc1) {
   const uint32_t MK = 0x0F0F0F0Fu;
   const uint8_t* bp[2] = {b0, b1};
-  uint32_t SC[2][2];
-  float dd[2];
+  uint32_t SC[NR][2];
+  float dd[NR];
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < NR; ++r) {
     load_words<P, 2>(bp[r] + 192 + 8 * n, SC[r]);
     dd[r] = ref_half(*reinterpret_cast<const uint16_t*>(bp[r] + 208)) * xb;
   }
-  int T[2][3] = {{0, 0, 0}, {0, 0, 0}};
+  int T[NR][3];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) T[r][0] = T[r][1] = T[r][2] = 0;
 #pragma unroll 1
   for (int is = 0; is < 2; ++is) {
-    uint32_t A[2][4], B[2][4], H[2][4];
+    uint32_t A[NR][4], B[NR][4], H[NR][4];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < NR; ++r) {
       load_words<P, 4>(bp[r] + 64 * n + 16 * is, A[r]);
       load_words<P, 4>(bp[r] + 64 * n + 32 + 16 * is, B[r]);
       load_words<P, 4>(bp[r] + 128 + 32 * n + 16 * is, H[r]);
     }
-    int S[2][4][3];
+    int S[NR][4][3];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int4 init = xi[2 * g + is];  // -32 * limb sums of this 16-group
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < NR; ++r) {
         S[r][g][0] = init.x;
         S[r][g][1] = init.y;
         S[r][g][2] = init.z;
@@ -215,7 +221,7 @@ __device__ __forceinline__ void q6k_half2(const uint8_t* __restrict__ b0, const 
 #pragma unroll
       for (int g = 0; g < 4; ++g) xv[g] = xh[8 * g + 4 * is + i];
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < NR; ++r) {
         const uint32_t h = H[r][i];
         const uint32_t hm = h & 0x33333333u, hn = h & 0xCCCCCCCCu;
         const uint32_t Q[4] = {lop_sel(A[r][i], hm << 4, MK), lop_sel(B[r][i], hn << 2, MK),
@@ -229,7 +235,7 @@ __device__ __forceinline__ void q6k_half2(const uint8_t* __restrict__ b0, const 
       }
     }
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
+    for (int r = 0; r < NR; ++r)
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const uint32_t si = (uint32_t)is + 2u * g;  // scale index within this half
@@ -240,7 +246,7 @@ __device__ __forceinline__ void q6k_half2(const uint8_t* __restrict__ b0, const 
       }
   }
   acc0 = fmaf(dd[0], limbs_to_float(T[0][0], T[0][1], T[0][2]), acc0);
-  acc1 = fmaf(dd[1], limbs_to_float(T[1][0], T[1][1], T[1][2]), acc1);
+  if (NR == 2) acc1 = fmaf(dd[NR - 1], limbs_to_float(T[NR - 1][0], T[NR - 1][1], T[NR - 1][2]), acc1);
 }
 
 // ------------------------------ chunk walk ----------------------------------
@@ -305,6 +311,7 @@ struct XView {
 //  Q4_K: 32/rg lanes per group, a lane takes blocks s, s + 32/rg, ...
 //  Q6_K: 16/rg block slots per group, two lanes (halves n) per slot; blocks of
 //        even then odd index (their word alignments differ).
+template <bool HAS4, bool HAS6>
 __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, const uint8_t* rows,
                                          uint32_t row0, int rows_valid, uint32_t dual_off,
                                          const XView& x, int lane) {
@@ -319,17 +326,23 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
   if (grp * rl < rows_valid) {
     const uint8_t* r0 = rows + (size_t)(grp * rl) * g.row_stride;
     const uint8_t* r1 = g.dual ? r0 + dual_off : ((rl == 2 && grp * 2 + 1 < rows_valid) ? r0 + g.row_stride : r0);
-    if (q4) {
+    if (HAS4 && (!HAS6 || q4)) {
       for (uint32_t b = s; b < g.nb; b += spr)
         q4k_block2(r0 + (size_t)b * Q4K_BYTES, r1 + (size_t)b * Q4K_BYTES, x.xq + 65 * b, x.xbs[b],
                    x.xs32 + 8 * b, o0, o1);
-    } else {
-      for (uint32_t b = 2 * s; b < g.nb; b += 2 * spr)
-        q6k_half2<0>(r0 + (size_t)b * Q6K_BYTES, r1 + (size_t)b * Q6K_BYTES, n, x.xq + 65 * b + 32 * n,
-                     x.xi16 + 16 * b + 8 * n, x.xbs[b], o0, o1);
-      for (uint32_t b = 2 * s + 1; b < g.nb; b += 2 * spr)
-        q6k_half2<1>(r0 + (size_t)b * Q6K_BYTES, r1 + (size_t)b * Q6K_BYTES, n, x.xq + 65 * b + 32 * n,
-                     x.xi16 + 16 * b + 8 * n, x.xbs[b], o0, o1);
+    } else if (HAS6) {
+#define SHK_Q6(P, NR)                                                                          \
+  for (uint32_t b = 2 * s + P; b < g.nb; b += 2 * spr)                                         \
+    q6k_half<P, NR>(r0 + (size_t)b * Q6K_BYTES, r1 + (size_t)b * Q6K_BYTES, n,                 \
+                    x.xq + 65 * b + 33 * n, x.xi16 + 16 * b + 8 * n, x.xbs[b], o0, o1)
+      if (rl == 1 && !g.dual) {  // single row
+        SHK_Q6(0, 1);
+        SHK_Q6(1, 1);
+      } else {
+        SHK_Q6(0, 2);
+        SHK_Q6(1, 2);
+      }
+#undef SHK_Q6
     }
   }
   for (int o = 16 >> lg_rg; o > 0; o >>= 1) {
@@ -355,8 +368,9 @@ __device__ __forceinline__ bool wait_gen(const volatile uint32_t* gen, uint32_t 
                                          int* err) {
   if (gen[st] == it) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (gen[st] != it) {
-    if (globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
+  for (uint32_t n = 1; gen[st] != it; ++n) {
+    __nanosleep(32);
+    if ((n & 31) == 0 && globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
       set_error(err, DERR_TIMEOUT_FULL);
       return false;
     }
@@ -642,6 +656,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
 // Consumers: walk this CTA's chunks of plan `a` in the producer's order; a
 // warp waits only for chunks that hold one of its tasks, and the last warp to
 // finish a chunk's tasks releases the stage.  False if a bounded wait ran out.
+template <bool HAS4, bool HAS6>
 __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const Ring& R, RingPos& p,
                                              uint32_t& gtask, uint64_t lo, uint64_t hi,
                                              const XView& xv, int warp, int lane) {
@@ -666,7 +681,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const Ring& R, R
         for (; t < ntasks; t += GEMV_WARPS, ++mine) {
           const int rv = (int)min(ur, nrows - (t << lg_ur));
           const uint8_t* rows = buf + (size_t)(t << lg_ur) * g.row_stride;
-          run_task(a, g, rows, r0 + (t << lg_ur), rv, dual_off, xv, lane);
+          run_task<HAS4, HAS6>(a, g, rows, r0 + (t << lg_ur), rv, dual_off, xv, lane);
         }
         __syncwarp();
         if (lane == 0) {

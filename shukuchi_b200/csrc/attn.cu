@@ -105,6 +105,93 @@ __global__ void kv_read_blocks_kernel(KvLayout kv, uint32_t layer, uint32_t star
   }
 }
 
+constexpr int ATTC_WARPS = 8;
+
+// One cluster per KV head (see attn_cluster in attn_dev.cuh).
+template <int HD, int G>
+__global__ void __launch_bounds__(32 * ATTC_WARPS) attn_cluster_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(16) float smc[];
+  pdl_trigger();
+  attn_cluster<HD, G, ATTC_WARPS>(a, smc);
+}
+
+// How many clusters of 16, 8 and 4 CTAs of this kernel can be resident at
+// once (0 where the size is refused).  Queried once per instantiation.
+template <int HD, int G>
+const int* cluster_capacity() {
+  static int cap[3] = {-1, -1, -1};
+  if (cap[0] >= 0) return cap;
+  auto k = attn_cluster_kernel<HD, G>;
+  const size_t smem = AttnCSmem<HD, G, ATTC_WARPS>::BYTES;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const bool np = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  const int sizes[3] = {16, 8, 4};
+  for (int i = 0; i < 3; ++i) {
+    cap[i] = 0;
+    if (sizes[i] > 8 && !np) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sizes[i], 1);
+    cfg.blockDim = dim3(32 * ATTC_WARPS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = sizes[i];
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess) cap[i] = n;
+  }
+  cudaGetLastError();  // a refused query leaves no sticky state
+  return cap;
+}
+
+// The largest cluster with which all n_kv clusters (one per KV head) are
+// resident together: a second wave would double the latency.
+template <int HD, int G>
+int cluster_ctas(uint32_t n_kv) {
+  const int* cap = cluster_capacity<HD, G>();
+  if (cap[0] >= (int)n_kv) return 16;
+  if (cap[1] >= (int)n_kv) return 8;
+  return 4;
+}
+
+template <int HD, int G>
+cudaError_t attn_cluster_launch(const AttnArgs& a, cudaStream_t st) {
+  const int cs = cluster_ctas<HD, G>(a.kv.n_kv);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs, a.kv.n_kv);
+  cfg.blockDim = dim3(32 * ATTC_WARPS);
+  cfg.dynamicSmemBytes = AttnCSmem<HD, G, ATTC_WARPS>::BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cs;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  int n = 1;
+  if (pdl_enabled()) {
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    n = 2;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD, G>, a);
+}
+
+template <int HD>
+cudaError_t attn_cluster_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
+  switch (G) {
+    case 1: return attn_cluster_launch<HD, 1>(a, st);
+    case 2: return attn_cluster_launch<HD, 2>(a, st);
+    case 4: return attn_cluster_launch<HD, 4>(a, st);
+    case 8: return attn_cluster_launch<HD, 8>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <int HD>
 cudaError_t attn_launch_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
   dim3 grid(a.kv.n_kv, a.max_splits);
@@ -121,6 +208,24 @@ cudaError_t attn_launch_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
 }  // namespace
 
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream) {
+  if (a.kv.n_kv == 0 || a.n_heads % a.kv.n_kv) return cudaErrorInvalidValue;
+  if (a.min_per_split == 0) return cudaErrorInvalidValue;
+  const uint32_t G = a.n_heads / a.kv.n_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return cudaErrorInvalidValue;
+  if (a.kv.hd != 64 && a.kv.hd != 128) return cudaErrorInvalidValue;
+  AttnArgs b = a;
+  if (a.k_new && ((reinterpret_cast<uintptr_t>(a.k_new) & 15) != 0)) {
+    // the in-kernel new row reads 16-byte vectors: append first, then attend
+    const cudaError_t e = kv_append_launch(a.kv, a.layer, a.pos, a.k_new, a.v_new, a.err, stream);
+    if (e != cudaSuccess) return e;
+    b.k_new = b.v_new = nullptr;
+  }
+  return a.kv.hd == 64 ? attn_cluster_hd<64>(b, G, stream) : attn_cluster_hd<128>(b, G, stream);
+}
+
+// The split-K kernel with partials in global memory (one item per CTA); kept
+// for callers that size `part` themselves.
+cudaError_t attn_decode_split_launch(const AttnArgs& a, cudaStream_t stream) {
   if (a.kv.n_kv == 0 || a.n_heads % a.kv.n_kv) return cudaErrorInvalidValue;
   if (a.max_splits == 0 || a.max_splits > (uint32_t)ATT_MAX_SPLITS) return cudaErrorInvalidValue;
   const uint32_t G = a.n_heads / a.kv.n_kv;

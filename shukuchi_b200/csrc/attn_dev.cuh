@@ -331,5 +331,313 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
   att_sync(NT);  // shared memory is reused by the caller's next item
 }
 
+
+// ------------------------- cluster attention --------------------------------
+// One thread-block cluster per KV head; CTA rank r of the cluster is split r of
+// the positions [0, pos].  Splits merge through distributed shared memory
+// (each CTA publishes its (max, sum, output) in its own shared memory; after a
+// cluster barrier every CTA combines a slice of the head dimension reading all
+// peers), so no partials go through global memory and no ticket is needed.
+// The new token's K/V row (position pos) is quantised in registers and used
+// directly -- the same bytes the append stores -- so the cache loads of the
+// older positions can be issued before the previous kernel's outputs (q, new
+// K/V) are waited for.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t n;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+  return n;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// Shared-memory address of `p` in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Q8_0 of one 32-element block read by one thread (q8_quantize_vec,
+// engine/src/kv_cache.c:28-55): same maximum, IEEE division and rounding as the
+// append kernels, so the bytes are identical.  Writes the quants as four
+// packed words per 16 bytes to q (4 x uint4) and returns the scale.  Not
+// inlined: it runs for one position per launch, and its 32 divisions would
+// otherwise enlarge the hot loop's code.
+static __device__ __noinline__ float q8_block_new(const float* __restrict__ src, uint4* __restrict__ q) {
+  float v[32];
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float4 f4 = __ldcg(s4 + u);
+    v[4 * u] = f4.x; v[4 * u + 1] = f4.y; v[4 * u + 2] = f4.z; v[4 * u + 3] = f4.w;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  float scale = amax / 127.0f;
+  if (scale == 0.0f) scale = 1.0f;
+  uint32_t w[8];
+#pragma unroll 4
+  for (int u = 0; u < 8; ++u) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int t = __float2int_rn(v[4 * u + e] / scale);
+      t = t > 127 ? 127 : (t < -127 ? -127 : t);
+      word |= ((uint32_t)t & 0xFFu) << (8 * e);
+    }
+    w[u] = word;
+  }
+  q[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  q[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  return scale;
+}
+
+template <int HD, int G, int NW>
+struct AttnCSmem {  // offsets in floats
+  static constexpr int LPP = HD / 32;
+  static constexpr int QROW = 36;
+  static constexpr int Q = 0;
+  static constexpr int WM = Q + G * LPP * QROW;
+  static constexpr int WL = WM + NW * G;
+  static constexpr int WACC = WL + NW * G;
+  static constexpr int CM = WACC + NW * G * HD;  // this CTA's max per query head
+  static constexpr int CL = CM + G;              // its sum of exponentials
+  static constexpr int CO = CL + G;              // its unnormalised output [G][HD]
+  static constexpr int FLOATS = CO + G * HD;
+  static constexpr size_t BYTES = (size_t)FLOATS * 4;
+};
+
+// Cluster attention for KV head blockIdx.y by NW warps; see above.
+template <int HD, int G, int NW>
+__device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
+  using Tile = AttnTile<HD>;
+  using SM = AttnCSmem<HD, G, NW>;
+  constexpr int LPP = Tile::LPP, PPI = Tile::PPI, EPL = Tile::EPL;
+  constexpr int NT = 32 * NW;
+  constexpr int LPB = 32 / EPL;  // lanes sharing one V block in the PV layout
+  const uint32_t KV = a.kv.n_kv, kvh = blockIdx.y;
+  const uint32_t rank = cluster_rank(), CS = cluster_size();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The position and the cache rows before it were written by earlier graph
+  // launches or stream work, never by the kernel this one may overlap.
+  const uint32_t pos = __ldcg(a.pos);
+  if (pos >= a.kv.max_seq) {
+    if (tid == 0 && rank == 0) set_error(a.err, DERR_BAD_POS);
+    return;  // the whole cluster leaves: no barrier is left waiting
+  }
+  const uint32_t seq = pos + 1;
+  uint32_t n0 = (seq + a.min_per_split - 1) / a.min_per_split;
+  n0 = n0 < 1 ? 1 : (n0 > CS ? CS : n0);
+  const uint32_t per = (((seq + n0 - 1) / n0) + PPI - 1) / PPI * PPI;
+  const uint32_t active = (seq + per - 1) / per;
+  const uint32_t p0 = rank * per, p1 = min(seq, p0 + per);
+  const bool mine = rank < active;
+  const bool own_new = a.k_new != nullptr && mine && pos >= p0 && pos < p1;
+
+  float (*qs)[LPP][SM::QROW] = reinterpret_cast<float (*)[LPP][SM::QROW]>(sm + SM::Q);
+  float (*wm)[G] = reinterpret_cast<float (*)[G]>(sm + SM::WM);
+  float (*wl)[G] = reinterpret_cast<float (*)[G]>(sm + SM::WL);
+  float (*wacc)[G][HD] = reinterpret_cast<float (*)[G][HD]>(sm + SM::WACC);
+  float* cm = sm + SM::CM;
+  float* cl = sm + SM::CL;
+  float (*co)[HD] = reinterpret_cast<float (*)[HD]>(sm + SM::CO);
+
+  int8_t* reg = const_cast<int8_t*>(a.kv.region(a.layer, kvh));
+  const int8_t* Kq = reg + a.kv.kq_off;
+  const float* Ks = reinterpret_cast<const float*>(reg + a.kv.ks_off);
+  const int8_t* Vq = reg + a.kv.vq_off;
+  const float* Vs = reinterpret_cast<const float*>(reg + a.kv.vs_off);
+  const int b = lane % LPP;
+  const uint32_t tl = lane / LPP;
+
+  constexpr uint32_t STEP = PPI * NW;
+  uint32_t T = p0 + PPI * warp;
+  Tile cur;
+  if (mine && T < p1) cur.load(Kq, Ks, Vq, Vs, T, p1, lane);  // in flight across the wait
+
+  pdl_wait();  // q and the new K/V row come from the previous kernel
+  for (int i = tid; i < G * HD; i += NT) {
+    const int g = i / HD, d = i % HD;
+    qs[g][d / 32][d % 32] = __ldcg(a.q + (kvh + KV * g) * HD + d);  // query head kvh + KV*g
+  }
+  // The new V row in the PV layout (EPL columns per lane, LPB lanes per block);
+  // warp 0 appends it to the cache.
+  uint32_t vw_new = 0;
+  float vs_new = 1.f;
+  if (own_new) {
+    float vv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) vv[e] = __ldcg(a.v_new + kvh * HD + lane * EPL + e);
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) amax = fmaxf(amax, fabsf(vv[e]));
+#pragma unroll
+    for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    vs_new = amax / 127.0f;
+    if (vs_new == 0.0f) vs_new = 1.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      int t = __float2int_rn(vv[e] / vs_new);
+      t = t > 127 ? 127 : (t < -127 ? -127 : t);
+      vw_new |= ((uint32_t)t & 0xFFu) << (8 * e);
+    }
+    if (warp == 0) {
+      int8_t* vq = reg + a.kv.vq_off + (size_t)pos * HD + lane * EPL;
+      if (EPL == 4)
+        *reinterpret_cast<uint32_t*>(vq) = vw_new;
+      else
+        *reinterpret_cast<uint16_t*>(vq) = (uint16_t)vw_new;
+      if (lane % LPB == 0)
+        reinterpret_cast<float*>(reg + a.kv.vs_off)[(size_t)pos * (HD / 32) + lane / LPB] = vs_new;
+    }
+  }
+  att_sync(NT);
+
+  float m[G], l[G], acc[G][EPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[g][e] = 0.f;
+  }
+  for (; mine && T < p1; T += STEP) {
+    Tile nxt;
+    if (T + STEP < p1) nxt.load(Kq, Ks, Vq, Vs, T + STEP, p1, lane);
+    const uint32_t nt = min((uint32_t)PPI, p1 - T);
+    const bool ok = tl < nt;
+    const uint32_t t = T + (ok ? tl : 0);
+    // ---- scores ----
+    float kf[32];
+    float ksc = cur.ks;
+    uint4 k0 = cur.k0, k1 = cur.k1;
+    if (own_new && t == pos) {  // the new row, quantised here; this lane appends its block
+      uint4 qn[2];
+      ksc = q8_block_new(a.k_new + kvh * HD + 32 * b, qn);
+      k0 = qn[0];
+      k1 = qn[1];
+      if (ok && warp == (int)((pos - p0) / PPI) % NW) {
+        uint4* dst = reinterpret_cast<uint4*>(reg + a.kv.kq_off + (size_t)pos * HD + 32 * b);
+        dst[0] = k0;
+        dst[1] = k1;
+        reinterpret_cast<float*>(reg + a.kv.ks_off)[(size_t)pos * (HD / 32) + b] = ksc;
+      }
+    }
+    s8x4_to_f32(k0.x, kf);
+    s8x4_to_f32(k0.y, kf + 4);
+    s8x4_to_f32(k0.z, kf + 8);
+    s8x4_to_f32(k0.w, kf + 12);
+    s8x4_to_f32(k1.x, kf + 16);
+    s8x4_to_f32(k1.y, kf + 20);
+    s8x4_to_f32(k1.z, kf + 24);
+    s8x4_to_f32(k1.w, kf + 28);
+    float p[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4* qv = reinterpret_cast<const float4*>(&qs[g][b][0]);
+      float sb = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 q4 = qv[u];
+        sb = fmaf(q4.x, kf[4 * u], sb);
+        sb = fmaf(q4.y, kf[4 * u + 1], sb);
+        sb = fmaf(q4.z, kf[4 * u + 2], sb);
+        sb = fmaf(q4.w, kf[4 * u + 3], sb);
+      }
+      float sc = sb * ksc;
+#pragma unroll
+      for (int o = 1; o < LPP; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+      p[g] = sc;
+    }
+    // ---- online softmax (per warp) ----
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float sg = ok ? p[g] * a.scale : -INFINITY;
+      const float mn = fmaxf(m[g], warp_max(sg));  // position T is valid: finite
+      const float pg = ok ? expf(sg - mn) : 0.f;
+      p[g] = pg;
+      const float corr = (m[g] == -INFINITY) ? 0.f : expf(m[g] - mn);
+      l[g] = fmaf(l[g], corr, warp_sum(b == 0 ? pg : 0.f));
+      m[g] = mn;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[g][e] *= corr;
+    }
+    // ---- P.V ----
+#pragma unroll
+    for (int j = 0; j < PPI; ++j) {
+      const uint32_t tj = T + ((uint32_t)j < nt ? j : 0);
+      const bool nw_ = own_new && tj == pos;
+      float vf[4];
+      s8x4_to_f32(nw_ ? vw_new : cur.vw[j], vf);
+      const float vsj = nw_ ? vs_new : cur.vs[j];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pj = __shfl_sync(0xffffffffu, p[g], j * LPP) * vsj;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(pj, vf[e], acc[g][e]);
+      }
+    }
+    cur = nxt;
+  }
+  // ---- merge the warps into this CTA's (max, sum, output) ----
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+  }
+  att_sync(NT);
+  for (int i = tid; i < G * HD; i += NT) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
+      L = fmaf(f, wl[w][g], L);
+      O = fmaf(f, wacc[w][g][d], O);
+    }
+    co[g][d] = O;
+    if (d == 0) {
+      cm[g] = M;
+      cl[g] = L;
+    }
+  }
+  // ---- merge the splits across the cluster ----
+  cluster_barrier();  // every CTA's (cm, cl, co) is published
+  for (uint32_t i = rank * NT + tid; i < (uint32_t)(G * HD); i += CS * NT) {
+    const uint32_t g = i / HD, d = i % HD;
+    float M = -INFINITY;
+    for (uint32_t r = 0; r < active; ++r) M = fmaxf(M, dsmem_ld(dsmem_addr(&cm[g], r)));
+    float L = 0.f, O = 0.f;
+    for (uint32_t r = 0; r < active; ++r) {
+      const float mr = dsmem_ld(dsmem_addr(&cm[g], r));
+      const float w = (mr == -INFINITY) ? 0.f : expf(mr - M);
+      L = fmaf(w, dsmem_ld(dsmem_addr(&cl[g], r)), L);
+      O = fmaf(w, dsmem_ld(dsmem_addr(&co[g][d], r)), O);
+    }
+    a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O * (1.0f / L);
+  }
+  cluster_barrier();  // peers keep their shared memory until every read is done
+}
+
 }  // namespace adev
 }  // namespace shk

@@ -15,7 +15,7 @@ enum GemvEpi : uint8_t {
 };
 
 constexpr int GEMV_MAX_SEGS = 4;
-constexpr int GEMV_WARPS = 12;  // consumer warps; one more warp issues the bulk copies
+constexpr int GEMV_WARPS = 15;  // consumer warps; one more warp issues the bulk copies
 constexpr int GEMV_THREADS = 32 * (GEMV_WARPS + 1);
 constexpr int GEMV_MAX_STAGES = 16;
 

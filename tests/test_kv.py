@@ -93,7 +93,8 @@ def test_append_bit_exact(oracle, ctx, KV, hd):
 
 @pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64)])
 @pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049])
-def test_attend(oracle, ctx, H, KV, hd, seq):
+@pytest.mark.parametrize("new_row", ["fused", "pre_appended"])
+def test_attend(oracle, ctx, H, KV, hd, seq, new_row):
     rng = np.random.default_rng(H * 131 + seq)
     k, v = kv_inputs(rng, seq, KV, hd)
     k[seq - 1, 5] = 3.0
@@ -101,16 +102,26 @@ def test_attend(oracle, ctx, H, KV, hd, seq):
     kv = sc.KvCache(ctx, 1, KV, hd, seq + 8)
     try:
         kd, vd, qd = to_dev(k), to_dev(v), to_dev(q)
-        for t in range(seq - 1):
-            kv.append(0, t, kd[t].data_ptr(), vd[t].data_ptr())
+        n_pre = seq - 1 if new_row == "fused" else seq
+        if n_pre:
+            kv.append_range(0, 0, n_pre, kd.data_ptr(), vd.data_ptr())
         out = torch.zeros(H * hd, device="cuda")
         scale = np.float32(1.0 / np.sqrt(hd))
-        # the last position is appended by the fused attention kernel itself
-        kv.attend(0, qd.data_ptr(), out.data_ptr(), H, seq, float(scale),
-                  k_new=kd[seq - 1].data_ptr(), v_new=vd[seq - 1].data_ptr())
+        if new_row == "fused":
+            # the last position is quantised and appended by the attention kernel itself
+            kv.attend(0, qd.data_ptr(), out.data_ptr(), H, seq, float(scale),
+                      k_new=kd[seq - 1].data_ptr(), v_new=vd[seq - 1].data_ptr())
+        else:
+            kv.attend(0, qd.data_ptr(), out.data_ptr(), H, seq, float(scale))
+        nb = KV * hd // 32 * 36
+        kb = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+        vb = torch.zeros_like(kb)
+        kv.read_blocks(0, seq - 1, seq, kb.data_ptr(), vb.data_ptr())
         torch.cuda.synchronize()
         ctx.check()
         got = out.cpu().numpy()
+        assert np.array_equal(kb.cpu().numpy(), oracle.q8_quantize(k[seq - 1]))
+        assert np.array_equal(vb.cpu().numpy(), oracle.q8_quantize(v[seq - 1]))
     finally:
         kv.close()
     okv = oracle.kv_create(1, KV, hd, seq + 8)

@@ -204,6 +204,15 @@ def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
     return 1.0 / per_token, kind, sample
 
 
+def workload_config(args, ws):
+    from shukuchi_b200 import synth
+    name = synth.SHAPES[args.shape].name
+    return {"workload": f"{name} Q4_K_M decode bs1 after a {args.prompt}-token prompt, Q8_0 KV",
+            "model": name, "global_batch": ws, "seq_len": args.prompt,
+            "parallelism": f"replicas{ws}" if ws > 1 else "single",
+            "l2": "no flush: 4.9 GB of weights per step exceed the 126 MB L2"}
+
+
 def run_reference(args, ws, rank):
     if rank != 0:
         return
@@ -212,8 +221,7 @@ def run_reference(args, ws, rank):
         "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.shape} Q4_K_M decode bs1 after a {args.prompt}-token prompt",
-                   "model": args.shape, "global_batch": 1, "seq_len": args.prompt, "parallelism": "none"},
+        "config": workload_config(args, 1),
         "impl": "reference",
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -350,11 +358,7 @@ def run_ours(args, ws, rank, local):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{shape.name} Q4_K_M decode bs1 after a {args.prompt}-token prompt, "
-                               f"Q8_0 KV, weights resident in HBM",
-                   "model": shape.name, "global_batch": ws, "seq_len": args.prompt,
-                   "parallelism": f"replicas{ws}" if ws > 1 else "single",
-                   "l2": "no flush: 4.9 GB of weights per step exceed the 126 MB L2"},
+        "config": workload_config(args, ws),
         "clocks": clk.summary(),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
         "gpu_launches": launches_per_step * args.steps,

@@ -209,7 +209,9 @@ def parts(args, ctx) -> None:
                     for _ in range(reps):
                         for layer in range(n):
                             m.launch_part(layer, part, stream=s.cuda_stream)
+            torch.cuda.nvtx.range_push(name)  # ncu --nvtx --nvtx-include "<part>/" picks one part
             ms = _time_graph(g, s, args.reps)
+            torch.cuda.nvtx.range_pop()
             ctx.check()
             us = ms * 1000.0 / (n * reps)
             gbs = wb[0] / (us * 1e-6) / 1e9

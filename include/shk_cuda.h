@@ -227,6 +227,10 @@ int shk_cuda_layer_commit(shk_ctx *ctx, uint32_t slot);
 int shk_cuda_layer_ready(shk_ctx *ctx, uint32_t slot, int wait);
 /* Make `stream` wait (on the device) for the slot's copies. */
 int shk_cuda_layer_wait(shk_ctx *ctx, uint32_t slot, void *stream);
+/* Device-slot reuse (prefetcher_release, engine/src/prefetch.c:262-280): the
+ * next staging into `slot` first waits, on the copy stream, for the work
+ * queued on `stream` so far -- the kernels that read the slot's old layer. */
+int shk_cuda_layer_release(shk_ctx *ctx, uint32_t slot, void *stream);
 
 /* ---- argmax without any device allocation.  No counterpart in the reference:
  *      it exists for callers that cannot call cudaMalloc (a sampler inside a

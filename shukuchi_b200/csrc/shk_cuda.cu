@@ -54,6 +54,8 @@ struct shk_ctx {
   // staging
   std::mutex stage_mu;
   std::unordered_map<uint32_t, cudaEvent_t> slot_ev;
+  std::unordered_map<uint32_t, cudaEvent_t> rel_ev;    // shk_cuda_layer_release
+  std::unordered_map<uint32_t, bool> rel_pending;
   // counters (shk_cuda_report)
   uint64_t n_matvec = 0, n_matvec_host = 0, n_fwd = 0, n_steps = 0, n_staged = 0, bytes_staged = 0;
 };
@@ -241,6 +243,7 @@ void shk_cuda_shutdown(shk_ctx* c) {
   if (c->compute) cudaStreamSynchronize(c->compute);
   if (c->copy) cudaStreamSynchronize(c->copy);
   for (auto& kv : c->slot_ev) cudaEventDestroy(kv.second);
+  for (auto& kv : c->rel_ev) cudaEventDestroy(kv.second);
   cudaFree(c->d_err);
   cudaFreeHost(c->h_err);
   cudaFree(c->d_u32);
@@ -1026,9 +1029,38 @@ static cudaEvent_t slot_event(shk_ctx* c, uint32_t slot) {
   return e;
 }
 
+// Before the first copy into a released slot, the copy stream waits for the
+// work the release recorded (kernels still reading the slot's old contents).
+static int stage_prepare(shk_ctx* c, uint32_t slot) {
+  cudaSetDevice(c->device);  // may run on the loader thread
+  std::lock_guard<std::mutex> g(c->stage_mu);
+  auto it = c->rel_pending.find(slot);
+  if (it != c->rel_pending.end() && it->second) {
+    it->second = false;
+    CK(cudaStreamWaitEvent(c->copy, c->rel_ev[slot], 0));
+  }
+  return SHK_OK;
+}
+
+int shk_cuda_layer_release(shk_ctx* c, uint32_t slot, void* s) {
+  if (!c) return SHK_EINVAL;
+  cudaSetDevice(c->device);
+  cudaStream_t st = pick(c, s);
+  std::lock_guard<std::mutex> g(c->stage_mu);
+  cudaEvent_t& e = c->rel_ev[slot];
+  if (!e && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+    e = nullptr;
+    return SHK_ECUDA;
+  }
+  CK(cudaEventRecord(e, st));
+  c->rel_pending[slot] = true;
+  return SHK_OK;
+}
+
 int shk_cuda_layer_stage(shk_ctx* c, uint32_t slot, void* dst, const void* src, size_t bytes) {
   if (!c || !dst || !src) return SHK_EINVAL;
-  (void)slot;
+  const int rc = stage_prepare(c, slot);
+  if (rc) return rc;
   CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->copy));
   {
     std::lock_guard<std::mutex> g(c->stage_mu);
@@ -1041,7 +1073,8 @@ int shk_cuda_layer_stage(shk_ctx* c, uint32_t slot, void* dst, const void* src, 
 int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_row,
                               const void* src, size_t src_row, size_t rows) {
   if (!c || !dst || !src || dst_row < src_row) return SHK_EINVAL;
-  (void)slot;
+  const int rc = stage_prepare(c, slot);
+  if (rc) return rc;
   CK(cudaMemcpy2DAsync(dst, dst_row, src, src_row, src_row, rows, cudaMemcpyHostToDevice, c->copy));
   {
     std::lock_guard<std::mutex> g(c->stage_mu);
@@ -1053,6 +1086,7 @@ int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_r
 
 int shk_cuda_layer_commit(shk_ctx* c, uint32_t slot) {
   if (!c) return SHK_EINVAL;
+  cudaSetDevice(c->device);
   cudaEvent_t e = slot_event(c, slot);
   if (!e) return SHK_ECUDA;
   CK(cudaEventRecord(e, c->copy));
@@ -1061,6 +1095,7 @@ int shk_cuda_layer_commit(shk_ctx* c, uint32_t slot) {
 
 int shk_cuda_layer_ready(shk_ctx* c, uint32_t slot, int wait) {
   if (!c) return SHK_EINVAL;
+  cudaSetDevice(c->device);
   cudaEvent_t e = slot_event(c, slot);
   if (!e) return SHK_ECUDA;
   if (wait) {

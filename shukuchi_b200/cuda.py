@@ -110,6 +110,7 @@ _SIGS = {
     "shk_cuda_layer_commit": (I, [P, U32]),
     "shk_cuda_layer_ready": (I, [P, U32, I]),
     "shk_cuda_layer_wait": (I, [P, U32, P]),
+    "shk_cuda_layer_release": (I, [P, U32, P]),
 }
 
 _lib = None

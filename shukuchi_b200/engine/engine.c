@@ -1,0 +1,605 @@
+/* engine.c -- GGUF llama model, layer-streaming loader and token loop over
+ * libshk_cuda (see engine.h).
+ *
+ * Reference behaviour kept (engine/src/engine.c:306-501): the prompt is fed
+ * token by token; each generated token is the first-index argmax of the
+ * logits of the previous position (no final norm, rope theta 10000), is
+ * printed as "<id>text", and is itself run through all layers.  An empty
+ * prompt decodes from token 1.  Prompt text is tokenised by greedy longest
+ * match over the vocabulary after mapping whitespace to U+2581, with the BOS
+ * id first when the file names one (engine/src/model_loader.c:441-513).
+ */
+#ifndef _GNU_SOURCE
+#define _GNU_SOURCE
+#endif
+#include "engine.h"
+
+#include <errno.h>
+#include <pthread.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/resource.h>
+#include <unistd.h>
+
+#include "../../include/shk_cuda.h"
+#include "gguf.h"
+
+enum { TN_ATTN_NORM, TN_Q, TN_K, TN_V, TN_O, TN_FFN_NORM, TN_GATE, TN_UP, TN_DOWN, TN_COUNT };
+static const char *const k_suffix[TN_COUNT] = {
+    "attn_norm.weight", "attn_q.weight",   "attn_k.weight", "attn_v.weight",   "attn_output.weight",
+    "ffn_norm.weight",  "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
+
+struct tensor_loc {
+    uint64_t off, size;  /* file offset (absolute), bytes */
+    uint32_t type;
+    uint64_t rows, row_bytes;
+    uint64_t dev_off;    /* offset in the layer's device buffer (256-aligned) */
+    uint64_t dev_row;    /* padded device row bytes, 0 = dense copy */
+};
+
+struct layer_map {
+    struct tensor_loc t[TN_COUNT];
+    uint64_t span_off, span_len; /* contiguous file range holding the nine tensors */
+    uint64_t dev_bytes;
+};
+
+struct engine_handle {
+    struct gguf_file g;
+    struct engine_config cfg;
+    uint32_t n_layers, n_embd, n_heads, n_kv, head_dim, n_ff, n_vocab;
+    char **vocab;
+    int has_bos;
+    uint32_t bos;
+    struct layer_map *lm;
+    uint64_t max_span, max_dev;
+    uint32_t depth;
+    int resident;
+    uint32_t max_seq;
+
+    shk_ctx *ctx;
+    shk_kv *kv;
+    shk_model *m;
+    void *d_embd, *d_out;
+    void **d_buf;   /* resident: one per layer; ring: one per slot */
+    uint32_t n_buf;
+    void **pinned;  /* depth staging buffers of max_span bytes */
+
+    pthread_t thr;
+    int thr_started;
+    pthread_mutex_t mu;
+    pthread_cond_t cv;
+    uint64_t n_req;        /* requests to stage: resident n_layers; ring: per generation */
+    uint64_t req_staged;   /* requests whose copies are queued */
+    uint64_t req_consumed; /* requests the engine has finished enqueuing work for */
+    int stop, loader_err;
+    struct streaming_stats st;
+    int registered;
+
+    char *prompt;
+    uint32_t *out_ids;
+    size_t n_out, cap_out;
+    char *text;
+    size_t text_len, text_cap;
+    volatile int cancel;
+    uint32_t pos;      /* next KV position */
+    uint64_t ring_next; /* ring mode: next loader request to consume */
+};
+
+static int env_int(const char *name, int def) {
+    const char *v = getenv(name);
+    if (!v || !*v) return def;
+    return (int)strtol(v, NULL, 10);
+}
+
+static uint64_t al256(uint64_t x) { return (x + 255) & ~(uint64_t)255; }
+
+/* ------------------------------ model map ------------------------------- */
+
+static int map_model(struct engine_handle *h) {
+    struct gguf_file *g = &h->g;
+    h->n_layers = (uint32_t)gguf_get_uint(g, "llama.block_count", 0);
+    h->n_embd = (uint32_t)gguf_get_uint(g, "llama.embedding_length", 0);
+    h->n_heads = (uint32_t)gguf_get_uint(g, "llama.attention.head_count", 0);
+    h->n_kv = (uint32_t)gguf_get_uint(g, "llama.attention.head_count_kv", h->n_heads);
+    if (!h->n_layers || !h->n_embd || !h->n_heads || !h->n_kv || h->n_embd % h->n_heads) return -1;
+    h->head_dim = h->n_embd / h->n_heads;
+    const struct gguf_value *tok = gguf_get(g, "tokenizer.ggml.tokens");
+    if (tok && tok->type == GGUF_ARRAY && tok->arr_type == GGUF_STRING && tok->arr_n) {
+        h->vocab = tok->arr_str;
+        h->n_vocab = (uint32_t)tok->arr_n;
+    }
+    const struct gguf_value *bos = gguf_get(g, "tokenizer.ggml.bos_token_id");
+    if (bos && bos->type == GGUF_U32) {
+        h->has_bos = 1;
+        h->bos = (uint32_t)bos->u;
+    }
+    const struct gguf_tensor_info *out = gguf_find_tensor(g, "output.weight");
+    const struct gguf_tensor_info *emb = gguf_find_tensor(g, "token_embd.weight");
+    if (!out || !emb || out->n_dims != 2 || emb->n_dims != 2) return -1;
+    if (!h->n_vocab) h->n_vocab = (uint32_t)out->dims[1];
+    if (out->dims[1] != h->n_vocab || out->dims[0] != h->n_embd) return -1;
+    h->lm = (struct layer_map *)calloc(h->n_layers, sizeof(struct layer_map));
+    if (!h->lm) return -1;
+    char name[96];
+    for (uint32_t l = 0; l < h->n_layers; ++l) {
+        struct layer_map *L = &h->lm[l];
+        uint64_t lo = UINT64_MAX, hi = 0, dev = 0;
+        for (int t = 0; t < TN_COUNT; ++t) {
+            snprintf(name, sizeof(name), "blk.%u.%s", l, k_suffix[t]);
+            const struct gguf_tensor_info *ti = gguf_find_tensor(g, name);
+            if (!ti || !ti->size) return -1;
+            struct tensor_loc *tl = &L->t[t];
+            tl->off = ti->offset;
+            tl->size = ti->size;
+            tl->type = ti->type;
+            tl->rows = ti->n_dims == 2 ? ti->dims[1] : 1;
+            tl->row_bytes = ti->size / tl->rows;
+            const int norm = t == TN_ATTN_NORM || t == TN_FFN_NORM;
+            if (norm && ti->type != 0) return -1; /* F32 norm weights */
+            if (!norm && ti->type != 12 && ti->type != 14) return -1; /* Q4_K / Q6_K */
+            tl->dev_row = 0;
+            if (!norm && tl->row_bytes % 16) {
+                /* Q6_K rows of a width that is not a multiple of 2048: pad to
+                 * 16 bytes so every row starts where a bulk copy can read it;
+                 * only attn_v and ffn_down carry a row stride */
+                if (t != TN_V && t != TN_DOWN) return -1;
+                tl->dev_row = (tl->row_bytes + 15) & ~(uint64_t)15;
+            }
+            tl->dev_off = dev;
+            dev = al256(dev + (tl->dev_row ? tl->dev_row * tl->rows : tl->size));
+            if (tl->off < lo) lo = tl->off;
+            if (tl->off + tl->size > hi) hi = tl->off + tl->size;
+        }
+        L->span_off = lo;
+        L->span_len = hi - lo;
+        L->dev_bytes = dev;
+        if (L->span_len > h->max_span) h->max_span = L->span_len;
+        if (L->dev_bytes > h->max_dev) h->max_dev = L->dev_bytes;
+        if (l == 0) h->n_ff = (uint32_t)L->t[TN_GATE].rows;
+    }
+    return 0;
+}
+
+static int pread_all(int fd, void *dst, uint64_t len, uint64_t off) {
+    uint8_t *d = (uint8_t *)dst;
+    while (len) {
+        ssize_t n = pread(fd, d, len > (1u << 30) ? (1u << 30) : len, (off_t)off);
+        if (n < 0 && errno == EINTR) continue;
+        if (n <= 0) return -1;
+        d += n;
+        off += (uint64_t)n;
+        len -= (uint64_t)n;
+    }
+    return 0;
+}
+
+static int upload_tensor(struct engine_handle *h, const struct gguf_tensor_info *ti, void **dev) {
+    void *host = NULL;
+    if (shk_cuda_host_alloc(h->ctx, ti->size, &host) != SHK_OK) return -1;
+    int rc = pread_all(h->g.fd, host, ti->size, ti->offset);
+    if (!rc) rc = shk_cuda_dev_alloc(h->ctx, ti->size, dev) == SHK_OK ? 0 : -1;
+    if (!rc) rc = shk_cuda_memcpy_h2d(h->ctx, *dev, host, ti->size, NULL) == SHK_OK ? 0 : -1;
+    if (!rc) rc = shk_cuda_sync(h->ctx, NULL) == SHK_OK ? 0 : -1; /* before the staging is freed */
+    shk_cuda_host_free(h->ctx, host);
+    return rc;
+}
+
+static void layer_desc(struct engine_handle *h, uint32_t l, const uint8_t *base, struct shk_layer_desc *d) {
+    const struct layer_map *L = &h->lm[l];
+    memset(d, 0, sizeof(*d));
+    d->attn_norm = (const float *)(base + L->t[TN_ATTN_NORM].dev_off);
+    d->ffn_norm = (const float *)(base + L->t[TN_FFN_NORM].dev_off);
+    d->attn_q = base + L->t[TN_Q].dev_off;
+    d->attn_k = base + L->t[TN_K].dev_off;
+    d->attn_v = base + L->t[TN_V].dev_off;
+    d->attn_o = base + L->t[TN_O].dev_off;
+    d->ffn_gate = base + L->t[TN_GATE].dev_off;
+    d->ffn_up = base + L->t[TN_UP].dev_off;
+    d->ffn_down = base + L->t[TN_DOWN].dev_off;
+    d->attn_q_dtype = L->t[TN_Q].type;
+    d->attn_k_dtype = L->t[TN_K].type;
+    d->attn_v_dtype = L->t[TN_V].type;
+    d->attn_o_dtype = L->t[TN_O].type;
+    d->ffn_gate_dtype = L->t[TN_GATE].type;
+    d->ffn_up_dtype = L->t[TN_UP].type;
+    d->ffn_down_dtype = L->t[TN_DOWN].type;
+    d->row_stride_v = (uint32_t)L->t[TN_V].dev_row;
+    d->row_stride_down = (uint32_t)L->t[TN_DOWN].dev_row;
+}
+
+/* ------------------------------- loader --------------------------------- */
+/* Request k stages layer k % n_layers through pinned buffer / event slot
+ * k % depth.  Resident mode: requests 0..n_layers-1 into each layer's own
+ * device buffer, once.  Ring mode: an endless sequence into device slot
+ * k % depth, at most `depth` requests ahead of the engine (the slot's previous
+ * layer must have been consumed; the copies also wait on the device for the
+ * kernels that read it, via shk_cuda_layer_release). */
+
+static void *loader_main(void *arg) {
+    struct engine_handle *h = (struct engine_handle *)arg;
+    for (uint64_t k = 0;; ++k) {
+        pthread_mutex_lock(&h->mu);
+        while (!h->stop && (k >= h->n_req || (!h->resident && k >= h->req_consumed + h->depth)))
+            pthread_cond_wait(&h->cv, &h->mu);
+        const int stop = h->stop;
+        pthread_mutex_unlock(&h->mu);
+        if (stop) break;
+        const uint32_t l = (uint32_t)(k % h->n_layers), s = (uint32_t)(k % h->depth);
+        const struct layer_map *L = &h->lm[l];
+        int rc = shk_cuda_layer_ready(h->ctx, s, 1) < 0; /* the staging buffer's last copies landed */
+        uint8_t *pin = (uint8_t *)h->pinned[s];
+        if (!rc) rc = pread_all(h->g.fd, pin, L->span_len, L->span_off);
+        uint8_t *dst = (uint8_t *)h->d_buf[h->resident ? l : s];
+        for (int t = 0; !rc && t < TN_COUNT; ++t) {
+            const struct tensor_loc *tl = &L->t[t];
+            const uint8_t *src = pin + (tl->off - L->span_off);
+            if (tl->dev_row)
+                rc = shk_cuda_layer_stage_rows(h->ctx, s, dst + tl->dev_off, tl->dev_row, src, tl->row_bytes,
+                                               tl->rows) != SHK_OK;
+            else
+                rc = shk_cuda_layer_stage(h->ctx, s, dst + tl->dev_off, src, tl->size) != SHK_OK;
+        }
+        if (!rc) rc = shk_cuda_layer_commit(h->ctx, s) != SHK_OK;
+        pthread_mutex_lock(&h->mu);
+        if (rc) {
+            h->loader_err = 1;
+        } else {
+            h->req_staged = k + 1;
+            h->st.layer_loads++;
+            h->st.layer_bytes_read += L->span_len;
+        }
+        pthread_cond_broadcast(&h->cv);
+        pthread_mutex_unlock(&h->mu);
+        if (rc) break;
+    }
+    return NULL;
+}
+
+/* Engine side: wait until request k is queued, count a prefetch hit when its
+ * copies have already landed, and make the compute stream wait for them. */
+static int acquire(struct engine_handle *h, uint64_t k) {
+    pthread_mutex_lock(&h->mu);
+    while (h->req_staged <= k && !h->loader_err) pthread_cond_wait(&h->cv, &h->mu);
+    const int err = h->loader_err && h->req_staged <= k;
+    pthread_mutex_unlock(&h->mu);
+    if (err) return -1;
+    const uint32_t s = (uint32_t)(k % h->depth);
+    const int ready = shk_cuda_layer_ready(h->ctx, s, 0);
+    if (ready < 0) return -1;
+    if (ready) h->st.prefetch_hits++;
+    else h->st.prefetch_misses++;
+    return shk_cuda_layer_wait(h->ctx, s, NULL) == SHK_OK ? 0 : -1;
+}
+
+static void consume(struct engine_handle *h, uint64_t k) {
+    if (!h->resident) shk_cuda_layer_release(h->ctx, (uint32_t)(k % h->depth), NULL);
+    pthread_mutex_lock(&h->mu);
+    if (k + 1 > h->req_consumed) h->req_consumed = k + 1;
+    pthread_cond_broadcast(&h->cv);
+    pthread_mutex_unlock(&h->mu);
+}
+
+/* Resident mode: all layers staged and registered for the captured step. */
+static int register_layers(struct engine_handle *h) {
+    if (h->registered) {
+        h->st.prefetch_hits += h->n_layers; /* resident: every layer is already in HBM */
+        return 0;
+    }
+    for (uint32_t l = 0; l < h->n_layers; ++l) {
+        if (acquire(h, l)) return -1;
+        struct shk_layer_desc d;
+        layer_desc(h, l, (const uint8_t *)h->d_buf[l], &d);
+        if (shk_cuda_model_set_layer(h->m, l, &d) != SHK_OK) return -1;
+        consume(h, l);
+    }
+    if (shk_cuda_sync(h->ctx, NULL) != SHK_OK) return -1;
+    h->registered = 1;
+    return 0;
+}
+
+/* ------------------------------ tokenizer ------------------------------- */
+
+static int tokenize(struct engine_handle *h, const char *text, uint32_t **out, uint32_t *n_out) {
+    *out = NULL;
+    *n_out = 0;
+    const size_t len = text ? strlen(text) : 0;
+    char *norm = (char *)malloc(3 * len + 1);
+    uint32_t *ids = (uint32_t *)malloc((len + 2) * sizeof(uint32_t));
+    if (!norm || !ids) {
+        free(norm);
+        free(ids);
+        return -1;
+    }
+    size_t nl = 0;
+    for (size_t i = 0; i < len; ++i) {
+        const char c = text[i];
+        if (c == ' ' || c == '\n' || c == '\t' || c == '\r') { /* U+2581 */
+            norm[nl++] = (char)0xE2;
+            norm[nl++] = (char)0x96;
+            norm[nl++] = (char)0x81;
+        } else {
+            norm[nl++] = c;
+        }
+    }
+    uint32_t n = 0;
+    if (h->has_bos) ids[n++] = h->bos;
+    for (size_t i = 0; i < nl;) {
+        size_t best = 0;
+        uint32_t best_id = 0;
+        for (uint32_t t = 0; h->vocab && t < h->n_vocab; ++t) {
+            const char *s = h->vocab[t];
+            const size_t sl = strlen(s);
+            if (sl > best && sl <= nl - i && memcmp(s, norm + i, sl) == 0) {
+                best = sl;
+                best_id = t;
+            }
+        }
+        if (!best) best = 1; /* unknown byte: token 0 */
+        if (n >= len + 2) break;
+        ids[n++] = best_id;
+        i += best;
+    }
+    free(norm);
+    *out = ids;
+    *n_out = n;
+    return 0;
+}
+
+static int emit(struct engine_handle *h, uint32_t id, token_callback cb, void *user, int print) {
+    if (h->n_out == h->cap_out) {
+        const size_t cap = h->cap_out ? 2 * h->cap_out : 64;
+        uint32_t *p = (uint32_t *)realloc(h->out_ids, cap * sizeof(uint32_t));
+        if (!p) return -1;
+        h->out_ids = p;
+        h->cap_out = cap;
+    }
+    h->out_ids[h->n_out++] = id;
+    const char *s = (h->vocab && id < h->n_vocab) ? h->vocab[id] : "";
+    char piece[64];
+    snprintf(piece, sizeof(piece), "<%u>", id);
+    const size_t need = h->text_len + strlen(piece) + strlen(s) + 1;
+    if (need > h->text_cap) {
+        const size_t cap = need * 2;
+        char *t = (char *)realloc(h->text, cap);
+        if (!t) return -1;
+        h->text = t;
+        h->text_cap = cap;
+    }
+    h->text_len += (size_t)sprintf(h->text + h->text_len, "%s%s", piece, s);
+    if (cb) cb(id, s, user);
+    if (print) {
+        printf("%s%s", piece, s);
+        fflush(stdout);
+    }
+    return 0;
+}
+
+static void note_rss(struct engine_handle *h) {
+    struct rusage ru;
+    if (getrusage(RUSAGE_SELF, &ru) == 0 && (size_t)ru.ru_maxrss * 1024u > h->st.peak_rss)
+        h->st.peak_rss = (size_t)ru.ru_maxrss * 1024u;
+}
+
+/* One token through all layers at h->pos; with want_next the lm_head argmax
+ * is returned in *next (and the logits copied to `logits` when given). */
+static int step(struct engine_handle *h, uint32_t tok, int want_next, uint32_t *next, float *logits) {
+    if (h->pos >= h->max_seq) return -1;
+    if (h->resident) {
+        if (register_layers(h)) return -1;
+        if (shk_cuda_token_step(h->m, tok, h->pos, want_next, next, logits) != SHK_OK) return -1;
+    } else {
+        if (shk_cuda_model_embed(h->m, tok, NULL) != SHK_OK) return -1;
+        float *hidden = shk_cuda_model_hidden(h->m);
+        for (uint32_t l = 0; l < h->n_layers; ++l) {
+            const uint64_t k = h->ring_next++; /* k % n_layers == l: passes run whole */
+            if (acquire(h, k)) return -1;
+            struct shk_layer_desc d;
+            layer_desc(h, l, (const uint8_t *)h->d_buf[k % h->depth], &d);
+            if (shk_cuda_forward_layer(h->m, &d, l, h->pos, hidden, NULL) != SHK_OK) return -1;
+            consume(h, k);
+        }
+        if (want_next && shk_cuda_model_lm_head(h->m, next, logits, NULL) != SHK_OK) return -1;
+        if (!want_next && shk_cuda_check(h->ctx) != SHK_OK) return -1;
+    }
+    h->pos++;
+    return 0;
+}
+
+/* engine/src/engine.c:306-501 token schedule. */
+static int generate(struct engine_handle *h, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_decode,
+                    token_callback cb, void *user, int print, float *logits_out) {
+    static const uint32_t k_default = 1;
+    if (!n_prompt) {
+        prompt = &k_default;
+        n_prompt = 1;
+    }
+    h->n_out = 0;
+    h->text_len = 0;
+    if (h->text) h->text[0] = '\0';
+    h->cancel = 0;
+    h->pos = 0; /* each generation starts a new sequence */
+    shk_cuda_kv_clear(h->kv);
+    if (!h->resident) {
+        /* the ring streams exactly the passes this generation runs, like the
+         * reference's per-token requests: one per layer per prompt token and
+         * per generated token */
+        pthread_mutex_lock(&h->mu);
+        h->n_req = h->ring_next + (uint64_t)(n_prompt + n_decode) * h->n_layers;
+        pthread_cond_broadcast(&h->cv);
+        pthread_mutex_unlock(&h->mu);
+    }
+    uint32_t next = 0;
+    for (uint32_t i = 0; i < n_prompt; ++i) {
+        if (prompt[i] >= h->n_vocab) return -1;
+        const int last = i + 1 == n_prompt;
+        if (step(h, prompt[i], last, &next, last ? logits_out : NULL)) return -1;
+    }
+    for (uint32_t j = 0; j < n_decode && !h->cancel; ++j) {
+        if (emit(h, next, cb, user, print)) return -1;
+        const int want = j + 1 < n_decode;
+        float *lg = (want && logits_out) ? logits_out + (size_t)(j + 1) * h->n_vocab : NULL;
+        uint32_t nx = 0;
+        if (step(h, next, want, &nx, lg)) return -1;
+        if (want) next = nx;
+        note_rss(h);
+    }
+    if (print) printf("\n");
+    return 0;
+}
+
+/* ------------------------------- public --------------------------------- */
+
+void engine_close(engine_handle_t *h) {
+    if (!h) return;
+    if (h->thr_started) {
+        pthread_mutex_lock(&h->mu);
+        h->stop = 1;
+        pthread_cond_broadcast(&h->cv);
+        pthread_mutex_unlock(&h->mu);
+        pthread_join(h->thr, NULL);
+    }
+    if (h->ctx) shk_cuda_sync(h->ctx, NULL);
+    if (h->m) shk_cuda_model_destroy(h->m);
+    if (h->kv) shk_cuda_kv_destroy(h->kv);
+    if (h->ctx) {
+        for (uint32_t i = 0; h->d_buf && i < h->n_buf; ++i)
+            if (h->d_buf[i]) shk_cuda_dev_free(h->ctx, h->d_buf[i]);
+        for (uint32_t i = 0; h->pinned && i < h->depth; ++i)
+            if (h->pinned[i]) shk_cuda_host_free(h->ctx, h->pinned[i]);
+        if (h->d_embd) shk_cuda_dev_free(h->ctx, h->d_embd);
+        if (h->d_out) shk_cuda_dev_free(h->ctx, h->d_out);
+        shk_cuda_shutdown(h->ctx);
+    }
+    free(h->d_buf);
+    free(h->pinned);
+    free(h->lm);
+    free(h->prompt);
+    free(h->out_ids);
+    free(h->text);
+    pthread_mutex_destroy(&h->mu);
+    pthread_cond_destroy(&h->cv);
+    gguf_close(&h->g);
+    free(h);
+}
+
+engine_handle_t *engine_open(const char *model_path, const struct engine_config *cfg) {
+    if (!model_path) return NULL;
+    struct engine_handle *h = (struct engine_handle *)calloc(1, sizeof(*h));
+    if (!h) return NULL;
+    h->g.fd = -1;
+    pthread_mutex_init(&h->mu, NULL);
+    pthread_cond_init(&h->cv, NULL);
+    if (cfg) h->cfg = *cfg;
+    h->depth = h->cfg.prefetch_depth ? h->cfg.prefetch_depth : 2;
+    if (h->depth < 2) h->depth = 2;
+    if (h->depth > 3) h->depth = 3;
+    h->resident = env_int("SHUKUCHI_HBM_RESIDENT", 1) != 0;
+    h->max_seq = (uint32_t)env_int("SHUKUCHI_MAX_SEQ", 2048);
+    if (gguf_open(model_path, &h->g) || map_model(h)) goto fail;
+    struct shk_cuda_config cc = {env_int("SHUKUCHI_DEVICE", 0), 0};
+    h->ctx = shk_cuda_init(&cc);
+    if (!h->ctx) goto fail;
+    struct shk_kv_config kc = {h->n_layers, h->n_kv, h->head_dim, h->cfg.kv_block_size ? h->cfg.kv_block_size : 32,
+                               h->max_seq};
+    h->kv = shk_cuda_kv_create(h->ctx, &kc);
+    if (!h->kv) goto fail;
+    const struct gguf_tensor_info *emb = gguf_find_tensor(&h->g, "token_embd.weight");
+    const struct gguf_tensor_info *out = gguf_find_tensor(&h->g, "output.weight");
+    if (upload_tensor(h, emb, &h->d_embd) || upload_tensor(h, out, &h->d_out)) goto fail;
+    struct shk_model_desc md = {h->n_layers, h->n_embd, h->n_heads, h->n_kv, h->head_dim, h->n_ff, h->n_vocab,
+                                10000.0f /* engine/src/ops.c:223: the reference's fixed theta */,
+                                h->d_embd, emb->type, h->d_out, out->type};
+    h->m = shk_cuda_model_create(h->ctx, &md, h->kv);
+    if (!h->m) goto fail;
+    h->n_buf = h->resident ? h->n_layers : h->depth;
+    h->d_buf = (void **)calloc(h->n_buf, sizeof(void *));
+    h->pinned = (void **)calloc(h->depth, sizeof(void *));
+    if (!h->d_buf || !h->pinned) goto fail;
+    for (uint32_t i = 0; i < h->n_buf; ++i)
+        if (shk_cuda_dev_alloc(h->ctx, h->max_dev, &h->d_buf[i]) != SHK_OK) goto fail;
+    for (uint32_t i = 0; i < h->depth; ++i)
+        if (shk_cuda_host_alloc(h->ctx, h->max_span, &h->pinned[i]) != SHK_OK) goto fail;
+    h->st.max_layer_size = (size_t)h->max_span;
+    h->st.peak_buffer_usage = (size_t)h->max_span * h->depth;
+    h->st.max_concurrent_buffers = h->depth;
+    h->n_req = h->resident ? h->n_layers : 0; /* ring: set per generation */
+    if (pthread_create(&h->thr, NULL, loader_main, h) != 0) goto fail;
+    h->thr_started = 1;
+    return h;
+fail:
+    engine_close(h);
+    return NULL;
+}
+
+int engine_set_prompt(engine_handle_t *h, const char *prompt) {
+    if (!h) return -1;
+    free(h->prompt);
+    h->prompt = prompt ? strdup(prompt) : NULL;
+    return (prompt && !h->prompt) ? -1 : 0;
+}
+
+static int generate_text(engine_handle_t *h, uint32_t max_tokens, token_callback cb, void *user, int print) {
+    if (!h || max_tokens == 0) return -1;
+    uint32_t *ids = NULL, n = 0;
+    if (tokenize(h, h->prompt ? h->prompt : "", &ids, &n)) return -1;
+    const int rc = generate(h, ids, n, max_tokens, cb, user, print, NULL);
+    free(ids);
+    return rc;
+}
+
+int engine_generate(engine_handle_t *h, uint32_t max_tokens) { return generate_text(h, max_tokens, NULL, NULL, 1); }
+
+int engine_generate_stream(engine_handle_t *h, uint32_t max_tokens, token_callback cb, void *user) {
+    return generate_text(h, max_tokens, cb, user, 0);
+}
+
+int engine_generate_ids(engine_handle_t *h, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_decode,
+                        uint32_t *out_ids, float *out_logits) {
+    if (!h || !n_decode || (n_prompt && !prompt)) return -1;
+    const int rc = generate(h, prompt, n_prompt, n_decode, NULL, NULL, 0, out_logits);
+    if (!rc && out_ids) memcpy(out_ids, h->out_ids, h->n_out * sizeof(uint32_t));
+    return rc ? rc : (int)h->n_out;
+}
+
+const char *engine_get_output(engine_handle_t *h) { return (h && h->text) ? h->text : ""; }
+
+const uint32_t *engine_get_tokens(engine_handle_t *h, size_t *n) {
+    if (n) *n = h ? h->n_out : 0;
+    return h ? h->out_ids : NULL;
+}
+
+void engine_cancel(engine_handle_t *h) {
+    if (h) h->cancel = 1;
+}
+
+int engine_get_streaming_stats(engine_handle_t *h, struct streaming_stats *out) {
+    if (!h || !out) return -1;
+    note_rss(h);
+    pthread_mutex_lock(&h->mu);
+    *out = h->st;
+    pthread_mutex_unlock(&h->mu);
+    return 0;
+}
+
+uint32_t engine_vocab_size(engine_handle_t *h) { return h ? h->n_vocab : 0; }
+
+int engine_inspect(const char *model_path, uint32_t out[6], uint64_t *max_layer_bytes) {
+    struct engine_handle *h = (struct engine_handle *)calloc(1, sizeof(*h));
+    if (!h) return -1;
+    int rc = gguf_open(model_path, &h->g);
+    if (!rc) rc = map_model(h);
+    if (!rc) {
+        out[0] = h->n_layers;
+        out[1] = h->n_embd;
+        out[2] = h->n_heads;
+        out[3] = h->n_kv;
+        out[4] = h->n_ff;
+        out[5] = h->n_vocab;
+        if (max_layer_bytes) *max_layer_bytes = h->max_span;
+    }
+    free(h->lm);
+    gguf_close(&h->g);
+    free(h);
+    return rc;
+}

@@ -11,8 +11,12 @@ token fed back on the device.  Weights (4.9 GB) are synthetic, seeded, and
 generated in HBM; the KV cache is prefilled with a 512-token random prompt.
 Weights exceed L2 (126 MB), so no flush is needed between steps.
 
-At --gpus N > 1 each rank decodes its own sequence on its own GPU (replicas,
-weak scaling; the value is the sum over ranks, timed as the max over ranks).
+At --gpus N > 1 the same single sequence is decoded tensor-parallel over N
+GPUs (one process per GPU; Wq/Wk/Wv/gate/up split by output rows, Wo/down by
+input columns, KV heads local to a rank, output head split by vocabulary rows;
+NCCL all-reduce after O and down inside the captured step): strong scaling,
+timed as the max over ranks.  Each rank generates its shard's synthetic
+weights directly (same distributions, rank-seeded).
 ``--impl reference`` times the reference's own C implementation of the path
 (oracle/_ref, compiled from the reference sources; else the oracle port) on
 host cores, on a bounded sample of the same workload.
@@ -208,8 +212,8 @@ def workload_config(args, ws):
     from shukuchi_b200 import synth
     name = synth.SHAPES[args.shape].name
     return {"workload": f"{name} Q4_K_M decode bs1 after a {args.prompt}-token prompt, Q8_0 KV",
-            "model": name, "global_batch": ws, "seq_len": args.prompt,
-            "parallelism": f"replicas{ws}" if ws > 1 else "single",
+            "model": name, "global_batch": 1, "seq_len": args.prompt,
+            "parallelism": f"tp{ws}" if ws > 1 else "single",
             "l2": "no flush: 4.9 GB of weights per step exceed the 126 MB L2"}
 
 
@@ -219,7 +223,7 @@ def run_reference(args, ws, rank):
     v, kind, sample = cpu_sample(args.steps, args.warmup, args.shape, args.prompt)
     line = {
         "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, 1),
         "impl": "reference",
@@ -235,6 +239,7 @@ def run_ours(args, ws, rank, local):
     import torch.distributed as dist
     from shukuchi_b200 import cuda as sc
     from shukuchi_b200 import synth
+    from shukuchi_b200 import tp as tpl
     from shukuchi_b200.synth_device import make_device_model
 
     torch.cuda.set_device(local)
@@ -244,17 +249,26 @@ def run_ours(args, ws, rank, local):
                                 device_id=torch.device("cuda", local))
     shape = synth.SHAPES[args.shape]
     ctx = sc.Context(local)
-    wts = make_device_model(shape, seed=1234 + rank, device=f"cuda:{local}")
+    lay = tpl.layout(shape, rank, ws)
+    lshape = tpl.local_shape(shape, lay)
+    if ws > 1:
+        obj = [sc.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.tp_init(rank, ws, obj[0])
+    wts = make_device_model(lshape, seed=1234 + rank, device=f"cuda:{local}",
+                            o_rows=lay.o_hi - lay.o_lo, out_rows=lay.v_hi - lay.v_lo)
     total = args.prompt + 2 * (args.warmup + args.steps) + 8
-    kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, total)
+    kv = sc.KvCache(ctx, lshape.n_layers, lshape.n_kv_heads, lshape.head_dim, total)
     m = sc.DeviceModel(ctx, kv, wts.desc)
+    if ws > 1:
+        m.set_tp_rows(lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi)
     for i, lv in enumerate(wts.layers):
         m.set_layer(i, lv)
     stream = torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{local}")
 
     # prompt, token by token (the reference has no batched prefill)
     import numpy as np
-    rng = np.random.default_rng(rank)
+    rng = np.random.default_rng(0)  # one sequence, the same on every rank
     prompt = rng.integers(0, shape.n_vocab, args.prompt).astype(np.uint32)
     nxt = 0
     for i, t in enumerate(prompt):
@@ -291,7 +305,7 @@ def run_ours(args, ws, rank, local):
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms_max = float(t_max.item())
     ms_per_step = ms_max / args.steps
-    value = ws * args.steps / (ms_max / 1000.0)
+    value = args.steps / (ms_max / 1000.0)
 
     # end to end through the public call: host token in (pinned H2D), host
     # token out (D2H), one call per token
@@ -306,7 +320,7 @@ def run_ours(args, ws, rank, local):
     e_ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
     if ws > 1:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    e2e = ws * args.steps / (float(e_ms.item()) / 1000.0)
+    e2e = args.steps / (float(e_ms.item()) / 1000.0)
 
     # dominant kernel: gate/up Q4_K GEMV (dual matrix, SwiGLU epilogue), timed
     # per launch with events on the launching stream, rotating layers so no
@@ -340,12 +354,19 @@ def run_ours(args, ws, rank, local):
         torch.cuda.synchronize()
         parts[name] = round(sum(a.elapsed_time(b) for a, b in evs) * 1000.0, 1)
     ctx.check()
-    alg = wbytes + 4 * (shape.n_embd + shape.n_ff)
+    alg = wbytes + 4 * (shape.n_embd + lshape.n_ff)
     peak, peak_kind = peaks()
     achieved = alg / avg / 1e9
-    # whole-step bytes at the mean context of the timed region
+    # whole-step bytes at the mean context of the timed region, summed over
+    # ranks (tensor parallel duplicates a few rows), against ws x the peak
     mean_ctx = args.prompt + args.warmup + args.steps / 2
-    step_bytes = synth.token_bytes(shape) + synth.kv_bytes_per_pos(shape) * mean_ctx
+    if ws == 1:
+        step_bytes = synth.token_bytes(shape) + synth.kv_bytes_per_pos(shape) * mean_ctx
+    else:
+        wb, kvb = tpl.rank_token_bytes(shape, lay)
+        tb = torch.tensor([wb + kvb * mean_ctx], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tb)
+        step_bytes = float(tb.item())
     step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
 
     cpu = None
@@ -353,11 +374,11 @@ def run_ours(args, ws, rank, local):
         v, kind, sample = cpu_sample(12, 1, args.shape, args.prompt)
         cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample}
 
-    launches_per_step = 1 + 5 * shape.n_layers + 2
+    launches_per_step = 1 + 5 * shape.n_layers + 2 + (1 if lay.v_hi - lay.v_lo < shape.n_vocab else 0)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, ws),
         "clocks": clk.summary(),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
@@ -365,10 +386,10 @@ def run_ours(args, ws, rank, local):
         "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K> gate/up (dual) + SwiGLU",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "bytes_per_launch": alg,
-                     "traffic": ncu_traffic("gemv_gateup_llama8b.md")},
+                     "traffic": ncu_traffic("gemv_gateup_llama8b.md") if ws == 1 else None},
         "token_parts_us": parts,
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
-                          "frac": step_gbs / peak},
+                          "frac": step_gbs / (ws * peak)},
         "cpu_baseline": cpu,
     }
     if rank == 0:

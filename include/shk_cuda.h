@@ -232,6 +232,27 @@ int shk_cuda_layer_wait(shk_ctx *ctx, uint32_t slot, void *stream);
  * queued on `stream` so far -- the kernels that read the slot's old layer. */
 int shk_cuda_layer_release(shk_ctx *ctx, uint32_t slot, void *stream);
 
+/* ---- tensor parallelism over the GPUs of one node: NCCL all-reduce over
+ *      NVLink after the O and down projections (north-star TP layout: Wq/Wk/Wv/
+ *      gate/up split by output rows, Wo/down by input columns, KV heads local
+ *      to a rank).  No counterpart in the reference (single device). ---- */
+#define SHK_TP_ID_BYTES 128
+/* Rank 0 creates the communicator id (returns its size); the caller passes
+ * it to every rank, which then calls shk_cuda_tp_init before creating its
+ * model.  NCCL is loaded at first use (libnccl.so.2). */
+int shk_cuda_tp_unique_id(void *out, size_t cap);
+int shk_cuda_tp_init(shk_ctx *ctx, int rank, int world, const void *id);
+/* This rank computes rows [o_lo, o_hi) of the O projection (its attn_o
+ * weights have o_hi - o_lo rows; ranks that share attention heads split the
+ * rows) and rows [v_lo, v_hi) of the output head (its output weights have
+ * v_hi - v_lo rows).  The head is either replicated (0, n_vocab) or split in
+ * equal slices in rank order (v_lo = rank * n_vocab / world); a split head's
+ * argmax is merged over the ranks, and a logits copy to the host gathers the
+ * slices first, so every rank must ask for logits on the same steps.
+ * Default: all rows.  Call after shk_cuda_tp_init and before
+ * shk_cuda_model_set_layer. */
+int shk_cuda_model_set_tp_rows(shk_model *m, uint32_t o_lo, uint32_t o_hi, uint32_t v_lo, uint32_t v_hi);
+
 /* ---- argmax without any device allocation.  No counterpart in the reference:
  *      it exists for callers that cannot call cudaMalloc (a sampler inside a
  *      host runtime that has already reserved the device's memory in its own

@@ -11,7 +11,7 @@
 // Kernel shape (one CTA per SM, persistent over a byte-balanced row range):
 //  * warp 8 is the producer: one lane streams whole-row chunks of the weight
 //    matrix into a shared-memory ring with cp.async.bulk (TMA, 1-D, no tensor
-//    map, no multicast), completion tracked by mbarrier tx-counts; a per-stage
+//    map, one destination CTA), completion tracked by mbarrier tx-counts; a per-stage
 //    generation tag orders consumers that skip ahead;
 //  * warps 0-7 are consumers: they load x (RMSNorm fused) and turn it into the
 //    fixed-point form below while the first chunks are in flight, then decode

@@ -34,11 +34,15 @@ __global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t dtype,
 // First index of the maximum (engine/src/engine.c:424-431).  Block partials
 // then the last block merges.  Optionally advances the device position counter
 // (token feedback in a captured step).
+// With idx_off / val_out (a tensor-parallel rank's slice of the vocabulary):
+// writes idx_off + local index and the maximum's value, for the merge over
+// ranks below.
 constexpr int AM_THREADS = 512;
 __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restrict__ x, uint32_t n,
                                                             float* part_v, uint32_t* part_i,
                                                             int* counter, uint32_t* tok_out,
-                                                            uint32_t* pos_inc) {
+                                                            uint32_t* pos_inc, uint32_t idx_off,
+                                                            float* val_out) {
   __shared__ float sv[AM_THREADS / 32];
   __shared__ uint32_t si[AM_THREADS / 32];
   __shared__ int last;
@@ -58,9 +62,31 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restr
   __syncthreads();
   if (!last || threadIdx.x != 0) return;
   __threadfence();
-  *tok_out = am_merge(part_v, part_i, gridDim.x);
+  *tok_out = idx_off + am_merge(part_v, part_i, gridDim.x, val_out);
   if (pos_inc) *pos_inc += 1;
   *counter = 0;
+}
+
+// Merge of the ranks' (value, global index) pairs, rank order, with the same
+// first-maximum rule as the blocks above: the vocabulary slices are in rank
+// order, so the result is the argmax of the whole logits vector.
+__global__ void argmax_ranks_kernel(const uint32_t* __restrict__ pairs, int world, uint32_t* tok_out,
+                                    uint32_t* pos_inc) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  float v = __uint_as_float(__ldcg(&pairs[0]));
+  uint32_t ix = __ldcg(&pairs[1]);
+  for (int r = 1; r < world; ++r) {
+    const float ov = __uint_as_float(__ldcg(&pairs[2 * r]));
+    const uint32_t oi = __ldcg(&pairs[2 * r + 1]);
+    if (am_better(v, ix, ov, oi)) {
+      v = ov;
+      ix = oi;
+    }
+  }
+  *tok_out = ix;
+  if (pos_inc) *pos_inc += 1;
 }
 
 // op_rmsnorm, n = 1 (engine/src/ops.c:195-214)
@@ -123,9 +149,15 @@ int argmax_blocks(uint32_t n) {
 }
 
 cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* part_i, int* counter,
-                          uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st) {
+                          uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st, uint32_t idx_off,
+                          float* val_out) {
   return launch_k(argmax_kernel, dim3(argmax_blocks(n)), dim3(AM_THREADS), 0, st, x, n, part_v, part_i,
-                  counter, tok_out, pos_inc);
+                  counter, tok_out, pos_inc, idx_off, val_out);
+}
+
+cudaError_t argmax_ranks_launch(const uint32_t* pairs, int world, uint32_t* tok_out, uint32_t* pos_inc,
+                                cudaStream_t st) {
+  return launch_k(argmax_ranks_kernel, dim3(1), dim3(32), 0, st, pairs, world, tok_out, pos_inc);
 }
 
 bool& pdl_enabled() {

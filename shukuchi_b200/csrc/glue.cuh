@@ -10,7 +10,11 @@ cudaError_t embed_launch(const void* table, uint32_t dtype, const uint32_t* tok,
                          float* out, uint32_t n_embd, int* err, cudaStream_t st);
 int argmax_blocks(uint32_t n);
 cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* part_i, int* counter,
-                          uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st);
+                          uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st, uint32_t idx_off = 0,
+                          float* val_out = nullptr);
+// pairs: world x {value bits, global index}; writes the first maximum's index.
+cudaError_t argmax_ranks_launch(const uint32_t* pairs, int world, uint32_t* tok_out, uint32_t* pos_inc,
+                                cudaStream_t st);
 cudaError_t rmsnorm_launch(const float* x, const float* w, float* y, uint32_t d, cudaStream_t st);
 cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t* pos,
                         const float* freq, cudaStream_t st);

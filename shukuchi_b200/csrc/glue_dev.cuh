@@ -91,7 +91,8 @@ __device__ __forceinline__ void am_block(const float* __restrict__ x, uint32_t l
 // Merge of the per-block partials by the last block (thread 0).  NaN logits
 // never compare greater; an all-NaN vector yields index 0 as in the reference
 // loop.
-__device__ __forceinline__ uint32_t am_merge(const float* part_v, const uint32_t* part_i, uint32_t n) {
+__device__ __forceinline__ uint32_t am_merge(const float* part_v, const uint32_t* part_i, uint32_t n,
+                                             float* v_out = nullptr) {
   float v = __ldcg(&part_v[0]);
   uint32_t ix = __ldcg(&part_i[0]);
   for (uint32_t b = 1; b < n; ++b) {
@@ -102,6 +103,7 @@ __device__ __forceinline__ uint32_t am_merge(const float* part_v, const uint32_t
       ix = oi;
     }
   }
+  if (v_out) *v_out = v;
   return (ix == 0xFFFFFFFFu) ? 0u : ix;
 }
 

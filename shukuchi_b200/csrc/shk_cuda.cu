@@ -2,6 +2,8 @@
 #include "../../include/shk_cuda.h"
 
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -28,8 +30,43 @@ using namespace shk;
     }                                                         \
   } while (0)
 
+// NCCL, loaded at first use: the process's libnccl.so.2 (the one a framework
+// already loaded, else the system's), so no second copy is linked in.
+namespace {
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*);
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t);
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*comm_destroy)(ncclComm_t);
+};
+const NcclApi* nccl() {
+  static NcclApi api;
+  static int state = 0;  // 0 untried, 1 loaded, -1 unavailable
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (state == 0) {
+    state = -1;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+      api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+      api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+      api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+      api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+      if (api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy)
+        state = 1;
+    }
+  }
+  return state == 1 ? &api : nullptr;
+}
+}  // namespace
+
 struct shk_ctx {
   int device = 0;
+  int tp_rank = 0, tp_world = 1;  // tensor parallelism (shk_cuda_tp_init)
+  ncclComm_t comm = nullptr;
   uint32_t flags = 0;  // SHK_CUDA_FLAG_*
   int num_sms = 148;
   cudaStream_t compute = nullptr;
@@ -110,6 +147,9 @@ struct shk_model {
     DecodePhase* d_phases = nullptr;
     GridBar* d_bar = nullptr;
   } pk;
+  uint32_t o_lo = 0, o_hi = 0;  // tensor parallel: this rank's rows of the O projection output
+  uint32_t v_lo = 0, v_hi = 0;  // ... and of the output head (logits); all rows when replicated
+  uint32_t* tp_pairs = nullptr; // world x {max value bits, index}: argmax over the vocabulary slices
   uint64_t* d_trace = nullptr;  // persistent-kernel timeline (shk_cuda_model_trace_enable)
   uint32_t trace_phases = 0;
   uint32_t trace_last = 0;      // phases recorded by the last launch
@@ -244,6 +284,7 @@ void shk_cuda_shutdown(shk_ctx* c) {
   if (c->copy) cudaStreamSynchronize(c->copy);
   for (auto& kv : c->slot_ev) cudaEventDestroy(kv.second);
   for (auto& kv : c->rel_ev) cudaEventDestroy(kv.second);
+  if (c->comm && nccl()) nccl()->comm_destroy(c->comm);
   cudaFree(c->d_err);
   cudaFreeHost(c->h_err);
   cudaFree(c->d_u32);
@@ -527,14 +568,17 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
   };
   int rc = gemv_plan(P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos, m->d_freq, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
-  GemvMat o{lv.attn_o, nullptr, m->hidden, d.n_embd, lv.attn_o_dtype, 0, EPI_ADD, 0};
+  // Tensor parallel: rank 0 adds the residual, the others store their partial
+  // sums (all-reduced afterwards); the O projection covers rows [o_lo, o_hi).
+  const uint8_t res_epi = c->tp_rank == 0 ? EPI_ADD : EPI_STORE;
+  GemvMat o{lv.attn_o, nullptr, m->hidden + m->o_lo, m->o_hi - m->o_lo, lv.attn_o_dtype, 0, res_epi, 0};
   rc = gemv_plan(P.o, &o, 1, qd, m->att, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
   if (lv.ffn_gate_dtype != lv.ffn_up_dtype) return SHK_EUNSUPPORTED;
   GemvMat gu{lv.ffn_gate, lv.ffn_up, m->act, d.n_ff, lv.ffn_gate_dtype, 0, EPI_SWIGLU, 0};
   rc = gemv_plan(P.gateup, &gu, 1, d.n_embd, m->hidden, lv.ffn_norm, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
-  GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, EPI_ADD, 0};
+  GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, res_epi, 0};
   rc = gemv_plan(P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
   P.ok = true;
@@ -562,30 +606,84 @@ AttnArgs layer_attn_args(shk_model* m, uint32_t layer, const uint32_t* pos) {
 
 // Enqueues one layer: fused RMSNorm+QKV(+RoPE), append+attention, O(+residual),
 // RMSNorm+gate/up(+SwiGLU), down(+residual).  `pos` is a device pointer.
+//
+// Tensor parallel (world > 1): the residual stream is replicated; after the O
+// and down projections the ranks' partial sums are all-reduced (rank 0's
+// epilogue adds the residual, the others store).  `pdl`: launches that follow
+// one of our kernels may be programmatic dependents; a launch that follows a
+// collective or a memset never is (the dependency edge is only defined
+// between kernels), and the caller's launch after this layer inherits
+// pdl_enabled() as left here.
 int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint32_t* pos,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool pdl) {
+  shk_ctx* c = m->ctx;
+  const bool tp = c->tp_world > 1;
   GemvPlan qkv = P.qkv;
   qkv.args.pos = pos;
   CK(gemv_launch(qkv, st));
+  pdl_enabled() = pdl;
   const AttnArgs a = layer_attn_args(m, layer, pos);
   CK(attn_decode_launch(a, st));
+  if (tp && c->tp_rank != 0 && m->o_hi - m->o_lo < m->d.n_embd) {  // rows this rank does not write
+    CK(cudaMemsetAsync(m->hidden, 0, (size_t)m->d.n_embd * sizeof(float), st));
+    pdl_enabled() = false;
+  }
   CK(gemv_launch(P.o, st));
+  if (tp) {
+    if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
+      return SHK_ENCCL;
+    pdl_enabled() = false;
+  }
   CK(gemv_launch(P.gateup, st));
+  pdl_enabled() = pdl;
   CK(gemv_launch(P.down, st));
+  if (tp) {
+    if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
+      return SHK_ENCCL;
+    pdl_enabled() = false;
+  }
+  return SHK_OK;
+}
+
+bool vocab_split(const shk_model* m) { return m->v_hi - m->v_lo < m->d.n_vocab; }
+
+// Tensor parallel with a split output head: every rank's logits slice is
+// gathered into the full vector (in place), e.g. before a copy to the host.
+int gather_logits(shk_model* m, cudaStream_t st) {
+  if (!vocab_split(m)) return SHK_OK;
+  const uint32_t n = m->v_hi - m->v_lo;
+  if (nccl()->all_gather(m->logits + m->v_lo, m->logits, n, ncclFloat, m->ctx->comm, st) != ncclSuccess)
+    return SHK_ENCCL;
   return SHK_OK;
 }
 
 // pdl_after_first: launches after the first one carry the programmatic
 // dependent launch attribute (used while capturing the decode-step graphs).
+// With the output head split over tensor-parallel ranks, each rank takes the
+// first maximum of its slice, the (value, index) pairs are all-gathered and
+// merged in rank order.
 int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos, bool pdl_after_first = false) {
+  const uint32_t nv = m->v_hi - m->v_lo;
   if (m->head_generic)
-    CK(gemv_generic_launch(m->d.output_dtype, m->d.output_dev, m->hidden, m->logits, m->d.n_vocab,
+    CK(gemv_generic_launch(m->d.output_dtype, m->d.output_dev, m->hidden, m->logits + m->v_lo, nv,
                            m->d.n_embd, st));
   else
     CK(gemv_launch(m->head, st));
   if (pdl_after_first) pdl_enabled() = true;
-  CK(argmax_launch(m->logits, m->d.n_vocab, m->am_v, m->am_i, m->am_cnt, m->d_tok,
-                   advance_pos ? m->d_tok + 1 : nullptr, st));
+  uint32_t* pos_inc = advance_pos ? m->d_tok + 1 : nullptr;
+  if (!vocab_split(m)) {
+    CK(argmax_launch(m->logits, m->d.n_vocab, m->am_v, m->am_i, m->am_cnt, m->d_tok, pos_inc, st));
+    return SHK_OK;
+  }
+  shk_ctx* c = m->ctx;
+  uint32_t* mine = m->tp_pairs + 2 * c->tp_rank;
+  CK(argmax_launch(m->logits + m->v_lo, nv, m->am_v, m->am_i, m->am_cnt, mine + 1, nullptr, st, m->v_lo,
+                   reinterpret_cast<float*>(mine)));
+  if (nccl()->all_gather(mine, m->tp_pairs, 2, ncclUint32, c->comm, st) != ncclSuccess) return SHK_ENCCL;
+  const bool pdl = pdl_enabled();
+  pdl_enabled() = false;
+  CK(argmax_ranks_launch(m->tp_pairs, c->tp_world, m->d_tok, pos_inc, st));
+  pdl_enabled() = pdl;
   return SHK_OK;
 }
 
@@ -594,7 +692,7 @@ int enqueue_layers(shk_model* m, cudaStream_t st, bool pdl_after_first = false) 
                   m->d.n_embd, m->ctx->d_err, st));
   if (pdl_after_first) pdl_enabled() = true;
   for (uint32_t l = 0; l < m->d.n_layers; ++l) {
-    const int rc = enqueue_layer(m, m->plans[l], l, m->d_tok + 1, st);
+    const int rc = enqueue_layer(m, m->plans[l], l, m->d_tok + 1, st, pdl_after_first);
     if (rc) return rc;
   }
   return SHK_OK;
@@ -632,7 +730,7 @@ int build_persist(shk_model* m) {
   shk_ctx* c = m->ctx;
   const shk_model_desc& d = m->d;
   k.state = -1;
-  if (!(c->flags & SHK_CUDA_FLAG_PERSISTENT) || m->head_generic) return SHK_OK;
+  if (!(c->flags & SHK_CUDA_FLAG_PERSISTENT) || m->head_generic || c->tp_world > 1) return SHK_OK;
   const uint32_t G = d.n_heads / d.n_kv_heads;
   if (d.n_heads % d.n_kv_heads) return SHK_OK;
   const uint32_t L = d.n_layers, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
@@ -749,7 +847,8 @@ shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv
   if (!c || !d || !kv) return nullptr;
   if (!d->n_layers || !d->n_embd || !d->n_heads || !d->n_kv_heads || !d->n_ff || !d->n_vocab)
     return nullptr;
-  if (d->head_dim * d->n_heads != d->n_embd || kv->L.hd != d->head_dim ||
+  // (a tensor-parallel rank holds n_heads / world query heads: q width != n_embd)
+  if ((c->tp_world == 1 && d->head_dim * d->n_heads != d->n_embd) || kv->L.hd != d->head_dim ||
       kv->L.n_kv != d->n_kv_heads || kv->L.n_layers != d->n_layers)
     return nullptr;
   shk_model* m = new (std::nothrow) shk_model();
@@ -757,6 +856,10 @@ shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv
   m->ctx = c;
   m->d = *d;
   m->kv = kv;
+  m->o_lo = 0;
+  m->o_hi = d->n_embd;
+  m->v_lo = 0;
+  m->v_hi = d->n_vocab;
   const uint32_t qd = d->n_heads * d->head_dim, kvd = d->n_kv_heads * d->head_dim;
   bool ok = true;
   auto A = [&](float** p, size_t n) { ok = ok && cudaMalloc(p, n * sizeof(float)) == cudaSuccess; };
@@ -813,6 +916,7 @@ void shk_cuda_model_destroy(shk_model* m) {
   cudaFree(m->att);
   cudaFree(m->act);
   cudaFree(m->logits);
+  cudaFree(m->tp_pairs);
   cudaFree(m->am_v);
   cudaFree(m->am_i);
   cudaFree(m->am_cnt);
@@ -845,7 +949,8 @@ int shk_cuda_forward_layer(shk_model* m, const shk_layer_desc* lv, uint32_t laye
   int rc = build_layer_plans(m, *lv, P);
   if (rc) return rc;
   if (hidden != m->hidden) CK(cudaMemcpyAsync(m->hidden, hidden, m->d.n_embd * 4, cudaMemcpyDeviceToDevice, st));
-  rc = enqueue_layer(m, P, layer, m->kv->d_iota + pos, st);
+  rc = enqueue_layer(m, P, layer, m->kv->d_iota + pos, st, false);
+  pdl_enabled() = false;
   if (rc) return rc;
   if (hidden != m->hidden) CK(cudaMemcpyAsync(hidden, m->hidden, m->d.n_embd * 4, cudaMemcpyDeviceToDevice, st));
   m->kv->seq[layer] = std::max(m->kv->seq[layer], pos + 1);
@@ -871,6 +976,7 @@ int shk_cuda_model_lm_head(shk_model* m, uint32_t* token, float* logits, void* s
   int rc = enqueue_head(m, st, false);
   if (rc) return rc;
   CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, st));
+  if (logits && (rc = gather_logits(m, st))) return rc;
   if (logits) CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->d.n_vocab * 4, cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   if (token) *token = m->h_tok[2];
@@ -901,6 +1007,7 @@ int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_nex
   }
   if (want_next) {
     CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, st));
+    if (logits && (rc = gather_logits(m, st))) return rc;
     if (logits) CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->d.n_vocab * 4, cudaMemcpyDeviceToHost, st));
   }
   CK(cudaStreamSynchronize(st));
@@ -935,6 +1042,56 @@ int shk_cuda_decode_steps(shk_model* m, uint32_t first_token, uint32_t first_pos
   for (uint32_t l = 0; l < m->d.n_layers; ++l)
     m->kv->seq[l] = std::max(m->kv->seq[l], first_pos + n);
   m->ctx->n_steps += n;
+  return SHK_OK;
+}
+
+int shk_cuda_tp_unique_id(void* out, size_t cap) {
+  if (!out || cap < sizeof(ncclUniqueId)) return SHK_EINVAL;
+  if (!nccl()) return SHK_EUNSUPPORTED;
+  ncclUniqueId id;
+  if (nccl()->get_unique_id(&id) != ncclSuccess) return SHK_ENCCL;
+  memcpy(out, &id, sizeof(id));
+  return (int)sizeof(id);
+}
+
+int shk_cuda_tp_init(shk_ctx* c, int rank, int world, const void* id) {
+  if (!c || !id || world < 1 || rank < 0 || rank >= world || c->comm) return SHK_EINVAL;
+  if (world == 1) return SHK_OK;
+  if (!nccl()) return SHK_EUNSUPPORTED;
+  cudaSetDevice(c->device);
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  if (nccl()->comm_init_rank(&c->comm, world, uid, rank) != ncclSuccess) {
+    c->comm = nullptr;
+    return SHK_ENCCL;
+  }
+  c->tp_rank = rank;
+  c->tp_world = world;
+  return SHK_OK;
+}
+
+int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint32_t v_lo, uint32_t v_hi) {
+  if (!m || o_lo >= o_hi || o_hi > m->d.n_embd || v_lo >= v_hi || v_hi > m->d.n_vocab) return SHK_EINVAL;
+  for (uint32_t l = 0; l < m->d.n_layers; ++l)
+    if (m->have[l]) return SHK_EINVAL;  // before any layer is registered
+  if (m->g_layers || m->g_head || m->g_loop) return SHK_EINVAL;  // graphs already captured
+  shk_ctx* c = m->ctx;
+  const uint32_t nv = v_hi - v_lo;
+  if (nv < m->d.n_vocab) {  // equal slices in rank order (the gathers need equal counts)
+    if (c->tp_world < 2 || (uint64_t)nv * c->tp_world != m->d.n_vocab || v_lo != nv * (uint32_t)c->tp_rank)
+      return SHK_EINVAL;
+    if (!m->tp_pairs && cudaMalloc(&m->tp_pairs, 2 * sizeof(uint32_t) * c->tp_world) != cudaSuccess)
+      return SHK_ENOMEM;
+  }
+  GemvMat hm{m->d.output_dev, nullptr, m->logits + v_lo, nv, m->d.output_dtype, 0, EPI_STORE, 0};
+  const int hp = gemv_plan(m->head, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err,
+                           c->num_sms);
+  if (hp == -2) return SHK_EUNSUPPORTED;
+  m->head_generic = hp != 0;
+  m->o_lo = o_lo;
+  m->o_hi = o_hi;
+  m->v_lo = v_lo;
+  m->v_hi = v_hi;
   return SHK_OK;
 }
 

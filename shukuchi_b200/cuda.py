@@ -83,6 +83,9 @@ _SIGS = {
     "shk_cuda_embed": (I, [P, P, U32, U32, U32, P, U32, P]),
     "shk_cuda_argmax": (I, [P, P, U32, C.POINTER(U32)]),
     "shk_cuda_argmax_noalloc": (I, [P, U32, P, P]),
+    "shk_cuda_tp_unique_id": (I, [P, SZ]),
+    "shk_cuda_tp_init": (I, [P, I, I, P]),
+    "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),
     "shk_cuda_kv_create": (P, [P, C.POINTER(KvConfig)]),
     "shk_cuda_kv_destroy": (None, [P]),
     "shk_cuda_kv_append": (I, [P, U32, U32, P, P, P]),
@@ -184,6 +187,12 @@ class Context:
     def report(self) -> None:
         lib().shk_cuda_report(self.h)
 
+    def tp_init(self, rank: int, world: int, uid: bytes) -> None:
+        """Joins this context to a tensor-parallel group of `world` ranks
+        (one process or thread per GPU); uid comes from tp_unique_id() on rank 0."""
+        buf = C.create_string_buffer(bytes(uid), len(uid))
+        _call("shk_cuda_tp_init", self.h, rank, world, buf)
+
     def matmul(self, qtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int,
                stream: int | None = None) -> None:
         name = "shk_cuda_matmul_q4k_vec" if qtype == 12 else "shk_cuda_matmul_q6k_vec"
@@ -226,6 +235,13 @@ class Context:
 
     def layer_wait(self, slot, stream=None):
         _call("shk_cuda_layer_wait", self.h, slot, stream)
+
+
+def tp_unique_id() -> bytes:
+    """A new communicator id for shk_cuda_tp_init (created on rank 0)."""
+    buf = C.create_string_buffer(128)
+    n = check("shk_cuda_tp_unique_id", lib().shk_cuda_tp_unique_id(buf, 128))
+    return buf.raw[:n]
 
 
 class KvCache:
@@ -282,6 +298,9 @@ class DeviceModel:
 
     def set_layer(self, layer: int, lv: LayerDesc):
         _call("shk_cuda_model_set_layer", self.h, layer, C.byref(lv))
+
+    def set_tp_rows(self, o_lo: int, o_hi: int, v_lo: int, v_hi: int):
+        _call("shk_cuda_model_set_tp_rows", self.h, o_lo, o_hi, v_lo, v_hi)
 
     def forward_layer(self, lv: LayerDesc, layer, pos, hidden_dev, stream=None):
         _call("shk_cuda_forward_layer", self.h, C.byref(lv), layer, pos, hidden_dev, stream)

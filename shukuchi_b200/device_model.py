@@ -66,11 +66,15 @@ def upload(model: Model, device: str | torch.device = "cuda:0") -> Uploaded:
 class GpuDecoder:
     """A DeviceModel + KV cache for a synthetic model, ready for token steps."""
 
-    def __init__(self, ctx: sc.Context, model: Model, max_seq: int, device="cuda:0"):
+    def __init__(self, ctx: sc.Context, model: Model, max_seq: int, device="cuda:0", tp_rows=None):
+        """tp_rows: (o_lo, o_hi, v_lo, v_hi) of a tensor-parallel rank whose
+        context has joined its group (the model is that rank's shard)."""
         s = model.shape
         self.up = upload(model, device)
         self.kv = sc.KvCache(ctx, s.n_layers, s.n_kv_heads, s.head_dim, max_seq)
         self.m = sc.DeviceModel(ctx, self.kv, self.up.desc)
+        if tp_rows is not None:
+            self.m.set_tp_rows(*tp_rows)
         for i, lv in enumerate(self.up.layers):
             self.m.set_layer(i, lv)
 

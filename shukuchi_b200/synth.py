@@ -74,10 +74,11 @@ class ModelShape:
     t_down: int = T_Q6K
     t_embd: int = T_Q4K
     t_out: int = T_Q6K
+    hd: int = 0  # head dimension when n_heads * head_dim != n_embd (a tensor-parallel rank)
 
     @property
     def head_dim(self) -> int:
-        return self.n_embd // self.n_heads
+        return self.hd or self.n_embd // self.n_heads
 
 
 SHAPES = {

@@ -53,9 +53,13 @@ class DeviceWeights:
 
 
 def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
-                      distinct_layers: int | None = None) -> DeviceWeights:
+                      distinct_layers: int | None = None, o_rows: int | None = None,
+                      out_rows: int | None = None) -> DeviceWeights:
     """All weights in HBM.  distinct_layers < n_layers reuses layer buffers
-    cyclically (only for smoke-sized runs; the benchmark uses distinct layers)."""
+    cyclically (only for smoke-sized runs; the benchmark uses distinct layers).
+    o_rows / out_rows: rows of the O projection and of the output head when
+    they differ from n_embd / n_vocab (a tensor-parallel rank's shard, whose
+    `shape` is the local one of shukuchi_b200.tp.local_shape)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     keep: list = []
@@ -70,7 +74,7 @@ def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
         q, _ = _matrix(s.t_q, s.n_heads * hd, s.n_embd, device, gen, keep)
         k, _ = _matrix(s.t_k, s.n_kv_heads * hd, s.n_embd, device, gen, keep)
         v, sv = _matrix(s.t_v, s.n_kv_heads * hd, s.n_embd, device, gen, keep)
-        o, _ = _matrix(s.t_o, s.n_embd, s.n_heads * hd, device, gen, keep)
+        o, _ = _matrix(s.t_o, o_rows or s.n_embd, s.n_heads * hd, device, gen, keep)
         g, _ = _matrix(s.t_gate, s.n_ff, s.n_embd, device, gen, keep)
         u, _ = _matrix(s.t_up, s.n_ff, s.n_embd, device, gen, keep)
         dn, sd = _matrix(s.t_down, s.n_embd, s.n_ff, device, gen, keep)
@@ -78,7 +82,7 @@ def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
                                  s.t_q, s.t_k, s.t_v, s.t_o, s.t_gate, s.t_up, s.t_down, sv, sd))
     layers = [made[i % nd] for i in range(s.n_layers)]
     te, _ = _matrix(s.t_embd, s.n_vocab, s.n_embd, device, gen, keep)
-    out, so = _matrix(s.t_out, s.n_vocab, s.n_embd, device, gen, keep)
+    out, so = _matrix(s.t_out, out_rows or s.n_vocab, s.n_embd, device, gen, keep)
     assert so == 0, "output head rows must be 16-byte multiples"
     desc = sc.ModelDesc(s.n_layers, s.n_embd, s.n_heads, s.n_kv_heads, hd, s.n_ff, s.n_vocab, 0.0,
                         te, s.t_embd, out, s.t_out)

@@ -232,6 +232,15 @@ int shk_cuda_layer_wait(shk_ctx *ctx, uint32_t slot, void *stream);
  * queued on `stream` so far -- the kernels that read the slot's old layer. */
 int shk_cuda_layer_release(shk_ctx *ctx, uint32_t slot, void *stream);
 
+/* ---- failure detection.  No counterpart in the reference (its only device
+ *      path is synchronous Metal).  Every device wait in this library is
+ *      bounded; on expiry the kernel records a timeout and returns, and the
+ *      next status check reports SHK_ETIMEOUT.  This launches one wait that
+ *      nothing satisfies (an mbarrier that never completes) with a budget of
+ *      budget_us microseconds (at most 1 s): it returns SHK_ETIMEOUT and the
+ *      context stays usable. ---- */
+int shk_cuda_selftest_wait_timeout(shk_ctx *ctx, uint32_t budget_us);
+
 /* ---- tensor parallelism over the GPUs of one node: NCCL all-reduce over
  *      NVLink after the O and down projections (north-star TP layout: Wq/Wk/Wv/
  *      gate/up split by output rows, Wo/down by input columns, KV heads local

@@ -81,13 +81,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // The clock is read once per 32 polls and each unsuccessful poll backs off
 // briefly, so waiting warps leave the issue slots to the working ones.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
-                                                  int code) {
+                                                  int code, uint64_t budget_ns = WAIT_BUDGET_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     __nanosleep(32);
-    if ((n & 31) == 0 && globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
+    if ((n & 31) == 0 && globaltimer_ns() - t0 > budget_ns) {
       set_error(err, code);
       return false;
     }

@@ -130,6 +130,21 @@ __global__ void swiglu_kernel(const float* g, const float* u, float* h, uint32_t
   }
 }
 
+// A wait that nothing satisfies: an mbarrier that never completes, waited on
+// with the same bounded wait as the GEMV ring (budget_ns instead of 1 s).  It
+// must end with DERR_TIMEOUT_FULL in the error word and leave the context
+// usable.
+__global__ void wait_selftest_kernel(int* err, uint64_t budget_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_bounded(&bar, 0, err, DERR_TIMEOUT_FULL, budget_ns);
+  __syncthreads();
+}
+
 __global__ void add_kernel(float* y, const float* x, uint32_t n) {
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     y[i] = y[i] + x[i];
@@ -158,6 +173,11 @@ cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* p
 cudaError_t argmax_ranks_launch(const uint32_t* pairs, int world, uint32_t* tok_out, uint32_t* pos_inc,
                                 cudaStream_t st) {
   return launch_k(argmax_ranks_kernel, dim3(1), dim3(32), 0, st, pairs, world, tok_out, pos_inc);
+}
+
+cudaError_t wait_selftest_launch(int* err, uint64_t budget_ns, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(err, budget_ns);
+  return cudaGetLastError();
 }
 
 bool& pdl_enabled() {

@@ -23,5 +23,7 @@ cudaError_t rope_launch(float* qk, uint32_t n_heads, uint32_t hd, const uint32_t
 void rope_freq_table(float theta, uint32_t head_dim, float* out);
 cudaError_t swiglu_launch(const float* g, const float* u, float* h, uint32_t n, cudaStream_t st);
 cudaError_t add_launch(float* y, const float* x, uint32_t n, cudaStream_t st);
+// One bounded wait on an mbarrier that never completes (test of the timeout path).
+cudaError_t wait_selftest_launch(int* err, uint64_t budget_ns, cudaStream_t st);
 
 }  // namespace shk

@@ -1045,6 +1045,12 @@ int shk_cuda_decode_steps(shk_model* m, uint32_t first_token, uint32_t first_pos
   return SHK_OK;
 }
 
+int shk_cuda_selftest_wait_timeout(shk_ctx* c, uint32_t budget_us) {
+  if (!c || budget_us == 0 || budget_us > 1000000u) return SHK_EINVAL;
+  CK(wait_selftest_launch(c->d_err, 1000ull * budget_us, c->compute));
+  return ctx_err_check(c);
+}
+
 int shk_cuda_tp_unique_id(void* out, size_t cap) {
   if (!out || cap < sizeof(ncclUniqueId)) return SHK_EINVAL;
   if (!nccl()) return SHK_EUNSUPPORTED;

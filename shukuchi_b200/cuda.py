@@ -83,6 +83,7 @@ _SIGS = {
     "shk_cuda_embed": (I, [P, P, U32, U32, U32, P, U32, P]),
     "shk_cuda_argmax": (I, [P, P, U32, C.POINTER(U32)]),
     "shk_cuda_argmax_noalloc": (I, [P, U32, P, P]),
+    "shk_cuda_selftest_wait_timeout": (I, [P, U32]),
     "shk_cuda_tp_unique_id": (I, [P, SZ]),
     "shk_cuda_tp_init": (I, [P, I, I, P]),
     "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),

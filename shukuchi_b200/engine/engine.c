@@ -20,6 +20,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include <sys/resource.h>
+#include <sys/stat.h>
 #include <unistd.h>
 
 #include "../../include/shk_cuda.h"
@@ -119,6 +120,12 @@ static int map_model(struct engine_handle *h) {
     if (!out || !emb || out->n_dims != 2 || emb->n_dims != 2) return -1;
     if (!h->n_vocab) h->n_vocab = (uint32_t)out->dims[1];
     if (out->dims[1] != h->n_vocab || out->dims[0] != h->n_embd) return -1;
+    /* every tensor must lie inside the file: a truncated file is rejected
+     * here instead of by a short read in the middle of a generation */
+    struct stat sb;
+    if (fstat(g->fd, &sb) != 0) return -1;
+    for (uint64_t i = 0; i < g->n_tensors; ++i)
+        if (g->tensors[i].offset + g->tensors[i].size > (uint64_t)sb.st_size) return -1;
     h->lm = (struct layer_map *)calloc(h->n_layers, sizeof(struct layer_map));
     if (!h->lm) return -1;
     char name[96];

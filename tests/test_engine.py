@@ -119,3 +119,25 @@ def test_engine_text_prompt_matches_reference_cli(model_file, reference):
     # token matches, so it becomes token 0 (the reference's unknown-byte rule)
     ids, _, _ = reference.generate_file(p, np.array([3, 141, 0, 0, 0, 59], np.uint32), 5, m.shape.n_vocab)
     assert text == "".join(f"<{i}>t{i:05d}" for i in ids)
+
+
+def test_inspect_rejects_broken_files(model_file, tmp_path):
+    """Host-side failures (no GPU): a truncated file, a missing layer tensor
+    and a file that is not GGUF are refused at open time with -1."""
+    m, p = model_file
+    data = open(p, "rb").read()
+    out = (C.c_uint32 * 6)()
+    mx = C.c_uint64()
+    L = lib()
+    cut = tmp_path / "cut.gguf"
+    cut.write_bytes(data[: len(data) - 1000])
+    assert L.engine_inspect(str(cut).encode(), out, C.byref(mx)) != 0
+    name = b"blk.1.ffn_down.weight"
+    assert data.count(name) == 1
+    miss = tmp_path / "missing.gguf"
+    miss.write_bytes(data.replace(name, b"blk.1.ffn_dowX.weight"))
+    assert L.engine_inspect(str(miss).encode(), out, C.byref(mx)) != 0
+    junk = tmp_path / "junk.gguf"
+    junk.write_bytes(b"GGUX" + data[4:4096])
+    assert L.engine_inspect(str(junk).encode(), out, C.byref(mx)) != 0
+    assert L.engine_inspect(p.encode(), out, C.byref(mx)) == 0

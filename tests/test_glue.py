@@ -82,3 +82,25 @@ def test_swiglu(oracle, ctx):
     ctx.swiglu(gd.data_ptr(), ud.data_ptr(), h.data_ptr(), 5000)
     torch.cuda.synchronize()
     np.testing.assert_allclose(h.cpu().numpy(), oracle.swiglu(g, u), rtol=2e-6, atol=1e-6)
+
+
+def test_bounded_wait_times_out_and_context_survives(oracle, ctx):
+    """A device wait that nothing satisfies ends after its budget with
+    SHK_ETIMEOUT (no hang, no trap); the same context then runs a GEMV."""
+    import time
+
+    from shukuchi_b200 import cuda as sc
+    t0 = time.monotonic()
+    rc = sc.lib().shk_cuda_selftest_wait_timeout(ctx.h, 20000)  # 20 ms
+    assert time.monotonic() - t0 < 10.0
+    assert rc == -5  # SHK_ETIMEOUT
+    ctx.check()  # error word was cleared by the report
+    rng = np.random.default_rng(2)
+    w = synth.quant_matrix(rng, 12, 64, 512)
+    x = rng.standard_normal(512).astype(np.float32)
+    y = torch.zeros(64, device="cuda")
+    wd, xd = to_dev(w), to_dev(x)
+    ctx.matmul(12, wd.data_ptr(), xd.data_ptr(), y.data_ptr(), 64, 512)
+    torch.cuda.synchronize()
+    ref = oracle.matvec(12, w, x, 64, 512)
+    assert np.allclose(y.cpu().numpy(), ref, rtol=1e-4, atol=1e-4)

@@ -256,7 +256,7 @@ def run_ours(args, ws, rank, local):
         dist.broadcast_object_list(obj, src=0)
         ctx.tp_init(rank, ws, obj[0])
     wts = make_device_model(lshape, seed=1234 + rank, device=f"cuda:{local}",
-                            o_rows=lay.o_hi - lay.o_lo, out_rows=lay.v_hi - lay.v_lo)
+                            o_rows=lay.o_hi - lay.o_lo, out_rows=lay.v_hi - lay.v_lo, ctx=ctx)
     total = args.prompt + 2 * (args.warmup + args.steps) + 8
     kv = sc.KvCache(ctx, lshape.n_layers, lshape.n_kv_heads, lshape.head_dim, total)
     m = sc.DeviceModel(ctx, kv, wts.desc)

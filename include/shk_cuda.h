@@ -90,6 +90,27 @@ int shk_cuda_matmul_q4k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev,
                             uint32_t m, uint32_t k, void *stream);
 int shk_cuda_matmul_q6k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev, float *y_dev,
                             uint32_t m, uint32_t k, void *stream);
+
+/* ---- Q6_K weight layout in HBM.  No counterpart in the reference (its
+ *      weights stay in the GGUF layout in host memory).  The staged GEMV reads
+ *      Q6_K rows in a planar layout: the same 210 * k/256 bytes of a row
+ *      regrouped as [ql of every block][qh][scales][d], each plane 16-byte
+ *      aligned, with the 16-byte chunks of a block rotated by the block index
+ *      (ql chunk c of block b at 128 b + 16 ((c + b) & 7), qh chunk c at
+ *      128 nb + 64 b + 16 ((c + (b >> 1)) & 3), scales at 192 nb + 16 b, d at
+ *      208 nb + 2 b).  Weights registered with a model as Q6_K must be in this
+ *      layout and carry dtype SHK_DTYPE_Q6_K_PLANAR (output head: GGUF Q6_K is
+ *      also accepted, on the plain-load kernel). ---- */
+#define SHK_DTYPE_Q6_K_PLANAR 0x10Eu
+/* Converts `rows` Q6_K rows of k elements, row_stride bytes apart (0 = 210 *
+ * k/256; must be a multiple of 16 and at most 227 KB), in place: to the
+ * planar layout (to_planar != 0) or back to GGUF blocks.  Async on stream. */
+int shk_cuda_q6k_repack(shk_ctx *ctx, void *w_dev, uint32_t rows, uint32_t k, uint32_t row_stride,
+                        int to_planar, void *stream);
+/* dequantise-matvec by dtype: 12 (Q4_K), 14 (GGUF Q6_K) or
+ * SHK_DTYPE_Q6_K_PLANAR; row_stride 0 = dense rows. */
+int shk_cuda_matvec(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
+                    const float *x_dev, float *y_dev, uint32_t m, uint32_t k, void *stream);
 /* Same contract as metal_matmul_q{4,6}k_vec: HOST weights/x/y, synchronous
  * (copies in, computes, copies out).  For callers that keep the reference's
  * host-resident layer buffers unchanged. */
@@ -220,6 +241,12 @@ int shk_cuda_layer_stage(shk_ctx *ctx, uint32_t slot, void *dst_dev, const void 
  * (pads Q6_K rows to 16-byte multiples). */
 int shk_cuda_layer_stage_rows(shk_ctx *ctx, uint32_t slot, void *dst_dev, size_t dst_row_bytes,
                               const void *pinned_src, size_t src_row_bytes, size_t rows);
+/* Converts Q6_K rows just staged into dst_dev (rows x k elements, row_stride
+ * bytes apart, 0 = dense) to the planar layout, in place, on the copy stream
+ * after the slot's copies; the slot's commit covers it.  Callable from the
+ * loader thread.  No counterpart in the reference. */
+int shk_cuda_layer_stage_q6k_planar(shk_ctx *ctx, uint32_t slot, void *dst_dev, uint32_t rows, uint32_t k,
+                                    uint32_t row_stride);
 /* Marks the end of a slot's staging sequence (records its event). */
 int shk_cuda_layer_commit(shk_ctx *ctx, uint32_t slot);
 /* 1 if the slot's copies completed, 0 if still in flight (wait = 0), or block

@@ -15,6 +15,7 @@ constexpr int Q6K_BYTES = 210;
 constexpr int Q8_BYTES = 36;  // reference KV block {float scale; int8 q[32]}
 constexpr int T_Q4K = 12;
 constexpr int T_Q6K = 14;
+constexpr int T_Q6K_PLANAR = 0x10E;  // Q6_K rows in the planar layout of repack.cu
 
 // Device error codes written to the context's error word (first error wins).
 constexpr int DERR_TIMEOUT_FULL = 1;   // consumer gave up waiting for a TMA stage

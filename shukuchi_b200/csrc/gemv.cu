@@ -151,7 +151,9 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
   for (int i = 0; i < nmats; ++i) {
     const GemvMat& mt = mats[i];
     GemvSeg& g = a.seg[i];
-    if (mt.qt != T_Q4K && mt.qt != T_Q6K) return -2;
+    // the staged kernel reads Q4_K and planar Q6_K (GGUF-layout Q6_K goes
+    // through repack.cu or the plain-load kernel)
+    if (mt.qt != T_Q4K && mt.qt != T_Q6K_PLANAR) return -2;
     const uint32_t bb = mt.qt == T_Q4K ? Q4K_BYTES : Q6K_BYTES;
     g.w = static_cast<const uint8_t*>(mt.w);
     g.w2 = static_cast<const uint8_t*>(mt.w2);
@@ -162,7 +164,7 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     if (g.row_stride % 16 || g.row_stride < nb * bb) return -3;
     if ((reinterpret_cast<uintptr_t>(g.w) & 15) || (g.w2 && (reinterpret_cast<uintptr_t>(g.w2) & 15)))
       return -3;
-    g.qt = (uint8_t)mt.qt;
+    g.qt = (uint8_t)(mt.qt == T_Q4K ? T_Q4K : T_Q6K);
     g.epi = mt.epi;
     g.dual = mt.w2 ? 1 : 0;
     if (g.dual != (mt.epi == EPI_SWIGLU)) return -1;
@@ -172,14 +174,12 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     // rl: output rows per lane group (2 rows, or 1 row / one gate-up pair).
     uint32_t rg = 1;
     const uint32_t mats_per_row = g.dual ? 2 : 1;
-    if (mt.qt == T_Q4K) {
-      p.has4 = 1;  // a lane per block: 32 block slots per warp
-      while (rg * 2 <= 32 && rg * 2 * nb <= 32) rg *= 2;
-    } else {
-      p.has6 = 1;  // a lane per half block, blocks walked by parity: 16 slots
-      const uint32_t nbc = (nb + 1) / 2;
-      while (rg * 2 <= 16 && rg * 2 * nbc <= 16) rg *= 2;
-    }
+    // a lane per block: 32 block slots per warp
+    if (mt.qt == T_Q4K)
+      p.has4 = 1;
+    else
+      p.has6 = 1;
+    while (rg * 2 <= 32 && rg * 2 * nb <= 32) rg *= 2;
     // Rows beyond 40 KB per task pair: one row per lane group (Q6_K has a
     // single-row body; for Q4_K the second row pointer repeats the first).
     uint32_t rl = g.dual ? 1 : 2;

@@ -29,7 +29,7 @@ struct GemvSeg {
   uint32_t chunk_rows;  // rows per pipeline stage (multiple of rg * rl)
   uint32_t unit_cost;   // bytes per task unit of rg * rl rows (both matrices for dual)
   uint32_t rope_hd;     // head_dim for EPI_ROPE
-  uint8_t qt;           // 12 = Q4_K, 14 = Q6_K
+  uint8_t qt;           // 12 = Q4_K, 14 = Q6_K (planar layout, repack.cu)
   uint8_t epi;          // GemvEpi
   uint8_t rg;           // row groups per warp task (lanes split across groups)
   uint8_t rl;           // rows per lane (each loaded x value feeds rl rows)
@@ -80,8 +80,13 @@ size_t gemv_x_region_bytes(uint32_t K, bool has4, bool has6);
 cudaError_t gemv_init();
 cudaError_t gemv_launch(const GemvPlan& p, cudaStream_t stream);
 
+// Q6_K rows, in place, between the GGUF block layout and the planar layout the
+// staged kernel reads (repack.cu).  stride: row bytes, a multiple of 16.
+cudaError_t q6k_repack_launch(void* w, uint32_t rows, uint32_t k, uint32_t stride, bool to_planar,
+                              int num_sms, cudaStream_t st);
+
 // Simple fallback for layouts the staged kernel does not take (rows not a
-// multiple of 16 bytes).  Same math, plain loads.
+// multiple of 16 bytes; GGUF-layout Q6_K).  Same math, plain loads.
 cudaError_t gemv_generic_launch(uint32_t qt, const void* w, const float* x, float* y, uint32_t m,
                                 uint32_t k, cudaStream_t stream);
 

@@ -39,6 +39,16 @@
 #include "common.cuh"
 #include "gemv.cuh"
 
+// Unroll factors of the per-block inner loops (1: rolled, compact code).
+#ifndef SHK_Q4_JU
+#define SHK_Q4_JU 1
+#endif
+#ifndef SHK_Q6_ISU
+#define SHK_Q6_ISU 1
+#endif
+#define SHK_PRAGMA(x) _Pragma(#x)
+#define SHK_UNROLL(n) SHK_PRAGMA(unroll n)
+
 namespace shk {
 namespace gdev {
 
@@ -104,7 +114,7 @@ __device__ __forceinline__ void q4k_block2(const uint8_t* __restrict__ r0, const
   }
   int A[2][3] = {{0, 0, 0}, {0, 0, 0}};
   float M[2] = {0.f, 0.f};
-#pragma unroll 1
+SHK_UNROLL(SHK_Q4_JU)
   for (int j = 0; j < 4; ++j) {
     int S[2][2][3] = {{{0, 0, 0}, {0, 0, 0}}, {{0, 0, 0}, {0, 0, 0}}};
 #pragma unroll
@@ -149,101 +159,92 @@ __device__ __forceinline__ void q4k_block2(const uint8_t* __restrict__ r0, const
 }
 
 // ------------------------------- Q6_K ---------------------------------------
-// Words of a Q6_K block at byte offset off from p.  Blocks are 210 bytes and
-// rows 16-byte aligned, so a block starts 2 bytes past a word boundary when
-// its index is odd (P = 1): read the enclosing words and shift.
-template <int P, int NW>
-__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&o)[NW]) {
-  if (P == 0) {
-    const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
-#pragma unroll
-    for (int i = 0; i < NW; ++i) o[i] = q[i];
-  } else {
-    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - 2);
-    uint32_t prev = q[0];
-#pragma unroll
-    for (int i = 0; i < NW; ++i) {
-      const uint32_t nx = q[i + 1];
-      o[i] = __byte_perm(prev, nx, 0x5432);
-      prev = nx;
-    }
-  }
+// Rows are in the planar layout of repack.cu: block b's ql chunk c (16 bytes)
+// at 128 b + 16 ((c + b) & 7), qh chunk c at 128 nb + 64 b + 16 ((c + (b >> 1))
+// & 3), scales at 192 nb + 16 b, d at 208 nb + 2 b -- every load is an aligned
+// vector load, and lanes on consecutive blocks hit distinct bank groups.
+__device__ __forceinline__ uint32_t w4(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-// Half n (128 elements) of one Q6_K block for two rows (engine/src/ops.c:167-193
-// dequantize_row_q6_k).  For each 32-bit word i of ql/qh, four words of exact
-// 6-bit quants are formed (element groups +0, +32, +64, +96) and fed to dp4a;
-// each 16-element scale group's three limb sums start at -32 * (sum of x
-// limbs), which applies the -32 offset.  The two 16-element halves `is` of the
-// 32-element groups run in a rolled loop, each loading only its own words.
-// NR = 2 rows (b0, b1) or NR = 1 (b0 only; rows of very long K, so that a
-// task and a pipeline stage stay small).
-template <int P, int NR>
-__device__ __forceinline__ void q6k_half(const uint8_t* __restrict__ b0, const uint8_t* __restrict__ b1,
-                                         int n, const int4* __restrict__ xh,
-                                         const int4* __restrict__ xi, float xb, float& acc0,
-                                         float& acc1) {
+// One Q6_K block (both 128-element halves n) of NR rows (engine/src/ops.c:
+// 167-193 dequantize_row_q6_k).  For each 32-bit word i of ql/qh, four words
+// of exact 6-bit quants are formed (element groups +0, +32, +64, +96) and fed
+// to dp4a; each 16-element scale group's three limb sums start at -32 * (sum
+// of x limbs), which applies the -32 offset.  |T| < 16 groups * 2^19 * 128 <
+// 2^31.  NR = 2 rows (r0, r1) or NR = 1 (r0 only).
+template <int NR>
+__device__ __forceinline__ void q6k_block(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
+                                          uint32_t nb, uint32_t b, const int4* __restrict__ xblk,
+                                          const int4* __restrict__ xib, float xb, float& acc0,
+                                          float& acc1) {
   const uint32_t MK = 0x0F0F0F0Fu;
-  const uint8_t* bp[2] = {b0, b1};
-  uint32_t SC[NR][2];
+  const uint8_t* rp[2] = {r0, r1};
+  const uint32_t qlb = 128u * b, qhb = 128u * nb + 64u * b, scb = 192u * nb + 16u * b;
+  const uint32_t rq = b & 7u, rh = (b >> 1) & 3u;
   float dd[NR];
 #pragma unroll
-  for (int r = 0; r < NR; ++r) {
-    load_words<P, 2>(bp[r] + 192 + 8 * n, SC[r]);
-    dd[r] = ref_half(*reinterpret_cast<const uint16_t*>(bp[r] + 208)) * xb;
-  }
+  for (int r = 0; r < NR; ++r) dd[r] = ref_half(*reinterpret_cast<const uint16_t*>(rp[r] + 208u * nb + 2u * b)) * xb;
   int T[NR][3];
 #pragma unroll
   for (int r = 0; r < NR; ++r) T[r][0] = T[r][1] = T[r][2] = 0;
 #pragma unroll 1
-  for (int is = 0; is < 2; ++is) {
-    uint32_t A[NR][4], B[NR][4], H[NR][4];
+  for (int n = 0; n < 2; ++n) {
+    uint2 SC[NR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      load_words<P, 4>(bp[r] + 64 * n + 16 * is, A[r]);
-      load_words<P, 4>(bp[r] + 64 * n + 32 + 16 * is, B[r]);
-      load_words<P, 4>(bp[r] + 128 + 32 * n + 16 * is, H[r]);
-    }
-    int S[NR][4][3];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int4 init = xi[2 * g + is];  // -32 * limb sums of this 16-group
+    for (int r = 0; r < NR; ++r) SC[r] = *reinterpret_cast<const uint2*>(rp[r] + scb + 8u * n);
+    const int4* xh = xblk + 33 * n;
+    const int4* xi = xib + 8 * n;
+SHK_UNROLL(SHK_Q6_ISU)
+    for (int is = 0; is < 2; ++is) {
+      uint4 A[NR], B[NR], H[NR];
 #pragma unroll
       for (int r = 0; r < NR; ++r) {
-        S[r][g][0] = init.x;
-        S[r][g][1] = init.y;
-        S[r][g][2] = init.z;
+        A[r] = *reinterpret_cast<const uint4*>(rp[r] + qlb + 16u * ((4u * n + is + rq) & 7u));
+        B[r] = *reinterpret_cast<const uint4*>(rp[r] + qlb + 16u * ((4u * n + 2u + is + rq) & 7u));
+        H[r] = *reinterpret_cast<const uint4*>(rp[r] + qhb + 16u * ((2u * n + is + rh) & 3u));
       }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      int4 xv[4];
-#pragma unroll
-      for (int g = 0; g < 4; ++g) xv[g] = xh[8 * g + 4 * is + i];
-#pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        const uint32_t h = H[r][i];
-        const uint32_t hm = h & 0x33333333u, hn = h & 0xCCCCCCCCu;
-        const uint32_t Q[4] = {lop_sel(A[r][i], hm << 4, MK), lop_sel(B[r][i], hn << 2, MK),
-                               lop_sel(A[r][i] >> 4, hm, MK), lop_sel(B[r][i] >> 4, hn >> 2, MK)};
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          S[r][g][0] = dp4a_u(Q[g], xv[g].x, S[r][g][0]);
-          S[r][g][1] = dp4a_u(Q[g], xv[g].y, S[r][g][1]);
-          S[r][g][2] = dp4a_us(Q[g], xv[g].z, S[r][g][2]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < NR; ++r)
+      int S[NR][4][3];
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const uint32_t si = (uint32_t)is + 2u * g;  // scale index within this half
-        const int sc = (int)(int8_t)__byte_perm(SC[r][g >> 1], 0u, 0x4440u + (si & 3u));
-        T[r][0] += sc * S[r][g][0];
-        T[r][1] += sc * S[r][g][1];
-        T[r][2] += sc * S[r][g][2];
+        const int4 init = xi[2 * g + is];  // -32 * limb sums of this 16-group
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          S[r][g][0] = init.x;
+          S[r][g][1] = init.y;
+          S[r][g][2] = init.z;
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int4 xv[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) xv[g] = xh[8 * g + 4 * is + i];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          const uint32_t h = w4(H[r], i), a = w4(A[r], i), bq = w4(B[r], i);
+          const uint32_t hm = h & 0x33333333u, hn = h & 0xCCCCCCCCu;
+          const uint32_t Q[4] = {lop_sel(a, hm << 4, MK), lop_sel(bq, hn << 2, MK), lop_sel(a >> 4, hm, MK),
+                                 lop_sel(bq >> 4, hn >> 2, MK)};
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            S[r][g][0] = dp4a_u(Q[g], xv[g].x, S[r][g][0]);
+            S[r][g][1] = dp4a_u(Q[g], xv[g].y, S[r][g][1]);
+            S[r][g][2] = dp4a_us(Q[g], xv[g].z, S[r][g][2]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NR; ++r)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t si = (uint32_t)is + 2u * g;  // scale index within this half
+          const int sc = (int)(int8_t)__byte_perm(g < 2 ? SC[r].x : SC[r].y, 0u, 0x4440u + (si & 3u));
+          T[r][0] += sc * S[r][g][0];
+          T[r][1] += sc * S[r][g][1];
+          T[r][2] += sc * S[r][g][2];
+        }
+    }
   }
   acc0 = fmaf(dd[0], limbs_to_float(T[0][0], T[0][1], T[0][2]), acc0);
   if (NR == 2) acc1 = fmaf(dd[NR - 1], limbs_to_float(T[NR - 1][0], T[NR - 1][1], T[NR - 1][2]), acc1);
@@ -301,16 +302,15 @@ struct XView {
   const int4* xq;     // padded limb vectors, K/4 (+ one pad vector per 256-block)
   const float* xbs;   // per-256-block scale X_b, K/256
   const float* xs32;  // Q4_K: fp32 sums of x per 32-element sub-block, K/32
-  const int4* xi16;   // Q6_K: -32 * limb sums per 16-element group, K/16
+  const int4* xi16;   // Q6_K: -32 * limb sums per 16-element group, 16 per block + 1 pad
 };
 
 // One task of a chunk: rg lane groups, each owning rl output rows (two row
 // pointers r0, r1 per lane: consecutive rows, gate/up rows, or r1 = r0 when a
 // single row is wanted).  Rows past rows_valid read stale (in-bounds) stage
 // bytes; their results are never stored.
-//  Q4_K: 32/rg lanes per group, a lane takes blocks s, s + 32/rg, ...
-//  Q6_K: 16/rg block slots per group, two lanes (halves n) per slot; blocks of
-//        even then odd index (their word alignments differ).
+//  32/rg lanes per group, a lane takes blocks s, s + 32/rg, ... (Q4_K and
+//  planar Q6_K alike).
 template <bool HAS4, bool HAS6>
 __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, const uint8_t* rows,
                                          uint32_t row0, int rows_valid, uint32_t dual_off,
@@ -318,10 +318,9 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
   const int lg_rg = __ffs(g.rg) - 1;
   const int rl = g.rl;
   const bool q4 = g.qt == T_Q4K;
-  const int spr = q4 ? (32 >> lg_rg) : (16 >> lg_rg);
-  const int slot = q4 ? lane : (lane >> 1), n = q4 ? 0 : (lane & 1);
-  const int grp = slot >> (q4 ? 5 - lg_rg : 4 - lg_rg);
-  const int s = slot & (spr - 1);
+  const int spr = 32 >> lg_rg;
+  const int grp = lane >> (5 - lg_rg);
+  const int s = lane & (spr - 1);
   float o0 = 0.f, o1 = 0.f;
   if (grp * rl < rows_valid) {
     const uint8_t* r0 = rows + (size_t)(grp * rl) * g.row_stride;
@@ -331,18 +330,13 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
         q4k_block2(r0 + (size_t)b * Q4K_BYTES, r1 + (size_t)b * Q4K_BYTES, x.xq + 65 * b, x.xbs[b],
                    x.xs32 + 8 * b, o0, o1);
     } else if (HAS6) {
-#define SHK_Q6(P, NR)                                                                          \
-  for (uint32_t b = 2 * s + P; b < g.nb; b += 2 * spr)                                         \
-    q6k_half<P, NR>(r0 + (size_t)b * Q6K_BYTES, r1 + (size_t)b * Q6K_BYTES, n,                 \
-                    x.xq + 65 * b + 33 * n, x.xi16 + 16 * b + 8 * n, x.xbs[b], o0, o1)
       if (rl == 1 && !g.dual) {  // single row
-        SHK_Q6(0, 1);
-        SHK_Q6(1, 1);
+        for (uint32_t b = s; b < g.nb; b += spr)
+          q6k_block<1>(r0, r1, g.nb, b, x.xq + 65 * b, x.xi16 + 17 * b, x.xbs[b], o0, o1);
       } else {
-        SHK_Q6(0, 2);
-        SHK_Q6(1, 2);
+        for (uint32_t b = s; b < g.nb; b += spr)
+          q6k_block<2>(r0, r1, g.nb, b, x.xq + 65 * b, x.xi16 + 17 * b, x.xbs[b], o0, o1);
       }
-#undef SHK_Q6
     }
   }
   for (int o = 16 >> lg_rg; o > 0; o >>= 1) {
@@ -355,7 +349,7 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
 }
 
 // Shared-memory map: [full | empty | xbar barriers][done][gen][red]
-// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)][xi16 (K*1, Q6_K)]
+// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)][xi16 (17 int4 per block, Q6_K)]
 // [stage ring].  The producer first bulk-copies x into the limb-vector slot;
 // consumers turn it into limbs in place.
 constexpr int SMEM_HDR = 8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES + 4 * 32;
@@ -389,7 +383,7 @@ __host__ __device__ __forceinline__ size_t xq_bytes(uint32_t K) {
 __host__ __device__ __forceinline__ size_t x_region_bytes(uint32_t K, bool has4, bool has6) {
   size_t b = xq_bytes(K) + (size_t)xbs_floats(K) * 4;
   if (has4) b += (size_t)(K / 32) * 4;
-  if (has6) b += (size_t)K;  // int4 per 16 elements
+  if (has6) b += (size_t)(K / 256) * 17 * 16;  // int4 per 16 elements + one pad per block
   return b;
 }
 
@@ -645,7 +639,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
-        if ((lane & 1) == 0) xi16[16 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
+        if ((lane & 1) == 0) xi16[17 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
       }
     }
   }

@@ -84,6 +84,8 @@ struct shk_ctx {
   // synchronous host-pointer matvec scratch
   void* hv_w = nullptr;
   size_t hv_w_cap = 0;
+  void* q6_scratch = nullptr;  // GGUF-layout Q6_K rows repacked for the staged GEMV
+  size_t q6_scratch_cap = 0;
   float* hv_x = nullptr;
   size_t hv_x_cap = 0;
   float* hv_y = nullptr;
@@ -171,25 +173,6 @@ int ctx_err_check(shk_ctx* c) {
 
 cudaStream_t pick(shk_ctx* c, void* s) { return s ? static_cast<cudaStream_t>(s) : c->compute; }
 
-int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y, uint32_t m,
-               uint32_t k, cudaStream_t st) {
-  if (!w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
-  if (m == 0) return SHK_OK;
-  GemvMat mt{w, nullptr, y, m, qt, 0, EPI_STORE, 0};
-  GemvPlan p;
-  const int rc = gemv_plan(p, &mt, 1, k, x, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
-  if (rc == -2) return SHK_EUNSUPPORTED;
-  if (rc == 0) {
-    CK(gemv_launch(p, st));
-  } else {
-    // rows not 16-byte multiples, unaligned base, or too large for the staged
-    // kernel: plain-load kernel with the same math
-    CK(gemv_generic_launch(qt, w, x, y, m, k, st));
-  }
-  c->n_matvec++;
-  return SHK_OK;
-}
-
 template <typename T>
 int grow(T** p, size_t* cap, size_t need) {
   if (*cap >= need) return SHK_OK;
@@ -198,6 +181,41 @@ int grow(T** p, size_t* cap, size_t need) {
   *cap = 0;
   if (cudaMalloc(reinterpret_cast<void**>(p), need) != cudaSuccess) return SHK_ENOMEM;
   *cap = need;
+  return SHK_OK;
+}
+
+// qt: T_Q4K, T_Q6K (GGUF layout) or T_Q6K_PLANAR; row_stride 0 = dense rows.
+int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, uint32_t row_stride, const float* x, float* y,
+               uint32_t m, uint32_t k, cudaStream_t st) {
+  if (!w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
+  if (qt != T_Q4K && qt != T_Q6K && qt != T_Q6K_PLANAR) return SHK_EUNSUPPORTED;
+  if (m == 0) return SHK_OK;
+  const uint32_t nb = k / QK;
+  if (qt == T_Q6K && !row_stride) {
+    // GGUF-layout rows: copy into padded rows of a scratch buffer, repack
+    // there, then the staged kernel (its weights must be planar)
+    const uint32_t stride = (210u * nb + 15u) & ~15u;
+    if (stride <= 227u * 1024u) {
+      int rc = grow(&c->q6_scratch, &c->q6_scratch_cap, (size_t)m * stride);
+      if (rc) return rc;
+      CK(cudaMemcpy2DAsync(c->q6_scratch, stride, w, 210u * nb, 210u * nb, m, cudaMemcpyDeviceToDevice, st));
+      CK(q6k_repack_launch(c->q6_scratch, m, k, stride, true, c->num_sms, st));
+      return matvec_dev(c, T_Q6K_PLANAR, c->q6_scratch, stride, x, y, m, k, st);
+    }
+  }
+  GemvMat mt{w, nullptr, y, m, qt, row_stride, EPI_STORE, 0};
+  GemvPlan p;
+  const int rc = gemv_plan(p, &mt, 1, k, x, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
+  if (rc == 0) {
+    CK(gemv_launch(p, st));
+  } else if (qt != T_Q6K_PLANAR && !row_stride) {
+    // rows not 16-byte multiples, unaligned base, or too large for the staged
+    // kernel: plain-load kernel with the same math
+    CK(gemv_generic_launch(qt, w, x, y, m, k, st));
+  } else {
+    return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  }
+  c->n_matvec++;
   return SHK_OK;
 }
 
@@ -211,7 +229,7 @@ int matvec_host(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y
     return rc;
   CK(cudaMemcpyAsync(c->hv_w, w, wb, cudaMemcpyHostToDevice, c->compute));
   CK(cudaMemcpyAsync(c->hv_x, x, (size_t)k * 4, cudaMemcpyHostToDevice, c->compute));
-  rc = matvec_dev(c, qt, c->hv_w, c->hv_x, c->hv_y, m, k, c->compute);
+  rc = matvec_dev(c, qt, c->hv_w, 0, c->hv_x, c->hv_y, m, k, c->compute);
   if (rc) return rc;
   CK(cudaMemcpyAsync(y, c->hv_y, (size_t)m * 4, cudaMemcpyDeviceToHost, c->compute));
   CK(cudaStreamSynchronize(c->compute));
@@ -295,6 +313,7 @@ void shk_cuda_shutdown(shk_ctx* c) {
   cudaFree(c->d_freq);
   cudaFreeHost(c->h_freq);
   cudaFree(c->hv_w);
+  cudaFree(c->q6_scratch);
   cudaFree(c->hv_x);
   cudaFree(c->hv_y);
   if (c->compute) cudaStreamDestroy(c->compute);
@@ -358,12 +377,26 @@ int shk_cuda_sync(shk_ctx* c, void* s) {
 int shk_cuda_matmul_q4k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                             uint32_t k, void* s) {
   if (!c) return SHK_EINVAL;
-  return matvec_dev(c, T_Q4K, w, x, y, m, k, pick(c, s));
+  return matvec_dev(c, T_Q4K, w, 0, x, y, m, k, pick(c, s));
 }
 int shk_cuda_matmul_q6k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                             uint32_t k, void* s) {
   if (!c) return SHK_EINVAL;
-  return matvec_dev(c, T_Q6K, w, x, y, m, k, pick(c, s));
+  return matvec_dev(c, T_Q6K, w, 0, x, y, m, k, pick(c, s));
+}
+int shk_cuda_matvec(shk_ctx* c, uint32_t dtype, const void* w, uint32_t row_stride, const float* x, float* y,
+                    uint32_t m, uint32_t k, void* s) {
+  if (!c) return SHK_EINVAL;
+  return matvec_dev(c, dtype, w, row_stride, x, y, m, k, pick(c, s));
+}
+int shk_cuda_q6k_repack(shk_ctx* c, void* w, uint32_t rows, uint32_t k, uint32_t row_stride, int to_planar,
+                        void* s) {
+  if (!c || !w || k == 0 || k % QK) return SHK_EINVAL;
+  const uint32_t stride = row_stride ? row_stride : 210u * (k / QK);
+  if (stride % 16 || stride < 210u * (k / QK) || stride > 227u * 1024u || (reinterpret_cast<uintptr_t>(w) & 15))
+    return SHK_EINVAL;
+  CK(q6k_repack_launch(w, rows, k, stride, to_planar != 0, c->num_sms, pick(c, s)));
+  return SHK_OK;
 }
 int shk_cuda_matmul_q4k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                                  uint32_t k) {
@@ -645,6 +678,13 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
   return SHK_OK;
 }
 
+// The output head runs staged (plan 0) or, for Q4_K / GGUF-layout Q6_K, on the
+// plain-load kernel; a planar head must plan.
+bool head_plan_ok(uint32_t dtype, int hp) {
+  if (hp == 0) return true;
+  return dtype == T_Q4K ? hp != -2 : dtype == T_Q6K;
+}
+
 bool vocab_split(const shk_model* m) { return m->v_hi - m->v_lo < m->d.n_vocab; }
 
 // Tensor parallel with a split output head: every rank's logits slice is
@@ -888,7 +928,8 @@ shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv
   GemvMat hm{d->output_dev, nullptr, m->logits, d->n_vocab, d->output_dtype, 0, EPI_STORE, 0};
   const int hp = gemv_plan(m->head, &hm, 1, d->n_embd, m->hidden, nullptr, nullptr, nullptr,
                            c->d_err, c->num_sms);
-  if (hp == -2 || d->n_embd % QK) {  // unsupported dtype
+  // GGUF-layout Q6_K (or rows the staged kernel cannot take): plain-load GEMV
+  if (d->n_embd % QK || !head_plan_ok(d->output_dtype, hp)) {
     shk_cuda_model_destroy(m);
     return nullptr;
   }
@@ -1092,7 +1133,7 @@ int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint3
   GemvMat hm{m->d.output_dev, nullptr, m->logits + v_lo, nv, m->d.output_dtype, 0, EPI_STORE, 0};
   const int hp = gemv_plan(m->head, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err,
                            c->num_sms);
-  if (hp == -2) return SHK_EUNSUPPORTED;
+  if (!head_plan_ok(m->d.output_dtype, hp)) return SHK_EUNSUPPORTED;
   m->head_generic = hp != 0;
   m->o_lo = o_lo;
   m->o_hi = o_hi;
@@ -1244,6 +1285,18 @@ int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_r
     c->n_staged++;
     c->bytes_staged += src_row * rows;
   }
+  return SHK_OK;
+}
+
+int shk_cuda_layer_stage_q6k_planar(shk_ctx* c, uint32_t slot, void* dst, uint32_t rows, uint32_t k,
+                                    uint32_t row_stride) {
+  if (!c || !dst || k == 0 || k % QK) return SHK_EINVAL;
+  (void)slot;  // same copy stream as the slot's copies: ordered after them, covered by its commit
+  const uint32_t stride = row_stride ? row_stride : 210u * (k / QK);
+  if (stride % 16 || stride < 210u * (k / QK) || stride > 227u * 1024u || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return SHK_EINVAL;
+  cudaSetDevice(c->device);
+  CK(q6k_repack_launch(dst, rows, k, stride, true, c->num_sms, c->copy));
   return SHK_OK;
 }
 

@@ -84,6 +84,9 @@ _SIGS = {
     "shk_cuda_argmax": (I, [P, P, U32, C.POINTER(U32)]),
     "shk_cuda_argmax_noalloc": (I, [P, U32, P, P]),
     "shk_cuda_selftest_wait_timeout": (I, [P, U32]),
+    "shk_cuda_q6k_repack": (I, [P, P, U32, U32, U32, I, P]),
+    "shk_cuda_layer_stage_q6k_planar": (I, [P, U32, P, U32, U32, U32]),
+    "shk_cuda_matvec": (I, [P, U32, P, U32, P, P, U32, U32, P]),
     "shk_cuda_tp_unique_id": (I, [P, SZ]),
     "shk_cuda_tp_init": (I, [P, I, I, P]),
     "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),
@@ -188,6 +191,15 @@ class Context:
     def report(self) -> None:
         lib().shk_cuda_report(self.h)
 
+    def q6k_repack(self, w_dev: int, rows: int, k: int, row_stride: int = 0, to_planar: bool = True,
+                   stream: int | None = None) -> None:
+        """Q6_K rows in place between the GGUF and the planar layout."""
+        _call("shk_cuda_q6k_repack", self.h, w_dev, rows, k, row_stride, 1 if to_planar else 0, stream)
+
+    def matvec(self, dtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int, row_stride: int = 0,
+               stream: int | None = None) -> None:
+        _call("shk_cuda_matvec", self.h, dtype, w_dev, row_stride, x_dev, y_dev, m, k, stream)
+
     def tp_init(self, rank: int, world: int, uid: bytes) -> None:
         """Joins this context to a tensor-parallel group of `world` ranks
         (one process or thread per GPU); uid comes from tp_unique_id() on rank 0."""
@@ -236,6 +248,9 @@ class Context:
 
     def layer_wait(self, slot, stream=None):
         _call("shk_cuda_layer_wait", self.h, slot, stream)
+
+
+DTYPE_Q6_K_PLANAR = 0x10E
 
 
 def tp_unique_id() -> bytes:

@@ -3,7 +3,10 @@
 Weights keep their GGUF block bytes.  Q6_K rows whose byte length is not a
 multiple of 16 (e.g. 22 blocks per row) are padded to the next 16-byte
 multiple so the staged GEMV can move whole rows with bulk copies; the row
-stride is passed to the library.  torch is only the allocator here.
+stride is passed to the library.  Q6_K matrices are then converted in place
+to the planar layout the staged GEMV reads (shk_cuda_q6k_repack) and carry
+dtype SHK_DTYPE_Q6_K_PLANAR; an output head whose rows stay unaligned keeps
+the GGUF layout (plain-load kernel).  torch is only the allocator here.
 """
 from __future__ import annotations
 
@@ -39,7 +42,23 @@ class Uploaded:
     desc: sc.ModelDesc
 
 
-def upload(model: Model, device: str | torch.device = "cuda:0") -> Uploaded:
+def to_planar(ctx: sc.Context, t: torch.Tensor, qtype: int, rows: int, cols: int, stride: int) -> int:
+    """Repacks a Q6_K matrix in place when its rows are 16-byte aligned;
+    returns the dtype to register it with."""
+    if qtype != T_Q6K:
+        return qtype
+    rb = stride or (cols // QK) * BLOCK_BYTES[qtype]
+    if rb % 16 or t.data_ptr() % 16:
+        return qtype
+    ctx.q6k_repack(t.data_ptr(), rows, cols, rb, True, ctx.stream)
+    return sc.DTYPE_Q6_K_PLANAR
+
+
+def upload(model: Model, device: str | torch.device = "cuda:0", ctx: sc.Context | None = None,
+           out_rows: int | None = None) -> Uploaded:
+    """ctx: the context whose stream runs the Q6_K repacks (all Q6_K weights
+    are expected planar by the model path).  out_rows: rows of the output head
+    (a tensor-parallel rank's vocabulary slice)."""
     s = model.shape
     keep = []
 
@@ -48,18 +67,35 @@ def upload(model: Model, device: str | torch.device = "cuda:0") -> Uploaded:
         keep.append(t)
         return t.data_ptr()
 
+    def mat(w, qt, rows, cols):
+        t, stride = upload_matrix(w, qt, rows, cols, device)
+        keep.append(t)
+        dt = to_planar(ctx, t, qt, rows, cols, stride) if ctx is not None else qt
+        return t.data_ptr(), stride, dt
+
     layers = []
     hd = s.head_dim
+    D, F, qd, kvd = s.n_embd, s.n_ff, s.n_heads * hd, s.n_kv_heads * hd
+    o_rows = len(np.asarray(model.layers[0].wo).reshape(-1)) // ((qd // QK) * BLOCK_BYTES[s.t_o]) \
+        if model.layers else D
     for Lw in model.layers:
-        wv, sv = upload_matrix(Lw.wv, s.t_v, s.n_kv_heads * hd, s.n_embd, device)
-        wd, sd = upload_matrix(Lw.wd, s.t_down, s.n_embd, s.n_ff, device)
-        keep += [wv, wd]
-        layers.append(sc.LayerDesc(
-            put(Lw.attn_norm), put(Lw.ffn_norm), put(Lw.wq), put(Lw.wk), wv.data_ptr(), put(Lw.wo),
-            put(Lw.wg), put(Lw.wu), wd.data_ptr(),
-            s.t_q, s.t_k, s.t_v, s.t_o, s.t_gate, s.t_up, s.t_down, sv, sd))
+        q, _, tq = mat(Lw.wq, s.t_q, qd, D)
+        k, _, tk = mat(Lw.wk, s.t_k, kvd, D)
+        v, sv, tv = mat(Lw.wv, s.t_v, kvd, D)
+        o, _, to = mat(Lw.wo, s.t_o, o_rows, qd)
+        g, _, tg = mat(Lw.wg, s.t_gate, F, D)
+        u, _, tu = mat(Lw.wu, s.t_up, F, D)
+        d, sd, td = mat(Lw.wd, s.t_down, D, F)
+        layers.append(sc.LayerDesc(put(Lw.attn_norm), put(Lw.ffn_norm), q, k, v, o, g, u, d,
+                                   tq, tk, tv, to, tg, tu, td, sv, sd))
+    out = _dev(model.output, device)
+    keep.append(out)
+    nv = out_rows or s.n_vocab
+    t_out = to_planar(ctx, out, s.t_out, nv, D, 0) if ctx is not None else s.t_out
     desc = sc.ModelDesc(s.n_layers, s.n_embd, s.n_heads, s.n_kv_heads, hd, s.n_ff, s.n_vocab, 0.0,
-                        put(model.tok_embd), s.t_embd, put(model.output), s.t_out)
+                        put(model.tok_embd), s.t_embd, out.data_ptr(), t_out)
+    if ctx is not None:
+        ctx.sync()
     return Uploaded(model, keep, layers, desc)
 
 
@@ -70,7 +106,8 @@ class GpuDecoder:
         """tp_rows: (o_lo, o_hi, v_lo, v_hi) of a tensor-parallel rank whose
         context has joined its group (the model is that rank's shard)."""
         s = model.shape
-        self.up = upload(model, device)
+        out_rows = tp_rows[3] - tp_rows[2] if tp_rows is not None else None
+        self.up = upload(model, device, ctx=ctx, out_rows=out_rows)
         self.kv = sc.KvCache(ctx, s.n_layers, s.n_kv_heads, s.head_dim, max_seq)
         self.m = sc.DeviceModel(ctx, self.kv, self.up.desc)
         if tp_rows is not None:

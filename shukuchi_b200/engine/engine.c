@@ -204,13 +204,16 @@ static void layer_desc(struct engine_handle *h, uint32_t l, const uint8_t *base,
     d->ffn_gate = base + L->t[TN_GATE].dev_off;
     d->ffn_up = base + L->t[TN_UP].dev_off;
     d->ffn_down = base + L->t[TN_DOWN].dev_off;
-    d->attn_q_dtype = L->t[TN_Q].type;
-    d->attn_k_dtype = L->t[TN_K].type;
-    d->attn_v_dtype = L->t[TN_V].type;
-    d->attn_o_dtype = L->t[TN_O].type;
-    d->ffn_gate_dtype = L->t[TN_GATE].type;
-    d->ffn_up_dtype = L->t[TN_UP].type;
-    d->ffn_down_dtype = L->t[TN_DOWN].type;
+    /* Q6_K tensors were converted to the planar layout while staging */
+#define DT(i) (L->t[i].type == 14 ? SHK_DTYPE_Q6_K_PLANAR : L->t[i].type)
+    d->attn_q_dtype = DT(TN_Q);
+    d->attn_k_dtype = DT(TN_K);
+    d->attn_v_dtype = DT(TN_V);
+    d->attn_o_dtype = DT(TN_O);
+    d->ffn_gate_dtype = DT(TN_GATE);
+    d->ffn_up_dtype = DT(TN_UP);
+    d->ffn_down_dtype = DT(TN_DOWN);
+#undef DT
     d->row_stride_v = (uint32_t)L->t[TN_V].dev_row;
     d->row_stride_down = (uint32_t)L->t[TN_DOWN].dev_row;
 }
@@ -246,6 +249,10 @@ static void *loader_main(void *arg) {
                                                tl->rows) != SHK_OK;
             else
                 rc = shk_cuda_layer_stage(h->ctx, s, dst + tl->dev_off, src, tl->size) != SHK_OK;
+            if (!rc && tl->type == 14) /* Q6_K: the GEMV reads the planar layout */
+                rc = shk_cuda_layer_stage_q6k_planar(h->ctx, s, dst + tl->dev_off, (uint32_t)tl->rows,
+                                                     (uint32_t)(tl->row_bytes / 210 * 256),
+                                                     (uint32_t)(tl->dev_row ? tl->dev_row : tl->row_bytes)) != SHK_OK;
         }
         if (!rc) rc = shk_cuda_layer_commit(h->ctx, s) != SHK_OK;
         pthread_mutex_lock(&h->mu);
@@ -514,9 +521,16 @@ engine_handle_t *engine_open(const char *model_path, const struct engine_config 
     const struct gguf_tensor_info *emb = gguf_find_tensor(&h->g, "token_embd.weight");
     const struct gguf_tensor_info *out = gguf_find_tensor(&h->g, "output.weight");
     if (upload_tensor(h, emb, &h->d_embd) || upload_tensor(h, out, &h->d_out)) goto fail;
+    uint32_t out_type = out->type;
+    if (out_type == 14 && (out->size / out->dims[1]) % 16 == 0) { /* planar Q6_K head */
+        if (shk_cuda_q6k_repack(h->ctx, h->d_out, (uint32_t)out->dims[1], h->n_embd, 0, 1, NULL) != SHK_OK ||
+            shk_cuda_sync(h->ctx, NULL) != SHK_OK)
+            goto fail;
+        out_type = SHK_DTYPE_Q6_K_PLANAR;
+    }
     struct shk_model_desc md = {h->n_layers, h->n_embd, h->n_heads, h->n_kv, h->head_dim, h->n_ff, h->n_vocab,
                                 10000.0f /* engine/src/ops.c:223: the reference's fixed theta */,
-                                h->d_embd, emb->type, h->d_out, out->type};
+                                h->d_embd, emb->type, h->d_out, out_type};
     h->m = shk_cuda_model_create(h->ctx, &md, h->kv);
     if (!h->m) goto fail;
     h->n_buf = h->resident ? h->n_layers : h->depth;

@@ -2,7 +2,8 @@
 
   python -m shukuchi_b200.microbench gemv [--shapes QT,M,K ...] [--reps R]
       Batch-1 dequant-matvec sweep (Q4_K = 12, Q6_K = 14), fp32 x ~ N(0,1),
-      seeded random blocks.  Each launch reads a different copy of the weights
+      seeded random blocks; Q6_K matrices repacked once to the planar layout
+      the decode path uses (shk_cuda_q6k_repack), outside the timed graph.  Each launch reads a different copy of the weights
       (copies totalling >= 4x the L2 size, at least 2), launches captured in a
       CUDA graph, CUDA-event timing on the launching stream.
       Bytes per launch = weights + 4*K (x) + 4*M (y).
@@ -92,18 +93,25 @@ def gemv(args, ctx) -> None:
             ws.append(t)
         if stride != row:
             raise SystemExit(f"rows of {qt},{m},{k} are not 16-byte multiples; use the C ABI row_stride")
+        dt = qt
+        if qt == 14:  # the layout the decode path registers Q6_K weights in
+            torch.cuda.synchronize()
+            for t in ws:
+                ctx.q6k_repack(t.data_ptr(), m, k, stride, True)
+            ctx.sync()
+            dt = sc.DTYPE_Q6_K_PLANAR
         x = torch.randn(k, device="cuda", generator=gen)
         y = torch.empty(m, device="cuda")
         s = torch.cuda.Stream()
         nl = max(ncopy, args.launches)
         with torch.cuda.stream(s):
             for i in range(3):  # warm-up (also loads the kernels)
-                ctx.matmul(qt, ws[i % ncopy].data_ptr(), x.data_ptr(), y.data_ptr(), m, k, stream=s.cuda_stream)
+                ctx.matvec(dt, ws[i % ncopy].data_ptr(), x.data_ptr(), y.data_ptr(), m, k, stream=s.cuda_stream)
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=s):
                 for i in range(nl):
-                    ctx.matmul(qt, ws[i % ncopy].data_ptr(), x.data_ptr(), y.data_ptr(), m, k,
+                    ctx.matvec(dt, ws[i % ncopy].data_ptr(), x.data_ptr(), y.data_ptr(), m, k,
                                stream=s.cuda_stream)
         ms = _time_graph(g, s, args.reps)
         ctx.check()
@@ -187,7 +195,7 @@ def parts(args, ctx) -> None:
 
     peak, kind = hbm_peak()
     shape = dataclasses.replace(synth.SHAPES[args.shape], n_layers=args.layers)
-    wts = make_device_model(shape, seed=7)
+    wts = make_device_model(shape, seed=7, ctx=ctx)
     kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, args.prompt + 16)
     m = sc.DeviceModel(ctx, kv, wts.desc)
     try:
@@ -233,7 +241,7 @@ def timeline(args, ctx) -> None:
     from .synth_device import make_device_model
 
     shape = dataclasses.replace(synth.SHAPES[args.shape], n_layers=args.layers)
-    wts = make_device_model(shape, seed=7)
+    wts = make_device_model(shape, seed=7, ctx=ctx)
     ctx = sc.Context(0, flags=sc.FLAG_PERSISTENT)
     kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, args.prompt + args.steps + 8)
     m = sc.DeviceModel(ctx, kv, wts.desc)

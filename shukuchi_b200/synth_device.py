@@ -32,13 +32,22 @@ def _fill_blocks(buf: torch.Tensor, qtype: int, rows: int, cols: int, stride: in
         blocks[:, :, 208:210] = d.view(torch.uint8).view(rows, nb, 2)
 
 
-def _matrix(qtype, rows, cols, device, gen, keep):
+def _matrix(qtype, rows, cols, device, gen, keep, ctx=None):
+    """Returns (device pointer, row stride or 0, dtype to register).  Q6_K
+    matrices are generated in GGUF blocks and repacked in place to the planar
+    layout of the staged GEMV when a context is given."""
     rb = (cols // QK) * BLOCK_BYTES[qtype]
     stride = (rb + 15) // 16 * 16
     t = torch.zeros(rows * stride, dtype=torch.uint8, device=device)
     _fill_blocks(t, qtype, rows, cols, stride, gen)
     keep.append(t)
-    return t.data_ptr(), (0 if stride == rb else stride)
+    dt = qtype
+    if ctx is not None and qtype == T_Q6K:
+        torch.cuda.synchronize(device)
+        ctx.q6k_repack(t.data_ptr(), rows, cols, stride, True)
+        ctx.sync()
+        dt = sc.DTYPE_Q6_K_PLANAR
+    return t.data_ptr(), (0 if stride == rb else stride), dt
 
 
 @dataclasses.dataclass
@@ -54,12 +63,14 @@ class DeviceWeights:
 
 def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
                       distinct_layers: int | None = None, o_rows: int | None = None,
-                      out_rows: int | None = None) -> DeviceWeights:
+                      out_rows: int | None = None, ctx: sc.Context | None = None) -> DeviceWeights:
     """All weights in HBM.  distinct_layers < n_layers reuses layer buffers
     cyclically (only for smoke-sized runs; the benchmark uses distinct layers).
     o_rows / out_rows: rows of the O projection and of the output head when
     they differ from n_embd / n_vocab (a tensor-parallel rank's shard, whose
-    `shape` is the local one of shukuchi_b200.tp.local_shape)."""
+    `shape` is the local one of shukuchi_b200.tp.local_shape).  ctx: the
+    context whose stream repacks Q6_K matrices to the planar layout (required
+    for a model the library runs; without it the matrices stay GGUF blocks)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     keep: list = []
@@ -71,20 +82,20 @@ def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
         an = (1 + 0.02 * torch.randn(s.n_embd, device=device, generator=gen)).float()
         fn = (1 + 0.02 * torch.randn(s.n_embd, device=device, generator=gen)).float()
         keep += [an, fn]
-        q, _ = _matrix(s.t_q, s.n_heads * hd, s.n_embd, device, gen, keep)
-        k, _ = _matrix(s.t_k, s.n_kv_heads * hd, s.n_embd, device, gen, keep)
-        v, sv = _matrix(s.t_v, s.n_kv_heads * hd, s.n_embd, device, gen, keep)
-        o, _ = _matrix(s.t_o, o_rows or s.n_embd, s.n_heads * hd, device, gen, keep)
-        g, _ = _matrix(s.t_gate, s.n_ff, s.n_embd, device, gen, keep)
-        u, _ = _matrix(s.t_up, s.n_ff, s.n_embd, device, gen, keep)
-        dn, sd = _matrix(s.t_down, s.n_embd, s.n_ff, device, gen, keep)
+        q, _, tq = _matrix(s.t_q, s.n_heads * hd, s.n_embd, device, gen, keep, ctx)
+        k, _, tk = _matrix(s.t_k, s.n_kv_heads * hd, s.n_embd, device, gen, keep, ctx)
+        v, sv, tv = _matrix(s.t_v, s.n_kv_heads * hd, s.n_embd, device, gen, keep, ctx)
+        o, _, to = _matrix(s.t_o, o_rows or s.n_embd, s.n_heads * hd, device, gen, keep, ctx)
+        g, _, tg = _matrix(s.t_gate, s.n_ff, s.n_embd, device, gen, keep, ctx)
+        u, _, tu = _matrix(s.t_up, s.n_ff, s.n_embd, device, gen, keep, ctx)
+        dn, sd, td = _matrix(s.t_down, s.n_embd, s.n_ff, device, gen, keep, ctx)
         made.append(sc.LayerDesc(an.data_ptr(), fn.data_ptr(), q, k, v, o, g, u, dn,
-                                 s.t_q, s.t_k, s.t_v, s.t_o, s.t_gate, s.t_up, s.t_down, sv, sd))
+                                 tq, tk, tv, to, tg, tu, td, sv, sd))
     layers = [made[i % nd] for i in range(s.n_layers)]
-    te, _ = _matrix(s.t_embd, s.n_vocab, s.n_embd, device, gen, keep)
-    out, so = _matrix(s.t_out, out_rows or s.n_vocab, s.n_embd, device, gen, keep)
+    te, _, _ = _matrix(s.t_embd, s.n_vocab, s.n_embd, device, gen, keep)
+    out, so, tout = _matrix(s.t_out, out_rows or s.n_vocab, s.n_embd, device, gen, keep, ctx)
     assert so == 0, "output head rows must be 16-byte multiples"
     desc = sc.ModelDesc(s.n_layers, s.n_embd, s.n_heads, s.n_kv_heads, hd, s.n_ff, s.n_vocab, 0.0,
-                        te, s.t_embd, out, s.t_out)
+                        te, s.t_embd, out, tout)
     torch.cuda.synchronize(device)
     return DeviceWeights(s, keep, layers, desc)

@@ -87,3 +87,55 @@ def test_rejects_bad_shapes(ctx):
     d = torch.zeros(1024, dtype=torch.uint8, device="cuda")
     with pytest.raises(ShkError):
         ctx.matmul(12, d.data_ptr(), d.data_ptr(), d.data_ptr(), 1, 100)  # k % 256
+
+
+def planar_ref(rows: np.ndarray, nb: int, stride: int) -> np.ndarray:
+    """The planar Q6_K row layout, restated in numpy: rows (GGUF blocks,
+    `stride` bytes apart) regrouped as [ql][qh][scales][d] with the 16-byte
+    chunks of block b rotated (ql chunk c at slot (c + b) & 7, qh chunk c at
+    slot (c + (b >> 1)) & 3)."""
+    out = rows.copy()
+    for r in range(rows.shape[0]):
+        src = rows[r]
+        dst = out[r]
+        for b in range(nb):
+            blk = src[210 * b:210 * b + 210]
+            for c in range(8):
+                s = ((c + b) & 7) * 16
+                dst[128 * b + s:128 * b + s + 16] = blk[16 * c:16 * c + 16]
+            for c in range(4):
+                s = ((c + (b >> 1)) & 3) * 16
+                dst[128 * nb + 64 * b + s:128 * nb + 64 * b + s + 16] = blk[128 + 16 * c:128 + 16 * c + 16]
+            dst[192 * nb + 16 * b:192 * nb + 16 * b + 16] = blk[192:208]
+            dst[208 * nb + 2 * b:208 * nb + 2 * b + 2] = blk[208:210]
+    return out
+
+
+@pytest.mark.parametrize("m,k", [(3, 256), (17, 4096), (5, 5632), (2, 14336)])
+def test_q6k_planar_layout_and_matvec(oracle, ctx, m, k):
+    """shk_cuda_q6k_repack writes exactly the planar layout (byte for byte),
+    the inverse restores the GGUF blocks, and the staged GEMV on planar rows
+    (padded strides included) matches the oracle on the GGUF bytes."""
+    from shukuchi_b200 import cuda as sc
+    rng = np.random.default_rng(m + k)
+    nb = k // 256
+    w = synth.quant_matrix(rng, 14, m, k).reshape(m, 210 * nb)
+    stride = (210 * nb + 15) // 16 * 16
+    rows = np.zeros((m, stride), np.uint8)
+    rows[:, :210 * nb] = w
+    d = to_dev(rows.reshape(-1))
+    ctx.q6k_repack(d.data_ptr(), m, k, stride, True)
+    ctx.sync()
+    assert np.array_equal(d.cpu().numpy().reshape(m, stride), planar_ref(rows, nb, stride))
+    x = rng.normal(0, 1, k).astype(np.float32)
+    xd = to_dev(x)
+    y = torch.full((m,), float("nan"), device="cuda")
+    ctx.matvec(sc.DTYPE_Q6_K_PLANAR, d.data_ptr(), xd.data_ptr(), y.data_ptr(), m, k, row_stride=stride)
+    ctx.sync()
+    ctx.check()
+    wf = w.reshape(-1)
+    tol = gemv_tolerance(oracle, 14, wf, x, m, k)
+    assert np.all(np.abs(y.cpu().numpy().astype(np.float64) - oracle.matvec(14, wf, x, m, k)) <= tol)
+    ctx.q6k_repack(d.data_ptr(), m, k, stride, False)
+    ctx.sync()
+    assert np.array_equal(d.cpu().numpy().reshape(m, stride), rows)

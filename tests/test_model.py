@@ -24,7 +24,7 @@ def assert_logits(got, ref):
 def test_layer_forward_matches_oracle(oracle, ctx):
     model = synth.make_model("small", seed=3)
     s = model.shape
-    up = upload(model)
+    up = upload(model, ctx=ctx)
     kv = sc.KvCache(ctx, s.n_layers, s.n_kv_heads, s.head_dim, 64)
     dm = sc.DeviceModel(ctx, kv, up.desc)
     okv = oracle.kv_create(s.n_layers, s.n_kv_heads, s.head_dim, 64)

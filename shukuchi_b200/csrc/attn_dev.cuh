@@ -334,14 +334,13 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
 
 // ------------------------- cluster attention --------------------------------
 // One thread-block cluster per KV head; CTA rank r of the cluster is split r of
-// the positions [0, pos].  Splits merge through distributed shared memory
-// (each CTA publishes its (max, sum, output) in its own shared memory; after a
-// cluster barrier every CTA combines a slice of the head dimension reading all
-// peers), so no partials go through global memory and no ticket is needed.
-// The new token's K/V row (position pos) is quantised in registers and used
-// directly -- the same bytes the append stores -- so the cache loads of the
-// older positions can be issued before the previous kernel's outputs (q, new
-// K/V) are waited for.
+// the positions [0, pos].  Splits merge through distributed shared memory:
+// each CTA stores its (max, sum, output) into its slot in the leader CTA's
+// shared memory and arrives on the leader's mbarrier, so no partials go
+// through global memory and only the leader waits.  The new token's K/V row
+// (position pos) is quantised in registers and used directly -- the same
+// bytes the append stores -- so the cache loads of the older positions can be
+// issued before the previous kernel's outputs (q, new K/V) are waited for.
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -353,48 +352,72 @@ __device__ __forceinline__ uint32_t cluster_size() {
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
   return n;
 }
-__device__ __forceinline__ void cluster_barrier() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
 // Shared-memory address of `p` in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
   uint32_t a;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
   return a;
 }
-__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+
+constexpr int ATT_CLUSTER_MAX = 16;  // largest cluster the launcher picks
+
+// Cluster-scope helpers for the split merge: peers store their partial result
+// into the leader CTA's shared memory and arrive on the leader's mbarrier.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
+  asm volatile(
+      "fence.acq_rel.cluster;\n\t"
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded (WAIT_BUDGET_NS) wait for the peers' partials; false on time-out.
+__device__ __forceinline__ bool wait_peers(uint64_t* bar) {
+  if (mbar_try_wait_cluster(bar, 0)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait_cluster(bar, 0)) return true;
+    __nanosleep(32);
+    if ((n & 31) == 0 && globaltimer_ns() - t0 > WAIT_BUDGET_NS) return false;
+  }
 }
 
-// Q8_0 of one 32-element block read by one thread (q8_quantize_vec,
-// engine/src/kv_cache.c:28-55): same maximum, IEEE division and rounding as the
-// append kernels, so the bytes are identical.  Writes the quants as four
-// packed words per 16 bytes to q (4 x uint4) and returns the scale.  Not
-// inlined: it runs for one position per launch, and its 32 divisions would
-// otherwise enlarge the hot loop's code.
-static __device__ __noinline__ float q8_block_new(const float* __restrict__ src, uint4* __restrict__ q) {
-  float v[32];
-  const float4* s4 = reinterpret_cast<const float4*>(src);
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const float4 f4 = __ldcg(s4 + u);
-    v[4 * u] = f4.x; v[4 * u + 1] = f4.y; v[4 * u + 2] = f4.z; v[4 * u + 3] = f4.w;
-  }
+// Q8_0 of one 32-element block already in registers (q8_quantize_vec,
+// engine/src/kv_cache.c:28-55): same maximum, IEEE division and rounding as
+// the append kernels, so the bytes are identical.
+__device__ __forceinline__ float q8_regs(const float4 (&v4)[8], uint4 (&q)[2]) {
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  for (int u = 0; u < 8; ++u)
+    amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v4[u].x), fabsf(v4[u].y))), fmaxf(fabsf(v4[u].z), fabsf(v4[u].w)));
   float scale = amax / 127.0f;
   if (scale == 0.0f) scale = 1.0f;
   uint32_t w[8];
-#pragma unroll 4
+#pragma unroll
   for (int u = 0; u < 8; ++u) {
+    const float e4[4] = {v4[u].x, v4[u].y, v4[u].z, v4[u].w};
     uint32_t word = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      int t = __float2int_rn(v[4 * u + e] / scale);
+      int t = __float2int_rn(e4[e] / scale);
       t = t > 127 ? 127 : (t < -127 ? -127 : t);
       word |= ((uint32_t)t & 0xFFu) << (8 * e);
     }
@@ -413,14 +436,19 @@ struct AttnCSmem {  // offsets in floats
   static constexpr int WM = Q + G * LPP * QROW;
   static constexpr int WL = WM + NW * G;
   static constexpr int WACC = WL + NW * G;
-  static constexpr int CM = WACC + NW * G * HD;  // this CTA's max per query head
-  static constexpr int CL = CM + G;              // its sum of exponentials
-  static constexpr int CO = CL + G;              // its unnormalised output [G][HD]
-  static constexpr int FLOATS = CO + G * HD;
+  static constexpr int SLOT = 2 * G + G * HD;  // one CTA's partial: m[G], l[G], o[G][HD]
+  static constexpr int SLOTS = WACC + NW * G * HD;  // leader: one slot per cluster rank
+  static constexpr int BAR = (SLOTS + ATT_CLUSTER_MAX * SLOT + 1) & ~1;  // leader's mbarrier
+  static constexpr int FLOATS = BAR + 2;
   static constexpr size_t BYTES = (size_t)FLOATS * 4;
 };
 
-// Cluster attention for KV head blockIdx.y by NW warps; see above.
+// Cluster attention for KV head blockIdx.y by NW warps; see above.  Each CTA
+// reduces its positions to a partial (max, sum of exponentials, unnormalised
+// output) per query head and stores it into its slot in the leader CTA's
+// shared memory; the leader (rank 0) waits for its peers on an mbarrier
+// (bounded), merges the slots in rank order and writes the output.  Peers
+// leave as soon as they have arrived.
 template <int HD, int G, int NW>
 __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   using Tile = AttnTile<HD>;
@@ -428,15 +456,25 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   constexpr int LPP = Tile::LPP, PPI = Tile::PPI, EPL = Tile::EPL;
   constexpr int NT = 32 * NW;
   constexpr int LPB = 32 / EPL;  // lanes sharing one V block in the PV layout
+  constexpr int QPT = (G * HD + NT - 1) / NT;  // q elements per thread
   const uint32_t KV = a.kv.n_kv, kvh = blockIdx.y;
   const uint32_t rank = cluster_rank(), CS = cluster_size();
+  const bool leader = rank == 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // The position and the cache rows before it were written by earlier graph
   // launches or stream work, never by the kernel this one may overlap.
   const uint32_t pos = __ldcg(a.pos);
   if (pos >= a.kv.max_seq) {
     if (tid == 0 && rank == 0) set_error(a.err, DERR_BAD_POS);
-    return;  // the whole cluster leaves: no barrier is left waiting
+    return;  // the whole cluster leaves before any cluster barrier
+  }
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + SM::BAR);
+  if (CS > 1) {
+    if (leader && tid == 0) {
+      mbar_init(bar, CS - 1);
+      fence_mbar_init();
+    }
+    cluster_arrive();  // paired with cluster_wait before the first remote store
   }
   const uint32_t seq = pos + 1;
   uint32_t n0 = (seq + a.min_per_split - 1) / a.min_per_split;
@@ -451,9 +489,6 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   float (*wm)[G] = reinterpret_cast<float (*)[G]>(sm + SM::WM);
   float (*wl)[G] = reinterpret_cast<float (*)[G]>(sm + SM::WL);
   float (*wacc)[G][HD] = reinterpret_cast<float (*)[G][HD]>(sm + SM::WACC);
-  float* cm = sm + SM::CM;
-  float* cl = sm + SM::CL;
-  float (*co)[HD] = reinterpret_cast<float (*)[HD]>(sm + SM::CO);
 
   int8_t* reg = const_cast<int8_t*>(a.kv.region(a.layer, kvh));
   const int8_t* Kq = reg + a.kv.kq_off;
@@ -469,18 +504,35 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   if (mine && T < p1) cur.load(Kq, Ks, Vq, Vs, T, p1, lane);  // in flight across the wait
 
   pdl_wait();  // q and the new K/V row come from the previous kernel
-  for (int i = tid; i < G * HD; i += NT) {
-    const int g = i / HD, d = i % HD;
-    qs[g][d / 32][d % 32] = __ldcg(a.q + (kvh + KV * g) * HD + d);  // query head kvh + KV*g
+  // every load that depends on it is issued before any is used
+  float4 kn4[8];
+  float vv[EPL];
+  if (own_new) {
+    const float4* ks4 = reinterpret_cast<const float4*>(a.k_new + kvh * HD + 32 * b);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) kn4[u] = __ldcg(ks4 + u);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) vv[e] = __ldcg(a.v_new + kvh * HD + lane * EPL + e);
   }
-  // The new V row in the PV layout (EPL columns per lane, LPB lanes per block);
-  // warp 0 appends it to the cache.
+  float qv[QPT];
+#pragma unroll
+  for (int j = 0; j < QPT; ++j) {
+    const int i = tid + j * NT;
+    if (i < G * HD) qv[j] = __ldcg(a.q + (kvh + KV * (i / HD)) * HD + i % HD);  // query head kvh + KV*g
+  }
+#pragma unroll
+  for (int j = 0; j < QPT; ++j) {
+    const int i = tid + j * NT;
+    if (i < G * HD) qs[i / HD][(i % HD) / 32][i % 32] = qv[j];
+  }
+  // The new K/V row: K in the QK layout (lane = 32-element block b), V in the
+  // PV layout (EPL columns per lane, LPB lanes per block); warp 0 appends both.
+  uint4 kq_new[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  float ks_new = 1.f;
   uint32_t vw_new = 0;
   float vs_new = 1.f;
   if (own_new) {
-    float vv[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) vv[e] = __ldcg(a.v_new + kvh * HD + lane * EPL + e);
+    ks_new = q8_regs(kn4, kq_new);
     float amax = 0.f;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) amax = fmaxf(amax, fabsf(vv[e]));
@@ -502,6 +554,12 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
         *reinterpret_cast<uint16_t*>(vq) = (uint16_t)vw_new;
       if (lane % LPB == 0)
         reinterpret_cast<float*>(reg + a.kv.vs_off)[(size_t)pos * (HD / 32) + lane / LPB] = vs_new;
+      if (tl == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(reg + a.kv.kq_off + (size_t)pos * HD + 32 * b);
+        dst[0] = kq_new[0];
+        dst[1] = kq_new[1];
+        reinterpret_cast<float*>(reg + a.kv.ks_off)[(size_t)pos * (HD / 32) + b] = ks_new;
+      }
     }
   }
   att_sync(NT);
@@ -524,17 +582,10 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
     float kf[32];
     float ksc = cur.ks;
     uint4 k0 = cur.k0, k1 = cur.k1;
-    if (own_new && t == pos) {  // the new row, quantised here; this lane appends its block
-      uint4 qn[2];
-      ksc = q8_block_new(a.k_new + kvh * HD + 32 * b, qn);
-      k0 = qn[0];
-      k1 = qn[1];
-      if (ok && warp == (int)((pos - p0) / PPI) % NW) {
-        uint4* dst = reinterpret_cast<uint4*>(reg + a.kv.kq_off + (size_t)pos * HD + 32 * b);
-        dst[0] = k0;
-        dst[1] = k1;
-        reinterpret_cast<float*>(reg + a.kv.ks_off)[(size_t)pos * (HD / 32) + b] = ksc;
-      }
+    if (own_new && t == pos) {  // the new row, quantised above
+      k0 = kq_new[0];
+      k1 = kq_new[1];
+      ksc = ks_new;
     }
     s8x4_to_f32(k0.x, kf);
     s8x4_to_f32(k0.y, kf + 4);
@@ -547,11 +598,11 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
     float p[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float4* qv = reinterpret_cast<const float4*>(&qs[g][b][0]);
+      const float4* qv4 = reinterpret_cast<const float4*>(&qs[g][b][0]);
       float sb = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float4 q4 = qv[u];
+        const float4 q4 = qv4[u];
         sb = fmaf(q4.x, kf[4 * u], sb);
         sb = fmaf(q4.y, kf[4 * u + 1], sb);
         sb = fmaf(q4.z, kf[4 * u + 2], sb);
@@ -592,7 +643,8 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
     }
     cur = nxt;
   }
-  // ---- merge the warps into this CTA's (max, sum, output) ----
+  // ---- merge the warps into this CTA's partial, stored into its slot in the
+  //      leader's shared memory ----
 #pragma unroll
   for (int g = 0; g < G; ++g) {
 #pragma unroll
@@ -603,40 +655,54 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
     }
   }
   att_sync(NT);
-  for (int i = tid; i < G * HD; i += NT) {
-    const int g = i / HD, d = i % HD;
-    float M = -INFINITY;
+  if (CS > 1) cluster_wait();  // the leader runs (its barrier is initialised)
+  float* slot = sm + SM::SLOTS + rank * SM::SLOT;
+  const uint32_t slot_r = dsmem_addr(slot, 0);  // the same offset in the leader
+  if (mine) {
+    for (int i = tid; i < G * HD; i += NT) {
+      const int g = i / HD, d = i % HD;
+      float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
-    float L = 0.f, O = 0.f;
+      for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+      float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
-      L = fmaf(f, wl[w][g], L);
-      O = fmaf(f, wacc[w][g][d], O);
-    }
-    co[g][d] = O;
-    if (d == 0) {
-      cm[g] = M;
-      cl[g] = L;
+      for (int w = 0; w < NW; ++w) {
+        const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
+        L = fmaf(f, wl[w][g], L);
+        O = fmaf(f, wacc[w][g][d], O);
+      }
+      dsmem_st(slot_r + 4u * (uint32_t)(2 * G + i), O);
+      if (d == 0) {
+        dsmem_st(slot_r + 4u * (uint32_t)g, M);
+        dsmem_st(slot_r + 4u * (uint32_t)(G + g), L);
+      }
     }
   }
-  // ---- merge the splits across the cluster ----
-  cluster_barrier();  // every CTA's (cm, cl, co) is published
-  for (uint32_t i = rank * NT + tid; i < (uint32_t)(G * HD); i += CS * NT) {
-    const uint32_t g = i / HD, d = i % HD;
+  att_sync(NT);  // this CTA's stores precede thread 0's release below
+  if (!leader) {
+    if (tid == 0) mbar_arrive_remote(dsmem_addr(bar, 0));
+    return;
+  }
+  // ---- leader: merge the splits in rank order ----
+  if (CS > 1 && !wait_peers(bar)) {
+    if (tid == 0) set_error(a.err, DERR_TIMEOUT_GRID);
+    return;
+  }
+  const float* sl0 = sm + SM::SLOTS;
+  for (int i = tid; i < G * HD; i += NT) {
+    const int g = i / HD;
     float M = -INFINITY;
-    for (uint32_t r = 0; r < active; ++r) M = fmaxf(M, dsmem_ld(dsmem_addr(&cm[g], r)));
+    for (uint32_t r = 0; r < active; ++r) M = fmaxf(M, sl0[r * SM::SLOT + g]);
     float L = 0.f, O = 0.f;
     for (uint32_t r = 0; r < active; ++r) {
-      const float mr = dsmem_ld(dsmem_addr(&cm[g], r));
+      const float* sr = sl0 + r * SM::SLOT;
+      const float mr = sr[g];
       const float w = (mr == -INFINITY) ? 0.f : expf(mr - M);
-      L = fmaf(w, dsmem_ld(dsmem_addr(&cl[g], r)), L);
-      O = fmaf(w, dsmem_ld(dsmem_addr(&co[g][d], r)), O);
+      L = fmaf(w, sr[G + g], L);
+      O = fmaf(w, sr[2 * G + i], O);
     }
-    a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O * (1.0f / L);
+    a.out[(kvh + KV * g) * HD + i % HD] = (L == 0.f) ? 0.f : O * (1.0f / L);
   }
-  cluster_barrier();  // peers keep their shared memory until every read is done
 }
 
 }  // namespace adev

@@ -45,7 +45,9 @@ constexpr uint32_t OFF_RED = OFF_GEN + 4 * GEMV_MAX_STAGES;
 constexpr uint32_t OFF_AMV = OFF_RED + 4 * 32;
 constexpr uint32_t OFF_AMI = OFF_AMV + 4 * (DC_CT / 32);
 constexpr uint32_t OFF_FLAG = OFF_AMI + 4 * (DC_CT / 32);
-constexpr uint32_t OFF_ARGS = (OFF_FLAG + 16 + 15) & ~15u;
+constexpr uint32_t OFF_KPART = (OFF_FLAG + 16 + 15) & ~15u;
+constexpr uint32_t OFF_KCNT = OFF_KPART + 4 * GEMV_MAX_STAGES * GEMV_KS_ROWT * GEMV_KS_MAX * 2;
+constexpr uint32_t OFF_ARGS = (OFF_KCNT + 4 * GEMV_MAX_STAGES * GEMV_KS_ROWT + 15) & ~15u;
 constexpr uint32_t HDR_BYTES = (OFF_ARGS + (uint32_t)sizeof(GemvArgs) + 127) & ~127u;
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
@@ -97,7 +99,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) decode_kernel(const __grid_co
   volatile int* flags = reinterpret_cast<volatile int*>(smem + OFF_FLAG);
   GemvArgs* sargs = reinterpret_cast<GemvArgs*>(smem + OFF_ARGS);
   uint8_t* xreg = smem + P.xreg_off;
-  const Ring R{full, empty, done, gen, smem + P.ring_off, P.ns, P.stage_bytes};
+  const Ring R{full,           empty, done, gen, smem + P.ring_off, P.ns, P.stage_bytes,
+               reinterpret_cast<float*>(smem + OFF_KPART), reinterpret_cast<int*>(smem + OFF_KCNT)};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -106,6 +109,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) decode_kernel(const __grid_co
       mbar_init(&empty[s], 1);
       done[s] = 0;
       gen[s] = 0xFFFFFFFFu;
+      for (int r = 0; r < GEMV_KS_ROWT; ++r) R.kcnt[s * GEMV_KS_ROWT + r] = 0;
     }
     fence_mbar_init();
   }

@@ -14,6 +14,15 @@
 #include "gemv.cuh"
 #include "gemv_dev.cuh"
 
+// Largest task (rg row groups x 2 rows) that keeps two rows per lane group.
+#ifndef SHK_RL2_MAX_BYTES
+#define SHK_RL2_MAX_BYTES 40960
+#endif
+// Blocks per K slice of a long row.
+#ifndef SHK_KS_BLOCKS
+#define SHK_KS_BLOCKS 32
+#endif
+
 namespace shk {
 namespace {
 using namespace gdev;
@@ -37,7 +46,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
                                     (HAS4 ? (size_t)(K / 32) * 4 : 0));
   size_t stage_off = (size_t)(xreg - smem) + x_region_bytes(K, HAS4, HAS6);
   stage_off = (stage_off + 127) & ~(size_t)127;
-  const Ring R{full, empty, done, gen, smem + stage_off, NS, a.stage_bytes};
+  const Ring R{full,           empty, done, gen, smem + stage_off, NS, a.stage_bytes,
+               reinterpret_cast<float*>(smem + SMEM_KPART), reinterpret_cast<int*>(smem + SMEM_KCNT)};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tid = threadIdx.x;
@@ -47,29 +57,33 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
       mbar_init(&empty[tid], 1);
       done[tid] = 0;
       gen[tid] = 0xFFFFFFFFu;
+#pragma unroll
+      for (int r = 0; r < GEMV_KS_ROWT; ++r) R.kcnt[tid * GEMV_KS_ROWT + r] = 0;
     } else {
       mbar_init(xbar, GEMV_WARPS);
     }
     fence_mbar_init();
   }
-  pdl_trigger();  // the next kernel may be scheduled; it waits for this one before its reads
-  if (warp < GEMV_WARPS) {
-    pdl_wait();  // x and the residual come from the previous kernel (weights do not)
-    gemv_x_issue(a, xb, warp, lane);
-  }
-  __syncthreads();
+  __syncthreads();  // barriers initialised
+  pdl_trigger();    // the next kernel may be scheduled; it waits for this one before its reads
 
   const uint64_t lo = a.total_cost * blockIdx.x / gridDim.x;
   const uint64_t hi = a.total_cost * (blockIdx.x + 1) / gridDim.x;
   RingPos pos;
   if (warp == GEMV_WARPS) {
+    // weights do not depend on the previous kernel: the first chunks stream in
+    // while it drains
     if (lane == 0) {
       gemv_produce(a, R, pos, lo, hi, xbar);
       ring_drain(R, pos, a.err);
     }
     return;
   }
-  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true);
+  NormPre np;
+  gemv_norm_prefetch(a, warp, lane, np);
+  pdl_wait();  // x and the residual come from the previous kernel
+  gemv_x_issue(a, xb, warp, lane);
+  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true, &np);
   uint32_t gtask = 0;
   gemv_consume<HAS4, HAS6>(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
 }
@@ -183,12 +197,16 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     // Rows beyond 40 KB per task pair: one row per lane group (Q6_K has a
     // single-row body; for Q4_K the second row pointer repeats the first).
     uint32_t rl = g.dual ? 1 : 2;
-    if (rl == 2 && (uint64_t)rg * 2 * g.row_stride > 40960) rl = 1;
+    if (rl == 2 && (uint64_t)rg * 2 * g.row_stride > SHK_RL2_MAX_BYTES) rl = 1;
     if (mt.epi == EPI_ROPE && rl != 2) return -2;
     g.rg = (uint8_t)rg;
     g.rl = (uint8_t)rl;
+    // rows of more than 32 blocks: one warp per slice of at most 32 blocks
+    const uint32_t ks = rg == 1 ? std::min<uint32_t>(GEMV_KS_MAX, (nb + SHK_KS_BLOCKS - 1) / SHK_KS_BLOCKS) : 1;
+    g.ks = (uint8_t)ks;
     g.unit_cost = rg * rl * g.row_stride * mats_per_row;
-    const uint32_t cu = std::max<uint32_t>(1, target / g.unit_cost);
+    uint32_t cu = std::max<uint32_t>(1, target / g.unit_cost);
+    if (ks > 1) cu = std::min<uint32_t>(cu, GEMV_KS_ROWT);
     g.chunk_rows = cu * rg * rl;
     stage = std::max<uint32_t>(stage, cu * g.unit_cost);
     const uint64_t units = (mt.m + rg * rl - 1) / (rg * rl);

@@ -34,6 +34,7 @@ struct GemvSeg {
   uint8_t rg;           // row groups per warp task (lanes split across groups)
   uint8_t rl;           // rows per lane (each loaded x value feeds rl rows)
   uint8_t dual;         // 1 for gate/up pairs
+  uint8_t ks;           // K slices per row task (long rows: one warp per slice)
 };
 
 struct GemvArgs {

@@ -311,30 +311,36 @@ struct XView {
 // bytes; their results are never stored.
 //  32/rg lanes per group, a lane takes blocks s, s + 32/rg, ... (Q4_K and
 //  planar Q6_K alike).
+// K split (g.ks > 1, then rg = 1): this task covers slice `sl` of the blocks;
+// each slice's warp leaves its two row sums in kp[sl] and the last slice to
+// finish (counter kc) adds the slices in slice order and stores.
 template <bool HAS4, bool HAS6>
 __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, const uint8_t* rows,
                                          uint32_t row0, int rows_valid, uint32_t dual_off,
-                                         const XView& x, int lane) {
+                                         const XView& x, int lane, uint32_t sl = 0, float* kp = nullptr,
+                                         int* kc = nullptr) {
   const int lg_rg = __ffs(g.rg) - 1;
   const int rl = g.rl;
   const bool q4 = g.qt == T_Q4K;
   const int spr = 32 >> lg_rg;
   const int grp = lane >> (5 - lg_rg);
   const int s = lane & (spr - 1);
+  const uint32_t sw = (g.nb + g.ks - 1) / g.ks;  // blocks per slice
+  const uint32_t blo = sl * sw, bhi = min(g.nb, blo + sw);
   float o0 = 0.f, o1 = 0.f;
   if (grp * rl < rows_valid) {
     const uint8_t* r0 = rows + (size_t)(grp * rl) * g.row_stride;
     const uint8_t* r1 = g.dual ? r0 + dual_off : ((rl == 2 && grp * 2 + 1 < rows_valid) ? r0 + g.row_stride : r0);
     if (HAS4 && (!HAS6 || q4)) {
-      for (uint32_t b = s; b < g.nb; b += spr)
+      for (uint32_t b = blo + s; b < bhi; b += spr)
         q4k_block2(r0 + (size_t)b * Q4K_BYTES, r1 + (size_t)b * Q4K_BYTES, x.xq + 65 * b, x.xbs[b],
                    x.xs32 + 8 * b, o0, o1);
     } else if (HAS6) {
       if (rl == 1 && !g.dual) {  // single row
-        for (uint32_t b = s; b < g.nb; b += spr)
+        for (uint32_t b = blo + s; b < bhi; b += spr)
           q6k_block<1>(r0, r1, g.nb, b, x.xq + 65 * b, x.xi16 + 17 * b, x.xbs[b], o0, o1);
       } else {
-        for (uint32_t b = s; b < g.nb; b += spr)
+        for (uint32_t b = blo + s; b < bhi; b += spr)
           q6k_block<2>(r0, r1, g.nb, b, x.xq + 65 * b, x.xi16 + 17 * b, x.xbs[b], o0, o1);
       }
     }
@@ -344,6 +350,25 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
     o1 += __shfl_xor_sync(0xffffffffu, o1, o);
   }
   const int lpg = 32 >> lg_rg;  // lanes per group
+  if (g.ks > 1) {
+    if (lane == 0) {
+      kp[2 * sl] = o0;
+      kp[2 * sl + 1] = o1;
+      __threadfence_block();
+      if (atomicAdd(kc, 1) == (int)g.ks - 1) {  // the last slice of this row task
+        __threadfence_block();
+        const volatile float* vp = kp;
+        float s0 = 0.f, s1 = 0.f;
+        for (uint32_t k = 0; k < g.ks; ++k) {
+          s0 += vp[2 * k];
+          s1 += vp[2 * k + 1];
+        }
+        *kc = 0;
+        if (rows_valid > 0) store2(a, g, row0, rows_valid, s0, s1);
+      }
+    }
+    return;
+  }
   if ((lane & (lpg - 1)) == 0 && grp * rl < rows_valid)
     store2(a, g, row0 + grp * rl, rows_valid - grp * rl, o0, o1);
 }
@@ -352,7 +377,14 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
 // [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)][xi16 (17 int4 per block, Q6_K)]
 // [stage ring].  The producer first bulk-copies x into the limb-vector slot;
 // consumers turn it into limbs in place.
-constexpr int SMEM_HDR = 8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES + 4 * 32;
+// K split of long rows (more than 32 blocks, e.g. the down projection): a row
+// task's blocks are cut into ks <= GEMV_KS_MAX slices processed by different
+// warps; a chunk then holds at most GEMV_KS_ROWT row tasks.
+constexpr int GEMV_KS_MAX = 8;
+constexpr int GEMV_KS_ROWT = 4;
+constexpr int SMEM_KPART = (8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES + 4 * 32 + 15) & ~15;
+constexpr int SMEM_KCNT = SMEM_KPART + GEMV_MAX_STAGES * GEMV_KS_ROWT * GEMV_KS_MAX * 2 * 4;
+constexpr int SMEM_HDR = SMEM_KCNT + GEMV_MAX_STAGES * GEMV_KS_ROWT * 4;
 
 // Bounded spin until the producer has claimed stage `st` for chunk `it`.  A
 // consumer may run several ring cycles ahead of a stage (it skips chunks with
@@ -401,6 +433,8 @@ struct Ring {
   uint8_t* stages;
   uint32_t ns;           // stages
   uint32_t stage_bytes;  // bytes per stage (>= every chunk of every plan on this ring)
+  float* kpart;          // K-split partial sums: [stage][row task][slice][2]
+  int* kcnt;             // K-split slices done: [stage][row task]
 };
 struct RingPos {
   uint32_t it = 0, st = 0, ph = 0;  // chunk index, its stage, stage use parity
@@ -414,7 +448,7 @@ struct RingPos {
 };
 
 #ifndef GEMV_PRE_STAGES
-#define GEMV_PRE_STAGES 1
+#define GEMV_PRE_STAGES 3
 #endif
 // Producer (one lane): streams this CTA's chunks of plan `a` (cost range
 // [lo, hi)) into the ring.  If xready is given, only GEMV_PRE_STAGES chunks
@@ -518,10 +552,31 @@ __device__ __forceinline__ void gemv_x_issue(const GemvArgs& a, const XBuf& xb_,
 
 // The rest: wait for the copies, RMSNorm scale, conversion.  x_issued: step 1
 // already ran (else it runs here).
+// RMSNorm weights of the blocks a consumer lane converts in the prologue's
+// first iteration, loaded before the wait for the previous kernel (they do
+// not depend on it): their global-memory latency leaves the critical path.
+constexpr int GEMV_PU = 4;  // blocks per conversion iteration
+struct NormPre {
+  float4 w[GEMV_PU][2];
+};
+__device__ __forceinline__ void gemv_norm_prefetch(const GemvArgs& a, int warp, int lane, NormPre& np) {
+  if (!a.norm_w) return;
+  const uint32_t NB = a.k / 256;
+#pragma unroll
+  for (int u = 0; u < GEMV_PU; ++u) {
+    const uint32_t kb = warp + u * GEMV_WARPS;
+    if (kb < NB) {
+      const float4* wn = reinterpret_cast<const float4*>(a.norm_w + 256 * (size_t)kb + 8 * lane);
+      np.w[u][0] = __ldg(wn);
+      np.w[u][1] = __ldg(wn + 1);
+    }
+  }
+}
+
 template <bool HAS4, bool HAS6>
 __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
                                               int warp, int lane, uint64_t* xready = nullptr,
-                                              bool x_issued = false) {
+                                              bool x_issued = false, const NormPre* np = nullptr) {
   constexpr int CT = 32 * GEMV_WARPS;
   const uint32_t K = a.k;
   const uint32_t NB = K / 256;
@@ -560,7 +615,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
   GEMV_STAMP(2);
   // Conversion, PU blocks per iteration: independent dependency chains in
   // flight (a single block's chain -- reductions, shuffles, packing -- is long).
-  constexpr int PU = 4;
+  constexpr int PU = GEMV_PU;
 #pragma unroll 1
   for (uint32_t kb0 = warp; kb0 < NB; kb0 += PU * GEMV_WARPS) {
     float v[PU][8];
@@ -574,7 +629,8 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
       v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
       if (nw) {
         const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)kc + 8 * lane);
-        const float4 w0 = __ldg(wn), w1 = __ldg(wn + 1);
+        const bool pre = np && kb0 == (uint32_t)warp && kb < NB;
+        const float4 w0 = pre ? np->w[u][0] : __ldg(wn), w1 = pre ? np->w[u][1] : __ldg(wn + 1);
         const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
@@ -592,10 +648,11 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
         finite[u] = finite[u] && isfinite(v[u][e]);
       }
     }
+    // warp maximum in one step: |x| >= 0, whose bit patterns order as unsigned
+    // integers (non-finite blocks are caught by `finite` below)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int u = 0; u < PU; ++u) amax[u] = fmaxf(amax[u], __shfl_xor_sync(0xffffffffu, amax[u], o));
+    for (int u = 0; u < PU; ++u)
+      amax[u] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax[u])));
 #pragma unroll
     for (int u = 0; u < PU; ++u) {
       const uint32_t kb = kb0 + u * GEMV_WARPS;
@@ -664,7 +721,8 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const Ring& R, R
       const uint32_t r0 = u << lg_ur;
       const uint32_t r1 = min(min(u + cu, rr.ue) << lg_ur, g.m);
       const uint32_t nrows = r1 - r0;
-      const uint32_t ntasks = (nrows + ur - 1) >> lg_ur;
+      const uint32_t ks = g.ks;
+      const uint32_t ntasks = ((nrows + ur - 1) >> lg_ur) * ks;
       uint32_t t = (uint32_t)(warp - (int)(gtask % GEMV_WARPS) + GEMV_WARPS) % GEMV_WARPS;
       if (t < ntasks) {
         if (!wait_gen(R.gen, p.st, p.it, a.err)) return false;
@@ -673,9 +731,12 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const Ring& R, R
         const uint32_t dual_off = nrows * g.row_stride;
         uint32_t mine = 0;
         for (; t < ntasks; t += GEMV_WARPS, ++mine) {
-          const int rv = (int)min(ur, nrows - (t << lg_ur));
-          const uint8_t* rows = buf + (size_t)(t << lg_ur) * g.row_stride;
-          run_task<HAS4, HAS6>(a, g, rows, r0 + (t << lg_ur), rv, dual_off, xv, lane);
+          const uint32_t rt = ks > 1 ? t / ks : t, sl = ks > 1 ? t % ks : 0;
+          const int rv = (int)min(ur, nrows - (rt << lg_ur));
+          const uint8_t* rows = buf + (size_t)(rt << lg_ur) * g.row_stride;
+          const uint32_t ki = p.st * GEMV_KS_ROWT + (rt < GEMV_KS_ROWT ? rt : 0);
+          run_task<HAS4, HAS6>(a, g, rows, r0 + (rt << lg_ur), rv, dual_off, xv, lane, sl,
+                               R.kpart + ki * (2 * GEMV_KS_MAX), R.kcnt + ki);
         }
         __syncwarp();
         if (lane == 0) {

@@ -193,9 +193,13 @@ int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, uint32_t row_stride, cons
   const uint32_t nb = k / QK;
   if (qt == T_Q6K && !row_stride) {
     // GGUF-layout rows: copy into padded rows of a scratch buffer, repack
-    // there, then the staged kernel (its weights must be planar)
+    // there, then the staged kernel (its weights must be planar) -- when the
+    // staged kernel takes this shape; else the plain-load kernel below
     const uint32_t stride = (210u * nb + 15u) & ~15u;
-    if (stride <= 227u * 1024u) {
+    GemvMat probe{reinterpret_cast<const void*>(uintptr_t(256)), nullptr, y, m, T_Q6K_PLANAR, stride, EPI_STORE, 0};
+    GemvPlan pp;
+    if (stride <= 227u * 1024u &&
+        gemv_plan(pp, &probe, 1, k, x, nullptr, nullptr, nullptr, c->d_err, c->num_sms) == 0) {
       int rc = grow(&c->q6_scratch, &c->q6_scratch_cap, (size_t)m * stride);
       if (rc) return rc;
       CK(cudaMemcpy2DAsync(c->q6_scratch, stride, w, 210u * nb, 210u * nb, m, cudaMemcpyDeviceToDevice, st));

@@ -107,6 +107,19 @@ int shk_cuda_matmul_q6k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev,
  * planar layout (to_planar != 0) or back to GGUF blocks.  Async on stream. */
 int shk_cuda_q6k_repack(shk_ctx *ctx, void *w_dev, uint32_t rows, uint32_t k, uint32_t row_stride,
                         int to_planar, void *stream);
+/* ---- batched prefill matmul on the tensor cores.  No counterpart in the
+ *      reference, which feeds prompt tokens one at a time
+ *      (engine/src/engine.c:306-501); this is the contraction those n_tokens
+ *      op_matmul_q4_k / op_matmul_q6_k calls (engine/src/ops.c:266-314,
+ *      361-404) add up to: y[t][r] = sum_k W[r][k] * x[t][k] for t <
+ *      n_tokens, x fp32 [n_tokens][k], y fp32 [n_tokens][m].  Weights are
+ *      dequantised to bf16 tiles and multiplied bf16 x bf16 -> fp32 with
+ *      tcgen05.mma (accumulators in TMEM), so results carry bf16 input
+ *      rounding.  dtype 12 (Q4_K) or SHK_DTYPE_Q6_K_PLANAR; row_stride 0 =
+ *      dense rows.  Async on stream. ---- */
+int shk_cuda_prefill_matmul(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
+                            const float *x_dev, float *y_dev, uint32_t m, uint32_t k, uint32_t n_tokens,
+                            void *stream);
 /* dequantise-matvec by dtype: 12 (Q4_K), 14 (GGUF Q6_K) or
  * SHK_DTYPE_Q6_K_PLANAR; row_stride 0 = dense rows. */
 int shk_cuda_matvec(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,

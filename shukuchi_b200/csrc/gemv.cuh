@@ -86,6 +86,14 @@ cudaError_t gemv_launch(const GemvPlan& p, cudaStream_t stream);
 cudaError_t q6k_repack_launch(void* w, uint32_t rows, uint32_t k, uint32_t stride, bool to_planar,
                               int num_sms, cudaStream_t st);
 
+// Batched dequantise-matmul on the tensor cores (prefill.cu): y[t][m] for
+// n_tokens tokens; x fp32 [n_tokens][k] is first converted into xb_scratch
+// (prefill_x_bytes) as bf16.  qt: T_Q4K or T_Q6K_PLANAR.
+size_t prefill_x_bytes(uint32_t k, uint32_t n_tokens);
+cudaError_t prefill_launch(uint32_t qt, const void* w, uint32_t row_stride, const float* x, void* xb_scratch,
+                           float* y, uint32_t m, uint32_t k, uint32_t n_tokens, int* err, int num_sms,
+                           cudaStream_t st);
+
 // Simple fallback for layouts the staged kernel does not take (rows not a
 // multiple of 16 bytes; GGUF-layout Q6_K).  Same math, plain loads.
 cudaError_t gemv_generic_launch(uint32_t qt, const void* w, const float* x, float* y, uint32_t m,

@@ -86,6 +86,8 @@ struct shk_ctx {
   size_t hv_w_cap = 0;
   void* q6_scratch = nullptr;  // GGUF-layout Q6_K rows repacked for the staged GEMV
   size_t q6_scratch_cap = 0;
+  void* pf_x = nullptr;  // bf16 copy of the prefill activations
+  size_t pf_x_cap = 0;
   float* hv_x = nullptr;
   size_t hv_x_cap = 0;
   float* hv_y = nullptr;
@@ -318,6 +320,7 @@ void shk_cuda_shutdown(shk_ctx* c) {
   cudaFreeHost(c->h_freq);
   cudaFree(c->hv_w);
   cudaFree(c->q6_scratch);
+  cudaFree(c->pf_x);
   cudaFree(c->hv_x);
   cudaFree(c->hv_y);
   if (c->compute) cudaStreamDestroy(c->compute);
@@ -393,6 +396,22 @@ int shk_cuda_matvec(shk_ctx* c, uint32_t dtype, const void* w, uint32_t row_stri
   if (!c) return SHK_EINVAL;
   return matvec_dev(c, dtype, w, row_stride, x, y, m, k, pick(c, s));
 }
+int shk_cuda_prefill_matmul(shk_ctx* c, uint32_t dtype, const void* w, uint32_t row_stride, const float* x,
+                            float* y, uint32_t m, uint32_t k, uint32_t n_tokens, void* s) {
+  if (!c || !w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
+  if (dtype != T_Q4K && dtype != T_Q6K_PLANAR) return SHK_EUNSUPPORTED;
+  if (m == 0 || n_tokens == 0) return SHK_OK;
+  const uint32_t nb = k / QK;
+  const uint32_t dense = nb * (dtype == T_Q4K ? Q4K_BYTES : Q6K_BYTES);
+  const uint32_t stride = row_stride ? row_stride : dense;
+  if (stride < dense || stride % 16 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 7))
+    return SHK_EINVAL;
+  int rc = grow(&c->pf_x, &c->pf_x_cap, prefill_x_bytes(k, n_tokens));
+  if (rc) return rc;
+  CK(prefill_launch(dtype, w, stride, x, c->pf_x, y, m, k, n_tokens, c->d_err, c->num_sms, pick(c, s)));
+  return SHK_OK;
+}
+
 int shk_cuda_q6k_repack(shk_ctx* c, void* w, uint32_t rows, uint32_t k, uint32_t row_stride, int to_planar,
                         void* s) {
   if (!c || !w || k == 0 || k % QK) return SHK_EINVAL;

@@ -87,6 +87,7 @@ _SIGS = {
     "shk_cuda_q6k_repack": (I, [P, P, U32, U32, U32, I, P]),
     "shk_cuda_layer_stage_q6k_planar": (I, [P, U32, P, U32, U32, U32]),
     "shk_cuda_matvec": (I, [P, U32, P, U32, P, P, U32, U32, P]),
+    "shk_cuda_prefill_matmul": (I, [P, U32, P, U32, P, P, U32, U32, U32, P]),
     "shk_cuda_tp_unique_id": (I, [P, SZ]),
     "shk_cuda_tp_init": (I, [P, I, I, P]),
     "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),
@@ -199,6 +200,11 @@ class Context:
     def matvec(self, dtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int, row_stride: int = 0,
                stream: int | None = None) -> None:
         _call("shk_cuda_matvec", self.h, dtype, w_dev, row_stride, x_dev, y_dev, m, k, stream)
+
+    def prefill_matmul(self, dtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int, n_tokens: int,
+                       row_stride: int = 0, stream: int | None = None) -> None:
+        """y[t][r] = sum_k W[r][k] x[t][k] on the tensor cores (bf16 inputs)."""
+        _call("shk_cuda_prefill_matmul", self.h, dtype, w_dev, row_stride, x_dev, y_dev, m, k, n_tokens, stream)
 
     def tp_init(self, rank: int, world: int, uid: bytes) -> None:
         """Joins this context to a tensor-parallel group of `world` ranks

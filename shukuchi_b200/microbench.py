@@ -8,6 +8,11 @@
       CUDA graph, CUDA-event timing on the launching stream.
       Bytes per launch = weights + 4*K (x) + 4*M (y).
 
+  python -m shukuchi_b200.microbench prefill [--shapes QT,M,K ...] [--tokens T]
+      Batched (prefill) dequantise-matmul of T tokens (default 512) on the
+      tensor cores over the GEMV sweep's matrices; TFLOP/s = 2 M K T / time
+      against the measured dense bf16 peak.
+
   python -m shukuchi_b200.microbench kv [--ctx C ...] [--batch B ...]
       Q8_0 KV cache: 64 query / 8 KV heads, head_dim 128, K/V ~ N(0,1).
       One step = for each of B independent sequences, append one new K/V row
@@ -123,6 +128,59 @@ def gemv(args, ctx) -> None:
                           "frac": round(gbs / peak, 4), "peak_gbs": peak, "peak_kind": kind,
                           "copies": ncopy}), flush=True)
         del g, ws
+        torch.cuda.empty_cache()
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = os.path.join(_ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def prefill(args, ctx) -> None:
+    """Batched dequantise-matmul on the tensor cores: T tokens through each
+    matrix of the GEMV sweep; one call = bf16 conversion of x + the tcgen05
+    kernel.  TFLOP/s = 2 M K T / time."""
+    peak, kind = bf16_peak()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    shapes = [tuple(int(v) for v in s.split(",")) for s in args.shapes] if args.shapes else GEMV_SHAPES
+    T = args.tokens
+    for qt, m, k in shapes:
+        row = (k // QK) * BLOCK_BYTES[qt]
+        stride = (row + 15) // 16 * 16
+        w = torch.empty(m * stride, dtype=torch.uint8, device="cuda")
+        _fill_blocks(w, qt, m, k, stride, gen)
+        dt = qt
+        if qt == 14:
+            torch.cuda.synchronize()
+            ctx.q6k_repack(w.data_ptr(), m, k, stride, True)
+            ctx.sync()
+            dt = sc.DTYPE_Q6_K_PLANAR
+        x = torch.randn(T, k, device="cuda", generator=gen)
+        y = torch.empty(T, m, device="cuda")
+        s = torch.cuda.Stream()
+        n = args.launches
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                ctx.prefill_matmul(dt, w.data_ptr(), x.data_ptr(), y.data_ptr(), m, k, T, row_stride=stride,
+                                   stream=s.cuda_stream)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(n):
+                    ctx.prefill_matmul(dt, w.data_ptr(), x.data_ptr(), y.data_ptr(), m, k, T, row_stride=stride,
+                                       stream=s.cuda_stream)
+        ms = _time_graph(g, s, args.reps)
+        ctx.check()
+        us = ms * 1000.0 / n
+        tf = 2.0 * m * k * T / (us * 1e-6) / 1e12
+        print(json.dumps({"bench": "prefill", "qtype": "Q4_K" if qt == 12 else "Q6_K", "m": m, "k": k,
+                          "tokens": T, "us": round(us, 2), "tflops": round(tf, 1), "frac": round(tf / peak, 4),
+                          "peak_tflops": peak, "peak_kind": kind}), flush=True)
+        del g
         torch.cuda.empty_cache()
 
 
@@ -290,6 +348,11 @@ def main() -> None:
     g.add_argument("--launches", type=int, default=20)
     g.add_argument("--reps", type=int, default=5)
     k = sub.add_parser("kv")
+    pf = sub.add_parser("prefill")
+    pf.add_argument("--shapes", nargs="*")
+    pf.add_argument("--tokens", type=int, default=512)
+    pf.add_argument("--launches", type=int, default=10)
+    pf.add_argument("--reps", type=int, default=5)
     k.add_argument("--ctx", type=int, nargs="*", default=[1024, 4096, 16384, 32768])
     k.add_argument("--batch", type=int, nargs="*", default=[1, 8, 32])
     k.add_argument("--reps", type=int, default=5)
@@ -307,7 +370,7 @@ def main() -> None:
     torch.cuda.set_device(0)
     ctx = sc.Context(0)
     try:
-        {"gemv": gemv, "kv": kv, "parts": parts, "timeline": timeline}[args.cmd](args, ctx)
+        {"gemv": gemv, "kv": kv, "parts": parts, "timeline": timeline, "prefill": prefill}[args.cmd](args, ctx)
     finally:
         ctx.close()
 

@@ -14,7 +14,9 @@ Weights exceed L2 (126 MB), so no flush is needed between steps.
 At --gpus N > 1 the same single sequence is decoded tensor-parallel over N
 GPUs (one process per GPU; Wq/Wk/Wv/gate/up split by output rows, Wo/down by
 input columns, KV heads local to a rank, output head split by vocabulary rows;
-NCCL all-reduce after O and down inside the captured step): strong scaling,
+NCCL all-reduce after O and down inside the captured step; `--p2p-allreduce`
+sends the partial rows straight into every rank's exchange buffer over NVLink
+and lets the next GEMV sum them instead): strong scaling,
 timed as the max over ranks.  Each rank generates its shard's synthetic
 weights directly (same distributions, rank-seeded).
 ``--impl reference`` times the reference's own C implementation of the path
@@ -51,6 +53,8 @@ def parse():
     ap.add_argument("--shape", default="llama8b")
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--p2p-allreduce", action="store_true",
+                    help="tensor parallel: the peer-memory exchange inside the GEMVs instead of NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -262,6 +266,10 @@ def run_ours(args, ws, rank, local):
     m = sc.DeviceModel(ctx, kv, wts.desc)
     if ws > 1:
         m.set_tp_rows(lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi)
+        if args.p2p_allreduce:  # all-reduce over NVLink peer memory inside the GEMVs
+            hs = [None] * ws
+            dist.all_gather_object(hs, m.tp_p2p_export())
+            m.tp_p2p_import(hs, [(L.o_lo, L.o_hi) for L in (tpl.layout(shape, r, ws) for r in range(ws))])
     for i, lv in enumerate(wts.layers):
         m.set_layer(i, lv)
     stream = torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{local}")
@@ -324,10 +332,12 @@ def run_ours(args, ws, rank, local):
 
     # dominant kernel: gate/up Q4_K GEMV (dual matrix, SwiGLU epilogue), timed
     # per launch with events on the launching stream, rotating layers so no
-    # launch finds its weights in L2
+    # launch finds its weights in L2.  (Tensor parallel with the peer-memory
+    # exchange: the parts wait on the peers, so they are not launched alone.)
+    solo_parts = ws == 1 or not args.p2p_allreduce
     durs = []
     wbytes = 0
-    for i in range(max(args.steps, 32)):
+    for i in range(max(args.steps, 32) if solo_parts else 0):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         wbytes = m.launch_part(i % shape.n_layers, GATEUP_PART)
@@ -335,12 +345,12 @@ def run_ours(args, ws, rank, local):
         durs.append((a, b))
     torch.cuda.synchronize()
     ctx.check()
-    avg = sum(a.elapsed_time(b) for a, b in durs[4:]) / len(durs[4:]) / 1000.0
+    avg = sum(a.elapsed_time(b) for a, b in durs[4:]) / len(durs[4:]) / 1000.0 if durs else None
     # per-part device time of one token (each part launched alone, all layers;
     # these serialise launches that the captured step overlaps, so they sum
     # to a little more than ms_per_step)
     parts = {}
-    for part, name in enumerate(PART_NAMES):
+    for part, name in enumerate(PART_NAMES if solo_parts else ()):
         evs = []
         n = 1 if part == 5 else shape.n_layers
         for rep in range(2):
@@ -356,7 +366,7 @@ def run_ours(args, ws, rank, local):
     ctx.check()
     alg = wbytes + 4 * (shape.n_embd + lshape.n_ff)
     peak, peak_kind = peaks()
-    achieved = alg / avg / 1e9
+    achieved = alg / avg / 1e9 if avg else None
     # whole-step bytes at the mean context of the timed region, summed over
     # ranks (tensor parallel duplicates a few rows), against ws x the peak
     mean_ctx = args.prompt + args.warmup + args.steps / 2
@@ -383,10 +393,14 @@ def run_ours(args, ws, rank, local):
         "clocks": clk.summary(),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K> gate/up (dual) + SwiGLU",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "bytes_per_launch": alg,
-                     "traffic": ncu_traffic("gemv_gateup_llama8b.md") if ws == 1 else None},
+        "roofline": ({"bound": "hbm", "kernel": "gemv_kernel<Q4_K> gate/up (dual) + SwiGLU",
+                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                      "peak_kind": peak_kind, "bytes_per_launch": alg,
+                      "traffic": ncu_traffic("gemv_gateup_llama8b.md") if ws == 1 else None}
+                     if achieved else
+                     {"bound": "hbm", "kernel": "whole decode step (tensor parallel, summed over ranks)",
+                      "achieved": step_gbs, "peak": ws * peak, "unit": "GB/s", "frac": step_gbs / (ws * peak),
+                      "peak_kind": peak_kind, "bytes_per_launch": step_bytes, "traffic": None}),
         "token_parts_us": parts,
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
                           "frac": step_gbs / (ws * peak)},
@@ -402,6 +416,7 @@ def run_ours(args, ws, rank, local):
 
 
 def main():
+    os.environ["NCCL_DEBUG"] = "WARN"  # one JSON line on stdout: no NCCL version banner
     args = parse()
     ws, rank, local = dist_setup(args)
     if args.impl == "reference":

@@ -302,6 +302,21 @@ int shk_cuda_tp_init(shk_ctx *ctx, int rank, int world, const void *id);
  * shk_cuda_model_set_layer. */
 int shk_cuda_model_set_tp_rows(shk_model *m, uint32_t o_lo, uint32_t o_hi, uint32_t v_lo, uint32_t v_hi);
 
+/* Tensor-parallel all-reduce over NVLink peer memory instead of NCCL: the O
+ * and down GEMVs send their partial output rows straight into every rank's
+ * exchange buffer (plain peer stores) and raise a per-rank flag; the next
+ * GEMV waits for the flags (bounded), adds the residual and the partials in
+ * rank order and proceeds -- no collective kernel between them.  Setup, after
+ * shk_cuda_model_set_tp_rows and before shk_cuda_model_set_layer: every rank
+ * exports its buffer's IPC handle (64 bytes, returned size), the caller
+ * gathers them in rank order and every rank imports the set together with
+ * every rank's O rows (o_ranges: world x {o_lo, o_hi}).  The ranks must run
+ * on separate GPUs of one node, one process per GPU (CUDA IPC).  NCCL is
+ * still used for the vocabulary-split argmax.  No counterpart in the
+ * reference. */
+int shk_cuda_model_tp_p2p_export(shk_model *m, void *handle_out, size_t cap);
+int shk_cuda_model_tp_p2p_import(shk_model *m, const void *handles, const uint32_t *o_ranges);
+
 /* ---- argmax without any device allocation.  No counterpart in the reference:
  *      it exists for callers that cannot call cudaMalloc (a sampler inside a
  *      host runtime that has already reserved the device's memory in its own

@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
       for (int r = 0; r < GEMV_KS_ROWT; ++r) R.kcnt[tid * GEMV_KS_ROWT + r] = 0;
     } else {
       mbar_init(xbar, GEMV_WARPS);
+      reinterpret_cast<int*>(red)[31] = 0;  // tensor-parallel producer: finished warps
     }
     fence_mbar_init();
   }
@@ -86,6 +87,36 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true, &np);
   uint32_t gtask = 0;
   gemv_consume<HAS4, HAS6>(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
+  if (a.tp.out) gemv_tp_signal(a, reinterpret_cast<int*>(red + 31), lane);
+}
+
+// Tensor-parallel exchange sum as a kernel of its own (for a consumer that is
+// not a staged GEMV): res_out = res_in + partials in rank order.
+__global__ void tp_sum_kernel(const __grid_constant__ GemvTp t, const float* __restrict__ res_in, int* err) {
+  __shared__ int ok;
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint32_t ep = __ldcg(t.epoch);
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t r = 0; r < t.world && ok; ++r)
+      for (uint32_t n = 0; (int)(ld_acquire_sys(t.flags_in + r) - ep) < 0; ++n) {
+        __nanosleep(64);
+        if ((n & 31) == 31 && globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
+          set_error(err, DERR_TIMEOUT_GRID);
+          ok = 0;
+          break;
+        }
+      }
+  }
+  __syncthreads();
+  for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < t.d; k += gridDim.x * blockDim.x) {
+    float v = __ldcg(res_in + k);
+    for (uint32_t r = 0; r < t.world && ok; ++r)
+      if (k >= t.cov_lo[r] && k < t.cov_hi[r]) v += __ldcg(t.parts_in + (size_t)r * t.d + k);
+    t.res_out[k] = v;
+  }
 }
 
 // --------------------------- generic fallback ---------------------------------
@@ -246,6 +277,10 @@ cudaError_t gemv_launch(const GemvPlan& p, cudaStream_t stream) {
   if (p.has4)
     return launch_k(gemv_kernel<true, false>, dim3(p.grid), dim3(GEMV_THREADS), p.smem, stream, p.args);
   return launch_k(gemv_kernel<false, true>, dim3(p.grid), dim3(GEMV_THREADS), p.smem, stream, p.args);
+}
+
+cudaError_t gemv_tp_sum_launch(const GemvArgs& a, cudaStream_t st) {
+  return launch_k(tp_sum_kernel, dim3((a.tp.d + 255) / 256), dim3(256), 0, st, a.tp, a.x, a.err);
 }
 
 cudaError_t gemv_generic_launch(uint32_t qt, const void* w, const float* x, float* y, uint32_t m,

@@ -12,6 +12,7 @@ enum GemvEpi : uint8_t {
   EPI_ADD = 1,     // y[r] += acc            (residual add, engine/src/engine.c:164-166)
   EPI_ROPE = 2,    // RoPE on the (2i, 2i+1) pair, then store (engine/src/ops.c:216-238)
   EPI_SWIGLU = 3,  // dual rows: y[r] = silu(gate) * up    (engine/src/ops.c:491-496)
+  EPI_TP = 4,      // partial rows to every rank's exchange buffer (GemvTp)
 };
 
 constexpr int GEMV_MAX_SEGS = 4;
@@ -37,6 +38,29 @@ struct GemvSeg {
   uint8_t ks;           // K slices per row task (long rows: one warp per slice)
 };
 
+// Tensor-parallel exchange over NVLink peer memory (one-shot all-reduce fused
+// into the GEMVs).  A producer GEMV (out) writes its partial output rows
+// (absolute rows row_off + r) into parts_out[p] + rank * d on every rank p;
+// its last CTA then stores the step's epoch into flags_out[p][rank].  A
+// consumer GEMV (in) waits until flags_in[r] reaches the epoch for every rank
+// r and takes x[k] = res_in[k] + sum over r in rank order of parts_in[r*d + k]
+// for k in [cov_lo[r], cov_hi[r]); CTA 0 also writes x to res_out (the
+// residual stream of the next step).
+constexpr int GEMV_TP_MAX = 8;
+struct GemvTp {
+  const float* parts_in;
+  const uint32_t* flags_in;
+  float* res_out;
+  float* parts_out[GEMV_TP_MAX];
+  uint32_t* flags_out[GEMV_TP_MAX];
+  uint32_t* counter;        // producer: CTAs done (the last one signals, then resets it)
+  const uint32_t* epoch;    // device step counter (advanced by the embedding kernel)
+  uint32_t cov_lo[GEMV_TP_MAX], cov_hi[GEMV_TP_MAX];
+  uint32_t d;               // elements of one partial
+  uint32_t row_off;         // producer: absolute row of output row 0
+  uint8_t rank, world, in, out;
+};
+
 struct GemvArgs {
   GemvSeg seg[GEMV_MAX_SEGS];
   uint32_t nseg;
@@ -49,6 +73,7 @@ struct GemvArgs {
   uint32_t n_stages;        // ring depth (<= GEMV_MAX_STAGES)
   uint64_t total_cost;      // sum over segments of units * unit_cost
   int* err;                 // device error word
+  GemvTp tp;                // tensor-parallel exchange (tp.in / tp.out = 0: none)
 };
 
 struct GemvPlan {
@@ -93,6 +118,10 @@ size_t prefill_x_bytes(uint32_t k, uint32_t n_tokens);
 cudaError_t prefill_launch(uint32_t qt, const void* w, uint32_t row_stride, const float* x, void* xb_scratch,
                            float* y, uint32_t m, uint32_t k, uint32_t n_tokens, int* err, int num_sms,
                            cudaStream_t st);
+
+// The tensor-parallel consumer sum of plan args a.tp / a.x as a kernel of its
+// own (writes a.tp.res_out).
+cudaError_t gemv_tp_sum_launch(const GemvArgs& a, cudaStream_t st);
 
 // Simple fallback for layouts the staged kernel does not take (rows not a
 // multiple of 16 bytes; GGUF-layout Q6_K).  Same math, plain loads.

@@ -278,6 +278,15 @@ __device__ __forceinline__ void store2(const GemvArgs& a, const GemvSeg& g, uint
     return;
   }
   const bool two = g.rl == 2 && nvalid > 1;
+  if (g.epi == EPI_TP) {  // peer stores over NVLink; the last CTA raises the flags
+    const GemvTp& t = a.tp;
+    const size_t base = (size_t)t.rank * t.d + t.row_off + row;
+    for (uint32_t p = 0; p < t.world; ++p) {
+      t.parts_out[p][base] = o0;
+      if (two) t.parts_out[p][base + 1] = o1;
+    }
+    return;
+  }
   if (g.epi == EPI_ROPE) {
     // (2i, 2i+1) pairs are the two rows of this lane (rl = 2, row even)
     if (!two) return;
@@ -531,9 +540,97 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // Rolled loops: this runs once per launch, compact code matters more.
 // Ends with a consumer-only barrier.
 // Step 1 of the prologue: start the copies of raw x into this lane's slots.
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Tensor-parallel consumer: wait (bounded) for every rank's partial of this
+// step, then x = residual + partials in rank order, into the raw-x slots.
+__device__ __forceinline__ bool gemv_x_tp(const GemvArgs& a, const XBuf& xb_, int warp, int lane) {
+  const GemvTp& t = a.tp;
+  const uint32_t NB = a.k / 256;
+  float4* xr = reinterpret_cast<float4*>(xb_.xq);
+  const uint32_t ep = __ldcg(t.epoch);
+  bool ok = true;
+  if (lane == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t r = 0; r < t.world && ok; ++r) {
+      for (uint32_t n = 0; (int)(ld_relaxed_sys(t.flags_in + r) - ep) < 0; ++n) {
+        __nanosleep(64);
+        if ((n & 31) == 31 && globaltimer_ns() - t0 > WAIT_BUDGET_NS) {
+          set_error(a.err, DERR_TIMEOUT_GRID);
+          ok = false;
+          break;
+        }
+      }
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");  // acquire: the partials are read below
+  }
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __syncwarp();
+#pragma unroll 1
+  for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
+    const uint32_t e0 = 256 * kb + 8 * lane;
+    float4 v[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) v[h] = __ldcg(reinterpret_cast<const float4*>(a.x + e0) + h);
+    for (uint32_t r = 0; r < t.world && ok; ++r) {
+      if (e0 < t.cov_lo[r] || e0 >= t.cov_hi[r]) continue;  // ranges are multiples of 8 elements
+      const float4* pr = reinterpret_cast<const float4*>(t.parts_in + (size_t)r * t.d + e0);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float4 q = __ldcg(pr + h);
+        v[h].x += q.x;
+        v[h].y += q.y;
+        v[h].z += q.z;
+        v[h].w += q.w;
+      }
+    }
+    const uint32_t v0 = 64 * kb + 2 * lane;
+    xr[xpad(v0)] = v[0];
+    xr[xpad(v0 + 1)] = v[1];
+    if (blockIdx.x == 0) {
+      reinterpret_cast<float4*>(t.res_out + e0)[0] = v[0];
+      reinterpret_cast<float4*>(t.res_out + e0)[1] = v[1];
+    }
+  }
+  return ok;
+}
+
+// Tensor-parallel producer, after this warp's last task: once every consumer
+// warp of every CTA is done, the last one raises this rank's flag on every
+// rank.  `done` counts this CTA's finished warps (shared memory).
+__device__ __forceinline__ void gemv_tp_signal(const GemvArgs& a, int* done, int lane) {
+  const GemvTp& t = a.tp;
+  __syncwarp();
+  if (lane != 0) return;
+  __threadfence_block();  // release (CTA scope): this warp's stores before its count
+  if (atomicAdd(done, 1) != GEMV_WARPS - 1) return;
+  // the CTA's last warp: one system-scope fence orders every warp's peer
+  // stores (they happen before it through the counts) before the count below
+  __threadfence_system();
+  if (atomicAdd(t.counter, 1u) != gridDim.x - 1) return;
+  __threadfence_system();
+  const uint32_t ep = __ldcg(t.epoch);
+  for (uint32_t p = 0; p < t.world; ++p)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(t.flags_out[p] + t.rank), "r"(ep) : "memory");
+  *t.counter = 0;
+}
+
 __device__ __forceinline__ void gemv_x_issue(const GemvArgs& a, const XBuf& xb_, int warp, int lane) {
   const uint32_t NB = a.k / 256;
   float4* xr = reinterpret_cast<float4*>(xb_.xq);  // raw x staged in the limb slots
+  if (a.tp.in) {
+    gemv_x_tp(a, xb_, warp, lane);
+    return;
+  }
   const bool xal = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
 #pragma unroll 1
   for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {

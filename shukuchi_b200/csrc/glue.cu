@@ -17,11 +17,14 @@ using namespace gldev;
 
 // op_embed (engine/src/ops.c:533-577).  The token id is read from device
 // memory so a captured graph can feed back the argmax.
+// step (optional): a device step counter advanced once per token (the epoch of
+// the tensor-parallel exchange).
 __global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t dtype,
                              const uint32_t* __restrict__ tok_p, uint32_t n_vocab, float* out,
-                             uint32_t n_embd, int* err) {
+                             uint32_t n_embd, int* err, uint32_t* step) {
   pdl_trigger();
   pdl_wait();
+  if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;
   const uint32_t tok = *tok_p;
   if (tok >= n_vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) set_error(err, DERR_BAD_TOKEN);
@@ -153,9 +156,9 @@ __global__ void add_kernel(float* y, const float* x, uint32_t n) {
 }  // namespace
 
 cudaError_t embed_launch(const void* table, uint32_t dtype, const uint32_t* tok, uint32_t n_vocab,
-                         float* out, uint32_t n_embd, int* err, cudaStream_t st) {
+                         float* out, uint32_t n_embd, int* err, cudaStream_t st, uint32_t* step) {
   return launch_k(embed_kernel, dim3((n_embd + 255) / 256), dim3(256), 0, st,
-                  static_cast<const uint8_t*>(table), dtype, tok, n_vocab, out, n_embd, err);
+                  static_cast<const uint8_t*>(table), dtype, tok, n_vocab, out, n_embd, err, step);
 }
 
 int argmax_blocks(uint32_t n) {

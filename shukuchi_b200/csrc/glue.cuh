@@ -7,7 +7,7 @@
 namespace shk {
 
 cudaError_t embed_launch(const void* table, uint32_t dtype, const uint32_t* tok, uint32_t n_vocab,
-                         float* out, uint32_t n_embd, int* err, cudaStream_t st);
+                         float* out, uint32_t n_embd, int* err, cudaStream_t st, uint32_t* step = nullptr);
 int argmax_blocks(uint32_t n);
 cudaError_t argmax_launch(const float* x, uint32_t n, float* part_v, uint32_t* part_i, int* counter,
                           uint32_t* tok_out, uint32_t* pos_inc, cudaStream_t st, uint32_t idx_off = 0,

@@ -153,6 +153,21 @@ struct shk_model {
   } pk;
   uint32_t o_lo = 0, o_hi = 0;  // tensor parallel: this rank's rows of the O projection output
   uint32_t v_lo = 0, v_hi = 0;  // ... and of the output head (logits); all rows when replicated
+  // Tensor-parallel exchange over NVLink peer memory (shk_cuda_model_tp_p2p_*):
+  // a symmetric buffer per rank, [flags: slot][rank] then [parts: slot][rank][n_embd],
+  // one slot per all-reduce of a token (2 per layer); the residual stream
+  // alternates between hidden and res2.
+  struct P2p {
+    bool on = false;
+    void* base = nullptr;          // this rank's symmetric buffer
+    size_t flag_bytes = 0, bytes = 0;
+    void* peer_base[GEMV_TP_MAX] = {};  // every rank's buffer (own included)
+    bool opened[GEMV_TP_MAX] = {};
+    uint32_t* counters = nullptr;  // per slot: producer CTAs done
+    uint32_t* d_step = nullptr;    // epoch, advanced by the embedding kernel
+    float* res2 = nullptr;
+    uint32_t cov_lo[GEMV_TP_MAX] = {}, cov_hi[GEMV_TP_MAX] = {};
+  } p2p;
   uint32_t* tp_pairs = nullptr; // world x {max value bits, index}: argmax over the vocabulary slices
   uint64_t* d_trace = nullptr;  // persistent-kernel timeline (shk_cuda_model_trace_enable)
   uint32_t trace_phases = 0;
@@ -612,7 +627,46 @@ void model_free_graphs(shk_model* m) {
   k = shk_model::Persist{};
 }
 
-int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
+// Tensor-parallel exchange fields of a plan: slot j's consumer (in) or producer
+// (out); see GemvTp.
+void p2p_in(shk_model* m, GemvArgs& a, uint32_t j, const float* res_in, float* res_out) {
+  const auto& q = m->p2p;
+  const uint32_t W = (uint32_t)m->ctx->tp_world, D = m->d.n_embd;
+  GemvTp& t = a.tp;
+  t.in = 1;
+  t.rank = (uint8_t)m->ctx->tp_rank;
+  t.world = (uint8_t)W;
+  t.d = D;
+  t.flags_in = reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(q.base)) + (size_t)j * W;
+  t.parts_in = reinterpret_cast<const float*>(static_cast<uint8_t*>(q.base) + q.flag_bytes) + (size_t)j * W * D;
+  t.res_out = res_out;
+  t.epoch = q.d_step;
+  const bool after_o = (j & 1) == 0;  // O partials cover each rank's O rows; down partials all rows
+  for (uint32_t r = 0; r < W; ++r) {
+    t.cov_lo[r] = after_o ? q.cov_lo[r] : 0;
+    t.cov_hi[r] = after_o ? q.cov_hi[r] : D;
+  }
+  a.x = res_in;
+}
+void p2p_out(shk_model* m, GemvArgs& a, uint32_t j, uint32_t row_off) {
+  const auto& q = m->p2p;
+  const uint32_t W = (uint32_t)m->ctx->tp_world, D = m->d.n_embd;
+  GemvTp& t = a.tp;
+  t.out = 1;
+  t.rank = (uint8_t)m->ctx->tp_rank;
+  t.world = (uint8_t)W;
+  t.d = D;
+  t.row_off = row_off;
+  t.counter = q.counters + j;
+  t.epoch = q.d_step;
+  for (uint32_t p = 0; p < W; ++p) {
+    uint8_t* b = static_cast<uint8_t*>(q.peer_base[p]);
+    t.flags_out[p] = reinterpret_cast<uint32_t*>(b) + (size_t)j * W;
+    t.parts_out[p] = reinterpret_cast<float*>(b + q.flag_bytes) + (size_t)j * W * D;
+  }
+}
+
+int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P, uint32_t layer) {
   const shk_model_desc& d = m->d;
   shk_ctx* c = m->ctx;
   const uint32_t hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
@@ -624,9 +678,12 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
   };
   int rc = gemv_plan(P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos, m->d_freq, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
-  // Tensor parallel: rank 0 adds the residual, the others store their partial
-  // sums (all-reduced afterwards); the O projection covers rows [o_lo, o_hi).
-  const uint8_t res_epi = c->tp_rank == 0 ? EPI_ADD : EPI_STORE;
+  // Tensor parallel over NCCL: rank 0 adds the residual, the others store
+  // their partial sums (all-reduced afterwards); the O projection covers rows
+  // [o_lo, o_hi).  Over peer memory (p2p): every rank sends pure partials
+  // (EPI_TP) and the consumer adds the residual.
+  const bool p2p = m->p2p.on;
+  const uint8_t res_epi = p2p ? EPI_TP : (c->tp_rank == 0 ? EPI_ADD : EPI_STORE);
   GemvMat o{lv.attn_o, nullptr, m->hidden + m->o_lo, m->o_hi - m->o_lo, lv.attn_o_dtype, 0, res_epi, 0};
   rc = gemv_plan(P.o, &o, 1, qd, m->att, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
@@ -637,6 +694,15 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P) {
   GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, res_epi, 0};
   rc = gemv_plan(P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
   if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  if (p2p) {
+    // slots: 2l = O of layer l (consumed by gate/up), 2l + 1 = down (consumed
+    // by the next layer's QKV or the head); consumer j reads the residual
+    // from buffer j % 2 (0 = hidden, 1 = res2) and writes it to the other
+    if (layer > 0) p2p_in(m, P.qkv.args, 2 * layer - 1, m->p2p.res2, m->hidden);
+    p2p_out(m, P.o.args, 2 * layer, m->o_lo);
+    p2p_in(m, P.gateup.args, 2 * layer, m->hidden, m->p2p.res2);
+    p2p_out(m, P.down.args, 2 * layer + 1, 0);
+  }
   P.ok = true;
   return SHK_OK;
 }
@@ -680,12 +746,13 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
   pdl_enabled() = pdl;
   const AttnArgs a = layer_attn_args(m, layer, pos);
   CK(attn_decode_launch(a, st));
-  if (tp && c->tp_rank != 0 && m->o_hi - m->o_lo < m->d.n_embd) {  // rows this rank does not write
+  const bool nccl_ar = tp && !m->p2p.on;
+  if (nccl_ar && c->tp_rank != 0 && m->o_hi - m->o_lo < m->d.n_embd) {  // rows this rank does not write
     CK(cudaMemsetAsync(m->hidden, 0, (size_t)m->d.n_embd * sizeof(float), st));
     pdl_enabled() = false;
   }
   CK(gemv_launch(P.o, st));
-  if (tp) {
+  if (nccl_ar) {
     if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
       return SHK_ENCCL;
     pdl_enabled() = false;
@@ -693,7 +760,7 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
   CK(gemv_launch(P.gateup, st));
   pdl_enabled() = pdl;
   CK(gemv_launch(P.down, st));
-  if (tp) {
+  if (nccl_ar) {
     if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
       return SHK_ENCCL;
     pdl_enabled() = false;
@@ -709,6 +776,25 @@ bool head_plan_ok(uint32_t dtype, int hp) {
 }
 
 bool vocab_split(const shk_model* m) { return m->v_hi - m->v_lo < m->d.n_vocab; }
+
+// (Re)plans the output head over rows [v_lo, v_hi); with the peer-memory
+// exchange the head is the consumer of the last layer's down partials.
+int plan_head(shk_model* m) {
+  shk_ctx* c = m->ctx;
+  const uint32_t nv = m->v_hi - m->v_lo;
+  GemvMat hm{m->d.output_dev, nullptr, m->logits + m->v_lo, nv, m->d.output_dtype, 0, EPI_STORE, 0};
+  const int hp = gemv_plan(m->head, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err,
+                           c->num_sms);
+  if (!head_plan_ok(m->d.output_dtype, hp)) return SHK_EUNSUPPORTED;
+  m->head_generic = hp != 0;
+  if (m->p2p.on) {
+    // the head consumes the last down partials: in its prologue, or (plain-load
+    // head) through a sum kernel before it that writes hidden
+    p2p_in(m, m->head.args, 2 * m->d.n_layers - 1, m->p2p.res2, m->hidden);
+  }
+  m->head_ok = true;
+  return SHK_OK;
+}
 
 // Tensor parallel with a split output head: every rank's logits slice is
 // gathered into the full vector (in place), e.g. before a copy to the host.
@@ -727,11 +813,16 @@ int gather_logits(shk_model* m, cudaStream_t st) {
 // merged in rank order.
 int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos, bool pdl_after_first = false) {
   const uint32_t nv = m->v_hi - m->v_lo;
-  if (m->head_generic)
+  if (m->head_generic) {
+    if (m->p2p.on) {
+      CK(gemv_tp_sum_launch(m->head.args, st));
+      pdl_enabled() = false;
+    }
     CK(gemv_generic_launch(m->d.output_dtype, m->d.output_dev, m->hidden, m->logits + m->v_lo, nv,
                            m->d.n_embd, st));
-  else
+  } else {
     CK(gemv_launch(m->head, st));
+  }
   if (pdl_after_first) pdl_enabled() = true;
   uint32_t* pos_inc = advance_pos ? m->d_tok + 1 : nullptr;
   if (!vocab_split(m)) {
@@ -752,7 +843,7 @@ int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos, bool pdl_after
 
 int enqueue_layers(shk_model* m, cudaStream_t st, bool pdl_after_first = false) {
   CK(embed_launch(m->d.tok_embd_dev, m->d.tok_embd_dtype, m->d_tok, m->d.n_vocab, m->hidden,
-                  m->d.n_embd, m->ctx->d_err, st));
+                  m->d.n_embd, m->ctx->d_err, st, m->p2p.on ? m->p2p.d_step : nullptr));
   if (pdl_after_first) pdl_enabled() = true;
   for (uint32_t l = 0; l < m->d.n_layers; ++l) {
     const int rc = enqueue_layer(m, m->plans[l], l, m->d_tok + 1, st, pdl_after_first);
@@ -981,6 +1072,12 @@ void shk_cuda_model_destroy(shk_model* m) {
   cudaFree(m->act);
   cudaFree(m->logits);
   cudaFree(m->tp_pairs);
+  for (int p = 0; p < GEMV_TP_MAX; ++p)
+    if (m->p2p.opened[p]) cudaIpcCloseMemHandle(m->p2p.peer_base[p]);
+  cudaFree(m->p2p.base);
+  cudaFree(m->p2p.counters);
+  cudaFree(m->p2p.d_step);
+  cudaFree(m->p2p.res2);
   cudaFree(m->am_v);
   cudaFree(m->am_i);
   cudaFree(m->am_cnt);
@@ -996,7 +1093,7 @@ float* shk_cuda_model_hidden(shk_model* m) { return m ? m->hidden : nullptr; }
 int shk_cuda_model_set_layer(shk_model* m, uint32_t layer, const shk_layer_desc* lv) {
   if (!m || !lv || layer >= m->d.n_layers) return SHK_EINVAL;
   LayerPlans P;
-  const int rc = build_layer_plans(m, *lv, P);
+  const int rc = build_layer_plans(m, *lv, P, layer);
   if (rc) return rc;
   m->layers[layer] = *lv;
   m->plans[layer] = P;
@@ -1009,8 +1106,9 @@ int shk_cuda_forward_layer(shk_model* m, const shk_layer_desc* lv, uint32_t laye
                            float* hidden, void* s) {
   if (!m || !lv || !hidden || layer >= m->d.n_layers || pos >= m->kv->L.max_seq) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
+  if (m->p2p.on) return SHK_EUNSUPPORTED;  // the exchange runs inside whole-token steps
   LayerPlans P;
-  int rc = build_layer_plans(m, *lv, P);
+  int rc = build_layer_plans(m, *lv, P, layer);
   if (rc) return rc;
   if (hidden != m->hidden) CK(cudaMemcpyAsync(m->hidden, hidden, m->d.n_embd * 4, cudaMemcpyDeviceToDevice, st));
   rc = enqueue_layer(m, P, layer, m->kv->d_iota + pos, st, false);
@@ -1144,7 +1242,7 @@ int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint3
   if (!m || o_lo >= o_hi || o_hi > m->d.n_embd || v_lo >= v_hi || v_hi > m->d.n_vocab) return SHK_EINVAL;
   for (uint32_t l = 0; l < m->d.n_layers; ++l)
     if (m->have[l]) return SHK_EINVAL;  // before any layer is registered
-  if (m->g_layers || m->g_head || m->g_loop) return SHK_EINVAL;  // graphs already captured
+  if (m->g_layers || m->g_head || m->g_loop || m->p2p.on) return SHK_EINVAL;  // graphs / exchange set up
   shk_ctx* c = m->ctx;
   const uint32_t nv = v_hi - v_lo;
   if (nv < m->d.n_vocab) {  // equal slices in rank order (the gathers need equal counts)
@@ -1153,16 +1251,74 @@ int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint3
     if (!m->tp_pairs && cudaMalloc(&m->tp_pairs, 2 * sizeof(uint32_t) * c->tp_world) != cudaSuccess)
       return SHK_ENOMEM;
   }
-  GemvMat hm{m->d.output_dev, nullptr, m->logits + v_lo, nv, m->d.output_dtype, 0, EPI_STORE, 0};
-  const int hp = gemv_plan(m->head, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err,
-                           c->num_sms);
-  if (!head_plan_ok(m->d.output_dtype, hp)) return SHK_EUNSUPPORTED;
-  m->head_generic = hp != 0;
-  m->o_lo = o_lo;
-  m->o_hi = o_hi;
+  const uint32_t ov_lo = m->v_lo, ov_hi = m->v_hi;
   m->v_lo = v_lo;
   m->v_hi = v_hi;
+  const int rc = plan_head(m);
+  if (rc) {
+    m->v_lo = ov_lo;
+    m->v_hi = ov_hi;
+    return rc;
+  }
+  m->o_lo = o_lo;
+  m->o_hi = o_hi;
   return SHK_OK;
+}
+
+int shk_cuda_model_tp_p2p_export(shk_model* m, void* handle_out, size_t cap) {
+  if (!m || !handle_out || cap < sizeof(cudaIpcMemHandle_t)) return SHK_EINVAL;
+  shk_ctx* c = m->ctx;
+  if (c->tp_world < 2 || c->tp_world > GEMV_TP_MAX) return SHK_EINVAL;
+  auto& q = m->p2p;
+  cudaSetDevice(c->device);
+  if (!q.base) {
+    const size_t W = (size_t)c->tp_world, D = m->d.n_embd, NS = 2 * (size_t)m->d.n_layers;
+    q.flag_bytes = (NS * W * 4 + 255) & ~(size_t)255;
+    q.bytes = q.flag_bytes + NS * W * D * 4;
+    if (cudaMalloc(&q.base, q.bytes) != cudaSuccess || cudaMalloc(&q.counters, NS * 4) != cudaSuccess ||
+        cudaMalloc(&q.d_step, 4) != cudaSuccess || cudaMalloc(&q.res2, D * 4) != cudaSuccess)
+      return SHK_ENOMEM;
+    CK(cudaMemset(q.base, 0, q.bytes));
+    CK(cudaMemset(q.counters, 0, NS * 4));
+    CK(cudaMemset(q.d_step, 0, 4));
+    CK(cudaMemset(q.res2, 0, D * 4));
+  }
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, q.base));
+  memcpy(handle_out, &h, sizeof(h));
+  return (int)sizeof(h);
+}
+
+int shk_cuda_model_tp_p2p_import(shk_model* m, const void* handles, const uint32_t* o_ranges) {
+  if (!m || !handles || !o_ranges) return SHK_EINVAL;
+  shk_ctx* c = m->ctx;
+  auto& q = m->p2p;
+  if (!q.base || q.on || m->g_layers || m->g_head || m->g_loop) return SHK_EINVAL;
+  for (uint32_t l = 0; l < m->d.n_layers; ++l)
+    if (m->have[l]) return SHK_EINVAL;  // before any layer is registered
+  cudaSetDevice(c->device);
+  const int W = c->tp_world;
+  for (int p = 0; p < W; ++p) {
+    if (o_ranges[2 * p] >= o_ranges[2 * p + 1] || o_ranges[2 * p + 1] > m->d.n_embd ||
+        o_ranges[2 * p] % 8 || o_ranges[2 * p + 1] % 8)
+      return SHK_EINVAL;
+    q.cov_lo[p] = o_ranges[2 * p];
+    q.cov_hi[p] = o_ranges[2 * p + 1];
+    if (p == c->tp_rank) {
+      q.peer_base[p] = q.base;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)p * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return SHK_ECUDA;
+    q.peer_base[p] = ptr;
+    q.opened[p] = true;
+  }
+  q.on = true;
+  const int rc = plan_head(m);
+  if (rc) q.on = false;
+  return rc;
 }
 
 int shk_cuda_model_trace_enable(shk_model* m, uint32_t n_phases) {
@@ -1202,6 +1358,7 @@ int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void
                                uint64_t* bytes_out) {
   if (!m || part > 5 || (part < 5 && (layer >= m->d.n_layers || !m->have[layer] || !m->plans[layer].ok)))
     return SHK_EINVAL;
+  if (m->p2p.on) return SHK_EUNSUPPORTED;  // parts wait on peers' partials
   cudaStream_t st = pick(m->ctx, s);
   auto wbytes = [](const GemvPlan& p) {
     uint64_t b = 0;

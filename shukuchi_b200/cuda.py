@@ -91,6 +91,8 @@ _SIGS = {
     "shk_cuda_tp_unique_id": (I, [P, SZ]),
     "shk_cuda_tp_init": (I, [P, I, I, P]),
     "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),
+    "shk_cuda_model_tp_p2p_export": (I, [P, P, SZ]),
+    "shk_cuda_model_tp_p2p_import": (I, [P, P, P]),
     "shk_cuda_kv_create": (P, [P, C.POINTER(KvConfig)]),
     "shk_cuda_kv_destroy": (None, [P]),
     "shk_cuda_kv_append": (I, [P, U32, U32, P, P, P]),
@@ -323,6 +325,19 @@ class DeviceModel:
 
     def set_tp_rows(self, o_lo: int, o_hi: int, v_lo: int, v_hi: int):
         _call("shk_cuda_model_set_tp_rows", self.h, o_lo, o_hi, v_lo, v_hi)
+
+    def tp_p2p_export(self) -> bytes:
+        """IPC handle of this rank's exchange buffer (peer-memory all-reduce)."""
+        buf = C.create_string_buffer(64)
+        n = check("shk_cuda_model_tp_p2p_export", lib().shk_cuda_model_tp_p2p_export(self.h, buf, 64))
+        return buf.raw[:n]
+
+    def tp_p2p_import(self, handles: list, o_ranges: list):
+        """handles: every rank's export in rank order; o_ranges: every rank's
+        (o_lo, o_hi)."""
+        hb = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        rg = (C.c_uint32 * (2 * len(o_ranges)))(*[v for r in o_ranges for v in r])
+        _call("shk_cuda_model_tp_p2p_import", self.h, hb, rg)
 
     def forward_layer(self, lv: LayerDesc, layer, pos, hidden_dev, stream=None):
         _call("shk_cuda_forward_layer", self.h, C.byref(lv), layer, pos, hidden_dev, stream)

@@ -102,9 +102,13 @@ def upload(model: Model, device: str | torch.device = "cuda:0", ctx: sc.Context 
 class GpuDecoder:
     """A DeviceModel + KV cache for a synthetic model, ready for token steps."""
 
-    def __init__(self, ctx: sc.Context, model: Model, max_seq: int, device="cuda:0", tp_rows=None):
+    def __init__(self, ctx: sc.Context, model: Model, max_seq: int, device="cuda:0", tp_rows=None,
+                 p2p_exchange=None, o_ranges=None):
         """tp_rows: (o_lo, o_hi, v_lo, v_hi) of a tensor-parallel rank whose
-        context has joined its group (the model is that rank's shard)."""
+        context has joined its group (the model is that rank's shard).
+        p2p_exchange: for the all-reduce over peer memory, a function taking
+        this rank's handle and returning every rank's in rank order (an
+        all-gather); o_ranges: every rank's (o_lo, o_hi)."""
         s = model.shape
         out_rows = tp_rows[3] - tp_rows[2] if tp_rows is not None else None
         self.up = upload(model, device, ctx=ctx, out_rows=out_rows)
@@ -112,6 +116,8 @@ class GpuDecoder:
         self.m = sc.DeviceModel(ctx, self.kv, self.up.desc)
         if tp_rows is not None:
             self.m.set_tp_rows(*tp_rows)
+        if p2p_exchange is not None:
+            self.m.tp_p2p_import(p2p_exchange(self.m.tp_p2p_export()), o_ranges)
         for i, lv in enumerate(self.up.layers):
             self.m.set_layer(i, lv)
 

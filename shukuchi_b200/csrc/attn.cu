@@ -107,21 +107,23 @@ __global__ void kv_read_blocks_kernel(KvLayout kv, uint32_t layer, uint32_t star
 
 constexpr int ATTC_WARPS = 8;
 
-// One cluster per KV head (see attn_cluster in attn_dev.cuh).
-template <int HD, int G>
+// One cluster per KV head (see attn_cluster in attn_dev.cuh).  LONG: the
+// variant with the long-context loop (more registers), launched only for
+// caches that can hold long contexts.
+template <int HD, int G, bool LONG>
 __global__ void __launch_bounds__(32 * ATTC_WARPS) attn_cluster_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(16) float smc[];
   pdl_trigger();
-  attn_cluster<HD, G, ATTC_WARPS>(a, smc);
+  attn_cluster<HD, G, ATTC_WARPS, LONG>(a, smc);
 }
 
 // How many clusters of 16, 8 and 4 CTAs of this kernel can be resident at
 // once (0 where the size is refused).  Queried once per instantiation.
-template <int HD, int G>
+template <int HD, int G, bool LONG>
 const int* cluster_capacity() {
   static int cap[3] = {-1, -1, -1};
   if (cap[0] >= 0) return cap;
-  auto k = attn_cluster_kernel<HD, G>;
+  auto k = attn_cluster_kernel<HD, G, LONG>;
   const size_t smem = AttnCSmem<HD, G, ATTC_WARPS>::BYTES;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const bool np = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
@@ -149,17 +151,17 @@ const int* cluster_capacity() {
 
 // The largest cluster with which all n_kv clusters (one per KV head) are
 // resident together: a second wave would double the latency.
-template <int HD, int G>
+template <int HD, int G, bool LONG>
 int cluster_ctas(uint32_t n_kv) {
-  const int* cap = cluster_capacity<HD, G>();
+  const int* cap = cluster_capacity<HD, G, LONG>();
   if (cap[0] >= (int)n_kv) return 16;
   if (cap[1] >= (int)n_kv) return 8;
   return 4;
 }
 
-template <int HD, int G>
+template <int HD, int G, bool LONG>
 cudaError_t attn_cluster_launch(const AttnArgs& a, cudaStream_t st) {
-  const int cs = cluster_ctas<HD, G>(a.kv.n_kv);
+  const int cs = cluster_ctas<HD, G, LONG>(a.kv.n_kv);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, a.kv.n_kv);
   cfg.blockDim = dim3(32 * ATTC_WARPS);
@@ -178,18 +180,25 @@ cudaError_t attn_cluster_launch(const AttnArgs& a, cudaStream_t st) {
   }
   cfg.attrs = at;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD, G>, a);
+  return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD, G, LONG>, a);
 }
 
-template <int HD>
-cudaError_t attn_cluster_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
+template <int HD, bool LONG>
+cudaError_t attn_cluster_g(const AttnArgs& a, uint32_t G, cudaStream_t st) {
   switch (G) {
-    case 1: return attn_cluster_launch<HD, 1>(a, st);
-    case 2: return attn_cluster_launch<HD, 2>(a, st);
-    case 4: return attn_cluster_launch<HD, 4>(a, st);
-    case 8: return attn_cluster_launch<HD, 8>(a, st);
+    case 1: return attn_cluster_launch<HD, 1, LONG>(a, st);
+    case 2: return attn_cluster_launch<HD, 2, LONG>(a, st);
+    case 4: return attn_cluster_launch<HD, 4, LONG>(a, st);
+    case 8: return attn_cluster_launch<HD, 8, LONG>(a, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// The long-context variant whenever the cache can hold enough positions for
+// a split of ATT_LONG_MIN positions per CTA (clusters have at least 4 CTAs).
+template <int HD>
+cudaError_t attn_cluster_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
+  return a.kv.max_seq >= 4 * ATT_LONG_MIN ? attn_cluster_g<HD, true>(a, G, st) : attn_cluster_g<HD, false>(a, G, st);
 }
 
 template <int HD>

@@ -92,7 +92,7 @@ def test_append_bit_exact(oracle, ctx, KV, hd):
 
 
 @pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64)])
-@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049])
+@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049, 9001, 20000])  # >= 8192: long-context loop
 @pytest.mark.parametrize("new_row", ["fused", "pre_appended"])
 def test_attend(oracle, ctx, H, KV, hd, seq, new_row):
     rng = np.random.default_rng(H * 131 + seq)

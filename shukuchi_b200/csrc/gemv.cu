@@ -233,8 +233,15 @@ int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const flo
     g.rg = (uint8_t)rg;
     g.rl = (uint8_t)rl;
     // rows of more than 32 blocks: one warp per slice of at most 32 blocks
-    const uint32_t ks = rg == 1 ? std::min<uint32_t>(GEMV_KS_MAX, (nb + SHK_KS_BLOCKS - 1) / SHK_KS_BLOCKS) : 1;
+    uint32_t ks = 1, lg_ks = 0;
+    if (rg == 1)
+      while (ks < (uint32_t)GEMV_KS_MAX && ks * SHK_KS_BLOCKS < nb) {
+        ks *= 2;
+        ++lg_ks;
+      }
     g.ks = (uint8_t)ks;
+    g.lg_ks = (uint8_t)lg_ks;
+    g.sw = (uint16_t)((nb + ks - 1) / ks);
     g.unit_cost = rg * rl * g.row_stride * mats_per_row;
     uint32_t cu = std::max<uint32_t>(1, target / g.unit_cost);
     if (ks > 1) cu = std::min<uint32_t>(cu, GEMV_KS_ROWT);

@@ -35,7 +35,9 @@ struct GemvSeg {
   uint8_t rg;           // row groups per warp task (lanes split across groups)
   uint8_t rl;           // rows per lane (each loaded x value feeds rl rows)
   uint8_t dual;         // 1 for gate/up pairs
-  uint8_t ks;           // K slices per row task (long rows: one warp per slice)
+  uint8_t ks;           // K slices per row task (long rows: one warp per slice), a power of two
+  uint8_t lg_ks;        // log2(ks)
+  uint16_t sw;          // blocks per K slice: ceil(nb / ks)
 };
 
 // Tensor-parallel exchange over NVLink peer memory (one-shot all-reduce fused

@@ -46,6 +46,9 @@
 #ifndef SHK_Q6_ISU
 #define SHK_Q6_ISU 1
 #endif
+#ifndef SHK_Q6_NU
+#define SHK_Q6_NU 1
+#endif
 #define SHK_PRAGMA(x) _Pragma(#x)
 #define SHK_UNROLL(n) SHK_PRAGMA(unroll n)
 
@@ -188,7 +191,7 @@ __device__ __forceinline__ void q6k_block(const uint8_t* __restrict__ r0, const 
   int T[NR][3];
 #pragma unroll
   for (int r = 0; r < NR; ++r) T[r][0] = T[r][1] = T[r][2] = 0;
-#pragma unroll 1
+SHK_UNROLL(SHK_Q6_NU)
   for (int n = 0; n < 2; ++n) {
     uint2 SC[NR];
 #pragma unroll
@@ -334,8 +337,7 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
   const int spr = 32 >> lg_rg;
   const int grp = lane >> (5 - lg_rg);
   const int s = lane & (spr - 1);
-  const uint32_t sw = (g.nb + g.ks - 1) / g.ks;  // blocks per slice
-  const uint32_t blo = sl * sw, bhi = min(g.nb, blo + sw);
+  const uint32_t blo = sl * g.sw, bhi = min(g.nb, blo + g.sw);
   float o0 = 0.f, o1 = 0.f;
   if (grp * rl < rows_valid) {
     const uint8_t* r0 = rows + (size_t)(grp * rl) * g.row_stride;
@@ -459,6 +461,11 @@ struct RingPos {
 #ifndef GEMV_PRE_STAGES
 #define GEMV_PRE_STAGES 3
 #endif
+// Where the consumers release the rest of the ring fill: 0 once their x loads
+// have landed, 1 after the RMSNorm reduction, 2 after the limb conversion.
+#ifndef GEMV_XREADY_AT
+#define GEMV_XREADY_AT 1
+#endif
 // Producer (one lane): streams this CTA's chunks of plan `a` (cost range
 // [lo, hi)) into the ring.  If xready is given, only GEMV_PRE_STAGES chunks
 // are issued before the consumers signal that their loads of x have landed:
@@ -536,7 +543,8 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // holds elements 8l..8l+7 of a block (limb vectors 2l, 2l+1), so a block's
 // maximum is a warp reduction.  Raw x is first copied (cp.async, all copies in
 // flight at once) into the very slots the lane later overwrites with limbs;
-// xready (nullable) is arrived on by each warp once its copies have landed.
+// xready (nullable) is arrived on by each warp at the point GEMV_XREADY_AT
+// names.
 // Rolled loops: this runs once per launch, compact code matters more.
 // Ends with a consumer-only barrier.
 // Step 1 of the prologue: start the copies of raw x into this lane's slots.
@@ -662,6 +670,7 @@ __device__ __forceinline__ void gemv_norm_prefetch(const GemvArgs& a, int warp, 
 #pragma unroll
   for (int u = 0; u < GEMV_PU; ++u) {
     const uint32_t kb = warp + u * GEMV_WARPS;
+    np.w[u][0] = np.w[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);  // slots past the row: unused
     if (kb < NB) {
       const float4* wn = reinterpret_cast<const float4*>(a.norm_w + 256 * (size_t)kb + 8 * lane);
       np.w[u][0] = __ldg(wn);
@@ -686,7 +695,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
   cp_async_wait_all();
   __syncwarp();
   GEMV_STAMP(1);
-  if (xready && lane == 0) mbar_arrive(xready);
+  if (GEMV_XREADY_AT == 0 && xready && lane == 0) mbar_arrive(xready);
 
   const float* nw = a.norm_w;
   float inv_rms = 1.0f;
@@ -710,9 +719,13 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
     inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
   }
   GEMV_STAMP(2);
+  if (GEMV_XREADY_AT == 1 && xready && lane == 0) mbar_arrive(xready);
   // Conversion, PU blocks per iteration: independent dependency chains in
   // flight (a single block's chain -- reductions, shuffles, packing -- is long).
   constexpr int PU = GEMV_PU;
+  // every block's norm weights are already in registers when one iteration
+  // covers the row (K <= 256 * PU * GEMV_WARPS): no global load at all then
+  const bool np_all = np && NB <= (uint32_t)(PU * GEMV_WARPS);
 #pragma unroll 1
   for (uint32_t kb0 = warp; kb0 < NB; kb0 += PU * GEMV_WARPS) {
     float v[PU][8];
@@ -724,11 +737,27 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
       const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
       v[u][0] = t0.x; v[u][1] = t0.y; v[u][2] = t0.z; v[u][3] = t0.w;
       v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
-      if (nw) {
-        const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)kc + 8 * lane);
-        const bool pre = np && kb0 == (uint32_t)warp && kb < NB;
-        const float4 w0 = pre ? np->w[u][0] : __ldg(wn), w1 = pre ? np->w[u][1] : __ldg(wn + 1);
-        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    }
+    if (nw) {
+      float4 w0[PU], w1[PU];
+      if (np_all) {
+#pragma unroll
+        for (int u = 0; u < PU; ++u) {
+          w0[u] = np->w[u][0];
+          w1[u] = np->w[u][1];
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < PU; ++u) {
+          const uint32_t kb = kb0 + u * GEMV_WARPS;
+          const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)(kb < NB ? kb : kb0) + 8 * lane);
+          w0[u] = __ldg(wn);
+          w1[u] = __ldg(wn + 1);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PU; ++u) {
+        const float w[8] = {w0[u].x, w0[u].y, w0[u].z, w0[u].w, w1[u].x, w1[u].y, w1[u].z, w1[u].w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
       }
@@ -798,6 +827,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
     }
   }
   GEMV_STAMP(3);
+  if (GEMV_XREADY_AT == 2 && xready && lane == 0) mbar_arrive(xready);
   named_sync(1, CT);
 }
 
@@ -828,7 +858,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const Ring& R, R
         const uint32_t dual_off = nrows * g.row_stride;
         uint32_t mine = 0;
         for (; t < ntasks; t += GEMV_WARPS, ++mine) {
-          const uint32_t rt = ks > 1 ? t / ks : t, sl = ks > 1 ? t % ks : 0;
+          const uint32_t rt = t >> g.lg_ks, sl = t & (ks - 1);
           const int rv = (int)min(ur, nrows - (rt << lg_ur));
           const uint8_t* rows = buf + (size_t)(rt << lg_ur) * g.row_stride;
           const uint32_t ki = p.st * GEMV_KS_ROWT + (rt < GEMV_KS_ROWT ? rt : 0);

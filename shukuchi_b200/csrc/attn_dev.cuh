@@ -336,8 +336,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
 // One thread-block cluster per KV head; CTA rank r of the cluster is split r of
 // the positions [0, pos].  Splits merge through distributed shared memory:
 // each CTA stores its (max, sum, output) into its slot in the leader CTA's
-// shared memory and arrives on the leader's mbarrier, so no partials go
-// through global memory and only the leader waits.  The new token's K/V row
+// shared memory with st.async, whose bytes complete on the leader's mbarrier
+// (no fence, no arrive), so no partials go through global memory and only the
+// leader waits.  The new token's K/V row
 // (position pos) is quantised in registers and used directly -- the same
 // bytes the append stores -- so the cache loads of the older positions can be
 // issued before the previous kernel's outputs (q, new K/V) are waited for.
@@ -362,21 +363,20 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
 constexpr int ATT_CLUSTER_MAX = 16;  // largest cluster the launcher picks
 
 // Cluster-scope helpers for the split merge: peers store their partial result
-// into the leader CTA's shared memory and arrive on the leader's mbarrier.
+// into the leader CTA's shared memory with transaction-counted async stores.
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
-  asm volatile(
-      "fence.acq_rel.cluster;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
-      : "memory");
+// Asynchronous store into a peer CTA's shared memory whose completion counts
+// 4 bytes on that CTA's mbarrier (no fence, no arrive: the receiver's barrier
+// expects the bytes).
+__device__ __forceinline__ void dsmem_st_async(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr),
+               "r"(__float_as_uint(v)), "r"(bar)
+               : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -553,7 +553,7 @@ struct AttnCSmem {  // offsets in floats
 // output) per query head and stores it into its slot in the leader CTA's
 // shared memory; the leader (rank 0) waits for its peers on an mbarrier
 // (bounded), merges the slots in rank order and writes the output.  Peers
-// leave as soon as they have arrived.
+// leave as soon as their async stores are issued.
 template <int HD, int G, int NW, bool LONG>
 __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   using Tile = AttnTile<HD>;
@@ -576,7 +576,7 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + SM::BAR);
   if (CS > 1) {
     if (leader && tid == 0) {
-      mbar_init(bar, CS - 1);
+      mbar_init(bar, 1);  // the leader's own arrive; the peers' bytes are transactions
       fence_mbar_init();
     }
     cluster_arrive();  // paired with cluster_wait before the first remote store
@@ -588,6 +588,8 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   const uint32_t active = (seq + per - 1) / per;
   const uint32_t p0 = rank * per, p1 = min(seq, p0 + per);
   const bool mine = rank < active;
+  if (CS > 1 && leader && tid == 0)  // every active peer sends one slot
+    mbar_arrive_expect_tx(bar, (active - 1) * (uint32_t)SM::SLOT * 4u);
   const bool own_new = a.k_new != nullptr && mine && pos >= p0 && pos < p1;
 
   float (*qs)[LPP][SM::QROW] = reinterpret_cast<float (*)[LPP][SM::QROW]>(sm + SM::Q);
@@ -766,6 +768,7 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   if (CS > 1) cluster_wait();  // the leader runs (its barrier is initialised)
   float* slot = sm + SM::SLOTS + rank * SM::SLOT;
   const uint32_t slot_r = dsmem_addr(slot, 0);  // the same offset in the leader
+  const uint32_t bar_r = dsmem_addr(bar, 0);
   if (mine) {
     for (int i = tid; i < G * HD; i += NT) {
       const int g = i / HD, d = i % HD;
@@ -779,18 +782,23 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
         L = fmaf(f, wl[w][g], L);
         O = fmaf(f, wacc[w][g][d], O);
       }
-      dsmem_st(slot_r + 4u * (uint32_t)(2 * G + i), O);
-      if (d == 0) {
-        dsmem_st(slot_r + 4u * (uint32_t)g, M);
-        dsmem_st(slot_r + 4u * (uint32_t)(G + g), L);
+      if (leader) {
+        slot[2 * G + i] = O;
+        if (d == 0) {
+          slot[g] = M;
+          slot[G + g] = L;
+        }
+      } else {
+        dsmem_st_async(slot_r + 4u * (uint32_t)(2 * G + i), O, bar_r);
+        if (d == 0) {
+          dsmem_st_async(slot_r + 4u * (uint32_t)g, M, bar_r);
+          dsmem_st_async(slot_r + 4u * (uint32_t)(G + g), L, bar_r);
+        }
       }
     }
   }
-  att_sync(NT);  // this CTA's stores precede thread 0's release below
-  if (!leader) {
-    if (tid == 0) mbar_arrive_remote(dsmem_addr(bar, 0));
-    return;
-  }
+  if (!leader) return;  // the async stores complete on the leader's barrier
+  att_sync(NT);         // the leader's own slot
   // ---- leader: merge the splits in rank order ----
   if (CS > 1 && !wait_peers(bar)) {
     if (tid == 0) set_error(a.err, DERR_TIMEOUT_GRID);

@@ -543,6 +543,8 @@ struct AttnCSmem {  // offsets in floats
   static constexpr int SLOT = 2 * G + G * HD;  // one CTA's partial: m[G], l[G], o[G][HD]
   static constexpr int PB = WACC + NW * G * HD;   // long contexts: per-warp p[G][32]
   static constexpr int SLOTS = PB + NW * G * 32;  // leader: one slot per cluster rank
+  static_assert(NW * 32 >= ATT_CLUSTER_MAX + 1 && NW * 32 >= NW + 2,
+                "merge weights fit in the long loop's scratch");
   static constexpr int BAR = (SLOTS + ATT_CLUSTER_MAX * SLOT + 1) & ~1;  // leader's mbarrier
   static constexpr int FLOATS = BAR + 2;
   static constexpr size_t BYTES = (size_t)FLOATS * 4;
@@ -769,19 +771,32 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   float* slot = sm + SM::SLOTS + rank * SM::SLOT;
   const uint32_t slot_r = dsmem_addr(slot, 0);  // the same offset in the leader
   const uint32_t bar_r = dsmem_addr(bar, 0);
+  // The warps' weights exp(m_w - M) per query head, once (G threads, into
+  // the long loop's scratch), then each output is a short FMA chain.
+  float* wf = sm + SM::PB;  // [NW][G] weights, then [G] M, then [G] L
+  if (mine && tid < G) {
+    const int g = tid;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
+      wf[w * G + g] = f;
+      L = fmaf(f, wl[w][g], L);
+    }
+    wf[NW * G + g] = M;
+    wf[NW * G + G + g] = L;
+  }
+  att_sync(NT);
   if (mine) {
     for (int i = tid; i < G * HD; i += NT) {
       const int g = i / HD, d = i % HD;
-      float M = -INFINITY;
+      const float M = wf[NW * G + g], L = wf[NW * G + G + g];
+      float O = 0.f;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
-      float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
-        L = fmaf(f, wl[w][g], L);
-        O = fmaf(f, wacc[w][g][d], O);
-      }
+      for (int w = 0; w < NW; ++w) O = fmaf(wf[w * G + g], wacc[w][g][d], O);
       if (leader) {
         slot[2 * G + i] = O;
         if (d == 0) {
@@ -800,24 +815,54 @@ __device__ __forceinline__ void attn_cluster(const AttnArgs& a, float* sm) {
   if (!leader) return;  // the async stores complete on the leader's barrier
   att_sync(NT);         // the leader's own slot
   // ---- leader: merge the splits in rank order ----
-  if (CS > 1 && !wait_peers(bar)) {
-    if (tid == 0) set_error(a.err, DERR_TIMEOUT_GRID);
-    return;
+  if (CS > 1) {  // one waiter; the others sleep in the CTA barrier
+    int* flag = reinterpret_cast<int*>(sm + SM::WM);  // the warp maxima are merged already
+    if (tid == 0) *flag = wait_peers(bar) ? 1 : 0;
+    att_sync(NT);
+    if (*flag == 0) {
+      if (tid == 0) set_error(a.err, DERR_TIMEOUT_GRID);
+      return;
+    }
   }
+  // The slot weights exp(m_r - M) and 1/L of each query head, once (G
+  // threads), into the long loop's scratch (free by now); then every output
+  // is a short fixed-order FMA chain over the slots.
   const float* sl0 = sm + SM::SLOTS;
+  float* wsc = sm + SM::PB;  // [ATT_CLUSTER_MAX][G] weights, then [G] 1/L
+  // Branch-free over ATT_CLUSTER_MAX slots (loads clamped to the last active
+  // slot, inactive slots weighted 0) so the loads and exponentials overlap.
+  if (tid < G) {
+    const int g = tid;
+    float mr[ATT_CLUSTER_MAX], lr[ATT_CLUSTER_MAX];
+#pragma unroll
+    for (int r = 0; r < ATT_CLUSTER_MAX; ++r) {
+      const int rr = r < (int)active ? r : (int)active - 1;
+      mr[r] = sl0[rr * SM::SLOT + g];
+      lr[r] = sl0[rr * SM::SLOT + G + g];
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < ATT_CLUSTER_MAX; ++r) M = fmaxf(M, mr[r]);
+    float L = 0.f;
+#pragma unroll
+    for (int r = 0; r < ATT_CLUSTER_MAX; ++r) {
+      const float e = expf(mr[r] - M);
+      const float w = (r < (int)active && mr[r] != -INFINITY) ? e : 0.f;
+      wsc[r * G + g] = w;
+      L = fmaf(w, lr[r], L);
+    }
+    wsc[ATT_CLUSTER_MAX * G + g] = (L == 0.f) ? 0.f : 1.0f / L;
+  }
+  att_sync(NT);
   for (int i = tid; i < G * HD; i += NT) {
     const int g = i / HD;
-    float M = -INFINITY;
-    for (uint32_t r = 0; r < active; ++r) M = fmaxf(M, sl0[r * SM::SLOT + g]);
-    float L = 0.f, O = 0.f;
-    for (uint32_t r = 0; r < active; ++r) {
-      const float* sr = sl0 + r * SM::SLOT;
-      const float mr = sr[g];
-      const float w = (mr == -INFINITY) ? 0.f : expf(mr - M);
-      L = fmaf(w, sr[G + g], L);
-      O = fmaf(w, sr[2 * G + i], O);
+    float O = 0.f;
+#pragma unroll
+    for (int r = 0; r < ATT_CLUSTER_MAX; ++r) {
+      const int rr = r < (int)active ? r : (int)active - 1;
+      O = fmaf(wsc[r * G + g], sl0[rr * SM::SLOT + 2 * G + i], O);
     }
-    a.out[(kvh + KV * g) * HD + i % HD] = (L == 0.f) ? 0.f : O * (1.0f / L);
+    a.out[(kvh + KV * g) * HD + i % HD] = O * wsc[ATT_CLUSTER_MAX * G + g];
   }
 }
 

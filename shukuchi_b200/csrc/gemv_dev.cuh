@@ -728,36 +728,32 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
   const bool np_all = np && NB <= (uint32_t)(PU * GEMV_WARPS);
 #pragma unroll 1
   for (uint32_t kb0 = warp; kb0 < NB; kb0 += PU * GEMV_WARPS) {
+    // slots of this iteration that hold a block (warp-uniform): short rows
+    // (K = 4096: one block per warp) skip the work of the empty slots
+    const uint32_t nu = min((uint32_t)PU, (NB - kb0 + GEMV_WARPS - 1) / GEMV_WARPS);
     float v[PU][8];
 #pragma unroll
     for (int u = 0; u < PU; ++u) {
-      const uint32_t kb = kb0 + u * GEMV_WARPS;
-      const uint32_t kc = kb < NB ? kb : kb0;
-      const uint32_t v0 = 64 * kc + 2 * lane;
+      if ((uint32_t)u >= nu) break;
+      const uint32_t v0 = 64 * (kb0 + u * GEMV_WARPS) + 2 * lane;
       const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
       v[u][0] = t0.x; v[u][1] = t0.y; v[u][2] = t0.z; v[u][3] = t0.w;
       v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
     }
     if (nw) {
-      float4 w0[PU], w1[PU];
-      if (np_all) {
-#pragma unroll
-        for (int u = 0; u < PU; ++u) {
-          w0[u] = np->w[u][0];
-          w1[u] = np->w[u][1];
-        }
-      } else {
-#pragma unroll
-        for (int u = 0; u < PU; ++u) {
-          const uint32_t kb = kb0 + u * GEMV_WARPS;
-          const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)(kb < NB ? kb : kb0) + 8 * lane);
-          w0[u] = __ldg(wn);
-          w1[u] = __ldg(wn + 1);
-        }
-      }
 #pragma unroll
       for (int u = 0; u < PU; ++u) {
-        const float w[8] = {w0[u].x, w0[u].y, w0[u].z, w0[u].w, w1[u].x, w1[u].y, w1[u].z, w1[u].w};
+        if ((uint32_t)u >= nu) break;
+        float4 w0, w1;
+        if (np_all) {
+          w0 = np->w[u][0];
+          w1 = np->w[u][1];
+        } else {
+          const float4* wn = reinterpret_cast<const float4*>(nw + 256 * (size_t)(kb0 + u * GEMV_WARPS) + 8 * lane);
+          w0 = __ldg(wn);
+          w1 = __ldg(wn + 1);
+        }
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
       }
@@ -766,6 +762,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
     bool finite[PU];
 #pragma unroll
     for (int u = 0; u < PU; ++u) {
+      if ((uint32_t)u >= nu) break;
       amax[u] = 0.f;
       finite[u] = true;
 #pragma unroll
@@ -773,16 +770,14 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
         amax[u] = fmaxf(amax[u], fabsf(v[u][e]));
         finite[u] = finite[u] && isfinite(v[u][e]);
       }
-    }
-    // warp maximum in one step: |x| >= 0, whose bit patterns order as unsigned
-    // integers (non-finite blocks are caught by `finite` below)
-#pragma unroll
-    for (int u = 0; u < PU; ++u)
+      // warp maximum in one step: |x| >= 0, whose bit patterns order as
+      // unsigned integers (non-finite blocks are caught by `finite` below)
       amax[u] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax[u])));
+    }
 #pragma unroll
     for (int u = 0; u < PU; ++u) {
       const uint32_t kb = kb0 + u * GEMV_WARPS;
-      if (kb >= NB) break;  // uniform across the warp
+      if ((uint32_t)u >= nu) break;  // uniform across the warp
       const bool fin = __all_sync(0xffffffffu, finite[u]);
       // X_b = 2^(f-21) with amax in [2^f, 2^(f+1)): |x / X_b| < 2^22.  Blocks
       // whose maximum is below 2^-104 (subnormal maxima included) are scaled as

@@ -164,14 +164,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) decode_kernel(const __grid_co
         const uint64_t lo = a.total_cost * blockIdx.x / gridDim.x;
         const uint64_t hi = a.total_cost * (blockIdx.x + 1) / gridDim.x;
         if (h4 && h6) {
-          gemv_prologue<true, true>(a, xb, red, warp, lane);
-          ok = gemv_consume<true, true>(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+          const float osc = gemv_prologue<true, true>(a, xb, red, warp, lane);
+          ok = gemv_consume<true, true>(a, R, p, gtask, lo, hi, xb.view(osc), warp, lane);
         } else if (h4) {
-          gemv_prologue<true, false>(a, xb, red, warp, lane);
-          ok = gemv_consume<true, false>(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+          const float osc = gemv_prologue<true, false>(a, xb, red, warp, lane);
+          ok = gemv_consume<true, false>(a, R, p, gtask, lo, hi, xb.view(osc), warp, lane);
         } else {
-          gemv_prologue<false, true>(a, xb, red, warp, lane);
-          ok = gemv_consume<false, true>(a, R, p, gtask, lo, hi, xb.view(), warp, lane);
+          const float osc = gemv_prologue<false, true>(a, xb, red, warp, lane);
+          ok = gemv_consume<false, true>(a, R, p, gtask, lo, hi, xb.view(osc), warp, lane);
         }
       } else if (d.kind == PH_ATTN) {
         const AttnArgs& aa = P.attn[d.idx];

@@ -84,9 +84,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   gemv_norm_prefetch(a, warp, lane, np);
   pdl_wait();  // x and the residual come from the previous kernel
   gemv_x_issue(a, xb, warp, lane);
-  gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true, &np);
+  const float osc = gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true, &np);
   uint32_t gtask = 0;
-  gemv_consume<HAS4, HAS6>(a, R, pos, gtask, lo, hi, xb.view(), warp, lane);
+  gemv_consume<HAS4, HAS6>(a, R, pos, gtask, lo, hi, xb.view(osc), warp, lane);
   if (a.tp.out) gemv_tp_signal(a, reinterpret_cast<int*>(red + 31), lane);
 }
 

@@ -315,6 +315,7 @@ struct XView {
   const float* xbs;   // per-256-block scale X_b, K/256
   const float* xs32;  // Q4_K: fp32 sums of x per 32-element sub-block, K/32
   const int4* xi16;   // Q6_K: -32 * limb sums per 16-element group, 16 per block + 1 pad
+  float oscale;       // output scale: the RMSNorm factor inv_rms, or 1
 };
 
 // One task of a chunk: rg lane groups, each owning rl output rows (two row
@@ -375,13 +376,13 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
           s1 += vp[2 * k + 1];
         }
         *kc = 0;
-        if (rows_valid > 0) store2(a, g, row0, rows_valid, s0, s1);
+        if (rows_valid > 0) store2(a, g, row0, rows_valid, s0 * x.oscale, s1 * x.oscale);
       }
     }
     return;
   }
   if ((lane & (lpg - 1)) == 0 && grp * rl < rows_valid)
-    store2(a, g, row0 + grp * rl, rows_valid - grp * rl, o0, o1);
+    store2(a, g, row0 + grp * rl, rows_valid - grp * rl, o0 * x.oscale, o1 * x.oscale);
 }
 
 // Shared-memory map: [full | empty | xbar barriers][done][gen][red]
@@ -462,7 +463,7 @@ struct RingPos {
 #define GEMV_PRE_STAGES 3
 #endif
 // Where the consumers release the rest of the ring fill: 0 once their x loads
-// have landed, 1 after the RMSNorm reduction, 2 after the limb conversion.
+// have landed, 1 after the limb conversion.
 #ifndef GEMV_XREADY_AT
 #define GEMV_XREADY_AT 1
 #endif
@@ -519,7 +520,7 @@ struct XBuf {
   float* xbs;
   float* xs32;
   int4* xi16;
-  __device__ __forceinline__ XView view() const { return XView{xq, xbs, xs32, xi16}; }
+  __device__ __forceinline__ XView view(float oscale = 1.0f) const { return XView{xq, xbs, xs32, xi16, oscale}; }
 };
 
 // Consumers (warps 0..GEMV_WARPS-1): x (optionally RMSNorm'ed) -> fixed-point
@@ -680,7 +681,7 @@ __device__ __forceinline__ void gemv_norm_prefetch(const GemvArgs& a, int warp, 
 }
 
 template <bool HAS4, bool HAS6>
-__device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
+__device__ __forceinline__ float gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
                                               int warp, int lane, uint64_t* xready = nullptr,
                                               bool x_issued = false, const NormPre* np = nullptr) {
   constexpr int CT = 32 * GEMV_WARPS;
@@ -697,29 +698,14 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
   GEMV_STAMP(1);
   if (GEMV_XREADY_AT == 0 && xready && lane == 0) mbar_arrive(xready);
 
+  // RMSNorm (engine/src/ops.c:195-214) is applied as a scale on the outputs:
+  // W (x * inv_rms * w) = inv_rms * W (x * w), so the limbs are made from
+  // x * w right away and the sum of squares is reduced alongside (same
+  // per-lane order and fixed warp order as a separate pass: every CTA gets
+  // the same scale), without a barrier between the two.
   const float* nw = a.norm_w;
-  float inv_rms = 1.0f;
-  if (nw) {
-    // RMSNorm prologue (engine/src/ops.c:195-214); the fixed-order reduction
-    // gives every CTA the same scale.
-    float ss = 0.f;
-#pragma unroll 1
-    for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
-      const uint32_t v0 = 64 * kb + 2 * lane;
-      const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
-      ss = fmaf(t0.x, t0.x, ss); ss = fmaf(t0.y, t0.y, ss); ss = fmaf(t0.z, t0.z, ss); ss = fmaf(t0.w, t0.w, ss);
-      ss = fmaf(t1.x, t1.x, ss); ss = fmaf(t1.y, t1.y, ss); ss = fmaf(t1.z, t1.z, ss); ss = fmaf(t1.w, t1.w, ss);
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    named_sync(1, CT);
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
-    inv_rms = 1.0f / sqrtf(tot / (float)K + 1e-5f);
-  }
+  float ss = 0.f;
   GEMV_STAMP(2);
-  if (GEMV_XREADY_AT == 1 && xready && lane == 0) mbar_arrive(xready);
   // Conversion, PU blocks per iteration: independent dependency chains in
   // flight (a single block's chain -- reductions, shuffles, packing -- is long).
   constexpr int PU = GEMV_PU;
@@ -739,6 +725,10 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
       const float4 t0 = xr[xpad(v0)], t1 = xr[xpad(v0 + 1)];
       v[u][0] = t0.x; v[u][1] = t0.y; v[u][2] = t0.z; v[u][3] = t0.w;
       v[u][4] = t1.x; v[u][5] = t1.y; v[u][6] = t1.z; v[u][7] = t1.w;
+      if (nw) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(v[u][e], v[u][e], ss);
+      }
     }
     if (nw) {
 #pragma unroll
@@ -755,7 +745,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
         }
         const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[u][e] = (v[u][e] * inv_rms) * w[e];
+        for (int e = 0; e < 8; ++e) v[u][e] *= w[e];
       }
     }
     float amax[PU];
@@ -821,9 +811,18 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const XBuf& xb_
       }
     }
   }
+  if (nw) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+  }
   GEMV_STAMP(3);
-  if (GEMV_XREADY_AT == 2 && xready && lane == 0) mbar_arrive(xready);
+  if (GEMV_XREADY_AT == 1 && xready && lane == 0) mbar_arrive(xready);
   named_sync(1, CT);
+  if (!nw) return 1.0f;
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < GEMV_WARPS; ++w) tot += red[w];
+  return 1.0f / sqrtf(tot / (float)K + 1e-5f);
 }
 
 // Consumers: walk this CTA's chunks of plan `a` in the producer's order; a

@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + GEMV_MAX_STAGES;
   uint64_t* xbar = empty + GEMV_MAX_STAGES;
+  uint64_t* xbars = reinterpret_cast<uint64_t*>(smem + SMEM_XBARS);
   int* done = reinterpret_cast<int*>(xbar + 1);
   volatile uint32_t* gen = reinterpret_cast<volatile uint32_t*>(done + GEMV_MAX_STAGES);
   float* red = reinterpret_cast<float*>(smem + 8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES);
@@ -64,6 +65,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
       reinterpret_cast<int*>(red)[31] = 0;  // tensor-parallel producer: finished warps
     }
     fence_mbar_init();
+  } else if (tid >= 32 * (GEMV_WARPS - 1) && tid < 32 * (GEMV_WARPS - 1) + GEMV_WARPS) {
+    mbar_init(&xbars[tid - 32 * (GEMV_WARPS - 1)], 1);  // x copies of consumer warp tid - 448
+    fence_mbar_init();
   }
   __syncthreads();  // barriers initialised
   pdl_trigger();    // the next kernel may be scheduled; it waits for this one before its reads
@@ -83,8 +87,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   NormPre np;
   gemv_norm_prefetch(a, warp, lane, np);
   pdl_wait();  // x and the residual come from the previous kernel
-  gemv_x_issue(a, xb, warp, lane);
-  const float osc = gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true, &np);
+  gemv_x_issue(a, xb, warp, lane, xbars);
+  const float osc = gemv_prologue<HAS4, HAS6>(a, xb, red, warp, lane, xbar, true, &np, xbars);
   uint32_t gtask = 0;
   gemv_consume<HAS4, HAS6>(a, R, pos, gtask, lo, hi, xb.view(osc), warp, lane);
   if (a.tp.out) gemv_tp_signal(a, reinterpret_cast<int*>(red + 31), lane);

@@ -9,13 +9,13 @@
 // sequential fp32 sum; results agree to fp32 rounding.
 //
 // Kernel shape (one CTA per SM, persistent over a byte-balanced row range):
-//  * warp 8 is the producer: one lane streams whole-row chunks of the weight
-//    matrix into a shared-memory ring with cp.async.bulk (TMA, 1-D, no tensor
-//    map, one destination CTA), completion tracked by mbarrier tx-counts; a per-stage
-//    generation tag orders consumers that skip ahead;
-//  * warps 0-7 are consumers: they load x (RMSNorm fused) and turn it into the
-//    fixed-point form below while the first chunks are in flight, then decode
-//    blocks from the ring.  The last warp to finish a chunk's tasks releases
+//  * warp GEMV_WARPS (15) is the producer: one lane streams whole-row chunks
+//    of the weight matrix into a shared-memory ring with cp.async.bulk (TMA,
+//    1-D, no tensor map, one destination CTA), completion tracked by mbarrier
+//    tx-counts; a per-stage generation tag orders consumers that skip ahead;
+//  * warps 0-14 are consumers: they load x (bulk copies, RMSNorm fused) and
+//    turn it into the fixed-point form below while the first chunks are in
+//    flight, then decode blocks from the ring.  The last warp to finish a chunk's tasks releases
 //    its stage.
 //
 // Arithmetic: the weights' integer quants are multiplied with integer limbs of
@@ -396,7 +396,8 @@ constexpr int GEMV_KS_MAX = 8;
 constexpr int GEMV_KS_ROWT = 4;
 constexpr int SMEM_KPART = (8 * (2 * GEMV_MAX_STAGES + 1) + 8 * GEMV_MAX_STAGES + 4 * 32 + 15) & ~15;
 constexpr int SMEM_KCNT = SMEM_KPART + GEMV_MAX_STAGES * GEMV_KS_ROWT * GEMV_KS_MAX * 2 * 4;
-constexpr int SMEM_HDR = SMEM_KCNT + GEMV_MAX_STAGES * GEMV_KS_ROWT * 4;
+constexpr int SMEM_XBARS = SMEM_KCNT + GEMV_MAX_STAGES * GEMV_KS_ROWT * 4;  // x copies: one mbarrier per warp
+constexpr int SMEM_HDR = SMEM_XBARS + 16 * 8;
 
 // Bounded spin until the producer has claimed stage `st` for chunk `it`.  A
 // consumer may run several ring cycles ahead of a stage (it skips chunks with
@@ -633,11 +634,31 @@ __device__ __forceinline__ void gemv_tp_signal(const GemvArgs& a, int* done, int
   *t.counter = 0;
 }
 
-__device__ __forceinline__ void gemv_x_issue(const GemvArgs& a, const XBuf& xb_, int warp, int lane) {
+// x by 1-D bulk copies (two 512-byte runs per 256-element block, around the
+// block's pad slot) on the warp's mbarrier, when the caller provides them,
+// x comes from an earlier launch (not the tensor-parallel exchange) and is
+// 16-byte aligned; else cp.async by every lane.
+__device__ __forceinline__ bool gemv_x_bulk(const GemvArgs& a, const uint64_t* xbars) {
+  return xbars && !a.tp.in && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+}
+__device__ __forceinline__ void gemv_x_issue(const GemvArgs& a, const XBuf& xb_, int warp, int lane,
+                                             uint64_t* xbars = nullptr) {
   const uint32_t NB = a.k / 256;
   float4* xr = reinterpret_cast<float4*>(xb_.xq);  // raw x staged in the limb slots
   if (a.tp.in) {
     gemv_x_tp(a, xb_, warp, lane);
+    return;
+  }
+  if (gemv_x_bulk(a, xbars)) {
+    if (lane == 0) {
+      const uint32_t nblk = NB > (uint32_t)warp ? (NB - (uint32_t)warp + GEMV_WARPS - 1) / GEMV_WARPS : 0u;
+      mbar_arrive_expect_tx(&xbars[warp], nblk * 1024u);
+      for (uint32_t kb = warp; kb < NB; kb += GEMV_WARPS) {
+        bulk_g2s(&xr[65 * kb], a.x + 256 * (size_t)kb, 512, &xbars[warp]);
+        bulk_g2s(&xr[65 * kb + 33], a.x + 256 * (size_t)kb + 128, 512, &xbars[warp]);
+      }
+    }
+    GEMV_STAMP(0);
     return;
   }
   const bool xal = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
@@ -683,7 +704,8 @@ __device__ __forceinline__ void gemv_norm_prefetch(const GemvArgs& a, int warp, 
 template <bool HAS4, bool HAS6>
 __device__ __forceinline__ float gemv_prologue(const GemvArgs& a, const XBuf& xb_, float* red,
                                               int warp, int lane, uint64_t* xready = nullptr,
-                                              bool x_issued = false, const NormPre* np = nullptr) {
+                                              bool x_issued = false, const NormPre* np = nullptr,
+                                              uint64_t* xbars = nullptr) {
   constexpr int CT = 32 * GEMV_WARPS;
   const uint32_t K = a.k;
   const uint32_t NB = K / 256;
@@ -692,8 +714,14 @@ __device__ __forceinline__ float gemv_prologue(const GemvArgs& a, const XBuf& xb
   float* xs32 = xb_.xs32;
   int4* xi16 = xb_.xi16;
   float4* xr = reinterpret_cast<float4*>(xq);
-  if (!x_issued) gemv_x_issue(a, xb_, warp, lane);
-  cp_async_wait_all();
+  if (!x_issued) gemv_x_issue(a, xb_, warp, lane, xbars);
+  if (gemv_x_bulk(a, xbars)) {
+    // on a time-out the error is recorded and the prologue still runs to its
+    // barrier (every consumer warp must reach it); the launch's result is void
+    mbar_wait_bounded(&xbars[warp], 0, a.err, DERR_TIMEOUT_FULL);
+  } else {
+    cp_async_wait_all();
+  }
   __syncwarp();
   GEMV_STAMP(1);
   if (GEMV_XREADY_AT == 0 && xready && lane == 0) mbar_arrive(xready);

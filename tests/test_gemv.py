@@ -38,7 +38,7 @@ def check(oracle, ctx, qt, m, k, seed, subnormal=False, xscale=1.0):
 
 @pytest.mark.parametrize("m,k", [(1, 256), (7, 512), (64, 2048), (333, 1024), (1024, 4096),
                                  (4096, 4096), (1000, 14336), (3, 8192), (4096, 14336), (14336, 4096),
-                                 (37, 28672), (5, 65536)])
+                                 (37, 28672), (5, 65536), (9475, 4096)])
 def test_q4k(oracle, ctx, m, k):
     # k > 8192 (more than 32 blocks a row): rows are split over warps in K slices
     check(oracle, ctx, 12, m, k, seed=m + k)

@@ -21,8 +21,18 @@ def assert_logits(got, ref):
         assert err <= tol, (t, err, tol)
 
 
-def test_layer_forward_matches_oracle(oracle, ctx):
-    model = synth.make_model("small", seed=3)
+# One layer of the 8B shape (4096 / 14336, 32 q / 8 KV heads) with a small
+# vocabulary: the GEMV plans of the bench's layers (dual gate/up, K-split down
+# projection, RoPE'd Q/K with 8 KV heads) against the oracle.  Position 0 only: the
+# synthetic weights drive this layer's activations into the thousands, where
+# attention over several positions (near one-hot softmax of huge scores)
+# amplifies fp32 rounding differences beyond any fixed tolerance.
+LAYER_8B = synth.ModelShape("llama-3.1-8b-layer", 1, 4096, 32, 8, 14336, 512)
+
+
+@pytest.mark.parametrize("shape,n_pos", [("small", 6), (LAYER_8B, 1)], ids=["small", "8b_layer"])
+def test_layer_forward_matches_oracle(oracle, ctx, shape, n_pos):
+    model = synth.make_model(shape, seed=3)
     s = model.shape
     up = upload(model, ctx=ctx)
     kv = sc.KvCache(ctx, s.n_layers, s.n_kv_heads, s.head_dim, 64)
@@ -30,7 +40,7 @@ def test_layer_forward_matches_oracle(oracle, ctx):
     okv = oracle.kv_create(s.n_layers, s.n_kv_heads, s.head_dim, 64)
     try:
         rng = np.random.default_rng(0)
-        for pos in range(6):
+        for pos in range(n_pos):
             hid = rng.normal(0, 1, s.n_embd).astype(np.float32)
             hd = torch.from_numpy(hid.copy()).cuda()
             ref = hid.copy()
@@ -47,7 +57,7 @@ def test_layer_forward_matches_oracle(oracle, ctx):
                 hd.copy_(torch.from_numpy(ref))  # re-sync so errors do not compound
             # KV blocks written by the fused path are bit-identical when fed the
             # same fp32 K/V: checked in test_kv; here the caches must agree closely
-        assert kv.seq_len(0) == 6
+        assert kv.seq_len(0) == n_pos
     finally:
         oracle.kv_destroy(okv)
         dm.close()

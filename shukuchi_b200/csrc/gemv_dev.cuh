@@ -461,12 +461,12 @@ struct RingPos {
 };
 
 #ifndef GEMV_PRE_STAGES
-#define GEMV_PRE_STAGES 3
+#define GEMV_PRE_STAGES 5
 #endif
 // Where the consumers release the rest of the ring fill: 0 once their x loads
 // have landed, 1 after the limb conversion.
 #ifndef GEMV_XREADY_AT
-#define GEMV_XREADY_AT 1
+#define GEMV_XREADY_AT 0
 #endif
 // Producer (one lane): streams this CTA's chunks of plan `a` (cost range
 // [lo, hi)) into the ring.  If xready is given, only GEMV_PRE_STAGES chunks

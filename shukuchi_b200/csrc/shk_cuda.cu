@@ -19,7 +19,12 @@
 #include "gemv.cuh"
 #include "glue.cuh"
 
-using namespace shk;
+using // Fewest cached positions per attention split (CTA of a KV head's cluster).
+#ifndef SHK_ATT_MIN_SPLIT
+#define SHK_ATT_MIN_SPLIT 32
+#endif
+
+namespace shk;
 
 #define CK(expr)                                              \
   do {                                                        \
@@ -595,7 +600,7 @@ int shk_cuda_kv_attend(shk_kv* kv, uint32_t layer, const float* q, const float* 
   a.part = kv->part;
   a.counters = kv->counters;
   a.max_splits = kv->max_splits;
-  a.min_per_split = 32;
+  a.min_per_split = SHK_ATT_MIN_SPLIT;
   a.err = kv->ctx->d_err;
   CK(attn_decode_launch(a, pick(kv->ctx, s)));
   if (k_new) kv->seq[layer] = std::max(kv->seq[layer], seq_len);
@@ -721,7 +726,7 @@ AttnArgs layer_attn_args(shk_model* m, uint32_t layer, const uint32_t* pos) {
   a.part = m->kv->part;
   a.counters = m->kv->counters;
   a.max_splits = m->kv->max_splits;
-  a.min_per_split = 32;
+  a.min_per_split = SHK_ATT_MIN_SPLIT;
   a.err = m->ctx->d_err;
   return a;
 }
@@ -1388,7 +1393,7 @@ int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void
     a.part = m->kv->part;
     a.counters = m->kv->counters;
     a.max_splits = m->kv->max_splits;
-    a.min_per_split = 32;
+    a.min_per_split = SHK_ATT_MIN_SPLIT;
     a.err = m->ctx->d_err;
     CK(attn_decode_launch(a, st));
   } else {

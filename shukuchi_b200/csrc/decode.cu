@@ -160,7 +160,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) decode_kernel(const __grid_co
         xb.xq = reinterpret_cast<int4*>(xreg);
         xb.xbs = reinterpret_cast<float*>(xreg + xq_bytes(K));
         xb.xs32 = xb.xbs + xbs_floats(K);
-        xb.xi16 = reinterpret_cast<int4*>(xreg + xq_bytes(K) + (size_t)xbs_floats(K) * 4 + (size_t)(K / 32) * 4);
         const uint64_t lo = a.total_cost * blockIdx.x / gridDim.x;
         const uint64_t hi = a.total_cost * (blockIdx.x + 1) / gridDim.x;
         if (h4 && h6) {

@@ -43,8 +43,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
   xb.xq = reinterpret_cast<int4*>(xreg);  // padded limb vectors, xpad(K/4) of them
   xb.xbs = reinterpret_cast<float*>(xreg + xq_bytes(K));
   xb.xs32 = xb.xbs + xbs_floats(K);
-  xb.xi16 = reinterpret_cast<int4*>(xreg + xq_bytes(K) + (size_t)xbs_floats(K) * 4 +
-                                    (HAS4 ? (size_t)(K / 32) * 4 : 0));
   size_t stage_off = (size_t)(xreg - smem) + x_region_bytes(K, HAS4, HAS6);
   stage_off = (stage_off + 127) & ~(size_t)127;
   const Ring R{full,           empty, done, gen, smem + stage_off, NS, a.stage_bytes,

@@ -27,8 +27,8 @@
 // the bytes of x_int exactly its limbs.  Per
 // sub-block the three limb sums are scaled by the 6-bit (Q4_K) or int8 (Q6_K)
 // sub-block scale with IMAD, then per block converted to float and multiplied by
-// d * X_b.  The Q4_K min term uses fp32 sums of x; the Q6_K -32 offset is folded
-// into the dp4a accumulators' initial value.  Integer packing keeps the
+// d * X_b.  The Q4_K min term uses fp32 sums of x; the Q6_K -32 offset comes
+// from -32 * limb sums carried in the unused fourth words of the x vectors.  Integer packing keeps the
 // per-weight work on the dp4a/IMAD path instead of the half-rate logic pipe.
 #pragma once
 
@@ -179,8 +179,7 @@ __device__ __forceinline__ uint32_t w4(const uint4& v, int i) {
 template <int NR>
 __device__ __forceinline__ void q6k_block(const uint8_t* __restrict__ r0, const uint8_t* __restrict__ r1,
                                           uint32_t nb, uint32_t b, const int4* __restrict__ xblk,
-                                          const int4* __restrict__ xib, float xb, float& acc0,
-                                          float& acc1) {
+                                          float xb, float& acc0, float& acc1) {
   const uint32_t MK = 0x0F0F0F0Fu;
   const uint8_t* rp[2] = {r0, r1};
   const uint32_t qlb = 128u * b, qhb = 128u * nb + 64u * b, scb = 192u * nb + 16u * b;
@@ -197,7 +196,6 @@ SHK_UNROLL(SHK_Q6_NU)
 #pragma unroll
     for (int r = 0; r < NR; ++r) SC[r] = *reinterpret_cast<const uint2*>(rp[r] + scb + 8u * n);
     const int4* xh = xblk + 33 * n;
-    const int4* xi = xib + 8 * n;
 SHK_UNROLL(SHK_Q6_ISU)
     for (int is = 0; is < 2; ++is) {
       uint4 A[NR], B[NR], H[NR];
@@ -209,15 +207,9 @@ SHK_UNROLL(SHK_Q6_ISU)
       }
       int S[NR][4][3];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int4 init = xi[2 * g + is];  // -32 * limb sums of this 16-group
+      for (int g = 0; g < 4; ++g)
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
-          S[r][g][0] = init.x;
-          S[r][g][1] = init.y;
-          S[r][g][2] = init.z;
-        }
-      }
+        for (int r = 0; r < NR; ++r) S[r][g][0] = S[r][g][1] = S[r][g][2] = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         int4 xv[4];
@@ -231,6 +223,9 @@ SHK_UNROLL(SHK_Q6_ISU)
                                  lop_sel(bq >> 4, hn >> 2, MK)};
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
+            // the -32 offset: vector i < 3 of a 16-group carries -32 * (sum of
+            // the group's limb i) in its fourth word
+            if (i < 3) S[r][g][i] += xv[g].w;
             S[r][g][0] = dp4a_u(Q[g], xv[g].x, S[r][g][0]);
             S[r][g][1] = dp4a_u(Q[g], xv[g].y, S[r][g][1]);
             S[r][g][2] = dp4a_us(Q[g], xv[g].z, S[r][g][2]);
@@ -314,7 +309,6 @@ struct XView {
   const int4* xq;     // padded limb vectors, K/4 (+ one pad vector per 256-block)
   const float* xbs;   // per-256-block scale X_b, K/256
   const float* xs32;  // Q4_K: fp32 sums of x per 32-element sub-block, K/32
-  const int4* xi16;   // Q6_K: -32 * limb sums per 16-element group, 16 per block + 1 pad
   float oscale;       // output scale: the RMSNorm factor inv_rms, or 1
 };
 
@@ -350,10 +344,10 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
     } else if (HAS6) {
       if (rl == 1 && !g.dual) {  // single row
         for (uint32_t b = blo + s; b < bhi; b += spr)
-          q6k_block<1>(r0, r1, g.nb, b, x.xq + 65 * b, x.xi16 + 17 * b, x.xbs[b], o0, o1);
+          q6k_block<1>(r0, r1, g.nb, b, x.xq + 65 * b, x.xbs[b], o0, o1);
       } else {
         for (uint32_t b = blo + s; b < bhi; b += spr)
-          q6k_block<2>(r0, r1, g.nb, b, x.xq + 65 * b, x.xi16 + 17 * b, x.xbs[b], o0, o1);
+          q6k_block<2>(r0, r1, g.nb, b, x.xq + 65 * b, x.xbs[b], o0, o1);
       }
     }
   }
@@ -386,7 +380,7 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
 }
 
 // Shared-memory map: [full | empty | xbar barriers][done][gen][red]
-// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)][xi16 (17 int4 per block, Q6_K)]
+// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)]
 // [stage ring].  The producer first bulk-copies x into the limb-vector slot;
 // consumers turn it into limbs in place.
 // K split of long rows (more than 32 blocks, e.g. the down projection): a row
@@ -417,18 +411,17 @@ __device__ __forceinline__ bool wait_gen(const volatile uint32_t* gen, uint32_t 
   return true;
 }
 
-// X_b array padded to a 16-byte multiple so xs32 (float2 loads) and xi16
-// (int4 loads) stay aligned for every K.
+// X_b array padded to a 16-byte multiple so xs32 (float2 loads) stays
+// aligned for every K.
 __host__ __device__ __forceinline__ uint32_t xbs_floats(uint32_t K) { return ((K / 256) + 3) & ~3u; }
 
 __host__ __device__ __forceinline__ size_t xq_bytes(uint32_t K) {
   return (size_t)(K / 4 + K / 256) * 16;  // one pad vector per 64
 }
 
-__host__ __device__ __forceinline__ size_t x_region_bytes(uint32_t K, bool has4, bool has6) {
+__host__ __device__ __forceinline__ size_t x_region_bytes(uint32_t K, bool has4, bool /*has6*/) {
   size_t b = xq_bytes(K) + (size_t)xbs_floats(K) * 4;
   if (has4) b += (size_t)(K / 32) * 4;
-  if (has6) b += (size_t)(K / 256) * 17 * 16;  // int4 per 16 elements + one pad per block
   return b;
 }
 
@@ -520,8 +513,7 @@ struct XBuf {
   int4* xq;
   float* xbs;
   float* xs32;
-  int4* xi16;
-  __device__ __forceinline__ XView view(float oscale = 1.0f) const { return XView{xq, xbs, xs32, xi16, oscale}; }
+  __device__ __forceinline__ XView view(float oscale = 1.0f) const { return XView{xq, xbs, xs32, oscale}; }
 };
 
 // Consumers (warps 0..GEMV_WARPS-1): x (optionally RMSNorm'ed) -> fixed-point
@@ -712,7 +704,6 @@ __device__ __forceinline__ float gemv_prologue(const GemvArgs& a, const XBuf& xb
   int4* xq = xb_.xq;
   float* xbs = xb_.xbs;
   float* xs32 = xb_.xs32;
-  int4* xi16 = xb_.xi16;
   float4* xr = reinterpret_cast<float4*>(xq);
   if (!x_issued) gemv_x_issue(a, xb_, warp, lane, xbars);
   if (gemv_x_bulk(a, xbars)) {
@@ -819,23 +810,28 @@ __device__ __forceinline__ float gemv_prologue(const GemvArgs& a, const XBuf& xb
           const uint32_t hi = __byte_perm((uint32_t)t[4 * h + 2], (uint32_t)t[4 * h + 3], sel);
           lw[h][k] = __byte_perm(lo, hi, 0x5410);
         }
-      const uint32_t v0 = 64 * kb + 2 * lane;
-      xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], 0);
-      xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], 0);
-      if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
-        float sm = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
-        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-        if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = sm;
-      }
-      if (HAS6) {  // -32 * limb sums per 16-element group (2 lanes)
+      // Q6_K: -32 * (sum of limb k over each 16-element group, lanes 2m and
+      // 2m+1) rides in the fourth word of the group's vector k (k < 3), where
+      // the dot-product loop adds it to its limb-k accumulators
+      int w3[2] = {0, 0};
+      if (HAS6) {
         int l0 = (int)__dp4a(lw[0][0], 0x01010101u, __dp4a(lw[1][0], 0x01010101u, 0u));
         int l1 = (int)__dp4a(lw[0][1], 0x01010101u, __dp4a(lw[1][1], 0x01010101u, 0u));
         int l2 = __dp4a((int)lw[0][2], 0x01010101, __dp4a((int)lw[1][2], 0x01010101, 0));
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
-        if ((lane & 1) == 0) xi16[17 * kb + (lane >> 1)] = make_int4(-32 * l0, -32 * l1, -32 * l2, 0);
+        w3[0] = (lane & 1) ? -32 * l2 : -32 * l0;
+        w3[1] = (lane & 1) ? 0 : -32 * l1;
+      }
+      const uint32_t v0 = 64 * kb + 2 * lane;
+      xq[xpad(v0)] = make_int4((int)lw[0][0], (int)lw[0][1], (int)lw[0][2], w3[0]);
+      xq[xpad(v0 + 1)] = make_int4((int)lw[1][0], (int)lw[1][1], (int)lw[1][2], w3[1]);
+      if (HAS4) {  // fp32 sums of x per 32-element sub-block (4 lanes)
+        float sm = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if ((lane & 3) == 0) xs32[8 * kb + (lane >> 2)] = sm;
       }
     }
   }

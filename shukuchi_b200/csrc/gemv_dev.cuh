@@ -380,9 +380,10 @@ __device__ __forceinline__ void run_task(const GemvArgs& a, const GemvSeg& g, co
 }
 
 // Shared-memory map: [full | empty | xbar barriers][done][gen][red]
-// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)]
-// [stage ring].  The producer first bulk-copies x into the limb-vector slot;
-// consumers turn it into limbs in place.
+// [K-split partials and counts][x-copy barriers, one per consumer warp]
+// [x raw / limb vectors (K*4)][X_b (K/256)][xs32 (K/32, Q4_K)][stage ring].
+// Each consumer warp bulk-copies its blocks of x into the limb-vector slots
+// and turns them into limbs in place.
 // K split of long rows (more than 32 blocks, e.g. the down projection): a row
 // task's blocks are cut into ks <= GEMV_KS_MAX slices processed by different
 // warps; a chunk then holds at most GEMV_KS_ROWT row tasks.
@@ -533,12 +534,12 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // Consumers (warps 0..GEMV_WARPS-1): x (optionally RMSNorm'ed) -> fixed-point
-// limb vectors in shared memory.  Warp w owns 256-blocks w, w+8, ...; lane l
+// limb vectors in shared memory.  Warp w owns 256-blocks w, w+15, ...; lane l
 // holds elements 8l..8l+7 of a block (limb vectors 2l, 2l+1), so a block's
-// maximum is a warp reduction.  Raw x is first copied (cp.async, all copies in
-// flight at once) into the very slots the lane later overwrites with limbs;
-// xready (nullable) is arrived on by each warp at the point GEMV_XREADY_AT
-// names.
+// maximum is a warp reduction.  Raw x is first copied (bulk copies on the
+// warp's barrier, or cp.async by every lane) into the very slots the lane
+// later overwrites with limbs; xready (nullable) is arrived on by each warp at
+// the point GEMV_XREADY_AT names.
 // Rolled loops: this runs once per launch, compact code matters more.
 // Ends with a consumer-only barrier.
 // Step 1 of the prologue: start the copies of raw x into this lane's slots.

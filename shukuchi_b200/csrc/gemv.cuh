@@ -99,9 +99,12 @@ struct GemvMat {
 
 // Returns 0 on success, negative on unsupported shapes (caller may fall back).
 // max_stage_bytes bounds the bytes of one pipeline stage (a chunk of rows).
+#ifndef SHK_GEMV_STAGE_BYTES
+#define SHK_GEMV_STAGE_BYTES 32768
+#endif
 int gemv_plan(GemvPlan& p, const GemvMat* mats, int nmats, uint32_t k, const float* x,
               const float* norm_w, const uint32_t* pos, const float* rope_freq, int* err,
-              int num_sms, uint32_t max_stage_bytes = 32768);
+              int num_sms, uint32_t max_stage_bytes = SHK_GEMV_STAGE_BYTES);
 // Bytes of the x region (fixed-point limbs and per-block sums) for input size K.
 size_t gemv_x_region_bytes(uint32_t K, bool has4, bool has6);
 // Sets the kernels' dynamic shared-memory limit; call once per device.

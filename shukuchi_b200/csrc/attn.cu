@@ -106,6 +106,10 @@ __global__ void kv_read_blocks_kernel(KvLayout kv, uint32_t layer, uint32_t star
 }
 
 constexpr int ATTC_WARPS = 8;
+// Largest cluster the launcher may pick (16, 8 or 4).
+#ifndef SHK_ATT_CLUSTER_CAP
+#define SHK_ATT_CLUSTER_CAP 16
+#endif
 
 // One cluster per KV head (see attn_cluster in attn_dev.cuh).  LONG: the
 // variant with the long-context loop (more registers), launched only for
@@ -154,8 +158,8 @@ const int* cluster_capacity() {
 template <int HD, int G, bool LONG>
 int cluster_ctas(uint32_t n_kv) {
   const int* cap = cluster_capacity<HD, G, LONG>();
-  if (cap[0] >= (int)n_kv) return 16;
-  if (cap[1] >= (int)n_kv) return 8;
+  if (SHK_ATT_CLUSTER_CAP >= 16 && cap[0] >= (int)n_kv) return 16;
+  if (SHK_ATT_CLUSTER_CAP >= 8 && cap[1] >= (int)n_kv) return 8;
   return 4;
 }
 

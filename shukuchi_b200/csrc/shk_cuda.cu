@@ -181,16 +181,18 @@ struct shk_model {
 
 namespace {
 
+// The status for a device error word already read into e: clears the word.
+int ctx_err_take(shk_ctx* c, int e) {
+  if (!e) return SHK_OK;
+  CK(cudaMemset(c->d_err, 0, sizeof(int)));
+  return (e == DERR_TIMEOUT_FULL || e == DERR_TIMEOUT_EMPTY || e == DERR_TIMEOUT_GRID) ? SHK_ETIMEOUT
+                                                                                      : SHK_EDEVICE;
+}
+
 int ctx_err_check(shk_ctx* c) {
   CK(cudaStreamSynchronize(c->compute));
   CK(cudaMemcpy(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-  const int e = *c->h_err;
-  if (e) {
-    CK(cudaMemset(c->d_err, 0, sizeof(int)));
-    return (e == DERR_TIMEOUT_FULL || e == DERR_TIMEOUT_EMPTY || e == DERR_TIMEOUT_GRID) ? SHK_ETIMEOUT
-                                                                                        : SHK_EDEVICE;
-  }
-  return SHK_OK;
+  return ctx_err_take(c, *c->h_err);
 }
 
 cudaStream_t pick(shk_ctx* c, void* s) { return s ? static_cast<cudaStream_t>(s) : c->compute; }
@@ -1177,10 +1179,12 @@ int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_nex
     if (logits && (rc = gather_logits(m, st))) return rc;
     if (logits) CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->d.n_vocab * 4, cudaMemcpyDeviceToHost, st));
   }
+  // the step's device error word comes back with the token: one stream sync
+  CK(cudaMemcpyAsync(m->ctx->h_err, m->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   for (uint32_t l = 0; l < m->d.n_layers; ++l) m->kv->seq[l] = std::max(m->kv->seq[l], pos + 1);
   m->ctx->n_steps++;
-  rc = ctx_err_check(m->ctx);
+  rc = ctx_err_take(m->ctx, *m->ctx->h_err);
   if (rc) return rc;
   if (want_next && next) *next = m->h_tok[2];
   return SHK_OK;

@@ -145,7 +145,8 @@ int shk_cuda_swiglu(shk_ctx *ctx, const float *gate_dev, const float *up_dev, fl
 /* op_embed for one token, Q4_K (12) or F16 (1) table (engine/src/ops.c:533-577) */
 int shk_cuda_embed(shk_ctx *ctx, const void *table_dev, uint32_t dtype, uint32_t n_vocab,
                    uint32_t token, float *out_dev, uint32_t n_embd, void *stream);
-/* first-index argmax (engine/src/engine.c:424-431); result to host */
+/* first-index argmax (engine/src/engine.c:424-431); result to host.
+ * n must be 1..0xFFFFFFFE (SHK_ARGMAX_NOALLOC_MAX_N below); else SHK_EINVAL. */
 int shk_cuda_argmax(shk_ctx *ctx, const float *x_dev, uint32_t n, uint32_t *out_host);
 
 /* ---- Q8_0 KV cache in HBM (engine/include/kv_cache.h:11-37).  Quantisation
@@ -329,8 +330,11 @@ int shk_cuda_model_tp_p2p_import(shk_model *m, const void *handles, const uint32
  *  - Scratch is a fixed 2304-byte array in the library's device image (block
  *    partials + merge ticket); every GPU that loads the library holds it until
  *    the process exits.  No cudaMalloc / cudaFree is called.
- *  - The first call on each device looks up the array's device address (set-up
- *    under a lock); make that first call before any stream capture.
+ *  - The first call in each CUDA context (one per device for runtime-API
+ *    callers; a new one after cudaDeviceReset or under a caller's own driver
+ *    context) looks up the array's device address in that context (set-up
+ *    under a lock, cached by the context's unique id); make that first call
+ *    before any stream capture.
  *  - All calls on a device share the array: calls whose kernels overlap on the
  *    GPU (e.g. on two streams at once) race and give wrong results.
  *  - n must be 1..SHK_ARGMAX_NOALLOC_MAX_N; larger or zero n returns

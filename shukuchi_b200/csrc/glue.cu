@@ -51,8 +51,10 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restr
   __shared__ int last;
   pdl_trigger();
   pdl_wait();
-  const uint32_t per = (n + gridDim.x - 1) / gridDim.x;
-  const uint32_t lo = blockIdx.x * per, hi = min(n, lo + per);
+  // 64-bit: n + gridDim.x and blockIdx.x * per may pass 2^32 for n near it
+  const uint64_t per = ((uint64_t)n + gridDim.x - 1) / gridDim.x;
+  const uint32_t lo = (uint32_t)min((uint64_t)n, blockIdx.x * per);
+  const uint32_t hi = (uint32_t)min((uint64_t)n, (uint64_t)lo + per);
   float bv;
   uint32_t bi;
   am_block<AM_THREADS>(x, lo, hi, sv, si, [] { __syncthreads(); }, bv, bi);
@@ -162,7 +164,7 @@ cudaError_t embed_launch(const void* table, uint32_t dtype, const uint32_t* tok,
 }
 
 int argmax_blocks(uint32_t n) {
-  const uint32_t b = (n + 4095) / 4096;
+  const uint64_t b = ((uint64_t)n + 4095) / 4096;  // 64-bit: n + 4095 may pass 2^32
   return (int)(b < 1 ? 1 : (b > 148 ? 148 : b));
 }
 

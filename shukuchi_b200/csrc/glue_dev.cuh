@@ -55,11 +55,12 @@ __device__ __forceinline__ void am_block(const float* __restrict__ x, uint32_t l
                                          uint32_t& bi_out) {
   float bv = -INFINITY;
   uint32_t bi = 0xFFFFFFFFu;
-  for (uint32_t i = lo + threadIdx.x; i < hi; i += NT) {
+  // 64-bit index: with hi close to 2^32 a 32-bit i + NT would wrap below hi
+  for (uint64_t i = (uint64_t)lo + threadIdx.x; i < hi; i += NT) {
     const float v = __ldcg(x + i);  // may have been written earlier in the same launch
     if (bi == 0xFFFFFFFFu || v > bv) {  // i increases: strict > keeps the first
       bv = v;
-      bi = i;
+      bi = (uint32_t)i;
     }
   }
 #pragma unroll

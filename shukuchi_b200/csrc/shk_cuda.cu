@@ -495,7 +495,8 @@ int shk_cuda_embed(shk_ctx* c, const void* table, uint32_t dtype, uint32_t n_voc
 }
 
 int shk_cuda_argmax(shk_ctx* c, const float* x, uint32_t n, uint32_t* out) {
-  if (!c || !x || !out || !n) return SHK_EINVAL;
+  // index 0xFFFFFFFF marks an empty block partial, so n stops one below it
+  if (!c || !x || !out || !n || n > SHK_ARGMAX_NOALLOC_MAX_N) return SHK_EINVAL;
   CK(argmax_launch(x, n, c->am_v, c->am_i, c->am_cnt, c->d_u32 + 2, nullptr, c->compute));
   CK(cudaMemcpyAsync(c->h_u32 + 2, c->d_u32 + 2, 4, cudaMemcpyDeviceToHost, c->compute));
   CK(cudaStreamSynchronize(c->compute));

@@ -44,11 +44,33 @@ def test_argmax_noalloc_matches_argmax():
         ctx.close()
 
 
+def test_argmax_noalloc_last_partial_block():
+    # n spans several 4096-element argmax blocks with a short last one; the
+    # maximum sits in that last partial block, then at its very last element
+    rng = np.random.default_rng(7)
+    n = 3 * 4096 + 100
+    x = rng.normal(0, 1, n).astype(np.float32)
+    for where in (3 * 4096 + 37, n - 1):
+        y = x.copy()
+        y[where] = 10.0
+        got = _noalloc(torch.from_numpy(y).cuda(), n)
+        assert got == where, (got, where)
+
+
 def test_argmax_noalloc_rejects_bad_sizes():
     lib = sc.lib()
     x = torch.zeros(4, device="cuda")
     out = torch.zeros(1, dtype=torch.int32, device="cuda")
     assert lib.shk_cuda_argmax_noalloc(x.data_ptr(), 0, out.data_ptr(), None) == -1
-    assert lib.shk_cuda_argmax_noalloc(x.data_ptr(), 0xFFFFFFFF, out.data_ptr(), None) == -1
+    # one past the largest accepted n (SHK_ARGMAX_NOALLOC_MAX_N = 0xFFFFFFFE)
+    assert lib.shk_cuda_argmax_noalloc(x.data_ptr(), 0xFFFFFFFE + 1, out.data_ptr(), None) == -1
     assert lib.shk_cuda_argmax_noalloc(None, 4, out.data_ptr(), None) == -1
     assert int(out.cpu()[0]) == 0  # nothing was launched
+    # the context-based argmax takes the same bound
+    ctx = sc.Context(0)
+    try:
+        res = C.c_uint32(7)
+        assert lib.shk_cuda_argmax(ctx.h, x.data_ptr(), 0xFFFFFFFE + 1, C.byref(res)) == -1
+        assert res.value == 7
+    finally:
+        ctx.close()

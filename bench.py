@@ -212,6 +212,51 @@ def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
     return 1.0 / per_token, kind, sample
 
 
+PARITY_SHAPE = ("tp-hd128", 2, 1024, 8, 4, 2048, 1024)  # 2 layers, d 1024, 8/4 heads x 128, ffn 2048
+
+
+def parity_check(ctx, ws, rank, local):
+    """The decode path of this run (same context, same rank layout) on a small
+    synthetic model against the oracle: 5 prompt ids + 8 greedy tokens,
+    greedy ids and max|dlogit| / std(logits).  Rank 0 runs the oracle; every
+    rank's ids are gathered.  Returns the JSON object (rank 0) or None."""
+    import numpy as np
+    from shukuchi_b200 import synth
+    from shukuchi_b200 import tp as tpl
+    from shukuchi_b200.device_model import GpuDecoder
+
+    shape = synth.ModelShape(*PARITY_SHAPE)
+    model = synth.make_model(shape, seed=21)
+    prompt = np.random.default_rng(7).integers(0, shape.n_vocab, 5).astype(np.uint32)
+    n_dec = 8
+    if ws > 1:
+        mr, lay = tpl.shard_model(model, rank, ws)
+        tp_rows = (lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi)
+    else:
+        mr, tp_rows = model, None
+    dec = GpuDecoder(ctx, mr, len(prompt) + n_dec + 1, device=f"cuda:{local}", tp_rows=tp_rows)
+    try:
+        logits = np.zeros((n_dec, shape.n_vocab), np.float32)
+        ids = dec.generate(prompt, n_dec, logits)
+        ctx.check()
+    finally:
+        dec.close()
+    all_ids = [ids.tolist()]
+    if ws > 1:
+        import torch.distributed as dist
+        all_ids = [None] * ws
+        dist.all_gather_object(all_ids, ids.tolist())
+    if rank != 0:
+        return None
+    from oracle.oracle_py import Oracle
+    t_ref, l_ref = Oracle().generate(model, prompt, n_dec)
+    dl = max(float(np.max(np.abs(logits[t] - l_ref[t]))) / float(np.std(l_ref[t])) for t in range(n_dec))
+    return {"model": f"{shape.name} (2 layers, d 1024, 8/4 heads x 128, ffn 2048, vocab 1024), "
+                     f"5 prompt + {n_dec} greedy ids vs the oracle",
+            "ids_match": all(list(r) == t_ref.tolist() for r in all_ids),
+            "ranks": ws, "max_dlogit_over_std": dl, "tolerance": 1e-2}
+
+
 def workload_config(args, ws):
     from shukuchi_b200 import synth
     name = synth.SHAPES[args.shape].name
@@ -244,6 +289,7 @@ def run_ours(args, ws, rank, local):
     from shukuchi_b200 import cuda as sc
     from shukuchi_b200 import synth
     from shukuchi_b200 import tp as tpl
+    from shukuchi_b200 import synth_device
     from shukuchi_b200.synth_device import make_device_model
 
     torch.cuda.set_device(local)
@@ -259,8 +305,11 @@ def run_ours(args, ws, rank, local):
         obj = [sc.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         ctx.tp_init(rank, ws, obj[0])
+    # correctness of this exact path before it is timed (small model, oracle on rank 0)
+    parity = parity_check(ctx, ws, rank, local) if not args.p2p_allreduce else None
     wts = make_device_model(lshape, seed=1234 + rank, device=f"cuda:{local}",
-                            o_rows=lay.o_hi - lay.o_lo, out_rows=lay.v_hi - lay.v_lo, ctx=ctx)
+                            o_rows=lay.o_hi - lay.o_lo, out_rows=lay.v_hi - lay.v_lo, ctx=ctx,
+                            tiled=(synth_device.TILED_DEFAULT if not args.p2p_allreduce else False))
     total = args.prompt + 2 * (args.warmup + args.steps) + 8
     kv = sc.KvCache(ctx, lshape.n_layers, lshape.n_kv_heads, lshape.head_dim, total)
     m = sc.DeviceModel(ctx, kv, wts.desc)
@@ -405,6 +454,8 @@ def run_ours(args, ws, rank, local):
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
                           "frac": step_gbs / (ws * peak)},
         "cpu_baseline": cpu,
+        "parity": parity,
+        "nccl_nranks": ctx.tp_comm_size() if ws > 1 else None,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

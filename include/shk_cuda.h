@@ -107,6 +107,32 @@ int shk_cuda_matmul_q6k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev,
  * planar layout (to_planar != 0) or back to GGUF blocks.  Async on stream. */
 int shk_cuda_q6k_repack(shk_ctx *ctx, void *w_dev, uint32_t rows, uint32_t k, uint32_t row_stride,
                         int to_planar, void *stream);
+/* ---- Row-tiled weight layout for the tensor-core matvec.  No counterpart in
+ *      the reference (its weights stay GGUF blocks in host memory, read by
+ *      op_matmul_q4_k / op_matmul_q6_k, engine/src/ops.c:266-314, 361-404).
+ *      A matrix of `rows` rows and nb = k/256 super-blocks becomes ceil(rows/16)
+ *      row tiles; tile (row tile t, block b) holds block b of rows 16t..16t+15
+ *      (rows past `rows` are zero) at byte (t * nb + b) * tile_bytes, tile_bytes
+ *      = 16 * 144 (Q4_K) or 16 * 210 (Q6_K).  Inside a tile the GGUF bytes are
+ *      only moved, into the order the tensor-core fragments read them:
+ *        Q4_K: [0,256) the 16 rows' 16-byte block headers (d, dmin, scales);
+ *              [256,2304) [chunk j<4][lane<32][16]: row g = lane/4 quant bytes
+ *              32j + 8(lane%4) .. +7, then row g+8's.
+ *        Q6_K: [0,3072) [half n<2][lane<32][48]: row g ql bytes 64n + 8t..+7,
+ *              ql 64n+32+8t..+7, qh 32n+8t..+7 (t = lane%4), then row g+8's;
+ *              [3072,3328) int8 scales[16] per row; [3328,3360) fp16 d per row.
+ *      Weights registered as SHK_DTYPE_Q4_K_TILED / SHK_DTYPE_Q6_K_TILED run on
+ *      the tensor-core matvec (mma.sync int8 over fixed-point x limbs). ---- */
+#define SHK_DTYPE_Q4_K_TILED 0x20Cu
+#define SHK_DTYPE_Q6_K_TILED 0x20Eu
+/* Bytes of the tiled form of a rows x k matrix of dtype 12/14 (or a tiled
+ * dtype); 0 for other dtypes or k not a multiple of 256. */
+size_t shk_cuda_tiled_bytes(uint32_t dtype, uint32_t rows, uint32_t k);
+/* GGUF rows (dtype 12 or 14, src_row_stride bytes apart, 0 = dense) -> the
+ * tiled layout at dst_dev (shk_cuda_tiled_bytes bytes, 16-byte aligned, not
+ * overlapping src).  Async on stream. */
+int shk_cuda_tile(shk_ctx *ctx, uint32_t dtype, const void *src_dev, uint32_t src_row_stride, uint32_t rows,
+                  uint32_t k, void *dst_dev, void *stream);
 /* ---- batched prefill matmul on the tensor cores.  No counterpart in the
  *      reference, which feeds prompt tokens one at a time
  *      (engine/src/engine.c:306-501); this is the contraction those n_tokens
@@ -120,8 +146,9 @@ int shk_cuda_q6k_repack(shk_ctx *ctx, void *w_dev, uint32_t rows, uint32_t k, ui
 int shk_cuda_prefill_matmul(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
                             const float *x_dev, float *y_dev, uint32_t m, uint32_t k, uint32_t n_tokens,
                             void *stream);
-/* dequantise-matvec by dtype: 12 (Q4_K), 14 (GGUF Q6_K) or
- * SHK_DTYPE_Q6_K_PLANAR; row_stride 0 = dense rows. */
+/* dequantise-matvec by dtype: 12 (Q4_K), 14 (GGUF Q6_K),
+ * SHK_DTYPE_Q6_K_PLANAR, SHK_DTYPE_Q4_K_TILED or SHK_DTYPE_Q6_K_TILED;
+ * row_stride 0 = dense rows (ignored for tiled weights). */
 int shk_cuda_matvec(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
                     const float *x_dev, float *y_dev, uint32_t m, uint32_t k, void *stream);
 /* Same contract as metal_matmul_q{4,6}k_vec: HOST weights/x/y, synchronous
@@ -292,6 +319,10 @@ int shk_cuda_selftest_wait_timeout(shk_ctx *ctx, uint32_t budget_us);
  * model.  NCCL is loaded at first use (libnccl.so.2). */
 int shk_cuda_tp_unique_id(void *out, size_t cap);
 int shk_cuda_tp_init(shk_ctx *ctx, int rank, int world, const void *id);
+/* Ranks in the context's NCCL communicator (ncclCommCount): world after
+ * shk_cuda_tp_init, 1 without one; negative on error.  No counterpart in the
+ * reference (which has no tensor parallelism). */
+int shk_cuda_tp_comm_size(shk_ctx *ctx);
 /* This rank computes rows [o_lo, o_hi) of the O projection (its attn_o
  * weights have o_hi - o_lo rows; ranks that share attention heads split the
  * rows) and rows [v_lo, v_hi) of the output head (its output weights have

@@ -66,6 +66,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(n) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -89,6 +92,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     __nanosleep(32);
     if ((n & 31) == 0 && globaltimer_ns() - t0 > budget_ns) {
+      set_error(err, code);
+      return false;
+    }
+  }
+}
+// Bounded wait without sleeping between polls: mbarrier.try_wait itself
+// suspends the warp in hardware until the phase completes or a short time
+// limit passes, so a waiter that is about to be released wakes at once.  For
+// pipelines whose stages turn over every microsecond or so.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               uint64_t budget_ns = WAIT_BUDGET_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 255) == 0 && globaltimer_ns() - t0 > budget_ns) {
       set_error(err, code);
       return false;
     }

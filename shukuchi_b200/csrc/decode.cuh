@@ -1,20 +1,22 @@
 // decode.cuh -- persistent whole-token decode kernel (host-side API).
 //
 // One cooperative launch runs n tokens: embed -> per layer (RMSNorm + QKV +
-// RoPE GEMV, append + attention, O + residual, RMSNorm + gate/up + SwiGLU,
+// RoPE matvec, append + attention, O + residual, RMSNorm + gate/up + SwiGLU,
 // down + residual) -> lm_head -> argmax, feeding the argmax back to the next
-// embed on the device (engine/src/engine.c:306-501 token loop,
-// :76-229 layer forward).  Phases are separated by grid-wide barriers; the
-// producer warp of every CTA keeps streaming the weights of the coming GEMV
-// phases into its shared-memory ring across those barriers, so HBM streaming
-// does not stop between projections, layers or tokens.
+// embed on the device (engine/src/engine.c:306-501 token loop, :76-229 layer
+// forward).  The projections are tensor-core matvecs over row-tiled weights
+// (mmv_dev.cuh).  A producer lane per CTA streams the weight chunks of every
+// matvec phase of every token into the CTA's shared-memory ring in program
+// order and never waits for activations, so HBM keeps streaming through the
+// phase boundaries (grid-wide waits on a monotonic counter), attention and
+// the x conversions.
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "attn.cuh"
-#include "gemv.cuh"
+#include "mmv.cuh"
 
 namespace shk {
 
@@ -22,17 +24,11 @@ enum DecodePhaseKind : uint32_t { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ARG
 
 struct DecodePhase {
   uint32_t kind;  // DecodePhaseKind
-  uint32_t idx;   // index into DecodeProgram::gemv or ::attn
-};
-
-// Grid barrier state in device memory (zeroed before each launch).
-struct GridBar {
-  uint32_t count;
-  uint32_t gen;
+  uint32_t idx;   // index into DecodeProgram::mmv or ::attn
 };
 
 struct DecodeProgram {
-  const GemvArgs* gemv;       // device array of GEMV phase plans
+  const MmvArgs* mmv;         // device array of matvec phase plans (common ring geometry)
   const AttnArgs* attn;       // device array of attention phases
   const DecodePhase* phases;  // device array: one token's phases in order
   uint32_t n_phases;          // phases per token
@@ -46,14 +42,15 @@ struct DecodeProgram {
   float* am_v;
   uint32_t* am_i;
   int* am_cnt;
-  uint32_t* tok;  // device [0] token, [1] position
-  uint32_t advance_pos;  // argmax advances tok[1] (device-fed token loop)
-  // shared-memory geometry
-  uint32_t ns, stage_bytes;  // ring stages and their size
+  uint32_t* tok;          // device [0] token, [1] position
+  uint32_t advance_pos;   // argmax advances tok[1] (device-fed token loop)
+  // shared-memory geometry: ring of ns stages of `chunk` slots of slot_bytes
+  uint32_t ns, slot_bytes, chunk, lg_chunk;
   uint32_t xreg_off, ring_off;
+  uint32_t kmax;          // largest matvec K (x region size)
   // attention work split: n_kv heads x attn_nsplit position splits
   uint32_t n_kv, attn_nsplit;
-  GridBar* bar;
+  uint32_t* bar;          // phases completed x grid (zeroed before each launch)
   int* err;
   // optional timeline (null = off): CTA 0 records %globaltimer at the start and,
   // per phase, when it reaches the barrier and when it leaves it:
@@ -63,9 +60,10 @@ struct DecodeProgram {
   uint32_t trace_cap_phases;
 };
 
-// Shared memory of the decode kernel for the given head geometry, largest K
-// and ring.  Fills P.xreg_off / P.ring_off.
-size_t decode_smem(DecodeProgram& P, uint32_t head_dim, uint32_t group, uint32_t kmax);
+// Shared memory of the decode kernel for the given head geometry and largest
+// K, with the ring geometry already in P (ns, slot_bytes, chunk).  Fills
+// P.xreg_off / P.ring_off.  fixed_out: bytes before the ring.
+size_t decode_smem(DecodeProgram& P, uint32_t head_dim, uint32_t group, size_t* fixed_out = nullptr);
 // Sets the kernel attributes; returns false if this (head_dim, group) is not
 // built or one CTA per SM does not fit.
 bool decode_supported(uint32_t head_dim, uint32_t group, size_t smem, int num_sms);

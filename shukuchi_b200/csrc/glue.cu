@@ -65,9 +65,17 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restr
     last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
   }
   __syncthreads();
-  if (!last || threadIdx.x != 0) return;
+  if (!last) return;
   __threadfence();
-  *tok_out = idx_off + am_merge(part_v, part_i, gridDim.x, val_out);
+  // the reference keeps index 0 when x[0] is NaN (only the slice holding the
+  // vocabulary's index 0 can see it)
+  const bool x0_nan = idx_off == 0 && n > 0 && isnan(__ldcg(x));
+  float v;
+  const uint32_t ix = am_merge_par<AM_THREADS>(part_v, part_i, gridDim.x, x0_nan, sv, si,
+                                               [] { __syncthreads(); }, &v);
+  if (threadIdx.x != 0) return;
+  *tok_out = idx_off + ix;
+  if (val_out) *val_out = v;
   if (pos_inc) *pos_inc += 1;
   *counter = 0;
 }

@@ -58,7 +58,9 @@ __device__ __forceinline__ void am_block(const float* __restrict__ x, uint32_t l
   // 64-bit index: with hi close to 2^32 a 32-bit i + NT would wrap below hi
   for (uint64_t i = (uint64_t)lo + threadIdx.x; i < hi; i += NT) {
     const float v = __ldcg(x + i);  // may have been written earlier in the same launch
-    if (bi == 0xFFFFFFFFu || v > bv) {  // i increases: strict > keeps the first
+    // NaN never wins (the reference's `x[i] > x[best]` is false for it; a NaN
+    // at index 0 is handled by the merge); i increases: strict > keeps the first
+    if (!isnan(v) && (bi == 0xFFFFFFFFu || v > bv)) {
       bv = v;
       bi = (uint32_t)i;
     }
@@ -89,20 +91,50 @@ __device__ __forceinline__ void am_block(const float* __restrict__ x, uint32_t l
   bi_out = bi;
 }
 
-// Merge of the per-block partials by the last block (thread 0).  NaN logits
-// never compare greater; an all-NaN vector yields index 0 as in the reference
-// loop.
-__device__ __forceinline__ uint32_t am_merge(const float* part_v, const uint32_t* part_i, uint32_t n,
-                                             float* v_out = nullptr) {
-  float v = __ldcg(&part_v[0]);
-  uint32_t ix = __ldcg(&part_i[0]);
-  for (uint32_t b = 1; b < n; ++b) {
+// Parallel merge of n per-block partials by the NT threads of the last block
+// (sync() synchronises them; sv/si: NT/32 entries); the result is valid in
+// thread 0.  (value, index) pairs with no NaN values order totally (larger
+// value, then lower index), so the tree gives the sequential answer.  The
+// reference's loop (best = 0; x[i] > x[best]) returns 0 when x[0] is NaN --
+// x0_nan -- and when every value is NaN.
+template <int NT, typename Sync>
+__device__ __forceinline__ uint32_t am_merge_par(const float* part_v, const uint32_t* part_i, uint32_t n,
+                                                 bool x0_nan, float* sv, uint32_t* si, Sync sync,
+                                                 float* v_out = nullptr) {
+  float v = -INFINITY;
+  uint32_t ix = 0xFFFFFFFFu;
+  for (uint32_t b = threadIdx.x; b < n; b += NT) {
     const float ov = __ldcg(&part_v[b]);
     const uint32_t oi = __ldcg(&part_i[b]);
     if (am_better(v, ix, ov, oi)) {
       v = ov;
       ix = oi;
     }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+    if (am_better(v, ix, ov, oi)) {
+      v = ov;
+      ix = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = ix;
+  }
+  sync();
+  if (threadIdx.x == 0)
+    for (int w = 1; w < NT / 32; ++w)
+      if (am_better(v, ix, sv[w], si[w])) {
+        v = sv[w];
+        ix = si[w];
+      }
+  if (x0_nan) {
+    v = __int_as_float(0x7fc00000);
+    ix = 0;
   }
   if (v_out) *v_out = v;
   return (ix == 0xFFFFFFFFu) ? 0u : ix;

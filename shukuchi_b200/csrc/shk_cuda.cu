@@ -18,6 +18,7 @@
 #include "decode.cuh"
 #include "gemv.cuh"
 #include "glue.cuh"
+#include "mmv.cuh"
 
 using // Fewest cached positions per attention split (CTA of a KV head's cluster).
 #ifndef SHK_ATT_MIN_SPLIT
@@ -45,6 +46,7 @@ struct NcclApi {
                              cudaStream_t);
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   ncclResult_t (*comm_destroy)(ncclComm_t);
+  ncclResult_t (*comm_count)(const ncclComm_t, int*);
 };
 const NcclApi* nccl() {
   static NcclApi api;
@@ -60,7 +62,9 @@ const NcclApi* nccl() {
       api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
       api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
       api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
-      if (api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy)
+      api.comm_count = reinterpret_cast<decltype(api.comm_count)>(dlsym(h, "ncclCommCount"));
+      if (api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy &&
+          api.comm_count)
         state = 1;
     }
   }
@@ -85,6 +89,7 @@ struct shk_ctx {
   uint32_t* am_i = nullptr;
   int* am_cnt = nullptr;
   float* d_freq = nullptr;  // RoPE frequency table for shk_cuda_rope (<= 512 entries)
+  void* mmv_scratch = nullptr;  // tensor-core matvec: cross-CTA combine of split row tiles
   float* h_freq = nullptr;  // pinned
   // synchronous host-pointer matvec scratch
   void* hv_w = nullptr;
@@ -118,8 +123,49 @@ struct shk_kv {
 
 namespace {
 
+// One projection: the staged dp4a GEMV over GGUF / planar rows, or the
+// tensor-core matvec over row-tiled weights (tiled = true).
+struct ProjPlan {
+  GemvPlan g;
+  MmvPlan mm;
+  bool tiled = false;
+};
+
+cudaError_t proj_launch(const ProjPlan& p, cudaStream_t st, const uint32_t* pos = nullptr) {
+  if (p.tiled) {
+    if (!pos) return mmv_launch(p.mm, st);
+    MmvPlan q = p.mm;
+    q.args.pos = pos;
+    return mmv_launch(q, st);
+  }
+  if (!pos) return gemv_launch(p.g, st);
+  GemvPlan q = p.g;
+  q.args.pos = pos;
+  return gemv_launch(q, st);
+}
+
+// Weight bytes one launch reads.
+uint64_t proj_weight_bytes(const ProjPlan& p) {
+  uint64_t b = 0;
+  if (p.tiled) {
+    for (uint32_t i = 0; i < p.mm.args.nseg; ++i) {
+      const MmvSeg& g = p.mm.args.seg[i];
+      b += (uint64_t)g.ntiles * g.nb * (g.qt == T_Q4K ? Q4T_BYTES : Q6T_BYTES) * (g.dual ? 2 : 1);
+    }
+    return b;
+  }
+  for (uint32_t i = 0; i < p.g.args.nseg; ++i) {
+    const GemvSeg& g = p.g.args.seg[i];
+    const uint64_t bb = g.qt == T_Q4K ? Q4K_BYTES : Q6K_BYTES;
+    b += (uint64_t)g.m * g.nb * bb * (g.dual ? 2 : 1);
+  }
+  return b;
+}
+
+bool dt_tiled(uint32_t dt) { return dt == (uint32_t)T_Q4K_TILED || dt == (uint32_t)T_Q6K_TILED; }
+
 struct LayerPlans {
-  GemvPlan qkv, o, gateup, down;
+  ProjPlan qkv, o, gateup, down;
   bool ok = false;
 };
 
@@ -140,7 +186,7 @@ struct shk_model {
   std::vector<uint8_t> have;
   std::vector<LayerPlans> plans;
   float* d_freq = nullptr;  // RoPE table: powf(1/theta, i/head_dim), host libm
-  GemvPlan head;
+  ProjPlan head;
   bool head_ok = false;      // staged plan available for the output head
   bool head_generic = false; // rows not 16-byte multiples: plain-load GEMV
   cudaGraphExec_t g_layers = nullptr, g_head = nullptr, g_loop = nullptr;
@@ -151,10 +197,10 @@ struct shk_model {
     size_t smem = 0;
     int grid = 0;
     uint32_t n_phases_full = 0;
-    GemvArgs* d_gemv = nullptr;
+    MmvArgs* d_mmv = nullptr;
     AttnArgs* d_attn = nullptr;
     DecodePhase* d_phases = nullptr;
-    GridBar* d_bar = nullptr;
+    uint32_t* d_bar = nullptr;
   } pk;
   uint32_t o_lo = 0, o_hi = 0;  // tensor parallel: this rank's rows of the O projection output
   uint32_t v_lo = 0, v_hi = 0;  // ... and of the output head (logits); all rows when replicated
@@ -185,6 +231,8 @@ namespace {
 int ctx_err_take(shk_ctx* c, int e) {
   if (!e) return SHK_OK;
   CK(cudaMemset(c->d_err, 0, sizeof(int)));
+  // a launch that gave up may have left a combine count behind
+  if (c->mmv_scratch) CK(cudaMemset(c->mmv_scratch, 0, MMV_SCRATCH_BYTES));
   return (e == DERR_TIMEOUT_FULL || e == DERR_TIMEOUT_EMPTY || e == DERR_TIMEOUT_GRID) ? SHK_ETIMEOUT
                                                                                       : SHK_EDEVICE;
 }
@@ -212,6 +260,16 @@ int grow(T** p, size_t* cap, size_t need) {
 int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, uint32_t row_stride, const float* x, float* y,
                uint32_t m, uint32_t k, cudaStream_t st) {
   if (!w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
+  if (dt_tiled(qt)) {
+    if (m == 0) return SHK_OK;
+    MmvMat mt{w, nullptr, y, m, qt, EPI_STORE, 0};
+    MmvPlan p;
+    const int rc = mmv_plan(p, &mt, 1, k, x, nullptr, nullptr, nullptr, c->d_err, c->num_sms, c->mmv_scratch);
+    if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+    CK(mmv_launch(p, st));
+    c->n_matvec++;
+    return SHK_OK;
+  }
   if (qt != T_Q4K && qt != T_Q6K && qt != T_Q6K_PLANAR) return SHK_EUNSUPPORTED;
   if (m == 0) return SHK_OK;
   const uint32_t nb = k / QK;
@@ -316,6 +374,9 @@ shk_ctx* shk_cuda_init(const shk_cuda_config* cfg) {
   ok = ok && cudaMalloc(&c->d_freq, 512 * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMallocHost(&c->h_freq, 512 * sizeof(float)) == cudaSuccess;
   ok = ok && gemv_init() == cudaSuccess;
+  ok = ok && mmv_init() == cudaSuccess;
+  ok = ok && cudaMalloc(&c->mmv_scratch, MMV_SCRATCH_BYTES) == cudaSuccess;
+  ok = ok && cudaMemset(c->mmv_scratch, 0, MMV_SCRATCH_BYTES) == cudaSuccess;
   if (!ok) {
     shk_cuda_shutdown(c);
     return nullptr;
@@ -339,6 +400,7 @@ void shk_cuda_shutdown(shk_ctx* c) {
   cudaFree(c->am_i);
   cudaFree(c->am_cnt);
   cudaFree(c->d_freq);
+  cudaFree(c->mmv_scratch);
   cudaFreeHost(c->h_freq);
   cudaFree(c->hv_w);
   cudaFree(c->q6_scratch);
@@ -441,6 +503,24 @@ int shk_cuda_q6k_repack(shk_ctx* c, void* w, uint32_t rows, uint32_t k, uint32_t
   if (stride % 16 || stride < 210u * (k / QK) || stride > 227u * 1024u || (reinterpret_cast<uintptr_t>(w) & 15))
     return SHK_EINVAL;
   CK(q6k_repack_launch(w, rows, k, stride, to_planar != 0, c->num_sms, pick(c, s)));
+  return SHK_OK;
+}
+
+size_t shk_cuda_tiled_bytes(uint32_t dtype, uint32_t rows, uint32_t k) {
+  if (k == 0 || k % QK) return 0;
+  if (dtype == T_Q4K || dtype == (uint32_t)T_Q4K_TILED) return mmv_tiled_bytes(T_Q4K_TILED, rows, k);
+  if (dtype == T_Q6K || dtype == (uint32_t)T_Q6K_TILED) return mmv_tiled_bytes(T_Q6K_TILED, rows, k);
+  return 0;
+}
+
+int shk_cuda_tile(shk_ctx* c, uint32_t dtype, const void* src, uint32_t src_row_stride, uint32_t rows, uint32_t k,
+                  void* dst, void* s) {
+  if (!c || !src || !dst || rows == 0 || k == 0 || k % QK) return SHK_EINVAL;
+  if (dtype != T_Q4K && dtype != T_Q6K) return SHK_EUNSUPPORTED;
+  cudaSetDevice(c->device);
+  const cudaError_t e = mmv_tile_launch(dtype, src, src_row_stride, rows, k, dst, pick(c, s));
+  if (e == cudaErrorInvalidValue) return SHK_EINVAL;
+  CK(e);
   return SHK_OK;
 }
 int shk_cuda_matmul_q4k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
@@ -628,7 +708,7 @@ void model_free_graphs(shk_model* m) {
   if (m->g_loop) cudaGraphExecDestroy(m->g_loop);
   m->g_layers = m->g_head = m->g_loop = nullptr;
   auto& k = m->pk;
-  cudaFree(k.d_gemv);
+  cudaFree(k.d_mmv);
   cudaFree(k.d_attn);
   cudaFree(k.d_phases);
   cudaFree(k.d_bar);
@@ -674,6 +754,29 @@ void p2p_out(shk_model* m, GemvArgs& a, uint32_t j, uint32_t row_off) {
   }
 }
 
+// Plans one projection: the tensor-core matvec when every matrix is row-tiled,
+// else the staged GEMV (a mix is not supported).
+int plan_proj(shk_model* m, ProjPlan& P, const GemvMat* mats, int n, uint32_t k, const float* x,
+              const float* norm_w, const uint32_t* pos) {
+  shk_ctx* c = m->ctx;
+  int nt = 0;
+  for (int i = 0; i < n; ++i) nt += dt_tiled(mats[i].qt) ? 1 : 0;
+  if (nt != 0 && nt != n) return SHK_EUNSUPPORTED;
+  P.tiled = nt == n;
+  int rc;
+  if (P.tiled) {
+    MmvMat mm[MMV_MAX_SEGS];
+    for (int i = 0; i < n; ++i)
+      mm[i] = MmvMat{mats[i].w, mats[i].w2, mats[i].y, mats[i].m, mats[i].qt, mats[i].epi, mats[i].rope_hd};
+    // the persistent kernel's shared ring: items of at most two Q6_K tiles
+    const uint32_t cap = (c->flags & SHK_CUDA_FLAG_PERSISTENT) ? 2u * Q6T_BYTES : 0u;
+    rc = mmv_plan(P.mm, mm, n, k, x, norm_w, pos, m->d_freq, c->d_err, c->num_sms, c->mmv_scratch, cap);
+  } else {
+    rc = gemv_plan(P.g, mats, n, k, x, norm_w, pos, m->d_freq, c->d_err, c->num_sms);
+  }
+  return rc == 0 ? SHK_OK : rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+}
+
 int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P, uint32_t layer) {
   const shk_model_desc& d = m->d;
   shk_ctx* c = m->ctx;
@@ -684,8 +787,8 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P, uin
       {lv.attn_k, nullptr, m->k, kvd, lv.attn_k_dtype, 0, EPI_ROPE, hd},
       {lv.attn_v, nullptr, m->v, kvd, lv.attn_v_dtype, lv.row_stride_v, EPI_STORE, 0},
   };
-  int rc = gemv_plan(P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos, m->d_freq, c->d_err, c->num_sms);
-  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  int rc = plan_proj(m, P.qkv, qkv, 3, d.n_embd, m->hidden, lv.attn_norm, pos);
+  if (rc) return rc;
   // Tensor parallel over NCCL: rank 0 adds the residual, the others store
   // their partial sums (all-reduced afterwards); the O projection covers rows
   // [o_lo, o_hi).  Over peer memory (p2p): every rank sends pure partials
@@ -693,23 +796,21 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P, uin
   const bool p2p = m->p2p.on;
   const uint8_t res_epi = p2p ? EPI_TP : (c->tp_rank == 0 ? EPI_ADD : EPI_STORE);
   GemvMat o{lv.attn_o, nullptr, m->hidden + m->o_lo, m->o_hi - m->o_lo, lv.attn_o_dtype, 0, res_epi, 0};
-  rc = gemv_plan(P.o, &o, 1, qd, m->att, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
-  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  if ((rc = plan_proj(m, P.o, &o, 1, qd, m->att, nullptr, nullptr))) return rc;
   if (lv.ffn_gate_dtype != lv.ffn_up_dtype) return SHK_EUNSUPPORTED;
   GemvMat gu{lv.ffn_gate, lv.ffn_up, m->act, d.n_ff, lv.ffn_gate_dtype, 0, EPI_SWIGLU, 0};
-  rc = gemv_plan(P.gateup, &gu, 1, d.n_embd, m->hidden, lv.ffn_norm, nullptr, nullptr, c->d_err, c->num_sms);
-  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  if ((rc = plan_proj(m, P.gateup, &gu, 1, d.n_embd, m->hidden, lv.ffn_norm, nullptr))) return rc;
   GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, res_epi, 0};
-  rc = gemv_plan(P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
-  if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  if ((rc = plan_proj(m, P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr))) return rc;
   if (p2p) {
+    if (P.qkv.tiled || P.o.tiled || P.gateup.tiled || P.down.tiled) return SHK_EUNSUPPORTED;
     // slots: 2l = O of layer l (consumed by gate/up), 2l + 1 = down (consumed
     // by the next layer's QKV or the head); consumer j reads the residual
     // from buffer j % 2 (0 = hidden, 1 = res2) and writes it to the other
-    if (layer > 0) p2p_in(m, P.qkv.args, 2 * layer - 1, m->p2p.res2, m->hidden);
-    p2p_out(m, P.o.args, 2 * layer, m->o_lo);
-    p2p_in(m, P.gateup.args, 2 * layer, m->hidden, m->p2p.res2);
-    p2p_out(m, P.down.args, 2 * layer + 1, 0);
+    if (layer > 0) p2p_in(m, P.qkv.g.args, 2 * layer - 1, m->p2p.res2, m->hidden);
+    p2p_out(m, P.o.g.args, 2 * layer, m->o_lo);
+    p2p_in(m, P.gateup.g.args, 2 * layer, m->hidden, m->p2p.res2);
+    p2p_out(m, P.down.g.args, 2 * layer + 1, 0);
   }
   P.ok = true;
   return SHK_OK;
@@ -748,9 +849,7 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
                   cudaStream_t st, bool pdl) {
   shk_ctx* c = m->ctx;
   const bool tp = c->tp_world > 1;
-  GemvPlan qkv = P.qkv;
-  qkv.args.pos = pos;
-  CK(gemv_launch(qkv, st));
+  CK(proj_launch(P.qkv, st, pos));
   pdl_enabled() = pdl;
   const AttnArgs a = layer_attn_args(m, layer, pos);
   CK(attn_decode_launch(a, st));
@@ -759,15 +858,15 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
     CK(cudaMemsetAsync(m->hidden, 0, (size_t)m->d.n_embd * sizeof(float), st));
     pdl_enabled() = false;
   }
-  CK(gemv_launch(P.o, st));
+  CK(proj_launch(P.o, st));
   if (nccl_ar) {
     if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
       return SHK_ENCCL;
     pdl_enabled() = false;
   }
-  CK(gemv_launch(P.gateup, st));
+  CK(proj_launch(P.gateup, st));
   pdl_enabled() = pdl;
-  CK(gemv_launch(P.down, st));
+  CK(proj_launch(P.down, st));
   if (nccl_ar) {
     if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
       return SHK_ENCCL;
@@ -790,15 +889,27 @@ bool vocab_split(const shk_model* m) { return m->v_hi - m->v_lo < m->d.n_vocab; 
 int plan_head(shk_model* m) {
   shk_ctx* c = m->ctx;
   const uint32_t nv = m->v_hi - m->v_lo;
+  if (dt_tiled(m->d.output_dtype)) {
+    if (m->p2p.on) return SHK_EUNSUPPORTED;
+    MmvMat hm{m->d.output_dev, nullptr, m->logits + m->v_lo, nv, m->d.output_dtype, EPI_STORE, 0};
+    m->head.tiled = true;
+    m->head_generic = false;
+    if (mmv_plan(m->head.mm, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err, c->num_sms,
+                 c->mmv_scratch))
+      return SHK_EUNSUPPORTED;
+    m->head_ok = true;
+    return SHK_OK;
+  }
+  m->head.tiled = false;
   GemvMat hm{m->d.output_dev, nullptr, m->logits + m->v_lo, nv, m->d.output_dtype, 0, EPI_STORE, 0};
-  const int hp = gemv_plan(m->head, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err,
+  const int hp = gemv_plan(m->head.g, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err,
                            c->num_sms);
   if (!head_plan_ok(m->d.output_dtype, hp)) return SHK_EUNSUPPORTED;
   m->head_generic = hp != 0;
   if (m->p2p.on) {
     // the head consumes the last down partials: in its prologue, or (plain-load
     // head) through a sum kernel before it that writes hidden
-    p2p_in(m, m->head.args, 2 * m->d.n_layers - 1, m->p2p.res2, m->hidden);
+    p2p_in(m, m->head.g.args, 2 * m->d.n_layers - 1, m->p2p.res2, m->hidden);
   }
   m->head_ok = true;
   return SHK_OK;
@@ -823,13 +934,13 @@ int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos, bool pdl_after
   const uint32_t nv = m->v_hi - m->v_lo;
   if (m->head_generic) {
     if (m->p2p.on) {
-      CK(gemv_tp_sum_launch(m->head.args, st));
+      CK(gemv_tp_sum_launch(m->head.g.args, st));
       pdl_enabled() = false;
     }
     CK(gemv_generic_launch(m->d.output_dtype, m->d.output_dev, m->hidden, m->logits + m->v_lo, nv,
                            m->d.n_embd, st));
   } else {
-    CK(gemv_launch(m->head, st));
+    CK(proj_launch(m->head, st));
   }
   if (pdl_after_first) pdl_enabled() = true;
   uint32_t* pos_inc = advance_pos ? m->d_tok + 1 : nullptr;
@@ -883,47 +994,68 @@ int capture(shk_model* m, int which, cudaGraphExec_t* out) {
   return ie == cudaSuccess ? SHK_OK : SHK_ECUDA;
 }
 
-// Builds the persistent decode kernel's program: GEMV plans with stages of at
-// most 16 KB (one ring serves every projection), per-layer attention args and
-// the phase list embed, [QKV, attention, O, gate/up, down] x L, lm_head,
-// argmax.  Leaves state -1 (graph path) when the shapes do not fit it.
+// Builds the persistent decode kernel's program: the layers' and the head's
+// tensor-core matvec plans (row-tiled weights) with one common ring geometry,
+// per-layer attention args and the phase list embed, [QKV, attention, O,
+// gate/up, down] x L, lm_head, argmax.  Leaves state -1 (graph path) when the
+// weights are not all tiled or the shapes do not fit it.
 int build_persist(shk_model* m) {
   auto& k = m->pk;
   shk_ctx* c = m->ctx;
   const shk_model_desc& d = m->d;
   k.state = -1;
-  if (!(c->flags & SHK_CUDA_FLAG_PERSISTENT) || m->head_generic || c->tp_world > 1) return SHK_OK;
+  if (!(c->flags & SHK_CUDA_FLAG_PERSISTENT) || !m->head.tiled || c->tp_world > 1) return SHK_OK;
   const uint32_t G = d.n_heads / d.n_kv_heads;
   if (d.n_heads % d.n_kv_heads) return SHK_OK;
-  const uint32_t L = d.n_layers, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
-  const uint32_t* pos = m->d_tok + 1;
-  const uint32_t stage_cap = 16384;
-  std::vector<GemvArgs> ga;
-  uint32_t stage = 0, kmax = 0;
-  auto add = [&](const GemvMat* mats, int n, uint32_t kk, const float* x, const float* nw) -> bool {
-    GemvPlan p;
-    if (gemv_plan(p, mats, n, kk, x, nw, pos, m->d_freq, c->d_err, c->num_sms, stage_cap)) return false;
-    ga.push_back(p.args);
-    stage = std::max(stage, p.args.stage_bytes);
-    kmax = std::max(kmax, kk);
-    return true;
-  };
+  const uint32_t L = d.n_layers;
+  std::vector<MmvArgs> ma;
+  uint32_t slot = 0, kmax = 0;
   for (uint32_t l = 0; l < L; ++l) {
-    const shk_layer_desc& lv = m->layers[l];
-    GemvMat qkv[3] = {
-        {lv.attn_q, nullptr, m->q, qd, lv.attn_q_dtype, 0, EPI_ROPE, hd},
-        {lv.attn_k, nullptr, m->k, kvd, lv.attn_k_dtype, 0, EPI_ROPE, hd},
-        {lv.attn_v, nullptr, m->v, kvd, lv.attn_v_dtype, lv.row_stride_v, EPI_STORE, 0},
-    };
-    GemvMat o{lv.attn_o, nullptr, m->hidden, d.n_embd, lv.attn_o_dtype, 0, EPI_ADD, 0};
-    GemvMat gu{lv.ffn_gate, lv.ffn_up, m->act, d.n_ff, lv.ffn_gate_dtype, 0, EPI_SWIGLU, 0};
-    GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, EPI_ADD, 0};
-    if (!add(qkv, 3, d.n_embd, m->hidden, lv.attn_norm) || !add(&o, 1, qd, m->att, nullptr) ||
-        !add(&gu, 1, d.n_embd, m->hidden, lv.ffn_norm) || !add(&dn, 1, d.n_ff, m->act, nullptr))
-      return SHK_OK;
+    const LayerPlans& P = m->plans[l];
+    for (const ProjPlan* pp : {&P.qkv, &P.o, &P.gateup, &P.down}) {
+      if (!pp->tiled) return SHK_OK;
+      ma.push_back(pp->mm.args);
+    }
   }
-  GemvMat hm{d.output_dev, nullptr, m->logits, d.n_vocab, d.output_dtype, 0, EPI_STORE, 0};
-  if (!add(&hm, 1, d.n_embd, m->hidden, nullptr)) return SHK_OK;
+  ma.push_back(m->head.mm.args);
+  for (const MmvArgs& a : ma) {
+    slot = std::max(slot, a.stage_bytes);
+    kmax = std::max(kmax, a.k);
+    if ((int)a.grid > c->num_sms) return SHK_OK;
+  }
+  // one ring for every plan: the largest slot, then the largest chunk whose
+  // stage count keeps the parity waits unambiguous
+  DecodeProgram& P = k.P;
+  P = DecodeProgram{};
+  P.kmax = kmax;
+  P.slot_bytes = slot;
+  P.ns = 1;
+  P.chunk = 1;
+  size_t fixed = 0;
+  decode_smem(P, d.head_dim, G, &fixed);
+  const size_t budget = 227 * 1024;
+  if (fixed >= budget) return SHK_OK;
+  uint32_t chunk = MMV_MAX_CHUNK, ns = 0;
+  for (;; chunk >>= 1) {
+    if (chunk == 0) return SHK_OK;
+    ns = (uint32_t)std::min<size_t>(MMV_MAX_STAGES, (budget - fixed) / ((size_t)chunk * slot));
+    if (ns >= (MMV_WARPS + chunk - 1) / chunk + 2) break;
+  }
+  P.ns = ns;
+  P.chunk = chunk;
+  P.lg_chunk = (uint32_t)__builtin_ctz(chunk);
+  for (MmvArgs& a : ma) {
+    for (uint32_t i = 0; i < a.nseg; ++i)
+      if (a.seg[i].ks + ns * chunk + MMV_WARPS + 1 >= a.red_slots) return SHK_OK;
+    a.stage_bytes = slot;
+    a.n_stages = ns;
+    a.chunk = chunk;
+    a.lg_chunk = P.lg_chunk;
+  }
+  k.smem = decode_smem(P, d.head_dim, G);
+  k.grid = c->num_sms;
+  if (!decode_supported(d.head_dim, G, k.smem, k.grid)) return SHK_OK;
+  const uint32_t* pos = m->d_tok + 1;
   std::vector<AttnArgs> aa(L);
   for (uint32_t l = 0; l < L; ++l) aa[l] = layer_attn_args(m, l, pos);
   std::vector<DecodePhase> ph;
@@ -937,23 +1069,11 @@ int build_persist(shk_model* m) {
   }
   ph.push_back({PH_GEMV, 4 * L});
   ph.push_back({PH_ARGMAX, 0});
-  DecodeProgram& P = k.P;
-  P = DecodeProgram{};
-  P.stage_bytes = (stage + 127) & ~127u;
-  P.ns = 1;  // sized below
-  const size_t fixed = decode_smem(P, hd, G, kmax);  // header + x region + one stage
-  const size_t budget = 227 * 1024;
-  if (fixed > budget || budget - fixed < (size_t)P.stage_bytes) return SHK_OK;
-  P.ns = (uint32_t)std::min<size_t>(GEMV_MAX_STAGES, 1 + (budget - fixed) / P.stage_bytes);
-  if (P.ns < 2) return SHK_OK;
-  k.smem = decode_smem(P, hd, G, kmax);
-  k.grid = c->num_sms;
-  if (!decode_supported(hd, G, k.smem, k.grid)) return SHK_OK;
-  bool ok = cudaMalloc(&k.d_gemv, ga.size() * sizeof(GemvArgs)) == cudaSuccess;
+  bool ok = cudaMalloc(&k.d_mmv, ma.size() * sizeof(MmvArgs)) == cudaSuccess;
   ok = ok && cudaMalloc(&k.d_attn, aa.size() * sizeof(AttnArgs)) == cudaSuccess;
   ok = ok && cudaMalloc(&k.d_phases, ph.size() * sizeof(DecodePhase)) == cudaSuccess;
-  ok = ok && cudaMalloc(&k.d_bar, sizeof(GridBar)) == cudaSuccess;
-  ok = ok && cudaMemcpy(k.d_gemv, ga.data(), ga.size() * sizeof(GemvArgs), cudaMemcpyHostToDevice) == cudaSuccess;
+  ok = ok && cudaMalloc(&k.d_bar, sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMemcpy(k.d_mmv, ma.data(), ma.size() * sizeof(MmvArgs), cudaMemcpyHostToDevice) == cudaSuccess;
   ok = ok && cudaMemcpy(k.d_attn, aa.data(), aa.size() * sizeof(AttnArgs), cudaMemcpyHostToDevice) == cudaSuccess;
   ok = ok && cudaMemcpy(k.d_phases, ph.data(), ph.size() * sizeof(DecodePhase), cudaMemcpyHostToDevice) == cudaSuccess;
   if (!ok) {
@@ -961,7 +1081,7 @@ int build_persist(shk_model* m) {
     m->pk.state = -1;
     return SHK_ENOMEM;
   }
-  P.gemv = k.d_gemv;
+  P.mmv = k.d_mmv;
   P.attn = k.d_attn;
   P.phases = k.d_phases;
   k.n_phases_full = (uint32_t)ph.size();
@@ -1047,16 +1167,11 @@ shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv
   m->layers.resize(d->n_layers);
   m->have.assign(d->n_layers, 0);
   m->plans.resize(d->n_layers);
-  GemvMat hm{d->output_dev, nullptr, m->logits, d->n_vocab, d->output_dtype, 0, EPI_STORE, 0};
-  const int hp = gemv_plan(m->head, &hm, 1, d->n_embd, m->hidden, nullptr, nullptr, nullptr,
-                           c->d_err, c->num_sms);
   // GGUF-layout Q6_K (or rows the staged kernel cannot take): plain-load GEMV
-  if (d->n_embd % QK || !head_plan_ok(d->output_dtype, hp)) {
+  if (d->n_embd % QK || plan_head(m) != SHK_OK) {
     shk_cuda_model_destroy(m);
     return nullptr;
   }
-  m->head_ok = true;
-  m->head_generic = hp != 0;
   // RoPE frequencies with the host C library (engine/src/ops.c:223-227)
   std::vector<float> fr(d->head_dim / 2);
   rope_freq_table(d->rope_theta > 0.f ? d->rope_theta : 10000.0f, d->head_dim, fr.data());
@@ -1248,6 +1363,14 @@ int shk_cuda_tp_init(shk_ctx* c, int rank, int world, const void* id) {
   return SHK_OK;
 }
 
+int shk_cuda_tp_comm_size(shk_ctx* c) {
+  if (!c) return SHK_EINVAL;
+  if (!c->comm) return 1;
+  int n = 0;
+  if (nccl()->comm_count(c->comm, &n) != ncclSuccess) return SHK_ENCCL;
+  return n;
+}
+
 int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint32_t v_lo, uint32_t v_hi) {
   if (!m || o_lo >= o_hi || o_hi > m->d.n_embd || v_lo >= v_hi || v_hi > m->d.n_vocab) return SHK_EINVAL;
   for (uint32_t l = 0; l < m->d.n_layers; ++l)
@@ -1370,20 +1493,11 @@ int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void
     return SHK_EINVAL;
   if (m->p2p.on) return SHK_EUNSUPPORTED;  // parts wait on peers' partials
   cudaStream_t st = pick(m->ctx, s);
-  auto wbytes = [](const GemvPlan& p) {
-    uint64_t b = 0;
-    for (uint32_t i = 0; i < p.args.nseg; ++i) {
-      const GemvSeg& g = p.args.seg[i];
-      const uint64_t bb = g.qt == T_Q4K ? Q4K_BYTES : Q6K_BYTES;
-      b += (uint64_t)g.m * g.nb * bb * (g.dual ? 2 : 1);
-    }
-    return b;
-  };
   uint64_t bytes = 0;
   if (part == 5) {
     if (!m->head_ok || m->head_generic) return SHK_EINVAL;
-    CK(gemv_launch(m->head, st));
-    bytes = wbytes(m->head);
+    CK(proj_launch(m->head, st));
+    bytes = proj_weight_bytes(m->head);
   } else if (part == 1) {
     AttnArgs a{};
     a.kv = m->kv->L;
@@ -1403,9 +1517,9 @@ int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void
     CK(attn_decode_launch(a, st));
   } else {
     const LayerPlans& P = m->plans[layer];
-    const GemvPlan* p = part == 0 ? &P.qkv : part == 2 ? &P.o : part == 3 ? &P.gateup : &P.down;
-    CK(gemv_launch(*p, st));
-    bytes = wbytes(*p);
+    const ProjPlan* p = part == 0 ? &P.qkv : part == 2 ? &P.o : part == 3 ? &P.gateup : &P.down;
+    CK(proj_launch(*p, st));
+    bytes = proj_weight_bytes(*p);
   }
   if (bytes_out) *bytes_out = bytes;
   return SHK_OK;

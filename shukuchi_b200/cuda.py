@@ -87,9 +87,12 @@ _SIGS = {
     "shk_cuda_q6k_repack": (I, [P, P, U32, U32, U32, I, P]),
     "shk_cuda_layer_stage_q6k_planar": (I, [P, U32, P, U32, U32, U32]),
     "shk_cuda_matvec": (I, [P, U32, P, U32, P, P, U32, U32, P]),
+    "shk_cuda_tiled_bytes": (SZ, [U32, U32, U32]),
+    "shk_cuda_tile": (I, [P, U32, P, U32, U32, U32, P, P]),
     "shk_cuda_prefill_matmul": (I, [P, U32, P, U32, P, P, U32, U32, U32, P]),
     "shk_cuda_tp_unique_id": (I, [P, SZ]),
     "shk_cuda_tp_init": (I, [P, I, I, P]),
+    "shk_cuda_tp_comm_size": (I, [P]),
     "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),
     "shk_cuda_model_tp_p2p_export": (I, [P, P, SZ]),
     "shk_cuda_model_tp_p2p_import": (I, [P, P, P]),
@@ -199,6 +202,12 @@ class Context:
         """Q6_K rows in place between the GGUF and the planar layout."""
         _call("shk_cuda_q6k_repack", self.h, w_dev, rows, k, row_stride, 1 if to_planar else 0, stream)
 
+    def tile(self, dtype: int, src_dev: int, rows: int, k: int, dst_dev: int, src_row_stride: int = 0,
+             stream: int | None = None) -> None:
+        """GGUF rows (dtype 12 / 14) -> the row-tiled layout at dst_dev
+        (tiled_bytes(dtype, rows, k) bytes)."""
+        _call("shk_cuda_tile", self.h, dtype, src_dev, src_row_stride, rows, k, dst_dev, stream)
+
     def matvec(self, dtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int, row_stride: int = 0,
                stream: int | None = None) -> None:
         _call("shk_cuda_matvec", self.h, dtype, w_dev, row_stride, x_dev, y_dev, m, k, stream)
@@ -213,6 +222,10 @@ class Context:
         (one process or thread per GPU); uid comes from tp_unique_id() on rank 0."""
         buf = C.create_string_buffer(bytes(uid), len(uid))
         _call("shk_cuda_tp_init", self.h, rank, world, buf)
+
+    def tp_comm_size(self) -> int:
+        """Ranks in this context's NCCL communicator (1 without one)."""
+        return _call("shk_cuda_tp_comm_size", self.h)
 
     def matmul(self, qtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int,
                stream: int | None = None) -> None:
@@ -259,6 +272,13 @@ class Context:
 
 
 DTYPE_Q6_K_PLANAR = 0x10E
+DTYPE_Q4_K_TILED = 0x20C
+DTYPE_Q6_K_TILED = 0x20E
+
+
+def tiled_bytes(dtype: int, rows: int, k: int) -> int:
+    """Bytes of the row-tiled form of a rows x k matrix (0 if not tileable)."""
+    return int(lib().shk_cuda_tiled_bytes(dtype, rows, k))
 
 
 def tp_unique_id() -> bytes:

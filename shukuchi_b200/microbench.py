@@ -99,7 +99,17 @@ def gemv(args, ctx) -> None:
         if stride != row:
             raise SystemExit(f"rows of {qt},{m},{k} are not 16-byte multiples; use the C ABI row_stride")
         dt = qt
-        if qt == 14:  # the layout the decode path registers Q6_K weights in
+        if args.tiled:  # row-tiled copies for the tensor-core matvec
+            torch.cuda.synchronize()
+            tw = []
+            for t in ws:
+                d = torch.empty(sc.tiled_bytes(qt, m, k), dtype=torch.uint8, device="cuda")
+                ctx.tile(qt, t.data_ptr(), m, k, d.data_ptr(), stride)
+                tw.append(d)
+            ctx.sync()
+            ws = tw
+            dt = sc.DTYPE_Q4_K_TILED if qt == 12 else sc.DTYPE_Q6_K_TILED
+        elif qt == 14:  # the layout the decode path registers Q6_K weights in
             torch.cuda.synchronize()
             for t in ws:
                 ctx.q6k_repack(t.data_ptr(), m, k, stride, True)
@@ -124,6 +134,7 @@ def gemv(args, ctx) -> None:
         alg = m * row + 4 * k + 4 * m
         gbs = alg / (us * 1e-6) / 1e9
         print(json.dumps({"bench": "gemv", "qtype": "Q4_K" if qt == 12 else "Q6_K", "m": m, "k": k,
+                          "layout": "tiled" if args.tiled else ("planar" if qt == 14 else "gguf"),
                           "us": round(us, 3), "bytes": alg, "gbs": round(gbs, 1),
                           "frac": round(gbs / peak, 4), "peak_gbs": peak, "peak_kind": kind,
                           "copies": ncopy}), flush=True)
@@ -347,6 +358,7 @@ def main() -> None:
     g.add_argument("--shapes", nargs="*")
     g.add_argument("--launches", type=int, default=20)
     g.add_argument("--reps", type=int, default=5)
+    g.add_argument("--tiled", action="store_true", help="row-tiled weights on the tensor-core matvec")
     k = sub.add_parser("kv")
     pf = sub.add_parser("prefill")
     pf.add_argument("--shapes", nargs="*")

@@ -32,14 +32,23 @@ def _fill_blocks(buf: torch.Tensor, qtype: int, rows: int, cols: int, stride: in
         blocks[:, :, 208:210] = d.view(torch.uint8).view(rows, nb, 2)
 
 
-def _matrix(qtype, rows, cols, device, gen, keep, ctx=None):
-    """Returns (device pointer, row stride or 0, dtype to register).  Q6_K
-    matrices are generated in GGUF blocks and repacked in place to the planar
-    layout of the staged GEMV when a context is given."""
+def _matrix(qtype, rows, cols, device, gen, keep, ctx=None, tiled=False):
+    """Returns (device pointer, row stride or 0, dtype to register).  Matrices
+    are generated in GGUF blocks; with a context they are converted on the
+    device to the row-tiled layout of the tensor-core matvec (tiled) or, for
+    Q6_K, repacked in place to the planar layout of the staged GEMV."""
     rb = (cols // QK) * BLOCK_BYTES[qtype]
     stride = (rb + 15) // 16 * 16
     t = torch.zeros(rows * stride, dtype=torch.uint8, device=device)
     _fill_blocks(t, qtype, rows, cols, stride, gen)
+    if ctx is not None and tiled:
+        dst = torch.empty(sc.tiled_bytes(qtype, rows, cols), dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)
+        ctx.tile(qtype, t.data_ptr(), rows, cols, dst.data_ptr(), stride)
+        ctx.sync()
+        del t
+        keep.append(dst)
+        return dst.data_ptr(), 0, (sc.DTYPE_Q4_K_TILED if qtype == T_Q4K else sc.DTYPE_Q6_K_TILED)
     keep.append(t)
     dt = qtype
     if ctx is not None and qtype == T_Q6K:
@@ -48,6 +57,27 @@ def _matrix(qtype, rows, cols, device, gen, keep, ctx=None):
         ctx.sync()
         dt = sc.DTYPE_Q6_K_PLANAR
     return t.data_ptr(), (0 if stride == rb else stride), dt
+
+
+# Projections whose matrices go row-tiled (tensor-core matvec) by default: the
+# ones where it measured faster than the staged dp4a GEMV on the 8B decode
+# step (O: 8.2 vs 9.0 us, down: 19.0 vs 21.1 us per layer); QKV, gate/up and
+# the output head stay GGUF / planar rows.
+TILED_DEFAULT = frozenset({"o", "down"})
+PROJECTIONS = frozenset({"qkv", "o", "gateup", "down", "output"})
+
+
+def tiled_set(tiled) -> frozenset:
+    """True: every projection; False: none; else an iterable of names from
+    PROJECTIONS (QKV and gate/up are planned as one launch each, so their
+    matrices share a layout)."""
+    if tiled is True:
+        return PROJECTIONS
+    if tiled is False or tiled is None:
+        return frozenset()
+    t = frozenset(tiled)
+    assert t <= PROJECTIONS, t - PROJECTIONS
+    return t
 
 
 @dataclasses.dataclass
@@ -63,14 +93,18 @@ class DeviceWeights:
 
 def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
                       distinct_layers: int | None = None, o_rows: int | None = None,
-                      out_rows: int | None = None, ctx: sc.Context | None = None) -> DeviceWeights:
+                      out_rows: int | None = None, ctx: sc.Context | None = None,
+                      tiled=TILED_DEFAULT) -> DeviceWeights:
     """All weights in HBM.  distinct_layers < n_layers reuses layer buffers
     cyclically (only for smoke-sized runs; the benchmark uses distinct layers).
     o_rows / out_rows: rows of the O projection and of the output head when
     they differ from n_embd / n_vocab (a tensor-parallel rank's shard, whose
     `shape` is the local one of shukuchi_b200.tp.local_shape).  ctx: the
-    context whose stream repacks Q6_K matrices to the planar layout (required
-    for a model the library runs; without it the matrices stay GGUF blocks)."""
+    context whose stream converts the matrices (required for a model the
+    library runs; without it the matrices stay GGUF blocks).  tiled: which
+    projections are row-tiled for the tensor-core matvec (tiled_set); the
+    others keep GGUF rows (Q6_K planar) for the staged GEMV."""
+    ts = tiled_set(tiled)
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     keep: list = []
@@ -82,18 +116,18 @@ def make_device_model(shape: ModelShape, seed: int = 0, device="cuda:0",
         an = (1 + 0.02 * torch.randn(s.n_embd, device=device, generator=gen)).float()
         fn = (1 + 0.02 * torch.randn(s.n_embd, device=device, generator=gen)).float()
         keep += [an, fn]
-        q, _, tq = _matrix(s.t_q, s.n_heads * hd, s.n_embd, device, gen, keep, ctx)
-        k, _, tk = _matrix(s.t_k, s.n_kv_heads * hd, s.n_embd, device, gen, keep, ctx)
-        v, sv, tv = _matrix(s.t_v, s.n_kv_heads * hd, s.n_embd, device, gen, keep, ctx)
-        o, _, to = _matrix(s.t_o, o_rows or s.n_embd, s.n_heads * hd, device, gen, keep, ctx)
-        g, _, tg = _matrix(s.t_gate, s.n_ff, s.n_embd, device, gen, keep, ctx)
-        u, _, tu = _matrix(s.t_up, s.n_ff, s.n_embd, device, gen, keep, ctx)
-        dn, sd, td = _matrix(s.t_down, s.n_embd, s.n_ff, device, gen, keep, ctx)
+        q, _, tq = _matrix(s.t_q, s.n_heads * hd, s.n_embd, device, gen, keep, ctx, "qkv" in ts)
+        k, _, tk = _matrix(s.t_k, s.n_kv_heads * hd, s.n_embd, device, gen, keep, ctx, "qkv" in ts)
+        v, sv, tv = _matrix(s.t_v, s.n_kv_heads * hd, s.n_embd, device, gen, keep, ctx, "qkv" in ts)
+        o, _, to = _matrix(s.t_o, o_rows or s.n_embd, s.n_heads * hd, device, gen, keep, ctx, "o" in ts)
+        g, _, tg = _matrix(s.t_gate, s.n_ff, s.n_embd, device, gen, keep, ctx, "gateup" in ts)
+        u, _, tu = _matrix(s.t_up, s.n_ff, s.n_embd, device, gen, keep, ctx, "gateup" in ts)
+        dn, sd, td = _matrix(s.t_down, s.n_embd, s.n_ff, device, gen, keep, ctx, "down" in ts)
         made.append(sc.LayerDesc(an.data_ptr(), fn.data_ptr(), q, k, v, o, g, u, dn,
                                  tq, tk, tv, to, tg, tu, td, sv, sd))
     layers = [made[i % nd] for i in range(s.n_layers)]
     te, _, _ = _matrix(s.t_embd, s.n_vocab, s.n_embd, device, gen, keep)
-    out, so, tout = _matrix(s.t_out, out_rows or s.n_vocab, s.n_embd, device, gen, keep, ctx)
+    out, so, tout = _matrix(s.t_out, out_rows or s.n_vocab, s.n_embd, device, gen, keep, ctx, "output" in ts)
     assert so == 0, "output head rows must be 16-byte multiples"
     desc = sc.ModelDesc(s.n_layers, s.n_embd, s.n_heads, s.n_kv_heads, hd, s.n_ff, s.n_vocab, 0.0,
                         te, s.t_embd, out, tout)

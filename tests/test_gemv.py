@@ -63,6 +63,21 @@ def test_large_and_tiny_inputs(oracle, ctx, qt):
     check(oracle, ctx, qt, 128, 2048, seed=6, xscale=1e-6)
 
 
+@pytest.mark.parametrize("qt", [12, 14])
+def test_outlier_in_block(oracle, ctx, qt):
+    # x is fixed point relative to each 256-element block's maximum; a 1000x
+    # outlier in a block must keep the row inside the per-row bound
+    rng = np.random.default_rng(11)
+    m, k = 300, 4096
+    w = synth.quant_matrix(rng, qt, m, k)
+    x = rng.normal(0, 1, k).astype(np.float32)
+    for b in (0, 5, 15):
+        x[256 * b + 17] = 1000.0 * (1 if b % 2 else -1)
+    y = run_gemv(ctx, qt, w, x, m, k)
+    tol = gemv_tolerance(oracle, qt, w, x, m, k)
+    assert np.all(np.abs(y.astype(np.float64) - oracle.matvec(qt, w, x, m, k)) <= tol)
+
+
 def test_golden_vectors(oracle, ctx):
     for name, qt in (("gemv_q4k", 12), ("gemv_q6k", 14)):
         g = golden(name)

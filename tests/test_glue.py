@@ -49,6 +49,27 @@ def test_argmax_first_index(oracle, ctx, n):
     assert ctx.argmax(xd.data_ptr(), n) == oracle.argmax(x)
 
 
+@pytest.mark.parametrize("case", ["nan_first", "nan_block_start", "all_nan", "nan_then_max"])
+def test_argmax_nan_like_the_reference(oracle, ctx, case):
+    # engine/src/engine.c:424-431 keeps best = 0 while x[best] is NaN (nothing
+    # compares greater) and skips NaN elements once best is a number
+    n = 3 * 4096 + 77
+    x = np.random.default_rng(5).normal(0, 1, n).astype(np.float32)
+    if case == "nan_first":
+        x[0] = np.nan
+        x[5000] = 50.0
+    elif case == "nan_block_start":
+        x[4096] = np.nan
+        x[4097] = 40.0
+    elif case == "all_nan":
+        x[:] = np.nan
+    else:
+        x[100:200] = np.nan
+        x[8000] = 60.0
+    xd = to_dev(x)
+    assert ctx.argmax(xd.data_ptr(), n) == oracle.argmax(x)
+
+
 def test_rmsnorm(oracle, ctx):
     rng = np.random.default_rng(2)
     for d in (256, 2048, 4096, 8192):

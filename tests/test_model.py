@@ -125,6 +125,25 @@ def test_generate_matches_oracle(oracle, ctx, ctx_persist, ctx_nopdl, shape, n_p
     assert first == t_ref[0] and last == t_ref[-1]
 
 
+@pytest.mark.parametrize("layout", ["gguf", "default_mix"])
+def test_generate_layouts_match_oracle(oracle, ctx, layout):
+    """The staged dp4a GEMV on GGUF / planar rows, and the bench's mix
+    (row-tiled O and down projections, the rest GGUF), give the oracle's ids."""
+    from shukuchi_b200.synth_device import TILED_DEFAULT
+    model = synth.make_model("small", seed=21)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, model.shape.n_vocab, 5).astype(np.uint32)
+    t_ref, l_ref = oracle.generate(model, prompt, 10)
+    dec = GpuDecoder(ctx, model, max_seq=64, tiled=False if layout == "gguf" else TILED_DEFAULT)
+    try:
+        logits = np.zeros_like(l_ref)
+        toks = dec.generate(prompt, 10, logits_out=logits)
+    finally:
+        dec.close()
+    assert np.array_equal(toks, t_ref)
+    assert_logits(logits, l_ref)
+
+
 @pytest.mark.slow
 def test_tinyllama_shape_8_plus_16(oracle, ctx):
     """TinyLlama-1.1B shape (22 layers, d 2048, 32/4 heads, ffn 5632, vocab
@@ -142,3 +161,39 @@ def test_tinyllama_shape_8_plus_16(oracle, ctx):
         dec.close()
     assert np.array_equal(toks, t_ref)
     assert_logits(logits, l_ref)
+
+
+def step_report(toks, t_ref, logits, l_ref):
+    """Per decode step: ids equal, max|dlogit| / std(ref), and the reference's
+    top-2 logit margin (how close the greedy choice was) over std(ref)."""
+    rows = []
+    for t in range(l_ref.shape[0]):
+        sd = float(np.std(l_ref[t]))
+        top2 = np.sort(l_ref[t])[-2:]
+        rows.append({"step": t, "id_ref": int(t_ref[t]), "id_gpu": int(toks[t]),
+                     "dlogit_over_std": float(np.max(np.abs(logits[t] - l_ref[t]))) / sd,
+                     "top2_margin_over_std": float(top2[1] - top2[0]) / sd})
+    return rows
+
+
+@pytest.mark.slow
+def test_llama8b_shape_8_plus_16(oracle, ctx):
+    """The bench's Llama-3.1-8B shape (32 layers, d 4096, 32/8 heads, ffn
+    14336, vocab 128256, Q4_K_M mix with Q6_K attn_v / ffn_down / output):
+    8 random prompt ids, 16 greedy tokens against the oracle
+    (engine/src/engine.c:306-501 token loop).  On failure the message lists,
+    per step, the ids, max|dlogit|/std and the reference's top-2 margin."""
+    model = synth.make_model("llama8b", seed=0)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, model.shape.n_vocab, 8).astype(np.uint32)
+    t_ref, l_ref = oracle.generate(model, prompt, 16)
+    dec = GpuDecoder(ctx, model, max_seq=64)
+    try:
+        logits = np.zeros_like(l_ref)
+        toks = dec.generate(prompt, 16, logits_out=logits)
+    finally:
+        dec.close()
+    rep = step_report(toks, t_ref, logits, l_ref)
+    print("llama8b 8+16:", rep)
+    assert np.array_equal(toks, t_ref), rep
+    assert all(r["dlogit_over_std"] <= 1e-2 for r in rep), rep

@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--p2p-allreduce", action="store_true",
                     help="tensor parallel: the peer-memory exchange inside the GEMVs instead of NCCL all-reduce")
+    ap.add_argument("--tp-allreduce", default="ll", choices=["ll", "nccl"],
+                    help="tensor parallel: one-shot all-reduce kernel over NVLink peer memory with the flags in "
+                         "the data words (ll, default) or NCCL's all-reduce")
     return ap.parse_args()
 
 
@@ -215,7 +218,7 @@ def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
 PARITY_SHAPE = ("tp-hd128", 2, 1024, 8, 4, 2048, 1024)  # 2 layers, d 1024, 8/4 heads x 128, ffn 2048
 
 
-def parity_check(ctx, ws, rank, local):
+def parity_check(ctx, ws, rank, local, allreduce="ll"):
     """The decode path of this run (same context, same rank layout) on a small
     synthetic model against the oracle: 5 prompt ids + 8 greedy tokens,
     greedy ids and max|dlogit| / std(logits).  Rank 0 runs the oracle; every
@@ -234,7 +237,18 @@ def parity_check(ctx, ws, rank, local):
         tp_rows = (lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi)
     else:
         mr, tp_rows = model, None
-    dec = GpuDecoder(ctx, mr, len(prompt) + n_dec + 1, device=f"cuda:{local}", tp_rows=tp_rows)
+    from shukuchi_b200.synth_device import TILED_DEFAULT
+    gather = None
+    if ws > 1 and allreduce == "ll":
+        import torch.distributed as dist
+
+        def gather(h):
+            hs = [None] * ws
+            dist.all_gather_object(hs, h)
+            return hs
+    # the layouts and the all-reduce the timed run uses
+    dec = GpuDecoder(ctx, mr, len(prompt) + n_dec + 1, device=f"cuda:{local}", tp_rows=tp_rows,
+                     tiled=TILED_DEFAULT, ll_exchange=gather)
     try:
         logits = np.zeros((n_dec, shape.n_vocab), np.float32)
         ids = dec.generate(prompt, n_dec, logits)
@@ -254,7 +268,8 @@ def parity_check(ctx, ws, rank, local):
     return {"model": f"{shape.name} (2 layers, d 1024, 8/4 heads x 128, ffn 2048, vocab 1024), "
                      f"5 prompt + {n_dec} greedy ids vs the oracle",
             "ids_match": all(list(r) == t_ref.tolist() for r in all_ids),
-            "ranks": ws, "max_dlogit_over_std": dl, "tolerance": 1e-2}
+            "ranks": ws, "allreduce": allreduce if ws > 1 else None, "max_dlogit_over_std": dl,
+            "tolerance": 1e-2}
 
 
 def workload_config(args, ws):
@@ -306,7 +321,7 @@ def run_ours(args, ws, rank, local):
         dist.broadcast_object_list(obj, src=0)
         ctx.tp_init(rank, ws, obj[0])
     # correctness of this exact path before it is timed (small model, oracle on rank 0)
-    parity = parity_check(ctx, ws, rank, local) if not args.p2p_allreduce else None
+    parity = parity_check(ctx, ws, rank, local, args.tp_allreduce) if not args.p2p_allreduce else None
     wts = make_device_model(lshape, seed=1234 + rank, device=f"cuda:{local}",
                             o_rows=lay.o_hi - lay.o_lo, out_rows=lay.v_hi - lay.v_lo, ctx=ctx,
                             tiled=(synth_device.TILED_DEFAULT if not args.p2p_allreduce else False))
@@ -319,6 +334,10 @@ def run_ours(args, ws, rank, local):
             hs = [None] * ws
             dist.all_gather_object(hs, m.tp_p2p_export())
             m.tp_p2p_import(hs, [(L.o_lo, L.o_hi) for L in (tpl.layout(shape, r, ws) for r in range(ws))])
+        elif args.tp_allreduce == "ll":  # one-shot all-reduce kernel, flags in the data words
+            hs = [None] * ws
+            dist.all_gather_object(hs, m.tp_ll_export())
+            m.tp_ll_import(hs)
     for i, lv in enumerate(wts.layers):
         m.set_layer(i, lv)
     stream = torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{local}")

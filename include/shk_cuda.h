@@ -349,6 +349,19 @@ int shk_cuda_model_set_tp_rows(shk_model *m, uint32_t o_lo, uint32_t o_hi, uint3
 int shk_cuda_model_tp_p2p_export(shk_model *m, void *handle_out, size_t cap);
 int shk_cuda_model_tp_p2p_import(shk_model *m, const void *handles, const uint32_t *o_ranges);
 
+/* Tensor-parallel all-reduce over NVLink peer memory with the flags in the
+ * data words, replacing the NCCL all-reduce after O and down: every rank
+ * stores its partial row as 8-byte {value, step} words into every rank's
+ * exchange buffer, then sums the ranks' rows from its own buffer in rank
+ * order once each word carries the current step (bounded waits).  One small
+ * kernel per all-reduce, inside the captured decode step.  Setup, after
+ * shk_cuda_model_set_tp_rows and before the first token step: every rank
+ * exports its buffer's IPC handle (64 bytes), the caller gathers them in rank
+ * order and every rank imports the set.  One process per GPU of one node.  No
+ * counterpart in the reference (which has no tensor parallelism). */
+int shk_cuda_model_tp_ll_export(shk_model *m, void *handle_out, size_t cap);
+int shk_cuda_model_tp_ll_import(shk_model *m, const void *handles);
+
 /* ---- argmax without any device allocation.  No counterpart in the reference:
  *      it exists for callers that cannot call cudaMalloc (a sampler inside a
  *      host runtime that has already reserved the device's memory in its own

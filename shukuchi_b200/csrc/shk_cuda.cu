@@ -19,6 +19,7 @@
 #include "gemv.cuh"
 #include "glue.cuh"
 #include "mmv.cuh"
+#include "tp_ll.cuh"
 
 using // Fewest cached positions per attention split (CTA of a KV head's cluster).
 #ifndef SHK_ATT_MIN_SPLIT
@@ -219,6 +220,18 @@ struct shk_model {
     float* res2 = nullptr;
     uint32_t cov_lo[GEMV_TP_MAX] = {}, cov_hi[GEMV_TP_MAX] = {};
   } p2p;
+  // Tensor-parallel all-reduce over NVLink peer memory with flags in the data
+  // words (shk_cuda_model_tp_ll_*): one exchange buffer per rank,
+  // [slot: 2 per layer][rank][n_embd] 8-byte words; replaces the NCCL
+  // all-reduce after O and down.
+  struct Ll {
+    bool on = false;
+    void* base = nullptr;          // this rank's buffer
+    size_t bytes = 0;
+    void* peer[LL_MAX_RANKS] = {};  // every rank's buffer (own included)
+    bool opened[LL_MAX_RANKS] = {};
+    uint32_t* d_step = nullptr;    // epoch, advanced by the embedding kernel
+  } ll;
   uint32_t* tp_pairs = nullptr; // world x {max value bits, index}: argmax over the vocabulary slices
   uint64_t* d_trace = nullptr;  // persistent-kernel timeline (shk_cuda_model_trace_enable)
   uint32_t trace_phases = 0;
@@ -845,6 +858,17 @@ AttnArgs layer_attn_args(shk_model* m, uint32_t layer, const uint32_t* pos) {
 // collective or a memset never is (the dependency edge is only defined
 // between kernels), and the caller's launch after this layer inherits
 // pdl_enabled() as left here.
+LlArgs ll_args(const shk_model* m) {
+  LlArgs a{};
+  for (int p = 0; p < m->ctx->tp_world && p < LL_MAX_RANKS; ++p) a.peer[p] = static_cast<uint64_t*>(m->ll.peer[p]);
+  a.epoch = m->ll.d_step;
+  a.err = m->ctx->d_err;
+  a.rank = (uint32_t)m->ctx->tp_rank;
+  a.world = (uint32_t)m->ctx->tp_world;
+  a.d = m->d.n_embd;
+  return a;
+}
+
 int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint32_t* pos,
                   cudaStream_t st, bool pdl) {
   shk_ctx* c = m->ctx;
@@ -853,8 +877,9 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
   pdl_enabled() = pdl;
   const AttnArgs a = layer_attn_args(m, layer, pos);
   CK(attn_decode_launch(a, st));
-  const bool nccl_ar = tp && !m->p2p.on;
-  if (nccl_ar && c->tp_rank != 0 && m->o_hi - m->o_lo < m->d.n_embd) {  // rows this rank does not write
+  const bool ll = tp && m->ll.on;  // all-reduce over peer memory, flags in the data words
+  const bool nccl_ar = tp && !m->p2p.on && !ll;
+  if ((nccl_ar || ll) && c->tp_rank != 0 && m->o_hi - m->o_lo < m->d.n_embd) {  // rows this rank does not write
     CK(cudaMemsetAsync(m->hidden, 0, (size_t)m->d.n_embd * sizeof(float), st));
     pdl_enabled() = false;
   }
@@ -863,7 +888,11 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
     if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
       return SHK_ENCCL;
     pdl_enabled() = false;
+  } else if (ll) {
+    pdl_enabled() = pdl;
+    CK(ar_ll_launch(ll_args(m), m->hidden, 2 * layer, st));
   }
+  pdl_enabled() = nccl_ar ? false : pdl;
   CK(proj_launch(P.gateup, st));
   pdl_enabled() = pdl;
   CK(proj_launch(P.down, st));
@@ -871,6 +900,8 @@ int enqueue_layer(shk_model* m, const LayerPlans& P, uint32_t layer, const uint3
     if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
       return SHK_ENCCL;
     pdl_enabled() = false;
+  } else if (ll) {
+    CK(ar_ll_launch(ll_args(m), m->hidden, 2 * layer + 1, st));
   }
   return SHK_OK;
 }
@@ -962,7 +993,8 @@ int enqueue_head(shk_model* m, cudaStream_t st, bool advance_pos, bool pdl_after
 
 int enqueue_layers(shk_model* m, cudaStream_t st, bool pdl_after_first = false) {
   CK(embed_launch(m->d.tok_embd_dev, m->d.tok_embd_dtype, m->d_tok, m->d.n_vocab, m->hidden,
-                  m->d.n_embd, m->ctx->d_err, st, m->p2p.on ? m->p2p.d_step : nullptr));
+                  m->d.n_embd, m->ctx->d_err, st,
+                  m->p2p.on ? m->p2p.d_step : m->ll.on ? m->ll.d_step : nullptr));
   if (pdl_after_first) pdl_enabled() = true;
   for (uint32_t l = 0; l < m->d.n_layers; ++l) {
     const int rc = enqueue_layer(m, m->plans[l], l, m->d_tok + 1, st, pdl_after_first);
@@ -1200,6 +1232,10 @@ void shk_cuda_model_destroy(shk_model* m) {
   cudaFree(m->p2p.base);
   cudaFree(m->p2p.counters);
   cudaFree(m->p2p.d_step);
+  for (int p = 0; p < LL_MAX_RANKS; ++p)
+    if (m->ll.opened[p]) cudaIpcCloseMemHandle(m->ll.peer[p]);
+  cudaFree(m->ll.base);
+  cudaFree(m->ll.d_step);
   cudaFree(m->p2p.res2);
   cudaFree(m->am_v);
   cudaFree(m->am_i);
@@ -1229,7 +1265,7 @@ int shk_cuda_forward_layer(shk_model* m, const shk_layer_desc* lv, uint32_t laye
                            float* hidden, void* s) {
   if (!m || !lv || !hidden || layer >= m->d.n_layers || pos >= m->kv->L.max_seq) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
-  if (m->p2p.on) return SHK_EUNSUPPORTED;  // the exchange runs inside whole-token steps
+  if (m->p2p.on || m->ll.on) return SHK_EUNSUPPORTED;  // the exchanges run inside whole-token steps
   LayerPlans P;
   int rc = build_layer_plans(m, *lv, P, layer);
   if (rc) return rc;
@@ -1420,6 +1456,46 @@ int shk_cuda_model_tp_p2p_export(shk_model* m, void* handle_out, size_t cap) {
   CK(cudaIpcGetMemHandle(&h, q.base));
   memcpy(handle_out, &h, sizeof(h));
   return (int)sizeof(h);
+}
+
+int shk_cuda_model_tp_ll_export(shk_model* m, void* handle_out, size_t cap) {
+  if (!m || !handle_out || cap < sizeof(cudaIpcMemHandle_t)) return SHK_EINVAL;
+  shk_ctx* c = m->ctx;
+  if (c->tp_world < 2 || c->tp_world > LL_MAX_RANKS || m->p2p.on) return SHK_EINVAL;
+  auto& q = m->ll;
+  cudaSetDevice(c->device);
+  if (!q.base) {
+    q.bytes = ll_buffer_bytes(2 * m->d.n_layers, (uint32_t)c->tp_world, m->d.n_embd);
+    if (cudaMalloc(&q.base, q.bytes) != cudaSuccess || cudaMalloc(&q.d_step, 4) != cudaSuccess) return SHK_ENOMEM;
+    CK(cudaMemset(q.base, 0, q.bytes));
+    CK(cudaMemset(q.d_step, 0, 4));
+  }
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, q.base));
+  memcpy(handle_out, &h, sizeof(h));
+  return (int)sizeof(h);
+}
+
+int shk_cuda_model_tp_ll_import(shk_model* m, const void* handles) {
+  if (!m || !handles) return SHK_EINVAL;
+  shk_ctx* c = m->ctx;
+  auto& q = m->ll;
+  if (!q.base || q.on || m->g_layers || m->g_head || m->g_loop) return SHK_EINVAL;
+  cudaSetDevice(c->device);
+  for (int p = 0; p < c->tp_world; ++p) {
+    if (p == c->tp_rank) {
+      q.peer[p] = q.base;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)p * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return SHK_ECUDA;
+    q.peer[p] = ptr;
+    q.opened[p] = true;
+  }
+  q.on = true;
+  return SHK_OK;
 }
 
 int shk_cuda_model_tp_p2p_import(shk_model* m, const void* handles, const uint32_t* o_ranges) {

@@ -96,6 +96,8 @@ _SIGS = {
     "shk_cuda_model_set_tp_rows": (I, [P, U32, U32, U32, U32]),
     "shk_cuda_model_tp_p2p_export": (I, [P, P, SZ]),
     "shk_cuda_model_tp_p2p_import": (I, [P, P, P]),
+    "shk_cuda_model_tp_ll_export": (I, [P, P, SZ]),
+    "shk_cuda_model_tp_ll_import": (I, [P, P]),
     "shk_cuda_kv_create": (P, [P, C.POINTER(KvConfig)]),
     "shk_cuda_kv_destroy": (None, [P]),
     "shk_cuda_kv_append": (I, [P, U32, U32, P, P, P]),
@@ -358,6 +360,18 @@ class DeviceModel:
         hb = C.create_string_buffer(b"".join(handles), 64 * len(handles))
         rg = (C.c_uint32 * (2 * len(o_ranges)))(*[v for r in o_ranges for v in r])
         _call("shk_cuda_model_tp_p2p_import", self.h, hb, rg)
+
+    def tp_ll_export(self) -> bytes:
+        """IPC handle of this rank's exchange buffer (all-reduce with flags in
+        the data words)."""
+        buf = C.create_string_buffer(64)
+        n = check("shk_cuda_model_tp_ll_export", lib().shk_cuda_model_tp_ll_export(self.h, buf, 64))
+        return buf.raw[:n]
+
+    def tp_ll_import(self, handles: list):
+        """handles: every rank's export in rank order."""
+        hb = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        _call("shk_cuda_model_tp_ll_import", self.h, hb)
 
     def forward_layer(self, lv: LayerDesc, layer, pos, hidden_dev, stream=None):
         _call("shk_cuda_forward_layer", self.h, C.byref(lv), layer, pos, hidden_dev, stream)

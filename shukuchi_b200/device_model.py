@@ -125,12 +125,14 @@ class GpuDecoder:
     """A DeviceModel + KV cache for a synthetic model, ready for token steps."""
 
     def __init__(self, ctx: sc.Context, model: Model, max_seq: int, device="cuda:0", tp_rows=None,
-                 p2p_exchange=None, o_ranges=None, tiled=True):
+                 p2p_exchange=None, o_ranges=None, tiled=True, ll_exchange=None):
         """tp_rows: (o_lo, o_hi, v_lo, v_hi) of a tensor-parallel rank whose
         context has joined its group (the model is that rank's shard).
         p2p_exchange: for the all-reduce over peer memory, a function taking
         this rank's handle and returning every rank's in rank order (an
-        all-gather); o_ranges: every rank's (o_lo, o_hi)."""
+        all-gather); o_ranges: every rank's (o_lo, o_hi).  ll_exchange: the
+        same all-gather for the all-reduce with flags in the data words
+        (shk_cuda_model_tp_ll_*), which replaces NCCL's."""
         s = model.shape
         out_rows = tp_rows[3] - tp_rows[2] if tp_rows is not None else None
         # the peer-memory exchange runs in the staged GEMV's epilogue (GGUF / planar rows)
@@ -141,6 +143,8 @@ class GpuDecoder:
             self.m.set_tp_rows(*tp_rows)
         if p2p_exchange is not None:
             self.m.tp_p2p_import(p2p_exchange(self.m.tp_p2p_export()), o_ranges)
+        if ll_exchange is not None:
+            self.m.tp_ll_import(ll_exchange(self.m.tp_ll_export()))
         for i, lv in enumerate(self.up.layers):
             self.m.set_layer(i, lv)
 

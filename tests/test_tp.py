@@ -220,7 +220,7 @@ def test_tp_ranks_match_oracle_cpu(oracle, tmp_path, name, world):
 
 
 # --------------------------------------------------------------- GPU ranks
-def _gpu_rank(rank, world, port, name, seed, prompt, n_dec, out_dir, p2p=False):
+def _gpu_rank(rank, world, port, name, seed, prompt, n_dec, out_dir, mode="nccl"):
     import datetime
 
     import torch
@@ -239,15 +239,15 @@ def _gpu_rank(rank, world, port, name, seed, prompt, n_dec, out_dir, p2p=False):
         ctx.tp_init(rank, world, obj[0])
         model = synth.make_model(_shape(name), seed=seed)
         mr, lay = tp.shard_model(model, rank, world)
-        ex = None
-        if p2p:
-            def ex(h):
-                hs = [None] * world
-                dist.all_gather_object(hs, h)
-                return hs
+        def gather(h):
+            hs = [None] * world
+            dist.all_gather_object(hs, h)
+            return hs
         o_ranges = [(L.o_lo, L.o_hi) for L in (tp.layout(model.shape, r, world) for r in range(world))]
         dec = GpuDecoder(ctx, mr, len(prompt) + n_dec + 1, device=f"cuda:{rank}",
-                         tp_rows=(lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi), p2p_exchange=ex, o_ranges=o_ranges)
+                         tp_rows=(lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi),
+                         p2p_exchange=gather if mode == "p2p" else None, o_ranges=o_ranges,
+                         ll_exchange=gather if mode == "ll" else None)
         try:
             logits = np.zeros((n_dec, model.shape.n_vocab), np.float32)
             ids = dec.generate(prompt, n_dec, logits)
@@ -264,17 +264,19 @@ def _gpu_rank(rank, world, port, name, seed, prompt, n_dec, out_dir, p2p=False):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "p2p"])
+@pytest.mark.parametrize("mode", ["nccl", "p2p", "ll"])
 @pytest.mark.parametrize("name,world", [("small", 2), ("tp-hd128", 2), ("tp-hd128", 4)])
-def test_tp_ranks_match_oracle_gpu(oracle, tmp_path, name, world, p2p):
+def test_tp_ranks_match_oracle_gpu(oracle, tmp_path, name, world, mode):
     """nccl: all-reduce kernels between the GEMVs; p2p: partials pushed into
-    peer memory by the O / down GEMVs and summed by the next GEMV."""
+    peer memory by the O / down GEMVs and summed by the next GEMV; ll: a
+    one-shot all-reduce kernel over peer memory with the flags in the data
+    words."""
     import torch
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     prompt = np.random.default_rng(7).integers(0, _shape(name).n_vocab, 5).astype(np.uint32)
     n_dec = 8
-    codes = _run_ranks(_gpu_rank, world, (name, 21, prompt, n_dec, str(tmp_path), p2p), 300)
+    codes = _run_ranks(_gpu_rank, world, (name, 21, prompt, n_dec, str(tmp_path), mode), 300)
     assert codes == [0] * world
     _check(oracle, name, 21, prompt, n_dec, world, str(tmp_path))
     for r in range(world):

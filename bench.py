@@ -39,7 +39,6 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s bs1, 8B-shape Q4_K_M; Q4_K/Q6_K GEMV HBM GB/s vs peak"
 PROMPT = 512
-GATEUP_PART = 3
 PART_NAMES = ("rmsnorm_qkv_rope", "append_attention", "o_proj_residual", "rmsnorm_gateup_swiglu",
               "down_residual", "lm_head")
 
@@ -76,18 +75,29 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def ncu_traffic(name: str):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
-    p = os.path.join(ROOT, "profiles", name)
+def recorded_traffic(shape: str, part: str):
+    """DRAM bytes (read + write) per launch of a decode part, as one ncu
+    capture of the current kernels measured them (profiles/dram_traffic.json:
+    per workload and part, the bytes and the capture command), or None."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
     if not os.path.exists(p):
         return None
-    for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+    rec = json.load(open(p)).get(shape, {}).get(part)
+    if not rec:
+        return None
+    return {"bytes": rec["dram_bytes_per_launch"], "source": rec["capture"]}
+
+
+def part_kernel(part: str) -> str:
+    """The kernel that runs a decode part in the bench's weight layouts."""
+    from shukuchi_b200.synth_device import TILED_DEFAULT
+    proj = {"rmsnorm_qkv_rope": "qkv", "o_proj_residual": "o", "rmsnorm_gateup_swiglu": "gateup",
+            "down_residual": "down", "lm_head": "output"}.get(part)
+    if proj is None:
+        return "attn_cluster_kernel"
+    if proj in TILED_DEFAULT:
+        return f"mmv_kernel (tensor-core matvec, row-tiled) {part}"
+    return f"gemv_kernel (dp4a, GGUF / planar rows) {part}"
 
 
 class ClockSampler:
@@ -212,7 +222,12 @@ def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
     per_token = 16.0 * sum(times) / len(times)
     sample = (f"{steps} steps of 2/32 layers of {s.name} at positions {prompt}+ plus 1/16 of the "
               f"output-head rows; token time = 16 x step time")
-    return 1.0 / per_token, kind, sample
+    return 1.0 / per_token, kind, sample, [1.0 / (16.0 * t) for t in times]
+
+
+def host_info() -> dict:
+    """Cores and load of the host the CPU baseline ran on."""
+    return {"host_nproc": os.cpu_count(), "host_loadavg_1m": round(os.getloadavg()[0], 2)}
 
 
 PARITY_SHAPE = ("tp-hd128", 2, 1024, 8, 4, 2048, 1024)  # 2 layers, d 1024, 8/4 heads x 128, ffn 2048
@@ -284,14 +299,16 @@ def workload_config(args, ws):
 def run_reference(args, ws, rank):
     if rank != 0:
         return
-    v, kind, sample = cpu_sample(args.steps, args.warmup, args.shape, args.prompt)
+    v, kind, sample, per_step = cpu_sample(args.steps, args.warmup, args.shape, args.prompt)
+    spread = {"min": min(per_step), "max": max(per_step), "steps": len(per_step)}
     line = {
         "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, 1),
         "impl": "reference",
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample,
+                         "per_step_tok_s": spread, **host_info()},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -398,43 +415,47 @@ def run_ours(args, ws, rank, local):
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     e2e = args.steps / (float(e_ms.item()) / 1000.0)
 
-    # dominant kernel: gate/up Q4_K GEMV (dual matrix, SwiGLU epilogue), timed
-    # per launch with events on the launching stream, rotating layers so no
-    # launch finds its weights in L2.  (Tensor parallel with the peer-memory
-    # exchange: the parts wait on the peers, so they are not launched alone.)
+    # Per-part device time of one token: each part launched alone over all
+    # layers (the second of two passes timed), CUDA events on the launching
+    # stream; the weights of 32 layers exceed L2, so no launch finds its
+    # weights there.  Bytes per launch: weights + x + y for a projection, the
+    # Q8_0 K/V of one layer's KV heads at the current context for attention.
+    # The roofline reports the part that takes the most time per token.
+    # (Tensor parallel with the peer-memory exchange inside the GEMVs: the
+    # parts wait on the peers, so they are not launched alone.)
     solo_parts = ws == 1 or not args.p2p_allreduce
-    durs = []
-    wbytes = 0
-    for i in range(max(args.steps, 32) if solo_parts else 0):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        wbytes = m.launch_part(i % shape.n_layers, GATEUP_PART)
-        b.record(stream)
-        durs.append((a, b))
-    torch.cuda.synchronize()
-    ctx.check()
-    avg = sum(a.elapsed_time(b) for a, b in durs[4:]) / len(durs[4:]) / 1000.0 if durs else None
-    # per-part device time of one token (each part launched alone, all layers;
-    # these serialise launches that the captured step overlaps, so they sum
-    # to a little more than ms_per_step)
-    parts = {}
+    peak, peak_kind = peaks()
+    hd = shape.head_dim
+    qd, kvd = lshape.n_heads * hd, lshape.n_kv_heads * hd
+    io = {0: (shape.n_embd, qd + 2 * kvd), 2: (qd, lay.o_hi - lay.o_lo), 3: (shape.n_embd, 2 * lshape.n_ff),
+          4: (lshape.n_ff, shape.n_embd), 5: (shape.n_embd, lay.v_hi - lay.v_lo)}
+    parts, part_rl = {}, {}
     for part, name in enumerate(PART_NAMES if solo_parts else ()):
         evs = []
         n = 1 if part == 5 else shape.n_layers
+        wb = 0
         for rep in range(2):
             for layer in range(n):
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                m.launch_part(layer, part)
+                wb = m.launch_part(layer, part)
                 b.record(stream)
                 if rep == 1:
                     evs.append((a, b))
         torch.cuda.synchronize()
-        parts[name] = round(sum(a.elapsed_time(b) for a, b in evs) * 1000.0, 1)
+        us = sum(a.elapsed_time(b) for a, b in evs) * 1000.0
+        parts[name] = round(us, 1)
+        if part == 1:
+            nb = synth.kv_bytes_per_pos(lshape) // lshape.n_layers * (pos + 1)
+        else:
+            k_in, m_out = io[part]
+            nb = wb + 4 * k_in + 4 * m_out
+        gbs = nb / (us / n * 1e-6) / 1e9
+        part_rl[name] = {"us_per_launch": round(us / n, 3), "bytes_per_launch": nb, "gbs": round(gbs, 1),
+                         "frac": round(gbs / peak, 4)}
     ctx.check()
-    alg = wbytes + 4 * (shape.n_embd + lshape.n_ff)
-    peak, peak_kind = peaks()
-    achieved = alg / avg / 1e9 if avg else None
+    dom = max((nm for nm in part_rl if nm != "append_attention"), key=lambda nm: parts[nm], default=None)
+    traffic = recorded_traffic(args.shape, dom) if dom and ws == 1 else None
     # whole-step bytes at the mean context of the timed region, summed over
     # ranks (tensor parallel duplicates a few rows), against ws x the peak
     mean_ctx = args.prompt + args.warmup + args.steps / 2
@@ -449,8 +470,14 @@ def run_ours(args, ws, rank, local):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        v, kind, sample = cpu_sample(12, 1, args.shape, args.prompt)
-        cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample}
+        # three repeats of a 4-step sample: the median is the value, the
+        # spread shows host noise (one compute thread, as the reference uses)
+        reps = []
+        for _ in range(3):
+            v, kind, sample, _ = cpu_sample(4, 1, args.shape, args.prompt)
+            reps.append(v)
+        cpu = {"value": statistics.median(reps), "unit": "tok/s", "cores": 1, "kind": kind,
+               "sample": sample + "; median of 3 repeats", "repeats": reps, **host_info()}
 
     launches_per_step = 1 + 5 * shape.n_layers + 2 + (1 if lay.v_hi - lay.v_lo < shape.n_vocab else 0)
     line = {
@@ -461,14 +488,17 @@ def run_ours(args, ws, rank, local):
         "clocks": clk.summary(),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": ({"bound": "hbm", "kernel": "gemv_kernel<Q4_K> gate/up (dual) + SwiGLU",
-                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                      "peak_kind": peak_kind, "bytes_per_launch": alg,
-                      "traffic": ncu_traffic("gemv_gateup_llama8b.md") if ws == 1 else None}
-                     if achieved else
+        "roofline": ({"bound": "hbm", "kernel": part_kernel(dom), "part": dom,
+                      "achieved": part_rl[dom]["gbs"], "peak": peak, "unit": "GB/s", "frac": part_rl[dom]["frac"],
+                      "peak_kind": peak_kind, "bytes_per_launch": part_rl[dom]["bytes_per_launch"],
+                      "us_per_launch": part_rl[dom]["us_per_launch"],
+                      "traffic": traffic["bytes"] if traffic else None,
+                      "traffic_source": traffic["source"] if traffic else None}
+                     if dom else
                      {"bound": "hbm", "kernel": "whole decode step (tensor parallel, summed over ranks)",
                       "achieved": step_gbs, "peak": ws * peak, "unit": "GB/s", "frac": step_gbs / (ws * peak),
                       "peak_kind": peak_kind, "bytes_per_launch": step_bytes, "traffic": None}),
+        "parts_roofline": part_rl,
         "token_parts_us": parts,
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs,
                           "frac": step_gbs / (ws * peak)},

@@ -95,7 +95,8 @@ def build_oracle() -> None:
     reference sources are present on this machine."""
     od = os.path.join(ROOT, "oracle")
     _run(["make", "-s", "-C", od, "liboracle.so"])
-    if os.path.isdir("/root/reference/engine/src"):
+    # the Makefile knows where the reference sources are (and whether they are)
+    if subprocess.run(["make", "-s", "-C", od, "ref-present"], capture_output=True).returncode == 0:
         _run(["make", "-s", "-C", od, "ref"])
 
 

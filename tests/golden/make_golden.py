@@ -1,7 +1,7 @@
 """Generates tests/golden/*.npz from the REFERENCE implementation itself.
 
 The reference's C sources are compiled unmodified into oracle/_ref/libshkref.so
-(``make -C oracle ref``, which reads them from /root/reference).  This script
+(``make -C oracle ref``, which reads them where oracle/Makefile's REF points).  This script
 feeds seeded inputs through the reference entry points (op_matmul_q4_k,
 op_matmul_q6_k, op_rmsnorm, op_rope, q8_quantize_vec, op_attention, op_embed,
 forward_layer_view) and stores inputs and outputs.  The committed fixtures

@@ -91,6 +91,60 @@ def test_append_bit_exact(oracle, ctx, KV, hd):
         kv.close()
 
 
+@pytest.mark.parametrize("path", ["append", "append_range", "fused"])
+def test_append_non_finite_like_the_reference(oracle, reference_q8, ctx, path):
+    """NaN and +-inf inputs: the reference's maximum skips NaN (a > max_abs is
+    false), an infinite maximum makes the scale inf, and (int)lrintf of NaN (NaN
+    / scale, inf / inf) is 0 with the x86-64 C library (lrintf returns LONG_MIN,
+    whose low 32 bits are 0); the GPU's round-to-nearest conversion gives 0 for
+    NaN too.  Every appended block, scale and quants, must match byte for byte."""
+    KV, hd, T = 2, 64, 6
+    rng = np.random.default_rng(3)
+    k = rng.normal(0, 1, (T, KV * hd)).astype(np.float32)
+    v = rng.normal(0, 1, (T, KV * hd)).astype(np.float32)
+    k[0, 3] = np.nan              # NaN among finite values
+    k[1, 40] = np.inf             # +inf: scale inf, finite values quantise to 0
+    v[2, 70] = -np.inf
+    v[3, :32] = np.nan            # an all-NaN block
+    k[4, 64:96] = np.inf          # an all-inf block
+    v[5, 1] = np.nan
+    v[5, 2] = np.inf
+    kv = sc.KvCache(ctx, 1, KV, hd, 16)
+    try:
+        kd, vd = to_dev(k), to_dev(v)
+        if path == "append":
+            for t in range(T):
+                kv.append(0, t, kd[t].data_ptr(), vd[t].data_ptr())
+        elif path == "append_range":
+            kv.append_range(0, 0, T, kd.data_ptr(), vd.data_ptr())
+        else:  # the attention kernel's in-register quantiser (new row fused)
+            q = to_dev(np.zeros(KV * hd, np.float32))
+            out = torch.zeros(KV * hd, device="cuda")
+            for t in range(T):
+                kv.attend(0, q.data_ptr(), out.data_ptr(), KV, t + 1, 0.125, k_new=kd[t].data_ptr(),
+                          v_new=vd[t].data_ptr())
+        nb = KV * hd // 32 * 36
+        kb = torch.zeros(T * nb, dtype=torch.uint8, device="cuda")
+        vb = torch.zeros_like(kb)
+        kv.read_blocks(0, 0, T, kb.data_ptr(), vb.data_ptr())
+        torch.cuda.synchronize()
+        ctx.check()
+        for arr, got in ((k, kb), (v, vb)):
+            want = np.concatenate([oracle.q8_quantize(arr[t]) for t in range(T)])
+            assert np.array_equal(got.cpu().numpy(), want)
+            if reference_q8 is not None:
+                assert np.array_equal(want, np.concatenate([reference_q8(arr[t]) for t in range(T)]))
+    finally:
+        kv.close()
+
+
+@pytest.fixture(scope="module")
+def reference_q8():
+    """The reference's own quantiser (oracle/_ref) when it is built here."""
+    from oracle.oracle_py import Reference
+    return Reference().q8_quantize if Reference.available() else None
+
+
 @pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64)])
 @pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049, 9001, 20000])  # >= 8192: long-context loop
 @pytest.mark.parametrize("new_row", ["fused", "pre_appended"])

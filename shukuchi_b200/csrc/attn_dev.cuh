@@ -27,7 +27,9 @@ namespace adev {
 
 // One warp quantises one 32-element block (lane = element).
 __device__ __forceinline__ void q8_block_store(float v, int8_t* q_dst, float* s_dst, int lane) {
-  const float amax = warp_max(fabsf(v));
+  // fmaxf with 0 first: a NaN lane counts as 0, as `a > max_abs` skips it in
+  // the reference (an all-NaN block then has scale 1, not NaN)
+  const float amax = warp_max(fmaxf(0.0f, fabsf(v)));
   float scale = amax / 127.0f;
   if (scale == 0.0f) scale = 1.0f;
   int q = __float2int_rn(v / scale);

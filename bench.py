@@ -516,7 +516,10 @@ def run_ours(args, ws, rank, local):
 
 
 def main():
-    os.environ["NCCL_DEBUG"] = "WARN"  # one JSON line on stdout: no NCCL version banner
+    # NCCL's log (its version banner and, at INFO, the communicator lines that
+    # name every rank) goes to stderr, so stdout carries the one JSON line
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
     args = parse()
     ws, rank, local = dist_setup(args)
     if args.impl == "reference":

@@ -108,6 +108,35 @@ void orc_dequant_q6k(const void *blocks, float *y, uint32_t k) {
     }
 }
 
+/* engine/src/ops.c:144-165 dequantize_row_q5_k.  Block = {u16 d, u16 dmin,
+ * u8 scales[12], u8 qh[32], u8 qs[128]} (176 B).  Unlike ggml's Q5_K, element
+ * idx of the block takes its low 4 bits from qs[idx/2] (low nibble for even
+ * idx, high nibble for odd) and its fifth bit from bit idx%8 of qh[idx/8];
+ * value = d*sc*q5 - dmin*m with the sub-block (idx/32) scale and min. */
+void orc_dequant_q5k(const void *blocks, float *y, uint32_t k) {
+    const uint8_t *b = (const uint8_t *)blocks;
+    for (uint32_t i = 0; i < k / ORC_QK; ++i, b += ORC_Q5K_BYTES) {
+        const float d = orc_half_to_float(rd16(b));
+        const float dmin = orc_half_to_float(rd16(b + 2));
+        const uint8_t *scales = b + 4, *qh = b + 16, *qs = b + 48;
+        for (int sb = 0; sb < 8; ++sb) {
+            uint8_t sc, mn;
+            scale_min_k4(sb, scales, &sc, &mn);
+            const float d1 = d * sc, m1 = dmin * mn;
+            for (int l = 0; l < 32; ++l) {
+                const int idx = sb * 32 + l;
+                const uint8_t lo = (idx & 1) ? (uint8_t)(qs[idx / 2] >> 4) : (uint8_t)(qs[idx / 2] & 0xF);
+                const uint8_t hi = (uint8_t)((qh[idx / 8] >> (idx & 7)) & 1);
+                *y++ = d1 * (float)(uint8_t)(lo | (hi << 4)) - m1;
+            }
+        }
+    }
+}
+
+static size_t dtype_block_bytes(uint32_t dtype) {
+    return dtype == ORC_T_Q4K ? ORC_Q4K_BYTES : dtype == ORC_T_Q5K ? ORC_Q5K_BYTES : ORC_Q6K_BYTES;
+}
+
 typedef struct {
     uint32_t dtype;
     const uint8_t *w;
@@ -116,12 +145,13 @@ typedef struct {
     uint32_t k, r0, r1;
 } mv_job;
 
-/* engine/src/ops.c:266-314 (Q4_K) and :361-404 (Q6_K): per row, dequantize
- * each 256-block into tmp[] and accumulate sum += tmp[i]*x[i] in order. */
+/* engine/src/ops.c:266-314 (Q4_K), :316-359 (Q5_K) and :361-404 (Q6_K): per
+ * row, dequantize each 256-block into tmp[] and accumulate sum += tmp[i]*x[i]
+ * in order. */
 static void *mv_rows(void *arg) {
     mv_job *j = (mv_job *)arg;
     const uint32_t nb = j->k / ORC_QK;
-    const size_t bb = j->dtype == ORC_T_Q4K ? ORC_Q4K_BYTES : ORC_Q6K_BYTES;
+    const size_t bb = dtype_block_bytes(j->dtype);
     float tmp[ORC_QK];
     for (uint32_t r = j->r0; r < j->r1; ++r) {
         float sum = 0.0f;
@@ -129,6 +159,8 @@ static void *mv_rows(void *arg) {
         for (uint32_t b = 0; b < nb; ++b) {
             if (j->dtype == ORC_T_Q4K)
                 orc_dequant_q4k(row + b * bb, tmp, ORC_QK);
+            else if (j->dtype == ORC_T_Q5K)
+                orc_dequant_q5k(row + b * bb, tmp, ORC_QK);
             else
                 orc_dequant_q6k(row + b * bb, tmp, ORC_QK);
             const float *xv = j->x + (size_t)b * ORC_QK;
@@ -142,7 +174,7 @@ static void *mv_rows(void *arg) {
 int orc_matvec(uint32_t dtype, const void *w, const float *x, float *y,
                uint32_t m, uint32_t k) {
     if (!w || !x || !y) return -1;
-    if (dtype != ORC_T_Q4K && dtype != ORC_T_Q6K) return -1;
+    if (dtype != ORC_T_Q4K && dtype != ORC_T_Q5K && dtype != ORC_T_Q6K) return -1;
     if (k == 0 || k % ORC_QK) return -1;
     int nt = g_threads;
     if ((uint32_t)nt > m) nt = m ? (int)m : 1;

@@ -25,6 +25,7 @@ extern "C" {
 
 #define ORC_QK 256
 #define ORC_Q4K_BYTES 144
+#define ORC_Q5K_BYTES 176
 #define ORC_Q6K_BYTES 210
 #define ORC_Q8_BYTES 36 /* {float scale; int8 q[32]} */
 
@@ -39,6 +40,7 @@ void orc_set_threads(int n);
 
 float orc_half_to_float(uint16_t h);
 void orc_dequant_q4k(const void *blocks, float *y, uint32_t k);
+void orc_dequant_q5k(const void *blocks, float *y, uint32_t k);
 void orc_dequant_q6k(const void *blocks, float *y, uint32_t k);
 int orc_matvec(uint32_t dtype, const void *w, const float *x, float *y,
                uint32_t m, uint32_t k);

@@ -56,6 +56,7 @@ class Oracle:
             "orc_set_threads": (None, [I]),
             "orc_half_to_float": (F, [C.c_uint16]),
             "orc_dequant_q4k": (None, [P, P, U32]),
+            "orc_dequant_q5k": (None, [P, P, U32]),
             "orc_dequant_q6k": (None, [P, P, U32]),
             "orc_matvec": (I, [U32, P, P, P, U32, U32]),
             "orc_rmsnorm": (I, [P, P, P, U32]),
@@ -87,7 +88,8 @@ class Oracle:
 
     def dequant(self, qtype: int, blocks: np.ndarray, k: int) -> np.ndarray:
         y = np.empty(k, np.float32)
-        (self.L.orc_dequant_q4k if qtype == 12 else self.L.orc_dequant_q6k)(_ptr(blocks), _ptr(y), k)
+        fn = {12: self.L.orc_dequant_q4k, 13: self.L.orc_dequant_q5k, 14: self.L.orc_dequant_q6k}[qtype]
+        fn(_ptr(blocks), _ptr(y), k)
         return y
 
     def matvec(self, qtype: int, w: np.ndarray, x: np.ndarray, m: int, k: int) -> np.ndarray:

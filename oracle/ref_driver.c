@@ -17,6 +17,7 @@
 int ref_matmul(uint32_t dtype, const void *w, const float *x, float *y,
                uint32_t m, uint32_t k) {
     if (dtype == 12) return op_matmul_q4_k(NULL, w, x, y, m, k);
+    if (dtype == 13) return op_matmul_q5_k(NULL, w, x, y, m, k);
     if (dtype == 14) return op_matmul_q6_k(NULL, w, x, y, m, k);
     return -1;
 }

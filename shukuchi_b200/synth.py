@@ -4,6 +4,8 @@ The value distributions follow the benchmark description of the decode path:
 
 * Q4_K super-blocks (144 B): fp16 ``d`` and ``dmin`` ~ |N(0, 0.002)|, 12 uniform
   scale bytes, 128 uniform quant bytes.
+* Q5_K super-blocks (176 B, the reference's layout): as Q4_K plus 32 uniform
+  high-bit bytes.
 * Q6_K super-blocks (210 B): 128 B ``ql`` + 64 B ``qh`` uniform, 16 int8 scales
   uniform in [-32, 31], fp16 ``d`` ~ |N(0, 0.0005)|.
 * Norm weights: fp32 1 + N(0, 0.02).
@@ -20,9 +22,10 @@ import numpy as np
 
 QK = 256
 Q4K_BYTES = 144
+Q5K_BYTES = 176
 Q6K_BYTES = 210
-T_F32, T_F16, T_Q4K, T_Q6K = 0, 1, 12, 14
-BLOCK_BYTES = {T_Q4K: Q4K_BYTES, T_Q6K: Q6K_BYTES}
+T_F32, T_F16, T_Q4K, T_Q5K, T_Q6K = 0, 1, 12, 13, 14
+BLOCK_BYTES = {T_Q4K: Q4K_BYTES, T_Q5K: Q5K_BYTES, T_Q6K: Q6K_BYTES}
 
 
 def q4k_blocks(rng: np.random.Generator, n_blocks: int, d_sigma: float = 0.002) -> np.ndarray:
@@ -43,11 +46,21 @@ def q6k_blocks(rng: np.random.Generator, n_blocks: int, d_sigma: float = 0.0005)
     return b
 
 
+def q5k_blocks(rng: np.random.Generator, n_blocks: int, d_sigma: float = 0.002) -> np.ndarray:
+    """n_blocks Q5_K super-blocks (the reference's 176-byte layout
+    {u16 d, u16 dmin, u8 scales[12], u8 qh[32], u8 qs[128]}) as a
+    (n_blocks, 176) uint8 array; d and dmin as for Q4_K."""
+    b = rng.integers(0, 256, size=(n_blocks, Q5K_BYTES), dtype=np.uint8)
+    d = np.abs(rng.normal(0.0, d_sigma, size=(n_blocks, 2))).astype(np.float16)
+    b[:, 0:4] = d.view(np.uint8).reshape(n_blocks, 4)
+    return b
+
+
 def quant_matrix(rng: np.random.Generator, qtype: int, rows: int, cols: int) -> np.ndarray:
     """A rows x cols matrix in GGUF row-major block layout (flat uint8)."""
     assert cols % QK == 0
     nb = rows * (cols // QK)
-    blocks = q4k_blocks(rng, nb) if qtype == T_Q4K else q6k_blocks(rng, nb)
+    blocks = {T_Q4K: q4k_blocks, T_Q5K: q5k_blocks, T_Q6K: q6k_blocks}[qtype](rng, nb)
     return blocks.reshape(-1)
 
 

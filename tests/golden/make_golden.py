@@ -3,12 +3,12 @@
 The reference's C sources are compiled unmodified into oracle/_ref/libshkref.so
 (``make -C oracle ref``, which reads them where oracle/Makefile's REF points).  This script
 feeds seeded inputs through the reference entry points (op_matmul_q4_k,
-op_matmul_q6_k, op_rmsnorm, op_rope, q8_quantize_vec, op_attention, op_embed,
+op_matmul_q5_k, op_matmul_q6_k, op_rmsnorm, op_rope, q8_quantize_vec, op_attention, op_embed,
 forward_layer_view) and stores inputs and outputs.  The committed fixtures
 pin the oracle restatement (tests/test_oracle.py) on machines where the
 reference sources are absent.
 
-Usage: python tests/golden/make_golden.py
+Usage: python tests/golden/make_golden.py [fixture names]   (default: all)
 """
 from __future__ import annotations
 
@@ -31,7 +31,7 @@ def subnormal_scales(blocks: np.ndarray, qtype: int, rng, frac=0.5) -> None:
     n = blocks.shape[0]
     pick = rng.random(n) < frac
     sub = rng.integers(1, 0x400, size=n).astype(np.uint16)
-    if qtype == synth.T_Q4K:
+    if qtype in (synth.T_Q4K, synth.T_Q5K):
         v = blocks[:, 0:2].copy().view(np.uint16).reshape(-1)
         v[pick] = sub[pick]
         blocks[:, 0:2] = v.view(np.uint8).reshape(n, 2)
@@ -46,7 +46,8 @@ def subnormal_scales(blocks: np.ndarray, qtype: int, rng, frac=0.5) -> None:
 
 def gemv_case(ref, rng, qtype, m, k):
     nb = m * (k // 256)
-    blocks = synth.q4k_blocks(rng, nb) if qtype == synth.T_Q4K else synth.q6k_blocks(rng, nb)
+    blocks = {synth.T_Q4K: synth.q4k_blocks, synth.T_Q5K: synth.q5k_blocks,
+              synth.T_Q6K: synth.q6k_blocks}[qtype](rng, nb)
     subnormal_scales(blocks, qtype, rng)
     w = blocks.reshape(-1)
     x = rng.normal(0.0, 1.0, size=k).astype(np.float32)
@@ -81,7 +82,7 @@ def tiny_generate(ref, model, prompt, n_decode):
         ref.L.ref_engine_free(h)
 
 
-def main() -> None:
+def main(only: list[str] | None = None) -> None:
     build(ref=True)
     ref = Reference()
     rng = np.random.default_rng(1234)
@@ -116,10 +117,15 @@ def main() -> None:
     toks, logits = tiny_generate(ref, model, prompt, 6)
     out["tiny_model"] = dict(seed=np.uint32(7), digest=np.frombuffer(model.digest().encode(), np.uint8),
                              prompt=prompt, tokens=toks, logits=logits)
+    # Q5_K (engine/src/ops.c:144-165, 316-359) from its own stream, so adding it
+    # left the fixtures above unchanged
+    out["gemv_q5k"] = gemv_case(ref, np.random.default_rng(1235), synth.T_Q5K, 16, 512)
     for name, d in out.items():
+        if only and name not in only:
+            continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
         print("wrote", name)
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:] or None)

@@ -102,7 +102,7 @@ def test_half_subnormal_quirk(oracle):
 
 # ------------------------------------------------------------- goldens
 def test_golden_gemv(oracle):
-    for name, qt in (("gemv_q4k", 12), ("gemv_q6k", 14)):
+    for name, qt in (("gemv_q4k", 12), ("gemv_q5k", 13), ("gemv_q6k", 14)):
         g = golden(name)
         y = oracle.matvec(qt, g["w"], g["x"], int(g["m"]), int(g["k"]))
         assert np.array_equal(y.view(np.uint32), g["y"].view(np.uint32)), name
@@ -143,7 +143,7 @@ def test_golden_tiny_model(oracle):
 
 
 # ------------------------------------------- live cross-check vs the reference
-@pytest.mark.parametrize("qt,m,k", [(12, 33, 768), (14, 33, 768), (14, 5, 5632), (12, 3, 2048)])
+@pytest.mark.parametrize("qt,m,k", [(12, 33, 768), (14, 33, 768), (14, 5, 5632), (12, 3, 2048), (13, 33, 768), (13, 4, 5632)])
 def test_live_gemv_vs_reference(oracle, reference, qt, m, k):
     rng = np.random.default_rng(m * 7 + k)
     w = synth.quant_matrix(rng, qt, m, k)

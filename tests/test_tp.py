@@ -228,6 +228,7 @@ def _gpu_rank(rank, world, port, name, seed, prompt, n_dec, out_dir, mode="nccl"
 
     from shukuchi_b200 import cuda as sc
     from shukuchi_b200.device_model import GpuDecoder
+    from shukuchi_b200.synth_device import TILED_DEFAULT
     torch.cuda.set_device(rank)
     # gloo carries only the communicator id; the decode's collectives are NCCL
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -244,7 +245,9 @@ def _gpu_rank(rank, world, port, name, seed, prompt, n_dec, out_dir, mode="nccl"
             dist.all_gather_object(hs, h)
             return hs
         o_ranges = [(L.o_lo, L.o_hi) for L in (tp.layout(model.shape, r, world) for r in range(world))]
-        dec = GpuDecoder(ctx, mr, len(prompt) + n_dec + 1, device=f"cuda:{rank}",
+        # the bench's weight layouts (O and down row-tiled): this ill-conditioned
+        # model (logits ~1e4) turns any change of rounding into a visible drift
+        dec = GpuDecoder(ctx, mr, len(prompt) + n_dec + 1, device=f"cuda:{rank}", tiled=TILED_DEFAULT,
                          tp_rows=(lay.o_lo, lay.o_hi, lay.v_lo, lay.v_hi),
                          p2p_exchange=gather if mode == "p2p" else None, o_ranges=o_ranges,
                          ll_exchange=gather if mode == "ll" else None)

@@ -90,6 +90,14 @@ int shk_cuda_matmul_q4k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev,
                             uint32_t m, uint32_t k, void *stream);
 int shk_cuda_matmul_q6k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev, float *y_dev,
                             uint32_t m, uint32_t k, void *stream);
+/* replaces metal_matmul_q5k_vec (engine/include/metal_ops.h:5-26) as called
+ * from op_matmul_q5_k (engine/src/ops.c:316-359).  W is in the reference's
+ * 176-byte Q5_K block layout {u16 d, u16 dmin, u8 scales[12], u8 qh[32],
+ * u8 qs[128]}, element i of a block = low nibble (i even) / high nibble (i odd)
+ * of qs[i/2] plus bit i%8 of qh[i/8] as the fifth bit (dequantize_row_q5_k,
+ * :144-165), rows dense; w_dev and x_dev 16-byte aligned.  Async. */
+int shk_cuda_matmul_q5k_vec(shk_ctx *ctx, const void *w_dev, const float *x_dev, float *y_dev,
+                            uint32_t m, uint32_t k, void *stream);
 
 /* ---- Q6_K weight layout in HBM.  No counterpart in the reference (its
  *      weights stay in the GGUF layout in host memory).  The staged GEMV reads
@@ -146,9 +154,10 @@ int shk_cuda_tile(shk_ctx *ctx, uint32_t dtype, const void *src_dev, uint32_t sr
 int shk_cuda_prefill_matmul(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
                             const float *x_dev, float *y_dev, uint32_t m, uint32_t k, uint32_t n_tokens,
                             void *stream);
-/* dequantise-matvec by dtype: 12 (Q4_K), 14 (GGUF Q6_K),
+/* dequantise-matvec by dtype: 12 (Q4_K), 13 (Q5_K), 14 (GGUF Q6_K),
  * SHK_DTYPE_Q6_K_PLANAR, SHK_DTYPE_Q4_K_TILED or SHK_DTYPE_Q6_K_TILED;
- * row_stride 0 = dense rows (ignored for tiled weights). */
+ * row_stride 0 = dense rows (ignored for tiled weights; Q5_K rows must be
+ * dense). */
 int shk_cuda_matvec(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
                     const float *x_dev, float *y_dev, uint32_t m, uint32_t k, void *stream);
 /* Same contract as metal_matmul_q{4,6}k_vec: HOST weights/x/y, synchronous
@@ -157,6 +166,8 @@ int shk_cuda_matvec(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t ro
 int shk_cuda_matmul_q4k_vec_host(shk_ctx *ctx, const void *w_host, const float *x_host,
                                  float *y_host, uint32_t m, uint32_t k);
 int shk_cuda_matmul_q6k_vec_host(shk_ctx *ctx, const void *w_host, const float *x_host,
+                                 float *y_host, uint32_t m, uint32_t k);
+int shk_cuda_matmul_q5k_vec_host(shk_ctx *ctx, const void *w_host, const float *x_host,
                                  float *y_host, uint32_t m, uint32_t k);
 
 /* ---- op-level glue on device (engine/include/ops.h:9-38) ---- */

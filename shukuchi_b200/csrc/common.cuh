@@ -14,6 +14,7 @@ constexpr int Q4K_BYTES = 144;
 constexpr int Q6K_BYTES = 210;
 constexpr int Q8_BYTES = 36;  // reference KV block {float scale; int8 q[32]}
 constexpr int T_Q4K = 12;
+constexpr int T_Q5K = 13;
 constexpr int T_Q6K = 14;
 constexpr int T_Q6K_PLANAR = 0x10E;  // Q6_K rows in the planar layout of repack.cu
 

@@ -19,6 +19,7 @@
 #include "gemv.cuh"
 #include "glue.cuh"
 #include "mmv.cuh"
+#include "q5k.cuh"
 #include "tp_ll.cuh"
 
 using // Fewest cached positions per attention split (CTA of a KV head's cluster).
@@ -283,6 +284,17 @@ int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, uint32_t row_stride, cons
     c->n_matvec++;
     return SHK_OK;
   }
+  if (qt == T_Q5K) {
+    if (m == 0) return SHK_OK;
+    if (row_stride && row_stride != (k / QK) * Q5K_BYTES) return SHK_EINVAL;
+    Q5Mat mt{w, nullptr, y, m, EPI_STORE, 0};
+    Q5Plan p;
+    const int rc = q5k_plan(p, &mt, 1, k, x, nullptr, nullptr, nullptr, c->d_err, c->num_sms);
+    if (rc) return rc == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+    CK(q5k_launch(p, st));
+    c->n_matvec++;
+    return SHK_OK;
+  }
   if (qt != T_Q4K && qt != T_Q6K && qt != T_Q6K_PLANAR) return SHK_EUNSUPPORTED;
   if (m == 0) return SHK_OK;
   const uint32_t nb = k / QK;
@@ -321,7 +333,7 @@ int matvec_dev(shk_ctx* c, uint32_t qt, const void* w, uint32_t row_stride, cons
 int matvec_host(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y, uint32_t m,
                 uint32_t k) {
   if (!w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
-  const size_t wb = (size_t)m * (k / QK) * (qt == T_Q4K ? Q4K_BYTES : Q6K_BYTES);
+  const size_t wb = (size_t)m * (k / QK) * (qt == T_Q4K ? Q4K_BYTES : qt == T_Q5K ? Q5K_BYTES : Q6K_BYTES);
   int rc;
   if ((rc = grow(&c->hv_w, &c->hv_w_cap, wb)) || (rc = grow(&c->hv_x, &c->hv_x_cap, (size_t)k * 4)) ||
       (rc = grow(&c->hv_y, &c->hv_y_cap, (size_t)m * 4)))
@@ -388,6 +400,7 @@ shk_ctx* shk_cuda_init(const shk_cuda_config* cfg) {
   ok = ok && cudaMallocHost(&c->h_freq, 512 * sizeof(float)) == cudaSuccess;
   ok = ok && gemv_init() == cudaSuccess;
   ok = ok && mmv_init() == cudaSuccess;
+  ok = ok && q5k_init() == cudaSuccess;
   ok = ok && cudaMalloc(&c->mmv_scratch, MMV_SCRATCH_BYTES) == cudaSuccess;
   ok = ok && cudaMemset(c->mmv_scratch, 0, MMV_SCRATCH_BYTES) == cudaSuccess;
   if (!ok) {
@@ -488,6 +501,11 @@ int shk_cuda_matmul_q6k_vec(shk_ctx* c, const void* w, const float* x, float* y,
   if (!c) return SHK_EINVAL;
   return matvec_dev(c, T_Q6K, w, 0, x, y, m, k, pick(c, s));
 }
+int shk_cuda_matmul_q5k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
+                            uint32_t k, void* s) {
+  if (!c) return SHK_EINVAL;
+  return matvec_dev(c, T_Q5K, w, 0, x, y, m, k, pick(c, s));
+}
 int shk_cuda_matvec(shk_ctx* c, uint32_t dtype, const void* w, uint32_t row_stride, const float* x, float* y,
                     uint32_t m, uint32_t k, void* s) {
   if (!c) return SHK_EINVAL;
@@ -545,6 +563,11 @@ int shk_cuda_matmul_q6k_vec_host(shk_ctx* c, const void* w, const float* x, floa
                                  uint32_t k) {
   if (!c) return SHK_EINVAL;
   return matvec_host(c, T_Q6K, w, x, y, m, k);
+}
+int shk_cuda_matmul_q5k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
+                                 uint32_t k) {
+  if (!c) return SHK_EINVAL;
+  return matvec_host(c, T_Q5K, w, x, y, m, k);
 }
 
 int shk_cuda_rmsnorm(shk_ctx* c, const float* x, const float* w, float* y, uint32_t d, void* s) {

@@ -75,8 +75,10 @@ _SIGS = {
     "shk_cuda_sync": (I, [P, P]),
     "shk_cuda_matmul_q4k_vec": (I, [P, P, P, P, U32, U32, P]),
     "shk_cuda_matmul_q6k_vec": (I, [P, P, P, P, U32, U32, P]),
+    "shk_cuda_matmul_q5k_vec": (I, [P, P, P, P, U32, U32, P]),
     "shk_cuda_matmul_q4k_vec_host": (I, [P, P, P, P, U32, U32]),
     "shk_cuda_matmul_q6k_vec_host": (I, [P, P, P, P, U32, U32]),
+    "shk_cuda_matmul_q5k_vec_host": (I, [P, P, P, P, U32, U32]),
     "shk_cuda_rmsnorm": (I, [P, P, P, P, U32, P]),
     "shk_cuda_rope": (I, [P, P, U32, U32, U32, F, P]),
     "shk_cuda_swiglu": (I, [P, P, P, P, U32, P]),
@@ -231,12 +233,13 @@ class Context:
 
     def matmul(self, qtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int,
                stream: int | None = None) -> None:
-        name = "shk_cuda_matmul_q4k_vec" if qtype == 12 else "shk_cuda_matmul_q6k_vec"
+        name = {12: "shk_cuda_matmul_q4k_vec", 13: "shk_cuda_matmul_q5k_vec", 14: "shk_cuda_matmul_q6k_vec"}[qtype]
         _call(name, self.h, w_dev, x_dev, y_dev, m, k, stream)
 
     def matmul_host(self, qtype: int, w, x, y, m: int, k: int) -> None:
         """Host-pointer, synchronous variant (numpy arrays)."""
-        name = "shk_cuda_matmul_q4k_vec_host" if qtype == 12 else "shk_cuda_matmul_q6k_vec_host"
+        name = {12: "shk_cuda_matmul_q4k_vec_host", 13: "shk_cuda_matmul_q5k_vec_host",
+                14: "shk_cuda_matmul_q6k_vec_host"}[qtype]
         _call(name, self.h, w.ctypes.data, x.ctypes.data, y.ctypes.data, m, k)
 
     def rmsnorm(self, x, w, y, d, stream=None):

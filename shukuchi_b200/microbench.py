@@ -51,7 +51,7 @@ from .synth import BLOCK_BYTES, QK
 from .synth_device import _fill_blocks
 
 GEMV_SHAPES = [(12, 4096, 4096), (12, 14336, 4096), (12, 4096, 14336), (14, 4096, 14336),
-               (14, 128256, 4096)]
+               (14, 128256, 4096), (13, 4096, 4096), (13, 14336, 4096), (13, 4096, 14336)]
 _ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -99,6 +99,8 @@ def gemv(args, ctx) -> None:
         if stride != row:
             raise SystemExit(f"rows of {qt},{m},{k} are not 16-byte multiples; use the C ABI row_stride")
         dt = qt
+        if args.tiled and qt == 13:
+            continue  # Q5_K has no row-tiled form: it runs on GGUF rows
         if args.tiled:  # row-tiled copies for the tensor-core matvec
             torch.cuda.synchronize()
             tw = []
@@ -133,7 +135,7 @@ def gemv(args, ctx) -> None:
         us = ms * 1000.0 / nl
         alg = m * row + 4 * k + 4 * m
         gbs = alg / (us * 1e-6) / 1e9
-        print(json.dumps({"bench": "gemv", "qtype": "Q4_K" if qt == 12 else "Q6_K", "m": m, "k": k,
+        print(json.dumps({"bench": "gemv", "qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "m": m, "k": k,
                           "layout": "tiled" if args.tiled else ("planar" if qt == 14 else "gguf"),
                           "us": round(us, 3), "bytes": alg, "gbs": round(gbs, 1),
                           "frac": round(gbs / peak, 4), "peak_gbs": peak, "peak_kind": kind,

@@ -12,7 +12,7 @@ import dataclasses
 import torch
 
 from . import cuda as sc
-from .synth import BLOCK_BYTES, QK, ModelShape, T_Q4K, T_Q6K
+from .synth import BLOCK_BYTES, QK, ModelShape, T_Q4K, T_Q5K, T_Q6K
 
 
 def _fill_blocks(buf: torch.Tensor, qtype: int, rows: int, cols: int, stride: int, gen) -> None:
@@ -22,7 +22,7 @@ def _fill_blocks(buf: torch.Tensor, qtype: int, rows: int, cols: int, stride: in
     v = buf.view(rows, stride)[:, : nb * bb]
     v.copy_(torch.randint(0, 256, v.shape, dtype=torch.uint8, device=buf.device, generator=gen))
     blocks = v.view(rows, nb, bb)
-    if qtype == T_Q4K:
+    if qtype in (T_Q4K, T_Q5K):
         d = (torch.randn((rows, nb, 2), device=buf.device, generator=gen) * 0.002).abs().half()
         blocks[:, :, 0:4] = d.view(torch.uint8).view(rows, nb, 4)
     else:

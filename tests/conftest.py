@@ -53,7 +53,7 @@ def to_dev(a):
 def gemv_tolerance(oracle, qtype, w, x, m, k):
     """Per-row bound: 4*sqrt(k)*2^-24 times the L1 mass sum_k |w_rk * x_k|
     (fp32 summation in two different orders), plus a tiny absolute floor."""
-    bb = 144 if qtype == 12 else 210
+    bb = {12: 144, 13: 176, 14: 210}[qtype]
     rowb = (k // 256) * bb
     W = np.stack([oracle.dequant(qtype, w[r * rowb:(r + 1) * rowb], k) for r in range(m)])
     mass = np.abs(W) @ np.abs(x.astype(np.float64))

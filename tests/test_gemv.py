@@ -1,5 +1,5 @@
-"""Q4_K / Q6_K dequantise-matvec on the GPU vs the oracle (op_matmul_q4_k /
-op_matmul_q6_k restated).  Tolerance: per row |dy| <= 4*sqrt(k)*2^-24 * sum|w*x|
+"""Q4_K / Q5_K / Q6_K dequantise-matvec on the GPU vs the oracle (op_matmul_q4_k
+/ op_matmul_q5_k / op_matmul_q6_k restated).  Tolerance: per row |dy| <= 4*sqrt(k)*2^-24 * sum|w*x|
 (two fp32 summation orders)."""
 import numpy as np
 import pytest
@@ -23,7 +23,7 @@ def run_gemv(ctx, qt, w, x, m, k):
 
 def check(oracle, ctx, qt, m, k, seed, subnormal=False, xscale=1.0):
     rng = np.random.default_rng(seed)
-    blocks = (synth.q4k_blocks if qt == 12 else synth.q6k_blocks)(rng, m * (k // 256))
+    blocks = {12: synth.q4k_blocks, 13: synth.q5k_blocks, 14: synth.q6k_blocks}[qt](rng, m * (k // 256))
     if subnormal:
         from golden.make_golden import subnormal_scales
         subnormal_scales(blocks, qt, rng, frac=0.7)
@@ -51,19 +51,36 @@ def test_q6k(oracle, ctx, m, k):
     check(oracle, ctx, 14, m, k, seed=m * 3 + k)
 
 
-@pytest.mark.parametrize("qt", [12, 14])
+@pytest.mark.parametrize("m,k", [(1, 256), (2, 512), (3, 1280), (64, 2048), (333, 1024), (4096, 4096),
+                                 (1000, 14336), (4096, 14336), (37, 28672), (5, 64512)])
+def test_q5k(oracle, ctx, m, k):
+    # the reference's own Q5_K element order (engine/src/ops.c:144-165); odd m
+    # (a last row pair of one row), 5 blocks a row (a partial 4-block step),
+    # k up to the largest x the kernel holds in shared memory
+    check(oracle, ctx, 13, m, k, seed=m * 5 + k)
+
+
+def test_q5k_rejects_too_long_rows(ctx):
+    from shukuchi_b200.cuda import ShkError
+    d = torch.zeros(65536 * 176 // 256, dtype=torch.uint8, device="cuda")
+    x = torch.zeros(65536, device="cuda")
+    with pytest.raises(ShkError):
+        ctx.matmul(13, d.data_ptr(), x.data_ptr(), x.data_ptr(), 1, 65536)
+
+
+@pytest.mark.parametrize("qt", [12, 13, 14])
 def test_subnormal_scales(oracle, ctx, qt):
     # the reference decodes subnormal fp16 scales at half value; GPU must too
     check(oracle, ctx, qt, 64, 1024, seed=99, subnormal=True)
 
 
-@pytest.mark.parametrize("qt", [12, 14])
+@pytest.mark.parametrize("qt", [12, 13, 14])
 def test_large_and_tiny_inputs(oracle, ctx, qt):
     check(oracle, ctx, qt, 128, 2048, seed=5, xscale=1e6)
     check(oracle, ctx, qt, 128, 2048, seed=6, xscale=1e-6)
 
 
-@pytest.mark.parametrize("qt", [12, 14])
+@pytest.mark.parametrize("qt", [12, 13, 14])
 def test_outlier_in_block(oracle, ctx, qt):
     # x is fixed point relative to each 256-element block's maximum; a 1000x
     # outlier in a block must keep the row inside the per-row bound
@@ -79,7 +96,7 @@ def test_outlier_in_block(oracle, ctx, qt):
 
 
 def test_golden_vectors(oracle, ctx):
-    for name, qt in (("gemv_q4k", 12), ("gemv_q6k", 14)):
+    for name, qt in (("gemv_q4k", 12), ("gemv_q5k", 13), ("gemv_q6k", 14)):
         g = golden(name)
         m, k = int(g["m"]), int(g["k"])
         y = run_gemv(ctx, qt, g["w"], g["x"], m, k)
@@ -89,7 +106,7 @@ def test_golden_vectors(oracle, ctx):
 
 def test_host_pointer_variant(oracle, ctx):
     rng = np.random.default_rng(3)
-    for qt in (12, 14):
+    for qt in (12, 13, 14):
         m, k = 300, 4096
         w = synth.quant_matrix(rng, qt, m, k)
         x = rng.normal(0, 1, k).astype(np.float32)

@@ -3,13 +3,18 @@
 Q4_K_M model, with the Q4_K GEMV's HBM roofline fraction.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--shape llama8b|llama70b] [--prompt P] [--kv-fill auto|tokens|synthetic]
 
-One step = one decoded token: embed -> 32 layers (RMSNorm+QKV+RoPE GEMV,
+One step = one decoded token: embed -> L layers (RMSNorm+QKV+RoPE GEMV,
 Q8_0 append + split-K attention, O GEMV + residual, RMSNorm+gate/up GEMV +
 SwiGLU, down GEMV + residual) -> lm_head GEMV -> first-index argmax, with the
-token fed back on the device.  Weights (4.9 GB) are synthetic, seeded, and
-generated in HBM; the KV cache is prefilled with a 512-token random prompt.
-Weights exceed L2 (126 MB), so no flush is needed between steps.
+token fed back on the device.  Weights (4.9 GB for the 8B shape, 44.4 GB for
+70B) are synthetic, seeded, and generated in HBM.  The 8B shape's KV cache is
+prefilled with a 512-token random prompt decoded token by token; the 70B
+shape's 8192-position context is N(0,1) K/V rows quantised straight into the
+Q8_0 cache (decoding 8192 prompt tokens one by one would take minutes and
+times nothing different).  Weights exceed L2 (126 MB), so no flush is needed
+between steps.
 
 At --gpus N > 1 the same single sequence is decoded tensor-parallel over N
 GPUs (one process per GPU; Wq/Wk/Wv/gate/up split by output rows, Wo/down by
@@ -39,6 +44,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s bs1, 8B-shape Q4_K_M; Q4_K/Q6_K GEMV HBM GB/s vs peak"
 PROMPT = 512
+PROMPTS = {"llama8b": 512, "llama70b": 8192}  # the context each model shape is measured at
 PART_NAMES = ("rmsnorm_qkv_rope", "append_attention", "o_proj_residual", "rmsnorm_gateup_swiglu",
               "down_residual", "lm_head")
 
@@ -50,14 +56,23 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--shape", default="llama8b")
-    ap.add_argument("--prompt", type=int, default=PROMPT)
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="KV context before the timed decode (default: 512 for the 8B shape, 8192 for 70B)")
+    ap.add_argument("--kv-fill", default="auto", choices=["auto", "tokens", "synthetic"],
+                    help="how the context is built: the prompt decoded token by token, or N(0,1) K/V rows "
+                         "appended straight into the Q8_0 cache (auto: synthetic above 1024 positions)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--p2p-allreduce", action="store_true",
                     help="tensor parallel: the peer-memory exchange inside the GEMVs instead of NCCL all-reduce")
     ap.add_argument("--tp-allreduce", default="ll", choices=["ll", "nccl"],
                     help="tensor parallel: one-shot all-reduce kernel over NVLink peer memory with the flags in "
                          "the data words (ll, default) or NCCL's all-reduce")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.prompt is None:
+        a.prompt = PROMPTS.get(a.shape, PROMPT)
+    if a.kv_fill == "auto":
+        a.kv_fill = "synthetic" if a.prompt > 1024 else "tokens"
+    return a
 
 
 def dist_setup(args):
@@ -156,18 +171,20 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- CPU side
 def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
-    """Reference (or oracle) CPU path on a bounded sample of the 8B-shape token:
-    each step runs 2 of the 32 layers (forward_layer_view at the current
-    position, KV prefilled to `prompt`) plus 1/16 of the output-head rows;
-    one token costs 16 such steps.  Returns (tok/s, kind, sample text)."""
+    """Reference (or oracle) CPU path on a bounded sample of the token: each
+    step runs 2 of the model's L layers (forward_layer_view at the current
+    position, KV prefilled to `prompt`) plus 2/L of the output-head rows; one
+    token costs L/2 such steps.  Returns (tok/s, kind, sample text, per-step
+    tok/s)."""
     import numpy as np
     from oracle.oracle_py import Oracle, Reference
     from shukuchi_b200 import synth
 
     s = synth.SHAPES[shape_name]
+    f = s.n_layers / 2.0  # steps per token
     rng = np.random.default_rng(0)
     layers = [synth.make_layer(rng, s) for _ in range(2)]
-    head_rows = s.n_vocab // 16
+    head_rows = int(round(s.n_vocab / f))
     head = synth.quant_matrix(rng, s.t_out, head_rows, s.n_embd)
     sub = synth.Model(s, layers, np.zeros(1, np.uint8), np.zeros(1, np.float32), head)
     import dataclasses
@@ -219,10 +236,10 @@ def cpu_sample(steps: int, warmup: int, shape_name: str, prompt: int):
         pos += 1
         if i >= warmup:
             times.append(dt)
-    per_token = 16.0 * sum(times) / len(times)
-    sample = (f"{steps} steps of 2/32 layers of {s.name} at positions {prompt}+ plus 1/16 of the "
-              f"output-head rows; token time = 16 x step time")
-    return 1.0 / per_token, kind, sample, [1.0 / (16.0 * t) for t in times]
+    per_token = f * sum(times) / len(times)
+    sample = (f"{steps} steps of 2/{s.n_layers} layers of {s.name} at positions {prompt}+ plus "
+              f"{head_rows}/{s.n_vocab} output-head rows; token time = {f:g} x step time")
+    return 1.0 / per_token, kind, sample, [1.0 / (f * t) for t in times]
 
 
 def host_info() -> dict:
@@ -289,11 +306,13 @@ def parity_check(ctx, ws, rank, local, allreduce="ll"):
 
 def workload_config(args, ws):
     from shukuchi_b200 import synth
-    name = synth.SHAPES[args.shape].name
-    return {"workload": f"{name} Q4_K_M decode bs1 after a {args.prompt}-token prompt, Q8_0 KV",
-            "model": name, "global_batch": 1, "seq_len": args.prompt,
+    s = synth.SHAPES[args.shape]
+    ctx = (f"after a {args.prompt}-token prompt" if args.kv_fill == "tokens" else
+           f"at a {args.prompt}-position context of N(0,1) K/V rows appended to the cache")
+    return {"workload": f"{s.name} Q4_K_M decode bs1 {ctx}, Q8_0 KV",
+            "model": s.name, "global_batch": 1, "seq_len": args.prompt, "kv_fill": args.kv_fill,
             "parallelism": f"tp{ws}" if ws > 1 else "single",
-            "l2": "no flush: 4.9 GB of weights per step exceed the 126 MB L2"}
+            "l2": f"no flush: {synth.token_bytes(s) / 1e9:.1f} GB of weights per step exceed the 126 MB L2"}
 
 
 def run_reference(args, ws, rank):
@@ -359,13 +378,29 @@ def run_ours(args, ws, rank, local):
         m.set_layer(i, lv)
     stream = torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{local}")
 
-    # prompt, token by token (the reference has no batched prefill)
     import numpy as np
     rng = np.random.default_rng(0)  # one sequence, the same on every rank
-    prompt = rng.integers(0, shape.n_vocab, args.prompt).astype(np.uint32)
-    nxt = 0
-    for i, t in enumerate(prompt):
-        nxt = m.token_step(int(t), i, want_next=(i == len(prompt) - 1))
+    if args.kv_fill == "tokens":
+        # prompt, token by token (the reference has no batched prefill)
+        prompt = rng.integers(0, shape.n_vocab, args.prompt).astype(np.uint32)
+        nxt = 0
+        for i, t in enumerate(prompt):
+            nxt = m.token_step(int(t), i, want_next=(i == len(prompt) - 1))
+    else:
+        # the context as N(0,1) K/V rows quantised into the cache (this rank's
+        # KV heads), then decode from a random token
+        kvd_l = lshape.n_kv_heads * lshape.head_dim
+        gen = torch.Generator(device=f"cuda:{local}")
+        gen.manual_seed(77 + rank)
+        with torch.cuda.stream(stream):
+            for layer in range(lshape.n_layers):
+                for p0 in range(0, args.prompt, 2048):
+                    n = min(2048, args.prompt - p0)
+                    kk = torch.randn((n, kvd_l), device=f"cuda:{local}", generator=gen)
+                    vv = torch.randn((n, kvd_l), device=f"cuda:{local}", generator=gen)
+                    kv.append_range(layer, p0, n, kk.data_ptr(), vv.data_ptr(), stream=ctx.stream)
+                    ctx.sync()
+        nxt = int(rng.integers(0, shape.n_vocab))
     pos = args.prompt
 
     def barrier():

@@ -56,13 +56,15 @@ __global__ void kv_append_range_kernel(KvLayout kv, uint32_t layer, uint32_t sta
 
 constexpr int ATT_WARPS = 4;
 constexpr int ATT_THREADS = 32 * ATT_WARPS;
+// Caches of at least this many positions attend with the split kernel.
+constexpr uint32_t ATT_SPLIT_CAPACITY = 4096;
 
 template <int HD, int G>
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
-  __shared__ __align__(16) float sm[AttnSmem<HD, G, ATT_WARPS>::FLOATS];
+  __shared__ __align__(16) float sm[AttnSmem<HD, G, ATT_WARPS>::FLOATS_LONG];
   pdl_trigger();
   pdl_wait();
-  attn_item<HD, G, ATT_WARPS>(a, blockIdx.x, blockIdx.y, gridDim.y, sm);
+  attn_item<HD, G, ATT_WARPS, true>(a, blockIdx.x, blockIdx.y, gridDim.y, sm);
 }
 
 __global__ void kv_read_range_kernel(KvLayout kv, uint32_t layer, uint32_t start, uint32_t end,
@@ -232,6 +234,15 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream) {
     const cudaError_t e = kv_append_launch(a.kv, a.layer, a.pos, a.k_new, a.v_new, a.err, stream);
     if (e != cudaSuccess) return e;
     b.k_new = b.v_new = nullptr;
+  }
+  if (a.kv.max_seq >= ATT_SPLIT_CAPACITY && a.part && a.counters && a.max_splits > 0 &&
+      a.max_splits <= (uint32_t)ATT_MAX_SPLITS) {
+    // Long caches: every SM takes splits of ATT_SPLIT_LONG+ positions (the
+    // one-cluster-per-KV-head kernel would leave most SMs idle, the more so
+    // with few KV heads per tensor-parallel rank); partials merge in global
+    // memory.
+    b.min_per_split = std::max(a.min_per_split, ATT_SPLIT_LONG);
+    return a.kv.hd == 64 ? attn_launch_hd<64>(b, G, stream) : attn_launch_hd<128>(b, G, stream);
   }
   return a.kv.hd == 64 ? attn_cluster_hd<64>(b, G, stream) : attn_cluster_hd<128>(b, G, stream);
 }

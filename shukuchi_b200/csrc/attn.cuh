@@ -40,8 +40,9 @@ struct AttnArgs {
   int* err;
 };
 
-// Append + decode attention, one thread-block cluster per KV head (splits
-// merged in distributed shared memory).  part/counters/max_splits unused.
+// Append + decode attention: one thread-block cluster per KV head (splits
+// merged in distributed shared memory), or, for caches of 4096 positions or
+// more, the split kernel below (part/counters/max_splits then required).
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream);
 // The same with splits merged through `part` and `counters` in global memory.
 cudaError_t attn_decode_split_launch(const AttnArgs& a, cudaStream_t stream);

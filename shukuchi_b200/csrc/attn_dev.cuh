@@ -109,10 +109,119 @@ struct AttnSmem {
   static constexpr int FLAG = SL + G;
   static constexpr int FLOATS = FLAG + 4;
   static constexpr size_t BYTES = (size_t)FLOATS * 4;
+  // the long-range loop's per-warp p[G][32] (attn_item<..., LONG = true> only)
+  static constexpr int PB = FLOATS;
+  static constexpr int FLOATS_LONG = PB + NW * G * 32;
 };
 
 __device__ __forceinline__ void att_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Long position ranges (at least ATT_LONG_MIN per CTA): a warp iteration
+// covers 32 positions, one per lane.  QK^T: the lane loads its position's
+// whole Q8_0 K row and forms all G scores (no shuffles); softmax: one warp
+// maximum per query head per 32 positions, sums kept per lane until the end;
+// PV: lane = EPL columns, the weights of the 32 positions broadcast through
+// shared memory (pb: this warp's [G][32]), the V words of all 32 positions
+// loaded at the start of the iteration.  The new K/V row (position pos) is
+// already in the cache, stored by this CTA before the loop.
+constexpr uint32_t ATT_LONG_MIN = 512;
+// Split kernel: a split of at least this many positions runs the long loop.
+constexpr uint32_t ATT_SPLIT_LONG = 256;
+
+template <int HD, int G, int NW>
+__device__ __forceinline__ void attn_long(const AttnArgs& a, const float* qsm, const int8_t* __restrict__ Kq,
+                                          const float* __restrict__ Ks, const int8_t* __restrict__ Vq,
+                                          const float* __restrict__ Vs, uint32_t p0, uint32_t p1, int warp,
+                                          int lane, float* pb, float (&m)[G], float (&l)[G],
+                                          float (&acc)[G][HD / 32]) {
+  constexpr int NB = HD / 32, EPL = HD / 32, KV4 = HD / 16, QROW = 36;
+  float lp[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) lp[g] = 0.f;
+  for (uint32_t T = p0 + 32u * warp; T < p1; T += 32u * NW) {
+    const uint32_t nt = min(32u, p1 - T);
+    const bool valid = (uint32_t)lane < nt;
+    const uint32_t t = T + (valid ? (uint32_t)lane : 0u);
+    // every load of the iteration first
+    uint4 kr[KV4];
+    const uint4* kp = reinterpret_cast<const uint4*>(Kq + (size_t)t * HD);
+#pragma unroll
+    for (int i = 0; i < KV4; ++i) kr[i] = kp[i];
+    float ksc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) ksc[b] = Ks[(size_t)t * NB + b];
+    uint32_t vw[32];
+    float vsc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t tj = T + ((uint32_t)j < nt ? (uint32_t)j : 0u);
+      const int8_t* vp = Vq + (size_t)tj * HD + lane * EPL;
+      vw[j] = EPL == 4 ? *reinterpret_cast<const uint32_t*>(vp) : *reinterpret_cast<const uint16_t*>(vp);
+      vsc[j] = Vs[(size_t)tj * NB + (lane * EPL) / 32];
+    }
+    // scores of this lane's position
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) sc[g] = 0.f;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      float kf[32];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint4 w = kr[2 * b + i];
+        s8x4_to_f32(w.x, kf + 16 * i);
+        s8x4_to_f32(w.y, kf + 16 * i + 4);
+        s8x4_to_f32(w.z, kf + 16 * i + 8);
+        s8x4_to_f32(w.w, kf + 16 * i + 12);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4* q4 = reinterpret_cast<const float4*>(qsm + (g * NB + b) * QROW);
+        float sb = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 qv = q4[u];
+          sb = fmaf(qv.x, kf[4 * u], sb);
+          sb = fmaf(qv.y, kf[4 * u + 1], sb);
+          sb = fmaf(qv.z, kf[4 * u + 2], sb);
+          sb = fmaf(qv.w, kf[4 * u + 3], sb);
+        }
+        sc[g] = fmaf(sb, ksc[b], sc[g]);
+      }
+    }
+    // online softmax over these 32 positions
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float sg = valid ? sc[g] * a.scale : -INFINITY;
+      const float mn = fmaxf(m[g], warp_max(sg));  // at least position T is valid: finite
+      const float corr = (m[g] == -INFINITY) ? 0.f : expf(m[g] - mn);
+      const float p = valid ? expf(sg - mn) : 0.f;
+      lp[g] = fmaf(lp[g], corr, p);
+      m[g] = mn;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[g][e] *= corr;
+      pb[g * 32 + lane] = p;
+    }
+    __syncwarp();
+    // P.V
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if ((uint32_t)j >= nt) break;  // uniform
+      float vf[4];
+      s8x4_to_f32(vw[j], vf);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pj = pb[g * 32 + j] * vsc[j];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(pj, vf[e], acc[g][e]);
+      }
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) l[g] = warp_sum(lp[g]);
 }
 
 // q, the new K/V rows, the position and the cache may have been written
@@ -132,7 +241,7 @@ __device__ __forceinline__ void att_sync(int nthreads) {
 //       p broadcast by shuffle with the V block scale folded in.
 // Warps merge in shared memory; splits merge through `part` (log-sum-exp),
 // the last item of the KV head (atomic ticket) writing the output.
-template <int HD, int G, int NW>
+template <int HD, int G, int NW, bool LONG = false>
 __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint32_t split,
                                           uint32_t nsplit, float* sm) {
   using Tile = AttnTile<HD>;
@@ -190,8 +299,12 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
   constexpr uint32_t STEP = PPI * NW;
   uint32_t T = p0 + PPI * warp;
   Tile cur;
-  if (T < p1) cur.load(Kq, Ks, Vq, Vs, T, p1, lane);
-  for (; T < p1; T += STEP) {
+  const bool long_range = LONG && p1 - p0 >= ATT_SPLIT_LONG;
+  if (long_range)
+    attn_long<HD, G, NW>(a, sm + SM::Q, Kq, Ks, Vq, Vs, p0, p1, warp, lane, sm + SM::PB + warp * G * 32, m, l, acc);
+  else if (T < p1)
+    cur.load(Kq, Ks, Vq, Vs, T, p1, lane);
+  for (; !long_range && T < p1; T += STEP) {
     Tile nxt;
     if (T + STEP < p1) nxt.load(Kq, Ks, Vq, Vs, T + STEP, p1, lane);
     const bool ok = T + tl < p1;
@@ -428,110 +541,6 @@ __device__ __forceinline__ float q8_regs(const float4 (&v4)[8], uint4 (&q)[2]) {
   q[0] = make_uint4(w[0], w[1], w[2], w[3]);
   q[1] = make_uint4(w[4], w[5], w[6], w[7]);
   return scale;
-}
-
-// Long position ranges (at least ATT_LONG_MIN per CTA): a warp iteration
-// covers 32 positions, one per lane.  QK^T: the lane loads its position's
-// whole Q8_0 K row and forms all G scores (no shuffles); softmax: one warp
-// maximum per query head per 32 positions, sums kept per lane until the end;
-// PV: lane = EPL columns, the weights of the 32 positions broadcast through
-// shared memory (pb: this warp's [G][32]), the V words of all 32 positions
-// loaded at the start of the iteration.  The new K/V row (position pos) is
-// already in the cache, stored by this CTA before the loop.
-constexpr uint32_t ATT_LONG_MIN = 512;
-
-template <int HD, int G, int NW>
-__device__ __forceinline__ void attn_long(const AttnArgs& a, const float* qsm, const int8_t* __restrict__ Kq,
-                                          const float* __restrict__ Ks, const int8_t* __restrict__ Vq,
-                                          const float* __restrict__ Vs, uint32_t p0, uint32_t p1, int warp,
-                                          int lane, float* pb, float (&m)[G], float (&l)[G],
-                                          float (&acc)[G][HD / 32]) {
-  constexpr int NB = HD / 32, EPL = HD / 32, KV4 = HD / 16, QROW = 36;
-  float lp[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) lp[g] = 0.f;
-  for (uint32_t T = p0 + 32u * warp; T < p1; T += 32u * NW) {
-    const uint32_t nt = min(32u, p1 - T);
-    const bool valid = (uint32_t)lane < nt;
-    const uint32_t t = T + (valid ? (uint32_t)lane : 0u);
-    // every load of the iteration first
-    uint4 kr[KV4];
-    const uint4* kp = reinterpret_cast<const uint4*>(Kq + (size_t)t * HD);
-#pragma unroll
-    for (int i = 0; i < KV4; ++i) kr[i] = kp[i];
-    float ksc[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) ksc[b] = Ks[(size_t)t * NB + b];
-    uint32_t vw[32];
-    float vsc[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t tj = T + ((uint32_t)j < nt ? (uint32_t)j : 0u);
-      const int8_t* vp = Vq + (size_t)tj * HD + lane * EPL;
-      vw[j] = EPL == 4 ? *reinterpret_cast<const uint32_t*>(vp) : *reinterpret_cast<const uint16_t*>(vp);
-      vsc[j] = Vs[(size_t)tj * NB + (lane * EPL) / 32];
-    }
-    // scores of this lane's position
-    float sc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) sc[g] = 0.f;
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      float kf[32];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const uint4 w = kr[2 * b + i];
-        s8x4_to_f32(w.x, kf + 16 * i);
-        s8x4_to_f32(w.y, kf + 16 * i + 4);
-        s8x4_to_f32(w.z, kf + 16 * i + 8);
-        s8x4_to_f32(w.w, kf + 16 * i + 12);
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4* q4 = reinterpret_cast<const float4*>(qsm + (g * NB + b) * QROW);
-        float sb = 0.f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 qv = q4[u];
-          sb = fmaf(qv.x, kf[4 * u], sb);
-          sb = fmaf(qv.y, kf[4 * u + 1], sb);
-          sb = fmaf(qv.z, kf[4 * u + 2], sb);
-          sb = fmaf(qv.w, kf[4 * u + 3], sb);
-        }
-        sc[g] = fmaf(sb, ksc[b], sc[g]);
-      }
-    }
-    // online softmax over these 32 positions
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float sg = valid ? sc[g] * a.scale : -INFINITY;
-      const float mn = fmaxf(m[g], warp_max(sg));  // at least position T is valid: finite
-      const float corr = (m[g] == -INFINITY) ? 0.f : expf(m[g] - mn);
-      const float p = valid ? expf(sg - mn) : 0.f;
-      lp[g] = fmaf(lp[g], corr, p);
-      m[g] = mn;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) acc[g][e] *= corr;
-      pb[g * 32 + lane] = p;
-    }
-    __syncwarp();
-    // P.V
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if ((uint32_t)j >= nt) break;  // uniform
-      float vf[4];
-      s8x4_to_f32(vw[j], vf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float pj = pb[g * 32 + j] * vsc[j];
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(pj, vf[e], acc[g][e]);
-      }
-    }
-    __syncwarp();
-  }
-#pragma unroll
-  for (int g = 0; g < G; ++g) l[g] = warp_sum(lp[g]);
 }
 
 template <int HD, int G, int NW>

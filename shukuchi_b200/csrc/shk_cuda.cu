@@ -126,29 +126,55 @@ struct shk_kv {
 namespace {
 
 // One projection: the staged dp4a GEMV over GGUF / planar rows, or the
-// tensor-core matvec over row-tiled weights (tiled = true).
+// tensor-core matvec over row-tiled weights (tiled = true); its Q5_K matrices
+// (if any) run on the Q5_K matvec, a second launch after the first when the
+// projection mixes Q5_K with other types (main = false: Q5_K only).
 struct ProjPlan {
   GemvPlan g;
   MmvPlan mm;
+  Q5Plan q5;
   bool tiled = false;
+  bool main = true;
+  bool has_q5 = false;
 };
 
 cudaError_t proj_launch(const ProjPlan& p, cudaStream_t st, const uint32_t* pos = nullptr) {
-  if (p.tiled) {
-    if (!pos) return mmv_launch(p.mm, st);
-    MmvPlan q = p.mm;
+  cudaError_t e = cudaSuccess;
+  if (!p.main) {
+  } else if (p.tiled) {
+    if (!pos) {
+      e = mmv_launch(p.mm, st);
+    } else {
+      MmvPlan q = p.mm;
+      q.args.pos = pos;
+      e = mmv_launch(q, st);
+    }
+  } else if (!pos) {
+    e = gemv_launch(p.g, st);
+  } else {
+    GemvPlan q = p.g;
     q.args.pos = pos;
-    return mmv_launch(q, st);
+    e = gemv_launch(q, st);
   }
-  if (!pos) return gemv_launch(p.g, st);
-  GemvPlan q = p.g;
+  if (e != cudaSuccess || !p.has_q5) return e;
+  if (!pos) return q5k_launch(p.q5, st);
+  Q5Plan q = p.q5;
   q.args.pos = pos;
-  return gemv_launch(q, st);
+  return q5k_launch(q, st);
 }
+
+// Launches of one projection.
+int proj_launches(const ProjPlan& p) { return (p.main ? 1 : 0) + (p.has_q5 ? 1 : 0); }
 
 // Weight bytes one launch reads.
 uint64_t proj_weight_bytes(const ProjPlan& p) {
   uint64_t b = 0;
+  if (p.has_q5)
+    for (uint32_t i = 0; i < p.q5.args.nseg; ++i) {
+      const Q5Seg& g = p.q5.args.seg[i];
+      b += (uint64_t)g.m * (p.q5.args.k / QK) * Q5K_BYTES * (g.w2 ? 2 : 1);
+    }
+  if (!p.main) return b;
   if (p.tiled) {
     for (uint32_t i = 0; i < p.mm.args.nseg; ++i) {
       const MmvSeg& g = p.mm.args.seg[i];
@@ -792,9 +818,33 @@ void p2p_out(shk_model* m, GemvArgs& a, uint32_t j, uint32_t row_off) {
 
 // Plans one projection: the tensor-core matvec when every matrix is row-tiled,
 // else the staged GEMV (a mix is not supported).
-int plan_proj(shk_model* m, ProjPlan& P, const GemvMat* mats, int n, uint32_t k, const float* x,
+int plan_proj(shk_model* m, ProjPlan& P, const GemvMat* all, int n_all, uint32_t k, const float* x,
               const float* norm_w, const uint32_t* pos) {
   shk_ctx* c = m->ctx;
+  // Q5_K matrices go to their own kernel (the reference's Q5_K layout, rows
+  // dense), the rest to one staged GEMV or tensor-core matvec launch
+  GemvMat mats[GEMV_MAX_SEGS];
+  Q5Mat q5[Q5_MAX_SEGS];
+  int n = 0, n5 = 0;
+  for (int i = 0; i < n_all; ++i) {
+    if (all[i].qt == (uint32_t)T_Q5K) {
+      if (all[i].row_stride && all[i].row_stride != (k / QK) * Q5K_BYTES) return SHK_EINVAL;
+      if (all[i].epi == EPI_TP) return SHK_EUNSUPPORTED;
+      q5[n5++] = Q5Mat{all[i].w, all[i].w2, all[i].y, all[i].m, all[i].epi, all[i].rope_hd};
+    } else {
+      mats[n++] = all[i];
+    }
+  }
+  P.has_q5 = n5 > 0;
+  P.main = n > 0;
+  if (P.has_q5) {
+    const int r5 = q5k_plan(P.q5, q5, n5, k, x, norm_w, pos, m->d_freq, c->d_err, c->num_sms);
+    if (r5) return r5 == -2 ? SHK_EUNSUPPORTED : SHK_EINVAL;
+  }
+  if (!P.main) {
+    P.tiled = false;
+    return SHK_OK;
+  }
   int nt = 0;
   for (int i = 0; i < n; ++i) nt += dt_tiled(mats[i].qt) ? 1 : 0;
   if (nt != 0 && nt != n) return SHK_EUNSUPPORTED;
@@ -839,7 +889,8 @@ int build_layer_plans(shk_model* m, const shk_layer_desc& lv, LayerPlans& P, uin
   GemvMat dn{lv.ffn_down, nullptr, m->hidden, d.n_embd, lv.ffn_down_dtype, lv.row_stride_down, res_epi, 0};
   if ((rc = plan_proj(m, P.down, &dn, 1, d.n_ff, m->act, nullptr, nullptr))) return rc;
   if (p2p) {
-    if (P.qkv.tiled || P.o.tiled || P.gateup.tiled || P.down.tiled) return SHK_EUNSUPPORTED;
+    for (const ProjPlan* pp : {&P.qkv, &P.o, &P.gateup, &P.down})
+      if (pp->tiled || pp->has_q5 || !pp->main) return SHK_EUNSUPPORTED;
     // slots: 2l = O of layer l (consumed by gate/up), 2l + 1 = down (consumed
     // by the next layer's QKV or the head); consumer j reads the residual
     // from buffer j % 2 (0 = hidden, 1 = res2) and writes it to the other
@@ -943,6 +994,20 @@ bool vocab_split(const shk_model* m) { return m->v_hi - m->v_lo < m->d.n_vocab; 
 int plan_head(shk_model* m) {
   shk_ctx* c = m->ctx;
   const uint32_t nv = m->v_hi - m->v_lo;
+  m->head.main = true;
+  m->head.has_q5 = false;
+  if (m->d.output_dtype == (uint32_t)T_Q5K) {  // engine/src/engine.c:410 (a Q5_K head)
+    if (m->p2p.on) return SHK_EUNSUPPORTED;
+    Q5Mat hm{m->d.output_dev, nullptr, m->logits + m->v_lo, nv, EPI_STORE, 0};
+    m->head.tiled = false;
+    m->head.main = false;
+    m->head.has_q5 = true;
+    m->head_generic = false;
+    if (q5k_plan(m->head.q5, &hm, 1, m->d.n_embd, m->hidden, nullptr, nullptr, nullptr, c->d_err, c->num_sms))
+      return SHK_EUNSUPPORTED;
+    m->head_ok = true;
+    return SHK_OK;
+  }
   if (dt_tiled(m->d.output_dtype)) {
     if (m->p2p.on) return SHK_EUNSUPPORTED;
     MmvMat hm{m->d.output_dev, nullptr, m->logits + m->v_lo, nv, m->d.output_dtype, EPI_STORE, 0};
@@ -1068,7 +1133,7 @@ int build_persist(shk_model* m) {
   for (uint32_t l = 0; l < L; ++l) {
     const LayerPlans& P = m->plans[l];
     for (const ProjPlan* pp : {&P.qkv, &P.o, &P.gateup, &P.down}) {
-      if (!pp->tiled) return SHK_OK;
+      if (!pp->tiled || !pp->main || pp->has_q5) return SHK_OK;
       ma.push_back(pp->mm.args);
     }
   }

@@ -18,7 +18,7 @@ import numpy as np
 import torch
 
 from . import cuda as sc
-from .synth import BLOCK_BYTES, QK, Model, T_Q6K
+from .synth import BLOCK_BYTES, QK, Model, T_Q5K, T_Q6K
 
 
 def _dev(a: np.ndarray, device) -> torch.Tensor:
@@ -83,7 +83,7 @@ def upload(model: Model, device: str | torch.device = "cuda:0", ctx: sc.Context 
         return t.data_ptr()
 
     def mat(w, qt, rows, cols, proj):
-        if proj in ts:
+        if proj in ts and qt != T_Q5K:  # Q5_K stays in GGUF rows (its own matvec)
             t, dt = to_tiled(ctx, w, qt, rows, cols, device)
             keep.append(t)
             return t.data_ptr(), 0, dt
@@ -108,7 +108,7 @@ def upload(model: Model, device: str | torch.device = "cuda:0", ctx: sc.Context 
         layers.append(sc.LayerDesc(put(Lw.attn_norm), put(Lw.ffn_norm), q, k, v, o, g, u, d,
                                    tq, tk, tv, to, tg, tu, td, sv, sd))
     nv = out_rows or s.n_vocab
-    if "output" in ts:
+    if "output" in ts and s.t_out != T_Q5K:
         out, t_out = to_tiled(ctx, model.output, s.t_out, nv, D, device)
     else:
         out = _dev(model.output, device)

@@ -104,6 +104,10 @@ SHAPES = {
     # small shapes for fast tests
     "tiny": ModelShape("tiny", 2, 256, 4, 2, 512, 1000),
     "small": ModelShape("small", 3, 512, 8, 2, 1536, 2048),
+    # a Q4/Q5/Q6 mix (as in the reference's 70B Q4_K_M file): Q5_K keys, gate/up,
+    # down and output head
+    "mix5": ModelShape("mix5", 2, 512, 8, 2, 1536, 2048, t_k=T_Q5K, t_gate=T_Q5K, t_up=T_Q5K,
+                       t_down=T_Q5K, t_out=T_Q5K),
 }
 
 

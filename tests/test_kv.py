@@ -146,14 +146,28 @@ def reference_q8():
 
 
 @pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64)])
-@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049, 9001, 20000])  # >= 8192: long-context loop
+@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049, 9001, 20000])  # >= 4096: split kernel
 @pytest.mark.parametrize("new_row", ["fused", "pre_appended"])
 def test_attend(oracle, ctx, H, KV, hd, seq, new_row):
+    check_attend(oracle, ctx, H, KV, hd, seq, new_row, seq + 8)
+
+
+@pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (64, 8, 128), (8, 1, 128)])
+@pytest.mark.parametrize("seq", [1, 65, 300, 700, 4000])
+def test_attend_long_cache(oracle, ctx, H, KV, hd, seq):
+    """A cache of 8192 positions attends with the split kernel at every
+    length: short ranges on the per-warp loop, splits of 256+ positions on the
+    long loop, partials merged in global memory; one KV head (a tensor-parallel
+    rank of the 70B shape) included."""
+    check_attend(oracle, ctx, H, KV, hd, seq, "fused", 8192)
+
+
+def check_attend(oracle, ctx, H, KV, hd, seq, new_row, cap):
     rng = np.random.default_rng(H * 131 + seq)
     k, v = kv_inputs(rng, seq, KV, hd)
     k[seq - 1, 5] = 3.0
     q = rng.normal(0, 1, H * hd).astype(np.float32)
-    kv = sc.KvCache(ctx, 1, KV, hd, seq + 8)
+    kv = sc.KvCache(ctx, 1, KV, hd, cap)
     try:
         kd, vd, qd = to_dev(k), to_dev(v), to_dev(q)
         n_pre = seq - 1 if new_row == "fused" else seq

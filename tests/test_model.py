@@ -144,6 +144,31 @@ def test_generate_layouts_match_oracle(oracle, ctx, layout):
     assert_logits(logits, l_ref)
 
 
+@pytest.mark.parametrize("layout", ["gguf", "all_tiled"])
+def test_generate_q5k_mix_matches_oracle(oracle, ctx, layout):
+    """A Q4/Q5/Q6 mix (Q5_K keys, gate/up, down and output head, as in the
+    reference's 70B Q4_K_M file): the Q5_K matrices run on their own matvec
+    (the key projection as a second launch next to Q and V, with RoPE),
+    the rest on the GEMV or the tensor-core matvec; greedy ids and logits
+    against the oracle, decode steps and the captured device loop."""
+    model = synth.make_model("mix5", seed=5)
+    rng = np.random.default_rng(15)
+    prompt = rng.integers(0, model.shape.n_vocab, 6).astype(np.uint32)
+    t_ref, l_ref = oracle.generate(model, prompt, 8)
+    dec = GpuDecoder(ctx, model, max_seq=64, tiled=(layout == "all_tiled"))
+    try:
+        logits = np.zeros_like(l_ref)
+        toks = dec.generate(prompt, 8, logits_out=logits)
+        dec.m.decode_steps(int(toks[0]), len(prompt), 7)
+        last = dec.m.last_token()
+        ctx.check()
+    finally:
+        dec.close()
+    assert np.array_equal(toks, t_ref)
+    assert_logits(logits, l_ref)
+    assert last == t_ref[-1]
+
+
 @pytest.mark.slow
 def test_tinyllama_shape_8_plus_16(oracle, ctx):
     """TinyLlama-1.1B shape (22 layers, d 2048, 32/4 heads, ffn 5632, vocab

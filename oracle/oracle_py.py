@@ -211,6 +211,7 @@ class Reference:
             "ref_engine_kv": (P, [P]),
             "ref_forward_layer": (I, [P, P, P, P, U32, U32, P]),
             "ref_generate_file": (I, [C.c_char_p, U32, P, U32, U32, P, P, P]),
+            "ref_tokenize": (I, [C.c_char_p, C.c_char_p, P, U32]),
             "ref_now": (C.c_double, []),
         }
         for n, (r, a) in sig.items():
@@ -250,6 +251,12 @@ class Reference:
         out = np.empty(n_embd, np.float32)
         assert self.L.ref_embed(_ptr(table), dtype, token, _ptr(out), n_embd) == 0
         return out
+
+    def tokenize_file(self, path, text: bytes, cap=1 << 16):
+        out = np.zeros(cap, np.uint32)
+        n = self.L.ref_tokenize(path.encode(), text, _ptr(out), cap)
+        assert n >= 0
+        return out[:min(n, cap)].copy()
 
     def generate_file(self, path, prompt, n_decode, n_vocab, depth=3):
         pr = np.ascontiguousarray(prompt, np.uint32)

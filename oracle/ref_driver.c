@@ -194,3 +194,23 @@ double ref_now(void) {
     clock_gettime(CLOCK_MONOTONIC, &ts);
     return ts.tv_sec + ts.tv_nsec * 1e-9;
 }
+
+/* model_tokenize (engine/src/model_loader.c:441-518) on a GGUF file's
+ * vocabulary: the ids (BOS first when the file names one), at most cap of
+ * them; returns the count or -1. */
+int ref_tokenize(const char *path, const char *text, uint32_t *out, uint32_t cap) {
+    struct model_config mcfg;
+    memset(&mcfg, 0, sizeof(mcfg));
+    mcfg.prefer_gguf = 1;
+    model_handle_t *m = model_open(path, &mcfg);
+    if (!m) return -1;
+    uint32_t *ids = NULL, n = 0;
+    int rc = model_tokenize(m, text, &ids, &n);
+    if (!rc) {
+        for (uint32_t i = 0; i < n && i < cap; ++i) out[i] = ids[i];
+        rc = (int)n;
+    }
+    free(ids);
+    model_close(m);
+    return rc;
+}

@@ -15,6 +15,7 @@
 #include "engine.h"
 
 #include <errno.h>
+#include <math.h>
 #include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -50,6 +51,8 @@ struct engine_handle {
     struct engine_config cfg;
     uint32_t n_layers, n_embd, n_heads, n_kv, head_dim, n_ff, n_vocab;
     char **vocab;
+    uint32_t *vocab_slot; /* open-addressing index: string -> lowest id (tokenizer) */
+    uint32_t vocab_cap, vocab_maxlen;
     int has_bos;
     uint32_t bos;
     struct layer_map *lm;
@@ -95,16 +98,52 @@ static int env_int(const char *name, int def) {
 
 static uint64_t al256(uint64_t x) { return (x + 255) & ~(uint64_t)255; }
 
+/* ------------------------------- debug ---------------------------------- */
+/* SHUKUCHI_DEBUG (set and not "0"), engine/src/engine.c:23-51: the quant
+ * types of every layer a token runs through, and for the first prompt token
+ * the embedding and layer 0's intermediates (min / max / mean / NaN / inf),
+ * computed through the op-level calls in the reference's op order. */
+
+static int debug_enabled(void) {
+    const char *e = getenv("SHUKUCHI_DEBUG");
+    return e && e[0] && strcmp(e, "0") != 0;
+}
+
+static void debug_stats(const char *name, const float *x, uint32_t n) {
+    if (!x || !n) {
+        printf("[DEBUG] %s: empty\n", name);
+        return;
+    }
+    float lo = x[0], hi = x[0], sum = 0.0f;
+    int nan = 0, inf = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const float v = x[i];
+        nan |= isnan(v) ? 1 : 0;
+        inf |= isinf(v) ? 1 : 0;
+        if (v < lo) lo = v;
+        if (v > hi) hi = v;
+        sum += v;
+    }
+    printf("[DEBUG] %s: min=%.4f max=%.4f mean=%.4f nan=%d inf=%d\n", name, lo, hi, sum / (float)n, nan, inf);
+}
+
+static int debug_dev(shk_ctx *c, const char *name, const float *dev, uint32_t n, float *host) {
+    if (shk_cuda_memcpy_d2h(c, host, dev, (size_t)n * 4, NULL) != SHK_OK || shk_cuda_sync(c, NULL) != SHK_OK)
+        return -1;
+    debug_stats(name, host, n);
+    return 0;
+}
+
+static void debug_dtypes(const struct shk_layer_desc *d) {
+    printf("[DEBUG] dtypes: q=%u k=%u v=%u o=%u gate=%u up=%u down=%u\n", d->attn_q_dtype, d->attn_k_dtype,
+           d->attn_v_dtype, d->attn_o_dtype, d->ffn_gate_dtype, d->ffn_up_dtype, d->ffn_down_dtype);
+}
+
 /* ------------------------------ model map ------------------------------- */
 
-static int map_model(struct engine_handle *h) {
+/* The tokenizer's vocabulary and BOS id (engine/src/model_loader.c:107-111). */
+static void map_vocab(struct engine_handle *h) {
     struct gguf_file *g = &h->g;
-    h->n_layers = (uint32_t)gguf_get_uint(g, "llama.block_count", 0);
-    h->n_embd = (uint32_t)gguf_get_uint(g, "llama.embedding_length", 0);
-    h->n_heads = (uint32_t)gguf_get_uint(g, "llama.attention.head_count", 0);
-    h->n_kv = (uint32_t)gguf_get_uint(g, "llama.attention.head_count_kv", h->n_heads);
-    if (!h->n_layers || !h->n_embd || !h->n_heads || !h->n_kv || h->n_embd % h->n_heads) return -1;
-    h->head_dim = h->n_embd / h->n_heads;
     const struct gguf_value *tok = gguf_get(g, "tokenizer.ggml.tokens");
     if (tok && tok->type == GGUF_ARRAY && tok->arr_type == GGUF_STRING && tok->arr_n) {
         h->vocab = tok->arr_str;
@@ -115,6 +154,17 @@ static int map_model(struct engine_handle *h) {
         h->has_bos = 1;
         h->bos = (uint32_t)bos->u;
     }
+}
+
+static int map_model(struct engine_handle *h) {
+    struct gguf_file *g = &h->g;
+    h->n_layers = (uint32_t)gguf_get_uint(g, "llama.block_count", 0);
+    h->n_embd = (uint32_t)gguf_get_uint(g, "llama.embedding_length", 0);
+    h->n_heads = (uint32_t)gguf_get_uint(g, "llama.attention.head_count", 0);
+    h->n_kv = (uint32_t)gguf_get_uint(g, "llama.attention.head_count_kv", h->n_heads);
+    if (!h->n_layers || !h->n_embd || !h->n_heads || !h->n_kv || h->n_embd % h->n_heads) return -1;
+    h->head_dim = h->n_embd / h->n_heads;
+    map_vocab(h);
     const struct gguf_tensor_info *out = gguf_find_tensor(g, "output.weight");
     const struct gguf_tensor_info *emb = gguf_find_tensor(g, "token_embd.weight");
     if (!out || !emb || out->n_dims != 2 || emb->n_dims != 2) return -1;
@@ -144,7 +194,7 @@ static int map_model(struct engine_handle *h) {
             tl->row_bytes = ti->size / tl->rows;
             const int norm = t == TN_ATTN_NORM || t == TN_FFN_NORM;
             if (norm && ti->type != 0) return -1; /* F32 norm weights */
-            if (!norm && ti->type != 12 && ti->type != 14) return -1; /* Q4_K / Q6_K */
+            if (!norm && ti->type != 12 && ti->type != 13 && ti->type != 14) return -1; /* Q4_K / Q5_K / Q6_K */
             tl->dev_row = 0;
             if (!norm && tl->row_bytes % 16) {
                 /* Q6_K rows of a width that is not a multiple of 2048: pad to
@@ -216,6 +266,71 @@ static void layer_desc(struct engine_handle *h, uint32_t l, const uint8_t *base,
 #undef DT
     d->row_stride_v = (uint32_t)L->t[TN_V].dev_row;
     d->row_stride_down = (uint32_t)L->t[TN_DOWN].dev_row;
+}
+
+/* Layer 0 at position 0 for SHUKUCHI_DEBUG: engine/src/engine.c:105-221's
+ * op order (RMSNorm, Q/K/V matvecs, RoPE, Q8_0 append and read-back,
+ * attention, O, residual, RMSNorm, gate/up, SwiGLU, down, residual) on
+ * scratch buffers and a one-position scratch KV cache, so the real pass that
+ * follows is untouched.  `hidden` is the embedded token (device). */
+static int debug_layer0(struct engine_handle *h, const struct shk_layer_desc *d, const float *hidden) {
+    shk_ctx *c = h->ctx;
+    const uint32_t D = h->n_embd, hd = h->head_dim, qd = h->n_heads * hd, kvd = h->n_kv * hd, F = h->n_ff;
+    const uint32_t big = (D > F ? D : F) > qd ? (D > F ? D : F) : qd;
+    float *host = (float *)malloc((size_t)big * 4), *hres = (float *)malloc((size_t)D * 4);
+    float *buf[12] = {0};
+    enum { NRM, Q, K, V, KC, VC, ATT, PRJ, HID, G, U, HM };
+    const uint32_t sz[12] = {D, qd, kvd, kvd, kvd, kvd, qd, D, D, F, F, F};
+    struct shk_kv_config kc = {1, h->n_kv, hd, 32, 8};
+    shk_kv *kv = shk_cuda_kv_create(c, &kc);
+    int rc = (!host || !hres || !kv) ? -1 : 0;
+    for (int i = 0; !rc && i < 12; ++i) rc = shk_cuda_dev_alloc(c, (size_t)sz[i] * 4, (void **)&buf[i]) != SHK_OK;
+#define OK(x) (!rc && (rc = ((x) != SHK_OK)) == 0)
+#define DUMP(name, i, n) (!rc && (rc = debug_dev(c, name, buf[i], n, host)) == 0)
+    OK(shk_cuda_rmsnorm(c, hidden, d->attn_norm, buf[NRM], D, NULL));
+    DUMP("attn_norm", NRM, D);
+    OK(shk_cuda_matvec(c, d->attn_q_dtype, d->attn_q, 0, buf[NRM], buf[Q], qd, D, NULL));
+    DUMP("Q", Q, qd);
+    OK(shk_cuda_matvec(c, d->attn_k_dtype, d->attn_k, 0, buf[NRM], buf[K], kvd, D, NULL));
+    DUMP("K", K, kvd);
+    OK(shk_cuda_matvec(c, d->attn_v_dtype, d->attn_v, d->row_stride_v, buf[NRM], buf[V], kvd, D, NULL));
+    DUMP("V", V, kvd);
+    OK(shk_cuda_rope(c, buf[Q], h->n_heads, hd, 0, 10000.0f, NULL));
+    OK(shk_cuda_rope(c, buf[K], h->n_kv, hd, 0, 10000.0f, NULL));
+    DUMP("Q_rope", Q, qd);
+    DUMP("K_rope", K, kvd);
+    OK(shk_cuda_kv_append(kv, 0, 0, buf[K], buf[V], NULL));
+    OK(shk_cuda_kv_read_range(kv, 0, 0, 1, buf[KC], buf[VC], NULL));
+    DUMP("K_cache", KC, kvd);
+    DUMP("V_cache", VC, kvd);
+    OK(shk_cuda_kv_attend(kv, 0, buf[Q], NULL, NULL, buf[ATT], h->n_heads, 1, 1.0f / sqrtf((float)hd), NULL));
+    DUMP("attn_out", ATT, qd);
+    OK(shk_cuda_matvec(c, d->attn_o_dtype, d->attn_o, 0, buf[ATT], buf[PRJ], D, qd, NULL));
+    DUMP("attn_proj", PRJ, D);
+    /* residual on the host: hidden + attn_proj */
+    OK(shk_cuda_memcpy_d2h(c, hres, hidden, (size_t)D * 4, NULL));
+    OK(shk_cuda_sync(c, NULL));
+    for (uint32_t i = 0; !rc && i < D; ++i) hres[i] += host[i];
+    if (!rc) debug_stats("hidden_after_attn", hres, D);
+    OK(shk_cuda_memcpy_h2d(c, buf[HID], hres, (size_t)D * 4, NULL));
+    OK(shk_cuda_rmsnorm(c, buf[HID], d->ffn_norm, buf[NRM], D, NULL));
+    DUMP("ffn_norm", NRM, D);
+    OK(shk_cuda_matvec(c, d->ffn_gate_dtype, d->ffn_gate, 0, buf[NRM], buf[G], F, D, NULL));
+    OK(shk_cuda_matvec(c, d->ffn_up_dtype, d->ffn_up, 0, buf[NRM], buf[U], F, D, NULL));
+    OK(shk_cuda_swiglu(c, buf[G], buf[U], buf[HM], F, NULL));
+    OK(shk_cuda_matvec(c, d->ffn_down_dtype, d->ffn_down, d->row_stride_down, buf[HM], buf[PRJ], D, F, NULL));
+    DUMP("mlp_out", PRJ, D);
+    for (uint32_t i = 0; !rc && i < D; ++i) hres[i] += host[i];
+    if (!rc) debug_stats("hidden_after_mlp", hres, D);
+    OK(shk_cuda_check(c));
+#undef OK
+#undef DUMP
+    for (int i = 0; i < 12; ++i)
+        if (buf[i]) shk_cuda_dev_free(c, buf[i]);
+    if (kv) shk_cuda_kv_destroy(kv);
+    free(host);
+    free(hres);
+    return rc ? -1 : 0;
 }
 
 /* ------------------------------- loader --------------------------------- */
@@ -313,13 +428,60 @@ static int register_layers(struct engine_handle *h) {
 }
 
 /* ------------------------------ tokenizer ------------------------------- */
+/* Greedy longest match (engine/src/model_loader.c:483-513 scans the whole
+ * vocabulary for every position: O(V * len)).  Here the vocabulary is hashed
+ * once; at each position the candidate lengths are tried from the longest
+ * vocabulary string down, so the first hit is the longest match, and among
+ * equal strings the index keeps the lowest id -- the reference's choice
+ * (strictly longer matches replace, ties keep the first). */
+
+static uint64_t str_hash(const char *p, size_t n) {
+    uint64_t x = 1469598103934665603ull; /* FNV-1a */
+    for (size_t i = 0; i < n; ++i) x = (x ^ (uint8_t)p[i]) * 1099511628211ull;
+    return x;
+}
+
+static int vocab_index_build(struct engine_handle *h) {
+    if (!h->vocab || !h->n_vocab) return 0;
+    uint32_t cap = 1;
+    while (cap < 2u * h->n_vocab) cap <<= 1;
+    h->vocab_slot = (uint32_t *)malloc((size_t)cap * sizeof(uint32_t));
+    if (!h->vocab_slot) return -1;
+    memset(h->vocab_slot, 0xFF, (size_t)cap * sizeof(uint32_t));
+    h->vocab_cap = cap;
+    for (uint32_t t = 0; t < h->n_vocab; ++t) {
+        const char *v = h->vocab[t];
+        const size_t n = strlen(v);
+        if (!n) continue;
+        if (n > h->vocab_maxlen) h->vocab_maxlen = (uint32_t)n;
+        for (uint32_t i = (uint32_t)str_hash(v, n) & (cap - 1);; i = (i + 1) & (cap - 1)) {
+            const uint32_t id = h->vocab_slot[i];
+            if (id == UINT32_MAX) {
+                h->vocab_slot[i] = t;
+                break;
+            }
+            if (strlen(h->vocab[id]) == n && memcmp(h->vocab[id], v, n) == 0) break; /* keep the first */
+        }
+    }
+    return 0;
+}
+
+static uint32_t vocab_find(const struct engine_handle *h, const char *p, size_t n) {
+    for (uint32_t i = (uint32_t)str_hash(p, n) & (h->vocab_cap - 1);; i = (i + 1) & (h->vocab_cap - 1)) {
+        const uint32_t id = h->vocab_slot[i];
+        if (id == UINT32_MAX) return UINT32_MAX;
+        const char *v = h->vocab[id];
+        if (strncmp(v, p, n) == 0 && v[n] == '\0') return id;
+    }
+}
 
 static int tokenize(struct engine_handle *h, const char *text, uint32_t **out, uint32_t *n_out) {
     *out = NULL;
     *n_out = 0;
     const size_t len = text ? strlen(text) : 0;
     char *norm = (char *)malloc(3 * len + 1);
-    uint32_t *ids = (uint32_t *)malloc((len + 2) * sizeof(uint32_t));
+    /* one id per normalised byte at most (unknown bytes), plus BOS */
+    uint32_t *ids = (uint32_t *)malloc((3 * len + 2) * sizeof(uint32_t));
     if (!norm || !ids) {
         free(norm);
         free(ids);
@@ -341,16 +503,18 @@ static int tokenize(struct engine_handle *h, const char *text, uint32_t **out, u
     for (size_t i = 0; i < nl;) {
         size_t best = 0;
         uint32_t best_id = 0;
-        for (uint32_t t = 0; h->vocab && t < h->n_vocab; ++t) {
-            const char *s = h->vocab[t];
-            const size_t sl = strlen(s);
-            if (sl > best && sl <= nl - i && memcmp(s, norm + i, sl) == 0) {
-                best = sl;
-                best_id = t;
+        if (h->vocab_slot) {
+            size_t len = nl - i < h->vocab_maxlen ? nl - i : h->vocab_maxlen;
+            for (; len > 0; --len) {
+                const uint32_t id = vocab_find(h, norm + i, len);
+                if (id != UINT32_MAX) {
+                    best = len;
+                    best_id = id;
+                    break;
+                }
             }
         }
         if (!best) best = 1; /* unknown byte: token 0 */
-        if (n >= len + 2) break;
         ids[n++] = best_id;
         i += best;
     }
@@ -399,17 +563,44 @@ static void note_rss(struct engine_handle *h) {
  * is returned in *next (and the logits copied to `logits` when given). */
 static int step(struct engine_handle *h, uint32_t tok, int want_next, uint32_t *next, float *logits) {
     if (h->pos >= h->max_seq) return -1;
+    const int dbg = debug_enabled();
     if (h->resident) {
         if (register_layers(h)) return -1;
+        if (dbg) {
+            if (h->pos == 0) { /* the embedded first token and layer 0's intermediates */
+                if (shk_cuda_model_embed(h->m, tok, NULL) != SHK_OK) return -1;
+                float *emb = (float *)malloc((size_t)h->n_embd * 4);
+                const int r = !emb || debug_dev(h->ctx, "embed", shk_cuda_model_hidden(h->m), h->n_embd, emb);
+                free(emb);
+                struct shk_layer_desc d0;
+                layer_desc(h, 0, (const uint8_t *)h->d_buf[0], &d0);
+                if (r || debug_layer0(h, &d0, shk_cuda_model_hidden(h->m))) return -1;
+            }
+            for (uint32_t l = 0; l < h->n_layers; ++l) {
+                struct shk_layer_desc d;
+                layer_desc(h, l, (const uint8_t *)h->d_buf[l], &d);
+                debug_dtypes(&d);
+            }
+        }
         if (shk_cuda_token_step(h->m, tok, h->pos, want_next, next, logits) != SHK_OK) return -1;
     } else {
         if (shk_cuda_model_embed(h->m, tok, NULL) != SHK_OK) return -1;
         float *hidden = shk_cuda_model_hidden(h->m);
+        if (dbg && h->pos == 0) {
+            float *emb = (float *)malloc((size_t)h->n_embd * 4);
+            const int r = !emb || debug_dev(h->ctx, "embed", hidden, h->n_embd, emb);
+            free(emb);
+            if (r) return -1;
+        }
         for (uint32_t l = 0; l < h->n_layers; ++l) {
             const uint64_t k = h->ring_next++; /* k % n_layers == l: passes run whole */
             if (acquire(h, k)) return -1;
             struct shk_layer_desc d;
             layer_desc(h, l, (const uint8_t *)h->d_buf[k % h->depth], &d);
+            if (dbg) {
+                debug_dtypes(&d);
+                if (l == 0 && h->pos == 0 && debug_layer0(h, &d, hidden)) return -1;
+            }
             if (shk_cuda_forward_layer(h->m, &d, l, h->pos, hidden, NULL) != SHK_OK) return -1;
             consume(h, k);
         }
@@ -488,6 +679,7 @@ void engine_close(engine_handle_t *h) {
     free(h->d_buf);
     free(h->pinned);
     free(h->lm);
+    free(h->vocab_slot);
     free(h->prompt);
     free(h->out_ids);
     free(h->text);
@@ -510,7 +702,7 @@ engine_handle_t *engine_open(const char *model_path, const struct engine_config 
     if (h->depth > 3) h->depth = 3;
     h->resident = env_int("SHUKUCHI_HBM_RESIDENT", 1) != 0;
     h->max_seq = (uint32_t)env_int("SHUKUCHI_MAX_SEQ", 2048);
-    if (gguf_open(model_path, &h->g) || map_model(h)) goto fail;
+    if (gguf_open(model_path, &h->g) || map_model(h) || vocab_index_build(h)) goto fail;
     struct shk_cuda_config cc = {env_int("SHUKUCHI_DEVICE", 0), 0};
     h->ctx = shk_cuda_init(&cc);
     if (!h->ctx) goto fail;
@@ -604,6 +796,32 @@ int engine_get_streaming_stats(engine_handle_t *h, struct streaming_stats *out) 
 }
 
 uint32_t engine_vocab_size(engine_handle_t *h) { return h ? h->n_vocab : 0; }
+
+void engine_report(engine_handle_t *h) {
+    if (h && h->ctx) shk_cuda_report(h->ctx);
+}
+
+int engine_tokenize_file(const char *model_path, const char *text, uint32_t *out, uint32_t cap) {
+    struct engine_handle *h = (struct engine_handle *)calloc(1, sizeof(*h));
+    if (!h) return -1;
+    h->g.fd = -1;
+    int rc = gguf_open(model_path, &h->g);
+    if (!rc) {
+        map_vocab(h);
+        rc = vocab_index_build(h);
+    }
+    uint32_t *ids = NULL, n = 0;
+    if (!rc) rc = tokenize(h, text, &ids, &n);
+    if (!rc) {
+        for (uint32_t i = 0; i < n && i < cap; ++i) out[i] = ids[i];
+        rc = (int)n;
+    }
+    free(ids);
+    free(h->vocab_slot);
+    gguf_close(&h->g);
+    free(h);
+    return rc;
+}
 
 int engine_inspect(const char *model_path, uint32_t out[6], uint64_t *max_layer_bytes) {
     struct engine_handle *h = (struct engine_handle *)calloc(1, sizeof(*h));

@@ -2,7 +2,8 @@
  * reference: same functions, same structs) running its decode on the B200
  * path of libshk_cuda.so.
  *
- * Model files are GGUF (llama architecture, Q4_K / Q6_K weights, F32 norms).
+ * Model files are GGUF (llama architecture, Q4_K / Q5_K / Q6_K weights, F32
+ * norms).
  * Layer weights reach HBM through the streaming loader: a loader thread
  * pread()s each layer's contiguous span into pinned host staging (depth
  * `prefetch_depth`, 2 or 3 buffers) and queues cudaMemcpyAsync copies into
@@ -18,6 +19,10 @@
  *                          prefetch_depth device slots on every token, as the
  *                          reference streams them from disk
  *   SHUKUCHI_MAX_SEQ       KV-cache capacity in positions (default 2048)
+ *   SHUKUCHI_DEBUG         set and not "0": per-layer quant types and, for
+ *                          the first prompt token, the embedding's and layer
+ *                          0's intermediate statistics on stdout, as the
+ *                          reference prints them (engine/src/engine.c:23-51)
  */
 #ifndef SHK_ENGINE_H
 #define SHK_ENGINE_H
@@ -69,6 +74,13 @@ int engine_get_streaming_stats(engine_handle_t *h, struct streaming_stats *out);
 int engine_generate_ids(engine_handle_t *h, const uint32_t *prompt, uint32_t n_prompt,
                         uint32_t n_decode, uint32_t *out_ids, float *out_logits);
 uint32_t engine_vocab_size(engine_handle_t *h);
+/* The GPU backend's counters on stderr (matvec calls, layer forwards, token
+ * steps, staged copies and bytes): the CLI's closing report, as the
+ * reference's main prints metal_ops_report() (engine/src/main.c:106). */
+void engine_report(engine_handle_t *h);
+/* The prompt tokenizer alone (no GPU needed): the ids of `text` under a GGUF
+ * file's vocabulary, at most cap of them; returns the count or -1. */
+int engine_tokenize_file(const char *model_path, const char *text, uint32_t *out, uint32_t cap);
 /* Parses a model file's header only (no GPU needed): layers, width, heads,
  * KV heads, FFN width, vocabulary, largest layer span.  0 on success. */
 int engine_inspect(const char *model_path, uint32_t out[6], uint64_t *max_layer_bytes);

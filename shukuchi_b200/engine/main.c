@@ -63,6 +63,7 @@ int main(int argc, char **argv) {
                 (unsigned long long)st.layer_loads, (unsigned long long)st.layer_bytes_read, st.max_layer_size,
                 st.peak_buffer_usage, st.peak_rss, st.max_concurrent_buffers, st.prefetch_hits,
                 st.prefetch_misses);
+    engine_report(h); /* engine/src/main.c:106 metal_ops_report() */
     engine_close(h);
     struct rusage ru;
     if (getrusage(RUSAGE_SELF, &ru) == 0) fprintf(stderr, "peak_rss_mb=%.2f\n", (double)ru.ru_maxrss / 1024.0);

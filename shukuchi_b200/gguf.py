@@ -71,15 +71,22 @@ def model_tensors(model: Model):
     return t
 
 
-def write_model(path: str, model: Model, rope_theta: float = 10000.0) -> None:
+def write_model(path: str, model: Model, rope_theta: float = 10000.0, tokens: list | None = None,
+                bos: int | None = None) -> None:
+    """tokens: the vocabulary strings (default: fixed-width token_text ids);
+    bos: tokenizer.ggml.bos_token_id (default: none, so no BOS is prepended)."""
     s = model.shape
     tensors = model_tensors(model)
+    vocab = tokens if tokens is not None else [token_text(i) for i in range(s.n_vocab)]
+    assert len(vocab) == s.n_vocab
     kvs = [_kv_str("general.architecture", "llama"), _kv_u32("general.alignment", ALIGN),
            _kv_u32("llama.block_count", s.n_layers), _kv_u32("llama.embedding_length", s.n_embd),
            _kv_u32("llama.feed_forward_length", s.n_ff), _kv_u32("llama.attention.head_count", s.n_heads),
            _kv_u32("llama.attention.head_count_kv", s.n_kv_heads),
            _kv_f32("llama.rope.freq_base", rope_theta),
-           _kv_str_array("tokenizer.ggml.tokens", [token_text(i) for i in range(s.n_vocab)])]
+           _kv_str_array("tokenizer.ggml.tokens", vocab)]
+    if bos is not None:
+        kvs.append(_kv_u32("tokenizer.ggml.bos_token_id", bos))
     infos, offs, off = [], [], 0
     for name, typ, dims, data in tensors:
         off = (off + ALIGN - 1) // ALIGN * ALIGN

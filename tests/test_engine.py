@@ -121,6 +121,45 @@ def test_engine_text_prompt_matches_reference_cli(model_file, reference):
     assert text == "".join(f"<{i}>t{i:05d}" for i in ids)
 
 
+def tokenizer_vocab(n: int, rng) -> list:
+    """A vocabulary that exercises greedy longest match: nested prefixes,
+    U+2581 word pieces, multi-byte UTF-8, duplicated strings (the lowest id
+    must win), an empty string, then random filler pieces."""
+    head = ["", "\u2581", "\u2581the", "the", "th", "t", "he", "h", "e", "\u2581t", "a", "ab", "abc", "abcd",
+            "abc", "b", "c", "d", "\u00e9", "\u65e5\u672c", "\u65e5", "\u2581\u2581", "x", "xy", "xyz", "\u2581a",
+            "lo", "low", "lower", "\u2581low", "e\u2581", "\u672c"]
+    alpha = list("abcdehltxyz") + ["\u2581", "\u00e9", "\u65e5"]
+    vocab = list(head)
+    while len(vocab) < n:
+        k = int(rng.integers(1, 7))
+        vocab.append("".join(alpha[int(i)] for i in rng.integers(0, len(alpha), k)))
+    return vocab
+
+
+@pytest.mark.parametrize("bos", [None, 7])
+def test_tokenizer_matches_reference(tmp_path, reference, bos):
+    """The engine's hashed greedy tokenizer (no GPU) gives the reference's
+    model_tokenize ids (engine/src/model_loader.c:441-518) on prompts with
+    spaces, tabs, newlines, unknown bytes and multi-byte characters."""
+    rng = np.random.default_rng(4)
+    m = synth.make_model("tiny", seed=1)
+    vocab = tokenizer_vocab(m.shape.n_vocab, rng)
+    p = str(tmp_path / "tok.gguf")
+    gguf.write_model(p, m, tokens=vocab, bos=bos)
+    L = lib()
+    L.engine_tokenize_file.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32]
+    alpha = list("abcdehltxyz qQ\t\n") + ["\u00e9", "\u65e5", "\u672c", "\u00fc"]
+    texts = ["the lower abcd", "  the\tthe\nthe\r", "QQQ", "", "\u65e5\u672c\u65e5 \u00e9\u00e9",
+             "lowerlowestabcabcd", "".join(alpha[int(i)] for i in rng.integers(0, len(alpha), 3000))]
+    for t in texts:
+        b = t.encode()
+        want = reference.tokenize_file(p, b)
+        out = np.zeros(len(b) * 3 + 8, np.uint32)
+        n = L.engine_tokenize_file(p.encode(), b, out.ctypes.data, out.size)
+        assert n == len(want), (t[:40], n, len(want))
+        assert np.array_equal(out[:n], want), t[:40]
+
+
 def test_inspect_rejects_broken_files(model_file, tmp_path):
     """Host-side failures (no GPU): a truncated file, a missing layer tensor
     and a file that is not GGUF are refused at open time with -1."""

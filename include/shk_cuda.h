@@ -293,6 +293,12 @@ int shk_cuda_layer_stage(shk_ctx *ctx, uint32_t slot, void *dst_dev, const void 
  * (pads Q6_K rows to 16-byte multiples). */
 int shk_cuda_layer_stage_rows(shk_ctx *ctx, uint32_t slot, void *dst_dev, size_t dst_row_bytes,
                               const void *pinned_src, size_t src_row_bytes, size_t rows);
+/* General strided copy: `rows` runs of `width` bytes, src_pitch apart in the
+ * pinned blob, to dst_pitch apart in HBM -- a tensor-parallel rank's column
+ * shard of a matrix (its block range of every row) or its row range.  No
+ * counterpart in the reference (it has no tensor parallelism). */
+int shk_cuda_layer_stage_2d(shk_ctx *ctx, uint32_t slot, void *dst_dev, size_t dst_pitch,
+                            const void *pinned_src, size_t src_pitch, size_t width, size_t rows);
 /* Converts Q6_K rows just staged into dst_dev (rows x k elements, row_stride
  * bytes apart, 0 = dense) to the planar layout, in place, on the copy stream
  * after the slot's copies; the slot's commit covers it.  Callable from the

@@ -1756,6 +1756,21 @@ int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_r
   return SHK_OK;
 }
 
+int shk_cuda_layer_stage_2d(shk_ctx* c, uint32_t slot, void* dst, size_t dst_pitch, const void* src,
+                            size_t src_pitch, size_t width, size_t rows) {
+  if (!c || !dst || !src || width > dst_pitch || width > src_pitch) return SHK_EINVAL;
+  if (!width || !rows) return SHK_OK;
+  const int rc = stage_prepare(c, slot);
+  if (rc) return rc;
+  CK(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width, rows, cudaMemcpyHostToDevice, c->copy));
+  {
+    std::lock_guard<std::mutex> g(c->stage_mu);
+    c->n_staged++;
+    c->bytes_staged += width * rows;
+  }
+  return SHK_OK;
+}
+
 int shk_cuda_layer_stage_q6k_planar(shk_ctx* c, uint32_t slot, void* dst, uint32_t rows, uint32_t k,
                                     uint32_t row_stride) {
   if (!c || !dst || k == 0 || k % QK) return SHK_EINVAL;

@@ -46,6 +46,27 @@ struct layer_map {
     uint64_t dev_bytes;
 };
 
+struct tp_layout { /* one rank's slices (tensor parallelism, see below) */
+    uint32_t A, kv_lo, kv_hi, o_lo, o_hi, f_lo, f_hi, v_lo, v_hi;
+};
+
+struct tp_rank {
+    uint32_t rank;
+    struct tp_layout lay;
+    shk_ctx *ctx;
+    shk_kv *kv;
+    shk_model *m;
+    void *d_embd, *d_out;
+    void **d_buf;              /* one per layer (resident) */
+    struct shk_layer_desc *ld; /* per layer */
+    /* a generation's inputs and results (rank threads) */
+    const uint32_t *prompt;
+    uint32_t n_prompt, n_decode;
+    int want_logits; /* rank 0 copies logits: every rank gathers on the same steps */
+    float *lg;       /* n_vocab floats of scratch for those copies */
+    int rc;
+};
+
 struct engine_handle {
     struct gguf_file g;
     struct engine_config cfg;
@@ -80,6 +101,12 @@ struct engine_handle {
     struct streaming_stats st;
     int registered;
 
+    /* tensor parallelism (SHUKUCHI_TP = world > 1): one GPU and context per
+     * rank; ranks[0] is also ctx/kv/m above */
+    uint32_t tp;
+    struct tp_rank *ranks;
+    int tp_broken;
+
     char *prompt;
     uint32_t *out_ids;
     size_t n_out, cap_out;
@@ -89,6 +116,8 @@ struct engine_handle {
     uint32_t pos;      /* next KV position */
     uint64_t ring_next; /* ring mode: next loader request to consume */
 };
+
+static void *tp_rank_main(void *arg);
 
 static int env_int(const char *name, int def) {
     const char *v = getenv(name);
@@ -563,7 +592,7 @@ static void note_rss(struct engine_handle *h) {
  * is returned in *next (and the logits copied to `logits` when given). */
 static int step(struct engine_handle *h, uint32_t tok, int want_next, uint32_t *next, float *logits) {
     if (h->pos >= h->max_seq) return -1;
-    const int dbg = debug_enabled();
+    const int dbg = debug_enabled() && h->tp <= 1; /* the dumps run the unsharded layer */
     if (h->resident) {
         if (register_layers(h)) return -1;
         if (dbg) {
@@ -634,23 +663,444 @@ static int generate(struct engine_handle *h, const uint32_t *prompt, uint32_t n_
         pthread_cond_broadcast(&h->cv);
         pthread_mutex_unlock(&h->mu);
     }
-    uint32_t next = 0;
-    for (uint32_t i = 0; i < n_prompt; ++i) {
+    for (uint32_t i = 0; i < n_prompt; ++i)
         if (prompt[i] >= h->n_vocab) return -1;
-        const int last = i + 1 == n_prompt;
-        if (step(h, prompt[i], last, &next, last ? logits_out : NULL)) return -1;
+    /* tensor parallel: ranks 1.. run the same steps on their own threads */
+    pthread_t th[8];
+    uint32_t started = 0;
+    if (h->tp > 1) {
+        if (h->tp_broken) return -1;
+        for (uint32_t ri = 1; ri < h->tp; ++ri) {
+            struct tp_rank *r = &h->ranks[ri];
+            r->prompt = prompt;
+            r->n_prompt = n_prompt;
+            r->n_decode = n_decode;
+            r->want_logits = logits_out != NULL;
+            if (r->want_logits && !r->lg && !(r->lg = (float *)malloc((size_t)h->n_vocab * 4))) break;
+            if (pthread_create(&th[ri], NULL, tp_rank_main, r) != 0) break;
+            started = ri;
+        }
+        if (started + 1 != h->tp) {
+            h->tp_broken = 1; /* the started ranks wait for rank 0 in their collectives */
+            return -1;
+        }
     }
-    for (uint32_t j = 0; j < n_decode && !h->cancel; ++j) {
-        if (emit(h, next, cb, user, print)) return -1;
+    int rc = 0;
+    uint32_t next = 0;
+    for (uint32_t i = 0; i < n_prompt && !rc; ++i) {
+        const int last = i + 1 == n_prompt;
+        rc = step(h, prompt[i], last, &next, last ? logits_out : NULL);
+    }
+    /* cancellation ends a generation between tokens; tensor-parallel ranks
+     * run every step in lockstep, so there it takes effect at the end */
+    for (uint32_t j = 0; j < n_decode && !rc && (h->tp > 1 || !h->cancel); ++j) {
+        rc = emit(h, next, cb, user, print);
         const int want = j + 1 < n_decode;
         float *lg = (want && logits_out) ? logits_out + (size_t)(j + 1) * h->n_vocab : NULL;
         uint32_t nx = 0;
-        if (step(h, next, want, &nx, lg)) return -1;
+        if (!rc) rc = step(h, next, want, &nx, lg);
         if (want) next = nx;
         note_rss(h);
     }
+    if (h->tp > 1) {
+        if (rc) {
+            h->tp_broken = 1; /* ranks left blocked in a collective: the handle is unusable */
+            return -1;
+        }
+        for (uint32_t ri = 1; ri < h->tp; ++ri) {
+            pthread_join(th[ri], NULL);
+            rc |= h->ranks[ri].rc;
+        }
+    }
+    if (rc) return -1;
     if (print) printf("\n");
     return 0;
+}
+
+/* ------------------------- tensor parallelism ---------------------------- */
+/* SHUKUCHI_TP = 2, 4 or 8 (resident mode): one GPU (SHUKUCHI_DEVICE + r),
+ * context and thread per rank, an NCCL communicator across them.  The split
+ * is the north-star one, and the same as the Python side's
+ * shukuchi_b200/tp.py: Wq/Wk/Wv and gate/up are cut by output rows, Wo and
+ * down by input columns in whole 256-element blocks, KV heads stay local to a
+ * rank.  Query head h reads KV head h % n_kv (engine/src/ops.c:423), so a rank
+ * owning KV heads [kv_lo, kv_hi) owns the query heads whose h % n_kv falls
+ * there, stored in the order (group g, KV head j).  When one KV head per rank
+ * would leave Wo column groups that are not whole blocks, A ranks share the
+ * heads and split the O projection's output rows.  The output head is split
+ * by vocabulary rows when n_vocab divides by the world (argmax merged over
+ * the ranks on the device), else replicated.  Each layer's span is read once
+ * into pinned staging and every rank copies its slices out of it with
+ * strided copies on its own copy stream. */
+
+int engine_tp_layout(const uint32_t shape[6], uint32_t rank, uint32_t world, uint32_t out[9]) {
+    const uint32_t D = shape[0], H = shape[1], KV = shape[2], hd = shape[3], F = shape[4], V = shape[5];
+    if (!world || rank >= world || !KV || !H || H % KV || F % 256 || F / 256 < world) return -1;
+    uint32_t A = 0, kvp = 0;
+    for (uint32_t a = 1; a <= world && !A; ++a) {
+        if (world % a || (KV * a) % world || D % a) continue;
+        kvp = KV * a / world;
+        if ((kvp * hd) % 256 == 0 || (kvp == KV && (H * hd) % 256 == 0)) A = a;
+    }
+    if (!A) return -1;
+    const uint32_t g = rank / A, ar = rank % A, rows = D / A, fb = F / 256;
+    out[0] = A;
+    out[1] = g * kvp;
+    out[2] = (g + 1) * kvp;
+    out[3] = ar * rows;
+    out[4] = (ar + 1) * rows;
+    out[5] = (uint32_t)((uint64_t)rank * fb / world) * 256;
+    out[6] = (uint32_t)((uint64_t)(rank + 1) * fb / world) * 256;
+    out[7] = V % world == 0 ? rank * (V / world) : 0;
+    out[8] = V % world == 0 ? (rank + 1) * (V / world) : V;
+    return 0;
+}
+
+static uint64_t blk_bytes(uint32_t type) { return type == 12 ? 144 : type == 13 ? 176 : type == 14 ? 210 : 0; }
+
+struct piece {             /* one strided copy out of the layer's pinned span */
+    uint64_t src_off;      /* from the tensor's first byte */
+    uint64_t src_pitch, width, rows;
+    uint64_t dst_off;      /* from the shard's first byte */
+};
+struct shard {
+    uint64_t rows, cols, pitch; /* shard rows, elements per row, bytes between rows */
+    int padded;                 /* pitch > dense row bytes (Q6_K V / down) */
+    uint32_t np;
+    struct piece p[8];
+};
+
+/* Rank `lay`'s slice of tensor t of layer l. */
+static int tp_shard(const struct engine_handle *h, const struct tensor_loc *tl, int t, const struct tp_layout *lay,
+                    struct shard *sh) {
+    const uint64_t hd = h->head_dim, KV = h->n_kv, G = h->n_heads / h->n_kv, kvp = lay->kv_hi - lay->kv_lo;
+    const uint64_t rb = tl->row_bytes, bb = blk_bytes(tl->type);
+    memset(sh, 0, sizeof(*sh));
+    if (t == TN_ATTN_NORM || t == TN_FFN_NORM) {
+        sh->rows = 1;
+        sh->cols = tl->size / 4;
+        sh->pitch = tl->size;
+        sh->np = 1;
+        sh->p[0] = (struct piece){0, tl->size, tl->size, 1, 0};
+        return 0;
+    }
+    if (!bb || rb % bb) return -1;
+    const uint64_t full_cols = rb / bb * 256;
+    uint64_t width = rb;
+    switch (t) {
+    case TN_Q:
+        sh->rows = G * kvp * hd;
+        sh->cols = full_cols;
+        if (G > 8) return -1;
+        for (uint64_t g = 0; g < G; ++g)
+            sh->p[sh->np++] = (struct piece){(g * KV + lay->kv_lo) * hd * rb, rb, rb, kvp * hd, g * kvp * hd};
+        break;
+    case TN_K:
+    case TN_V:
+        sh->rows = kvp * hd;
+        sh->cols = full_cols;
+        sh->p[sh->np++] = (struct piece){lay->kv_lo * hd * rb, rb, rb, kvp * hd, 0};
+        break;
+    case TN_O: {
+        sh->rows = lay->o_hi - lay->o_lo;
+        /* column ranges of this rank's heads, merged where adjacent */
+        uint64_t c0[8], c1[8], n = 0;
+        if (G > 8) return -1;
+        for (uint64_t g = 0; g < G; ++g) {
+            const uint64_t a = (g * KV + lay->kv_lo) * hd, b = a + kvp * hd;
+            if (n && c1[n - 1] == a)
+                c1[n - 1] = b;
+            else {
+                c0[n] = a;
+                c1[n] = b;
+                ++n;
+            }
+        }
+        width = 0;
+        for (uint64_t i = 0; i < n; ++i) {
+            if (c0[i] % 256 || c1[i] % 256) return -1;
+            const uint64_t w = (c1[i] - c0[i]) / 256 * bb;
+            sh->p[sh->np++] = (struct piece){lay->o_lo * rb + c0[i] / 256 * bb, rb, w, sh->rows, width};
+            width += w;
+        }
+        sh->cols = width / bb * 256;
+        break;
+    }
+    case TN_GATE:
+    case TN_UP:
+        sh->rows = lay->f_hi - lay->f_lo;
+        sh->cols = full_cols;
+        sh->p[sh->np++] = (struct piece){lay->f_lo * rb, rb, rb, sh->rows, 0};
+        break;
+    case TN_DOWN:
+        sh->rows = tl->rows;
+        width = (lay->f_hi - lay->f_lo) / 256 * bb;
+        sh->cols = lay->f_hi - lay->f_lo;
+        sh->p[sh->np++] = (struct piece){lay->f_lo / 256 * bb, rb, width, sh->rows, 0};
+        break;
+    default:
+        return -1;
+    }
+    sh->pitch = width;
+    if (width % 16) {
+        /* Q6_K rows whose width is not a 16-byte multiple: padded rows, as the
+         * single-GPU loader pads them; only V and down carry a row stride */
+        if (t != TN_V && t != TN_DOWN) return -1;
+        sh->pitch = (width + 15) & ~(uint64_t)15;
+        sh->padded = 1;
+    }
+    /* destination offsets of row-packed pieces are in rows: scale to bytes */
+    for (uint32_t i = 0; i < sh->np; ++i)
+        if (t == TN_Q) sh->p[i].dst_off *= sh->pitch;
+    return 0;
+}
+
+struct tp_init_job {
+    struct engine_handle *h;
+    struct tp_rank *r;
+    const uint8_t *id;
+    int rc;
+};
+
+/* Per-rank setup that joins the communicator (NCCL initialisation is
+ * collective: every rank's call runs concurrently, one thread each). */
+static void *tp_init_main(void *arg) {
+    struct tp_init_job *j = (struct tp_init_job *)arg;
+    struct engine_handle *h = j->h;
+    struct tp_rank *r = j->r;
+    j->rc = -1;
+    if (shk_cuda_tp_init(r->ctx, (int)r->rank, (int)h->tp, j->id) != SHK_OK) return NULL;
+    const uint32_t kvp = r->lay.kv_hi - r->lay.kv_lo;
+    struct shk_kv_config kc = {h->n_layers, kvp, h->head_dim, 32, h->max_seq};
+    r->kv = shk_cuda_kv_create(r->ctx, &kc);
+    if (!r->kv) return NULL;
+    j->rc = 0;
+    return NULL;
+}
+
+/* Reads rows [r0, r0 + n) of a tensor into pinned memory and copies them to a
+ * new device buffer of this rank (Q6_K rows converted to the planar layout
+ * when they are 16-byte multiples). */
+static int tp_upload_rows(struct engine_handle *h, struct tp_rank *r, const struct gguf_tensor_info *ti,
+                          uint64_t r0, uint64_t n, void **dev, uint32_t *dtype) {
+    const uint64_t rows = ti->n_dims == 2 ? ti->dims[1] : 1, rb = ti->size / rows, bytes = n * rb;
+    void *host = NULL;
+    if (shk_cuda_host_alloc(r->ctx, bytes, &host) != SHK_OK) return -1;
+    int rc = pread_all(h->g.fd, host, bytes, ti->offset + r0 * rb);
+    if (!rc) rc = shk_cuda_dev_alloc(r->ctx, bytes, dev) == SHK_OK ? 0 : -1;
+    if (!rc) rc = shk_cuda_memcpy_h2d(r->ctx, *dev, host, bytes, NULL) == SHK_OK ? 0 : -1;
+    if (!rc) rc = shk_cuda_sync(r->ctx, NULL) == SHK_OK ? 0 : -1;
+    shk_cuda_host_free(r->ctx, host);
+    *dtype = ti->type;
+    if (!rc && ti->type == 14 && rb % 16 == 0) {
+        rc = shk_cuda_q6k_repack(r->ctx, *dev, (uint32_t)n, (uint32_t)(rb / 210 * 256), 0, 1, NULL) == SHK_OK &&
+                     shk_cuda_sync(r->ctx, NULL) == SHK_OK
+                 ? 0
+                 : -1;
+        *dtype = SHK_DTYPE_Q6_K_PLANAR;
+    }
+    return rc;
+}
+
+/* Every layer: its span read once into pinned staging (two buffers
+ * alternating), each rank's slices copied into the rank's device buffer for
+ * the layer (Q6_K shards converted to the planar layout there) and
+ * registered with the rank's model. */
+static int tp_stage_layers(struct engine_handle *h) {
+    for (uint32_t l = 0; l < h->n_layers; ++l) {
+        const struct layer_map *L = &h->lm[l];
+        const uint32_t s = l % 2;
+        for (uint32_t ri = 0; ri < h->tp; ++ri) /* the pinned buffer's previous copies landed */
+            if (shk_cuda_layer_ready(h->ranks[ri].ctx, s, 1) < 0) return -1;
+        uint8_t *pin = (uint8_t *)h->pinned[s];
+        if (pread_all(h->g.fd, pin, L->span_len, L->span_off)) return -1;
+        h->st.layer_loads++;
+        h->st.layer_bytes_read += L->span_len;
+        for (uint32_t ri = 0; ri < h->tp; ++ri) {
+            struct tp_rank *r = &h->ranks[ri];
+            struct shard sh[TN_COUNT];
+            uint64_t off[TN_COUNT], dev = 0;
+            for (int t = 0; t < TN_COUNT; ++t) {
+                if (tp_shard(h, &L->t[t], t, &r->lay, &sh[t])) return -1;
+                off[t] = dev;
+                dev = al256(dev + sh[t].pitch * sh[t].rows);
+            }
+            if (shk_cuda_dev_alloc(r->ctx, dev, &r->d_buf[l]) != SHK_OK) return -1;
+            uint8_t *base = (uint8_t *)r->d_buf[l];
+            for (int t = 0; t < TN_COUNT; ++t) {
+                const struct tensor_loc *tl = &L->t[t];
+                const uint8_t *src = pin + (tl->off - L->span_off);
+                for (uint32_t i = 0; i < sh[t].np; ++i) {
+                    const struct piece *pc = &sh[t].p[i];
+                    if (shk_cuda_layer_stage_2d(r->ctx, s, base + off[t] + pc->dst_off, sh[t].pitch,
+                                                src + pc->src_off, pc->src_pitch, pc->width, pc->rows) != SHK_OK)
+                        return -1;
+                }
+                if (tl->type == 14 &&
+                    shk_cuda_layer_stage_q6k_planar(r->ctx, s, base + off[t], (uint32_t)sh[t].rows,
+                                                    (uint32_t)sh[t].cols,
+                                                    (uint32_t)(sh[t].padded ? sh[t].pitch : 0)) != SHK_OK)
+                    return -1;
+            }
+            if (shk_cuda_layer_commit(r->ctx, s) != SHK_OK) return -1;
+            struct shk_layer_desc *d = &r->ld[l];
+            memset(d, 0, sizeof(*d));
+            d->attn_norm = (const float *)(base + off[TN_ATTN_NORM]);
+            d->ffn_norm = (const float *)(base + off[TN_FFN_NORM]);
+            d->attn_q = base + off[TN_Q];
+            d->attn_k = base + off[TN_K];
+            d->attn_v = base + off[TN_V];
+            d->attn_o = base + off[TN_O];
+            d->ffn_gate = base + off[TN_GATE];
+            d->ffn_up = base + off[TN_UP];
+            d->ffn_down = base + off[TN_DOWN];
+#define DT(i) (L->t[i].type == 14 ? SHK_DTYPE_Q6_K_PLANAR : L->t[i].type)
+            d->attn_q_dtype = DT(TN_Q);
+            d->attn_k_dtype = DT(TN_K);
+            d->attn_v_dtype = DT(TN_V);
+            d->attn_o_dtype = DT(TN_O);
+            d->ffn_gate_dtype = DT(TN_GATE);
+            d->ffn_up_dtype = DT(TN_UP);
+            d->ffn_down_dtype = DT(TN_DOWN);
+#undef DT
+            d->row_stride_v = sh[TN_V].padded ? (uint32_t)sh[TN_V].pitch : 0;
+            d->row_stride_down = sh[TN_DOWN].padded ? (uint32_t)sh[TN_DOWN].pitch : 0;
+        }
+    }
+    for (uint32_t ri = 0; ri < h->tp; ++ri) {
+        struct tp_rank *r = &h->ranks[ri];
+        for (uint32_t s = 0; s < 2; ++s)
+            if (shk_cuda_layer_ready(r->ctx, s, 1) < 0 || shk_cuda_layer_wait(r->ctx, s, NULL) != SHK_OK) return -1;
+        for (uint32_t l = 0; l < h->n_layers; ++l)
+            if (shk_cuda_model_set_layer(r->m, l, &r->ld[l]) != SHK_OK) return -1;
+        if (shk_cuda_sync(r->ctx, NULL) != SHK_OK) return -1;
+    }
+    h->registered = 1;
+    return 0;
+}
+
+static int tp_open(struct engine_handle *h) {
+    if (!h->resident) return -1; /* tensor parallel runs from HBM-resident shards */
+    const int base = env_int("SHUKUCHI_DEVICE", 0);
+    h->ranks = (struct tp_rank *)calloc(h->tp, sizeof(struct tp_rank));
+    if (!h->ranks) return -1;
+    const uint32_t shape[6] = {h->n_embd, h->n_heads, h->n_kv, h->head_dim, h->n_ff, h->n_vocab};
+    for (uint32_t ri = 0; ri < h->tp; ++ri) {
+        struct tp_rank *r = &h->ranks[ri];
+        r->rank = ri;
+        uint32_t o[9];
+        if (engine_tp_layout(shape, ri, h->tp, o)) return -1;
+        r->lay = (struct tp_layout){o[0], o[1], o[2], o[3], o[4], o[5], o[6], o[7], o[8]};
+        struct shk_cuda_config cc = {base + (int)ri, 0};
+        r->ctx = shk_cuda_init(&cc);
+        r->d_buf = (void **)calloc(h->n_layers, sizeof(void *));
+        r->ld = (struct shk_layer_desc *)calloc(h->n_layers, sizeof(struct shk_layer_desc));
+        if (!r->ctx || !r->d_buf || !r->ld) return -1;
+    }
+    uint8_t id[SHK_TP_ID_BYTES];
+    if (shk_cuda_tp_unique_id(id, sizeof(id)) <= 0) return -1;
+    struct tp_init_job jobs[8];
+    pthread_t th[8];
+    if (h->tp > 8) return -1;
+    for (uint32_t ri = 0; ri < h->tp; ++ri) {
+        jobs[ri] = (struct tp_init_job){h, &h->ranks[ri], id, -1};
+        if (pthread_create(&th[ri], NULL, tp_init_main, &jobs[ri]) != 0) {
+            for (uint32_t j = 0; j < ri; ++j) pthread_join(th[j], NULL);
+            return -1;
+        }
+    }
+    int rc = 0;
+    for (uint32_t ri = 0; ri < h->tp; ++ri) {
+        pthread_join(th[ri], NULL);
+        rc |= jobs[ri].rc;
+    }
+    if (rc) return -1;
+    const struct gguf_tensor_info *emb = gguf_find_tensor(&h->g, "token_embd.weight");
+    const struct gguf_tensor_info *out = gguf_find_tensor(&h->g, "output.weight");
+    for (uint32_t ri = 0; ri < h->tp; ++ri) {
+        struct tp_rank *r = &h->ranks[ri];
+        uint32_t emb_t = 0, out_t = 0;
+        if (tp_upload_rows(h, r, emb, 0, h->n_vocab, &r->d_embd, &emb_t)) return -1;
+        if (emb_t != emb->type) return -1; /* the embedding table keeps its GGUF layout */
+        if (tp_upload_rows(h, r, out, r->lay.v_lo, r->lay.v_hi - r->lay.v_lo, &r->d_out, &out_t)) return -1;
+        const uint32_t kvp = r->lay.kv_hi - r->lay.kv_lo, G = h->n_heads / h->n_kv;
+        struct shk_model_desc md = {h->n_layers, h->n_embd, G * kvp, kvp, h->head_dim,
+                                    r->lay.f_hi - r->lay.f_lo, h->n_vocab, 10000.0f, r->d_embd, emb->type,
+                                    r->d_out, out_t};
+        r->m = shk_cuda_model_create(r->ctx, &md, r->kv);
+        if (!r->m) return -1;
+        if (shk_cuda_model_set_tp_rows(r->m, r->lay.o_lo, r->lay.o_hi, r->lay.v_lo, r->lay.v_hi) != SHK_OK)
+            return -1;
+    }
+    /* rank 0 is the handle's own context (reports, the debug dumps' device) */
+    h->ctx = h->ranks[0].ctx;
+    h->kv = h->ranks[0].kv;
+    h->m = h->ranks[0].m;
+    h->pinned = (void **)calloc(2, sizeof(void *));
+    if (!h->pinned) return -1;
+    h->depth = 2;
+    for (uint32_t i = 0; i < 2; ++i)
+        if (shk_cuda_host_alloc(h->ctx, h->max_span, &h->pinned[i]) != SHK_OK) return -1;
+    h->st.max_layer_size = (size_t)h->max_span;
+    h->st.peak_buffer_usage = (size_t)h->max_span * 2;
+    h->st.max_concurrent_buffers = 2;
+    return tp_stage_layers(h);
+}
+
+static void tp_close(struct engine_handle *h) {
+    for (uint32_t ri = 0; h->ranks && ri < h->tp; ++ri) {
+        struct tp_rank *r = &h->ranks[ri];
+        if (r->ctx) shk_cuda_sync(r->ctx, NULL);
+        if (r->m) shk_cuda_model_destroy(r->m);
+        if (r->kv) shk_cuda_kv_destroy(r->kv);
+        if (r->ctx) {
+            for (uint32_t l = 0; r->d_buf && l < h->n_layers; ++l)
+                if (r->d_buf[l]) shk_cuda_dev_free(r->ctx, r->d_buf[l]);
+            if (r->d_embd) shk_cuda_dev_free(r->ctx, r->d_embd);
+            if (r->d_out) shk_cuda_dev_free(r->ctx, r->d_out);
+        }
+    }
+    if (h->pinned && h->ranks && h->ranks[0].ctx)
+        for (uint32_t i = 0; i < 2; ++i)
+            if (h->pinned[i]) shk_cuda_host_free(h->ranks[0].ctx, h->pinned[i]);
+    free(h->pinned);
+    h->pinned = NULL;
+    for (uint32_t ri = 0; h->ranks && ri < h->tp; ++ri) {
+        struct tp_rank *r = &h->ranks[ri];
+        if (r->ctx) shk_cuda_shutdown(r->ctx);
+        free(r->d_buf);
+        free(r->ld);
+        free(r->lg);
+    }
+    free(h->ranks);
+    h->ranks = NULL;
+    h->ctx = NULL;
+    h->kv = NULL;
+    h->m = NULL;
+}
+
+/* A rank's token loop (ranks 1..world-1 on their own threads; rank 0 runs in
+ * generate()): the same steps on every rank, in lockstep through the
+ * collectives inside each step; every rank gets the same next token. */
+static void *tp_rank_main(void *arg) {
+    struct tp_rank *r = (struct tp_rank *)arg;
+    r->rc = -1;
+    shk_cuda_kv_clear(r->kv);
+    uint32_t pos = 0, next = 0;
+    for (uint32_t i = 0; i < r->n_prompt; ++i, ++pos) {
+        const int last = i + 1 == r->n_prompt;
+        float *lg = (last && r->want_logits) ? r->lg : NULL;
+        if (shk_cuda_token_step(r->m, r->prompt[i], pos, last, &next, lg) != SHK_OK) return NULL;
+    }
+    for (uint32_t j = 0; j < r->n_decode; ++j, ++pos) {
+        const int want = j + 1 < r->n_decode;
+        uint32_t nx = 0;
+        float *lg = (want && r->want_logits) ? r->lg : NULL;
+        if (shk_cuda_token_step(r->m, next, pos, want, &nx, lg) != SHK_OK) return NULL;
+        if (want) next = nx;
+    }
+    r->rc = 0;
+    return NULL;
 }
 
 /* ------------------------------- public --------------------------------- */
@@ -663,6 +1113,13 @@ void engine_close(engine_handle_t *h) {
         pthread_cond_broadcast(&h->cv);
         pthread_mutex_unlock(&h->mu);
         pthread_join(h->thr, NULL);
+    }
+    if (h->ranks) {
+        if (h->tp_broken) { /* rank threads may still hold the contexts: leave them */
+            gguf_close(&h->g);
+            return;
+        }
+        tp_close(h);
     }
     if (h->ctx) shk_cuda_sync(h->ctx, NULL);
     if (h->m) shk_cuda_model_destroy(h->m);
@@ -703,6 +1160,12 @@ engine_handle_t *engine_open(const char *model_path, const struct engine_config 
     h->resident = env_int("SHUKUCHI_HBM_RESIDENT", 1) != 0;
     h->max_seq = (uint32_t)env_int("SHUKUCHI_MAX_SEQ", 2048);
     if (gguf_open(model_path, &h->g) || map_model(h) || vocab_index_build(h)) goto fail;
+    h->tp = (uint32_t)env_int("SHUKUCHI_TP", 1);
+    if (h->tp != 1 && h->tp != 2 && h->tp != 4 && h->tp != 8) goto fail;
+    if (h->tp > 1) {
+        if (tp_open(h)) goto fail;
+        return h;
+    }
     struct shk_cuda_config cc = {env_int("SHUKUCHI_DEVICE", 0), 0};
     h->ctx = shk_cuda_init(&cc);
     if (!h->ctx) goto fail;

@@ -19,6 +19,14 @@
  *                          prefetch_depth device slots on every token, as the
  *                          reference streams them from disk
  *   SHUKUCHI_MAX_SEQ       KV-cache capacity in positions (default 2048)
+ *   SHUKUCHI_TP            1 (default), 2, 4 or 8: tensor parallel over GPUs
+ *                          SHUKUCHI_DEVICE.. +TP-1, one context and thread per
+ *                          rank, NCCL between them; Wq/Wk/Wv and gate/up split
+ *                          by output rows, Wo and down by input columns, KV
+ *                          heads local to a rank, the output head by vocabulary
+ *                          rows; resident mode only (each layer is read once
+ *                          and every rank copies its slices).  engine_cancel
+ *                          takes effect at the end of a generation here
  *   SHUKUCHI_DEBUG         set and not "0": per-layer quant types and, for
  *                          the first prompt token, the embedding's and layer
  *                          0's intermediate statistics on stdout, as the
@@ -78,6 +86,12 @@ uint32_t engine_vocab_size(engine_handle_t *h);
  * steps, staged copies and bytes): the CLI's closing report, as the
  * reference's main prints metal_ops_report() (engine/src/main.c:106). */
 void engine_report(engine_handle_t *h);
+/* The tensor-parallel split of rank `rank` of `world` (no GPU needed):
+ * shape = {n_embd, n_heads, n_kv_heads, head_dim, n_ff, n_vocab}; out = {A
+ * (ranks sharing attention heads), kv_lo, kv_hi, o_lo, o_hi (O-projection
+ * output rows), f_lo, f_hi (FFN columns), v_lo, v_hi (output-head rows)}.
+ * 0 on success, -1 when the shape has no block-aligned split. */
+int engine_tp_layout(const uint32_t shape[6], uint32_t rank, uint32_t world, uint32_t out[9]);
 /* The prompt tokenizer alone (no GPU needed): the ids of `text` under a GGUF
  * file's vocabulary, at most cap of them; returns the count or -1. */
 int engine_tokenize_file(const char *model_path, const char *text, uint32_t *out, uint32_t cap);

@@ -102,6 +102,48 @@ def test_engine_matches_oracle(model_file, oracle, resident, depth, monkeypatch)
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_engine_tp_matches_oracle(tmp_path, oracle, world, monkeypatch):
+    """SHUKUCHI_TP: the C engine split over `world` GPUs (a thread and a
+    context per rank, NCCL between them) on a GGUF file gives the oracle's
+    greedy ids and logits (gathered over the vocabulary-split head); the
+    layers are read once and every rank stages its slices.  Needs `world`
+    GPUs."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"{world} GPUs needed")
+    s = synth.ModelShape("tp-hd128", 2, 1024, 8, 4, 2048, 1024)
+    m = synth.make_model(s, seed=21)
+    p = str(tmp_path / "tp.gguf")
+    gguf.write_model(p, m)
+    monkeypatch.setenv("SHUKUCHI_TP", str(world))
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, s.n_vocab, 5).astype(np.uint32)
+    n_dec = 8
+    t_ref, l_ref = oracle.generate(m, prompt, n_dec)
+    L = lib()
+    cfg = Config(4, 1, 3, 32, 0, 0)
+    h = L.engine_open(p.encode(), C.byref(cfg))
+    assert h, "engine_open failed"
+    try:
+        ids = np.zeros(n_dec, np.uint32)
+        logits = np.zeros((n_dec, s.n_vocab), np.float32)
+        assert L.engine_generate_ids(h, prompt.ctypes.data, prompt.size, n_dec, ids.ctypes.data,
+                                     logits.ctypes.data) == n_dec
+        ids2 = np.zeros(n_dec, np.uint32)
+        assert L.engine_generate_ids(h, prompt.ctypes.data, prompt.size, n_dec, ids2.ctypes.data, None) == n_dec
+        st = Stats()
+        assert L.engine_get_streaming_stats(h, C.byref(st)) == 0
+    finally:
+        L.engine_close(h)
+    assert np.array_equal(ids, t_ref) and np.array_equal(ids2, t_ref)
+    for t in range(n_dec):
+        assert np.max(np.abs(logits[t] - l_ref[t])) <= 1e-2 * np.std(l_ref[t]), t
+    assert st.layer_loads == s.n_layers  # each layer read once for all ranks
+
+
+@pytest.mark.gpu
 def test_engine_text_prompt_matches_reference_cli(model_file, reference):
     """Prompt text through the greedy tokenizer: same ids as the reference."""
     m, p = model_file
@@ -158,6 +200,29 @@ def test_tokenizer_matches_reference(tmp_path, reference, bos):
         n = L.engine_tokenize_file(p.encode(), b, out.ctypes.data, out.size)
         assert n == len(want), (t[:40], n, len(want))
         assert np.array_equal(out[:n], want), t[:40]
+
+
+@pytest.mark.parametrize("name", ["tiny", "small", "tp-hd128", "llama8b", "llama70b", "tinyllama"])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_engine_tp_layout_matches_python(name, world):
+    """The C engine's tensor-parallel split (SHUKUCHI_TP) is the Python
+    side's shukuchi_b200/tp.py layout, rank by rank (no GPU)."""
+    from shukuchi_b200 import tp
+    s = synth.SHAPES[name] if name in synth.SHAPES else synth.ModelShape(name, 2, 1024, 8, 4, 2048, 1024)
+    L = lib()
+    L.engine_tp_layout.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
+    shape = np.array([s.n_embd, s.n_heads, s.n_kv_heads, s.head_dim, s.n_ff, s.n_vocab], np.uint32)
+    for rank in range(world):
+        out = np.zeros(9, np.uint32)
+        rc = L.engine_tp_layout(shape.ctypes.data, rank, world, out.ctypes.data)
+        try:
+            lay = tp.layout(s, rank, world)
+        except ValueError:
+            assert rc != 0
+            continue
+        assert rc == 0
+        assert list(out) == [lay.group_size, lay.kv_lo, lay.kv_hi, lay.o_lo, lay.o_hi, lay.f_lo, lay.f_hi,
+                             lay.v_lo, lay.v_hi], (name, world, rank)
 
 
 def test_inspect_rejects_broken_files(model_file, tmp_path):

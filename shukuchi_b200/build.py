@@ -83,6 +83,13 @@ def build_engine() -> str | None:
     if _stale(lib, lib_srcs + hdrs + [LIB]):
         _run(["gcc"] + cflags + ["-shared", "-o", lib] + lib_srcs +
              ["-L" + PKG, "-lshk_cuda", "-Wl,-rpath,$ORIGIN/..", "-lpthread", "-lm"])
+    packer_dir = os.path.join(PKG, "packer")
+    if os.path.isdir(packer_dir):  # the LSTR packer CLI (GGUF -> container)
+        psrcs = [os.path.join(packer_dir, f) for f in ("packer.c", "main.c")] + \
+                [os.path.join(ENGINE, f) for f in ("gguf.c", "lstr.c")]
+        pbin = os.path.join(packer_dir, "shukuchi-pack")
+        if _stale(pbin, psrcs + hdrs + _headers(packer_dir)):
+            _run(["gcc"] + cflags + ["-o", pbin] + psrcs)
     main = os.path.join(ENGINE, "main.c")
     if os.path.exists(main) and _stale(cli, [main, lib]):
         _run(["gcc"] + cflags + ["-o", cli, main, "-L" + ENGINE, "-lshukuchi",

@@ -26,6 +26,7 @@
 
 #include "../../include/shk_cuda.h"
 #include "gguf.h"
+#include "lstr.h"
 
 enum { TN_ATTN_NORM, TN_Q, TN_K, TN_V, TN_O, TN_FFN_NORM, TN_GATE, TN_UP, TN_DOWN, TN_COUNT };
 static const char *const k_suffix[TN_COUNT] = {
@@ -118,6 +119,11 @@ struct engine_handle {
 };
 
 static void *tp_rank_main(void *arg);
+
+/* A model file: GGUF, or the LSTR container (engine/lstr.h) by its magic. */
+static int model_file_open(const char *path, struct gguf_file *g) {
+    return lstr_is(path) ? lstr_open(path, g) : gguf_open(path, g);
+}
 
 static int env_int(const char *name, int def) {
     const char *v = getenv(name);
@@ -1159,7 +1165,7 @@ engine_handle_t *engine_open(const char *model_path, const struct engine_config 
     if (h->depth > 3) h->depth = 3;
     h->resident = env_int("SHUKUCHI_HBM_RESIDENT", 1) != 0;
     h->max_seq = (uint32_t)env_int("SHUKUCHI_MAX_SEQ", 2048);
-    if (gguf_open(model_path, &h->g) || map_model(h) || vocab_index_build(h)) goto fail;
+    if (model_file_open(model_path, &h->g) || map_model(h) || vocab_index_build(h)) goto fail;
     h->tp = (uint32_t)env_int("SHUKUCHI_TP", 1);
     if (h->tp != 1 && h->tp != 2 && h->tp != 4 && h->tp != 8) goto fail;
     if (h->tp > 1) {
@@ -1268,7 +1274,7 @@ int engine_tokenize_file(const char *model_path, const char *text, uint32_t *out
     struct engine_handle *h = (struct engine_handle *)calloc(1, sizeof(*h));
     if (!h) return -1;
     h->g.fd = -1;
-    int rc = gguf_open(model_path, &h->g);
+    int rc = model_file_open(model_path, &h->g);
     if (!rc) {
         map_vocab(h);
         rc = vocab_index_build(h);
@@ -1289,7 +1295,7 @@ int engine_tokenize_file(const char *model_path, const char *text, uint32_t *out
 int engine_inspect(const char *model_path, uint32_t out[6], uint64_t *max_layer_bytes) {
     struct engine_handle *h = (struct engine_handle *)calloc(1, sizeof(*h));
     if (!h) return -1;
-    int rc = gguf_open(model_path, &h->g);
+    int rc = model_file_open(model_path, &h->g);
     if (!rc) rc = map_model(h);
     if (!rc) {
         out[0] = h->n_layers;

@@ -34,6 +34,14 @@
       barrier; reports per phase kind the mean wall time (barrier to barrier)
       and the part of it CTA 0 spent waiting at the barrier.
 
+  python -m shukuchi_b200.microbench loader [--shape llama8b] [--prompt 8] [--decode 16] [--depth 3]
+      The C engine on a GGUF file of the shape (written once under --dir):
+      HBM-resident mode (every layer pread -> pinned -> HBM once, then the
+      captured step) and ring mode (SHUKUCHI_HBM_RESIDENT=0: every layer
+      streamed through `depth` device slots on every token, as the reference
+      streams them from disk): open and first-generation times, tok/s,
+      streamed GB/s and the prefetch hit / miss statistics.
+
 One JSON line per case; `frac` is achieved GB/s over the measured HBM copy
 bandwidth (MEASURED_PEAKS.json when present).
 """
@@ -353,6 +361,83 @@ def timeline(args, ctx) -> None:
         ctx.close()
 
 
+def loader(args, ctx) -> None:
+    import ctypes as C
+    import time
+
+    import numpy as np
+
+    from . import gguf, synth
+
+    class Stats(C.Structure):
+        _fields_ = [("layer_loads", C.c_uint64), ("layer_bytes_read", C.c_uint64), ("max_layer_size", C.c_size_t),
+                    ("peak_buffer_usage", C.c_size_t), ("peak_rss", C.c_size_t),
+                    ("max_concurrent_buffers", C.c_uint32), ("prefetch_hits", C.c_uint32),
+                    ("prefetch_misses", C.c_uint32)]
+
+    class Config(C.Structure):
+        _fields_ = [("n_threads", C.c_uint32), ("batch_size", C.c_uint32), ("prefetch_depth", C.c_uint32),
+                    ("kv_block_size", C.c_uint32), ("kv_quant", C.c_uint32), ("use_mmap", C.c_int)]
+
+    L = C.CDLL(os.path.join(os.path.dirname(os.path.abspath(__file__)), "engine", "libshukuchi.so"))
+    L.engine_open.restype = C.c_void_p
+    L.engine_open.argtypes = [C.c_char_p, C.POINTER(Config)]
+    L.engine_generate_ids.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
+    L.engine_get_streaming_stats.argtypes = [C.c_void_p, C.POINTER(Stats)]
+    L.engine_close.argtypes = [C.c_void_p]
+    s = synth.SHAPES[args.shape]
+    os.makedirs(args.dir, exist_ok=True)
+    path = os.path.join(args.dir, f"{args.shape}.gguf")
+    write_s = 0.0
+    if not os.path.exists(path):
+        t = time.perf_counter()
+        gguf.write_model(path, synth.make_model(s, seed=3))
+        write_s = time.perf_counter() - t
+    size = os.path.getsize(path)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, s.n_vocab, args.prompt).astype(np.uint32)
+    n = args.prompt + args.decode
+    ids = np.zeros(args.decode, np.uint32)
+    for mode in ("resident", "ring"):
+        os.environ["SHUKUCHI_HBM_RESIDENT"] = "1" if mode == "resident" else "0"
+        os.environ["SHUKUCHI_MAX_SEQ"] = str(n + 8)
+        t0 = time.perf_counter()
+        h = L.engine_open(path.encode(), C.byref(Config(4, 1, args.depth, 32, 0, 0)))
+        t1 = time.perf_counter()
+        if not h:
+            raise SystemExit("engine_open failed")
+        try:
+            rc = L.engine_generate_ids(h, prompt.ctypes.data, prompt.size, args.decode, ids.ctypes.data, None)
+            t2 = time.perf_counter()
+            rc2, t3 = rc, t2
+            if mode == "resident":  # a second generation: the layers are in HBM already
+                rc2 = L.engine_generate_ids(h, prompt.ctypes.data, prompt.size, args.decode, ids.ctypes.data, None)
+                t3 = time.perf_counter()
+            st = Stats()
+            L.engine_get_streaming_stats(h, C.byref(st))
+        finally:
+            L.engine_close(h)
+        if rc != args.decode or rc2 != args.decode:
+            raise SystemExit(f"generation failed ({mode})")
+        gen = t2 - t1
+        line = {"bench": "loader", "shape": s.name, "mode": mode, "file_bytes": size, "file_write_s": round(write_s, 2),
+                "depth": args.depth, "tokens": n, "open_s": round(t1 - t0, 3), "first_generation_s": round(gen, 3),
+                "first_generation_tok_s": round(n / gen, 2), "layer_loads": st.layer_loads,
+                "layer_bytes_read": st.layer_bytes_read, "max_layer_size": st.max_layer_size,
+                "peak_buffer_usage": st.peak_buffer_usage, "max_concurrent_buffers": st.max_concurrent_buffers,
+                "prefetch_hits": st.prefetch_hits, "prefetch_misses": st.prefetch_misses,
+                "prefetch_hit_rate": round(st.prefetch_hits / max(1, st.prefetch_hits + st.prefetch_misses), 4)}
+        if mode == "resident":
+            warm = t3 - t2
+            line["warm_generation_tok_s"] = round(n / warm, 2)
+            # staging: the first generation's extra time over the warm one
+            line["staging_s"] = round(max(gen - warm, 1e-9), 3)
+            line["staged_gbs"] = round(st.layer_bytes_read / max(gen - warm, 1e-9) / 1e9, 2)
+        else:
+            line["streamed_gbs"] = round(st.layer_bytes_read / gen / 1e9, 2)
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -380,11 +465,18 @@ def main() -> None:
     tl.add_argument("--layers", type=int, default=32)
     tl.add_argument("--prompt", type=int, default=512)
     tl.add_argument("--steps", type=int, default=4)
+    ld = sub.add_parser("loader")
+    ld.add_argument("--shape", default="llama8b")
+    ld.add_argument("--prompt", type=int, default=8)
+    ld.add_argument("--decode", type=int, default=16)
+    ld.add_argument("--depth", type=int, default=3)
+    ld.add_argument("--dir", default="/tmp/shk_gguf")
     args = ap.parse_args()
     torch.cuda.set_device(0)
     ctx = sc.Context(0)
     try:
-        {"gemv": gemv, "kv": kv, "parts": parts, "timeline": timeline, "prefill": prefill}[args.cmd](args, ctx)
+        {"gemv": gemv, "kv": kv, "parts": parts, "timeline": timeline, "prefill": prefill,
+         "loader": loader}[args.cmd](args, ctx)
     finally:
         ctx.close()
 

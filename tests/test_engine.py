@@ -63,9 +63,14 @@ def test_inspect_matches_reference(model_file, reference):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("resident,depth", [(1, 3), (0, 2), (0, 3)])
-def test_engine_matches_oracle(model_file, oracle, resident, depth, monkeypatch):
+@pytest.mark.parametrize("resident,depth,container", [(1, 3, "gguf"), (0, 2, "gguf"), (0, 3, "gguf"),
+                                                     (1, 3, "lstr"), (0, 3, "lstr")])
+def test_engine_matches_oracle(model_file, oracle, resident, depth, container, monkeypatch, tmp_path):
     m, p = model_file
+    if container == "lstr":  # the same model through the LSTR container (4 KiB-aligned layer blocks)
+        lp = str(tmp_path / "small.lstr")
+        pack(p, lp, "--checksums")
+        p = lp
     monkeypatch.setenv("SHUKUCHI_HBM_RESIDENT", str(resident))
     rng = np.random.default_rng(5)
     prompt = rng.integers(0, m.shape.n_vocab, 6).astype(np.uint32)
@@ -223,6 +228,83 @@ def test_engine_tp_layout_matches_python(name, world):
         assert rc == 0
         assert list(out) == [lay.group_size, lay.kv_lo, lay.kv_hi, lay.o_lo, lay.o_hi, lay.f_lo, lay.f_hi,
                              lay.v_lo, lay.v_hi], (name, world, rank)
+
+
+PACKER = os.path.join(os.path.dirname(ENGINE), "..", "packer", "shukuchi-pack")
+
+
+def pack(src: str, dst: str, *flags) -> None:
+    import subprocess
+    subprocess.run([PACKER, src, dst, *flags], check=True)
+
+
+@pytest.mark.parametrize("align,checksums", [(4096, True), (2 << 20, False)])
+def test_lstr_container(model_file, tmp_path, align, checksums):
+    """The packer (model_packer's packer_run) writes the LSTR container: the
+    256-byte header, the layer index, the resident section and aligned layer
+    blocks with tensor tables and XXH64 checksums (checked here with the
+    xxhash package); the engine reads it as the same model as the GGUF file
+    (shape, largest layer span, tokenizer ids) without a GPU."""
+    import struct
+    m, p = model_file
+    out = str(tmp_path / "small.lstr")
+    pack(p, out, "--align", str(align), *(["--checksums"] if checksums else []))
+    data = open(out, "rb").read()
+    (magic, endian, version, hsize, minv, flags, n_layers, n_vocab, n_embd, n_heads, n_kv, ctx, rope_type,
+     theta, rscale, n_ff, hd, _r2, idx_off, idx_size, res_off, res_size, lay_off, fsize) = struct.unpack_from(
+        "<13I2f3I6Q", data, 0)
+    s = m.shape
+    assert (magic, endian, version, hsize) == (0x5254534C, 0x01020304, 1, 256)
+    assert (n_layers, n_vocab, n_embd, n_heads, n_kv, n_ff, hd) == (s.n_layers, s.n_vocab, s.n_embd, s.n_heads,
+                                                                    s.n_kv_heads, s.n_ff, s.head_dim)
+    assert fsize == len(data) and idx_off == 256 and idx_size == 40 * s.n_layers
+    assert flags & 2 and bool(flags & 1) == checksums and bool(flags & 4) == (align == 4096)
+    assert bool(flags & 8) == (align == 2 << 20) and lay_off % align == 0
+    import xxhash
+    for l in range(s.n_layers):
+        lid, nt, off, size, dt, tto, csum = struct.unpack_from("<IIQQIIQ", data, idx_off + 40 * l)
+        assert (lid, nt) == (l, 9) and off % align == 0 and off >= lay_off
+        blk = data[off:off + size]
+        assert csum == (xxhash.xxh64(blk, seed=0).intdigest() if checksums else 0)
+        for t in range(9):
+            tid, tdt, toff, tsz = struct.unpack_from("<IIQQ", blk, tto + 24 * t)
+            assert tid == t and toff % 256 == 0 and toff + tsz <= tto
+    L = lib()
+    L.lstr_verify.argtypes = [C.c_char_p]
+    assert L.lstr_verify(out.encode()) == 0
+    a, b = (C.c_uint32 * 6)(), (C.c_uint32 * 6)()
+    ma, mb = C.c_uint64(), C.c_uint64()
+    assert L.engine_inspect(p.encode(), a, C.byref(ma)) == 0
+    assert L.engine_inspect(out.encode(), b, C.byref(mb)) == 0
+    assert list(a) == list(b) and ma.value == mb.value
+    L.engine_tokenize_file.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_uint32]
+    text = b"t00003t00141 t00059t01000"
+    ia, ib = np.zeros(64, np.uint32), np.zeros(64, np.uint32)
+    na = L.engine_tokenize_file(p.encode(), text, ia.ctypes.data, 64)
+    nb = L.engine_tokenize_file(out.encode(), text, ib.ctypes.data, 64)
+    assert na == nb > 0 and np.array_equal(ia[:na], ib[:nb])
+    if checksums:  # a flipped byte inside a layer block fails the check
+        bad = bytearray(data)
+        off = struct.unpack_from("<IIQQIIQ", data, idx_off)[2]
+        bad[off + 100] ^= 0xFF
+        bp = tmp_path / "bad.lstr"
+        bp.write_bytes(bytes(bad))
+        assert L.lstr_verify(str(bp).encode()) != 0
+
+
+def test_xxh64_known_answers():
+    """The container's XXH64 against the xxhash package on lengths around the
+    stripe and tail boundaries."""
+    import xxhash
+    L = lib()
+    L.lstr_xxh64.restype = C.c_uint64
+    L.lstr_xxh64.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64]
+    rng = np.random.default_rng(0)
+    for n in (0, 1, 3, 4, 7, 8, 9, 31, 32, 33, 63, 64, 100, 1000, 4099):
+        b = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+        buf = C.create_string_buffer(b, max(n, 1))
+        for seed in (0, 12345):
+            assert L.lstr_xxh64(buf, n, seed) == xxhash.xxh64(b, seed=seed).intdigest(), (n, seed)
 
 
 def test_inspect_rejects_broken_files(model_file, tmp_path):

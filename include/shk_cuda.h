@@ -264,6 +264,20 @@ int shk_cuda_token_step(shk_model *m, uint32_t token, uint32_t pos, int want_nex
 int shk_cuda_decode_steps(shk_model *m, uint32_t first_token, uint32_t first_pos, uint32_t n_steps,
                           void *stream);
 int shk_cuda_model_token(shk_model *m, uint32_t *token_host); /* last argmax */
+/* Batched prompt prefill: tokens[0..n) (host) at positions pos0.. run through
+ * every layer as T = n rows at a time -- the projections on the tensor-core
+ * matmul (shk_cuda_prefill_matmul: bf16 operands, fp32 accumulation), RMSNorm,
+ * RoPE, SwiGLU and residuals row-batched, the n K/V rows appended to the
+ * Q8_0 cache in one launch per layer and every row's causal attention over
+ * [0, pos0 + row] -- then the output head on the last row: its argmax to
+ * *next_host (and its logits to logits_host when non-NULL).  The reference
+ * feeds the prompt one token at a time (engine/src/engine.c:343-394); this is
+ * the same computation with bf16 rounding of the matmul inputs, so logits
+ * differ from the token-by-token path by that rounding.  Weights must be
+ * Q4_K or planar Q6_K (else SHK_EUNSUPPORTED: feed the prompt through
+ * shk_cuda_token_step); single GPU. */
+int shk_cuda_prefill(shk_model *m, const uint32_t *tokens_host, uint32_t n, uint32_t pos0,
+                     uint32_t *next_host, float *logits_host, void *stream);
 /* Timeline of the persistent decode kernel, for profiling (no counterpart in
  * the reference, whose CPU loop has no phases).  shk_cuda_model_trace_enable
  * (m, n) makes the following token_step / decode_steps launches record, on

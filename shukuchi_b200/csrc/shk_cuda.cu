@@ -20,6 +20,7 @@
 #include "glue.cuh"
 #include "mmv.cuh"
 #include "q5k.cuh"
+#include "prefill_layer.cuh"
 #include "tp_ll.cuh"
 
 using // Fewest cached positions per attention split (CTA of a KV head's cluster).
@@ -260,6 +261,10 @@ struct shk_model {
     uint32_t* d_step = nullptr;    // epoch, advanced by the embedding kernel
   } ll;
   uint32_t* tp_pairs = nullptr; // world x {max value bits, index}: argmax over the vocabulary slices
+  float* pf_buf = nullptr;      // prompt prefill: T-row activation blocks (shk_cuda_prefill)
+  size_t pf_cap = 0;
+  uint32_t* pf_tok = nullptr;
+  size_t pf_tok_cap = 0;
   uint64_t* d_trace = nullptr;  // persistent-kernel timeline (shk_cuda_model_trace_enable)
   uint32_t trace_phases = 0;
   uint32_t trace_last = 0;      // phases recorded by the last launch
@@ -1332,6 +1337,8 @@ void shk_cuda_model_destroy(shk_model* m) {
   cudaFreeHost(m->h_tok);
   cudaFree(m->d_freq);
   cudaFree(m->d_trace);
+  cudaFree(m->pf_buf);
+  cudaFree(m->pf_tok);
   delete m;
 }
 
@@ -1390,6 +1397,80 @@ int shk_cuda_model_lm_head(shk_model* m, uint32_t* token, float* logits, void* s
   CK(cudaStreamSynchronize(st));
   if (token) *token = m->h_tok[2];
   return ctx_err_check(m->ctx);
+}
+
+int shk_cuda_prefill(shk_model* m, const uint32_t* tokens, uint32_t n, uint32_t pos0, uint32_t* next,
+                     float* logits, void* s) {
+  if (!m || !tokens || !n || (uint64_t)pos0 + n > m->kv->L.max_seq) return SHK_EINVAL;
+  if (!model_ready(m)) return SHK_EINVAL;
+  shk_ctx* c = m->ctx;
+  if (c->tp_world > 1 || m->p2p.on || m->ll.on || n > 65535) return SHK_EUNSUPPORTED;
+  const shk_model_desc& d = m->d;
+  const uint32_t D = d.n_embd, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd, F = d.n_ff;
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] >= d.n_vocab) return SHK_EINVAL;
+  // the tensor-core matmul takes Q4_K and planar Q6_K rows
+  auto ok_dt = [](uint32_t t) { return t == (uint32_t)T_Q4K || t == (uint32_t)T_Q6K_PLANAR; };
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    const shk_layer_desc& lv = m->layers[l];
+    if (!ok_dt(lv.attn_q_dtype) || !ok_dt(lv.attn_k_dtype) || !ok_dt(lv.attn_v_dtype) ||
+        !ok_dt(lv.attn_o_dtype) || !ok_dt(lv.ffn_gate_dtype) || !ok_dt(lv.ffn_up_dtype) ||
+        !ok_dt(lv.ffn_down_dtype))
+      return SHK_EUNSUPPORTED;
+  }
+  cudaStream_t st = pick(c, s);
+  const size_t per = 2 * (size_t)D + qd + 2 * (size_t)kvd + qd + D + 3 * (size_t)F;  // floats per row
+  int rc;
+  if ((rc = grow(&m->pf_buf, &m->pf_cap, per * n * sizeof(float))) ||
+      (rc = grow(&m->pf_tok, &m->pf_tok_cap, (size_t)n * sizeof(uint32_t))) ||
+      (rc = grow(&c->pf_x, &c->pf_x_cap, prefill_x_bytes(std::max(std::max(D, qd), F), n))))
+    return rc;
+  float* X = m->pf_buf;
+  float* Xn = X + (size_t)n * D;
+  float* Q = Xn + (size_t)n * D;
+  float* K = Q + (size_t)n * qd;
+  float* V = K + (size_t)n * kvd;
+  float* A = V + (size_t)n * kvd;
+  float* P = A + (size_t)n * qd;
+  float* G = P + (size_t)n * D;
+  float* U = G + (size_t)n * F;
+  float* H = U + (size_t)n * F;
+  CK(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+  for (uint32_t t = 0; t < n; ++t)
+    CK(embed_launch(d.tok_embd_dev, d.tok_embd_dtype, m->pf_tok + t, d.n_vocab, X + (size_t)t * D, D, c->d_err, st));
+  auto mm = [&](uint32_t dt, const void* w, uint32_t stride, const float* x, float* y, uint32_t rows,
+                uint32_t k) -> cudaError_t {
+    const uint32_t dense = (k / QK) * (dt == (uint32_t)T_Q4K ? Q4K_BYTES : Q6K_BYTES);
+    return prefill_launch(dt, w, stride ? stride : dense, x, c->pf_x, y, rows, k, n, c->d_err, c->num_sms, st);
+  };
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    const shk_layer_desc& lv = m->layers[l];
+    // attention block (engine/src/engine.c:105-167), T rows at a time
+    CK(rmsnorm_rows_launch(X, lv.attn_norm, Xn, D, n, st));
+    CK(mm(lv.attn_q_dtype, lv.attn_q, 0, Xn, Q, qd, D));
+    CK(mm(lv.attn_k_dtype, lv.attn_k, 0, Xn, K, kvd, D));
+    CK(mm(lv.attn_v_dtype, lv.attn_v, lv.row_stride_v, Xn, V, kvd, D));
+    CK(rope_rows_launch(Q, d.n_heads, hd, pos0, n, m->d_freq, st));
+    CK(rope_rows_launch(K, d.n_kv_heads, hd, pos0, n, m->d_freq, st));
+    CK(kv_append_range_launch(m->kv->L, l, pos0, n, K, V, st));
+    AttnArgs a = layer_attn_args(m, l, nullptr);
+    a.q = Q;
+    a.out = A;
+    CK(attn_prefill_launch(a, m->kv->d_iota, pos0, n, st));
+    CK(mm(lv.attn_o_dtype, lv.attn_o, 0, A, P, D, qd));
+    CK(add_launch(X, P, n * D, st));
+    // FFN block (engine/src/engine.c:170-221)
+    CK(rmsnorm_rows_launch(X, lv.ffn_norm, Xn, D, n, st));
+    CK(mm(lv.ffn_gate_dtype, lv.ffn_gate, 0, Xn, G, F, D));
+    CK(mm(lv.ffn_up_dtype, lv.ffn_up, 0, Xn, U, F, D));
+    CK(swiglu_launch(G, U, H, n * F, st));
+    CK(mm(lv.ffn_down_dtype, lv.ffn_down, lv.row_stride_down, H, P, D, F));
+    CK(add_launch(X, P, n * D, st));
+  }
+  for (uint32_t l = 0; l < d.n_layers; ++l) m->kv->seq[l] = std::max(m->kv->seq[l], pos0 + n);
+  // the last row is the hidden state the output head reads
+  CK(cudaMemcpyAsync(m->hidden, X + (size_t)(n - 1) * D, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+  return shk_cuda_model_lm_head(m, next, logits, s);
 }
 
 int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_next, uint32_t* next,

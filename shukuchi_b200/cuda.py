@@ -76,6 +76,7 @@ _SIGS = {
     "shk_cuda_matmul_q4k_vec": (I, [P, P, P, P, U32, U32, P]),
     "shk_cuda_matmul_q6k_vec": (I, [P, P, P, P, U32, U32, P]),
     "shk_cuda_matmul_q5k_vec": (I, [P, P, P, P, U32, U32, P]),
+    "shk_cuda_prefill": (I, [P, P, U32, U32, P, P, P]),
     "shk_cuda_matmul_q4k_vec_host": (I, [P, P, P, P, U32, U32]),
     "shk_cuda_matmul_q6k_vec_host": (I, [P, P, P, P, U32, U32]),
     "shk_cuda_matmul_q5k_vec_host": (I, [P, P, P, P, U32, U32]),
@@ -124,6 +125,7 @@ _SIGS = {
     "shk_cuda_model_launch_part": (I, [P, U32, U32, P, C.POINTER(U64)]),
     "shk_cuda_layer_stage": (I, [P, U32, P, P, SZ]),
     "shk_cuda_layer_stage_rows": (I, [P, U32, P, SZ, P, SZ, SZ]),
+    "shk_cuda_layer_stage_2d": (I, [P, U32, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t]),
     "shk_cuda_layer_commit": (I, [P, U32]),
     "shk_cuda_layer_ready": (I, [P, U32, I]),
     "shk_cuda_layer_wait": (I, [P, U32, P]),
@@ -395,6 +397,15 @@ class DeviceModel:
         t = C.c_uint32(0)
         _call("shk_cuda_token_step", self.h, token, pos, 1 if want_next else 0, C.byref(t), logits_host_ptr)
         return t.value
+
+    def prefill(self, tokens, pos0=0, logits_host_ptr=None, stream=None) -> int:
+        """Batched prompt prefill of `tokens` (uint32 numpy array) at positions
+        pos0..; returns the argmax of the last row's logits."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, np.uint32)
+        nx = C.c_uint32(0)
+        _call("shk_cuda_prefill", self.h, t.ctypes.data, t.size, pos0, C.byref(nx), logits_host_ptr, stream)
+        return nx.value
 
     def decode_steps(self, first_token, first_pos, n, stream=None):
         _call("shk_cuda_decode_steps", self.h, first_token, first_pos, n, stream)

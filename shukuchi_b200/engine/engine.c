@@ -692,8 +692,22 @@ static int generate(struct engine_handle *h, const uint32_t *prompt, uint32_t n_
         }
     }
     int rc = 0;
-    uint32_t next = 0;
-    for (uint32_t i = 0; i < n_prompt && !rc; ++i) {
+    uint32_t next = 0, first = 0;
+    /* prompts of SHUKUCHI_PREFILL (default 64) tokens or more: one batched
+     * prefill on the tensor cores instead of a step per token (single GPU,
+     * HBM-resident, Q4_K / Q6_K weights; else the token loop below) */
+    const int pf_min = env_int("SHUKUCHI_PREFILL", 64);
+    if (pf_min > 0 && n_prompt >= (uint32_t)pf_min && h->resident && h->tp <= 1 && !debug_enabled() &&
+        !register_layers(h)) {
+        const int r = shk_cuda_prefill(h->m, prompt, n_prompt, 0, &next, logits_out, NULL);
+        if (r == SHK_OK) {
+            h->pos = n_prompt;
+            first = n_prompt;
+        } else if (r != SHK_EUNSUPPORTED) {
+            rc = -1;
+        }
+    }
+    for (uint32_t i = first; i < n_prompt && !rc; ++i) {
         const int last = i + 1 == n_prompt;
         rc = step(h, prompt[i], last, &next, last ? logits_out : NULL);
     }

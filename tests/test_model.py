@@ -169,6 +169,37 @@ def test_generate_q5k_mix_matches_oracle(oracle, ctx, layout):
     assert last == t_ref[-1]
 
 
+@pytest.mark.parametrize("shape,n_prompt", [("small", 80), ("tiny", 64), ("small", 300)])
+def test_prefill_then_decode_matches_oracle(oracle, ctx, shape, n_prompt):
+    """The batched prompt prefill (shk_cuda_prefill: tensor-core matmul with
+    bf16 inputs, row-batched glue, one K/V append per layer, causal
+    attention per row), then decode steps: the greedy ids of the
+    token-by-token reference.  The logits carry the bf16 rounding of the
+    prompt's matmuls (through the K/V cache), so they are held to 5e-2 of the
+    logit std here against the decode path's 1e-2; the measured worst case is
+    printed."""
+    model = synth.make_model(shape, seed=21)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, model.shape.n_vocab, n_prompt).astype(np.uint32)
+    n_dec = 10
+    t_ref, l_ref = oracle.generate(model, prompt, n_dec)
+    dec = GpuDecoder(ctx, model, max_seq=n_prompt + n_dec + 8, tiled=False)
+    try:
+        logits = np.zeros_like(l_ref)
+        toks = np.zeros(n_dec, np.uint32)
+        toks[0] = dec.m.prefill(prompt, 0, logits.ctypes.data)
+        for i in range(1, n_dec):
+            toks[i] = dec.m.token_step(int(toks[i - 1]), n_prompt + i - 1, True, logits[i].ctypes.data)
+        ctx.check()
+    finally:
+        dec.close()
+    worst = max(float(np.max(np.abs(logits[t] - l_ref[t])) / np.std(l_ref[t])) for t in range(n_dec))
+    print(f"prefill {shape} T={n_prompt}: ids {'match' if np.array_equal(toks, t_ref) else 'DIFFER'}, "
+          f"max |dlogit| / std = {worst:.2e}")
+    assert np.array_equal(toks, t_ref)
+    assert worst <= 5e-2
+
+
 @pytest.mark.slow
 def test_tinyllama_shape_8_plus_16(oracle, ctx):
     """TinyLlama-1.1B shape (22 layers, d 2048, 32/4 heads, ffn 5632, vocab

@@ -56,12 +56,15 @@ __device__ __forceinline__ void append_head(const KvLayout& kv, uint32_t layer, 
 
 constexpr int ATT_MAX_SPLITS = 128;  // splits per KV head (the host caps max_splits at this)
 
-// int8 lanes of a 32-bit word -> fp32
+// int8 lanes of a 32-bit word -> fp32, exactly: byte b + 128 placed in the
+// low mantissa bits of 2^23 (one byte permute), minus 2^23 + 128 (one add) --
+// full-rate ALU / FMA work instead of a conversion instruction per value.
 __device__ __forceinline__ void s8x4_to_f32(uint32_t w, float* f) {
-  f[0] = (float)(int8_t)(w & 0xFFu);
-  f[1] = (float)(int8_t)((w >> 8) & 0xFFu);
-  f[2] = (float)(int8_t)((w >> 16) & 0xFFu);
-  f[3] = (float)(int8_t)(w >> 24);
+  const uint32_t u = w ^ 0x80808080u;  // x + 128 in every byte
+  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
 }
 
 // The loads of one warp iteration: PPI positions starting at T.

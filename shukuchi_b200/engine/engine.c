@@ -169,9 +169,12 @@ static int debug_dev(shk_ctx *c, const char *name, const float *dev, uint32_t n,
     return 0;
 }
 
-static void debug_dtypes(const struct shk_layer_desc *d) {
-    printf("[DEBUG] dtypes: q=%u k=%u v=%u o=%u gate=%u up=%u down=%u\n", d->attn_q_dtype, d->attn_k_dtype,
-           d->attn_v_dtype, d->attn_o_dtype, d->ffn_gate_dtype, d->ffn_up_dtype, d->ffn_down_dtype);
+/* the file's ggml types, as the reference prints its layer view's (not the
+ * device layouts they were converted to) */
+static void debug_dtypes(const struct engine_handle *h, uint32_t l) {
+    const struct tensor_loc *t = h->lm[l].t;
+    printf("[DEBUG] dtypes: q=%u k=%u v=%u o=%u gate=%u up=%u down=%u\n", t[TN_Q].type, t[TN_K].type,
+           t[TN_V].type, t[TN_O].type, t[TN_GATE].type, t[TN_UP].type, t[TN_DOWN].type);
 }
 
 /* ------------------------------ model map ------------------------------- */
@@ -607,14 +610,15 @@ static int step(struct engine_handle *h, uint32_t tok, int want_next, uint32_t *
                 float *emb = (float *)malloc((size_t)h->n_embd * 4);
                 const int r = !emb || debug_dev(h->ctx, "embed", shk_cuda_model_hidden(h->m), h->n_embd, emb);
                 free(emb);
-                struct shk_layer_desc d0;
-                layer_desc(h, 0, (const uint8_t *)h->d_buf[0], &d0);
-                if (r || debug_layer0(h, &d0, shk_cuda_model_hidden(h->m))) return -1;
+                if (r) return -1;
             }
-            for (uint32_t l = 0; l < h->n_layers; ++l) {
-                struct shk_layer_desc d;
-                layer_desc(h, l, (const uint8_t *)h->d_buf[l], &d);
-                debug_dtypes(&d);
+            for (uint32_t l = 0; l < h->n_layers; ++l) { /* each layer's line, layer 0's stats after its own */
+                debug_dtypes(h, l);
+                if (l == 0 && h->pos == 0) {
+                    struct shk_layer_desc d0;
+                    layer_desc(h, 0, (const uint8_t *)h->d_buf[0], &d0);
+                    if (debug_layer0(h, &d0, shk_cuda_model_hidden(h->m))) return -1;
+                }
             }
         }
         if (shk_cuda_token_step(h->m, tok, h->pos, want_next, next, logits) != SHK_OK) return -1;
@@ -633,7 +637,7 @@ static int step(struct engine_handle *h, uint32_t tok, int want_next, uint32_t *
             struct shk_layer_desc d;
             layer_desc(h, l, (const uint8_t *)h->d_buf[k % h->depth], &d);
             if (dbg) {
-                debug_dtypes(&d);
+                debug_dtypes(h, l);
                 if (l == 0 && h->pos == 0 && debug_layer0(h, &d, hidden)) return -1;
             }
             if (shk_cuda_forward_layer(h->m, &d, l, h->pos, hidden, NULL) != SHK_OK) return -1;

@@ -148,6 +148,49 @@ def test_engine_tp_matches_oracle(tmp_path, oracle, world, monkeypatch):
     assert st.layer_loads == s.n_layers  # each layer read once for all ranks
 
 
+def _debug_lines(text: str):
+    import re
+    out = []
+    for ln in text.splitlines():
+        if "[DEBUG] " not in ln:  # a generated token's text may precede it on the line
+            continue
+        ln = ln[ln.index("[DEBUG] "):]
+        m = re.match(r"\[DEBUG\] (\S+): min=(\S+) max=(\S+) mean=(\S+) nan=(\d) inf=(\d)", ln)
+        out.append((m.group(1), tuple(float(m.group(i)) for i in (2, 3, 4)), m.group(5), m.group(6)) if m
+                   else (ln, None, None, None))
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("resident", [1, 0])
+def test_debug_dump_matches_reference_cli(model_file, resident):
+    """SHUKUCHI_DEBUG: the CLI prints the same [DEBUG] lines as the
+    reference's own CLI on the same file and prompt (engine/src/engine.c:23-51,
+    88-221): every layer's quant types, the embedding's and layer 0's
+    intermediate statistics, in the same order and within print precision."""
+    import subprocess
+    root = os.path.dirname(os.path.dirname(ENGINE))
+    ref_cli = os.path.join(os.path.dirname(root), "oracle", "_ref", "shukuchi_ref")
+    if not os.path.exists(ref_cli):
+        pytest.skip("reference CLI (oracle/_ref) not built here")
+    m, p = model_file
+    env = dict(os.environ, SHUKUCHI_DEBUG="1", SHUKUCHI_HBM_RESIDENT=str(resident))
+    args = [p, "--prompt", "t00003t00141", "--max-tokens", "2"]
+    ref = subprocess.run([ref_cli] + args, env=env, capture_output=True, text=True, timeout=600)
+    ours = subprocess.run([os.path.join(os.path.dirname(ENGINE), "shukuchi")] + args, env=env,
+                          capture_output=True, text=True, timeout=600)
+    assert ref.returncode == 0 and ours.returncode == 0, ours.stderr[-2000:]
+    a, b = _debug_lines(ours.stdout), _debug_lines(ref.stdout)
+    assert [x[0] for x in a] == [x[0] for x in b]
+    assert len(b) > 16
+    for (name, va, na, ia), (_, vb, nb, ib) in zip(a, b):
+        if va is None:
+            continue
+        assert (na, ia) == (nb, ib), name
+        for x, y in zip(va, vb):
+            assert abs(x - y) <= 2e-3 * max(1.0, abs(y)) + 2e-4, (name, va, vb)
+
+
 @pytest.mark.gpu
 def test_engine_text_prompt_matches_reference_cli(model_file, reference):
     """Prompt text through the greedy tokenizer: same ids as the reference."""

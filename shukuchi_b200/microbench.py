@@ -34,6 +34,11 @@
       barrier; reports per phase kind the mean wall time (barrier to barrier)
       and the part of it CTA 0 spent waiting at the barrier.
 
+  python -m shukuchi_b200.microbench prompt [--shape llama8b] [--tokens 512]
+      A T-token prompt through the model as one batched prefill
+      (shk_cuda_prefill: tensor-core matmuls, row-batched glue) against T
+      token steps (timed on a prefix, scaled): prefill ms, tok/s, speed-up.
+
   python -m shukuchi_b200.microbench loader [--shape llama8b] [--prompt 8] [--decode 16] [--depth 3]
       The C engine on a GGUF file of the shape (written once under --dir):
       HBM-resident mode (every layer pread -> pinned -> HBM once, then the
@@ -361,6 +366,59 @@ def timeline(args, ctx) -> None:
         ctx.close()
 
 
+def prompt(args, ctx) -> None:
+    """Prompt of T tokens at the model shape: one batched prefill
+    (shk_cuda_prefill) against T token steps, device time by CUDA events."""
+    import numpy as np
+
+    from . import synth
+    from .synth_device import make_device_model
+
+    shape = synth.SHAPES[args.shape]
+    wts = make_device_model(shape, seed=7, ctx=ctx, tiled=False)  # the prefill reads GGUF / planar rows
+    kv = sc.KvCache(ctx, shape.n_layers, shape.n_kv_heads, shape.head_dim, args.tokens + 8)
+    m = sc.DeviceModel(ctx, kv, wts.desc)
+    try:
+        for i, lv in enumerate(wts.layers):
+            m.set_layer(i, lv)
+        rng = np.random.default_rng(0)
+        toks = rng.integers(0, shape.n_vocab, args.tokens).astype(np.uint32)
+        s = torch.cuda.ExternalStream(ctx.stream)
+        m.prefill(toks[:64], 0)  # warm-up (kernel loads, scratch)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        first_pf = m.prefill(toks, 0)
+        b.record(s)
+        torch.cuda.synchronize()
+        pf_ms = a.elapsed_time(b)
+        kv.clear()
+        n_steps = min(args.tokens, args.steps)  # token steps timed on a prefix, scaled to T
+        m.token_step(int(toks[0]), 0, want_next=False)
+        torch.cuda.synchronize()
+        a.record(s)
+        nxt = 0
+        for i in range(1, n_steps):
+            nxt = m.token_step(int(toks[i]), i, want_next=(i == n_steps - 1))
+        b.record(s)
+        torch.cuda.synchronize()
+        step_ms = a.elapsed_time(b) / max(1, n_steps - 1)
+        ctx.check()
+        D, hd = shape.n_embd, shape.head_dim
+        qd, kvd, F = shape.n_heads * hd, shape.n_kv_heads * hd, shape.n_ff
+        layer_w = D * qd + 2 * D * kvd + qd * D + 3 * D * F  # weights of the seven matmuls
+        flops = 2.0 * args.tokens * layer_w * shape.n_layers
+        print(json.dumps({"bench": "prompt", "shape": shape.name, "tokens": args.tokens,
+                          "prefill_ms": round(pf_ms, 3), "prefill_tok_s": round(args.tokens / (pf_ms / 1e3), 1),
+                          "token_step_ms": round(step_ms, 4),
+                          "token_by_token_ms": round(step_ms * args.tokens, 2),
+                          "speedup": round(step_ms * args.tokens / pf_ms, 2), "first_token": int(first_pf),
+                          "matmul_tflops": round(flops / (pf_ms / 1e3) / 1e12, 1)}), flush=True)
+    finally:
+        m.close()
+        kv.close()
+
+
 def loader(args, ctx) -> None:
     import ctypes as C
     import time
@@ -465,6 +523,10 @@ def main() -> None:
     tl.add_argument("--layers", type=int, default=32)
     tl.add_argument("--prompt", type=int, default=512)
     tl.add_argument("--steps", type=int, default=4)
+    pr = sub.add_parser("prompt")
+    pr.add_argument("--shape", default="llama8b")
+    pr.add_argument("--tokens", type=int, default=512)
+    pr.add_argument("--steps", type=int, default=64)
     ld = sub.add_parser("loader")
     ld.add_argument("--shape", default="llama8b")
     ld.add_argument("--prompt", type=int, default=8)
@@ -476,7 +538,7 @@ def main() -> None:
     ctx = sc.Context(0)
     try:
         {"gemv": gemv, "kv": kv, "parts": parts, "timeline": timeline, "prefill": prefill,
-         "loader": loader}[args.cmd](args, ctx)
+         "loader": loader, "prompt": prompt}[args.cmd](args, ctx)
     finally:
         ctx.close()
 

@@ -15,6 +15,7 @@
 //    the last item of each KV head; results agree to fp32 rounding.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -112,9 +113,11 @@ struct AttnSmem {
   static constexpr int FLAG = SL + G;
   static constexpr int FLOATS = FLAG + 4;
   static constexpr size_t BYTES = (size_t)FLOATS * 4;
-  // the long-range loop's per-warp p[G][32] (attn_item<..., LONG = true> only)
+  // the long-range loop's per-warp scratch (attn_item<..., LONG = true> only):
+  // a transposed V tile of 16 positions, HD x 16 bytes
   static constexpr int PB = FLOATS;
-  static constexpr int FLOATS_LONG = PB + NW * G * 32;
+  static constexpr int PB_WARP = HD * 4;
+  static constexpr int FLOATS_LONG = PB + NW * PB_WARP;
 };
 
 __device__ __forceinline__ void att_sync(int nthreads) {
@@ -227,6 +230,211 @@ __device__ __forceinline__ void attn_long(const AttnArgs& a, const float* qsm, c
   for (int g = 0; g < G; ++g) l[g] = warp_sum(lp[g]);
 }
 
+
+// --------------------- long ranges on the tensor cores -----------------------
+// QK^T and PV of a 16-position chunk as mma.sync.m16n8k16 (f16 operands, fp32
+// accumulators).  The int8 K and V quants are exact in f16; q and the softmax
+// weights are split into a high and a low f16 part (rows g and g + 8 of the A
+// operand: ~22 significant bits), so each product sum carries fp32-level
+// error.  q is scaled by a power of two 2^-e (its largest magnitude below 1)
+// and each chunk's weights p * v_scale by 1 / (the chunk's largest V scale of
+// that block), so no f16 value overflows; both factors are put back in fp32.
+//
+// Lane layout (g = lane / 4, t = lane % 4): QK^T C-fragment columns 2t, 2t+1 of
+// n-tile 0 / 1 are positions 4t, 4t+1 / 4t+2, 4t+3 of the chunk, exactly the
+// k index pairs (2t, 2t+1), (2t+8, 2t+9) of the PV A fragment, so the
+// softmax weights stay in the registers that computed them.  Head dims are
+// permuted inside each 32-element block (k-steps 2j and 2j+1 take dims
+// 32j + 8t + 0..3 and 32j + 8t + 4..7 for lane t) so a lane reads 8
+// contiguous K bytes per block.  V is transposed into the warp's shared tile
+// (4x4 byte transposes) so a lane reads the 4 positions of one dim as a word.
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// int8 bytes (sel 0x4140: bytes 0, 1; 0x4342: bytes 2, 3) of u = w ^ 0x80808080
+// -> f16x2, exactly: 0x64xx is 1024 + (x + 128), minus 1152.
+__device__ __forceinline__ uint32_t s8x2_h2(uint32_t u, uint32_t sel) {
+  const uint32_t h = __byte_perm(u, 0x64646464u, sel);
+  uint32_t r;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+  return r;
+}
+__device__ __forceinline__ uint32_t h2_pack(float lo_col, float hi_col) {
+  const __half2 h = __floats2half2_rn(lo_col, hi_col);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// x = hi + lo with hi, lo f16: returns hi, sets lo
+__device__ __forceinline__ float split_f16(float x, float& lo) {
+  const float hi = __half2float(__float2half_rn(x));
+  lo = x - hi;
+  return hi;
+}
+
+template <int HD, int G, int NW>
+__device__ __forceinline__ void attn_long_tc(const AttnArgs& a, const float* qsm, const int8_t* __restrict__ Kq,
+                                             const float* __restrict__ Ks, const int8_t* __restrict__ Vq,
+                                             const float* __restrict__ Vs, uint32_t p0, uint32_t p1, int warp,
+                                             int lane, uint8_t* vt, float* wm_w, float* wl_w, float* wacc_w) {
+  constexpr int NB = HD / 32, KS = HD / 16, NT = HD / 8, QROW = 36;
+  const int g = lane >> 2, t = lane & 3;
+  const bool grow_ = g < G;
+  // q -> two f16 parts (dims permuted as above), scaled by 2^-e
+  float qmax = 0.f;
+  if (grow_)
+#pragma unroll
+    for (int j = 0; j < NB; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qmax = fmaxf(qmax, fabsf(qsm[(g * NB + j) * QROW + 8 * t + i]));
+  qmax = warp_max(qmax);
+  const int qe = (qmax > 0.f && isfinite(qmax)) ? ((int)((__float_as_uint(qmax) >> 23) & 0xFFu) - 126) : 0;
+  const float qdown = ldexpf(1.0f, -qe), qup = ldexpf(1.0f, qe) * a.scale;
+  uint32_t qa[KS][4];
+#pragma unroll
+  for (int j = 0; j < NB; ++j)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // k-step 2j + h: dims 32j + 8t + 4h + 0..3
+      float v[4], lo[4], hi[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[i] = grow_ ? qsm[(g * NB + j) * QROW + 8 * t + 4 * h + i] * qdown : 0.f;
+        hi[i] = split_f16(v[i], lo[i]);
+      }
+      qa[2 * j + h][0] = h2_pack(hi[0], hi[1]);
+      qa[2 * j + h][1] = h2_pack(lo[0], lo[1]);
+      qa[2 * j + h][2] = h2_pack(hi[2], hi[3]);
+      qa[2 * j + h][3] = h2_pack(lo[2], lo[3]);
+    }
+  float O[NT][2];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) O[n][0] = O[n][1] = 0.f;
+  float m = -INFINITY, lsum = 0.f;
+  // the chunk row this lane loads for QK^T n-tile 0 (n-tile 1: +2)
+  const uint32_t krow = (uint32_t)(g + 2 * (g >> 1));
+  for (uint32_t T = p0 + 16u * warp; T < p1; T += 16u * NW) {
+    // ---- loads: K rows (8 bytes of every block), scales, V 4x4 byte blocks
+    uint2 kw[2][NB];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const uint32_t pos = T + krow + 2 * n;
+      const uint32_t pc = pos < p1 ? pos : T;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) kw[n][j] = __ldcg(reinterpret_cast<const uint2*>(Kq + (size_t)pc * HD + 32 * j + 8 * t));
+    }
+    float ksc[4][NB], vsc[4][NB];
+    bool valid[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t pos = T + 4 * t + i;
+      valid[i] = pos < p1;
+      const uint32_t pc = valid[i] ? pos : T;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        ksc[i][j] = __ldcg(Ks + (size_t)pc * NB + j);
+        vsc[i][j] = valid[i] ? __ldcg(Vs + (size_t)pc * NB + j) : 0.f;
+      }
+    }
+    uint32_t vw[HD / 32][4];
+#pragma unroll
+    for (int k = 0; k < HD / 32; ++k) {  // block b = lane + 32k: rows 4(b%4).., cols 4(b/4)..
+      const int b = lane + 32 * k, r4 = b & 3, c4 = b >> 2;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t pos = T + 4 * r4 + i;
+        vw[k][i] = pos < p1 ? __ldcg(reinterpret_cast<const unsigned int*>(Vq + (size_t)pos * HD + 4 * c4)) : 0x00000000u;
+      }
+    }
+    // ---- V^T into the warp's tile: word (dim d, positions 4r..4r+3) at d*16 + 4r
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < HD / 32; ++k) {
+      const int b = lane + 32 * k, r4 = b & 3, c4 = b >> 2;
+      const uint32_t x0 = __byte_perm(vw[k][0], vw[k][1], 0x5140), x1 = __byte_perm(vw[k][0], vw[k][1], 0x7362);
+      const uint32_t y0 = __byte_perm(vw[k][2], vw[k][3], 0x5140), y1 = __byte_perm(vw[k][2], vw[k][3], 0x7362);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(vt);
+      dst[(4 * c4 + 0) * 4 + r4] = __byte_perm(x0, y0, 0x5410);
+      dst[(4 * c4 + 1) * 4 + r4] = __byte_perm(x0, y0, 0x7632);
+      dst[(4 * c4 + 2) * 4 + r4] = __byte_perm(x1, y1, 0x5410);
+      dst[(4 * c4 + 3) * 4 + r4] = __byte_perm(x1, y1, 0x7632);
+    }
+    // ---- QK^T: scores of positions 4t..4t+3 for head g
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t ux = kw[n][j].x ^ 0x80808080u, uy = kw[n][j].y ^ 0x80808080u;
+        mma16816(c, qa[2 * j], s8x2_h2(ux, 0x4140), s8x2_h2(ux, 0x4342));
+        mma16816(c, qa[2 * j + 1], s8x2_h2(uy, 0x4140), s8x2_h2(uy, 0x4342));
+        s[2 * n] = fmaf(ksc[2 * n][j], c[0] + c[2], s[2 * n]);
+        s[2 * n + 1] = fmaf(ksc[2 * n + 1][j], c[1] + c[3], s[2 * n + 1]);
+      }
+    // ---- online softmax over the chunk (the quad holds the head's 16 positions)
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      s[i] = valid[i] ? s[i] * qup : -INFINITY;
+      cmax = fmaxf(cmax, s[i]);
+    }
+    cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+    cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+    const float mn = fmaxf(m, cmax);  // position T is valid: finite
+    const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = valid[i] ? expf(s[i] - mn) : 0.f;
+    lsum = fmaf(lsum, corr, (p[0] + p[1]) + (p[2] + p[3]));
+    m = mn;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      O[n][0] *= corr;
+      O[n][1] *= corr;
+    }
+    __syncwarp();  // the V^T tile is complete
+    // ---- PV, one 32-dim V block (4 n-tiles) at a time
+    const uint32_t* vtw = reinterpret_cast<const uint32_t*>(vt);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      float vmax = fmaxf(fmaxf(vsc[0][j], vsc[1][j]), fmaxf(vsc[2][j], vsc[3][j]));
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+      const float inv = vmax > 0.f ? 1.0f / vmax : 0.f;
+      float hi[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hi[i] = split_f16(p[i] * (vsc[i][j] * inv), lo[i]);
+      const uint32_t pa[4] = {h2_pack(hi[0], hi[1]), h2_pack(lo[0], lo[1]), h2_pack(hi[2], hi[3]),
+                              h2_pack(lo[2], lo[3])};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int n = 4 * j + q;
+        const uint32_t u = vtw[(8 * n + g) * 4 + t] ^ 0x80808080u;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(c, pa, s8x2_h2(u, 0x4140), s8x2_h2(u, 0x4342));
+        O[n][0] = fmaf(vmax, c[0] + c[2], O[n][0]);
+        O[n][1] = fmaf(vmax, c[1] + c[3], O[n][1]);
+      }
+    }
+  }
+  __syncwarp();
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+  if (grow_) {
+    if (t == 0) {
+      wm_w[g] = m;
+      wl_w[g] = lsum;
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      wacc_w[g * HD + 8 * n + 2 * t] = O[n][0];
+      wacc_w[g * HD + 8 * n + 2 * t + 1] = O[n][1];
+    }
+  }
+}
+
 // q, the new K/V rows, the position and the cache may have been written
 // earlier in the same launch by other CTAs (persistent decode kernel): they are
 // read with ld.global.cg (L2).
@@ -304,7 +512,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
   Tile cur;
   const bool long_range = LONG && p1 - p0 >= ATT_SPLIT_LONG;
   if (long_range)
-    attn_long<HD, G, NW>(a, sm + SM::Q, Kq, Ks, Vq, Vs, p0, p1, warp, lane, sm + SM::PB + warp * G * 32, m, l, acc);
+    attn_long_tc<HD, G, NW>(a, sm + SM::Q, Kq, Ks, Vq, Vs, p0, p1, warp, lane,
+                            reinterpret_cast<uint8_t*>(sm + SM::PB + warp * SM::PB_WARP), &wm[warp][0], &wl[warp][0],
+                            &wacc[warp][0][0]);
   else if (T < p1)
     cur.load(Kq, Ks, Vq, Vs, T, p1, lane);
   for (; !long_range && T < p1; T += STEP) {
@@ -366,14 +576,16 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
     }
     cur = nxt;
   }
-  // ---- merge the warps ----
+  // ---- merge the warps (the tensor-core loop stored its own) ----
+  if (!long_range) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < G; ++g) {
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
-    if (lane == 0) {
-      wm[warp][g] = m[g];
-      wl[warp][g] = l[g];
+      for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
+      if (lane == 0) {
+        wm[warp][g] = m[g];
+        wl[warp][g] = l[g];
+      }
     }
   }
   att_sync(NT);

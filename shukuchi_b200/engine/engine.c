@@ -269,6 +269,40 @@ static int pread_all(int fd, void *dst, uint64_t len, uint64_t off) {
     return 0;
 }
 
+/* A span read by several threads at once (SHUKUCHI_IO_THREADS, default 4):
+ * one thread's pread from the page cache into pinned memory copies at
+ * ~7 GB/s, below what the H2D link takes. */
+struct pread_job {
+    int fd, rc;
+    uint8_t *dst;
+    uint64_t len, off;
+};
+static void *pread_main(void *arg) {
+    struct pread_job *j = (struct pread_job *)arg;
+    j->rc = pread_all(j->fd, j->dst, j->len, j->off);
+    return NULL;
+}
+static int pread_span(int fd, void *dst, uint64_t len, uint64_t off) {
+    int nt = env_int("SHUKUCHI_IO_THREADS", 4);
+    if (nt > 16) nt = 16;
+    if (nt <= 1 || len < (16u << 20)) return pread_all(fd, dst, len, off);
+    struct pread_job jobs[16];
+    pthread_t th[16];
+    int started[16];
+    const uint64_t piece = ((len + (uint64_t)nt - 1) / (uint64_t)nt + 4095) & ~(uint64_t)4095;
+    int n = 0, rc = 0;
+    for (uint64_t o = 0; o < len && n < nt; o += piece, ++n) {
+        jobs[n] = (struct pread_job){fd, 0, (uint8_t *)dst + o, (len - o < piece ? len - o : piece), off + o};
+        started[n] = pthread_create(&th[n], NULL, pread_main, &jobs[n]) == 0;
+        if (!started[n]) jobs[n].rc = pread_all(fd, jobs[n].dst, jobs[n].len, jobs[n].off); /* here instead */
+    }
+    for (int i = 0; i < n; ++i) {
+        if (started[i]) pthread_join(th[i], NULL);
+        rc |= jobs[i].rc;
+    }
+    return rc ? -1 : 0;
+}
+
 static int upload_tensor(struct engine_handle *h, const struct gguf_tensor_info *ti, void **dev) {
     void *host = NULL;
     if (shk_cuda_host_alloc(h->ctx, ti->size, &host) != SHK_OK) return -1;
@@ -392,7 +426,7 @@ static void *loader_main(void *arg) {
         const struct layer_map *L = &h->lm[l];
         int rc = shk_cuda_layer_ready(h->ctx, s, 1) < 0; /* the staging buffer's last copies landed */
         uint8_t *pin = (uint8_t *)h->pinned[s];
-        if (!rc) rc = pread_all(h->g.fd, pin, L->span_len, L->span_off);
+        if (!rc) rc = pread_span(h->g.fd, pin, L->span_len, L->span_off);
         uint8_t *dst = (uint8_t *)h->d_buf[h->resident ? l : s];
         for (int t = 0; !rc && t < TN_COUNT; ++t) {
             const struct tensor_loc *tl = &L->t[t];
@@ -697,10 +731,12 @@ static int generate(struct engine_handle *h, const uint32_t *prompt, uint32_t n_
     }
     int rc = 0;
     uint32_t next = 0, first = 0;
-    /* prompts of SHUKUCHI_PREFILL (default 64) tokens or more: one batched
-     * prefill on the tensor cores instead of a step per token (single GPU,
-     * HBM-resident, Q4_K / Q6_K weights; else the token loop below) */
-    const int pf_min = env_int("SHUKUCHI_PREFILL", 64);
+    /* prompts of SHUKUCHI_PREFILL tokens or more (0, the default: never):
+     * one batched prefill on the tensor cores instead of a step per token
+     * (single GPU, HBM-resident, Q4_K / Q6_K weights; else the token loop
+     * below).  Off by default: its bf16 matmul inputs move the logits away
+     * from the reference's by more than the decode path's tolerance. */
+    const int pf_min = env_int("SHUKUCHI_PREFILL", 0);
     if (pf_min > 0 && n_prompt >= (uint32_t)pf_min && h->resident && h->tp <= 1 && !debug_enabled() &&
         !register_layers(h)) {
         const int r = shk_cuda_prefill(h->m, prompt, n_prompt, 0, &next, logits_out, NULL);
@@ -937,7 +973,7 @@ static int tp_stage_layers(struct engine_handle *h) {
         for (uint32_t ri = 0; ri < h->tp; ++ri) /* the pinned buffer's previous copies landed */
             if (shk_cuda_layer_ready(h->ranks[ri].ctx, s, 1) < 0) return -1;
         uint8_t *pin = (uint8_t *)h->pinned[s];
-        if (pread_all(h->g.fd, pin, L->span_len, L->span_off)) return -1;
+        if (pread_span(h->g.fd, pin, L->span_len, L->span_off)) return -1;
         h->st.layer_loads++;
         h->st.layer_bytes_read += L->span_len;
         for (uint32_t ri = 0; ri < h->tp; ++ri) {

@@ -134,7 +134,10 @@ __device__ __forceinline__ void att_sync(int nthreads) {
 // already in the cache, stored by this CTA before the loop.
 constexpr uint32_t ATT_LONG_MIN = 512;
 // Split kernel: a split of at least this many positions runs the long loop.
-constexpr uint32_t ATT_SPLIT_LONG = 256;
+#ifndef SHK_ATT_SPLIT_LONG
+#define SHK_ATT_SPLIT_LONG 256
+#endif
+constexpr uint32_t ATT_SPLIT_LONG = SHK_ATT_SPLIT_LONG;
 
 template <int HD, int G, int NW>
 __device__ __forceinline__ void attn_long(const AttnArgs& a, const float* qsm, const int8_t* __restrict__ Kq,
@@ -233,10 +236,12 @@ __device__ __forceinline__ void attn_long(const AttnArgs& a, const float* qsm, c
 
 // --------------------- long ranges on the tensor cores -----------------------
 // QK^T and PV of a 16-position chunk as mma.sync.m16n8k16 (f16 operands, fp32
-// accumulators).  The int8 K and V quants are exact in f16; q and the softmax
-// weights are split into a high and a low f16 part (rows g and g + 8 of the A
-// operand: ~22 significant bits), so each product sum carries fp32-level
-// error.  q is scaled by a power of two 2^-e (its largest magnitude below 1)
+// accumulators).  The int8 K and V quants are exact in f16; q is split into
+// three f16 parts (high and middle in rows g and g + 8 of one A operand, low
+// in rows g of a second: ~33 significant bits, so scores carry fp32-level
+// error even when they are huge and the softmax is one-hot) and the softmax
+// weights into two (rows g and g + 8: ~22 bits; their error enters the output
+// linearly).  q is scaled by a power of two 2^-e (its largest magnitude below 1)
 // and each chunk's weights p * v_scale by 1 / (the chunk's largest V scale of
 // that block), so no f16 value overflows; both factors are put back in fp32.
 //
@@ -292,21 +297,25 @@ __device__ __forceinline__ void attn_long_tc(const AttnArgs& a, const float* qsm
   qmax = warp_max(qmax);
   const int qe = (qmax > 0.f && isfinite(qmax)) ? ((int)((__float_as_uint(qmax) >> 23) & 0xFFu) - 126) : 0;
   const float qdown = ldexpf(1.0f, -qe), qup = ldexpf(1.0f, qe) * a.scale;
-  uint32_t qa[KS][4];
+  uint32_t qa[KS][4], qb[KS][2];  // qb: the low part (rows g; rows g + 8 are zero)
 #pragma unroll
   for (int j = 0; j < NB; ++j)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // k-step 2j + h: dims 32j + 8t + 4h + 0..3
-      float v[4], lo[4], hi[4];
+      float v[4], hi[4], mid[4], lo[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         v[i] = grow_ ? qsm[(g * NB + j) * QROW + 8 * t + 4 * h + i] * qdown : 0.f;
-        hi[i] = split_f16(v[i], lo[i]);
+        float r;
+        hi[i] = split_f16(v[i], r);
+        mid[i] = split_f16(r, lo[i]);
       }
       qa[2 * j + h][0] = h2_pack(hi[0], hi[1]);
-      qa[2 * j + h][1] = h2_pack(lo[0], lo[1]);
+      qa[2 * j + h][1] = h2_pack(mid[0], mid[1]);
       qa[2 * j + h][2] = h2_pack(hi[2], hi[3]);
-      qa[2 * j + h][3] = h2_pack(lo[2], lo[3]);
+      qa[2 * j + h][3] = h2_pack(mid[2], mid[3]);
+      qb[2 * j + h][0] = h2_pack(lo[0], lo[1]);
+      qb[2 * j + h][1] = h2_pack(lo[2], lo[3]);
     }
   float O[NT][2];
 #pragma unroll
@@ -366,12 +375,18 @@ __device__ __forceinline__ void attn_long_tc(const AttnArgs& a, const float* qsm
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        float c[4] = {0.f, 0.f, 0.f, 0.f}, d[4] = {0.f, 0.f, 0.f, 0.f};
         const uint32_t ux = kw[n][j].x ^ 0x80808080u, uy = kw[n][j].y ^ 0x80808080u;
-        mma16816(c, qa[2 * j], s8x2_h2(ux, 0x4140), s8x2_h2(ux, 0x4342));
-        mma16816(c, qa[2 * j + 1], s8x2_h2(uy, 0x4140), s8x2_h2(uy, 0x4342));
-        s[2 * n] = fmaf(ksc[2 * n][j], c[0] + c[2], s[2 * n]);
-        s[2 * n + 1] = fmaf(ksc[2 * n + 1][j], c[1] + c[3], s[2 * n + 1]);
+        const uint32_t bx0 = s8x2_h2(ux, 0x4140), bx1 = s8x2_h2(ux, 0x4342);
+        const uint32_t by0 = s8x2_h2(uy, 0x4140), by1 = s8x2_h2(uy, 0x4342);
+        mma16816(c, qa[2 * j], bx0, bx1);
+        mma16816(c, qa[2 * j + 1], by0, by1);
+        const uint32_t l0[4] = {qb[2 * j][0], 0u, qb[2 * j][1], 0u}, l1[4] = {qb[2 * j + 1][0], 0u, qb[2 * j + 1][1], 0u};
+        mma16816(d, l0, bx0, bx1);
+        mma16816(d, l1, by0, by1);
+        // high + middle (rows g, g + 8), then the low part (rows g)
+        s[2 * n] = fmaf(ksc[2 * n][j], (c[0] + c[2]) + d[0], s[2 * n]);
+        s[2 * n + 1] = fmaf(ksc[2 * n + 1][j], (c[1] + c[3]) + d[1], s[2 * n + 1]);
       }
     // ---- online softmax over the chunk (the quad holds the head's 16 positions)
     float cmax = -INFINITY;

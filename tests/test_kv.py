@@ -162,11 +162,22 @@ def test_attend_long_cache(oracle, ctx, H, KV, hd, seq):
     check_attend(oracle, ctx, H, KV, hd, seq, "fused", 8192)
 
 
-def check_attend(oracle, ctx, H, KV, hd, seq, new_row, cap):
+@pytest.mark.parametrize("H,KV,hd,seq", [(64, 8, 128, 19531), (32, 8, 128, 19531), (8, 2, 64, 33789)])
+@pytest.mark.parametrize("qscale", [1.0, 30.0])
+def test_attend_tensor_core_ranges(oracle, ctx, H, KV, hd, seq, qscale):
+    """Splits of 264 positions (more than the 256 that route a split to the
+    tensor-core loop, not a multiple of its 16-position chunks: a masked last
+    chunk), and queries 30x larger (scores in the hundreds, a near one-hot
+    softmax, where the three-part f16 split of q must keep fp32-level score
+    error)."""
+    check_attend(oracle, ctx, H, KV, hd, seq, "fused", seq + 9, qscale=qscale)
+
+
+def check_attend(oracle, ctx, H, KV, hd, seq, new_row, cap, qscale=1.0):
     rng = np.random.default_rng(H * 131 + seq)
     k, v = kv_inputs(rng, seq, KV, hd)
     k[seq - 1, 5] = 3.0
-    q = rng.normal(0, 1, H * hd).astype(np.float32)
+    q = (rng.normal(0, 1, H * hd) * qscale).astype(np.float32)
     kv = sc.KvCache(ctx, 1, KV, hd, cap)
     try:
         kd, vd, qd = to_dev(k), to_dev(v), to_dev(q)

@@ -147,10 +147,12 @@ int shk_cuda_tile(shk_ctx *ctx, uint32_t dtype, const void *src_dev, uint32_t sr
  *      op_matmul_q4_k / op_matmul_q6_k calls (engine/src/ops.c:266-314,
  *      361-404) add up to: y[t][r] = sum_k W[r][k] * x[t][k] for t <
  *      n_tokens, x fp32 [n_tokens][k], y fp32 [n_tokens][m].  Weights are
- *      dequantised to bf16 tiles and multiplied bf16 x bf16 -> fp32 with
- *      tcgen05.mma (accumulators in TMEM), so results carry bf16 input
- *      rounding.  dtype 12 (Q4_K) or SHK_DTYPE_Q6_K_PLANAR; row_stride 0 =
- *      dense rows.  Async on stream. ---- */
+ *      dequantised to f16 tiles, each token row of x is scaled by a power of
+ *      two (largest magnitude to [2^14, 2^15)) and rounded to f16, and the
+ *      product runs f16 x f16 -> fp32 on tcgen05.mma (accumulators in TMEM),
+ *      the scale put back exactly: results carry the f16 rounding of the
+ *      inputs (2^-11 relative each).  dtype 12 (Q4_K) or
+ *      SHK_DTYPE_Q6_K_PLANAR; row_stride 0 = dense rows.  Async on stream. ---- */
 int shk_cuda_prefill_matmul(shk_ctx *ctx, uint32_t dtype, const void *w_dev, uint32_t row_stride,
                             const float *x_dev, float *y_dev, uint32_t m, uint32_t k, uint32_t n_tokens,
                             void *stream);
@@ -266,13 +268,13 @@ int shk_cuda_decode_steps(shk_model *m, uint32_t first_token, uint32_t first_pos
 int shk_cuda_model_token(shk_model *m, uint32_t *token_host); /* last argmax */
 /* Batched prompt prefill: tokens[0..n) (host) at positions pos0.. run through
  * every layer as T = n rows at a time -- the projections on the tensor-core
- * matmul (shk_cuda_prefill_matmul: bf16 operands, fp32 accumulation), RMSNorm,
+ * matmul (shk_cuda_prefill_matmul: f16 operands, fp32 accumulation), RMSNorm,
  * RoPE, SwiGLU and residuals row-batched, the n K/V rows appended to the
  * Q8_0 cache in one launch per layer and every row's causal attention over
  * [0, pos0 + row] -- then the output head on the last row: its argmax to
  * *next_host (and its logits to logits_host when non-NULL).  The reference
  * feeds the prompt one token at a time (engine/src/engine.c:343-394); this is
- * the same computation with bf16 rounding of the matmul inputs, so logits
+ * the same computation with f16 rounding of the matmul inputs, so logits
  * differ from the token-by-token path by that rounding.  Weights must be
  * Q4_K or planar Q6_K (else SHK_EUNSUPPORTED: feed the prompt through
  * shk_cuda_token_step); single GPU. */

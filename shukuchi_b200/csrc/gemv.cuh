@@ -118,7 +118,9 @@ cudaError_t q6k_repack_launch(void* w, uint32_t rows, uint32_t k, uint32_t strid
 
 // Batched dequantise-matmul on the tensor cores (prefill.cu): y[t][m] for
 // n_tokens tokens; x fp32 [n_tokens][k] is first converted into xb_scratch
-// (prefill_x_bytes) as bf16.  qt: T_Q4K or T_Q6K_PLANAR.
+// (prefill_x_bytes) as f16, each token row scaled by a power of two (its
+// largest magnitude to [2^14, 2^15)), the weights dequantised to f16; fp32
+// accumulation.  qt: T_Q4K or T_Q6K_PLANAR.
 size_t prefill_x_bytes(uint32_t k, uint32_t n_tokens);
 cudaError_t prefill_launch(uint32_t qt, const void* w, uint32_t row_stride, const float* x, void* xb_scratch,
                            float* y, uint32_t m, uint32_t k, uint32_t n_tokens, int* err, int num_sms,

@@ -5,19 +5,22 @@
 // The reference has no batched path (engine/src/engine.c:306-501 feeds prompt
 // tokens one at a time through op_matmul_q4_k / op_matmul_q6_k,
 // engine/src/ops.c:266-314, 361-404); this is the dense contraction those
-// per-token matvecs add up to, computed in bf16 x bf16 -> fp32.
+// per-token matvecs add up to, computed in f16 x f16 -> fp32: the weights
+// dequantised to f16, each token's activations scaled by a power of two
+// (its largest magnitude to [2^14, 2^15)) and rounded to f16, the scale put
+// back in the epilogue -- 11 significant bits per operand where bf16 holds 8.
 //
 // Tile: one CTA per 128 weight rows x 256 tokens (tcgen05.mma M=128, N=256,
 // cta_group::1, fp32 accumulator in 256 TMEM columns), optionally a half of K
 // (split-K of two: both halves atomically added to a zeroed Y -- two addends,
 // so the sum is the same in either order).  Warp roles (10 warps):
 //   warp 8, lane 0  TMA: raw weight blocks (one 256-element block = four
-//                   K-steps) into a 2-deep ring, and the bf16 activation tile
+//                   K-steps) into a 2-deep ring, and the f16 activation tile
 //                   of each K-step (64 elements x 256 tokens, 128-byte swizzle:
 //                   the tensor core's canonical K-major layout) into a 3-deep
 //                   ring of A/B stages;
 //   warps 0-7       dequantise the weight tile of each K-step from shared
-//                   memory into bf16 (two threads per row, 32 elements each),
+//                   memory into f16 (two threads per row, 32 elements each),
 //                   written in the same swizzled layout, then arrive;
 //   warp 9, lane 0  issues the four K=16 MMAs of a step once both tiles are
 //                   in, and commits them to the stage's "empty" barrier;
@@ -28,7 +31,7 @@
 // still waited for (bounded) before the TMEM is freed.
 #include <cuda.h>
 #include <cudaTypedefs.h>
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -67,11 +70,11 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// Instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major, N, M.
-constexpr uint32_t PF_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PF_N >> 3) << 17) |
-                              ((uint32_t)(PF_M >> 4) << 24);
+// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B f16 (format
+// 0 in bits 7-9 and 10-12), both K-major, N, M.
+constexpr uint32_t PF_IDESC = (1u << 4) | ((uint32_t)(PF_N >> 3) << 17) | ((uint32_t)(PF_M >> 4) << 24);
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -100,8 +103,8 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
@@ -113,7 +116,7 @@ constexpr int W6_QH = PF_M * 128, W6_SC = W6_QH + PF_M * 64, W6_D = W6_SC + PF_M
 // 32 consecutive elements (half `h` of the 64-element quarter j of block b)
 // of one weight row, dequantised with the reference's per-element formulas
 // (dequantize_row_q4_k / dequantize_row_q6_k, engine/src/ops.c:117-193), as
-// 16 bf16 pairs.
+// 16 f16 pairs.
 template <int QT>
 __device__ __forceinline__ void dequant32(const uint8_t* __restrict__ wblk, uint32_t r, uint32_t b, uint32_t j,
                                           uint32_t h, uint32_t (&out)[16]) {
@@ -144,8 +147,8 @@ __device__ __forceinline__ void dequant32(const uint8_t* __restrict__ wblk, uint
       float v[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = __fsub_rn(__fmul_rn(d1, (float)((q >> (8 * e)) & 0xF)), m1);
-      out[2 * i] = pack_bf16(v[0], v[1]);
-      out[2 * i + 1] = pack_bf16(v[2], v[3]);
+      out[2 * i] = pack_f16(v[0], v[1]);
+      out[2 * i + 1] = pack_f16(v[2], v[3]);
     }
   } else {  // planar Q6_K (repack.cu): chunk rotations as in the global layout
     const uint32_t n = j >> 1, g = 2 * (j & 1) + h;  // half, 32-element group
@@ -171,8 +174,8 @@ __device__ __forceinline__ void dequant32(const uint8_t* __restrict__ wblk, uint
         const int q = (int)(((lo >> (8 * e)) & 0xF) | (((hi >> (8 * e)) & 3) << 4)) - 32;
         v[e] = (i < 4 ? ds0 : ds1) * (float)q;  // elements 0-15: first scale, 16-31: second
       }
-      out[2 * i] = pack_bf16(v[0], v[1]);
-      out[2 * i + 1] = pack_bf16(v[2], v[3]);
+      out[2 * i] = pack_f16(v[0], v[1]);
+      out[2 * i + 1] = pack_f16(v[2], v[3]);
     }
   }
 }
@@ -182,7 +185,7 @@ __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
 }
 
 struct PfMaps {
-  CUtensorMap x;     // bf16 activations [T][K], box {64, 256}, 128-byte swizzle
+  CUtensorMap x;     // f16 scaled activations [T][K], box {64, 256}, 128-byte swizzle
   CUtensorMap w0;    // weights as bytes [M][row_stride]: Q4_K box {144, 128}; Q6_K box {128, 128}
   CUtensorMap w1;    // Q6_K box {64, 128}
   CUtensorMap w2;    // Q6_K box {16, 128}
@@ -208,8 +211,8 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, int* err
 
 template <int QT>
 __global__ void __launch_bounds__(PF_THREADS, 1)
-    prefill_kernel(const __grid_constant__ PfMaps maps, float* __restrict__ y, uint32_t M, uint32_t K,
-                   uint32_t T, uint32_t k_split, int* err) {
+    prefill_kernel(const __grid_constant__ PfMaps maps, float* __restrict__ y, const float* __restrict__ xs,
+                   uint32_t M, uint32_t K, uint32_t T, uint32_t k_split, int* err) {
   extern __shared__ uint8_t pf_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const uint32_t a0 = smem_u32(sm + OFF_A + s * PF_TILE_A), bb0 = smem_u32(sm + OFF_B + s * PF_TILE_B);
 #pragma unroll
         for (uint32_t k4 = 0; k4 < PF_K / 16; ++k4)
-          mma_bf16(tmem, desc_sw128(a0 + 32 * k4), desc_sw128(bb0 + 32 * k4), (ks | k4) ? 1u : 0u);
+          mma_f16(tmem, desc_sw128(a0 + 32 * k4), desc_sw128(bb0 + 32 * k4), (ks | k4) ? 1u : 0u);
         mma_commit(&ab_empty[s]);
       }
       mma_commit(done);  // arrives once every MMA issued above has completed
@@ -337,10 +340,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           for (int jj = 0; jj < 32; ++jj) {
             const uint32_t t = t0 + 32 * cc + jj;
             if (t < T) {
+              const float r = __uint_as_float(v[jj]) * __ldg(xs + t);  // a power of two: exact
               if (k_split > 1)
-                atomicAdd(&y[(size_t)t * M + m], __uint_as_float(v[jj]));
+                atomicAdd(&y[(size_t)t * M + m], r);
               else
-                y[(size_t)t * M + m] = __uint_as_float(v[jj]);
+                y[(size_t)t * M + m] = r;
             }
           }
         }
@@ -357,10 +361,36 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS) : "memory");
 }
 
-__global__ void to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ xb, size_t n) {
-  for (size_t i = 2 * ((size_t)blockIdx.x * blockDim.x + threadIdx.x); i < n; i += 2 * (size_t)gridDim.x * blockDim.x) {
-    const float2 v = *reinterpret_cast<const float2*>(x + i);
-    *reinterpret_cast<__nv_bfloat162*>(xb + i) = __floats2bfloat162_rn(v.x, v.y);
+// Token row blockIdx.x of x [T][k] -> f16 row of xb scaled by 2^s, s such that
+// the row's largest magnitude lands in [2^14, 2^15) (|s| <= 100: the scaling
+// stays exact in fp32); xs[t] = 2^-s undoes it in the epilogue.  A zero or
+// non-finite row keeps s = 0.
+__global__ void __launch_bounds__(256) to_f16_rows_kernel(const float* __restrict__ x, __half* __restrict__ xb,
+                                                          float* __restrict__ xs, uint32_t k) {
+  __shared__ float red[8];
+  const float* xr = x + (size_t)blockIdx.x * k;
+  __half* br = xb + (size_t)blockIdx.x * k;
+  float mx = 0.f;
+  for (uint32_t i = 2 * threadIdx.x; i < k; i += 2 * blockDim.x) {
+    const float2 v = *reinterpret_cast<const float2*>(xr + i);
+    mx = fmaxf(mx, fmaxf(fabsf(v.x), fabsf(v.y)));  // fmaxf drops NaN: checked below
+  }
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  int e = 0;
+  if (mx > 0.f && isfinite(mx)) {
+    frexpf(mx, &e);  // mx < 2^e <= 2 mx
+    e = 15 - e;
+    e = e > 100 ? 100 : (e < -100 ? -100 : e);
+  }
+  const float f = ldexpf(1.0f, e);
+  if (threadIdx.x == 0) xs[blockIdx.x] = ldexpf(1.0f, -e);
+  for (uint32_t i = 2 * threadIdx.x; i < k; i += 2 * blockDim.x) {
+    const float2 v = *reinterpret_cast<const float2*>(xr + i);
+    *reinterpret_cast<__half2*>(br + i) = __floats2half2_rn(v.x * f, v.y * f);
   }
 }
 
@@ -389,18 +419,21 @@ bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
 
 }  // namespace
 
-size_t prefill_x_bytes(uint32_t k, uint32_t n_tokens) { return (size_t)k * n_tokens * 2; }
+// f16 rows, then one fp32 scale per token (k % 256 == 0: the scales start
+// 512-byte aligned)
+size_t prefill_x_bytes(uint32_t k, uint32_t n_tokens) { return (size_t)k * n_tokens * 2 + (size_t)n_tokens * 4; }
 
 cudaError_t prefill_launch(uint32_t qt, const void* w, uint32_t row_stride, const float* x, void* xb_scratch,
                            float* y, uint32_t m, uint32_t k, uint32_t n_tokens, int* err, int num_sms,
                            cudaStream_t st) {
   if (!encode_fn()) return cudaErrorNotSupported;
-  const size_t n = (size_t)k * n_tokens;  // k % 256 == 0: even
-  to_bf16_kernel<<<4 * num_sms, 256, 0, st>>>(x, static_cast<__nv_bfloat16*>(xb_scratch), n);
+  if (!n_tokens || k % QK) return cudaErrorInvalidValue;
+  float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(xb_scratch) + (size_t)k * n_tokens * 2);
+  to_f16_rows_kernel<<<n_tokens, 256, 0, st>>>(x, static_cast<__half*>(xb_scratch), xs, k);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   PfMaps maps;
-  bool ok = make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb_scratch, k, n_tokens, (uint64_t)k * 2, PF_K, PF_N,
+  bool ok = make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb_scratch, k, n_tokens, (uint64_t)k * 2, PF_K, PF_N,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (qt == T_Q4K) {
     ok = ok && make_map(&maps.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row_stride, m, row_stride, Q4K_BYTES, PF_M,
@@ -426,11 +459,11 @@ cudaError_t prefill_launch(uint32_t qt, const void* w, uint32_t row_stride, cons
   const dim3 grid(gx, gy, ksplit);
   if (qt == T_Q4K) {
     e = cudaFuncSetAttribute(prefill_kernel<T_Q4K>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
-    if (e == cudaSuccess) prefill_kernel<T_Q4K><<<grid, PF_THREADS, PF_SMEM, st>>>(maps, y, m, k, n_tokens, ksplit, err);
+    if (e == cudaSuccess) prefill_kernel<T_Q4K><<<grid, PF_THREADS, PF_SMEM, st>>>(maps, y, xs, m, k, n_tokens, ksplit, err);
   } else {
     e = cudaFuncSetAttribute(prefill_kernel<T_Q6K_PLANAR>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
     if (e == cudaSuccess)
-      prefill_kernel<T_Q6K_PLANAR><<<grid, PF_THREADS, PF_SMEM, st>>>(maps, y, m, k, n_tokens, ksplit, err);
+      prefill_kernel<T_Q6K_PLANAR><<<grid, PF_THREADS, PF_SMEM, st>>>(maps, y, xs, m, k, n_tokens, ksplit, err);
   }
   return e != cudaSuccess ? e : cudaGetLastError();
 }

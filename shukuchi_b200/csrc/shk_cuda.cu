@@ -99,7 +99,7 @@ struct shk_ctx {
   size_t hv_w_cap = 0;
   void* q6_scratch = nullptr;  // GGUF-layout Q6_K rows repacked for the staged GEMV
   size_t q6_scratch_cap = 0;
-  void* pf_x = nullptr;  // bf16 copy of the prefill activations
+  void* pf_x = nullptr;  // f16 copy of the prefill activations + per-token scales
   size_t pf_x_cap = 0;
   float* hv_x = nullptr;
   size_t hv_x_cap = 0;

@@ -220,7 +220,8 @@ class Context:
 
     def prefill_matmul(self, dtype: int, w_dev: int, x_dev: int, y_dev: int, m: int, k: int, n_tokens: int,
                        row_stride: int = 0, stream: int | None = None) -> None:
-        """y[t][r] = sum_k W[r][k] x[t][k] on the tensor cores (bf16 inputs)."""
+        """y[t][r] = sum_k W[r][k] x[t][k] on the tensor cores (f16 inputs, each token row
+        scaled by a power of two)."""
         _call("shk_cuda_prefill_matmul", self.h, dtype, w_dev, row_stride, x_dev, y_dev, m, k, n_tokens, stream)
 
     def tp_init(self, rank: int, world: int, uid: bytes) -> None:

@@ -734,7 +734,7 @@ static int generate(struct engine_handle *h, const uint32_t *prompt, uint32_t n_
     /* prompts of SHUKUCHI_PREFILL tokens or more (0, the default: never):
      * one batched prefill on the tensor cores instead of a step per token
      * (single GPU, HBM-resident, Q4_K / Q6_K weights; else the token loop
-     * below).  Off by default: its bf16 matmul inputs move the logits away
+     * below).  Off by default: its f16 matmul inputs move the logits away
      * from the reference's by more than the decode path's tolerance. */
     const int pf_min = env_int("SHUKUCHI_PREFILL", 0);
     if (pf_min > 0 && n_prompt >= (uint32_t)pf_min && h->resident && h->tp <= 1 && !debug_enabled() &&

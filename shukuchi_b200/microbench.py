@@ -167,12 +167,14 @@ def bf16_peak() -> tuple[float, str]:
 
 def prefill(args, ctx) -> None:
     """Batched dequantise-matmul on the tensor cores: T tokens through each
-    matrix of the GEMV sweep; one call = bf16 conversion of x + the tcgen05
-    kernel.  TFLOP/s = 2 M K T / time."""
+    matrix of the GEMV sweep that it takes (Q4_K, Q6_K); one call = the f16
+    conversion of x (a power-of-two scale per token) + the tcgen05 kernel.
+    TFLOP/s = 2 M K T / time."""
     peak, kind = bf16_peak()
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0)
     shapes = [tuple(int(v) for v in s.split(",")) for s in args.shapes] if args.shapes else GEMV_SHAPES
+    shapes = [s for s in shapes if s[0] in (12, 14)]
     T = args.tokens
     for qt, m, k in shapes:
         row = (k // QK) * BLOCK_BYTES[qt]

@@ -56,11 +56,40 @@ def q5k_blocks(rng: np.random.Generator, n_blocks: int, d_sigma: float = 0.002) 
     return b
 
 
-def quant_matrix(rng: np.random.Generator, qtype: int, rows: int, cols: int) -> np.ndarray:
-    """A rows x cols matrix in GGUF row-major block layout (flat uint8)."""
+# rms of the dequantised weight per unit of d_sigma: Q4_K d * sc * (q - 7.5)
+# with sc uniform 0..63 (rms 36.4) and q uniform 0..15 (std 4.6); Q5_K with q
+# 0..31 (std 9.2); Q6_K sc * (q - 32), both uniform over 64 values (rms 18.5).
+_GAIN = {T_Q4K: 36.4 * 4.6, T_Q5K: 36.4 * 9.2, T_Q6K: 18.5 * 18.5}
+
+
+def _center(b: np.ndarray, qtype: int) -> None:
+    """Q4_K / Q5_K blocks in place: mins = scales and dmin = d * (qmax / 2), so
+    every sub-block dequantises to d * sc * (q - qmax / 2), zero-mean."""
+    if qtype == T_Q6K:
+        return
+    sc = b[:, 4:16]
+    sc[:, 4:8] = sc[:, 0:4]
+    lo = sc[:, 8:12] & 0xF
+    sc[:, 8:12] = lo | (lo << 4)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    half = 7.5 if qtype == T_Q4K else 15.5
+    b[:, 2:4] = (d * half).astype(np.float16).view(np.uint8).reshape(-1, 2)
+
+
+def quant_matrix(rng: np.random.Generator, qtype: int, rows: int, cols: int,
+                 conditioned: bool = False) -> np.ndarray:
+    """A rows x cols matrix in GGUF row-major block layout (flat uint8).
+
+    conditioned: zero-mean weights of rms 1/sqrt(cols) (a unit-gain map, as
+    trained weights are), instead of the benchmark distributions whose
+    activations grow into the thousands across layers."""
     assert cols % QK == 0
     nb = rows * (cols // QK)
-    blocks = {T_Q4K: q4k_blocks, T_Q5K: q5k_blocks, T_Q6K: q6k_blocks}[qtype](rng, nb)
+    gen = {T_Q4K: q4k_blocks, T_Q5K: q5k_blocks, T_Q6K: q6k_blocks}[qtype]
+    if not conditioned:
+        return gen(rng, nb).reshape(-1)
+    blocks = gen(rng, nb, d_sigma=1.0 / (_GAIN[qtype] * np.sqrt(cols)))
+    _center(blocks, qtype)
     return blocks.reshape(-1)
 
 
@@ -142,31 +171,47 @@ class Model:
         return h.hexdigest()
 
 
-def make_layer(rng: np.random.Generator, s: ModelShape) -> LayerWeights:
+def make_layer(rng: np.random.Generator, s: ModelShape, conditioned: bool = False) -> LayerWeights:
     D, hd = s.n_embd, s.head_dim
+
+    def qm(t, rows, cols):
+        return quant_matrix(rng, t, rows, cols, conditioned)
+
     return LayerWeights(
         attn_norm=norm_weight(rng, D),
-        wq=quant_matrix(rng, s.t_q, s.n_heads * hd, D),
-        wk=quant_matrix(rng, s.t_k, s.n_kv_heads * hd, D),
-        wv=quant_matrix(rng, s.t_v, s.n_kv_heads * hd, D),
-        wo=quant_matrix(rng, s.t_o, D, s.n_heads * hd),
+        wq=qm(s.t_q, s.n_heads * hd, D),
+        wk=qm(s.t_k, s.n_kv_heads * hd, D),
+        wv=qm(s.t_v, s.n_kv_heads * hd, D),
+        wo=qm(s.t_o, D, s.n_heads * hd),
         ffn_norm=norm_weight(rng, D),
-        wg=quant_matrix(rng, s.t_gate, s.n_ff, D),
-        wu=quant_matrix(rng, s.t_up, s.n_ff, D),
-        wd=quant_matrix(rng, s.t_down, D, s.n_ff),
+        wg=qm(s.t_gate, s.n_ff, D),
+        wu=qm(s.t_up, s.n_ff, D),
+        wd=qm(s.t_down, D, s.n_ff),
     )
 
 
-def make_model(shape: ModelShape | str, seed: int = 0, n_layers: int | None = None) -> Model:
+def make_model(shape: ModelShape | str, seed: int = 0, n_layers: int | None = None,
+               conditioned: bool = False) -> Model:
+    """A seeded model of `shape`; conditioned: unit-gain zero-mean weights
+    (quant_matrix), so activations and attention scores stay of order one."""
     s = SHAPES[shape] if isinstance(shape, str) else shape
     if n_layers is not None:
         s = dataclasses.replace(s, n_layers=n_layers)
     rng = np.random.default_rng(seed)
-    layers = [make_layer(rng, s) for _ in range(s.n_layers)]
-    tok = quant_matrix(rng, s.t_embd, s.n_vocab, s.n_embd)
+    layers = [make_layer(rng, s, conditioned) for _ in range(s.n_layers)]
+    # embedding rows of rms ~1 (a 1-column gain), output head of unit gain
+    tok = (quant_matrix(rng, s.t_embd, s.n_vocab, s.n_embd, False) if not conditioned else
+           _embedding(rng, s.t_embd, s.n_vocab, s.n_embd))
     onorm = norm_weight(rng, s.n_embd)
-    out = quant_matrix(rng, s.t_out, s.n_vocab, s.n_embd)
+    out = quant_matrix(rng, s.t_out, s.n_vocab, s.n_embd, conditioned)
     return Model(s, layers, tok, onorm, out)
+
+
+def _embedding(rng: np.random.Generator, qtype: int, rows: int, cols: int) -> np.ndarray:
+    gen = {T_Q4K: q4k_blocks, T_Q5K: q5k_blocks, T_Q6K: q6k_blocks}[qtype]
+    blocks = gen(rng, rows * (cols // QK), d_sigma=1.0 / _GAIN[qtype])
+    _center(blocks, qtype)
+    return blocks.reshape(-1)
 
 
 def layer_bytes(s: ModelShape) -> int:

@@ -169,18 +169,23 @@ def test_generate_q5k_mix_matches_oracle(oracle, ctx, layout):
     assert last == t_ref[-1]
 
 
-@pytest.mark.parametrize("shape,n_prompt", [("small", 80), ("tiny", 64), ("small", 300)])
-def test_prefill_then_decode_matches_oracle(oracle, ctx, shape, n_prompt):
+@pytest.mark.parametrize("shape,n_prompt,conditioned,bar", [
+    ("small", 80, False, 0.05), ("tiny", 64, False, 0.05), ("small", 300, True, 0.03)])
+def test_prefill_then_decode_matches_oracle(oracle, ctx, shape, n_prompt, conditioned, bar):
     """The batched prompt prefill (shk_cuda_prefill: tensor-core matmul with
-    bf16 inputs, row-batched glue, one K/V append per layer, causal
+    f16 inputs, row-batched glue, one K/V append per layer, causal
     attention per row), then decode steps: the greedy ids of the
-    token-by-token reference.  The logits carry the bf16 rounding of the
-    prompt's matmuls (bf16 cannot hold the dequantised weights d*sc*q
+    token-by-token reference.  The logits carry the f16 rounding of the
+    prompt's matmuls (f16 cannot hold every dequantised weight d*sc*q
     exactly) through the K/V cache into every later step; on these synthetic
-    models, whose logits run into the thousands, that is up to ~0.1 of the
-    logit std, so the bar here is 0.15 against the decode path's 1e-2; the
-    measured worst case is printed."""
-    model = synth.make_model(shape, seed=21)
+    models, whose logits run into the thousands, that is up to ~0.03 of the
+    logit std (measured 0.026 and 0.004), so the bar here is 0.05 against the
+    decode path's 1e-2; the measured worst case is printed.  The 300-token prompt (rows past 256
+    positions take the tensor-core attention loop) runs on a conditioned
+    model (unit-gain zero-mean weights: activations and scores of order one),
+    where the f16 rounding stays a small fraction of the logit std (measured
+    0.013)."""
+    model = synth.make_model(shape, seed=21, conditioned=conditioned)
     rng = np.random.default_rng(9)
     prompt = rng.integers(0, model.shape.n_vocab, n_prompt).astype(np.uint32)
     n_dec = 10
@@ -199,7 +204,7 @@ def test_prefill_then_decode_matches_oracle(oracle, ctx, shape, n_prompt):
     print(f"prefill {shape} T={n_prompt}: ids {'match' if np.array_equal(toks, t_ref) else 'DIFFER'}, "
           f"max |dlogit| / std = {worst:.2e}")
     assert np.array_equal(toks, t_ref)
-    assert worst <= 0.15
+    assert worst <= bar
 
 
 @pytest.mark.slow

@@ -1,5 +1,5 @@
 // attn.cu -- Q8_0 KV cache: layout, append / read kernels and the stand-alone
-// split-K decode attention kernel (device math in attn_dev.cuh).
+// decode attention kernels (device math in attn_dev.cuh and attn_split.cuh).
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -8,6 +8,7 @@
 
 #include "attn.cuh"
 #include "attn_dev.cuh"
+#include "attn_split.cuh"
 #include "common.cuh"
 
 namespace shk {
@@ -29,6 +30,8 @@ KvLayout kv_layout_make(uint32_t n_layers, uint32_t n_kv, uint32_t hd, uint32_t 
 }
 
 size_t attn_part_floats(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_splits) {
+  // [n_kv][max_splits][8][2] (max, sum) pairs, then [n_kv][max_splits][G][hd]
+  // outputs: n_heads (= 8 * n_kv at most) * max_splits * (hd + 2) covers both
   return (size_t)n_heads * max_splits * (hd + 2);
 }
 
@@ -207,6 +210,64 @@ cudaError_t attn_cluster_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
   return a.kv.max_seq >= 4 * ATT_LONG_MIN ? attn_cluster_g<HD, true>(a, G, st) : attn_cluster_g<HD, false>(a, G, st);
 }
 
+// Long caches: (KV head, split) CTAs with the split staged through shared
+// memory, SPL_CLUSTER consecutive splits per thread-block cluster
+// (attn_split.cuh); at most as many clusters as fit the GPU in one wave.
+constexpr int SPL_CLUSTER = 8;
+
+template <int HD, int G>
+__global__ void __launch_bounds__(SPL_THREADS, 4) attn_split_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t spl_smem[];
+  pdl_trigger();
+  pdl_wait();
+  attn_split_item<HD, G, SPL_CLUSTER>(a, blockIdx.x, blockIdx.y, gridDim.y, spl_smem);
+}
+
+// cudaErrorNotSupported: fewer than one cluster of splits per KV head fits
+// (the caller then takes the single-level split kernel).
+template <int HD, int G>
+cudaError_t attn_split_go(const AttnArgs& a, cudaStream_t st) {
+  auto k = attn_split_kernel<HD, G>;
+  const int smem = SplitRing<HD>::BYTES;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.kv.n_kv, SPL_CLUSTER);
+  cfg.blockDim = dim3(SPL_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = SPL_CLUSTER;
+  at[0].val.clusterDim.z = 1;
+  int n = 1;
+  if (pdl_enabled()) {
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    n = 2;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  int clusters = 0;
+  if ((e = cudaOccupancyMaxActiveClusters(&clusters, k, &cfg)) != cudaSuccess) return e;
+  const uint32_t per_head = std::min<uint32_t>(a.max_splits / SPL_CLUSTER, (uint32_t)clusters / a.kv.n_kv);
+  if (per_head == 0) return cudaErrorNotSupported;
+  cfg.gridDim = dim3(a.kv.n_kv, per_head * SPL_CLUSTER);
+  return cudaLaunchKernelEx(&cfg, k, a);
+}
+
+template <int HD>
+cudaError_t attn_split_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
+  switch (G) {
+    case 1: return attn_split_go<HD, 1>(a, st);
+    case 2: return attn_split_go<HD, 2>(a, st);
+    case 4: return attn_split_go<HD, 4>(a, st);
+    case 8: return attn_split_go<HD, 8>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <int HD>
 cudaError_t attn_launch_hd(const AttnArgs& a, uint32_t G, cudaStream_t st) {
   dim3 grid(a.kv.n_kv, a.max_splits);
@@ -241,6 +302,12 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream) {
     // one-cluster-per-KV-head kernel would leave most SMs idle, the more so
     // with few KV heads per tensor-parallel rank); partials merge in global
     // memory.
+    if ((reinterpret_cast<uintptr_t>(a.q) & 15) == 0) {  // q rows are read as 16-byte vectors
+      AttnArgs c = b;
+      c.min_per_split = std::max(a.min_per_split, SPL_MIN_PER_SPLIT);
+      const cudaError_t e = a.kv.hd == 64 ? attn_split_hd<64>(c, G, stream) : attn_split_hd<128>(c, G, stream);
+      if (e != cudaErrorNotSupported) return e;  // else not launched: the split kernel below
+    }
     b.min_per_split = std::max(a.min_per_split, ATT_SPLIT_LONG);
     return a.kv.hd == 64 ? attn_launch_hd<64>(b, G, stream) : attn_launch_hd<128>(b, G, stream);
   }

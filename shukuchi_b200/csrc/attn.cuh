@@ -34,7 +34,7 @@ struct AttnArgs {
   const uint32_t* pos;      // device: position of the new token; attention covers [0, pos]
   float* out;               // n_heads * hd
   float* part;              // split partials: attn_part_floats(8 * n_kv, n_kv, hd, max_splits)
-  int* counters;            // n_kv ints, zero between launches (self-resetting)
+  int* counters;            // 8 * n_kv ints, zero between launches (self-resetting)
   uint32_t max_splits;
   uint32_t min_per_split;
   int* err;

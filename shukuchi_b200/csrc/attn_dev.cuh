@@ -467,7 +467,7 @@ __device__ __forceinline__ void attn_long_tc(const AttnArgs& a, const float* qsm
 //       p broadcast by shuffle with the V block scale folded in.
 // Warps merge in shared memory; splits merge through `part` (log-sum-exp),
 // the last item of the KV head (atomic ticket) writing the output.
-template <int HD, int G, int NW, int STAGE_BYTES>
+template <int HD, int G, int NW>
 __device__ __forceinline__ void attn_finish(const AttnArgs& a, uint32_t kvh, uint32_t split, uint32_t active,
                                             float* sm);
 
@@ -604,7 +604,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, uint32_t kvh, uint3
       }
     }
   }
-  attn_finish<HD, G, NW, 0>(a, kvh, split, active, sm);
+  attn_finish<HD, G, NW>(a, kvh, split, active, sm);
 }
 
 
@@ -629,101 +629,11 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// The last item's merge of `active` split partials with the records staged
-// through shared memory (cp.async; one chunk, or double-buffered chunks):
-// loads without registers in flight, so the whole head's partials stream at
-// the SM's L2 bandwidth instead of a handful of loads per thread at a time.
-// `sm` holds STAGE_BYTES usable bytes (nothing else live).
-template <int HD, int G, int NW, int STAGE_BYTES>
-__device__ __forceinline__ void attn_merge_staged(const AttnArgs& a, uint32_t kvh, uint32_t active, uint8_t* sm) {
-  constexpr int NT = 32 * NW;
-  constexpr int W_OFF = 0, L_OFF = ATT_MAX_SPLITS * G * 4, ML_OFF = L_OFF + 128;
-  constexpr int BUF_OFF = ML_OFF + ATT_MAX_SPLITS * 64;
-  constexpr int SPLIT_B = G * HD * 4;
-  constexpr int CH1 = (STAGE_BYTES - BUF_OFF) / SPLIT_B;  // splits one buffer can hold
-  constexpr int CH0 = CH1 / 2;
-  constexpr int CH = CH0 > 32 ? 32 : CH0;
-  static_assert(CH >= 1, "no room for a staged chunk");
-  constexpr int PER = (G * HD + NT - 1) / NT;
-  const uint32_t KV = a.kv.n_kv;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* s_w = reinterpret_cast<float*>(sm + W_OFF);  // [split][G] weights
-  float* s_L = reinterpret_cast<float*>(sm + L_OFF);  // [G]
-  const float* s_ml = reinterpret_cast<const float*>(sm + ML_OFF);
-  const float* mlh = part_ml(a, kvh);
-  const float* oh = part_o<HD, G>(a, kvh);
-  // one chunk when every record fits one buffer, else double-buffered chunks
-  const uint32_t chs = active <= (uint32_t)CH1 ? active : (uint32_t)CH;
-  const uint32_t nch = (active + chs - 1) / chs;
-  auto issue_o = [&](uint32_t c) {
-    const uint32_t s0 = c * chs, n = min(chs, active - s0);
-    const float* src = oh + (size_t)s0 * G * HD;
-    const uint32_t dst = smem_u32(sm + BUF_OFF + (c & 1) * chs * SPLIT_B);
-    for (uint32_t i = tid; i < n * (G * HD / 4); i += NT) cp_async16(dst + 16 * i, src + 4 * i);
-  };
-  for (uint32_t i = tid; i < active * 4; i += NT) cp_async16(smem_u32(sm + ML_OFF) + 16 * i, mlh + 4 * i);
-  issue_o(0);
-  cp_async_commit();
-  cp_async_wait<0>();
-  att_sync(NT);
-  if (nch > 1) issue_o(1);
-  cp_async_commit();
-  // weights exp(m_s - M) per query head (warp per head), the sums L
-  for (int g = warp; g < G; g += NW) {
-    float M = -INFINITY;
-    for (uint32_t sp = lane; sp < active; sp += 32) M = fmaxf(M, s_ml[(sp * 8 + g) * 2]);
-    M = warp_max(M);
-    float L = 0.f;
-    for (uint32_t sp = lane; sp < active; sp += 32) {
-      const float ms = s_ml[(sp * 8 + g) * 2];
-      const float w = (ms == -INFINITY) ? 0.f : expf(ms - M);
-      s_w[sp * G + g] = w;
-      L = fmaf(w, s_ml[(sp * 8 + g) * 2 + 1], L);
-    }
-    L = warp_sum(L);
-    if (lane == 0) s_L[g] = L;
-  }
-  float O[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) O[k] = 0.f;
-  for (uint32_t c = 0; c < nch; ++c) {
-    cp_async_wait<1>();  // all but the newest group: chunk c is in
-    att_sync(NT);
-    const float* bf = reinterpret_cast<const float*>(sm + BUF_OFF + (c & 1) * chs * SPLIT_B);
-    const uint32_t s0 = c * chs, n = min(chs, active - s0);
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int i = tid + k * NT;
-      if (i < G * HD) {
-        const int g = i / HD, d = i % HD;
-        float acc = O[k];
-        for (uint32_t u = 0; u < n; ++u) acc = fmaf(s_w[(s0 + u) * G + g], bf[(u * G + g) * HD + d], acc);
-        O[k] = acc;
-      }
-    }
-    att_sync(NT);  // buffer c & 1 is free again
-    if (c + 2 < nch) issue_o(c + 2);
-    cp_async_commit();
-  }
-  cp_async_wait<0>();
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int i = tid + k * NT;
-    if (i < G * HD) {
-      const int g = i / HD, d = i % HD;
-      const float L = s_L[g];
-      a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O[k] * (1.0f / L);
-    }
-  }
-}
-
 // The end of an item: the NW warps' partial results (wm, wl, wacc of
 // AttnSmem, every warp's slots written) merge into this split's result, then
 // the splits of the KV head merge through `part` in log-sum-exp form, the last
-// item of the head (atomic ticket) writing the output -- from registers, or
-// (STAGE_BYTES > 0: that many bytes of `sm` are free for it) staged through
-// shared memory.
-template <int HD, int G, int NW, int STAGE_BYTES>
+// item of the head (atomic ticket) writing the output.
+template <int HD, int G, int NW>
 __device__ __forceinline__ void attn_finish(const AttnArgs& a, uint32_t kvh, uint32_t split, uint32_t active,
                                             float* sm) {
   using SM = AttnSmem<HD, G, NW>;
@@ -790,10 +700,7 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, uint32_t kvh, uin
     return;
   }
   __threadfence();
-  if constexpr (STAGE_BYTES > 0) {
-    att_sync(NT);  // is_last has been read: the staging may overwrite it
-    attn_merge_staged<HD, G, NW, STAGE_BYTES>(a, kvh, active, reinterpret_cast<uint8_t*>(sm));
-  } else {
+  {
     const float* mlh = part_ml(a, kvh);
     const float* oh = part_o<HD, G>(a, kvh);
     // split weights exp(m_s - M) per query head, then the weighted sums

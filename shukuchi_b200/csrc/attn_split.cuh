@@ -162,29 +162,14 @@ __device__ __forceinline__ void spl_issue(uint32_t slot, uint8_t* slot_p, const 
 // start of `sm` (the ring is consumed by then).
 template <int HD, int G>
 __device__ __forceinline__ void spl_compute(const AttnArgs& a, uint32_t kvh, uint32_t pos, uint32_t p0, uint32_t p1,
-                                            uint8_t* sm) {
+                                            const float (&qv)[HD / 32][8], uint8_t* sm) {
   using R = SplitRing<HD>;
   using SM = AttnSmem<HD, G, SPL_WARPS>;
   static_assert(SM::BYTES <= (size_t)R::BYTES, "merge area exceeds the ring");
   constexpr int NB = HD / 32, MT = HD / 16;
   constexpr float L2E = 1.4426950408889634f, LN2 = 0.6931471805599453f;
-  const uint32_t KV = a.kv.n_kv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  // q of head g (query head kvh + KV * g): loaded first, so the loads are in
-  // flight while the new row is appended and the first stages are issued
-  float qv[NB][8];
-#pragma unroll
-  for (int j = 0; j < NB; ++j) {
-    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-    if (g < G) {
-      const float* qh = a.q + (size_t)(kvh + KV * g) * HD + 32 * j + 4 * t;
-      v0 = __ldcg(reinterpret_cast<const float4*>(qh));
-      v1 = __ldcg(reinterpret_cast<const float4*>(qh + 16));
-    }
-    qv[j][0] = v0.x; qv[j][1] = v0.y; qv[j][2] = v0.z; qv[j][3] = v0.w;
-    qv[j][4] = v1.x; qv[j][5] = v1.y; qv[j][6] = v1.z; qv[j][7] = v1.w;
-  }
   int8_t* reg = a.kv.region(a.layer, kvh);
   const int8_t* Kq = reg + a.kv.kq_off;
   const float* Ks = reinterpret_cast<const float*>(reg + a.kv.ks_off);
@@ -432,10 +417,13 @@ __device__ __forceinline__ float ld_dsmem(uint32_t addr) {
 //   2. cluster barrier; CTA r of the cluster merges outputs
 //      [r * SLICE, (r + 1) * SLICE) of all CL results over distributed shared
 //      memory -- the cluster's log-sum-exp merge, written to the output when
-//      one cluster holds every split, else as record `cluster` of `part`;
-//   3. cluster barrier (no CTA leaves while a peer reads its memory); the
-//      clusters of the KV head take tickets and the last one's rank-0 CTA
-//      merges the cluster records (attn_merge_staged).
+//      one cluster holds every split, else as slice r of record `cluster` of
+//      `part`;
+//   3. per (KV head, r) ticket: the last cluster to write slice r merges
+//      slice r of every cluster record (one load per record and output, all
+//      in flight at once);
+//   4. no CTA leaves before every CTA of its cluster has finished reading
+//      its peers (split cluster barrier around steps 2-3).
 template <int HD, int G, int CL>
 __device__ __forceinline__ void attn_split_item(const AttnArgs& a, uint32_t kvh, uint32_t split, uint32_t nsplit,
                                                 uint8_t* sm) {
@@ -446,8 +434,25 @@ __device__ __forceinline__ void attn_split_item(const AttnArgs& a, uint32_t kvh,
   constexpr int NT = SPL_THREADS;
   constexpr int SLICE = (G * HD + CL - 1) / CL;
   static_assert(SLICE <= NT, "one output per thread in the cluster merge");
+  static_assert((G * HD) % CL == 0 && HD % SLICE == 0, "a merge slice lies within one query head");
+  constexpr int NB = HD / 32;
   const uint32_t KV = a.kv.n_kv;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  // q of head g = lane / 4 (query head kvh + KV * g), dims 32j + 4t..4t+3 and
+  // 32j + 16 + 4t..+3 (t = lane % 4): issued before the position, on which
+  // nothing of it depends
+  float qv[NB][8];
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+    if ((lane >> 2) < G) {
+      const float* qh = a.q + (size_t)(kvh + KV * (lane >> 2)) * HD + 32 * j + 4 * (lane & 3);
+      v0 = __ldcg(reinterpret_cast<const float4*>(qh));
+      v1 = __ldcg(reinterpret_cast<const float4*>(qh + 16));
+    }
+    qv[j][0] = v0.x; qv[j][1] = v0.y; qv[j][2] = v0.z; qv[j][3] = v0.w;
+    qv[j][4] = v1.x; qv[j][5] = v1.y; qv[j][6] = v1.z; qv[j][7] = v1.w;
+  }
   const uint32_t pos = __ldcg(a.pos);
   if (pos >= a.kv.max_seq) {  // the same in every CTA: before any cluster barrier
     if (tid == 0) set_error(a.err, DERR_BAD_POS);
@@ -469,7 +474,7 @@ __device__ __forceinline__ void attn_split_item(const AttnArgs& a, uint32_t kvh,
   float* cO = reinterpret_cast<float*>(sm + RS::O);
   if (split < active) {
     const uint32_t p0 = split * per, p1 = min(seq, p0 + per);
-    spl_compute<HD, G>(a, kvh, pos, p0, p1, sm);
+    spl_compute<HD, G>(a, kvh, pos, p0, p1, qv, sm);
     float (*wm)[G] = reinterpret_cast<float (*)[G]>(smf + SM::WM);
     float (*wl)[G] = reinterpret_cast<float (*)[G]>(smf + SM::WL);
     float (*wacc)[G][HD] = reinterpret_cast<float (*)[G][HD]>(smf + SM::WACC);
@@ -507,52 +512,81 @@ __device__ __forceinline__ void attn_split_item(const AttnArgs& a, uint32_t kvh,
   }
   cluster_arrive();
   cluster_wait();  // every CTA's result is in its shared memory
+  // CTA `rank` merges outputs [rank * SLICE, (rank + 1) * SLICE): within one
+  // query head g (SLICE divides HD)
+  const int i = (int)rank * SLICE + tid;
+  const int g = i / HD, d = i % HD;
+  float M = -INFINITY, L = 0.f, O = 0.f;
   if (tid < SLICE) {
-    const int i = (int)rank * SLICE + tid;
-    if (i < G * HD) {
-      const int g = i / HD, d = i % HD;
-      float Mq[CL], Lq[CL], Oq[CL];
+    float Mq[CL], Lq[CL], Oq[CL];
 #pragma unroll
-      for (int q = 0; q < CL; ++q) {
-        Mq[q] = ld_dsmem(dsmem_addr(cM + g, q));
-        Lq[q] = ld_dsmem(dsmem_addr(cL + g, q));
-        Oq[q] = ld_dsmem(dsmem_addr(cO + i, q));
-      }
-      float M = -INFINITY;
+    for (int q = 0; q < CL; ++q) {
+      Mq[q] = ld_dsmem(dsmem_addr(cM + g, q));
+      Lq[q] = ld_dsmem(dsmem_addr(cL + g, q));
+      Oq[q] = ld_dsmem(dsmem_addr(cO + i, q));
+    }
 #pragma unroll
-      for (int q = 0; q < CL; ++q) M = fmaxf(M, Mq[q]);
-      float L = 0.f, O = 0.f;
+    for (int q = 0; q < CL; ++q) M = fmaxf(M, Mq[q]);
 #pragma unroll
-      for (int q = 0; q < CL; ++q) {
-        const float w = (Mq[q] == -INFINITY) ? 0.f : expf(Mq[q] - M);
-        L = fmaf(w, Lq[q], L);
-        O = fmaf(w, Oq[q], O);
-      }
-      if (ncl == 1) {
-        a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O * (1.0f / L);
-      } else {
-        part_o<HD, G>(a, kvh)[((size_t)cl * G + g) * HD + d] = O;
-        if (d == 0) {
-          float* ml = part_ml(a, kvh) + ((size_t)cl * 8 + g) * 2;
-          ml[0] = M;
-          ml[1] = L;
-        }
-      }
+    for (int q = 0; q < CL; ++q) {
+      const float w = (Mq[q] == -INFINITY) ? 0.f : expf(Mq[q] - M);
+      L = fmaf(w, Lq[q], L);
+      O = fmaf(w, Oq[q], O);
     }
   }
-  if (ncl > 1) __threadfence();
+  // this CTA's reads of its peers are done; it leaves only after every peer
+  // has said the same (the wait below), and works on in between
   cluster_arrive();
-  cluster_wait();  // peers are done with this CTA's memory; the cluster's record is out
-  if (ncl == 1 || rank != 0) return;
-  int* flag = reinterpret_cast<int*>(smf + SM::FLAG);
-  if (tid == 0) *flag = (atomicAdd(&a.counters[kvh], 1) == (int)ncl - 1);
-  __syncthreads();
-  const bool last = *flag != 0;
-  __syncthreads();  // the flag is read before the merge reuses the memory
-  if (!last) return;
+  if (ncl == 1) {
+    if (tid < SLICE) a.out[(kvh + KV * g) * HD + d] = (L == 0.f) ? 0.f : O * (1.0f / L);
+    cluster_wait();
+    return;
+  }
+  // slice `rank` of the cluster's record; the last cluster to finish slice
+  // `rank` (ticket per (KV head, rank)) merges that slice over every record
+  if (tid < SLICE) {
+    part_o<HD, G>(a, kvh)[((size_t)cl * G + g) * HD + d] = O;
+    if (tid == 0) {
+      float* ml = part_ml(a, kvh) + ((size_t)cl * 8 + rank) * 2;
+      ml[0] = M;
+      ml[1] = L;
+    }
+  }
   __threadfence();
-  attn_merge_staged<HD, G, SPL_WARPS, R::BYTES>(a, kvh, ncl, sm);
-  if (tid == 0) a.counters[kvh] = 0;
+  __syncthreads();
+  int* flag = reinterpret_cast<int*>(smf + SM::FLAG);
+  int* counter = a.counters + kvh * 8 + rank;
+  if (tid == 0) *flag = (atomicAdd(counter, 1) == (int)ncl - 1);
+  __syncthreads();
+  if (*flag) {
+    __threadfence();
+    constexpr int NCL_MAX = ATT_MAX_SPLITS / CL;
+    if (tid < SLICE) {
+      const float* ml = part_ml(a, kvh);
+      const float* po = part_o<HD, G>(a, kvh);
+      float Mc[NCL_MAX], Lc[NCL_MAX], Oc[NCL_MAX];
+#pragma unroll
+      for (int c = 0; c < NCL_MAX; ++c) {
+        const bool in = (uint32_t)c < ncl;
+        Mc[c] = in ? __ldcg(ml + ((size_t)c * 8 + rank) * 2) : -INFINITY;
+        Lc[c] = in ? __ldcg(ml + ((size_t)c * 8 + rank) * 2 + 1) : 0.f;
+        Oc[c] = in ? __ldcg(po + ((size_t)c * G + g) * HD + d) : 0.f;
+      }
+      float Mf = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < NCL_MAX; ++c) Mf = fmaxf(Mf, Mc[c]);
+      float Lf = 0.f, Of = 0.f;
+#pragma unroll
+      for (int c = 0; c < NCL_MAX; ++c) {
+        const float w = (Mc[c] == -INFINITY) ? 0.f : expf(Mc[c] - Mf);
+        Lf = fmaf(w, Lc[c], Lf);
+        Of = fmaf(w, Oc[c], Of);
+      }
+      a.out[(kvh + KV * g) * HD + d] = (Lf == 0.f) ? 0.f : Of * (1.0f / Lf);
+    }
+    if (tid == 0) *counter = 0;
+  }
+  cluster_wait();  // no CTA leaves while a peer may still read its memory
 }
 
 }  // namespace adev

@@ -669,8 +669,10 @@ shk_kv* shk_cuda_kv_create(shk_ctx* c, const shk_kv_config* cfg) {
   bool ok = cudaMalloc(&kv->L.base, bytes) == cudaSuccess;
   ok = ok && cudaMemset(kv->L.base, 0, bytes) == cudaSuccess;
   ok = ok && cudaMalloc(&kv->part, part * sizeof(float)) == cudaSuccess;
-  ok = ok && cudaMalloc(&kv->counters, cfg->n_kv_heads * sizeof(int)) == cudaSuccess;
-  ok = ok && cudaMemset(kv->counters, 0, cfg->n_kv_heads * sizeof(int)) == cudaSuccess;
+  // one ticket counter per KV head, or per (KV head, cluster rank) in the
+  // long-cache attention kernel: 8 per head
+  ok = ok && cudaMalloc(&kv->counters, 8 * cfg->n_kv_heads * sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMemset(kv->counters, 0, 8 * cfg->n_kv_heads * sizeof(int)) == cudaSuccess;
   ok = ok && cudaMalloc(&kv->d_iota, (size_t)cfg->max_seq_len * sizeof(uint32_t)) == cudaSuccess;
   if (ok) {
     std::vector<uint32_t> io(cfg->max_seq_len);

@@ -40,9 +40,12 @@ struct AttnArgs {
   int* err;
 };
 
-// Append + decode attention: one thread-block cluster per KV head (splits
-// merged in distributed shared memory), or, for caches of 4096 positions or
-// more, the split kernel below (part/counters/max_splits then required).
+// Append + decode attention.  With part / counters / max_splits (>= 8) set
+// and q 16-byte aligned: the split kernel of attn_split.cuh (K/V staged
+// through shared memory, tensor-core QK^T and PV, splits merged per
+// thread-block cluster, then across clusters through `part`).  Otherwise one
+// cluster per KV head (splits merged in distributed shared memory), or for
+// caches of 4096 positions or more the single-level split kernel.
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream);
 // The same with splits merged through `part` and `counters` in global memory.
 cudaError_t attn_decode_split_launch(const AttnArgs& a, cudaStream_t stream);

@@ -53,7 +53,12 @@ constexpr int SPL_THREADS = 32 * SPL_WARPS;
 constexpr int SPL_CHUNK = 16;                      // positions per warp per stage
 constexpr int SPL_STAGE = SPL_CHUNK * SPL_WARPS;   // positions per stage
 constexpr int SPL_NSTAGE = 3;                      // ring depth
-constexpr uint32_t SPL_MIN_PER_SPLIT = 128;        // positions per split, at least
+// Splits: of SPL_MIN_PER_SPLIT positions or more, at most CL of them (one
+// cluster: no merge through global memory) while splits of SPL_LONG_SPLIT
+// positions would fit one cluster, else of SPL_LONG_SPLIT positions or more
+// (as many as the grid holds).
+constexpr uint32_t SPL_MIN_PER_SPLIT = 64;
+constexpr uint32_t SPL_LONG_SPLIT = 128;
 
 template <int HD>
 struct SplitRing {
@@ -460,6 +465,7 @@ __device__ __forceinline__ void attn_split_item(const AttnArgs& a, uint32_t kvh,
   }
   const uint32_t seq = pos + 1;
   uint32_t n0 = (seq + a.min_per_split - 1) / a.min_per_split;
+  if (n0 > (uint32_t)CL) n0 = max((uint32_t)CL, (seq + SPL_LONG_SPLIT - 1) / SPL_LONG_SPLIT);
   n0 = n0 < 1 ? 1 : (n0 > nsplit ? nsplit : n0);
   const uint32_t per = (((seq + n0 - 1) / n0) + SPL_CHUNK - 1) / SPL_CHUNK * SPL_CHUNK;
   const uint32_t active = (seq + per - 1) / per;  // every active split is non-empty

@@ -383,6 +383,13 @@ int matvec_host(shk_ctx* c, uint32_t qt, const void* w, const float* x, float* y
 
 extern "C" {
 
+// Every entry point runs on its context's device: a process may hold contexts
+// on several GPUs (tensor-parallel ranks) and call them from any thread.
+static void on_dev(const shk_ctx* c) {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess || d != c->device) cudaSetDevice(c->device);
+}
+
 int shk_cuda_available(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
@@ -470,6 +477,7 @@ void shk_cuda_shutdown(shk_ctx* c) {
 }
 
 void shk_cuda_report(shk_ctx* c) {
+  if (c) on_dev(c);
   if (!c) return;
   fprintf(stderr,
           "shk_cuda: device=%d sms=%d matvec_calls=%llu matvec_host_calls=%llu layer_forwards=%llu "
@@ -481,6 +489,7 @@ void shk_cuda_report(shk_ctx* c) {
 }
 
 int shk_cuda_check(shk_ctx* c) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return ctx_err_check(c);
 }
@@ -489,34 +498,41 @@ void* shk_cuda_stream(shk_ctx* c) { return c ? c->compute : nullptr; }
 int shk_cuda_num_sms(shk_ctx* c) { return c ? c->num_sms : 0; }
 
 int shk_cuda_dev_alloc(shk_ctx* c, size_t bytes, void** out) {
+  if (c) on_dev(c);
   if (!c || !out) return SHK_EINVAL;
   *out = nullptr;
   return cudaMalloc(out, bytes ? bytes : 1) == cudaSuccess ? SHK_OK : SHK_ENOMEM;
 }
 int shk_cuda_dev_free(shk_ctx* c, void* p) {
+  if (c) on_dev(c);
   (void)c;
   return cudaFree(p) == cudaSuccess ? SHK_OK : SHK_ECUDA;
 }
 int shk_cuda_host_alloc(shk_ctx* c, size_t bytes, void** out) {
+  if (c) on_dev(c);
   if (!c || !out) return SHK_EINVAL;
   *out = nullptr;
   return cudaMallocHost(out, bytes ? bytes : 1) == cudaSuccess ? SHK_OK : SHK_ENOMEM;
 }
 int shk_cuda_host_free(shk_ctx* c, void* p) {
+  if (c) on_dev(c);
   (void)c;
   return cudaFreeHost(p) == cudaSuccess ? SHK_OK : SHK_ECUDA;
 }
 int shk_cuda_memcpy_h2d(shk_ctx* c, void* dst, const void* src, size_t bytes, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, pick(c, s)));
   return SHK_OK;
 }
 int shk_cuda_memcpy_d2h(shk_ctx* c, void* dst, const void* src, size_t bytes, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, pick(c, s)));
   return SHK_OK;
 }
 int shk_cuda_sync(shk_ctx* c, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   CK(cudaStreamSynchronize(pick(c, s)));
   return SHK_OK;
@@ -524,26 +540,31 @@ int shk_cuda_sync(shk_ctx* c, void* s) {
 
 int shk_cuda_matmul_q4k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                             uint32_t k, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_dev(c, T_Q4K, w, 0, x, y, m, k, pick(c, s));
 }
 int shk_cuda_matmul_q6k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                             uint32_t k, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_dev(c, T_Q6K, w, 0, x, y, m, k, pick(c, s));
 }
 int shk_cuda_matmul_q5k_vec(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                             uint32_t k, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_dev(c, T_Q5K, w, 0, x, y, m, k, pick(c, s));
 }
 int shk_cuda_matvec(shk_ctx* c, uint32_t dtype, const void* w, uint32_t row_stride, const float* x, float* y,
                     uint32_t m, uint32_t k, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_dev(c, dtype, w, row_stride, x, y, m, k, pick(c, s));
 }
 int shk_cuda_prefill_matmul(shk_ctx* c, uint32_t dtype, const void* w, uint32_t row_stride, const float* x,
                             float* y, uint32_t m, uint32_t k, uint32_t n_tokens, void* s) {
+  if (c) on_dev(c);
   if (!c || !w || !x || !y || k == 0 || k % QK) return SHK_EINVAL;
   if (dtype != T_Q4K && dtype != T_Q6K_PLANAR) return SHK_EUNSUPPORTED;
   if (m == 0 || n_tokens == 0) return SHK_OK;
@@ -560,6 +581,7 @@ int shk_cuda_prefill_matmul(shk_ctx* c, uint32_t dtype, const void* w, uint32_t 
 
 int shk_cuda_q6k_repack(shk_ctx* c, void* w, uint32_t rows, uint32_t k, uint32_t row_stride, int to_planar,
                         void* s) {
+  if (c) on_dev(c);
   if (!c || !w || k == 0 || k % QK) return SHK_EINVAL;
   const uint32_t stride = row_stride ? row_stride : 210u * (k / QK);
   if (stride % 16 || stride < 210u * (k / QK) || stride > 227u * 1024u || (reinterpret_cast<uintptr_t>(w) & 15))
@@ -577,6 +599,7 @@ size_t shk_cuda_tiled_bytes(uint32_t dtype, uint32_t rows, uint32_t k) {
 
 int shk_cuda_tile(shk_ctx* c, uint32_t dtype, const void* src, uint32_t src_row_stride, uint32_t rows, uint32_t k,
                   void* dst, void* s) {
+  if (c) on_dev(c);
   if (!c || !src || !dst || rows == 0 || k == 0 || k % QK) return SHK_EINVAL;
   if (dtype != T_Q4K && dtype != T_Q6K) return SHK_EUNSUPPORTED;
   cudaSetDevice(c->device);
@@ -587,21 +610,25 @@ int shk_cuda_tile(shk_ctx* c, uint32_t dtype, const void* src, uint32_t src_row_
 }
 int shk_cuda_matmul_q4k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                                  uint32_t k) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_host(c, T_Q4K, w, x, y, m, k);
 }
 int shk_cuda_matmul_q6k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                                  uint32_t k) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_host(c, T_Q6K, w, x, y, m, k);
 }
 int shk_cuda_matmul_q5k_vec_host(shk_ctx* c, const void* w, const float* x, float* y, uint32_t m,
                                  uint32_t k) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   return matvec_host(c, T_Q5K, w, x, y, m, k);
 }
 
 int shk_cuda_rmsnorm(shk_ctx* c, const float* x, const float* w, float* y, uint32_t d, void* s) {
+  if (c) on_dev(c);
   if (!c || !x || !w || !y || !d) return SHK_EINVAL;
   CK(rmsnorm_launch(x, w, y, d, pick(c, s)));
   return SHK_OK;
@@ -609,6 +636,7 @@ int shk_cuda_rmsnorm(shk_ctx* c, const float* x, const float* w, float* y, uint3
 
 int shk_cuda_rope(shk_ctx* c, float* qk, uint32_t n_heads, uint32_t hd, uint32_t pos, float theta,
                   void* s) {
+  if (c) on_dev(c);
   if (!c || !qk || hd == 0 || (hd & 1) || hd > 1024 || !(theta > 0.f)) return SHK_EINVAL;
   cudaStream_t st = pick(c, s);
   // position and frequency table go through stream-ordered copies
@@ -622,6 +650,7 @@ int shk_cuda_rope(shk_ctx* c, float* qk, uint32_t n_heads, uint32_t hd, uint32_t
 }
 
 int shk_cuda_swiglu(shk_ctx* c, const float* g, const float* u, float* h, uint32_t n, void* s) {
+  if (c) on_dev(c);
   if (!c || !g || !u || !h) return SHK_EINVAL;
   CK(swiglu_launch(g, u, h, n, pick(c, s)));
   return SHK_OK;
@@ -629,6 +658,7 @@ int shk_cuda_swiglu(shk_ctx* c, const float* g, const float* u, float* h, uint32
 
 int shk_cuda_embed(shk_ctx* c, const void* table, uint32_t dtype, uint32_t n_vocab, uint32_t token,
                    float* out, uint32_t n_embd, void* s) {
+  if (c) on_dev(c);
   if (!c || !table || !out || !n_embd) return SHK_EINVAL;
   if (dtype != 1 && dtype != T_Q4K) return SHK_EUNSUPPORTED;
   if (dtype == T_Q4K && n_embd % QK) return SHK_EINVAL;
@@ -642,6 +672,7 @@ int shk_cuda_embed(shk_ctx* c, const void* table, uint32_t dtype, uint32_t n_voc
 }
 
 int shk_cuda_argmax(shk_ctx* c, const float* x, uint32_t n, uint32_t* out) {
+  if (c) on_dev(c);
   // index 0xFFFFFFFF marks an empty block partial, so n stops one below it
   if (!c || !x || !out || !n || n > SHK_ARGMAX_NOALLOC_MAX_N) return SHK_EINVAL;
   CK(argmax_launch(x, n, c->am_v, c->am_i, c->am_cnt, c->d_u32 + 2, nullptr, c->compute));
@@ -654,6 +685,7 @@ int shk_cuda_argmax(shk_ctx* c, const float* x, uint32_t n, uint32_t* out) {
 // ------------------------------- KV cache -------------------------------------
 
 shk_kv* shk_cuda_kv_create(shk_ctx* c, const shk_kv_config* cfg) {
+  if (c) on_dev(c);
   if (!c || !cfg || !cfg->n_layers || !cfg->n_kv_heads || !cfg->max_seq_len) return nullptr;
   if (cfg->head_dim != 64 && cfg->head_dim != 128) return nullptr;
   shk_kv* kv = new (std::nothrow) shk_kv();
@@ -687,6 +719,7 @@ shk_kv* shk_cuda_kv_create(shk_ctx* c, const shk_kv_config* cfg) {
 }
 
 void shk_cuda_kv_destroy(shk_kv* kv) {
+  if (kv) on_dev(kv->ctx);
   if (!kv) return;
   if (kv->ctx) cudaStreamSynchronize(kv->ctx->compute);
   cudaFree(kv->L.base);
@@ -698,6 +731,7 @@ void shk_cuda_kv_destroy(shk_kv* kv) {
 
 int shk_cuda_kv_append(shk_kv* kv, uint32_t layer, uint32_t pos, const float* k, const float* v,
                        void* s) {
+  if (kv) on_dev(kv->ctx);
   if (!kv || !k || !v || layer >= kv->L.n_layers || pos >= kv->L.max_seq) return SHK_EINVAL;
   CK(kv_append_launch(kv->L, layer, kv->d_iota + pos, k, v, kv->ctx->d_err, pick(kv->ctx, s)));
   kv->seq[layer] = std::max(kv->seq[layer], pos + 1);
@@ -706,6 +740,7 @@ int shk_cuda_kv_append(shk_kv* kv, uint32_t layer, uint32_t pos, const float* k,
 
 int shk_cuda_kv_append_range(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t n,
                              const float* k, const float* v, void* s) {
+  if (kv) on_dev(kv->ctx);
   if (!kv || !k || !v || layer >= kv->L.n_layers || start > kv->L.max_seq ||
       n > kv->L.max_seq - start)
     return SHK_EINVAL;
@@ -717,6 +752,7 @@ int shk_cuda_kv_append_range(shk_kv* kv, uint32_t layer, uint32_t start, uint32_
 
 int shk_cuda_kv_read_range(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t end, float* k,
                            float* v, void* s) {
+  if (kv) on_dev(kv->ctx);
   if (!kv || !k || !v || end < start || layer >= kv->L.n_layers || end > kv->L.max_seq)
     return SHK_EINVAL;
   CK(kv_read_range_launch(kv->L, layer, start, end, k, v, pick(kv->ctx, s)));
@@ -725,6 +761,7 @@ int shk_cuda_kv_read_range(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t 
 
 int shk_cuda_kv_read_blocks(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t end, void* k,
                             void* v, void* s) {
+  if (kv) on_dev(kv->ctx);
   if (!kv || !k || !v || end < start || layer >= kv->L.n_layers || end > kv->L.max_seq)
     return SHK_EINVAL;
   CK(kv_read_blocks_launch(kv->L, layer, start, end, static_cast<uint8_t*>(k),
@@ -735,6 +772,7 @@ int shk_cuda_kv_read_blocks(shk_kv* kv, uint32_t layer, uint32_t start, uint32_t
 int shk_cuda_kv_attend(shk_kv* kv, uint32_t layer, const float* q, const float* k_new,
                        const float* v_new, float* out, uint32_t n_heads, uint32_t seq_len,
                        float scale, void* s) {
+  if (kv) on_dev(kv->ctx);
   if (!kv || !q || !out || layer >= kv->L.n_layers || seq_len == 0 || seq_len > kv->L.max_seq)
     return SHK_EINVAL;
   if (n_heads % kv->L.n_kv || n_heads / kv->L.n_kv > 8) return SHK_EUNSUPPORTED;
@@ -1253,6 +1291,7 @@ bool model_ready(shk_model* m) {
 }  // namespace
 
 shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv) {
+  if (c) on_dev(c);
   if (!c || !d || !kv) return nullptr;
   if (!d->n_layers || !d->n_embd || !d->n_heads || !d->n_kv_heads || !d->n_ff || !d->n_vocab)
     return nullptr;
@@ -1311,6 +1350,7 @@ shk_model* shk_cuda_model_create(shk_ctx* c, const shk_model_desc* d, shk_kv* kv
 }
 
 void shk_cuda_model_destroy(shk_model* m) {
+  if (m) on_dev(m->ctx);
   if (!m) return;
   if (m->ctx) cudaStreamSynchronize(m->ctx->compute);
   model_free_graphs(m);
@@ -1347,6 +1387,7 @@ void shk_cuda_model_destroy(shk_model* m) {
 float* shk_cuda_model_hidden(shk_model* m) { return m ? m->hidden : nullptr; }
 
 int shk_cuda_model_set_layer(shk_model* m, uint32_t layer, const shk_layer_desc* lv) {
+  if (m) on_dev(m->ctx);
   if (!m || !lv || layer >= m->d.n_layers) return SHK_EINVAL;
   LayerPlans P;
   const int rc = build_layer_plans(m, *lv, P, layer);
@@ -1360,6 +1401,7 @@ int shk_cuda_model_set_layer(shk_model* m, uint32_t layer, const shk_layer_desc*
 
 int shk_cuda_forward_layer(shk_model* m, const shk_layer_desc* lv, uint32_t layer, uint32_t pos,
                            float* hidden, void* s) {
+  if (m) on_dev(m->ctx);
   if (!m || !lv || !hidden || layer >= m->d.n_layers || pos >= m->kv->L.max_seq) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
   if (m->p2p.on || m->ll.on) return SHK_EUNSUPPORTED;  // the exchanges run inside whole-token steps
@@ -1377,6 +1419,7 @@ int shk_cuda_forward_layer(shk_model* m, const shk_layer_desc* lv, uint32_t laye
 }
 
 int shk_cuda_model_embed(shk_model* m, uint32_t token, void* s) {
+  if (m) on_dev(m->ctx);
   if (!m) return SHK_EINVAL;
   if (token >= m->d.n_vocab) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
@@ -1389,6 +1432,7 @@ int shk_cuda_model_embed(shk_model* m, uint32_t token, void* s) {
 }
 
 int shk_cuda_model_lm_head(shk_model* m, uint32_t* token, float* logits, void* s) {
+  if (m) on_dev(m->ctx);
   if (!m || !m->head_ok) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
   int rc = enqueue_head(m, st, false);
@@ -1403,6 +1447,7 @@ int shk_cuda_model_lm_head(shk_model* m, uint32_t* token, float* logits, void* s
 
 int shk_cuda_prefill(shk_model* m, const uint32_t* tokens, uint32_t n, uint32_t pos0, uint32_t* next,
                      float* logits, void* s) {
+  if (m) on_dev(m->ctx);
   if (!m || !tokens || !n || (uint64_t)pos0 + n > m->kv->L.max_seq) return SHK_EINVAL;
   if (!model_ready(m)) return SHK_EINVAL;
   shk_ctx* c = m->ctx;
@@ -1477,6 +1522,7 @@ int shk_cuda_prefill(shk_model* m, const uint32_t* tokens, uint32_t n, uint32_t 
 
 int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_next, uint32_t* next,
                         float* logits) {
+  if (m) on_dev(m->ctx);
   if (!m || token >= m->d.n_vocab || pos >= m->kv->L.max_seq) return SHK_EINVAL;
   if (!model_ready(m)) return SHK_EINVAL;
   cudaStream_t st = m->ctx->compute;
@@ -1515,6 +1561,7 @@ int shk_cuda_token_step(shk_model* m, uint32_t token, uint32_t pos, int want_nex
 
 int shk_cuda_decode_steps(shk_model* m, uint32_t first_token, uint32_t first_pos, uint32_t n,
                           void* s) {
+  if (m) on_dev(m->ctx);
   if (!m || first_token >= m->d.n_vocab || (uint64_t)first_pos + n > m->kv->L.max_seq) return SHK_EINVAL;
   if (!model_ready(m)) return SHK_EINVAL;
   cudaStream_t st = pick(m->ctx, s);
@@ -1540,6 +1587,7 @@ int shk_cuda_decode_steps(shk_model* m, uint32_t first_token, uint32_t first_pos
 }
 
 int shk_cuda_selftest_wait_timeout(shk_ctx* c, uint32_t budget_us) {
+  if (c) on_dev(c);
   if (!c || budget_us == 0 || budget_us > 1000000u) return SHK_EINVAL;
   CK(wait_selftest_launch(c->d_err, 1000ull * budget_us, c->compute));
   return ctx_err_check(c);
@@ -1555,6 +1603,7 @@ int shk_cuda_tp_unique_id(void* out, size_t cap) {
 }
 
 int shk_cuda_tp_init(shk_ctx* c, int rank, int world, const void* id) {
+  if (c) on_dev(c);
   if (!c || !id || world < 1 || rank < 0 || rank >= world || c->comm) return SHK_EINVAL;
   if (world == 1) return SHK_OK;
   if (!nccl()) return SHK_EUNSUPPORTED;
@@ -1571,6 +1620,7 @@ int shk_cuda_tp_init(shk_ctx* c, int rank, int world, const void* id) {
 }
 
 int shk_cuda_tp_comm_size(shk_ctx* c) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   if (!c->comm) return 1;
   int n = 0;
@@ -1579,6 +1629,7 @@ int shk_cuda_tp_comm_size(shk_ctx* c) {
 }
 
 int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint32_t v_lo, uint32_t v_hi) {
+  if (m) on_dev(m->ctx);
   if (!m || o_lo >= o_hi || o_hi > m->d.n_embd || v_lo >= v_hi || v_hi > m->d.n_vocab) return SHK_EINVAL;
   for (uint32_t l = 0; l < m->d.n_layers; ++l)
     if (m->have[l]) return SHK_EINVAL;  // before any layer is registered
@@ -1606,6 +1657,7 @@ int shk_cuda_model_set_tp_rows(shk_model* m, uint32_t o_lo, uint32_t o_hi, uint3
 }
 
 int shk_cuda_model_tp_p2p_export(shk_model* m, void* handle_out, size_t cap) {
+  if (m) on_dev(m->ctx);
   if (!m || !handle_out || cap < sizeof(cudaIpcMemHandle_t)) return SHK_EINVAL;
   shk_ctx* c = m->ctx;
   if (c->tp_world < 2 || c->tp_world > GEMV_TP_MAX) return SHK_EINVAL;
@@ -1630,6 +1682,7 @@ int shk_cuda_model_tp_p2p_export(shk_model* m, void* handle_out, size_t cap) {
 }
 
 int shk_cuda_model_tp_ll_export(shk_model* m, void* handle_out, size_t cap) {
+  if (m) on_dev(m->ctx);
   if (!m || !handle_out || cap < sizeof(cudaIpcMemHandle_t)) return SHK_EINVAL;
   shk_ctx* c = m->ctx;
   if (c->tp_world < 2 || c->tp_world > LL_MAX_RANKS || m->p2p.on) return SHK_EINVAL;
@@ -1648,6 +1701,7 @@ int shk_cuda_model_tp_ll_export(shk_model* m, void* handle_out, size_t cap) {
 }
 
 int shk_cuda_model_tp_ll_import(shk_model* m, const void* handles) {
+  if (m) on_dev(m->ctx);
   if (!m || !handles) return SHK_EINVAL;
   shk_ctx* c = m->ctx;
   auto& q = m->ll;
@@ -1670,6 +1724,7 @@ int shk_cuda_model_tp_ll_import(shk_model* m, const void* handles) {
 }
 
 int shk_cuda_model_tp_p2p_import(shk_model* m, const void* handles, const uint32_t* o_ranges) {
+  if (m) on_dev(m->ctx);
   if (!m || !handles || !o_ranges) return SHK_EINVAL;
   shk_ctx* c = m->ctx;
   auto& q = m->p2p;
@@ -1702,6 +1757,7 @@ int shk_cuda_model_tp_p2p_import(shk_model* m, const void* handles, const uint32
 }
 
 int shk_cuda_model_trace_enable(shk_model* m, uint32_t n_phases) {
+  if (m) on_dev(m->ctx);
   if (!m) return SHK_EINVAL;
   CK(cudaStreamSynchronize(m->ctx->compute));
   cudaFree(m->d_trace);
@@ -1718,6 +1774,7 @@ int shk_cuda_model_trace_enable(shk_model* m, uint32_t n_phases) {
 }
 
 int shk_cuda_model_trace_read(shk_model* m, uint64_t* out, uint32_t cap) {
+  if (m) on_dev(m->ctx);
   if (!m || !out) return SHK_EINVAL;
   if (!m->d_trace || m->trace_last == 0) return 0;
   const uint32_t n = std::min<uint32_t>(cap, 1 + 2 * m->trace_last);
@@ -1727,6 +1784,7 @@ int shk_cuda_model_trace_read(shk_model* m, uint64_t* out, uint32_t cap) {
 }
 
 int shk_cuda_model_token(shk_model* m, uint32_t* token) {
+  if (m) on_dev(m->ctx);
   if (!m || !token) return SHK_EINVAL;
   CK(cudaMemcpyAsync(m->h_tok + 2, m->d_tok, 4, cudaMemcpyDeviceToHost, m->ctx->compute));
   CK(cudaStreamSynchronize(m->ctx->compute));
@@ -1736,6 +1794,7 @@ int shk_cuda_model_token(shk_model* m, uint32_t* token) {
 
 int shk_cuda_model_launch_part(shk_model* m, uint32_t layer, uint32_t part, void* s,
                                uint64_t* bytes_out) {
+  if (m) on_dev(m->ctx);
   if (!m || part > 5 || (part < 5 && (layer >= m->d.n_layers || !m->have[layer] || !m->plans[layer].ok)))
     return SHK_EINVAL;
   if (m->p2p.on) return SHK_EUNSUPPORTED;  // parts wait on peers' partials
@@ -1798,6 +1857,7 @@ static int stage_prepare(shk_ctx* c, uint32_t slot) {
 }
 
 int shk_cuda_layer_release(shk_ctx* c, uint32_t slot, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   cudaSetDevice(c->device);
   cudaStream_t st = pick(c, s);
@@ -1813,6 +1873,7 @@ int shk_cuda_layer_release(shk_ctx* c, uint32_t slot, void* s) {
 }
 
 int shk_cuda_layer_stage(shk_ctx* c, uint32_t slot, void* dst, const void* src, size_t bytes) {
+  if (c) on_dev(c);
   if (!c || !dst || !src) return SHK_EINVAL;
   const int rc = stage_prepare(c, slot);
   if (rc) return rc;
@@ -1827,6 +1888,7 @@ int shk_cuda_layer_stage(shk_ctx* c, uint32_t slot, void* dst, const void* src, 
 
 int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_row,
                               const void* src, size_t src_row, size_t rows) {
+  if (c) on_dev(c);
   if (!c || !dst || !src || dst_row < src_row) return SHK_EINVAL;
   const int rc = stage_prepare(c, slot);
   if (rc) return rc;
@@ -1841,6 +1903,7 @@ int shk_cuda_layer_stage_rows(shk_ctx* c, uint32_t slot, void* dst, size_t dst_r
 
 int shk_cuda_layer_stage_2d(shk_ctx* c, uint32_t slot, void* dst, size_t dst_pitch, const void* src,
                             size_t src_pitch, size_t width, size_t rows) {
+  if (c) on_dev(c);
   if (!c || !dst || !src || width > dst_pitch || width > src_pitch) return SHK_EINVAL;
   if (!width || !rows) return SHK_OK;
   const int rc = stage_prepare(c, slot);
@@ -1856,6 +1919,7 @@ int shk_cuda_layer_stage_2d(shk_ctx* c, uint32_t slot, void* dst, size_t dst_pit
 
 int shk_cuda_layer_stage_q6k_planar(shk_ctx* c, uint32_t slot, void* dst, uint32_t rows, uint32_t k,
                                     uint32_t row_stride) {
+  if (c) on_dev(c);
   if (!c || !dst || k == 0 || k % QK) return SHK_EINVAL;
   (void)slot;  // same copy stream as the slot's copies: ordered after them, covered by its commit
   const uint32_t stride = row_stride ? row_stride : 210u * (k / QK);
@@ -1867,6 +1931,7 @@ int shk_cuda_layer_stage_q6k_planar(shk_ctx* c, uint32_t slot, void* dst, uint32
 }
 
 int shk_cuda_layer_commit(shk_ctx* c, uint32_t slot) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   cudaSetDevice(c->device);
   cudaEvent_t e = slot_event(c, slot);
@@ -1876,6 +1941,7 @@ int shk_cuda_layer_commit(shk_ctx* c, uint32_t slot) {
 }
 
 int shk_cuda_layer_ready(shk_ctx* c, uint32_t slot, int wait) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   cudaSetDevice(c->device);
   cudaEvent_t e = slot_event(c, slot);
@@ -1891,6 +1957,7 @@ int shk_cuda_layer_ready(shk_ctx* c, uint32_t slot, int wait) {
 }
 
 int shk_cuda_layer_wait(shk_ctx* c, uint32_t slot, void* s) {
+  if (c) on_dev(c);
   if (!c) return SHK_EINVAL;
   cudaEvent_t e = slot_event(c, slot);
   if (!e) return SHK_ECUDA;

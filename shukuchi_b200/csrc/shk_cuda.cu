@@ -261,6 +261,7 @@ struct shk_model {
     uint32_t* d_step = nullptr;    // epoch, advanced by the embedding kernel
   } ll;
   uint32_t* tp_pairs = nullptr; // world x {max value bits, index}: argmax over the vocabulary slices
+  bool tp_warm = false;          // the graphs' collectives have run once outside capture
   float* pf_buf = nullptr;      // prompt prefill: T-row activation blocks (shk_cuda_prefill)
   size_t pf_cap = 0;
   uint32_t* pf_tok = nullptr;
@@ -275,6 +276,7 @@ namespace {
 // The status for a device error word already read into e: clears the word.
 int ctx_err_take(shk_ctx* c, int e) {
   if (!e) return SHK_OK;
+  fprintf(stderr, "shk_cuda: device %d reported error %d\n", c->device, e);
   CK(cudaMemset(c->d_err, 0, sizeof(int)));
   // a launch that gave up may have left a combine count behind
   if (c->mmv_scratch) CK(cudaMemset(c->mmv_scratch, 0, MMV_SCRATCH_BYTES));
@@ -1136,9 +1138,29 @@ int enqueue_layers(shk_model* m, cudaStream_t st, bool pdl_after_first = false) 
   return SHK_OK;
 }
 
+// The collectives the captured graphs hold, run once outside any capture:
+// NCCL connects its peers on a communicator's first use of an algorithm, and
+// with several GPUs in one process that enables peer access, which is not
+// allowed while a stream captures.  The residual all-reduce runs in place on
+// the hidden state, which every step's embedding overwrites.
+int tp_warm(shk_model* m) {
+  shk_ctx* c = m->ctx;
+  if (!c->comm || c->tp_world < 2 || m->tp_warm) return SHK_OK;
+  cudaStream_t st = c->compute;
+  if (nccl()->all_reduce(m->hidden, m->hidden, m->d.n_embd, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
+    return SHK_ENCCL;
+  if (vocab_split(m) &&
+      nccl()->all_gather(m->tp_pairs + 2 * c->tp_rank, m->tp_pairs, 2, ncclUint32, c->comm, st) != ncclSuccess)
+    return SHK_ENCCL;
+  CK(cudaStreamSynchronize(st));
+  m->tp_warm = true;
+  return SHK_OK;
+}
+
 int capture(shk_model* m, int which, cudaGraphExec_t* out) {
   cudaStream_t st = m->ctx->compute;
   cudaGraph_t g = nullptr;
+  if (const int wr = tp_warm(m)) return wr;
   CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
   // 0: embed + all layers;  1: lm_head + argmax;  2: both, argmax advancing *pos.
   // Every kernel after the first is a programmatic dependent launch: it is
@@ -1153,9 +1175,13 @@ int capture(shk_model* m, int which, cudaGraphExec_t* out) {
     if (g) cudaGraphDestroy(g);
     return rc;
   }
-  if (ee != cudaSuccess) return SHK_ECUDA;
+  if (ee != cudaSuccess) {
+    fprintf(stderr, "shk_cuda: graph capture %d: %s\n", which, cudaGetErrorString(ee));
+    return SHK_ECUDA;
+  }
   const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
+  if (ie != cudaSuccess) fprintf(stderr, "shk_cuda: graph instantiate %d: %s\n", which, cudaGetErrorString(ie));
   return ie == cudaSuccess ? SHK_OK : SHK_ECUDA;
 }
 

@@ -655,7 +655,11 @@ static int step(struct engine_handle *h, uint32_t tok, int want_next, uint32_t *
                 }
             }
         }
-        if (shk_cuda_token_step(h->m, tok, h->pos, want_next, next, logits) != SHK_OK) return -1;
+        const int e = shk_cuda_token_step(h->m, tok, h->pos, want_next, next, logits);
+        if (e != SHK_OK) {
+            fprintf(stderr, "engine: position %u: token step failed (%d)\n", h->pos, e);
+            return -1;
+        }
     } else {
         if (shk_cuda_model_embed(h->m, tok, NULL) != SHK_OK) return -1;
         float *hidden = shk_cuda_model_hidden(h->m);
@@ -1150,13 +1154,21 @@ static void *tp_rank_main(void *arg) {
     for (uint32_t i = 0; i < r->n_prompt; ++i, ++pos) {
         const int last = i + 1 == r->n_prompt;
         float *lg = (last && r->want_logits) ? r->lg : NULL;
-        if (shk_cuda_token_step(r->m, r->prompt[i], pos, last, &next, lg) != SHK_OK) return NULL;
+        const int e = shk_cuda_token_step(r->m, r->prompt[i], pos, last, &next, lg);
+        if (e != SHK_OK) {
+            fprintf(stderr, "engine: rank %u, prompt position %u: token step failed (%d)\n", r->rank, pos, e);
+            return NULL;
+        }
     }
     for (uint32_t j = 0; j < r->n_decode; ++j, ++pos) {
         const int want = j + 1 < r->n_decode;
         uint32_t nx = 0;
         float *lg = (want && r->want_logits) ? r->lg : NULL;
-        if (shk_cuda_token_step(r->m, next, pos, want, &nx, lg) != SHK_OK) return NULL;
+        const int e = shk_cuda_token_step(r->m, next, pos, want, &nx, lg);
+        if (e != SHK_OK) {
+            fprintf(stderr, "engine: rank %u, position %u: token step failed (%d)\n", r->rank, pos, e);
+            return NULL;
+        }
         if (want) next = nx;
     }
     r->rc = 0;

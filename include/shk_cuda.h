@@ -221,6 +221,16 @@ int shk_cuda_kv_read_blocks(shk_kv *kv, uint32_t layer, uint32_t start, uint32_t
 int shk_cuda_kv_attend(shk_kv *kv, uint32_t layer, const float *q_dev, const float *k_new_dev,
                        const float *v_new_dev, float *out_dev, uint32_t n_heads, uint32_t seq_len,
                        float scale, void *stream);
+/* shk_cuda_kv_attend for n_seq sequences in one launch -- the KV
+ * microbenchmark's batch of decode streams (no counterpart in the reference,
+ * which decodes one sequence): sequence z appends to and attends cache layer
+ * layer0 + z with q / out rows at z * n_heads * hd floats and k_new / v_new
+ * rows at z * n_kv * hd; every sequence at seq_len.  Scratch for the split
+ * partials grows on the first call of a larger n_seq (make that call outside
+ * graph capture). */
+int shk_cuda_kv_attend_batch(shk_kv *kv, uint32_t layer0, uint32_t n_seq, const float *q_dev,
+                             const float *k_new_dev, const float *v_new_dev, float *out_dev,
+                             uint32_t n_heads, uint32_t seq_len, float scale, void *stream);
 /* kv_cache_clear / kv_cache_get_seq_len (engine/src/kv_cache.c:230-248) */
 void shk_cuda_kv_clear(shk_kv *kv);
 uint32_t shk_cuda_kv_seq_len(shk_kv *kv, uint32_t layer);

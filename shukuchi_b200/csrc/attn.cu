@@ -220,7 +220,22 @@ __global__ void __launch_bounds__(SPL_THREADS, 4) attn_split_kernel(const __grid
   extern __shared__ __align__(128) uint8_t spl_smem[];
   pdl_trigger();
   pdl_wait();
-  attn_split_item<HD, G, SPL_CLUSTER>(a, blockIdx.x, blockIdx.y, gridDim.y, spl_smem);
+  if (gridDim.z == 1) {
+    attn_split_item<HD, G, SPL_CLUSTER>(a, blockIdx.x, blockIdx.y, gridDim.y, spl_smem);
+  } else {  // sequence blockIdx.z of a batch
+    AttnArgs b = a;
+    const uint32_t z = blockIdx.z;
+    b.layer = a.layer + z;
+    b.q = a.q + z * a.qo_stride;
+    b.out = a.out + z * a.qo_stride;
+    if (a.k_new) {
+      b.k_new = a.k_new + z * a.kv_stride;
+      b.v_new = a.v_new + z * a.kv_stride;
+    }
+    b.part = a.part + z * a.part_stride;
+    b.counters = a.counters + z * 8 * a.kv.n_kv;
+    attn_split_item<HD, G, SPL_CLUSTER>(b, blockIdx.x, blockIdx.y, gridDim.y, spl_smem);
+  }
 }
 
 // cudaErrorNotSupported: fewer than one cluster of splits per KV head fits
@@ -251,9 +266,13 @@ cudaError_t attn_split_go(const AttnArgs& a, cudaStream_t st) {
   cfg.numAttrs = n;
   int clusters = 0;
   if ((e = cudaOccupancyMaxActiveClusters(&clusters, k, &cfg)) != cudaSuccess) return e;
-  const uint32_t per_head = std::min<uint32_t>(a.max_splits / SPL_CLUSTER, (uint32_t)clusters / a.kv.n_kv);
-  if (per_head == 0) return cudaErrorNotSupported;
-  cfg.gridDim = dim3(a.kv.n_kv, per_head * SPL_CLUSTER);
+  const uint32_t n_seq = std::max<uint32_t>(1, a.n_seq);
+  if (clusters < 1 || a.max_splits < (uint32_t)SPL_CLUSTER) return cudaErrorNotSupported;
+  // one wave of clusters over the (KV head, sequence) pairs; with more pairs
+  // than clusters, one cluster each (later waves wait for nothing)
+  const uint32_t per_head = std::max<uint32_t>(
+      1, std::min<uint32_t>(a.max_splits / SPL_CLUSTER, (uint32_t)clusters / (a.kv.n_kv * n_seq)));
+  cfg.gridDim = dim3(a.kv.n_kv, per_head * SPL_CLUSTER, n_seq);
   return cudaLaunchKernelEx(&cfg, k, a);
 }
 
@@ -315,6 +334,24 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream) {
     }
   }
   return a.kv.hd == 64 ? attn_cluster_hd<64>(b, G, stream) : attn_cluster_hd<128>(b, G, stream);
+}
+
+cudaError_t attn_decode_batch_launch(const AttnArgs& a, cudaStream_t stream) {
+  if (a.kv.n_kv == 0 || a.n_heads % a.kv.n_kv || a.n_seq == 0) return cudaErrorInvalidValue;
+  const uint32_t G = a.n_heads / a.kv.n_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return cudaErrorInvalidValue;
+  if (a.kv.hd != 64 && a.kv.hd != 128) return cudaErrorInvalidValue;
+  if (a.layer + a.n_seq > a.kv.n_layers || !a.part || !a.counters || a.max_splits == 0 ||
+      a.max_splits > (uint32_t)ATT_MAX_SPLITS)
+    return cudaErrorInvalidValue;
+  // 16-byte vectors: q rows and the new K/V rows of every sequence
+  const bool al = (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && (a.qo_stride & 3) == 0 &&
+                  (!a.k_new || ((reinterpret_cast<uintptr_t>(a.k_new) & 15) == 0 &&
+                                (reinterpret_cast<uintptr_t>(a.v_new) & 15) == 0 && (a.kv_stride & 3) == 0));
+  if (!al) return cudaErrorNotSupported;
+  AttnArgs c = a;
+  c.min_per_split = std::max(a.min_per_split, SPL_MIN_PER_SPLIT);
+  return a.kv.hd == 64 ? attn_split_hd<64>(c, G, stream) : attn_split_hd<128>(c, G, stream);
 }
 
 // The split-K kernel with partials in global memory (one item per CTA); kept

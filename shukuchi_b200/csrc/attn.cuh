@@ -38,6 +38,12 @@ struct AttnArgs {
   uint32_t max_splits;
   uint32_t min_per_split;
   int* err;
+  // several sequences in one launch (attn_decode_batch_launch): sequence z
+  // attends cache layer `layer + z` with q / out at z * qo_stride floats,
+  // k_new / v_new at z * kv_stride, partials at z * part_stride floats and
+  // counters at z * 8 * n_kv; the position is shared
+  uint32_t n_seq;
+  size_t qo_stride, kv_stride, part_stride;
 };
 
 // Append + decode attention.  With part / counters / max_splits (>= 8) set
@@ -47,6 +53,10 @@ struct AttnArgs {
 // cluster per KV head (splits merged in distributed shared memory), or for
 // caches of 4096 positions or more the single-level split kernel.
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream);
+// n_seq sequences at the same position in one launch of the staged split
+// kernel (a.n_seq and the strides set; q 16-byte aligned; part / counters
+// sized for n_seq); cudaErrorNotSupported when that kernel cannot run.
+cudaError_t attn_decode_batch_launch(const AttnArgs& a, cudaStream_t stream);
 // The same with splits merged through `part` and `counters` in global memory.
 cudaError_t attn_decode_split_launch(const AttnArgs& a, cudaStream_t stream);
 size_t attn_part_floats(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_splits);

@@ -122,6 +122,10 @@ struct shk_kv {
   int* counters = nullptr;
   uint32_t max_splits = 1;
   uint32_t* d_iota = nullptr;  // d_iota[p] == p, used as a device position pointer
+  // partials and ticket counters of batched attention (shk_cuda_kv_attend_batch)
+  float* part_batch = nullptr;
+  int* counters_batch = nullptr;
+  uint32_t batch_cap = 0;  // sequences they are sized for
 };
 
 namespace {
@@ -728,6 +732,8 @@ void shk_cuda_kv_destroy(shk_kv* kv) {
   cudaFree(kv->part);
   cudaFree(kv->counters);
   cudaFree(kv->d_iota);
+  cudaFree(kv->part_batch);
+  cudaFree(kv->counters_batch);
   delete kv;
 }
 
@@ -796,6 +802,65 @@ int shk_cuda_kv_attend(shk_kv* kv, uint32_t layer, const float* q, const float* 
   a.err = kv->ctx->d_err;
   CK(attn_decode_launch(a, pick(kv->ctx, s)));
   if (k_new) kv->seq[layer] = std::max(kv->seq[layer], seq_len);
+  return SHK_OK;
+}
+
+int shk_cuda_kv_attend_batch(shk_kv* kv, uint32_t layer0, uint32_t n_seq, const float* q, const float* k_new,
+                             const float* v_new, float* out, uint32_t n_heads, uint32_t seq_len, float scale,
+                             void* s) {
+  if (kv) on_dev(kv->ctx);
+  if (!kv || !q || !out || n_seq == 0 || layer0 + n_seq > kv->L.n_layers || layer0 + n_seq < layer0 ||
+      seq_len == 0 || seq_len > kv->L.max_seq)
+    return SHK_EINVAL;
+  if (n_heads % kv->L.n_kv || n_heads / kv->L.n_kv > 8) return SHK_EUNSUPPORTED;
+  if ((k_new == nullptr) != (v_new == nullptr)) return SHK_EINVAL;
+  const size_t per = attn_part_floats(8 * kv->L.n_kv, kv->L.n_kv, kv->L.hd, kv->max_splits);
+  if (n_seq > kv->batch_cap) {  // grown outside any capture (first call of a size)
+    cudaStream_t st = pick(kv->ctx, s);
+    CK(cudaStreamSynchronize(st));
+    cudaFree(kv->part_batch);
+    cudaFree(kv->counters_batch);
+    kv->part_batch = nullptr;
+    kv->counters_batch = nullptr;
+    kv->batch_cap = 0;
+    if (cudaMalloc(&kv->part_batch, per * n_seq * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&kv->counters_batch, (size_t)8 * kv->L.n_kv * n_seq * sizeof(int)) != cudaSuccess)
+      return SHK_ENOMEM;
+    CK(cudaMemset(kv->counters_batch, 0, (size_t)8 * kv->L.n_kv * n_seq * sizeof(int)));
+    kv->batch_cap = n_seq;
+  }
+  AttnArgs a{};
+  a.kv = kv->L;
+  a.layer = layer0;
+  a.n_heads = n_heads;
+  a.scale = scale;
+  a.q = q;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.pos = kv->d_iota + (seq_len - 1);
+  a.out = out;
+  a.part = kv->part_batch;
+  a.counters = kv->counters_batch;
+  a.max_splits = kv->max_splits;
+  a.min_per_split = SHK_ATT_MIN_SPLIT;
+  a.err = kv->ctx->d_err;
+  a.n_seq = n_seq;
+  a.qo_stride = (size_t)n_heads * kv->L.hd;
+  a.kv_stride = (size_t)kv->L.n_kv * kv->L.hd;
+  a.part_stride = per;
+  const cudaError_t e = attn_decode_batch_launch(a, pick(kv->ctx, s));
+  if (e == cudaErrorNotSupported) {  // unaligned rows: one launch per sequence
+    for (uint32_t z = 0; z < n_seq; ++z) {
+      const int rc = shk_cuda_kv_attend(kv, layer0 + z, q + z * a.qo_stride, k_new ? k_new + z * a.kv_stride : nullptr,
+                                        v_new ? v_new + z * a.kv_stride : nullptr, out + z * a.qo_stride, n_heads,
+                                        seq_len, scale, s);
+      if (rc) return rc;
+    }
+    return SHK_OK;
+  }
+  CK(e);
+  if (k_new)
+    for (uint32_t z = 0; z < n_seq; ++z) kv->seq[layer0 + z] = std::max(kv->seq[layer0 + z], seq_len);
   return SHK_OK;
 }
 

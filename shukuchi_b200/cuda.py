@@ -108,6 +108,7 @@ _SIGS = {
     "shk_cuda_kv_read_range": (I, [P, U32, U32, U32, P, P, P]),
     "shk_cuda_kv_read_blocks": (I, [P, U32, U32, U32, P, P, P]),
     "shk_cuda_kv_attend": (I, [P, U32, P, P, P, P, U32, U32, F, P]),
+    "shk_cuda_kv_attend_batch": (I, [P, U32, U32, P, P, P, P, U32, U32, F, P]),
     "shk_cuda_kv_clear": (None, [P]),
     "shk_cuda_kv_seq_len": (U32, [P, U32]),
     "shk_cuda_model_create": (P, [P, C.POINTER(ModelDesc), P]),
@@ -326,6 +327,12 @@ class KvCache:
 
     def attend(self, layer, q, out, n_heads, seq_len, scale, k_new=None, v_new=None, stream=None):
         _call("shk_cuda_kv_attend", self.h, layer, q, k_new, v_new, out, n_heads, seq_len, scale, stream)
+
+    def attend_batch(self, layer0, n_seq, q, out, n_heads, seq_len, scale, k_new=None, v_new=None,
+                     stream=None):
+        """attend for n_seq sequences (cache layers layer0..) in one launch."""
+        _call("shk_cuda_kv_attend_batch", self.h, layer0, n_seq, q, k_new, v_new, out, n_heads, seq_len, scale,
+              stream)
 
     def clear(self):
         lib().shk_cuda_kv_clear(self.h)

@@ -243,6 +243,60 @@ def score_rounding_bound(q, K, V, H, KV, hd, seq, scale):
     return out
 
 
+@pytest.mark.parametrize("H,KV,hd,seq", [(64, 8, 128, 300), (64, 8, 128, 5000), (8, 2, 64, 1500)])
+def test_attend_batch(oracle, ctx, H, KV, hd, seq):
+    """Three sequences (cache layers 1..3) in one launch: each appends its new
+    row bit-exactly and attends as the oracle does on its own K/V."""
+    B = 3
+    rng = np.random.default_rng(H * 7 + seq)
+    kv = sc.KvCache(ctx, B + 1, KV, hd, seq + 16)
+    try:
+        ks, vs, keep = [], [], []
+        for b in range(B):
+            k, v = kv_inputs(rng, seq, KV, hd)
+            k[seq - 1, 5] = 3.0
+            ks.append(k)
+            vs.append(v)
+            keep += [to_dev(k), to_dev(v)]  # alive until the appends have run
+            kv.append_range(1 + b, 0, seq - 1, keep[-2].data_ptr(), keep[-1].data_ptr())
+        q = (rng.normal(0, 1, (B, H * hd))).astype(np.float32)
+        kn = np.stack([k[seq - 1] for k in ks])
+        vn = np.stack([v[seq - 1] for v in vs])
+        qd, knd, vnd = to_dev(q), to_dev(kn), to_dev(vn)
+        out = torch.zeros(B, H * hd, device="cuda")
+        scale = np.float32(1.0 / np.sqrt(hd))
+        kv.attend_batch(1, B, qd.data_ptr(), out.data_ptr(), H, seq, float(scale), knd.data_ptr(), vnd.data_ptr())
+        torch.cuda.synchronize()
+        ctx.check()
+        got = out.cpu().numpy()
+        nb = KV * hd // 32 * 36
+        for b in range(B):
+            kb = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+            vb = torch.zeros_like(kb)
+            kv.read_blocks(1 + b, seq - 1, seq, kb.data_ptr(), vb.data_ptr())
+            torch.cuda.synchronize()
+            assert np.array_equal(kb.cpu().numpy(), oracle.q8_quantize(ks[b][seq - 1]))
+            assert np.array_equal(vb.cpu().numpy(), oracle.q8_quantize(vs[b][seq - 1]))
+            assert kv.seq_len(1 + b) == seq
+    finally:
+        kv.close()
+    for b in range(B):
+        okv = oracle.kv_create(1, KV, hd, seq + 8)
+        try:
+            for t in range(seq):
+                oracle.L.orc_kv_append(okv, 0, t, ks[b][t].ctypes.data, vs[b][t].ctypes.data)
+            K = np.zeros(seq * KV * hd, np.float32)
+            V = np.zeros_like(K)
+            oracle.L.orc_kv_read_range(okv, 0, 0, seq, K.ctypes.data, V.ctypes.data)
+        finally:
+            oracle.kv_destroy(okv)
+        ref = oracle.attention(q[b], K, V, H, KV, hd, seq, scale)
+        err = np.abs(got[b] - ref).reshape(H, hd).max(axis=1)
+        lim = 2e-5 * np.maximum(np.abs(ref).reshape(H, hd).max(axis=1), 1.0) + 8.0 * score_rounding_bound(
+            q[b], K, V, H, KV, hd, seq, scale)
+        assert np.all(err <= lim), (b, (err / lim).max())
+
+
 def test_attend_rejects_out_of_range(ctx):
     kv = sc.KvCache(ctx, 1, 2, 64, 16)
     try:

@@ -46,12 +46,12 @@ struct AttnArgs {
   size_t qo_stride, kv_stride, part_stride;
 };
 
-// Append + decode attention.  With part / counters / max_splits (>= 8) set
-// and q 16-byte aligned: the split kernel of attn_split.cuh (K/V staged
-// through shared memory, tensor-core QK^T and PV, splits merged per
-// thread-block cluster, then across clusters through `part`).  Otherwise one
-// cluster per KV head (splits merged in distributed shared memory), or for
-// caches of 4096 positions or more the single-level split kernel.
+// Append + decode attention.  Caches of 4096 positions or more (with part /
+// counters / max_splits >= 8 and q 16-byte aligned): the split kernel of
+// attn_split.cuh (K/V staged through shared memory, tensor-core QK^T and PV,
+// splits merged per thread-block cluster, then across clusters through
+// `part`), else the single-level split kernel.  Shorter caches: one cluster
+// per KV head (splits merged in distributed shared memory).
 cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream);
 // n_seq sequences at the same position in one launch of the staged split
 // kernel (a.n_seq and the strides set; q 16-byte aligned; part / counters

@@ -353,7 +353,7 @@ int shk_cuda_layer_release(shk_ctx *ctx, uint32_t slot, void *stream);
 int shk_cuda_selftest_wait_timeout(shk_ctx *ctx, uint32_t budget_us);
 
 /* ---- tensor parallelism over the GPUs of one node: NCCL all-reduce over
- *      NVLink after the O and down projections (north-star TP layout: Wq/Wk/Wv/
+ *      NVLink after the O and down projections (layout: Wq/Wk/Wv/
  *      gate/up split by output rows, Wo/down by input columns, KV heads local
  *      to a rank).  No counterpart in the reference (single device). ---- */
 #define SHK_TP_ID_BYTES 128

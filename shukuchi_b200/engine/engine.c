@@ -784,7 +784,7 @@ static int generate(struct engine_handle *h, const uint32_t *prompt, uint32_t n_
 /* ------------------------- tensor parallelism ---------------------------- */
 /* SHUKUCHI_TP = 2, 4 or 8 (resident mode): one GPU (SHUKUCHI_DEVICE + r),
  * context and thread per rank, an NCCL communicator across them.  The split
- * is the north-star one, and the same as the Python side's
+ * is the Megatron-style one, and the same as the Python side's
  * shukuchi_b200/tp.py: Wq/Wk/Wv and gate/up are cut by output rows, Wo and
  * down by input columns in whole 256-element blocks, KV heads stay local to a
  * rank.  Query head h reads KV head h % n_kv (engine/src/ops.c:423), so a rank

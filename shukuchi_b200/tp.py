@@ -1,6 +1,6 @@
 """Tensor-parallel layout and weight sharding (host side).
 
-Layout for `world` ranks (the north-star split): Wq/Wk/Wv and gate/up are cut
+Layout for `world` ranks (a Megatron-style split): Wq/Wk/Wv and gate/up are cut
 by output rows, Wo and down by input columns, KV heads stay local to a rank;
 one all-reduce after the O projection and one after down.
 

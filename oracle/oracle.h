@@ -1,7 +1,7 @@
 /*
  * oracle.h -- CPU restatement of Shukuchi's batch-1 decode path.
  *
- * TEST INFRASTRUCTURE ONLY.  This library is the checker that the CUDA path
+ * TEST INFRASTRUCTURE ONLY.  This library is the oracle that the CUDA path
  * (libshk_cuda.so) is compared against.  Only tests/, __graft_entry__.smoke()
  * and bench.py's cpu_baseline / reference leg may load it.  The product path
  * never calls into it and has no CPU fallback.

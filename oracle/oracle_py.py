@@ -1,4 +1,4 @@
-"""Python access to the checker libraries (TEST INFRASTRUCTURE ONLY).
+"""Python access to the oracle libraries (TEST INFRASTRUCTURE ONLY).
 
 * ``Oracle``    -- oracle/liboracle.so, the C restatement of the reference path.
 * ``Reference`` -- oracle/_ref/libshkref.so, the unmodified reference sources

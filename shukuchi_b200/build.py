@@ -98,7 +98,7 @@ def build_engine() -> str | None:
 
 
 def build_oracle() -> None:
-    """Compiles the checker: oracle/liboracle.so always, oracle/_ref when the
+    """Compiles the oracle: oracle/liboracle.so always, oracle/_ref when the
     reference sources are present on this machine."""
     od = os.path.join(ROOT, "oracle")
     _run(["make", "-s", "-C", od, "liboracle.so"])

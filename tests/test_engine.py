@@ -108,7 +108,7 @@ def test_engine_matches_oracle(model_file, oracle, resident, depth, container, m
 
 @pytest.mark.gpu
 # Two ranks only: the four-rank run of the C engine (one process, four
-# threads and NCCL communicators) did not finish on a 4-GPU box and is not run
+# threads and NCCL communicators) did not finish on four GPUs and is not run
 # until its cause is found; four-rank decode is covered by the multi-process
 # path (tests/test_tp.py, bench.py --gpus 4).
 @pytest.mark.parametrize("world", [2])

@@ -1,10 +1,11 @@
 // attn_split.cuh -- decode attention over long caches (device code).
 //
 // One CTA per (KV head, split) of the positions [0, pos]; the split's Q8_0 K
-// and V rows and their block scales stream through a ring of shared-memory
-// stages (cp.async, 16-byte pieces, 128-byte-swizzled rows so the tensor-core
-// fragment loads below are conflict-free), 64 positions per stage, one
-// 16-position chunk per warp per stage.  Per chunk:
+// and V rows and their block scales stream through shared memory in
+// 16-position chunks (cp.async, 16-byte pieces, 128-byte-swizzled rows so the
+// tensor-core fragment loads below are conflict-free): warp w takes chunks
+// w, w + 4, w + 8, ... of the split, each through its own ring of
+// SPL_NSTAGE slots, so the warps never wait for one another.  Per chunk:
 //
 //   QK^T  exact integer products on the tensor cores (mma.sync m16n8k32,
 //         s8 x s8 -> s32): the K bytes are the B operand as stored (ldmatrix
@@ -35,9 +36,9 @@
 //
 // Splits merge in two levels: the CTAs of a thread-block cluster (CL
 // consecutive splits) over distributed shared memory, then the clusters'
-// records through `part` (atomic ticket, the last cluster's merge staged
-// through shared memory).  Every wait is a hardware one (cp.async.wait_group,
-// bar.sync, barrier.cluster).
+// records through `part` (a ticket per output slice: the last cluster to
+// write a slice merges it over every record).  Every wait is a hardware one
+// (cp.async.wait_group, bar.sync, barrier.cluster).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -51,8 +52,7 @@ namespace adev {
 constexpr int SPL_WARPS = 4;
 constexpr int SPL_THREADS = 32 * SPL_WARPS;
 constexpr int SPL_CHUNK = 16;                      // positions per warp per stage
-constexpr int SPL_STAGE = SPL_CHUNK * SPL_WARPS;   // positions per stage
-constexpr int SPL_NSTAGE = 3;                      // ring depth
+constexpr int SPL_NSTAGE = 3;                      // ring depth (chunks per warp)
 // Splits: of SPL_MIN_PER_SPLIT positions or more, at most CL of them (one
 // cluster: no merge through global memory) while splits of SPL_LONG_SPLIT
 // positions would fit one cluster, else of SPL_LONG_SPLIT positions or more
@@ -60,14 +60,17 @@ constexpr int SPL_NSTAGE = 3;                      // ring depth
 constexpr uint32_t SPL_MIN_PER_SPLIT = 64;
 constexpr uint32_t SPL_LONG_SPLIT = 128;
 
+// Each warp streams its own 16-position chunks through SPL_NSTAGE slots of
+// the ring (no CTA-wide barrier in the loop): slot = [K rows][V rows][K
+// scales][V scales] of one chunk.
 template <int HD>
 struct SplitRing {
   static constexpr int NB = HD / 32;
-  static constexpr int KB = SPL_STAGE * HD;      // K (and V) bytes of a stage
-  static constexpr int SB = SPL_STAGE * NB * 4;  // K (and V) scale bytes of a stage
+  static constexpr int KB = SPL_CHUNK * HD;      // K (and V) bytes of a chunk
+  static constexpr int SB = SPL_CHUNK * NB * 4;  // K (and V) scale bytes of a chunk
   static constexpr int K = 0, V = KB, KS = 2 * KB, VS = 2 * KB + SB;
-  static constexpr int STAGE = 2 * KB + 2 * SB;
-  static constexpr int BYTES = SPL_NSTAGE * STAGE;
+  static constexpr int CHUNK = 2 * KB + 2 * SB;
+  static constexpr int BYTES = SPL_WARPS * SPL_NSTAGE * CHUNK;
 };
 
 // Byte offset of 16-byte piece c of row r of a staged K or V block: rows of
@@ -132,15 +135,16 @@ __device__ __forceinline__ void lds_scales(const float* p, float (&o)[NB]) {
   }
 }
 
-// Stage `b`..`e` (e - b <= SPL_STAGE positions) of the split into the ring
-// slot at shared address `slot`: K and V rows swizzled, scales linear.
+// Positions `b`..`e` (e - b <= SPL_CHUNK) into the ring slot at shared
+// address `slot`, by the 32 lanes of one warp: K and V rows swizzled, scales
+// linear.
 template <int HD>
 __device__ __forceinline__ void spl_issue(uint32_t slot, uint8_t* slot_p, const int8_t* Kq, const float* Ks,
-                                          const int8_t* Vq, const float* Vs, uint32_t b, uint32_t e, int tid) {
+                                          const int8_t* Vq, const float* Vs, uint32_t b, uint32_t e, int lane) {
   using R = SplitRing<HD>;
   constexpr uint32_t CPR = HD / 16;
   const uint32_t n = e - b;
-  for (uint32_t i = tid; i < n * CPR; i += SPL_THREADS) {
+  for (uint32_t i = lane; i < n * CPR; i += 32) {
     const uint32_t r = i / CPR, c = i % CPR;
     const uint32_t o = spl_swz<HD>(r, c);
     cp_async16(slot + R::K + o, Kq + (size_t)(b + r) * HD + 16 * c);
@@ -148,13 +152,13 @@ __device__ __forceinline__ void spl_issue(uint32_t slot, uint8_t* slot_p, const 
   }
   // b is a multiple of 16 positions: the scale rows start 16-byte aligned
   const uint32_t nf = n * R::NB, n16 = nf / 4;
-  for (uint32_t i = tid; i < n16; i += SPL_THREADS) {
+  for (uint32_t i = lane; i < n16; i += 32) {
     cp_async16(slot + R::KS + 16 * i, Ks + (size_t)b * R::NB + 4 * i);
     cp_async16(slot + R::VS + 16 * i, Vs + (size_t)b * R::NB + 4 * i);
   }
   // head_dim 64 with an odd row count: the last row's two scales, by plain
   // loads (published by the same barrier as the copies)
-  for (uint32_t i = 4 * n16 + tid; i < nf; i += SPL_THREADS) {
+  for (uint32_t i = 4 * n16 + lane; i < nf; i += 32) {
     reinterpret_cast<float*>(slot_p + R::KS)[i] = __ldcg(Ks + (size_t)b * R::NB + i);
     reinterpret_cast<float*>(slot_p + R::VS)[i] = __ldcg(Vs + (size_t)b * R::NB + i);
   }
@@ -184,13 +188,18 @@ __device__ __forceinline__ void spl_compute(const AttnArgs& a, uint32_t kvh, uin
     append_head(a.kv, a.layer, kvh, pos, a.k_new, a.v_new, warp, lane, SPL_WARPS);
   __syncthreads();  // the new row is in the cache before any stage copies it
 
-  const uint32_t ring = smem_u32(sm);
-  const uint32_t nst = (p1 - p0 + SPL_STAGE - 1) / SPL_STAGE;
+  // this warp's chunks: positions p0 + 16 (warp + 4k), k < nk, each through
+  // the warp's own slots
+  const uint32_t nchunks = (p1 - p0 + SPL_CHUNK - 1) / SPL_CHUNK;
+  const uint32_t nk = nchunks > (uint32_t)warp ? (nchunks - warp + SPL_WARPS - 1) / SPL_WARPS : 0;
+  const uint32_t wring = smem_u32(sm) + warp * SPL_NSTAGE * R::CHUNK;
+  uint8_t* wring_p = sm + warp * SPL_NSTAGE * R::CHUNK;
 #pragma unroll
   for (int s = 0; s < SPL_NSTAGE - 1; ++s) {
-    if ((uint32_t)s < nst)
-      spl_issue<HD>(ring + s * R::STAGE, sm + s * R::STAGE, Kq, Ks, Vq, Vs, p0 + s * SPL_STAGE,
-                    min(p1, p0 + (s + 1) * SPL_STAGE), tid);
+    if ((uint32_t)s < nk) {
+      const uint32_t b = p0 + SPL_CHUNK * (warp + SPL_WARPS * s);
+      spl_issue<HD>(wring + s * R::CHUNK, wring_p + s * R::CHUNK, Kq, Ks, Vq, Vs, b, min(p1, b + SPL_CHUNK), lane);
+    }
     cp_async_commit();
   }
 
@@ -237,7 +246,7 @@ __device__ __forceinline__ void spl_compute(const AttnArgs& a, uint32_t kvh, uin
   // per-lane fragment addresses inside a stage (warp rows 16*warp..+15)
   uint32_t koff[NB], voff[NB];
   {
-    const int i = lane >> 3, rr = lane & 7, row0 = SPL_CHUNK * warp;
+    const int i = lane >> 3, rr = lane & 7, row0 = 0;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
       // K: matrices (rows 0-7, piece 2j), (0-7, 2j+1), (8-15, 2j), (8-15, 2j+1)
@@ -254,30 +263,29 @@ __device__ __forceinline__ void spl_compute(const AttnArgs& a, uint32_t kvh, uin
   float m = -INFINITY, l = 0.f;
   float vsE = 0.f, vsInv = 0.f;  // 2^E and 2^-E (0, 0 until a nonzero V scale is seen)
 
-  for (uint32_t s = 0; s < nst; ++s) {
+  for (uint32_t s = 0; s < nk; ++s) {
     cp_async_wait<SPL_NSTAGE - 2>();
-    __syncthreads();  // stage s is complete for every thread; slot (s - 1) % NSTAGE is free
+    __syncwarp();  // chunk s is in for every lane; slot (s - 1) % NSTAGE is free
     {
       const uint32_t sn = s + SPL_NSTAGE - 1;
-      if (sn < nst) {
-        const uint32_t sl = sn % SPL_NSTAGE;
-        spl_issue<HD>(ring + sl * R::STAGE, sm + sl * R::STAGE, Kq, Ks, Vq, Vs, p0 + sn * SPL_STAGE,
-                      min(p1, p0 + (sn + 1) * SPL_STAGE), tid);
+      if (sn < nk) {
+        const uint32_t sl = sn % SPL_NSTAGE, b = p0 + SPL_CHUNK * (warp + SPL_WARPS * sn);
+        spl_issue<HD>(wring + sl * R::CHUNK, wring_p + sl * R::CHUNK, Kq, Ks, Vq, Vs, b, min(p1, b + SPL_CHUNK),
+                      lane);
       }
       cp_async_commit();
     }
-    const uint32_t c0 = p0 + s * SPL_STAGE + SPL_CHUNK * warp;  // this warp's chunk
-    if (c0 >= p1) continue;                                     // warp-uniform
+    const uint32_t c0 = p0 + SPL_CHUNK * (warp + SPL_WARPS * s);  // this warp's chunk
     const uint32_t nvalid = min((uint32_t)SPL_CHUNK, p1 - c0);
-    const uint32_t slot = ring + (s % SPL_NSTAGE) * R::STAGE;
-    const uint8_t* slot_p = sm + (s % SPL_NSTAGE) * R::STAGE;
+    const uint32_t slot = wring + (s % SPL_NSTAGE) * R::CHUNK;
+    const uint8_t* slot_p = wring_p + (s % SPL_NSTAGE) * R::CHUNK;
     bool valid[4];
     float ksc[4][NB], vsc[4][NB];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       valid[i] = (uint32_t)pr[i] < nvalid;
-      const float* kr = reinterpret_cast<const float*>(slot_p + R::KS) + (SPL_CHUNK * warp + pr[i]) * NB;
-      const float* vr = reinterpret_cast<const float*>(slot_p + R::VS) + (SPL_CHUNK * warp + pr[i]) * NB;
+      const float* kr = reinterpret_cast<const float*>(slot_p + R::KS) + pr[i] * NB;
+      const float* vr = reinterpret_cast<const float*>(slot_p + R::VS) + pr[i] * NB;
       float kv4[NB], vv4[NB];
       lds_scales<NB>(kr, kv4);
       lds_scales<NB>(vr, vv4);

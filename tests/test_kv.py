@@ -145,7 +145,8 @@ def reference_q8():
     return Reference().q8_quantize if Reference.available() else None
 
 
-@pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64)])
+@pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (32, 8, 128), (64, 8, 128), (4, 4, 128), (32, 4, 64),
+                                     (8, 4, 128)])
 @pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 300, 2049, 9001, 20000])  # >= 4096: split kernel
 @pytest.mark.parametrize("new_row", ["fused", "pre_appended"])
 def test_attend(oracle, ctx, H, KV, hd, seq, new_row):
@@ -155,10 +156,10 @@ def test_attend(oracle, ctx, H, KV, hd, seq, new_row):
 @pytest.mark.parametrize("H,KV,hd", [(8, 2, 64), (64, 8, 128), (8, 1, 128)])
 @pytest.mark.parametrize("seq", [1, 65, 300, 700, 4000])
 def test_attend_long_cache(oracle, ctx, H, KV, hd, seq):
-    """A cache of 8192 positions attends with the split kernel at every
-    length: short ranges on the per-warp loop, splits of 256+ positions on the
-    long loop, partials merged in global memory; one KV head (a tensor-parallel
-    rank of the 70B shape) included."""
+    """A cache of 8192 positions attends with the staged split kernel at
+    every length: one cluster of splits (merged in distributed shared memory)
+    up to 1024 positions, several clusters merged through global memory
+    beyond; one KV head (a tensor-parallel rank of the 70B shape) included."""
     check_attend(oracle, ctx, H, KV, hd, seq, "fused", 8192)
 
 
@@ -243,7 +244,8 @@ def score_rounding_bound(q, K, V, H, KV, hd, seq, scale):
     return out
 
 
-@pytest.mark.parametrize("H,KV,hd,seq", [(64, 8, 128, 300), (64, 8, 128, 5000), (8, 2, 64, 1500)])
+@pytest.mark.parametrize("H,KV,hd,seq", [(64, 8, 128, 300), (64, 8, 128, 5000), (8, 2, 64, 1500),
+                                          (8, 4, 64, 4200), (4, 4, 128, 9000)])
 def test_attend_batch(oracle, ctx, H, KV, hd, seq):
     """Three sequences (cache layers 1..3) in one launch: each appends its new
     row bit-exactly and attends as the oracle does on its own K/V."""

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "attn.cuh"
 #include "attn_dev.cuh"
@@ -244,8 +245,15 @@ template <int HD, int G>
 cudaError_t attn_split_go(const AttnArgs& a, cudaStream_t st) {
   auto k = attn_split_kernel<HD, G>;
   const int smem = SplitRing<HD>::BYTES;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // per device, once: the shared-memory attribute and the co-resident cluster
+  // count (a process may drive several GPUs, from several threads)
+  static std::atomic<int> co_resident[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  int clusters = (dev >= 0 && dev < 64) ? co_resident[dev].load() : 0;
+  if (clusters == 0 && (e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+    return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.kv.n_kv, SPL_CLUSTER);
   cfg.blockDim = dim3(SPL_THREADS);
@@ -264,8 +272,10 @@ cudaError_t attn_split_go(const AttnArgs& a, cudaStream_t st) {
   }
   cfg.attrs = at;
   cfg.numAttrs = n;
-  int clusters = 0;
-  if ((e = cudaOccupancyMaxActiveClusters(&clusters, k, &cfg)) != cudaSuccess) return e;
+  if (clusters == 0) {
+    if ((e = cudaOccupancyMaxActiveClusters(&clusters, k, &cfg)) != cudaSuccess) return e;
+    if (clusters > 0 && dev >= 0 && dev < 64) co_resident[dev].store(clusters);
+  }
   const uint32_t n_seq = std::max<uint32_t>(1, a.n_seq);
   if (clusters < 1 || a.max_splits < (uint32_t)SPL_CLUSTER) return cudaErrorNotSupported;
   // one wave of clusters over the (KV head, sequence) pairs; with more pairs

@@ -175,3 +175,26 @@ def test_live_model_vs_reference(oracle, reference):
     t_orc, l_orc = oracle.generate(model, prompt, 5)
     assert np.array_equal(t_ref, t_orc)
     assert np.array_equal(l_ref, l_orc)
+
+
+@pytest.mark.parametrize("qt", [12, 13, 14])
+def test_conditioned_weights_are_unit_gain(oracle, qt):
+    """synth's conditioned matrices (used by the multi-position layer and
+    prefill tests): dequantised by the oracle they are zero-mean with rms
+    about 1/sqrt(cols), so a matvec keeps activations of order one; the
+    Q4_K / Q5_K blocks carry mins equal to their scales.  (Blocks whose fp16
+    d is subnormal decode d at half its value -- the reference's quirk -- while
+    dmin = 7.5 d or 15.5 d is normal, so those blocks are not centred: a small
+    mean remains, largest for Q5_K, whose d are smallest.)"""
+    rng = np.random.default_rng(qt)
+    rows, cols = 64, 1024
+    w = synth.quant_matrix(rng, qt, rows, cols, conditioned=True)
+    d = oracle.dequant(qt, w, rows * cols).astype(np.float64)
+    target = 1.0 / math.sqrt(cols)
+    assert abs(d.mean()) < 0.25 * target
+    assert 0.8 * target < d.std() < 1.25 * target
+    if qt in (12, 13):
+        b = w.reshape(-1, synth.BLOCK_BYTES[qt])
+        sc = b[:, 4:16]
+        assert np.array_equal(sc[:, 4:8], sc[:, 0:4])
+        assert np.array_equal(sc[:, 8:12] >> 4, sc[:, 8:12] & 0xF)

@@ -158,7 +158,7 @@ def test_attend(oracle, ctx, H, KV, hd, seq, new_row):
 def test_attend_long_cache(oracle, ctx, H, KV, hd, seq):
     """A cache of 8192 positions attends with the staged split kernel at
     every length: one cluster of splits (merged in distributed shared memory)
-    up to 1024 positions, several clusters merged through global memory
+    up to 2048 positions, several clusters merged through global memory
     beyond; one KV head (a tensor-parallel rank of the 70B shape) included."""
     check_attend(oracle, ctx, H, KV, hd, seq, "fused", 8192)
 

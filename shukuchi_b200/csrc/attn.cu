@@ -364,17 +364,6 @@ cudaError_t attn_decode_batch_launch(const AttnArgs& a, cudaStream_t stream) {
   return a.kv.hd == 64 ? attn_split_hd<64>(c, G, stream) : attn_split_hd<128>(c, G, stream);
 }
 
-// The split-K kernel with partials in global memory (one item per CTA); kept
-// for callers that size `part` themselves.
-cudaError_t attn_decode_split_launch(const AttnArgs& a, cudaStream_t stream) {
-  if (a.kv.n_kv == 0 || a.n_heads % a.kv.n_kv) return cudaErrorInvalidValue;
-  if (a.max_splits == 0 || a.max_splits > (uint32_t)ATT_MAX_SPLITS) return cudaErrorInvalidValue;
-  const uint32_t G = a.n_heads / a.kv.n_kv;
-  if (a.kv.hd == 64) return attn_launch_hd<64>(a, G, stream);
-  if (a.kv.hd == 128) return attn_launch_hd<128>(a, G, stream);
-  return cudaErrorInvalidValue;
-}
-
 cudaError_t kv_append_launch(const KvLayout& kv, uint32_t layer, const uint32_t* pos,
                              const float* k, const float* v, int* err, cudaStream_t stream) {
   kv_append_kernel<<<kv.n_kv, 128, 0, stream>>>(kv, layer, pos, k, v, err);

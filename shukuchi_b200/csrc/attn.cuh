@@ -57,8 +57,6 @@ cudaError_t attn_decode_launch(const AttnArgs& a, cudaStream_t stream);
 // kernel (a.n_seq and the strides set; q 16-byte aligned; part / counters
 // sized for n_seq); cudaErrorNotSupported when that kernel cannot run.
 cudaError_t attn_decode_batch_launch(const AttnArgs& a, cudaStream_t stream);
-// The same with splits merged through `part` and `counters` in global memory.
-cudaError_t attn_decode_split_launch(const AttnArgs& a, cudaStream_t stream);
 size_t attn_part_floats(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_splits);
 
 // Quantise and store one token's K and V (engine/src/kv_cache.c:130-155).

@@ -157,7 +157,7 @@ __device__ __forceinline__ void spl_issue(uint32_t slot, uint8_t* slot_p, const 
     cp_async16(slot + R::VS + 16 * i, Vs + (size_t)b * R::NB + 4 * i);
   }
   // head_dim 64 with an odd row count: the last row's two scales, by plain
-  // loads (published by the same barrier as the copies)
+  // loads (published to the warp by the same __syncwarp as the copies)
   for (uint32_t i = 4 * n16 + lane; i < nf; i += 32) {
     reinterpret_cast<float*>(slot_p + R::KS)[i] = __ldcg(Ks + (size_t)b * R::NB + i);
     reinterpret_cast<float*>(slot_p + R::VS)[i] = __ldcg(Vs + (size_t)b * R::NB + i);
@@ -243,16 +243,16 @@ __device__ __forceinline__ void spl_compute(const AttnArgs& a, uint32_t kvh, uin
       }
   }
 
-  // per-lane fragment addresses inside a stage (warp rows 16*warp..+15)
+  // per-lane fragment addresses inside a chunk slot (rows 0..15)
   uint32_t koff[NB], voff[NB];
   {
-    const int i = lane >> 3, rr = lane & 7, row0 = 0;
+    const int i = lane >> 3, rr = lane & 7;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
       // K: matrices (rows 0-7, piece 2j), (0-7, 2j+1), (8-15, 2j), (8-15, 2j+1)
-      koff[j] = R::K + spl_swz<HD>(row0 + (i >> 1) * 8 + rr, 2 * j + (i & 1));
+      koff[j] = R::K + spl_swz<HD>((i >> 1) * 8 + rr, 2 * j + (i & 1));
       // V: matrices (rows 0-7, piece 2j), (8-15, 2j), (0-7, 2j+1), (8-15, 2j+1)
-      voff[j] = R::V + spl_swz<HD>(row0 + (i & 1) * 8 + rr, 2 * j + (i >> 1));
+      voff[j] = R::V + spl_swz<HD>((i & 1) * 8 + rr, 2 * j + (i >> 1));
     }
   }
   const int pr[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};  // this lane's chunk positions
